@@ -1,0 +1,305 @@
+/*
+ * mg_b200.h -- C ABI of the B200 (sm_100a) Gaussian-splatting training path.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream, allocates nothing (the caller owns every output and every scratch
+ * buffer, sized with the *_scratch_bytes queries), launches on `stream` and
+ * returns an mg_status. No entry point synchronises the device except where
+ * its comment says so. Reference citations are `path:line` inside the
+ * nandometzger/metal-gauss project.
+ *
+ * Layouts (all fp32 unless stated, row-major, contiguous unless a stride is
+ * passed):
+ *   means (N,3), quats (N,4) wxyz unnormalised, scales (N,3) linear,
+ *   opacities (N,) in [0,1]; SH rows are 3 floats (one RGB triple). SH is
+ *   either one (N,16,3) tensor ("fused") or a DC band (N,1,3) plus bands 1+
+ *   (N,15,3) ("split"), described by mg_sh_layout exactly as the reference's
+ *   `shl` uniform (metal_gauss/csrc/preprocess.metal:30-51).
+ *   Per-Gaussian screen-space gradients use one packed record of
+ *   MG_G2D_STRIDE floats per Gaussian (see MG_G2D_*), so the rasteriser's
+ *   backward can add a whole record with three 16-byte vector atomics.
+ */
+#ifndef MG_B200_H
+#define MG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* mg_stream_t;
+
+typedef enum mg_status {
+    MG_OK = 0,
+    MG_ERR_INVALID_ARGUMENT = 1, /* bad size, layout, tile or null pointer   */
+    MG_ERR_CAPACITY = 2,         /* a count exceeds a buffer or a 32-bit index */
+    MG_ERR_CUDA = 3,             /* a CUDA launch or runtime call failed      */
+    MG_ERR_DEVICE = 4            /* a kernel set the device error word        */
+} mg_status;
+
+/* Human-readable reason for the last non-MG_OK status on this host thread. */
+const char* mg_last_error(void);
+
+/* Library version, for the loader's sanity check. */
+int mg_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Camera and layout PODs                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* One pinhole view. Passed by pointer to host memory and copied into the
+ * kernels' parameter space, so no device->host traffic is needed for it
+ * (the reference reads viewmat/cam_center on the host in makeParams,
+ * metal_gauss/csrc/rasterize.mm:226-242). */
+typedef struct mg_camera {
+    float viewmat[16];   /* world -> camera, row-major 4x4 (rows 0..2 used) */
+    float fx, fy, cx, cy;
+    float cam_center[4]; /* xyz = -R^T t, computed by the caller; w unused  */
+    int32_t width, height;
+    float near_plane, far_plane;
+    float blur;          /* 2D dilation added to the covariance diagonal    */
+    float max_radius;    /* radius cull, pixels                             */
+} mg_camera;
+
+/* SH row addressing, in units of 3-float rows (preprocess.metal:30-51):
+ *   fused (N,16,3): {16, 16, 1};   split (N,1,3)+(N,15,3): {1, 15, 0}. */
+typedef struct mg_sh_layout {
+    int32_t stride_dc;
+    int32_t stride_rest;
+    int32_t offset_rest;
+    int32_t unused;
+} mg_sh_layout;
+
+/* Packed per-Gaussian screen-space gradient record (floats). */
+#define MG_G2D_STRIDE 12
+#define MG_G2D_UV 0      /* d uv.x, d uv.y                       */
+#define MG_G2D_OPACITY 2 /* d opacity                            */
+#define MG_G2D_ABSUV 3   /* sum over pixels of |d uv| (absgrad)  */
+#define MG_G2D_CONIC 4   /* d conic.x, .y, .z                    */
+#define MG_G2D_COLOR 8   /* d color.r, .g, .b                    */
+
+/* ------------------------------------------------------------------------ */
+/* Preprocess: projection + EWA conic + SnugBox extent + SH colour          */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces preprocess_forward (metal_gauss/csrc/rasterize.mm:244-284,
+ * kernel metal_gauss/csrc/preprocess.metal:114-221).
+ * sh_degree in 0..3; sh_dc/sh_rest may be NULL (with sh_degree < 0) to skip
+ * colour entirely, which is the explicit-colour route of render()
+ * (metal_gauss/metal_backend.py:449-462). Outputs: uv (N,2), conic (N,3),
+ * depth (N,), rxy (N,2), valid (N,) int32, color (N,3). */
+mg_status mg_preprocess_forward(
+    const float* means, const float* quats, const float* scales,
+    const float* sh_dc, const float* sh_rest, mg_sh_layout shl,
+    const float* opacities, const mg_camera* cam, int32_t sh_degree, int64_t n,
+    float* uv, float* conic, float* depth, float* rxy, int32_t* valid,
+    float* color, mg_stream_t stream);
+
+/* Replaces preprocess_backward (rasterize.mm:286-327, kernel
+ * preprocess.metal:223-411). The incoming gradients are read through row
+ * strides (in floats) so they may point into a packed MG_G2D record
+ * (stride MG_G2D_STRIDE) or into plain (N,2)/(N,3) tensors. d_color may be
+ * NULL (explicit colours: SH branch skipped, d_sh untouched).
+ * Outputs are overwritten: d_means (N,3), d_quats (N,4), d_scales (N,3),
+ * d_sh_dc / d_sh_rest in the layout `shl` (may alias, as the fused layout
+ * does). */
+mg_status mg_preprocess_backward(
+    const float* means, const float* quats, const float* scales,
+    const float* sh_dc, const float* sh_rest, mg_sh_layout shl,
+    const float* d_uv, int64_t d_uv_stride,
+    const float* d_conic, int64_t d_conic_stride,
+    const float* d_color, int64_t d_color_stride,
+    const int32_t* valid, const mg_camera* cam, int32_t sh_degree, int64_t n,
+    float* d_means, float* d_quats, float* d_scales,
+    float* d_sh_dc, float* d_sh_rest, mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Binning: exact ellipse-vs-tile test, keys, sort, per-tile ranges         */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces bin_count (rasterize.mm:485-497; binning.metal:92-104):
+ * counts[g] = number of tiles whose rectangle the Gaussian's alpha >= 1/255
+ * level set reaches (0 for invalid rows). */
+mg_status mg_bin_count(
+    const float* uv, const float* rxy, const float* conic,
+    const float* opacity, const int32_t* valid, int64_t n,
+    int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
+    int32_t tiles_y, int32_t* counts, mg_stream_t stream);
+
+/* Replaces bin_write (rasterize.mm:499-516; binning.metal:106-120):
+ * keys[offsets[g] + k] = (tile_id << 32) | bits(depth[g]), ids[...] = g,
+ * tiles in row-major order per Gaussian. `total` is the key capacity. */
+mg_status mg_bin_write(
+    const float* uv, const float* rxy, const float* conic,
+    const float* opacity, const int32_t* valid, const float* depth,
+    const int32_t* offsets, int64_t total, int64_t n,
+    int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
+    int32_t tiles_y, uint64_t* keys, int32_t* ids, mg_stream_t stream);
+
+/* Stable LSD onesweep radix sort of (key, value) pairs on the low `bits`
+ * bits of the key. Replaces torch.argsort(keys) (metal_backend.py:256), which
+ * the reference uses because MPS exposes no radix sort. keys_alt/vals_alt are
+ * ping-pong buffers of n elements; the sorted result is left in keys/vals.
+ * scratch must hold mg_sort_scratch_bytes(n, bits, key_bytes) bytes. The
+ * decoupled look-back is bounded; a timeout sets the device error word. */
+size_t mg_sort_scratch_bytes(int64_t n, int32_t bits, int32_t key_bytes);
+mg_status mg_sort_pairs_u32(uint32_t* keys, uint32_t* vals,
+                            uint32_t* keys_alt, uint32_t* vals_alt,
+                            int64_t n, int32_t bits, void* scratch,
+                            size_t scratch_bytes, mg_stream_t stream);
+mg_status mg_sort_pairs_u64(uint64_t* keys, uint32_t* vals,
+                            uint64_t* keys_alt, uint32_t* vals_alt,
+                            int64_t n, int32_t bits, void* scratch,
+                            size_t scratch_bytes, mg_stream_t stream);
+
+/* Replaces `keys[order] >> 32` + torch.searchsorted (metal_backend.py:
+ * 257-260): offsets[t] = first index whose tile id is >= t, offsets[T] = m.
+ * `tile_ids` are the sorted tile ids (u32), or NULL with `keys64` set to the
+ * sorted 64-bit keys, whose high word is the tile id. */
+mg_status mg_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64,
+                         int64_t m, int32_t n_tiles, int32_t* offsets,
+                         mg_stream_t stream);
+
+/* The whole binning of one view in the two-stage form, replacing
+ * build_tile_lists_metal (metal_backend.py:217-285):
+ *   stage A (mg_bin_prepare): per-Gaussian tile counts; stable depth sort of
+ *     all Gaussians (invalid ones last); exclusive scan of the counts in
+ *     depth order. Writes the pair total to *total_dev (device int64).
+ *   stage B (mg_bin_emit): the caller reads the total (the one host sync of
+ *     the reference, metal_backend.py:247), then this writes every
+ *     (tile, Gaussian) pair in depth order, stably sorts the pairs by tile id
+ *     and extracts the per-tile ranges.
+ * The result equals a stable sort on (tile_id << 32 | depth_bits) keys
+ * emitted in Gaussian order: within a tile, front to back, equal depths by
+ * Gaussian index. Scratch sizes come from the two queries. */
+size_t mg_bin_prepare_scratch_bytes(int64_t n);
+mg_status mg_bin_prepare(
+    const float* uv, const float* rxy, const float* conic,
+    const float* opacity, const int32_t* valid, const float* depth, int64_t n,
+    int32_t width, int32_t height, int32_t tile, int64_t* total_dev,
+    void* scratch, size_t scratch_bytes, mg_stream_t stream);
+size_t mg_bin_emit_scratch_bytes(int64_t n, int64_t m, int32_t n_tiles);
+mg_status mg_bin_emit(
+    const float* uv, const float* rxy, const float* conic,
+    const float* opacity, int64_t n, int64_t m,
+    int32_t width, int32_t height, int32_t tile,
+    const void* prepare_scratch, int32_t* gauss_ids, int32_t* tile_offsets,
+    void* scratch, size_t scratch_bytes, mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Rasterisation                                                            */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces rasterize_forward (rasterize.mm:79-113; rasterize.metal:61-167).
+ * One CTA per tile, tile in {8, 12, 16, 32}. Outputs rgb (H,W,3),
+ * alpha (H,W), final transmittance T (H,W), stop index (H,W) int32.
+ * background: NULL, or 3 host floats blended as rgb + max(1-alpha,0)*bg,
+ * which is metal_backend.py:539-541 folded into the kernel. */
+mg_status mg_rasterize_forward(
+    const float* uv, const float* conic, const float* opacity,
+    const float* color, const int32_t* gauss_ids, const int32_t* tile_offsets,
+    int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
+    const float* background, float* out_rgb, float* out_alpha, float* out_T,
+    int32_t* out_stop, mg_stream_t stream);
+
+/* Replaces rasterize_backward (rasterize.mm:147-194; rasterize.metal:
+ * 173-340). grad2d (N, MG_G2D_STRIDE) is ACCUMULATED into (zero it first for
+ * a fresh gradient). background as in the forward: the blend's adjoint is
+ * applied in-kernel, which needs the forward's alpha (H,W) (ignored when
+ * background is NULL; grad_alpha may then also be NULL for zero).
+ * want_absgrad adds per-pixel |d uv| into MG_G2D_ABSUV. */
+mg_status mg_rasterize_backward(
+    const float* uv, const float* conic, const float* opacity,
+    const float* color, const int32_t* gauss_ids, const int32_t* tile_offsets,
+    const float* final_T, const int32_t* stop, const float* grad_rgb,
+    const float* grad_alpha, int32_t width, int32_t height, int32_t tile,
+    int32_t tiles_x, const float* background, const float* alpha,
+    int32_t want_absgrad, int64_t n, float* grad2d, mg_stream_t stream);
+
+/* Replaces pack_intersections (rasterize.mm:115-145; rasterize.metal:
+ * 358-376): gathers (u, v, opacity), conic and colour by sorted id. */
+mg_status mg_pack_intersections(
+    const float* uv, const float* conic, const float* opacity,
+    const float* color, const int32_t* gauss_ids, int64_t m,
+    float* p_xy_opac, float* p_conic, float* p_rgb, mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Optimisers                                                               */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces adam_step (rasterize.mm:329-360; adam.metal:25-42): one in-place
+ * torch.optim.Adam step, eps added after dividing by sqrt(bc2). bc1 and
+ * sqrt_bc2 are computed by the caller in double, as torch does. */
+mg_status mg_adam_step(float* p, const float* g, float* m, float* v,
+                       int64_t n, float lr, float b1, float b2, float eps,
+                       float bc1, float sqrt_bc2, mg_stream_t stream);
+
+/* SelectiveAdam row update (metal_gauss/selective_adam.py:116-186): for each
+ * row r with visible[r] != 0, k = steps[r] + 1,
+ *   m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2;
+ *   p -= lr * sqrt(1-b2^k) / (1-b1^k) * m / (sqrt(v) + eps),
+ * over the row's `row_width` contiguous elements; rows not visible are left
+ * untouched. `rows` may exceed the mask length `n_visible` (preallocated
+ * capacity rows, selective_adam.py:47-59, are treated as invisible).
+ * steps[r] is advanced by mg_selective_adam_advance_steps afterwards. */
+mg_status mg_selective_adam_step(float* p, const float* g, float* m, float* v,
+                                 const float* steps, const uint8_t* visible,
+                                 int64_t n_visible, int64_t rows,
+                                 int64_t row_width, float lr, float b1,
+                                 float b2, float eps, mg_stream_t stream);
+mg_status mg_selective_adam_advance_steps(float* steps, const uint8_t* visible,
+                                          int64_t n_visible, int64_t rows,
+                                          mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* SSIM (11-tap separable Gaussian, zero padding) and the training loss     */
+/* ------------------------------------------------------------------------ */
+
+/* The reference's five SSIM kernels, same layouts (ssim.metal:23-188,
+ * bridge rasterize.mm:362-461): x, y are (H,W,3); stacks are (15,H,W) with
+ * channels 0-2 x, 3-5 y, 6-8 xx, 9-11 yy, 12-14 xy; w is 11 floats. */
+mg_status mg_ssim_stack_blur_h(const float* x, const float* y, const float* w,
+                               int32_t height, int32_t width, float* out,
+                               mg_stream_t stream);
+mg_status mg_ssim_blur15(const float* src, const float* w, int32_t dir,
+                         int32_t height, int32_t width, float* dst,
+                         mg_stream_t stream);
+mg_status mg_ssim_tail_forward(const float* b, int32_t height, int32_t width,
+                               float* out, mg_stream_t stream);
+mg_status mg_ssim_tail_backward(const float* b, const float* gout,
+                                int32_t height, int32_t width, float* gb,
+                                mg_stream_t stream);
+mg_status mg_ssim_chain_backward(const float* x, const float* y,
+                                 const float* d_stack, int32_t height,
+                                 int32_t width, float* d_x, mg_stream_t stream);
+
+/* Fused training loss for one view, forward and backward in one pass:
+ *   loss = w_l1 * mean|x - y| + w_ssim * (1 - SSIM(x, y))
+ * (train.py:389-393 with the defaults w_l1 = 0.8, w_ssim = 0.2), scaled by
+ * `scale` (e.g. 1/V for a mean over V views). Writes grad_x (H,W,3) =
+ * scale * dloss/dx and ADDS scale*loss into *loss_dev (device float).
+ * x, y (H,W,3); w is 11 floats. */
+size_t mg_l1_ssim_scratch_bytes(int32_t height, int32_t width);
+mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
+                          int32_t height, int32_t width, float w_l1,
+                          float w_ssim, float scale, float* grad_x,
+                          float* loss_dev, void* scratch, size_t scratch_bytes,
+                          mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Device error word                                                        */
+/* ------------------------------------------------------------------------ */
+
+/* Reads and clears the device error word of the current device (bounded
+ * spins that gave up, checked-mode index faults). Synchronises `stream`.
+ * *code_out receives 0 when nothing was recorded. */
+mg_status mg_read_device_error(int32_t* code_out, mg_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MG_B200_H */

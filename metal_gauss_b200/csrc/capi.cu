@@ -1,0 +1,277 @@
+// C ABI glue: error reporting, the device error word, and the entry points
+// that orchestrate several kernels (binning and sorting).
+#include <mutex>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace mg {
+
+namespace {
+thread_local std::string g_last_error;
+
+__device__ int32_t g_device_error_word;
+
+constexpr int kMaxDevices = 64;
+int32_t* g_error_ptr[kMaxDevices] = {nullptr};
+std::mutex g_error_mu;
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int tile_bits(int n_tiles) {
+    int b = 0;
+    while ((1 << b) < n_tiles) ++b;
+    return b < 1 ? 1 : b;
+}
+
+// Stage-A scratch carved into named arrays.
+struct PrepareScratch {
+    uint32_t* counts;
+    uint32_t* dkeys;
+    uint32_t* dvals;
+    uint32_t* dkeys_alt;
+    uint32_t* dvals_alt;
+    uint32_t* offsets;
+    void* sort;
+    size_t sort_bytes;
+    void* scan;
+    size_t total;
+};
+
+PrepareScratch carve_prepare(const void* base, int64_t n) {
+    PrepareScratch s;
+    char* p = const_cast<char*>(static_cast<const char*>(base));
+    const size_t arr = align256(sizeof(uint32_t) * (size_t)std::max<int64_t>(n, 1));
+    s.counts = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.dkeys = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.dvals = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.dkeys_alt = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.dvals_alt = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.offsets = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.sort_bytes = align256(radix_sort_scratch_bytes(n, 32, 4));
+    s.sort = p; p += s.sort_bytes;
+    s.scan = p; p += align256(scan_scratch_bytes(n));
+    s.total = (size_t)(p - static_cast<const char*>(base));
+    return s;
+}
+
+struct EmitScratch {
+    uint32_t* pair_tiles;
+    uint32_t* tiles_alt;
+    uint32_t* ids_alt;
+    void* sort;
+    size_t sort_bytes;
+    size_t total;
+};
+
+EmitScratch carve_emit(void* base, int64_t m, int n_tiles) {
+    EmitScratch s;
+    char* p = static_cast<char*>(base);
+    const size_t arr = align256(sizeof(uint32_t) * (size_t)std::max<int64_t>(m, 1));
+    s.pair_tiles = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.tiles_alt = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.ids_alt = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.sort_bytes = align256(radix_sort_scratch_bytes(m, tile_bits(n_tiles), 4));
+    s.sort = p; p += s.sort_bytes;
+    s.total = (size_t)(p - static_cast<char*>(base));
+    return s;
+}
+
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+mg_status check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return MG_OK;
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return MG_ERR_CUDA;
+}
+
+int32_t* device_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_error_mu);
+    if (g_error_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) return nullptr;
+        g_error_ptr[dev] = static_cast<int32_t*>(p);
+    }
+    return g_error_ptr[dev];
+}
+
+}  // namespace mg
+
+using namespace mg;
+
+extern "C" const char* mg_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int mg_version(void) { return 1; }
+
+extern "C" mg_status mg_read_device_error(int32_t* code_out, mg_stream_t stream) {
+    MG_REQUIRE(code_out != nullptr, "read_device_error: null output");
+    int32_t* w = device_error_word();
+    if (w == nullptr) return fail(MG_ERR_CUDA, "read_device_error: no device error word");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int32_t host = 0;
+    if (cudaMemcpyAsync(&host, w, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaMemsetAsync(w, 0, sizeof(int32_t), s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return check_launch("read_device_error");
+    *code_out = host;
+    return MG_OK;
+}
+
+extern "C" mg_status mg_preprocess_forward(const float* means, const float* quats,
+                                           const float* scales, const float* sh_dc,
+                                           const float* sh_rest, mg_sh_layout shl,
+                                           const float* opacities, const mg_camera* cam,
+                                           int32_t sh_degree, int64_t n, float* uv,
+                                           float* conic, float* depth, float* rxy,
+                                           int32_t* valid, float* color,
+                                           mg_stream_t stream) {
+    MG_REQUIRE(cam != nullptr, "preprocess_forward: null camera");
+    MG_REQUIRE(sh_degree <= 3, "preprocess_forward: sh_degree must be <= 3");
+    MG_REQUIRE(cam->width > 0 && cam->height > 0, "preprocess_forward: empty image");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(means && quats && scales && opacities && uv && conic && depth && rxy && valid,
+               "preprocess_forward: null pointer");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u,
+               "preprocess_forward: quats must be 16-byte aligned");
+    if (sh_degree >= 0 && sh_dc != nullptr) {
+        const bool fused = shl.stride_dc == 16 && shl.stride_rest == 16 && shl.offset_rest == 1;
+        const bool split = shl.stride_dc == 1 && shl.stride_rest == 15 && shl.offset_rest == 0;
+        MG_REQUIRE(fused || split, "SH must be either one (N,16,3) tensor or (N,1,3)+(N,15,3)");
+        MG_REQUIRE(sh_rest != nullptr && color != nullptr, "preprocess_forward: null SH pointer");
+    }
+    return launch_preprocess_forward(means, quats, scales, sh_dc, sh_rest, shl, opacities, *cam,
+                                     sh_degree, n, uv, conic, depth, rxy, valid, color,
+                                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" mg_status mg_bin_count(const float* uv, const float* rxy, const float* conic,
+                                  const float* opacity, const int32_t* valid, int64_t n,
+                                  int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
+                                  int32_t tiles_y, int32_t* counts, mg_stream_t stream) {
+    MG_REQUIRE(tile > 0 && tiles_x > 0 && tiles_y > 0, "bin_count: bad tiling");
+    return launch_bin_count(uv, rxy, conic, opacity, valid, n, width, height, tile, tiles_x,
+                            tiles_y, counts, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" mg_status mg_bin_write(const float* uv, const float* rxy, const float* conic,
+                                  const float* opacity, const int32_t* valid,
+                                  const float* depth, const int32_t* offsets, int64_t total,
+                                  int64_t n, int32_t width, int32_t height, int32_t tile,
+                                  int32_t tiles_x, int32_t tiles_y, uint64_t* keys,
+                                  int32_t* ids, mg_stream_t stream) {
+    MG_REQUIRE(tile > 0 && tiles_x > 0 && tiles_y > 0, "bin_write: bad tiling");
+    return launch_bin_write(uv, rxy, conic, opacity, valid, depth, offsets, total, n, width,
+                            height, tile, tiles_x, tiles_y, keys, ids,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mg_sort_scratch_bytes(int64_t n, int32_t bits, int32_t key_bytes) {
+    return radix_sort_scratch_bytes(n, bits, key_bytes);
+}
+
+template <typename K>
+static mg_status sort_pairs_impl(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt,
+                                 int64_t n, int32_t bits, void* scratch, size_t scratch_bytes,
+                                 mg_stream_t stream) {
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    bool in_alt = false;
+    MG_TRY(radix_sort_pairs<K>(keys, vals, keys_alt, vals_alt, n, bits, scratch, scratch_bytes,
+                               &in_alt, s));
+    if (in_alt) {
+        if (cudaMemcpyAsync(keys, keys_alt, sizeof(K) * n, cudaMemcpyDeviceToDevice, s) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(vals, vals_alt, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, s) !=
+                cudaSuccess)
+            return check_launch("sort result copy");
+    }
+    return MG_OK;
+}
+
+extern "C" mg_status mg_sort_pairs_u32(uint32_t* keys, uint32_t* vals, uint32_t* keys_alt,
+                                       uint32_t* vals_alt, int64_t n, int32_t bits,
+                                       void* scratch, size_t scratch_bytes,
+                                       mg_stream_t stream) {
+    return sort_pairs_impl<uint32_t>(keys, vals, keys_alt, vals_alt, n, bits, scratch,
+                                     scratch_bytes, stream);
+}
+
+extern "C" mg_status mg_sort_pairs_u64(uint64_t* keys, uint32_t* vals, uint64_t* keys_alt,
+                                       uint32_t* vals_alt, int64_t n, int32_t bits,
+                                       void* scratch, size_t scratch_bytes,
+                                       mg_stream_t stream) {
+    return sort_pairs_impl<uint64_t>(keys, vals, keys_alt, vals_alt, n, bits, scratch,
+                                     scratch_bytes, stream);
+}
+
+extern "C" mg_status mg_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64, int64_t m,
+                                    int32_t n_tiles, int32_t* offsets, mg_stream_t stream) {
+    MG_REQUIRE(n_tiles > 0 && offsets != nullptr, "tile_ranges: bad arguments");
+    MG_REQUIRE(m == 0 || tile_ids != nullptr || keys64 != nullptr, "tile_ranges: no keys");
+    return launch_tile_ranges(tile_ids, keys64, m, n_tiles, offsets,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mg_bin_prepare_scratch_bytes(int64_t n) { return carve_prepare(nullptr, n).total; }
+
+extern "C" mg_status mg_bin_prepare(const float* uv, const float* rxy, const float* conic,
+                                    const float* opacity, const int32_t* valid,
+                                    const float* depth, int64_t n, int32_t width, int32_t height,
+                                    int32_t tile, int64_t* total_dev, void* scratch,
+                                    size_t scratch_bytes, mg_stream_t stream) {
+    MG_REQUIRE(tile > 0 && width > 0 && height > 0, "bin_prepare: bad tiling");
+    MG_REQUIRE(total_dev != nullptr, "bin_prepare: null total");
+    MG_REQUIRE(n < (int64_t)1 << 30, "bin_prepare: more than 2^30 Gaussians");
+    const PrepareScratch s = carve_prepare(scratch, n);
+    MG_REQUIRE(scratch != nullptr && scratch_bytes >= s.total, "bin_prepare: scratch too small");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
+    MG_TRY(launch_bin_count_depth(uv, rxy, conic, opacity, valid, depth, n, width, height, tile,
+                                  tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, st));
+    bool in_alt = false;
+    MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, n, 32, s.sort,
+                                      s.sort_bytes, &in_alt, st));
+    if (in_alt &&
+        cudaMemcpyAsync(s.dvals, s.dvals_alt, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice,
+                        st) != cudaSuccess)
+        return check_launch("bin_prepare copy");
+    return exclusive_scan_gather(s.counts, s.dvals, n, s.offsets, total_dev, s.scan, st);
+}
+
+extern "C" size_t mg_bin_emit_scratch_bytes(int64_t n, int64_t m, int32_t n_tiles) {
+    (void)n;
+    return carve_emit(nullptr, m, n_tiles).total;
+}
+
+extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float* conic,
+                                 const float* opacity, int64_t n, int64_t m, int32_t width,
+                                 int32_t height, int32_t tile, const void* prepare_scratch,
+                                 int32_t* gauss_ids, int32_t* tile_offsets, void* scratch,
+                                 size_t scratch_bytes, mg_stream_t stream) {
+    MG_REQUIRE(tile > 0 && width > 0 && height > 0, "bin_emit: bad tiling");
+    MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 31), "bin_emit: pair count exceeds 2^31");
+    MG_REQUIRE(prepare_scratch != nullptr && tile_offsets != nullptr, "bin_emit: null pointer");
+    const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
+    const int n_tiles = tiles_x * tiles_y;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (m == 0) return launch_tile_ranges(nullptr, nullptr, 0, n_tiles, tile_offsets, st);
+    MG_REQUIRE(gauss_ids != nullptr, "bin_emit: null gauss_ids");
+    const EmitScratch e = carve_emit(scratch, m, n_tiles);
+    MG_REQUIRE(scratch != nullptr && scratch_bytes >= e.total, "bin_emit: scratch too small");
+    const PrepareScratch p = carve_prepare(prepare_scratch, n);
+    uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
+    MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m, width,
+                           height, tile, tiles_x, tiles_y, e.pair_tiles, ids, st));
+    bool in_alt = false;
+    MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m,
+                                      tile_bits(n_tiles), e.sort, e.sort_bytes, &in_alt, st));
+    const uint32_t* sorted_tiles = in_alt ? e.tiles_alt : e.pair_tiles;
+    if (in_alt && cudaMemcpyAsync(ids, e.ids_alt, sizeof(uint32_t) * m,
+                                  cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return check_launch("bin_emit copy");
+    return launch_tile_ranges(sorted_tiles, nullptr, m, n_tiles, tile_offsets, st);
+}

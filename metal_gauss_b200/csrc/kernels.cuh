@@ -1,0 +1,56 @@
+// Internal launchers shared between the translation units of libmg_b200.so.
+#pragma once
+
+#include "common.cuh"
+
+namespace mg {
+
+// preprocess_fwd.cu (built with -fmad=false)
+mg_status launch_preprocess_forward(const float* means, const float* quats,
+                                    const float* scales, const float* sh_dc,
+                                    const float* sh_rest, mg_sh_layout shl,
+                                    const float* opacities, const mg_camera& cam,
+                                    int sh_degree, int64_t n, float* uv, float* conic,
+                                    float* depth, float* rxy, int32_t* valid,
+                                    float* color, cudaStream_t stream);
+mg_status launch_bin_count(const float* uv, const float* rxy, const float* conic,
+                           const float* opacity, const int32_t* valid, int64_t n,
+                           int W, int H, int tile, int tiles_x, int tiles_y,
+                           int32_t* counts, cudaStream_t stream);
+mg_status launch_bin_write(const float* uv, const float* rxy, const float* conic,
+                           const float* opacity, const int32_t* valid,
+                           const float* depth, const int32_t* offsets, int64_t total,
+                           int64_t n, int W, int H, int tile, int tiles_x,
+                           int tiles_y, uint64_t* keys, int32_t* ids,
+                           cudaStream_t stream);
+mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float* conic,
+                                 const float* opacity, const int32_t* valid,
+                                 const float* depth, int64_t n, int W, int H, int tile,
+                                 int tiles_x, int tiles_y, uint32_t* counts,
+                                 uint32_t* dkeys, uint32_t* dvals, cudaStream_t stream);
+mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
+                          const float* opacity, const uint32_t* sorted_gid,
+                          const uint32_t* counts, const uint32_t* offsets, int64_t n,
+                          int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
+                          uint32_t* pair_tiles, uint32_t* pair_ids,
+                          cudaStream_t stream);
+
+// sort.cu
+// Sorts in place between (keys, vals) and (keys_alt, vals_alt); returns in
+// *result_in_alt whether the sorted data ended in the alt buffers.
+template <typename K>
+mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt,
+                           int64_t n, int bits, void* scratch, size_t scratch_bytes,
+                           bool* result_in_alt, cudaStream_t stream);
+size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes);
+// Exclusive scan of counts[order[i]] (order may be null: identity) into
+// out[i] (u32); writes the 64-bit total to *total_dev.
+size_t scan_scratch_bytes(int64_t n);
+mg_status exclusive_scan_gather(const uint32_t* counts, const uint32_t* order,
+                                int64_t n, uint32_t* out, int64_t* total_dev,
+                                void* scratch, cudaStream_t stream);
+mg_status launch_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64,
+                             int64_t m, int n_tiles, int32_t* offsets,
+                             cudaStream_t stream);
+
+}  // namespace mg

@@ -1,0 +1,111 @@
+// Adam updates: dense (torch.optim.Adam, adam.metal:25-42) and row-selective
+// (SelectiveAdam, metal_gauss/selective_adam.py:116-186). Both are single
+// HBM passes: read p, g, m, v; write p, m, v (28 B per element).
+#include "kernels.cuh"
+
+namespace mg {
+
+namespace {
+
+// torch's single-tensor Adam, in its operation order:
+//   m.lerp_(g, 1-b1); v.mul_(b2).addcmul_(g, g, 1-b2);
+//   denom = sqrt(v) / sqrt(bc2) + eps; p.addcdiv_(m, denom, -lr/bc1)
+__global__ void adam_kernel(float* __restrict__ p, const float* __restrict__ g,
+                            float* __restrict__ m, float* __restrict__ v, int64_t n,
+                            float lr_over_bc1, float b1, float b2, float eps,
+                            float sqrt_bc2) {
+    const float w1 = 1.0f - b1, w2 = 1.0f - b2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float gi = g[i];
+        float mi = m[i];
+        // lerp(start, end, w) with w < 0.5: start + w * (end - start)
+        mi = __fadd_rn(mi, __fmul_rn(w1, __fsub_rn(gi, mi)));
+        float vi = __fmul_rn(v[i], b2);
+        vi = __fadd_rn(vi, __fmul_rn(__fmul_rn(w2, gi), gi));
+        m[i] = mi;
+        v[i] = vi;
+        const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), sqrt_bc2), eps);
+        p[i] = __fadd_rn(p[i], __fdiv_rn(__fmul_rn(-lr_over_bc1, mi), denom));
+    }
+}
+
+__global__ void selective_adam_kernel(float* __restrict__ p, const float* __restrict__ g,
+                                      float* __restrict__ m, float* __restrict__ v,
+                                      const float* __restrict__ steps,
+                                      const uint8_t* __restrict__ visible,
+                                      int64_t n_visible, int64_t rows, int64_t width,
+                                      float lr, float b1, float b2, float eps, float w1,
+                                      float w2) {
+    const int64_t n = rows * width;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / width;
+        if (r >= n_visible || visible[r] == 0) continue;
+        const float k = __fadd_rn(steps[r], 1.0f);
+        const float bc1 = __fsub_rn(1.0f, powf(b1, k));
+        const float bc2 = __fsub_rn(1.0f, powf(b2, k));
+        const float step_size = __fmul_rn(lr, __fdiv_rn(__fsqrt_rn(bc2), bc1));
+        const float gi = g[i];
+        const float mi = __fadd_rn(__fmul_rn(m[i], b1), __fmul_rn(gi, w1));
+        const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(gi, gi), w2));
+        m[i] = mi;
+        v[i] = vi;
+        p[i] = __fsub_rn(p[i], __fdiv_rn(__fmul_rn(step_size, mi), __fadd_rn(__fsqrt_rn(vi), eps)));
+    }
+}
+
+__global__ void advance_steps_kernel(float* __restrict__ steps,
+                                     const uint8_t* __restrict__ visible, int64_t n_visible) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < n_visible && visible[r] != 0) steps[r] = __fadd_rn(steps[r], 1.0f);
+}
+
+int grid_for(int64_t n) {
+    return (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+}
+
+}  // namespace
+
+}  // namespace mg
+
+using namespace mg;
+
+extern "C" mg_status mg_adam_step(float* p, const float* g, float* m, float* v, int64_t n,
+                                  float lr, float b1, float b2, float eps, float bc1,
+                                  float sqrt_bc2, mg_stream_t stream) {
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(p && g && m && v, "adam_step: null pointer");
+    MG_REQUIRE(bc1 > 0.0f && sqrt_bc2 > 0.0f, "adam_step: bias corrections must be > 0");
+    adam_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        p, g, m, v, n, lr / bc1, b1, b2, eps, sqrt_bc2);
+    return check_launch("adam_step");
+}
+
+extern "C" mg_status mg_selective_adam_step(float* p, const float* g, float* m, float* v,
+                                            const float* steps, const uint8_t* visible,
+                                            int64_t n_visible, int64_t rows,
+                                            int64_t row_width, float lr, float b1, float b2,
+                                            float eps, mg_stream_t stream) {
+    if (rows == 0 || row_width == 0) return MG_OK;
+    MG_REQUIRE(p && g && m && v && steps && visible, "selective_adam_step: null pointer");
+    MG_REQUIRE(n_visible <= rows, "visibility mask has more rows than the parameter");
+    // (1 - b) is formed in double and rounded once, as torch does for the
+    // Python scalar in `grad * (1 - b1)`.
+    const float w1 = (float)(1.0 - (double)b1), w2 = (float)(1.0 - (double)b2);
+    selective_adam_kernel<<<grid_for(rows * row_width), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(
+        p, g, m, v, steps, visible, n_visible, rows, row_width, lr, b1, b2, eps, w1, w2);
+    return check_launch("selective_adam_step");
+}
+
+extern "C" mg_status mg_selective_adam_advance_steps(float* steps, const uint8_t* visible,
+                                                     int64_t n_visible, int64_t rows,
+                                                     mg_stream_t stream) {
+    if (n_visible == 0) return MG_OK;
+    MG_REQUIRE(n_visible <= rows, "visibility mask has more rows than the parameter");
+    advance_steps_kernel<<<ceil_div(n_visible, 256), 256, 0,
+                           reinterpret_cast<cudaStream_t>(stream)>>>(steps, visible,
+                                                                     n_visible);
+    return check_launch("selective_adam_advance_steps");
+}

@@ -1,0 +1,340 @@
+// Preprocess backward (preprocess.metal:223-411): SH adjoint gated on a
+// non-zero colour gradient and the ReLU of the pre-clamp colour, then the
+// projection adjoint (conic -> 2D covariance -> Sigma and J -> camera point,
+// with the Jacobian clamp routing the gradient to zc) and the quaternion VJP
+// through normalisation. Rows with valid == 0 get zero scale and quaternion
+// gradients. One thread per Gaussian, no atomics.
+//
+// SH coefficient rows are staged per warp through shared memory: the split
+// layout's (N,15,3) rows and the fused layout's (N,16,3) rows are 180 B and
+// 192 B, so per-thread access would scatter every load and store across 32
+// rows; the warp moves its 32 rows as one contiguous block instead.
+#include "exact_math.cuh"
+#include "kernels.cuh"
+
+namespace mg {
+
+namespace {
+
+constexpr int kBwdBlock = 128;
+constexpr int kRowBlock = 48;  // floats staged per Gaussian (16 rows x 3)
+
+__device__ __forceinline__ void sh_basis_grad(int b, float x, float y, float z, float& gx,
+                                              float& gy, float& gz) {
+    const float xx = x * x, yy = y * y, zz = z * z;
+    switch (b) {
+        case 1: gx = 0.f; gy = -MG_SH_C1; gz = 0.f; break;
+        case 2: gx = 0.f; gy = 0.f; gz = MG_SH_C1; break;
+        case 3: gx = -MG_SH_C1; gy = 0.f; gz = 0.f; break;
+        case 4: gx = MG_SH_C2_0 * y; gy = MG_SH_C2_0 * x; gz = 0.f; break;
+        case 5: gx = 0.f; gy = MG_SH_C2_1 * z; gz = MG_SH_C2_1 * y; break;
+        case 6: gx = MG_SH_C2_2 * (-2.f * x); gy = MG_SH_C2_2 * (-2.f * y); gz = MG_SH_C2_2 * (4.f * z); break;
+        case 7: gx = MG_SH_C2_3 * z; gy = 0.f; gz = MG_SH_C2_3 * x; break;
+        case 8: gx = MG_SH_C2_4 * (2.f * x); gy = MG_SH_C2_4 * (-2.f * y); gz = 0.f; break;
+        case 9: gx = MG_SH_C3_0 * (6.f * x * y); gy = MG_SH_C3_0 * (3.f * xx - 3.f * yy); gz = 0.f; break;
+        case 10: gx = MG_SH_C3_1 * (y * z); gy = MG_SH_C3_1 * (x * z); gz = MG_SH_C3_1 * (x * y); break;
+        case 11: gx = MG_SH_C3_2 * (-2.f * x * y); gy = MG_SH_C3_2 * (4.f * zz - xx - 3.f * yy); gz = MG_SH_C3_2 * (8.f * y * z); break;
+        case 12: gx = MG_SH_C3_3 * (-6.f * x * z); gy = MG_SH_C3_3 * (-6.f * y * z); gz = MG_SH_C3_3 * (6.f * zz - 3.f * xx - 3.f * yy); break;
+        case 13: gx = MG_SH_C3_4 * (4.f * zz - 3.f * xx - yy); gy = MG_SH_C3_4 * (-2.f * x * y); gz = MG_SH_C3_4 * (8.f * x * z); break;
+        case 14: gx = MG_SH_C3_5 * (2.f * x * z); gy = MG_SH_C3_5 * (-2.f * y * z); gz = MG_SH_C3_5 * (xx - yy); break;
+        case 15: gx = MG_SH_C3_6 * (3.f * xx - 3.f * yy); gy = MG_SH_C3_6 * (-6.f * x * y); gz = 0.f; break;
+        default: gx = gy = gz = 0.f;
+    }
+}
+
+// The warp's SH block: row r (0 = DC, 1..15 = bands 1+) of lane `lane`.
+struct ShBlock {
+    float* s;        // shared memory, 32 x kRowBlock floats
+    bool fused;      // fused: rows 0..15 staged; split: rows 1..15 staged
+    __device__ __forceinline__ float* row(int lane, int r) const {
+        return s + lane * kRowBlock + (fused ? r : r - 1) * 3;
+    }
+};
+
+__global__ void __launch_bounds__(kBwdBlock)
+preprocess_backward_kernel(const float* __restrict__ means, const float* __restrict__ quats,
+                           const float* __restrict__ scales, const float* __restrict__ sh_dc,
+                           const float* __restrict__ sh_rest, mg_sh_layout shl,
+                           const float* __restrict__ d_uv, int64_t d_uv_stride,
+                           const float* __restrict__ d_conic, int64_t d_conic_stride,
+                           const float* __restrict__ d_color, int64_t d_color_stride,
+                           const int32_t* __restrict__ valid, CamParams P, int sh_degree,
+                           int64_t n, float* __restrict__ d_means,
+                           float* __restrict__ d_quats, float* __restrict__ d_scales,
+                           float* __restrict__ d_sh_dc, float* __restrict__ d_sh_rest,
+                           int fused, int contiguous_rest) {
+    __shared__ float s_sh[kBwdBlock / 32][32 * kRowBlock];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
+    const int64_t g0 = g - lane;
+    const bool in = g < n;
+    const int64_t warp_n = min((int64_t)32, n - g0);
+
+    float mx = 0.f, my = 0.f, mz = 0.f;
+    if (in) { mx = means[3 * g]; my = means[3 * g + 1]; mz = means[3 * g + 2]; }
+    float dmx = 0.f, dmy = 0.f, dmz = 0.f;
+
+    // ---------------------------------------------------------- SH branch
+    const bool do_sh = sh_degree >= 0 && d_color != nullptr && sh_dc != nullptr;
+    if (do_sh) {
+        const ShBlock blk{s_sh[wib], fused != 0};
+        const int nb = (sh_degree + 1) * (sh_degree + 1);
+        float dcr = 0.f, dcg = 0.f, dcb = 0.f;
+        if (in) {
+            dcr = d_color[g * d_color_stride];
+            dcg = d_color[g * d_color_stride + 1];
+            dcb = d_color[g * d_color_stride + 2];
+        }
+        const bool need = in && !(dcr == 0.f && dcg == 0.f && dcb == 0.f);
+        const bool staged = (fused != 0) || (contiguous_rest != 0);
+        const unsigned any_need = __ballot_sync(0xffffffffu, need);
+        // Stage coefficient rows (only when some lane reads them).
+        if (staged && any_need) {
+            const int per_g = fused ? 48 : 45;
+            const float* src = fused ? sh_dc + g0 * 48 : sh_rest + g0 * 45;
+            const int total = (int)warp_n * per_g;
+            for (int i = lane; i < total; i += 32)
+                blk.s[(i / per_g) * kRowBlock + (i % per_g)] = __ldg(src + i);
+        }
+        __syncwarp();
+        // Row writer: the split layout's DC row goes straight to global memory
+        // (12 B per Gaussian, coalesced across the warp); staged rows go to the
+        // shared block; the rare unstaged layout writes in place.
+        auto wr = [&](int i, float r0, float r1, float r2) {
+            float* r;
+            if (i == 0 && !blk.fused) r = d_sh_dc + g * (int64_t)shl.stride_dc * 3;
+            else if (staged) r = blk.row(lane, i);
+            else r = (i == 0) ? d_sh_dc + g * (int64_t)shl.stride_dc * 3
+                              : d_sh_rest + (g * (int64_t)shl.stride_rest + shl.offset_rest + (i - 1)) * 3;
+            r[0] = r0; r[1] = r1; r[2] = r2;
+        };
+        if (need) {
+            auto rd = [&](int i, int c) -> float {
+                if (i == 0) return sh_dc[g * (int64_t)shl.stride_dc * 3 + c];
+                if (staged) return blk.row(lane, i)[c];
+                return sh_rest[(g * (int64_t)shl.stride_rest + shl.offset_rest + (i - 1)) * 3 + c];
+            };
+            const float dvx = mx - P.ccx, dvy = my - P.ccy, dvz = mz - P.ccz;
+            const float len = fmaxf(sqrtf(dvx * dvx + dvy * dvy + dvz * dvz), 1e-12f);
+            const float x = dvx / len, y = dvy / len, z = dvz / len;
+            float B[16];
+            sh_basis(sh_degree, x, y, z, B);
+            float pr = 0.f, pg = 0.f, pb = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (i < nb) { pr += B[i] * rd(i, 0); pg += B[i] * rd(i, 1); pb += B[i] * rd(i, 2); }
+            }
+            pr += 0.5f; pg += 0.5f; pb += 0.5f;
+            const float er = pr > 0.f ? dcr : 0.f;
+            const float eg = pg > 0.f ? dcg : 0.f;
+            const float eb = pb > 0.f ? dcb : 0.f;
+            float ddx = 0.f, ddy = 0.f, ddz = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (i < nb) {
+                    float gx, gy, gz;
+                    sh_basis_grad(i, x, y, z, gx, gy, gz);
+                    const float k = rd(i, 0) * er + rd(i, 1) * eg + rd(i, 2) * eb;
+                    ddx += gx * k; ddy += gy * k; ddz += gz * k;
+                    wr(i, B[i] * er, B[i] * eg, B[i] * eb);  // after this row's reads
+                } else {
+                    wr(i, 0.f, 0.f, 0.f);
+                }
+            }
+            // dir = v/|v|: d v = (I - dir dir^T) d dir / |v|
+            const float dd = x * ddx + y * ddy + z * ddz;
+            dmx += (ddx - x * dd) / len;
+            dmy += (ddy - y * dd) / len;
+            dmz += (ddz - z * dd) / len;
+        } else if (in) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) wr(i, 0.f, 0.f, 0.f);
+        }
+        __syncwarp();
+        if (staged) {
+            const int per_g = fused ? 48 : 45;
+            float* dst = fused ? d_sh_dc + g0 * 48 : d_sh_rest + g0 * 45;
+            const int total = (int)warp_n * per_g;
+            for (int i = lane; i < total; i += 32)
+                dst[i] = blk.s[(i / per_g) * kRowBlock + (i % per_g)];
+        }
+    }
+    if (!in) return;
+
+    // --------------------------------------------------- projection branch
+    if (valid[g] != 0) {
+        const float fx = P.fx, fy = P.fy;
+        const float pcx = P.R0.x * mx + P.R0.y * my + P.R0.z * mz + P.R0.w;
+        const float pcy = P.R1.x * mx + P.R1.y * my + P.R1.z * mz + P.R1.w;
+        const float pcz = P.R2.x * mx + P.R2.y * my + P.R2.z * mz + P.R2.w;
+        const float z = pcz, zc = fmaxf(z, P.near_plane);
+        const float izc = 1.0f / zc, izc2 = izc * izc;
+        const float lim_x = 1.3f * (0.5f * (float)P.W / fx);
+        const float lim_y = 1.3f * (0.5f * (float)P.H / fy);
+        const float txn = pcx / zc, tyn = pcy / zc;
+        const bool clx = (txn < -lim_x) || (txn > lim_x);
+        const bool cly = (tyn < -lim_y) || (tyn > lim_y);
+        const float tx = clampf(txn, -lim_x, lim_x) * zc;
+        const float ty = clampf(tyn, -lim_y, lim_y) * zc;
+
+        const float4 q4 = reinterpret_cast<const float4*>(quats)[g];
+        const float qn = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+        const float qd = fmaxf(qn, 1e-12f);
+        const float w = q4.x / qd, x = q4.y / qd, y = q4.z / qd, zq = q4.w / qd;
+        float R[3][3];
+        R[0][0] = 1.f - 2.f * (y * y + zq * zq); R[0][1] = 2.f * (x * y - w * zq); R[0][2] = 2.f * (x * zq + w * y);
+        R[1][0] = 2.f * (x * y + w * zq); R[1][1] = 1.f - 2.f * (x * x + zq * zq); R[1][2] = 2.f * (y * zq - w * x);
+        R[2][0] = 2.f * (x * zq - w * y); R[2][1] = 2.f * (y * zq + w * x); R[2][2] = 1.f - 2.f * (x * x + y * y);
+        const float s[3] = {scales[3 * g], scales[3 * g + 1], scales[3 * g + 2]};
+        float M[3][3], S[3][3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) M[i][j] = R[i][j] * s[j];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) S[i][j] = M[i][0] * M[j][0] + M[i][1] * M[j][1] + M[i][2] * M[j][2];
+
+        const float Rw[3][3] = {{P.R0.x, P.R0.y, P.R0.z}, {P.R1.x, P.R1.y, P.R1.z},
+                                {P.R2.x, P.R2.y, P.R2.z}};
+        const float J0x = fx * izc, J0z = -fx * tx * izc2;
+        const float J1y = fy * izc, J1z = -fy * ty * izc2;
+        float T0[3], T1[3], ST0[3], ST1[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            T0[k] = J0x * Rw[0][k] + J0z * Rw[2][k];
+            T1[k] = J1y * Rw[1][k] + J1z * Rw[2][k];
+        }
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            ST0[i] = S[i][0] * T0[0] + S[i][1] * T0[1] + S[i][2] * T0[2];
+            ST1[i] = S[i][0] * T1[0] + S[i][1] * T1[1] + S[i][2] * T1[2];
+        }
+        const float a = T0[0] * ST0[0] + T0[1] * ST0[1] + T0[2] * ST0[2] + P.blur;
+        const float b = T0[0] * ST1[0] + T0[1] * ST1[1] + T0[2] * ST1[2];
+        const float c = T1[0] * ST1[0] + T1[1] * ST1[1] + T1[2] * ST1[2] + P.blur;
+        const float det = a * c - b * b;
+        const float dets = fmaxf(det, 1e-12f);
+        const float id = 1.0f / dets;
+
+        const float dcx = d_conic[g * d_conic_stride];
+        const float dcy = d_conic[g * d_conic_stride + 1];
+        const float dcz = d_conic[g * d_conic_stride + 2];
+        const float ddet = -(dcx * c - dcy * b + dcz * a) * id * id;
+        float da = dcz * id + ddet * c;
+        float db = -dcy * id - 2.0f * ddet * b;
+        float dc = dcx * id + ddet * a;
+        if (det <= 1e-12f) { da = db = dc = 0.f; }
+
+        // dSigma (unsymmetrised) = da T0 T0^T + db T0 T1^T + dc T1 T1^T
+        float dS[3][3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+                dS[i][j] = da * T0[i] * T0[j] + db * T0[i] * T1[j] + dc * T1[i] * T1[j];
+        float dT0[3], dT1[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            dT0[k] = 2.0f * (da * ST0[k]) + db * ST1[k];
+            dT1[k] = 2.0f * (dc * ST1[k]) + db * ST0[k];
+        }
+        float dJ0[3], dJ1[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            dJ0[r] = dT0[0] * Rw[r][0] + dT0[1] * Rw[r][1] + dT0[2] * Rw[r][2];
+            dJ1[r] = dT1[0] * Rw[r][0] + dT1[1] * Rw[r][1] + dT1[2] * Rw[r][2];
+        }
+        const float dtx = -fx * izc2 * dJ0[2];
+        const float dty = -fy * izc2 * dJ1[2];
+        float dzc = -fx * izc2 * dJ0[0] - fy * izc2 * dJ1[1] +
+                    2.0f * fx * tx * izc2 * izc * dJ0[2] + 2.0f * fy * ty * izc2 * izc * dJ1[2];
+        const float dux = d_uv[g * d_uv_stride], duy = d_uv[g * d_uv_stride + 1];
+        float dpx = fx * izc * dux;
+        float dpy = fy * izc * duy;
+        dzc += -fx * pcx * izc2 * dux - fy * pcy * izc2 * duy;
+        if (!clx) dpx += dtx; else dzc += dtx * (tx * izc);
+        if (!cly) dpy += dty; else dzc += dty * (ty * izc);
+        const float dpz = (z > P.near_plane) ? dzc : 0.0f;
+        dmx += Rw[0][0] * dpx + Rw[1][0] * dpy + Rw[2][0] * dpz;
+        dmy += Rw[0][1] * dpx + Rw[1][1] * dpy + Rw[2][1] * dpz;
+        dmz += Rw[0][2] * dpx + Rw[1][2] * dpy + Rw[2][2] * dpz;
+
+        // dM = 2 sym(dSigma) M
+        float dM[3][3];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                float acc = 0.f;
+#pragma unroll
+                for (int k = 0; k < 3; ++k) acc += 0.5f * (dS[i][k] + dS[k][i]) * M[k][j];
+                dM[i][j] = 2.0f * acc;
+            }
+        d_scales[3 * g + 0] = dM[0][0] * R[0][0] + dM[1][0] * R[1][0] + dM[2][0] * R[2][0];
+        d_scales[3 * g + 1] = dM[0][1] * R[0][1] + dM[1][1] * R[1][1] + dM[2][1] * R[2][1];
+        d_scales[3 * g + 2] = dM[0][2] * R[0][2] + dM[1][2] * R[1][2] + dM[2][2] * R[2][2];
+        float G[3][3];  // dL/dR
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) G[i][j] = dM[i][j] * s[j];
+        const float dw = 2.f * (x * (G[2][1] - G[1][2]) + y * (G[0][2] - G[2][0]) + zq * (G[1][0] - G[0][1]));
+        const float dqx = 2.f * (w * (G[2][1] - G[1][2]) + y * (G[1][0] + G[0][1]) + zq * (G[2][0] + G[0][2]) - 2.f * x * (G[1][1] + G[2][2]));
+        const float dqy = 2.f * (w * (G[0][2] - G[2][0]) + x * (G[1][0] + G[0][1]) + zq * (G[2][1] + G[1][2]) - 2.f * y * (G[0][0] + G[2][2]));
+        const float dqz = 2.f * (w * (G[1][0] - G[0][1]) + x * (G[2][0] + G[0][2]) + y * (G[2][1] + G[1][2]) - 2.f * zq * (G[0][0] + G[1][1]));
+        const float qdot = w * dw + x * dqx + y * dqy + zq * dqz;
+        reinterpret_cast<float4*>(d_quats)[g] =
+            make_float4((dw - w * qdot) / qd, (dqx - x * qdot) / qd, (dqy - y * qdot) / qd,
+                        (dqz - zq * qdot) / qd);
+    } else {
+        d_scales[3 * g + 0] = 0.f; d_scales[3 * g + 1] = 0.f; d_scales[3 * g + 2] = 0.f;
+        reinterpret_cast<float4*>(d_quats)[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    d_means[3 * g + 0] = dmx;
+    d_means[3 * g + 1] = dmy;
+    d_means[3 * g + 2] = dmz;
+}
+
+}  // namespace
+
+}  // namespace mg
+
+using namespace mg;
+
+extern "C" mg_status mg_preprocess_backward(
+    const float* means, const float* quats, const float* scales, const float* sh_dc,
+    const float* sh_rest, mg_sh_layout shl, const float* d_uv, int64_t d_uv_stride,
+    const float* d_conic, int64_t d_conic_stride, const float* d_color,
+    int64_t d_color_stride, const int32_t* valid, const mg_camera* cam, int32_t sh_degree,
+    int64_t n, float* d_means, float* d_quats, float* d_scales, float* d_sh_dc,
+    float* d_sh_rest, mg_stream_t stream) {
+    MG_REQUIRE(cam != nullptr, "preprocess_backward: null camera");
+    MG_REQUIRE(sh_degree <= 3, "preprocess_backward: sh_degree must be <= 3");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(means && quats && scales && d_uv && d_conic && valid && d_means && d_quats &&
+                   d_scales,
+               "preprocess_backward: null pointer");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(d_quats) & 15u) == 0u,
+               "preprocess_backward: quats must be 16-byte aligned");
+    const bool fused = shl.stride_dc == 16 && shl.stride_rest == 16 && shl.offset_rest == 1;
+    const bool split = shl.stride_dc == 1 && shl.stride_rest == 15 && shl.offset_rest == 0;
+    if (sh_degree >= 0 && d_color != nullptr) {
+        MG_REQUIRE(fused || split,
+                   "SH must be either one (N,16,3) tensor or (N,1,3)+(N,15,3)");
+        MG_REQUIRE(sh_dc && sh_rest && d_sh_dc && d_sh_rest,
+                   "preprocess_backward: null SH pointer");
+        if (fused)
+            MG_REQUIRE(sh_rest == sh_dc && d_sh_rest == d_sh_dc,
+                       "preprocess_backward: the fused SH layout passes one tensor twice");
+    }
+    const CamParams P = make_cam_params(*cam);
+    preprocess_backward_kernel<<<ceil_div(n, kBwdBlock), kBwdBlock, 0,
+                                 reinterpret_cast<cudaStream_t>(stream)>>>(
+        means, quats, scales, sh_dc, sh_rest, shl, d_uv, d_uv_stride, d_conic, d_conic_stride,
+        d_color, d_color_stride, valid, P, sh_degree, n, d_means, d_quats, d_scales, d_sh_dc,
+        d_sh_rest, fused ? 1 : 0, split ? 1 : 0);
+    return check_launch("preprocess_backward");
+}

@@ -1,0 +1,479 @@
+// Stable LSD radix sort (onesweep form), the gathered exclusive scan and the
+// per-tile range extraction used by the binning.
+//
+// Onesweep: one histogram kernel counts the digits of every pass at once;
+// then each 8-bit pass is ONE kernel that reads each key/value once, ranks it
+// inside its CTA tile, learns the tile's global offset per digit through a
+// decoupled look-back over the previous tiles, and writes each key/value
+// once. Tiles are claimed through an atomic counter, so a CTA only ever waits
+// for tiles already claimed by running CTAs; every wait is bounded and a
+// timeout records DEV_ERR_SORT_LOOKBACK_TIMEOUT in the device error word
+// instead of hanging.
+//
+// Ranking is stable: a warp ranks its 32 x ITEMS keys in input order with
+// __match_any_sync peer groups and warp-private counters; warps are combined
+// in warp order, tiles in tile order, so equal digits keep their input order
+// and the sort is stable across passes.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace mg {
+
+namespace {
+
+constexpr int kRadixBits = 8;
+constexpr int kRadix = 1 << kRadixBits;
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+
+template <typename K> struct SortTraits;
+template <> struct SortTraits<uint32_t> { static constexpr int kItems = 16; };
+template <> struct SortTraits<uint64_t> { static constexpr int kItems = 10; };
+
+template <typename K>
+__host__ __device__ constexpr int tile_keys() { return kSortThreads * SortTraits<K>::kItems; }
+
+constexpr uint32_t kFlagAgg = 1u << 30;
+constexpr uint32_t kFlagInc = 2u << 30;
+constexpr uint32_t kCountMask = (1u << 30) - 1u;
+constexpr uint32_t kLookbackSpinLimit = 1u << 22;
+
+struct SortScratch {
+    uint32_t* hist;           // passes x 256: histogram, then exclusive offsets
+    uint32_t* tile_counter;   // passes
+    uint32_t* status;         // passes x tiles x 256 look-back words
+    int tiles;
+    int passes;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+SortScratch carve(void* base, int64_t n, int bits, int key_bytes) {
+    SortScratch s;
+    s.passes = (bits + kRadixBits - 1) / kRadixBits;
+    const int tk = key_bytes == 4 ? tile_keys<uint32_t>() : tile_keys<uint64_t>();
+    s.tiles = (int)std::max<int64_t>(1, (n + tk - 1) / tk);
+    char* p = static_cast<char*>(base);
+    s.hist = reinterpret_cast<uint32_t*>(p);
+    p += align256(sizeof(uint32_t) * kRadix * s.passes);
+    s.tile_counter = reinterpret_cast<uint32_t*>(p);
+    p += align256(sizeof(uint32_t) * s.passes);
+    s.status = reinterpret_cast<uint32_t*>(p);
+    return s;
+}
+
+size_t sort_scratch_size(int64_t n, int bits, int key_bytes) {
+    const int passes = (bits + kRadixBits - 1) / kRadixBits;
+    const int tk = key_bytes == 4 ? tile_keys<uint32_t>() : tile_keys<uint64_t>();
+    const int64_t tiles = std::max<int64_t>(1, (n + tk - 1) / tk);
+    return align256(sizeof(uint32_t) * kRadix * passes) +
+           align256(sizeof(uint32_t) * passes) +
+           align256(sizeof(uint32_t) * (size_t)tiles * kRadix * passes);
+}
+
+template <typename K>
+__device__ __forceinline__ uint32_t digit_of(K key, int shift, uint32_t mask) {
+    return (uint32_t)(key >> shift) & mask;
+}
+
+// Digit histograms of all passes in one read of the keys.
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads)
+radix_histogram_kernel(const K* __restrict__ keys, int64_t n, int bits, int passes,
+                       uint32_t* __restrict__ hist) {
+    __shared__ uint32_t s_hist[8][kRadix];
+    for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads)
+        s_hist[i / kRadix][i % kRadix] = 0u;
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * kSortThreads + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * kSortThreads) {
+        const K k = keys[i];
+        for (int p = 0; p < passes; ++p) {
+            const int shift = p * kRadixBits;
+            const int db = min(kRadixBits, bits - shift);
+            atomicAdd(&s_hist[p][digit_of(k, shift, (1u << db) - 1u)], 1u);
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) {
+        const uint32_t c = s_hist[i / kRadix][i % kRadix];
+        if (c) atomicAdd(&hist[i], c);
+    }
+}
+
+// Exclusive scan of each pass's 256 digit counts (one CTA per pass).
+__global__ void __launch_bounds__(kRadix) radix_offsets_kernel(uint32_t* hist) {
+    __shared__ uint32_t s[kRadix];
+    uint32_t* h = hist + blockIdx.x * kRadix;
+    const int t = threadIdx.x;
+    const uint32_t v = h[t];
+    s[t] = v;
+    __syncthreads();
+    for (int off = 1; off < kRadix; off <<= 1) {
+        const uint32_t add = t >= off ? s[t - off] : 0u;
+        __syncthreads();
+        s[t] += add;
+        __syncthreads();
+    }
+    h[t] = s[t] - v;
+}
+
+template <typename K>
+struct OnesweepSmem {
+    K keys[tile_keys<K>()];
+    uint32_t vals[tile_keys<K>()];
+    uint32_t warp_hist[kSortWarps][kRadix];
+    uint32_t local_start[kRadix];
+    uint32_t bin_offset[kRadix];
+    uint32_t tile_id;
+};
+
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads)
+onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+                     K* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
+                     int64_t n, int shift, int digit_bits,
+                     const uint32_t* __restrict__ digit_offsets,
+                     uint32_t* __restrict__ tile_counter, uint32_t* status,
+                     int32_t* err_word) {
+    constexpr int ITEMS = SortTraits<K>::kItems;
+    constexpr int TK = tile_keys<K>();
+    __shared__ OnesweepSmem<K> sm;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t mask = (1u << digit_bits) - 1u;
+
+    for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads)
+        (&sm.warp_hist[0][0])[i] = 0u;
+    if (tid == 0) sm.tile_id = atomicAdd(tile_counter, 1u);
+    __syncthreads();
+    const uint32_t tile = sm.tile_id;
+    const int64_t base = (int64_t)tile * TK;
+
+    // Warp w owns input slots [w*32*ITEMS, (w+1)*32*ITEMS) of the tile; item i
+    // of lane l is slot i*32 + l inside it, so (i, l) order is input order.
+    K key[ITEMS];
+    uint32_t val[ITEMS];
+    uint32_t rank[ITEMS];
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const int64_t idx = base + (int64_t)warp * 32 * ITEMS + i * 32 + lane;
+        if (idx < n) {
+            key[i] = keys_in[idx];
+            val[i] = vals_in[idx];
+        } else {
+            key[i] = ~(K)0;  // max digit: ranks after every real key of the tile
+            val[i] = 0u;
+        }
+    }
+    const unsigned lt_mask = (1u << lane) - 1u;
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t d = digit_of(key[i], shift, mask);
+        const unsigned peers = __match_any_sync(0xffffffffu, d);
+        const int leader = __ffs(peers) - 1;
+        uint32_t before = 0u;
+        if (lane == leader) {
+            before = sm.warp_hist[warp][d];
+            sm.warp_hist[warp][d] = before + (uint32_t)__popc(peers);
+        }
+        before = __shfl_sync(0xffffffffu, before, leader);
+        rank[i] = before + (uint32_t)__popc(peers & lt_mask);
+        __syncwarp();
+    }
+    __syncthreads();
+
+    // Per digit (one thread each): warp offsets inside the tile, tile count.
+    const int d = tid;
+    uint32_t tile_count = 0u;
+    for (int w = 0; w < kSortWarps; ++w) {
+        const uint32_t c = sm.warp_hist[w][d];
+        sm.warp_hist[w][d] = tile_count;
+        tile_count += c;
+    }
+    // Publish this tile's aggregate first so successors can proceed.
+    uint32_t* my_status = status + (int64_t)tile * kRadix + d;
+    if (tile == 0) {
+        atomicExch(my_status, kFlagInc | tile_count);
+    } else {
+        atomicExch(my_status, kFlagAgg | tile_count);
+    }
+    // Exclusive scan of tile counts over digits -> local layout.
+    sm.local_start[d] = tile_count;
+    __syncthreads();
+    for (int off = 1; off < kRadix; off <<= 1) {
+        const uint32_t add = d >= off ? sm.local_start[d - off] : 0u;
+        __syncthreads();
+        sm.local_start[d] += add;
+        __syncthreads();
+    }
+    sm.local_start[d] -= tile_count;
+
+    // Decoupled look-back over previous tiles for this digit.
+    uint32_t excl = 0u;
+    if (tile > 0) {
+        int64_t t = (int64_t)tile - 1;
+        uint32_t spins = 0u;
+        while (t >= 0) {
+            const uint32_t s = *(volatile uint32_t*)(status + t * kRadix + d);
+            const uint32_t flag = s & ~kCountMask;
+            if (flag == 0u) {
+                if (++spins > kLookbackSpinLimit) {
+                    record_device_error(err_word, DEV_ERR_SORT_LOOKBACK_TIMEOUT);
+                    break;
+                }
+                continue;
+            }
+            excl += s & kCountMask;
+            if (flag == kFlagInc) break;
+            --t;
+        }
+        atomicExch(my_status, kFlagInc | ((excl + tile_count) & kCountMask));
+    }
+    sm.bin_offset[d] = digit_offsets[d] + excl;
+    __syncthreads();
+
+    // Scatter into shared memory in tile-sorted order...
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const uint32_t dd = digit_of(key[i], shift, mask);
+        const uint32_t pos = sm.local_start[dd] + sm.warp_hist[warp][dd] + rank[i];
+        sm.keys[pos] = key[i];
+        sm.vals[pos] = val[i];
+    }
+    __syncthreads();
+    // ...and write out; consecutive positions of a digit run are consecutive
+    // in the output. Padding keys land at output positions >= n.
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+        const int p = i * kSortThreads + tid;
+        const K k = sm.keys[p];
+        const uint32_t dd = digit_of(k, shift, mask);
+        const int64_t out = (int64_t)sm.bin_offset[dd] + (p - (int)sm.local_start[dd]);
+        if (out < n) {
+            keys_out[out] = k;
+            vals_out[out] = sm.vals[p];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ scan
+
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 4;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ uint32_t gathered(const uint32_t* counts,
+                                             const uint32_t* order, int64_t i,
+                                             int64_t n) {
+    if (i >= n) return 0u;
+    return order ? counts[order[i]] : counts[i];
+}
+
+__device__ __forceinline__ unsigned long long block_sum_ull(unsigned long long v,
+                                                            unsigned long long* s_warp) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) s_warp[w] = v;
+    __syncthreads();
+    unsigned long long t = 0ull;
+    if (threadIdx.x < 32) {
+        t = threadIdx.x < (blockDim.x >> 5) ? s_warp[threadIdx.x] : 0ull;
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    }
+    return t;  // valid in warp 0
+}
+
+__global__ void __launch_bounds__(kScanThreads)
+scan_reduce_kernel(const uint32_t* __restrict__ counts, const uint32_t* __restrict__ order,
+                   int64_t n, unsigned long long* __restrict__ partials) {
+    __shared__ unsigned long long s_warp[32];
+    const int64_t base = (int64_t)blockIdx.x * kScanTile;
+    unsigned long long v = 0ull;
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i)
+        v += gathered(counts, order, base + i * kScanThreads + threadIdx.x, n);
+    const unsigned long long t = block_sum_ull(v, s_warp);
+    if (threadIdx.x == 0) partials[blockIdx.x] = t;
+}
+
+// Exclusive scan of the per-block partials in place, one CTA, any length.
+__global__ void __launch_bounds__(kScanThreads)
+scan_partials_kernel(unsigned long long* partials, int nblocks) {
+    __shared__ unsigned long long s[kScanThreads];
+    __shared__ unsigned long long carry;
+    if (threadIdx.x == 0) carry = 0ull;
+    __syncthreads();
+    for (int base = 0; base < nblocks; base += kScanThreads) {
+        const int i = base + threadIdx.x;
+        const unsigned long long v = i < nblocks ? partials[i] : 0ull;
+        s[threadIdx.x] = v;
+        __syncthreads();
+        for (int off = 1; off < kScanThreads; off <<= 1) {
+            const unsigned long long add = threadIdx.x >= off ? s[threadIdx.x - off] : 0ull;
+            __syncthreads();
+            s[threadIdx.x] += add;
+            __syncthreads();
+        }
+        if (i < nblocks) partials[i] = carry + s[threadIdx.x] - v;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += s[kScanThreads - 1];
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kScanThreads)
+scan_downsweep_kernel(const uint32_t* __restrict__ counts, const uint32_t* __restrict__ order,
+                      int64_t n, const unsigned long long* __restrict__ partials,
+                      uint32_t* __restrict__ out, int64_t* __restrict__ total_dev) {
+    __shared__ unsigned long long s_warp[32];
+    const int64_t base = (int64_t)blockIdx.x * kScanTile;
+    // Blocked arrangement: thread t owns items [t*4, t*4+4) of the tile.
+    uint32_t v[kScanItems];
+    unsigned long long local = 0ull;
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i) {
+        v[i] = gathered(counts, order, base + threadIdx.x * kScanItems + i, n);
+        local += v[i];
+    }
+    // Block-wide exclusive scan of the per-thread sums.
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    unsigned long long incl = local;
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+        unsigned long long x = lane < (kScanThreads >> 5) ? s_warp[lane] : 0ull;
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        s_warp[lane] = x;  // inclusive over warps
+    }
+    __syncthreads();
+    unsigned long long run = partials[blockIdx.x] + (w > 0 ? s_warp[w - 1] : 0ull) +
+                             (incl - local);
+#pragma unroll
+    for (int i = 0; i < kScanItems; ++i) {
+        const int64_t idx = base + threadIdx.x * kScanItems + i;
+        if (idx < n) out[idx] = (uint32_t)run;
+        run += v[i];
+    }
+    if (blockIdx.x == gridDim.x - 1 && threadIdx.x == kScanThreads - 1)
+        *total_dev = (int64_t)run;
+}
+
+// ------------------------------------------------------------- tile ranges
+
+__device__ __forceinline__ int64_t tile_at(const uint32_t* tiles, const uint64_t* keys64,
+                                           int64_t i) {
+    return tiles ? (int64_t)tiles[i] : (int64_t)(keys64[i] >> 32);
+}
+
+__global__ void tile_ranges_kernel(const uint32_t* __restrict__ tiles,
+                                   const uint64_t* __restrict__ keys64, int64_t m,
+                                   int n_tiles, int32_t* __restrict__ offsets) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const int64_t t = min(tile_at(tiles, keys64, i), (int64_t)n_tiles);
+    const int64_t prev = i == 0 ? -1 : min(tile_at(tiles, keys64, i - 1), (int64_t)n_tiles);
+    for (int64_t tt = prev + 1; tt <= t; ++tt) offsets[tt] = (int32_t)i;
+    if (i == m - 1)
+        for (int64_t tt = t + 1; tt <= n_tiles; ++tt) offsets[tt] = (int32_t)m;
+}
+
+}  // namespace
+
+size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes) {
+    return sort_scratch_size(n, bits, key_bytes);
+}
+
+template <typename K>
+mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt,
+                           int64_t n, int bits, void* scratch, size_t scratch_bytes,
+                           bool* result_in_alt, cudaStream_t stream) {
+    *result_in_alt = false;
+    if (n <= 1 || bits <= 0) return MG_OK;
+    if (bits > (int)(8 * sizeof(K)))
+        return fail(MG_ERR_INVALID_ARGUMENT, "sort: bits exceeds the key width");
+    if (n >= (int64_t)kCountMask)
+        return fail(MG_ERR_CAPACITY, "sort: more than 2^30 elements");
+    const size_t need = sort_scratch_size(n, bits, (int)sizeof(K));
+    if (scratch == nullptr || scratch_bytes < need)
+        return fail(MG_ERR_INVALID_ARGUMENT, "sort: scratch buffer too small");
+    SortScratch s = carve(scratch, n, bits, (int)sizeof(K));
+    if (cudaMemsetAsync(scratch, 0, need, stream) != cudaSuccess)
+        return check_launch("sort scratch memset");
+
+    const int hist_blocks = std::min<int64_t>((n + 4095) / 4096, 148 * 4);
+    radix_histogram_kernel<K><<<std::max(1, hist_blocks), kSortThreads, 0, stream>>>(
+        keys, n, bits, s.passes, s.hist);
+    MG_TRY(check_launch("radix_histogram"));
+    radix_offsets_kernel<<<s.passes, kRadix, 0, stream>>>(s.hist);
+    MG_TRY(check_launch("radix_offsets"));
+
+    int32_t* err = device_error_word();
+    K* kin = keys; uint32_t* vin = vals;
+    K* kout = keys_alt; uint32_t* vout = vals_alt;
+    for (int p = 0; p < s.passes; ++p) {
+        const int shift = p * kRadixBits;
+        const int db = std::min(kRadixBits, bits - shift);
+        onesweep_pass_kernel<K><<<s.tiles, kSortThreads, 0, stream>>>(
+            kin, vin, kout, vout, n, shift, db, s.hist + p * kRadix, s.tile_counter + p,
+            s.status + (size_t)p * s.tiles * kRadix, err);
+        MG_TRY(check_launch("onesweep_pass"));
+        std::swap(kin, kout);
+        std::swap(vin, vout);
+    }
+    *result_in_alt = (kin == keys_alt);
+    return MG_OK;
+}
+
+template mg_status radix_sort_pairs<uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*,
+                                              int64_t, int, void*, size_t, bool*,
+                                              cudaStream_t);
+template mg_status radix_sort_pairs<uint64_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*,
+                                              int64_t, int, void*, size_t, bool*,
+                                              cudaStream_t);
+
+size_t scan_scratch_bytes(int64_t n) {
+    const int64_t blocks = std::max<int64_t>(1, (n + kScanTile - 1) / kScanTile);
+    return align256(sizeof(unsigned long long) * blocks);
+}
+
+mg_status exclusive_scan_gather(const uint32_t* counts, const uint32_t* order, int64_t n,
+                                uint32_t* out, int64_t* total_dev, void* scratch,
+                                cudaStream_t stream) {
+    if (n == 0) {
+        if (cudaMemsetAsync(total_dev, 0, sizeof(int64_t), stream) != cudaSuccess)
+            return check_launch("scan total memset");
+        return MG_OK;
+    }
+    const int blocks = ceil_div(n, kScanTile);
+    auto* partials = static_cast<unsigned long long*>(scratch);
+    scan_reduce_kernel<<<blocks, kScanThreads, 0, stream>>>(counts, order, n, partials);
+    MG_TRY(check_launch("scan_reduce"));
+    scan_partials_kernel<<<1, kScanThreads, 0, stream>>>(partials, blocks);
+    MG_TRY(check_launch("scan_partials"));
+    scan_downsweep_kernel<<<blocks, kScanThreads, 0, stream>>>(counts, order, n, partials,
+                                                              out, total_dev);
+    return check_launch("scan_downsweep");
+}
+
+mg_status launch_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64, int64_t m,
+                             int n_tiles, int32_t* offsets, cudaStream_t stream) {
+    if (m == 0) {
+        if (cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (n_tiles + 1), stream) !=
+            cudaSuccess)
+            return check_launch("tile_ranges memset");
+        return MG_OK;
+    }
+    tile_ranges_kernel<<<ceil_div(m, 256), 256, 0, stream>>>(tile_ids, keys64, m, n_tiles,
+                                                             offsets);
+    return check_launch("tile_ranges");
+}
+
+}  // namespace mg
