@@ -1,0 +1,462 @@
+"""Benchmark: train steps/s of the metal-gauss training hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json's metric is quoted on it, configs[2]): 1M Gaussians
+near the surfaces of 20 random ellipsoids, SH degree 3, 800x800, cameras on a
+radius-4 hemisphere; one step = a batch of 8 views (sharded over the N GPUs)
+rendered, lossed (0.8 L1 + 0.2 (1 - SSIM) against seeded U[0,1] targets) and
+back-propagated, the gradient all-reduced over NCCL, then selective Adam on the
+union-visible Gaussians. Inputs are seeded synthetic data of those shapes; the
+reference's datasets are not available here.
+
+`value` is whole-job steps/s with every input resident in HBM (K steps timed
+with CUDA events, max over ranks). `e2e` is the same metric through the public
+API (engine.Trainer.train_step) with the targets copied host->device from
+pinned memory every step and the loss read back every step. `--impl
+reference` times the reference's algorithm on the host cores (the CPU oracle,
+all threads) on the same workload, one view of each step as the sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("train steps/s (fwd+bwd+Adam) at 800×800, 1M Gaussians, 1/2/4/8 B200; "
+          "% HBM roofline")
+WORKLOAD = ("cfg3: 1M Gaussians near the surfaces of 20 random ellipsoids, SH3, 800x800, "
+            "100 hemisphere cameras, batch of 8 views per step sharded over the GPUs, NCCL "
+            "all-reduce of the flat gradient, selective Adam on union-visible Gaussians")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n-gaussians", type=int, default=1_000_000)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--width", type=int, default=800)
+    ap.add_argument("--height", type=int, default=800)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dense-adam", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=120.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ helpers
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return dict(json.loads(p.read_text()), source="measured")
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the
+    timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if self.path is None or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), sm_max=float(parts[2]),
+                                 power=float(parts[3]), hw=parts[5], hw_th=parts[6],
+                                 sw_th=parts[7], sw_pc=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hw_th", "hw_thermal_slowdown"),
+                              ("sw_th", "sw_thermal_slowdown"), ("sw_pc", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
+                "sm_max_mhz": max(r["sm_max"] for r in rows),
+                "power_w_max": max(r["power"] for r in rows),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------- workload
+
+def workload(args):
+    from metal_gauss_b200 import scenes
+    p, views, spec = scenes.config("cfg3", n=args.n_gaussians, seed=0)
+    if args.width != 800 or args.height != 800:
+        views = scenes.sphere_views(100, 4.0, args.width, args.height, 40.0, 1, hemisphere=True)
+    g = torch.Generator().manual_seed(1234)
+    targets_u8 = [torch.randint(0, 256, (v.height, v.width, 3), dtype=torch.uint8, generator=g)
+                  for v in views]
+    return p, views, spec, targets_u8
+
+
+from metal_gauss_b200.dp import batch_indices, shard  # noqa: E402
+
+
+# ---------------------------------------------------------- algorithmic bytes
+
+def stage_bytes(stage: str, n: int, m: int, P: int, n_tiles: int) -> float:
+    """Compulsory HBM bytes of one launch of a stage (per view), from the
+    dataflow: every input read once, every output written once."""
+    if stage == "raster_bwd":
+        # per pair: id (4) + gathered uv/conic/opacity/colour (36); per pixel:
+        # T, stop, dL/drgb (24); per Gaussian: the 48-byte gradient record
+        return 40.0 * m + 24.0 * P + 48.0 * n
+    if stage == "raster_fwd":
+        return 40.0 * m + 8.0 * n_tiles + 24.0 * P          # + rgb, alpha, T, stop out
+    if stage == "preprocess_fwd":
+        return (44.0 + 192.0 + 48.0) * n
+    if stage == "preprocess_bwd":
+        return (44.0 + 48.0 + 192.0 + 4.0 + 2 * 236.0) * n
+    if stage == "loss":
+        return 40.0 * P + 36.0 * P
+    if stage == "adam":
+        return 28.0 * 59 * n + 8.0 * n
+    return 0.0
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_ours(args, rank, world, local):
+    from metal_gauss_b200 import _lib
+    from metal_gauss_b200.engine import Trainer
+
+    dev = torch.device("cuda", local)
+    p, views, spec, targets_u8 = workload(args)
+    trainer = Trainer(p, dev, sh_degree=3, background=spec["background"],
+                      selective=not args.dense_adam)
+    targets = [t.to(dev).float().div_(255.0) for t in targets_u8]
+    B = args.batch
+    if B % world:
+        raise SystemExit(f"batch {B} is not divisible by {world} GPUs")
+
+    def step(i):
+        idx = shard(batch_indices(i, B, len(views)), rank, world)
+        return trainer.train_step([views[j] for j in idx], [targets[j] for j in idx], B)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    L = _lib.load()
+    launches0 = L.mg_launch_count()
+    trainer.stage_events = {}
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        t0.record()
+        for i in range(args.steps):
+            step(args.warmup + i)
+        t1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = L.mg_launch_count() - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(ms, world)
+    stage_ms = trainer.stage_times_ms()
+    trainer.stage_events = None
+    pairs = [s.pairs for s in trainer.last_stats]
+    loss_val = float(trainer.loss.item())
+
+    # roofline of the dominant single-kernel stage
+    P = args.width * args.height
+    n = trainer.n
+    n_tiles = math.ceil(args.width / 16) * math.ceil(args.height / 16)
+    m_avg = float(np.mean(pairs)) if pairs else 0.0
+    singles = {k: v for k, v in stage_ms.items()
+               if k in ("raster_bwd", "raster_fwd", "preprocess_fwd", "preprocess_bwd", "loss",
+                        "adam")}
+    dom = max(singles, key=lambda k: sum(singles[k]))
+    dom_ms = float(np.mean(singles[dom]))
+    dom_bytes = stage_bytes(dom, n, int(m_avg), P, n_tiles)
+    peaks = measured_peaks()
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "peak_source": peaks["source"], "traffic": None,
+                "bytes_per_launch": dom_bytes, "avg_launch_ms": round(dom_ms, 4)}
+
+    # whole-step algorithmic bytes against the same peak
+    step_bytes = trainer.bytes_per_step([views[0]] * len(trainer.last_stats),
+                                        trainer.last_stats)
+    step_bytes = max_over_ranks(step_bytes, world)
+
+    # ----------------------------------------------------------------- e2e
+    e2e = None
+    if not args.no_e2e:
+        pinned = [t.pin_memory() for t in targets_u8]
+        dev_u8 = [torch.empty_like(t, device=dev) for t in targets_u8[:B]]
+
+        def e2e_step(i):
+            idx = shard(batch_indices(i, B, len(views)), rank, world)
+            tg = []
+            for k, j in enumerate(idx):
+                dev_u8[k].copy_(pinned[j], non_blocking=True)
+                tg.append(dev_u8[k].float().div_(255.0))
+            loss = trainer.train_step([views[j] for j in idx], tg, B)
+            return float(loss.item())                     # device -> host every step
+
+        e2e_step(0)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            e2e_step(args.warmup + args.steps + i)
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+        per_rank_views = B // world
+        e2e = {"value": round(1000.0 / e_ms, 3), "unit": "steps/s", "ms_per_step": round(e_ms, 3),
+               "h2d_bytes_per_step": per_rank_views * args.width * args.height * 3 * world,
+               "d2h_bytes_per_step": 4 * world, "api": "metal_gauss_b200.engine.Trainer.train_step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, p, views, targets_u8)
+
+    if rank == 0:
+        clk = clocks.summary()
+        out = {
+            "metric": METRIC, "value": round(1000.0 / ms, 3), "unit": "steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "n_gaussians": n, "width": args.width,
+                       "height": args.height, "global_batch": B, "views_per_gpu": B // world,
+                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "optimizer": "dense Adam" if args.dense_adam else "selective Adam",
+                       "l2": "no flush: inputs larger than L2 (parameters + Adam state "
+                             f"{3 * 59 * n * 4 / 1e6:.0f} MB, targets {len(targets) * P * 12 / 1e6:.0f} MB)"},
+            "roofline": roofline,
+            "step_hbm": {"algorithmic_bytes": step_bytes,
+                         "achieved_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+                         "frac": round(step_bytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)},
+            "stages_ms": {k: round(float(np.sum(v)) / args.steps, 4) for k, v in stage_ms.items()},
+            "pairs_per_view": int(m_avg), "loss": round(loss_val, 6),
+            "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------- CPU (oracle)
+
+def cpu_view_step(op, params_np, view, target, batch, selective_state=None):
+    """One view of the training step on the host with the CPU oracle: render,
+    loss, backward, activation chain. Returns (loss, grads dict, visible)."""
+    means, quats = params_np["means"], params_np["quats"]
+    scales = np.exp(params_np["log_scales"]).astype(np.float32)
+    opac = (1.0 / (1.0 + np.exp(-params_np["logit_opac"]))).astype(np.float32)
+    rgb, alpha, st = op.render(means, quats, scales, opac, params_np["sh_dc"], view.K.numpy(),
+                               view.viewmat.numpy(), view.width, view.height, sh_degree=3,
+                               sh_rest=params_np["sh_rest"], background=None)
+    loss, grad_rgb = op.l1_ssim_loss(rgb, target)
+    g = op.render_backward(st, (grad_rgb / batch).astype(np.float32), None)
+    grads = {"means": g["means"], "quats": g["quats"], "log_scales": g["scales"] * scales,
+             "logit_opac": g["opacities"] * opac * (1 - opac), "sh_dc": g["sh"],
+             "sh_rest": g["sh_rest"]}
+    return loss / batch, grads, st["pre"]["valid"].astype(bool)
+
+
+def cpu_adam(op, params_np, grads, visible, state, lrs):
+    for name, lr in lrs.items():
+        p = params_np[name]
+        st = state.setdefault(name, (np.zeros_like(p), np.zeros_like(p),
+                                     np.zeros(p.shape[0], np.float32)))
+        op.selective_adam_step(p, np.ascontiguousarray(grads[name], np.float32), st[0], st[1],
+                               st[2], visible, lr)
+
+
+def cpu_baseline(args, p, views, targets_u8, max_views: int = 1) -> dict:
+    """The oracle (the reference's algorithm restated in C, OpenMP over all host
+    cores) on a bounded sample: `max_views` view(s) of the step plus the
+    selective Adam update over all 1M Gaussians; scaled to steps/s of the
+    whole 8-view step."""
+    import oracle as op
+    from metal_gauss_b200.engine import DEFAULT_LRS
+    params_np = {k: np.ascontiguousarray(v.numpy(), np.float32) for k, v in p.items()}
+    t_views = []
+    for j in range(max_views):
+        tgt = (targets_u8[j].numpy().astype(np.float32) / 255.0)
+        t = time.perf_counter()
+        _, grads, vis = cpu_view_step(op, params_np, views[j], tgt, args.batch)
+        t_views.append(time.perf_counter() - t)
+    t = time.perf_counter()
+    cpu_adam(op, params_np, grads, vis.astype(np.uint8), {}, DEFAULT_LRS)
+    t_adam = time.perf_counter() - t
+    t_view = float(np.mean(t_views))
+    step_s = args.batch * t_view + t_adam
+    return {"value": round(1.0 / step_s, 5), "unit": "steps/s", "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"{max_views} of the {args.batch} views of one step (fwd+loss+bwd, "
+                      f"{t_view:.2f} s each) + selective Adam over all "
+                      f"{args.n_gaussians} Gaussians ({t_adam:.2f} s); steps/s = "
+                      f"1 / ({args.batch} x view + Adam)",
+            "cpu_model": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's algorithm (CPU oracle, all host
+    threads) on the same workload and metric. Rank 0 only."""
+    if rank != 0:
+        return
+    import oracle as op
+    from metal_gauss_b200.engine import DEFAULT_LRS
+    op.build()
+    p, views, spec, targets_u8 = workload(args)
+    params_np = {k: np.ascontiguousarray(v.numpy(), np.float32) for k, v in p.items()}
+    state: dict = {}
+    times = []
+    budget_t0 = time.perf_counter()
+    total = args.warmup + args.steps
+    done = 0
+    for i in range(total):
+        j = batch_indices(i, args.batch, len(views))[0]
+        tgt = targets_u8[j].numpy().astype(np.float32) / 255.0
+        t = time.perf_counter()
+        _, grads, vis = cpu_view_step(op, params_np, views[j], tgt, args.batch)
+        t_view = time.perf_counter() - t
+        t = time.perf_counter()
+        cpu_adam(op, params_np, grads, vis.astype(np.uint8), state, DEFAULT_LRS)
+        t_adam = time.perf_counter() - t
+        if i >= args.warmup or total == 1:
+            times.append(args.batch * t_view + t_adam)
+            done += 1
+        if time.perf_counter() - budget_t0 > args.cpu_budget_s and done >= 1:
+            break
+    step_s = float(np.mean(times))
+    value = 1.0 / step_s
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "steps/s",
+        "n_gpus": world, "steps": done, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "n_gaussians": args.n_gaussians, "width": args.width,
+                   "height": args.height, "global_batch": args.batch},
+        "cpu_baseline": {"value": round(value, 5), "unit": "steps/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"per step: 1 of its {args.batch} views (fwd+loss+bwd) timed "
+                                   "and scaled by the batch, plus the selective Adam update over "
+                                   "all Gaussians; CPU oracle (C, OpenMP, all host threads)",
+                         "cpu_model": _cpu_model()},
+        "e2e": {"value": round(value, 5), "unit": "steps/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -46,6 +46,10 @@ const char* mg_last_error(void);
 /* Library version, for the loader's sanity check. */
 int mg_version(void);
 
+/* Number of kernels this library has launched in this process (all
+ * devices); a benchmark reads it before and after its timed region. */
+uint64_t mg_launch_count(void);
+
 /* ------------------------------------------------------------------------ */
 /* Camera and layout PODs                                                   */
 /* ------------------------------------------------------------------------ */
@@ -115,6 +119,24 @@ mg_status mg_preprocess_backward(
     const int32_t* valid, const mg_camera* cam, int32_t sh_degree, int64_t n,
     float* d_means, float* d_quats, float* d_scales,
     float* d_sh_dc, float* d_sh_rest, mg_stream_t stream);
+
+/* Training-engine form of mg_preprocess_backward (same math,
+ * preprocess.metal:223-411): reads the rasteriser's packed record grad2d
+ * (N, MG_G2D_STRIDE) directly and ADDS one view's gradients into the
+ * trainer's parameter storage, with the activation chain of train.py:221-222
+ * applied in-kernel:
+ *   d_log_scales += d_scales * scales,  d_logit_opac += d_opacity * op (1-op).
+ * scales/opacities are the activated values; SH uses the split layout
+ * (N,1,3) + (N,15,3). Rows whose colour gradient is zero add nothing to the
+ * SH gradients and rows with valid == 0 add nothing to the scale/quaternion
+ * gradients, so rows a view never touched cost only their reads. */
+mg_status mg_preprocess_backward_accumulate(
+    const float* means, const float* quats, const float* scales,
+    const float* opacities, const float* sh_dc, const float* sh_rest,
+    const float* grad2d, const int32_t* valid, const mg_camera* cam,
+    int32_t sh_degree, int64_t n, float* d_means, float* d_quats,
+    float* d_log_scales, float* d_logit_opac, float* d_sh_dc,
+    float* d_sh_rest, mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Binning: exact ellipse-vs-tile test, keys, sort, per-tile ranges         */
@@ -253,6 +275,27 @@ mg_status mg_selective_adam_step(float* p, const float* g, float* m, float* v,
 mg_status mg_selective_adam_advance_steps(float* steps, const uint8_t* visible,
                                           int64_t n_visible, int64_t rows,
                                           mg_stream_t stream);
+
+/* Adam over several parameter segments of one flat buffer in ONE launch
+ * (the training engine keeps all Gaussian parameters in one allocation).
+ * Segment s covers elements [offset, offset + rows * width) of p/g/m/v and
+ * uses learning rate lr. With visible_count == NULL this is dense
+ * torch.optim.Adam at scalar step `step` (adam.metal:25-42). Otherwise it is
+ * SelectiveAdam (selective_adam.py:116-186): only rows r with
+ * visible_count[r] > 0 are updated, with the shared per-row step count
+ * steps[r] + 1, and steps is advanced for those rows afterwards. At most
+ * MG_MAX_ADAM_SEGMENTS segments. */
+#define MG_MAX_ADAM_SEGMENTS 8
+typedef struct mg_adam_segment {
+    int64_t offset;
+    int32_t width;
+    float lr;
+} mg_adam_segment;
+mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
+                        int64_t rows, const mg_adam_segment* segments,
+                        int32_t n_segments, float b1, float b2, float eps,
+                        const float* visible_count, float* steps, int64_t step,
+                        mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* SSIM (11-tap separable Gaussian, zero padding) and the training loss     */

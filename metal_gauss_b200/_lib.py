@@ -34,6 +34,10 @@ class ShLayout(C.Structure):
                 ("offset_rest", C.c_int32), ("unused", C.c_int32)]
 
 
+class AdamSegment(C.Structure):
+    _fields_ = [("offset", C.c_int64), ("width", C.c_int32), ("lr", C.c_float)]
+
+
 SH_FUSED = ShLayout(16, 16, 1, 0)
 SH_SPLIT = ShLayout(1, 15, 0, 0)
 
@@ -44,10 +48,13 @@ CAM = C.POINTER(Camera)
 SIGNATURES = {
     "mg_last_error": (C.c_char_p, []),
     "mg_version": (C.c_int, []),
+    "mg_launch_count": (C.c_uint64, []),
     "mg_preprocess_forward": (i32, [vp, vp, vp, vp, vp, ShLayout, vp, CAM, i32, i64, vp, vp, vp,
                                     vp, vp, vp, vp]),
     "mg_preprocess_backward": (i32, [vp, vp, vp, vp, vp, ShLayout, vp, i64, vp, i64, vp, i64,
                                      vp, CAM, i32, i64, vp, vp, vp, vp, vp, vp]),
+    "mg_preprocess_backward_accumulate": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, CAM, i32, i64,
+                                                vp, vp, vp, vp, vp, vp, vp]),
     "mg_bin_count": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]),
     "mg_bin_write": (i32, [vp, vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32, vp, vp,
                            vp]),
@@ -68,6 +75,8 @@ SIGNATURES = {
     "mg_selective_adam_step": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, f32,
                                      vp]),
     "mg_selective_adam_advance_steps": (i32, [vp, vp, i64, i64, vp]),
+    "mg_adam_multi": (i32, [vp, vp, vp, vp, i64, C.POINTER(AdamSegment), i32, f32, f32, f32, vp,
+                            vp, i64, vp]),
     "mg_ssim_stack_blur_h": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "mg_ssim_blur15": (i32, [vp, vp, i32, i32, i32, vp, vp]),
     "mg_ssim_tail_forward": (i32, [vp, i32, i32, vp, vp]),

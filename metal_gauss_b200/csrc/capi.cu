@@ -1,5 +1,6 @@
 // C ABI glue: error reporting, the device error word, and the entry points
 // that orchestrate several kernels (binning and sorting).
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -9,6 +10,7 @@ namespace mg {
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
 
 __device__ int32_t g_device_error_word;
 
@@ -82,6 +84,7 @@ EmitScratch carve_emit(void* base, int64_t m, int n_tiles) {
 void set_error(const std::string& msg) { g_last_error = msg; }
 
 mg_status check_launch(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     const cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) return MG_OK;
     set_error(std::string(what) + ": " + cudaGetErrorString(e));
@@ -107,6 +110,8 @@ using namespace mg;
 extern "C" const char* mg_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" int mg_version(void) { return 1; }
+
+extern "C" uint64_t mg_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" mg_status mg_read_device_error(int32_t* code_out, mg_stream_t stream) {
     MG_REQUIRE(code_out != nullptr, "read_device_error: null output");

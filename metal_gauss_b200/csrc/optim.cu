@@ -1,6 +1,8 @@
 // Adam updates: dense (torch.optim.Adam, adam.metal:25-42) and row-selective
 // (SelectiveAdam, metal_gauss/selective_adam.py:116-186). Both are single
 // HBM passes: read p, g, m, v; write p, m, v (28 B per element).
+#include <cmath>
+
 #include "kernels.cuh"
 
 namespace mg {
@@ -61,6 +63,59 @@ __global__ void advance_steps_kernel(float* __restrict__ steps,
     if (r < n_visible && visible[r] != 0) steps[r] = __fadd_rn(steps[r], 1.0f);
 }
 
+struct AdamSegments {
+    int64_t offset[MG_MAX_ADAM_SEGMENTS];
+    int32_t width[MG_MAX_ADAM_SEGMENTS];
+    float lr[MG_MAX_ADAM_SEGMENTS];
+};
+
+// One launch over every segment (blockIdx.y). Selective mode (vis != null)
+// follows selective_adam_kernel's arithmetic with the shared per-row step
+// count; dense mode follows adam_kernel's.
+__global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict__ g,
+                                  float* __restrict__ m, float* __restrict__ v, int64_t rows,
+                                  AdamSegments segs, float b1, float b2, float eps, float w1,
+                                  float w2, const float* __restrict__ vis,
+                                  const float* __restrict__ steps, float bc1, float sqrt_bc2) {
+    const int s = blockIdx.y;
+    const int64_t off = segs.offset[s];
+    const int width = segs.width[s];
+    const float lr = segs.lr[s];
+    const int64_t count = rows * width;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = off + e;
+        const float gi = g[i];
+        if (vis != nullptr) {
+            const int64_t r = e / width;
+            if (!(vis[r] > 0.0f)) continue;
+            const float k = __fadd_rn(steps[r], 1.0f);
+            const float c1 = __fsub_rn(1.0f, powf(b1, k));
+            const float c2 = __fsub_rn(1.0f, powf(b2, k));
+            const float step_size = __fmul_rn(lr, __fdiv_rn(__fsqrt_rn(c2), c1));
+            const float mi = __fadd_rn(__fmul_rn(m[i], b1), __fmul_rn(gi, w1));
+            const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(gi, gi), w2));
+            m[i] = mi;
+            v[i] = vi;
+            p[i] = __fsub_rn(p[i], __fdiv_rn(__fmul_rn(step_size, mi), __fadd_rn(__fsqrt_rn(vi), eps)));
+        } else {
+            float mi = m[i];
+            mi = __fadd_rn(mi, __fmul_rn(1.0f - b1, __fsub_rn(gi, mi)));
+            const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(1.0f - b2, gi), gi));
+            m[i] = mi;
+            v[i] = vi;
+            const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), sqrt_bc2), eps);
+            p[i] = __fadd_rn(p[i], __fdiv_rn(__fmul_rn(-(lr / bc1), mi), denom));
+        }
+    }
+}
+
+__global__ void advance_steps_count_kernel(float* __restrict__ steps,
+                                           const float* __restrict__ vis, int64_t rows) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < rows && vis[r] > 0.0f) steps[r] = __fadd_rn(steps[r], 1.0f);
+}
+
 int grid_for(int64_t n) {
     return (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
 }
@@ -108,4 +163,38 @@ extern "C" mg_status mg_selective_adam_advance_steps(float* steps, const uint8_t
                            reinterpret_cast<cudaStream_t>(stream)>>>(steps, visible,
                                                                      n_visible);
     return check_launch("selective_adam_advance_steps");
+}
+
+extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v, int64_t rows,
+                                   const mg_adam_segment* segments, int32_t n_segments,
+                                   float b1, float b2, float eps, const float* visible_count,
+                                   float* steps, int64_t step, mg_stream_t stream) {
+    MG_REQUIRE(n_segments > 0 && n_segments <= MG_MAX_ADAM_SEGMENTS && segments != nullptr,
+               "adam_multi: 1..MG_MAX_ADAM_SEGMENTS segments");
+    MG_REQUIRE(p && g && m && v, "adam_multi: null pointer");
+    MG_REQUIRE(visible_count == nullptr || steps != nullptr, "adam_multi: selective mode needs steps");
+    MG_REQUIRE(visible_count != nullptr || step >= 1, "adam_multi: dense mode needs step >= 1");
+    if (rows == 0) return MG_OK;
+    AdamSegments segs;
+    int max_w = 1;
+    for (int s = 0; s < n_segments; ++s) {
+        MG_REQUIRE(segments[s].width > 0 && segments[s].offset >= 0, "adam_multi: bad segment");
+        segs.offset[s] = segments[s].offset;
+        segs.width[s] = segments[s].width;
+        segs.lr[s] = segments[s].lr;
+        max_w = std::max(max_w, (int)segments[s].width);
+    }
+    const double bc1 = visible_count ? 1.0 : 1.0 - std::pow((double)b1, (double)step);
+    const double sq = visible_count ? 1.0 : std::sqrt(1.0 - std::pow((double)b2, (double)step));
+    const float w1 = (float)(1.0 - (double)b1), w2 = (float)(1.0 - (double)b2);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int gx = (int)std::min<int64_t>((rows * max_w + 255) / 256, 148 * 8);
+    adam_multi_kernel<<<dim3(std::max(gx, 1), n_segments), 256, 0, st>>>(
+        p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, (float)bc1, (float)sq);
+    MG_TRY(check_launch("adam_multi"));
+    if (visible_count) {
+        advance_steps_count_kernel<<<ceil_div(rows, 256), 256, 0, st>>>(steps, visible_count, rows);
+        return check_launch("adam_multi steps");
+    }
+    return MG_OK;
 }

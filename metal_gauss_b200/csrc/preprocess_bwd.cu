@@ -18,6 +18,7 @@ namespace {
 
 constexpr int kBwdBlock = 128;
 constexpr int kRowBlock = 48;  // floats staged per Gaussian (16 rows x 3)
+constexpr mg_sh_layout SH_SPLIT_LAYOUT = {1, 15, 0, 0};
 
 __device__ __forceinline__ void sh_basis_grad(int b, float x, float y, float z, float& gx,
                                               float& gy, float& gz) {
@@ -51,6 +52,12 @@ struct ShBlock {
     }
 };
 
+// kAccum = false: the reference bridge's semantics (every output overwritten).
+// kAccum = true: the training engine's form -- gradients are ADDED, the
+// activation chain is applied (d_log_scales = d_scales * scales, d_logit =
+// d_opacity * op (1 - op), with d_opacity read from `d_opac`), and rows that
+// receive nothing are not written at all.
+template <bool kAccum>
 __global__ void __launch_bounds__(kBwdBlock)
 preprocess_backward_kernel(const float* __restrict__ means, const float* __restrict__ quats,
                            const float* __restrict__ scales, const float* __restrict__ sh_dc,
@@ -62,7 +69,9 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
                            int64_t n, float* __restrict__ d_means,
                            float* __restrict__ d_quats, float* __restrict__ d_scales,
                            float* __restrict__ d_sh_dc, float* __restrict__ d_sh_rest,
-                           int fused, int contiguous_rest) {
+                           int fused, int contiguous_rest,
+                           const float* __restrict__ opac, const float* __restrict__ d_opac,
+                           int64_t d_opac_stride, float* __restrict__ d_logit) {
     __shared__ float s_sh[kBwdBlock / 32][32 * kRowBlock];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
@@ -102,11 +111,16 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
         // shared block; the rare unstaged layout writes in place.
         auto wr = [&](int i, float r0, float r1, float r2) {
             float* r;
+            bool global = true;
             if (i == 0 && !blk.fused) r = d_sh_dc + g * (int64_t)shl.stride_dc * 3;
-            else if (staged) r = blk.row(lane, i);
+            else if (staged) { r = blk.row(lane, i); global = false; }
             else r = (i == 0) ? d_sh_dc + g * (int64_t)shl.stride_dc * 3
                               : d_sh_rest + (g * (int64_t)shl.stride_rest + shl.offset_rest + (i - 1)) * 3;
-            r[0] = r0; r[1] = r1; r[2] = r2;
+            if (kAccum && global) {
+                if (r0 != 0.f || r1 != 0.f || r2 != 0.f) { r[0] += r0; r[1] += r1; r[2] += r2; }
+            } else {
+                r[0] = r0; r[1] = r1; r[2] = r2;
+            }
         };
         if (need) {
             auto rd = [&](int i, int c) -> float {
@@ -146,17 +160,21 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
             dmx += (ddx - x * dd) / len;
             dmy += (ddy - y * dd) / len;
             dmz += (ddz - z * dd) / len;
-        } else if (in) {
+        } else if (in && (!kAccum || (staged && any_need))) {
+            // overwrite mode writes zeros; accumulate mode only clears this
+            // lane's staged rows so the warp's block add below adds nothing
 #pragma unroll
             for (int i = 0; i < 16; ++i) wr(i, 0.f, 0.f, 0.f);
         }
         __syncwarp();
-        if (staged) {
+        if (staged && (!kAccum || any_need)) {
             const int per_g = fused ? 48 : 45;
             float* dst = fused ? d_sh_dc + g0 * 48 : d_sh_rest + g0 * 45;
             const int total = (int)warp_n * per_g;
-            for (int i = lane; i < total; i += 32)
-                dst[i] = blk.s[(i / per_g) * kRowBlock + (i % per_g)];
+            for (int i = lane; i < total; i += 32) {
+                const float x = blk.s[(i / per_g) * kRowBlock + (i % per_g)];
+                if (kAccum) dst[i] += x; else dst[i] = x;
+            }
         }
     }
     if (!in) return;
@@ -272,9 +290,20 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
                 for (int k = 0; k < 3; ++k) acc += 0.5f * (dS[i][k] + dS[k][i]) * M[k][j];
                 dM[i][j] = 2.0f * acc;
             }
-        d_scales[3 * g + 0] = dM[0][0] * R[0][0] + dM[1][0] * R[1][0] + dM[2][0] * R[2][0];
-        d_scales[3 * g + 1] = dM[0][1] * R[0][1] + dM[1][1] * R[1][1] + dM[2][1] * R[2][1];
-        d_scales[3 * g + 2] = dM[0][2] * R[0][2] + dM[1][2] * R[1][2] + dM[2][2] * R[2][2];
+        const float ds0 = dM[0][0] * R[0][0] + dM[1][0] * R[1][0] + dM[2][0] * R[2][0];
+        const float ds1 = dM[0][1] * R[0][1] + dM[1][1] * R[1][1] + dM[2][1] * R[2][1];
+        const float ds2 = dM[0][2] * R[0][2] + dM[1][2] * R[1][2] + dM[2][2] * R[2][2];
+        if (kAccum) {  // d log s = d s * s
+            d_scales[3 * g + 0] += ds0 * s[0];
+            d_scales[3 * g + 1] += ds1 * s[1];
+            d_scales[3 * g + 2] += ds2 * s[2];
+            const float op = opac[g];
+            d_logit[g] += d_opac[g * d_opac_stride] * (op * (1.0f - op));
+        } else {
+            d_scales[3 * g + 0] = ds0;
+            d_scales[3 * g + 1] = ds1;
+            d_scales[3 * g + 2] = ds2;
+        }
         float G[3][3];  // dL/dR
 #pragma unroll
         for (int i = 0; i < 3; ++i)
@@ -285,16 +314,30 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
         const float dqy = 2.f * (w * (G[0][2] - G[2][0]) + x * (G[1][0] + G[0][1]) + zq * (G[2][1] + G[1][2]) - 2.f * y * (G[0][0] + G[2][2]));
         const float dqz = 2.f * (w * (G[1][0] - G[0][1]) + x * (G[2][0] + G[0][2]) + y * (G[2][1] + G[1][2]) - 2.f * zq * (G[0][0] + G[1][1]));
         const float qdot = w * dw + x * dqx + y * dqy + zq * dqz;
-        reinterpret_cast<float4*>(d_quats)[g] =
-            make_float4((dw - w * qdot) / qd, (dqx - x * qdot) / qd, (dqy - y * qdot) / qd,
-                        (dqz - zq * qdot) / qd);
-    } else {
+        const float4 dq = make_float4((dw - w * qdot) / qd, (dqx - x * qdot) / qd,
+                                      (dqy - y * qdot) / qd, (dqz - zq * qdot) / qd);
+        float4* dqp = reinterpret_cast<float4*>(d_quats) + g;
+        if (kAccum) {
+            const float4 o = *dqp;
+            *dqp = make_float4(o.x + dq.x, o.y + dq.y, o.z + dq.z, o.w + dq.w);
+        } else {
+            *dqp = dq;
+        }
+    } else if (!kAccum) {
         d_scales[3 * g + 0] = 0.f; d_scales[3 * g + 1] = 0.f; d_scales[3 * g + 2] = 0.f;
         reinterpret_cast<float4*>(d_quats)[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    d_means[3 * g + 0] = dmx;
-    d_means[3 * g + 1] = dmy;
-    d_means[3 * g + 2] = dmz;
+    if (kAccum) {
+        if (dmx != 0.f || dmy != 0.f || dmz != 0.f) {
+            d_means[3 * g + 0] += dmx;
+            d_means[3 * g + 1] += dmy;
+            d_means[3 * g + 2] += dmz;
+        }
+    } else {
+        d_means[3 * g + 0] = dmx;
+        d_means[3 * g + 1] = dmy;
+        d_means[3 * g + 2] = dmz;
+    }
 }
 
 }  // namespace
@@ -331,10 +374,40 @@ extern "C" mg_status mg_preprocess_backward(
                        "preprocess_backward: the fused SH layout passes one tensor twice");
     }
     const CamParams P = make_cam_params(*cam);
-    preprocess_backward_kernel<<<ceil_div(n, kBwdBlock), kBwdBlock, 0,
-                                 reinterpret_cast<cudaStream_t>(stream)>>>(
+    preprocess_backward_kernel<false><<<ceil_div(n, kBwdBlock), kBwdBlock, 0,
+                                        reinterpret_cast<cudaStream_t>(stream)>>>(
         means, quats, scales, sh_dc, sh_rest, shl, d_uv, d_uv_stride, d_conic, d_conic_stride,
         d_color, d_color_stride, valid, P, sh_degree, n, d_means, d_quats, d_scales, d_sh_dc,
-        d_sh_rest, fused ? 1 : 0, split ? 1 : 0);
+        d_sh_rest, fused ? 1 : 0, split ? 1 : 0, nullptr, nullptr, 0, nullptr);
     return check_launch("preprocess_backward");
+}
+
+extern "C" mg_status mg_preprocess_backward_accumulate(
+    const float* means, const float* quats, const float* scales, const float* opacities,
+    const float* sh_dc, const float* sh_rest, const float* grad2d, const int32_t* valid,
+    const mg_camera* cam, int32_t sh_degree, int64_t n, float* d_means, float* d_quats,
+    float* d_log_scales, float* d_logit_opac, float* d_sh_dc, float* d_sh_rest,
+    mg_stream_t stream) {
+    MG_REQUIRE(cam != nullptr, "preprocess_backward_accumulate: null camera");
+    MG_REQUIRE(sh_degree <= 3, "preprocess_backward_accumulate: sh_degree must be <= 3");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(means && quats && scales && opacities && grad2d && valid && d_means && d_quats &&
+                   d_log_scales && d_logit_opac,
+               "preprocess_backward_accumulate: null pointer");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(d_quats) & 15u) == 0u,
+               "preprocess_backward_accumulate: quats must be 16-byte aligned");
+    const bool with_sh = sh_degree >= 0 && sh_dc != nullptr;
+    if (with_sh)
+        MG_REQUIRE(sh_rest && d_sh_dc && d_sh_rest,
+                   "preprocess_backward_accumulate: null SH pointer");
+    const CamParams P = make_cam_params(*cam);
+    preprocess_backward_kernel<true><<<ceil_div(n, kBwdBlock), kBwdBlock, 0,
+                                       reinterpret_cast<cudaStream_t>(stream)>>>(
+        means, quats, scales, with_sh ? sh_dc : nullptr, sh_rest, SH_SPLIT_LAYOUT,
+        grad2d + MG_G2D_UV, MG_G2D_STRIDE, grad2d + MG_G2D_CONIC, MG_G2D_STRIDE,
+        with_sh ? grad2d + MG_G2D_COLOR : nullptr, MG_G2D_STRIDE, valid, P,
+        with_sh ? sh_degree : -1, n, d_means, d_quats, d_log_scales, d_sh_dc, d_sh_rest, 0, 1,
+        opacities, grad2d + MG_G2D_OPACITY, MG_G2D_STRIDE, d_logit_opac);
+    return check_launch("preprocess_backward_accumulate");
 }

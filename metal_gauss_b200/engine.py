@@ -1,0 +1,305 @@
+"""Batched multi-view training step on one or more B200s.
+
+The reference trains one view per step on one device (train.py:352-402).
+This engine runs the same per-view math -- render, 0.8 L1 + 0.2 (1 - SSIM),
+backward through the rasteriser and the fused preprocess, activation chain,
+then selective (or dense) Adam -- over a batch of views, sharded across
+ranks when torch.distributed is initialised:
+
+  * every Gaussian parameter lives in ONE flat fp32 buffer in the trainer's
+    storage form, 59 floats per Gaussian, as consecutive segments
+    means (N,3) | quats (N,4) | log_scales (N,3) | logit_opac (N,) |
+    sh_dc (N,1,3) | sh_rest (N,15,3);
+  * the gradient buffer has the same segments plus one more: the number of
+    views in which each Gaussian was visible, so a SINGLE collective
+    (NCCL all-reduce over NVLink) sums the gradients and forms the union
+    visibility mask that selective Adam needs;
+  * per view: preprocess -> binning (device sort) -> raster forward -> fused
+    loss -> raster backward (packed gradient record) -> preprocess backward
+    that ADDS into the flat gradient with the exp/sigmoid chain applied;
+  * the loss of a batch is the mean over its views, so each view's
+    gradient is scaled by 1 / (global batch).
+
+The parameters are replicated on every rank and stay bit-identical: all
+ranks apply the same Adam update to the same all-reduced gradient.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, dp, ext
+from ._lib import G2D_STRIDE, ptr
+
+# (name, floats per Gaussian)
+SEGMENTS = (("means", 3), ("quats", 4), ("log_scales", 3), ("logit_opac", 1), ("sh_dc", 3),
+            ("sh_rest", 45))
+FLOATS_PER_GAUSSIAN = sum(w for _, w in SEGMENTS)           # 59
+SHAPES = {"means": (3,), "quats": (4,), "log_scales": (3,), "logit_opac": (), "sh_dc": (1, 3),
+          "sh_rest": (15, 3)}
+# make_optimizer's learning rates (train.py:167-191) with its defaults
+DEFAULT_LRS = {"means": 2e-4, "log_scales": 5e-3, "quats": 1e-3, "logit_opac": 1e-2,
+               "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
+
+
+@dataclass
+class ViewStats:
+    visible: int = 0
+    pairs: int = 0
+
+
+class _ViewBuffers:
+    """Per-resolution scratch reused by every view of that size."""
+
+    def __init__(self, n: int, W: int, H: int, device):
+        f32 = dict(dtype=torch.float32, device=device)
+        self.uv = torch.empty(n, 2, **f32)
+        self.conic = torch.empty(n, 3, **f32)
+        self.depth = torch.empty(n, **f32)
+        self.rxy = torch.empty(n, 2, **f32)
+        self.valid = torch.empty(n, dtype=torch.int32, device=device)
+        self.color = torch.empty(n, 3, **f32)
+        self.grad2d = torch.empty(n, G2D_STRIDE, **f32)
+        self.rgb = torch.empty(H, W, 3, **f32)
+        self.alpha = torch.empty(H, W, **f32)
+        self.T = torch.empty(H, W, **f32)
+        self.stop = torch.empty(H, W, dtype=torch.int32, device=device)
+        self.grad_rgb = torch.empty(H, W, 3, **f32)
+        nbytes = _lib.load().mg_l1_ssim_scratch_bytes(H, W)
+        self.loss_scratch = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self.bins = ext.BinWorkspace()
+
+
+class Trainer:
+    """Data-parallel batched trainer. `params` holds the trainer's storage
+    tensors (means, quats, log_scales, logit_opac, sh_dc (N,1,3),
+    sh_rest (N,15,3)); they are copied into the flat device buffer."""
+
+    def __init__(self, params: dict, device="cuda", *, sh_degree: int = 3, tile: int = 16,
+                 background=(0.0, 0.0, 0.0), lrs: dict | None = None, w_l1: float = 0.8,
+                 w_ssim: float = 0.2, selective: bool = True, near: float = 0.01,
+                 far: float = 100.0, max_radius_frac: float = 1.0, group=None,
+                 betas=(0.9, 0.999), eps: float = 1e-15):
+        self.device = torch.device(device)
+        self.n = n = int(params["means"].shape[0])
+        self.sh_degree, self.tile = sh_degree, tile
+        self.background = None if background is None or all(b == 0 for b in background) \
+            else tuple(float(b) for b in background)
+        self.w_l1, self.w_ssim = w_l1, w_ssim
+        self.selective = selective
+        self.near, self.far, self.max_radius_frac = near, far, max_radius_frac
+        self.group = group
+        self.betas, self.eps = betas, eps
+        self.lrs = dict(DEFAULT_LRS, **(lrs or {}))
+        f32 = dict(dtype=torch.float32, device=self.device)
+        # segment starts rounded up to 64 floats (256 B): quaternions are read
+        # as float4 and every segment stays aligned for vector access
+        self.offsets = {}
+        off = 0
+        for name, w in SEGMENTS:
+            self.offsets[name] = off
+            off += (w * n + 63) // 64 * 64
+        self.vis_offset = off
+        self.P = torch.zeros(off, **f32)
+        self.G = torch.zeros(off + n, **f32)
+        self.M = torch.zeros(off, **f32)
+        self.V = torch.zeros(off, **f32)
+        self.steps = torch.zeros(n, **f32)
+        self.step_count = 0
+        for name, _ in SEGMENTS:
+            self.param(name).copy_(params[name].to(self.device, torch.float32).reshape(
+                (n,) + SHAPES[name]))
+        self.scales = torch.empty(n, 3, **f32)
+        self.opac = torch.empty(n, **f32)
+        self.loss = torch.zeros(1, **f32)
+        self.window = torch.empty(11, **f32)
+        x = torch.arange(11, dtype=torch.float32) - 5
+        w = torch.exp(-x ** 2 / (2 * 1.5 ** 2))
+        self.window.copy_(w / w.sum())
+        self._bufs: dict[tuple[int, int], _ViewBuffers] = {}
+        self._cams: dict[int, _lib.Camera] = {}
+        self.last_stats: list[ViewStats] = []
+        # stage name -> list of (start, end) CUDA events, when timing is on
+        self.stage_events: dict[str, list] | None = None
+
+    # ---------------------------------------------------------------- timing
+
+    def _begin(self, name: str):
+        if self.stage_events is None:
+            return None
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        self.stage_events.setdefault(name, []).append((a, b))
+        return b
+
+    @staticmethod
+    def _end(ev) -> None:
+        if ev is not None:
+            ev.record()
+
+    def stage_times_ms(self) -> dict[str, list[float]]:
+        """Per-stage event durations recorded since timing was switched on
+        (call after a synchronize)."""
+        return {k: [a.elapsed_time(b) for a, b in v] for k, v in (self.stage_events or {}).items()}
+
+    # ------------------------------------------------------------- storage
+
+    def _view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
+        w = dict(SEGMENTS)[name]
+        o = self.offsets[name]
+        return buf[o:o + w * self.n].view((self.n,) + SHAPES[name])
+
+    def param(self, name: str) -> torch.Tensor:
+        return self._view(self.P, name)
+
+    def grad(self, name: str) -> torch.Tensor:
+        return self._view(self.G, name)
+
+    def visibility_count(self) -> torch.Tensor:
+        return self.G[self.vis_offset:self.vis_offset + self.n]
+
+    def state_dict(self) -> dict:
+        return {name: self.param(name).detach().clone() for name, _ in SEGMENTS}
+
+    # --------------------------------------------------------------- views
+
+    def _camera(self, view) -> _lib.Camera:
+        key = id(view)
+        cam = self._cams.get(key)
+        if cam is None:
+            vm = view.viewmat.to(torch.float32)
+            K = view.K
+            cc = -vm[:3, :3].T @ vm[:3, 3]
+            cam = _lib.make_camera(vm, float(K[0, 0]), float(K[1, 1]), float(K[0, 2]),
+                                   float(K[1, 2]), view.width, view.height, self.near, self.far,
+                                   0.3, self.max_radius_frac * max(view.width, view.height), cc)
+            self._cams[key] = cam
+        return cam
+
+    def _buffers(self, W: int, H: int) -> _ViewBuffers:
+        b = self._bufs.get((W, H))
+        if b is None:
+            b = _ViewBuffers(self.n, W, H, self.device)
+            self._bufs[(W, H)] = b
+        return b
+
+    # ------------------------------------------------------------ one step
+
+    def forward_backward_view(self, view, target: torch.Tensor, scale: float) -> ViewStats:
+        """Render one view, add scale * its loss into self.loss and
+        scale * its parameter gradients into self.G."""
+        L = _lib.load()
+        s = _lib.stream()
+        W, H, n = view.width, view.height, self.n
+        b = self._buffers(W, H)
+        cam = self._camera(view)
+        byref = _lib.C.byref(cam)
+        sh_dc, sh_rest = self.param("sh_dc"), self.param("sh_rest")
+        ev = self._begin("preprocess_fwd")
+        _lib.check(L.mg_preprocess_forward(
+            ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales), ptr(sh_dc),
+            ptr(sh_rest), _lib.SH_SPLIT, ptr(self.opac), byref, self.sh_degree, n, ptr(b.uv),
+            ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color), s),
+            "preprocess_forward")
+        self.visibility_count().add_(b.valid)
+        self._end(ev)
+        ev = self._begin("binning")
+        ids, offsets, tiles_x = ext.bin_and_sort(b.uv, b.rxy, b.conic, self.opac, b.valid,
+                                                 b.depth, W, H, self.tile, workspace=b.bins)
+        self._end(ev)
+        bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
+        bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
+        ev = self._begin("raster_fwd")
+        _lib.check(L.mg_rasterize_forward(
+            ptr(b.uv), ptr(b.conic), ptr(self.opac), ptr(b.color), ptr(ids), ptr(offsets), W, H,
+            self.tile, tiles_x, bgp, ptr(b.rgb), ptr(b.alpha), ptr(b.T), ptr(b.stop), s),
+            "rasterize_forward")
+        self._end(ev)
+        ev = self._begin("loss")
+        _lib.check(L.mg_l1_ssim_loss(
+            ptr(b.rgb), ptr(target), ptr(self.window), H, W, self.w_l1, self.w_ssim, scale,
+            ptr(b.grad_rgb), ptr(self.loss), ptr(b.loss_scratch), b.loss_scratch.numel(), s),
+            "l1_ssim_loss")
+        b.grad2d.zero_()
+        self._end(ev)
+        ev = self._begin("raster_bwd")
+        _lib.check(L.mg_rasterize_backward(
+            ptr(b.uv), ptr(b.conic), ptr(self.opac), ptr(b.color), ptr(ids), ptr(offsets),
+            ptr(b.T), ptr(b.stop), ptr(b.grad_rgb), None, W, H, self.tile, tiles_x, bgp,
+            ptr(b.alpha), 0, n, ptr(b.grad2d), s), "rasterize_backward")
+        self._end(ev)
+        ev = self._begin("preprocess_bwd")
+        _lib.check(L.mg_preprocess_backward_accumulate(
+            ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales), ptr(self.opac),
+            ptr(sh_dc), ptr(sh_rest), ptr(b.grad2d), ptr(b.valid), byref, self.sh_degree, n,
+            ptr(self.grad("means")), ptr(self.grad("quats")), ptr(self.grad("log_scales")),
+            ptr(self.grad("logit_opac")), ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")), s),
+            "preprocess_backward_accumulate")
+        self._end(ev)
+        return ViewStats(pairs=int(ids.numel()))
+
+    def optimizer_step(self) -> None:
+        self.step_count += 1
+        segs = (_lib.AdamSegment * len(SEGMENTS))(
+            *[_lib.AdamSegment(self.offsets[name], w, self.lrs[name]) for name, w in SEGMENTS])
+        b1, b2 = self.betas
+        vis = self.visibility_count() if self.selective else None
+        ev = self._begin("adam")
+        _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
+                  segs, len(SEGMENTS), b1, b2, self.eps, ptr(vis), ptr(self.steps),
+                  self.step_count, _lib.stream())
+        self._end(ev)
+
+    def train_step(self, views, targets, global_batch: int | None = None) -> torch.Tensor:
+        """One optimisation step over this rank's `views` (with device
+        targets (H,W,3) in [0,1]). `global_batch` is the batch size summed
+        over ranks (defaults to len(views) times the world size). Returns the
+        batch-mean loss as a device tensor (1,), all-reduced across ranks."""
+        world = self._world_size()
+        gb = global_batch or len(views) * world
+        ev = self._begin("activations")
+        torch.exp(self.param("log_scales"), out=self.scales)
+        torch.sigmoid(self.param("logit_opac"), out=self.opac)
+        self.G.zero_()
+        self.loss.zero_()
+        self._end(ev)
+        self.last_stats = [self.forward_backward_view(v, t, 1.0 / gb)
+                           for v, t in zip(views, targets)]
+        if world > 1:
+            ev = self._begin("allreduce")
+            dp.exchange(self.G, self.loss, self.group)
+            self._end(ev)
+        self.optimizer_step()
+        return self.loss
+
+    def _world_size(self) -> int:
+        return dp.world_size(self.group)
+
+    # ------------------------------------------------------------ counters
+
+    def bytes_per_step(self, views, stats: list[ViewStats] | None = None) -> float:
+        """Algorithmic HBM bytes of one step on this rank (the compulsory
+        traffic of the dataflow; see the per-stage table in DESIGN.md)."""
+        stats = stats or self.last_stats
+        n = self.n
+        nv = float(self.visibility_count().gt(0).sum()) if self.selective else n
+        total = 0.0
+        for v, st in zip(views, stats):
+            P = v.width * v.height
+            M = st.pairs
+            total += (44 + 192 + 48) * n            # preprocess fwd
+            total += 40 * n + 8 * n + 16 * n        # bin count, depth keys, scan
+            total += 16 * n * 4                     # depth sort (4 passes x r/w 8 B)
+            total += (36 + 8) * n + 8 * M           # pair emission
+            total += 16 * M * math.ceil(math.log2(max(2, (v.width // self.tile + 1)
+                                                       * (v.height // self.tile + 1))) / 8)
+            total += 4 * M                          # ranges
+            total += 40 * M + 24 * P                # raster fwd
+            total += 40 * P + 36 * P                # fused loss (2 kernels)
+            total += 40 * M + 24 * P + 48 * n       # raster bwd (+ record)
+            total += (44 + 48 + 192) * n + 236 * 2 * n  # preprocess bwd (+ RMW grads)
+        total += 28 * FLOATS_PER_GAUSSIAN * nv + 8 * n   # selective Adam
+        return total

@@ -10,7 +10,8 @@ HEADER = _lib.build_native.ROOT / "include" / "mg_b200.h"
 
 def declared() -> set[str]:
     text = HEADER.read_text()
-    return set(re.findall(r"^\s*(?:mg_status|size_t|const char\*|int)\s+(mg_\w+)\s*\(", text, re.M))
+    return set(re.findall(r"^\s*(?:mg_status|size_t|const char\*|int|uint64_t)\s+(mg_\w+)\s*\(",
+                          text, re.M))
 
 
 def test_header_declares_the_entry_points():
