@@ -177,6 +177,33 @@ mg_status mg_sort_pairs_u64(uint64_t* keys, uint32_t* vals,
                             int64_t n, int32_t bits, void* scratch,
                             size_t scratch_bytes, mg_stream_t stream);
 
+/* Allocation-free form of mg_sort_pairs_u32 (this entry point has no
+ * counterpart in the reference). For callers that cannot allocate device
+ * memory -- a host that owns every byte of the GPU through its own pool and
+ * forbids libraries from calling cudaMalloc/cudaFree (those calls synchronise
+ * the device and fragment the pool), or a caller whose memory is already
+ * fully handed to another allocator such as PyTorch's caching allocator.
+ * The caller passes only the pairs to sort; the ping-pong buffers,
+ * histograms and look-back words live in one static device array of
+ * MG_SORT_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that
+ * loads the library holds until the process exits.
+ *   - n must be <= MG_SORT_NOALLOC_MAX_N; larger n is rejected with
+ *     MG_ERR_CAPACITY and a message, nothing is launched.
+ *   - The first call on a device looks up the array's device address for that
+ *     device (cudaGetSymbolAddress with that device current); make that first
+ *     call before any stream capture.
+ *   - Every call on a device shares the one array, so calls whose work
+ *     overlaps on the GPU (different streams, or different host threads)
+ *     race and corrupt each other's results: serialise them. The array keeps
+ *     the last call's contents; each call clears the parts that must start at
+ *     zero itself.
+ *   - Calls no cudaMalloc, cudaFree or allocating library routine. */
+#define MG_SORT_NOALLOC_MAX_N (1 << 20)
+/* 8 MiB of ping-pong buffers + 1 MiB of look-back words + histograms */
+#define MG_SORT_NOALLOC_SCRATCH_BYTES 9441536
+mg_status mg_sort_pairs_u32_noalloc(uint32_t* keys, uint32_t* vals, int64_t n,
+                                    int32_t bits, mg_stream_t stream);
+
 /* Replaces `keys[order] >> 32` + torch.searchsorted (metal_backend.py:
  * 257-260): offsets[t] = first index whose tile id is >= t, offsets[T] = m.
  * `tile_ids` are the sorted tile ids (u32), or NULL with `keys64` set to the

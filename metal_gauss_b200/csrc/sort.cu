@@ -15,6 +15,8 @@
 // in warp order, tiles in tile order, so equal digits keep their input order
 // and the sort is stable across passes.
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "kernels.cuh"
 
@@ -477,3 +479,86 @@ mg_status launch_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64, i
 }
 
 }  // namespace mg
+
+// ------------------------------------------------- allocation-free entry point
+//
+// mg_sort_pairs_u32_noalloc: the same onesweep sort with all of its scratch in
+// one static device array, for callers that cannot allocate device memory
+// (see include/mg_b200.h). Layout of the array: keys_alt (MAX_N u32) |
+// vals_alt (MAX_N u32) | sort scratch for MAX_N 32-bit keys.
+namespace mg {
+namespace {
+
+constexpr int64_t kNoallocMaxN = MG_SORT_NOALLOC_MAX_N;
+constexpr size_t kNoallocPairBytes = sizeof(uint32_t) * (size_t)kNoallocMaxN;
+// histograms + tile counters + look-back words for kNoallocMaxN keys, 4 passes
+constexpr size_t kNoallocSortBytes =
+    ((sizeof(uint32_t) * kRadix * 4 + 255) & ~(size_t)255) + 256 +
+    ((sizeof(uint32_t) * (size_t)((kNoallocMaxN + tile_keys<uint32_t>() - 1) /
+                                  tile_keys<uint32_t>()) * kRadix * 4 + 255) & ~(size_t)255);
+constexpr size_t kNoallocBytes = 2 * kNoallocPairBytes + kNoallocSortBytes;
+static_assert(kNoallocBytes == MG_SORT_NOALLOC_SCRATCH_BYTES,
+              "MG_SORT_NOALLOC_SCRATCH_BYTES must state the static array's size");
+
+static __device__ __align__(256) unsigned char g_noalloc_sort_scratch[kNoallocBytes];
+
+constexpr int kNoallocMaxDevices = 64;
+unsigned char* g_noalloc_base[kNoallocMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of the static array on the current device, looked up once
+// per device with that device current.
+mg_status noalloc_base(unsigned char** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices)
+        return fail(MG_ERR_CUDA, "sort_pairs_u32_noalloc: no current CUDA device");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_base[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_sort_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(MG_ERR_CUDA, std::string("sort_pairs_u32_noalloc: cudaGetSymbolAddress "
+                                                 "failed: ") + cudaGetErrorString(e));
+        g_noalloc_base[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_noalloc_base[dev];
+    return MG_OK;
+}
+
+}  // namespace
+}  // namespace mg
+
+extern "C" mg_status mg_sort_pairs_u32_noalloc(uint32_t* keys, uint32_t* vals, int64_t n,
+                                               int32_t bits, mg_stream_t stream) {
+    using namespace mg;
+    if (n < 0 || n > kNoallocMaxN)
+        return fail(MG_ERR_CAPACITY,
+                    "sort_pairs_u32_noalloc: " + std::to_string(n) +
+                        " pairs exceed the static scratch maximum of " +
+                        std::to_string(kNoallocMaxN) +
+                        " (MG_SORT_NOALLOC_MAX_N); use mg_sort_pairs_u32 with caller scratch");
+    if (bits < 0 || bits > 32)
+        return fail(MG_ERR_INVALID_ARGUMENT, "sort_pairs_u32_noalloc: bits must be in 0..32");
+    if (n <= 1 || bits == 0) return MG_OK;
+    if (keys == nullptr || vals == nullptr)
+        return fail(MG_ERR_INVALID_ARGUMENT, "sort_pairs_u32_noalloc: null pointer");
+    unsigned char* base = nullptr;
+    MG_TRY(noalloc_base(&base));
+    uint32_t* keys_alt = reinterpret_cast<uint32_t*>(base);
+    uint32_t* vals_alt = reinterpret_cast<uint32_t*>(base + kNoallocPairBytes);
+    void* scratch = base + 2 * kNoallocPairBytes;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    bool in_alt = false;
+    // radix_sort_pairs clears the histogram, counter and look-back region it
+    // uses before its first kernel, so the array's previous contents are harmless.
+    MG_TRY(radix_sort_pairs<uint32_t>(keys, vals, keys_alt, vals_alt, n, bits, scratch,
+                                      kNoallocSortBytes, &in_alt, s));
+    if (in_alt) {
+        if (cudaMemcpyAsync(keys, keys_alt, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, s) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(vals, vals_alt, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice, s) !=
+                cudaSuccess)
+            return check_launch("sort_pairs_u32_noalloc copy");
+    }
+    return MG_OK;
+}
