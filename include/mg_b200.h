@@ -246,27 +246,42 @@ mg_status mg_bin_emit(
  * One CTA per tile, tile in {8, 12, 16, 32}. Outputs rgb (H,W,3),
  * alpha (H,W), final transmittance T (H,W), stop index (H,W) int32.
  * background: NULL, or 3 host floats blended as rgb + max(1-alpha,0)*bg,
- * which is metal_backend.py:539-541 folded into the kernel. */
+ * which is metal_backend.py:539-541 folded into the kernel.
+ * tile_order (optional, n_tiles ids from mg_tile_order) is the order in which
+ * CTAs take tiles -- heaviest first, so long tiles do not form the tail.
+ * tile_work (optional, n_tiles ints) receives each tile's walk length, the
+ * largest stop index minus the tile's first index: the backward's cost. */
 mg_status mg_rasterize_forward(
     const float* uv, const float* conic, const float* opacity,
     const float* color, const int32_t* gauss_ids, const int32_t* tile_offsets,
     int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
     const float* background, float* out_rgb, float* out_alpha, float* out_T,
-    int32_t* out_stop, mg_stream_t stream);
+    int32_t* out_stop, const int32_t* tile_order, int32_t* tile_work,
+    mg_stream_t stream);
 
 /* Replaces rasterize_backward (rasterize.mm:147-194; rasterize.metal:
  * 173-340). grad2d (N, MG_G2D_STRIDE) is ACCUMULATED into (zero it first for
  * a fresh gradient). background as in the forward: the blend's adjoint is
  * applied in-kernel, which needs the forward's alpha (H,W) (ignored when
  * background is NULL; grad_alpha may then also be NULL for zero).
- * want_absgrad adds per-pixel |d uv| into MG_G2D_ABSUV. */
+ * want_absgrad adds per-pixel |d uv| into MG_G2D_ABSUV. tile_order is
+ * optional, as in the forward (order the tiles by the forward's tile_work).
+ */
 mg_status mg_rasterize_backward(
     const float* uv, const float* conic, const float* opacity,
     const float* color, const int32_t* gauss_ids, const int32_t* tile_offsets,
     const float* final_T, const int32_t* stop, const float* grad_rgb,
     const float* grad_alpha, int32_t width, int32_t height, int32_t tile,
     int32_t tiles_x, const float* background, const float* alpha,
-    int32_t want_absgrad, int64_t n, float* grad2d, mg_stream_t stream);
+    int32_t want_absgrad, int64_t n, float* grad2d, const int32_t* tile_order,
+    mg_stream_t stream);
+
+/* Tile ids ordered by decreasing work, for the rasteriser's tile_order:
+ * work[t] when `work` is given (e.g. the forward's tile_work), else the list
+ * length tile_offsets[t+1] - tile_offsets[t]. Bucketed by powers of two
+ * (order inside a bucket is unspecified; results do not depend on it). */
+mg_status mg_tile_order(const int32_t* tile_offsets, const int32_t* work,
+                        int32_t n_tiles, int32_t* order, mg_stream_t stream);
 
 /* Replaces pack_intersections (rasterize.mm:115-145; rasterize.metal:
  * 358-376): gathers (u, v, opacity), conic and colour by sorted id. */

@@ -68,9 +68,10 @@ SIGNATURES = {
     "mg_bin_emit_scratch_bytes": (sz, [i64, i64, i32]),
     "mg_bin_emit": (i32, [vp, vp, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
     "mg_rasterize_forward": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp,
-                                   vp, vp]),
+                                   vp, vp, vp, vp]),
     "mg_rasterize_backward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
-                                    vp, vp, i32, i64, vp, vp]),
+                                    vp, vp, i32, i64, vp, vp, vp]),
+    "mg_tile_order": (i32, [vp, vp, i32, vp, vp]),
     "mg_pack_intersections": (i32, [vp, vp, vp, vp, vp, i64, vp, vp, vp, vp]),
     "mg_adam_step": (i32, [vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, f32, vp]),
     "mg_selective_adam_step": (i32, [vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, f32,

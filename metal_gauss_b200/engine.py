@@ -49,19 +49,15 @@ DEFAULT_LRS = {"means": 2e-4, "log_scales": 5e-3, "quats": 1e-3, "logit_opac": 1
 class ViewStats:
     visible: int = 0
     pairs: int = 0
+    walked: float = 0.0
 
 
-class _ViewBuffers:
-    """Per-resolution scratch reused by every view of that size."""
+class _ImageBuffers:
+    """Per-resolution scratch shared by the views of that size (phase B runs
+    the views one after another on the stream)."""
 
     def __init__(self, n: int, W: int, H: int, device):
         f32 = dict(dtype=torch.float32, device=device)
-        self.uv = torch.empty(n, 2, **f32)
-        self.conic = torch.empty(n, 3, **f32)
-        self.depth = torch.empty(n, **f32)
-        self.rxy = torch.empty(n, 2, **f32)
-        self.valid = torch.empty(n, dtype=torch.int32, device=device)
-        self.color = torch.empty(n, 3, **f32)
         self.grad2d = torch.empty(n, G2D_STRIDE, **f32)
         self.rgb = torch.empty(H, W, 3, **f32)
         self.alpha = torch.empty(H, W, **f32)
@@ -70,7 +66,27 @@ class _ViewBuffers:
         self.grad_rgb = torch.empty(H, W, 3, **f32)
         nbytes = _lib.load().mg_l1_ssim_scratch_bytes(H, W)
         self.loss_scratch = torch.empty(nbytes, dtype=torch.uint8, device=device)
-        self.bins = ext.BinWorkspace()
+        self.order = None
+        self.tile_work = None
+        self.ids = torch.empty(0, dtype=torch.int32, device=device)
+        self.offsets = None
+        self.emit = torch.empty(0, dtype=torch.uint8, device=device)
+
+
+class _ViewState:
+    """Per-view projection outputs and binning scratch, alive from phase A
+    (projection + binning preparation of every view) to phase B."""
+
+    def __init__(self, n: int, device):
+        f32 = dict(dtype=torch.float32, device=device)
+        self.uv = torch.empty(n, 2, **f32)
+        self.conic = torch.empty(n, 3, **f32)
+        self.depth = torch.empty(n, **f32)
+        self.rxy = torch.empty(n, 2, **f32)
+        self.valid = torch.empty(n, dtype=torch.int32, device=device)
+        self.color = torch.empty(n, 3, **f32)
+        nbytes = _lib.load().mg_bin_prepare_scratch_bytes(n)
+        self.prep = torch.empty(nbytes, dtype=torch.uint8, device=device)
 
 
 class Trainer:
@@ -119,16 +135,24 @@ class Trainer:
         x = torch.arange(11, dtype=torch.float32) - 5
         w = torch.exp(-x ** 2 / (2 * 1.5 ** 2))
         self.window.copy_(w / w.sum())
-        self._bufs: dict[tuple[int, int], _ViewBuffers] = {}
+        self._bufs: dict[tuple[int, int], _ImageBuffers] = {}
+        self._states: list[_ViewState] = []
+        self._totals = torch.zeros(64, dtype=torch.int64, device=self.device)
         self._cams: dict[int, _lib.Camera] = {}
         self.last_stats: list[ViewStats] = []
-        # stage name -> list of (start, end) CUDA events, when timing is on
+        # stage name -> list of (start, end) CUDA events, when timing is on;
+        # timed_stages restricts the recording to those names (None: all)
         self.stage_events: dict[str, list] | None = None
+        self.timed_stages: set | None = None
+        # per-view list entries walked by the rasteriser (device scalars),
+        # recorded while timing is on
+        self.walked: list[torch.Tensor] = []
 
     # ---------------------------------------------------------------- timing
 
     def _begin(self, name: str):
-        if self.stage_events is None:
+        if self.stage_events is None or (self.timed_stages is not None
+                                         and name not in self.timed_stages):
             return None
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
@@ -179,45 +203,78 @@ class Trainer:
             self._cams[key] = cam
         return cam
 
-    def _buffers(self, W: int, H: int) -> _ViewBuffers:
+    def _buffers(self, W: int, H: int) -> _ImageBuffers:
         b = self._bufs.get((W, H))
         if b is None:
-            b = _ViewBuffers(self.n, W, H, self.device)
+            b = _ImageBuffers(self.n, W, H, self.device)
             self._bufs[(W, H)] = b
         return b
 
-    # ------------------------------------------------------------ one step
+    def _state(self, v: int) -> _ViewState:
+        while len(self._states) <= v:
+            self._states.append(_ViewState(self.n, self.device))
+        return self._states[v]
 
-    def forward_backward_view(self, view, target: torch.Tensor, scale: float) -> ViewStats:
-        """Render one view, add scale * its loss into self.loss and
-        scale * its parameter gradients into self.G."""
+    def _project_and_prepare(self, v: int, view) -> None:
+        """Phase A for view v: projection + SH colour, visibility count, tile
+        counts, depth sort and the scan that yields the view's pair total."""
+        L = _lib.load()
+        s = _lib.stream()
+        st = self._state(v)
+        cam = self._camera(view)
+        ev = self._begin("preprocess_fwd")
+        _lib.check(L.mg_preprocess_forward(
+            ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales),
+            ptr(self.param("sh_dc")), ptr(self.param("sh_rest")), _lib.SH_SPLIT, ptr(self.opac),
+            _lib.C.byref(cam), self.sh_degree, self.n, ptr(st.uv), ptr(st.conic), ptr(st.depth),
+            ptr(st.rxy), ptr(st.valid), ptr(st.color), s), "preprocess_forward")
+        self.visibility_count().add_(st.valid)
+        self._end(ev)
+        ev = self._begin("bin_prepare")
+        _lib.check(L.mg_bin_prepare(
+            ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), ptr(st.valid), ptr(st.depth),
+            self.n, view.width, view.height, self.tile, ptr(self._totals[v:v + 1]), ptr(st.prep),
+            st.prep.numel(), s), "bin_prepare")
+        self._end(ev)
+
+    def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
+                             scale: float) -> ViewStats:
+        """Phase B for view v (its pair total m known on the host): pair
+        emission and tile sort, raster forward, fused loss, raster backward,
+        and the preprocess backward that adds into the flat gradient."""
         L = _lib.load()
         s = _lib.stream()
         W, H, n = view.width, view.height, self.n
+        st = self._state(v)
         b = self._buffers(W, H)
         cam = self._camera(view)
-        byref = _lib.C.byref(cam)
-        sh_dc, sh_rest = self.param("sh_dc"), self.param("sh_rest")
-        ev = self._begin("preprocess_fwd")
-        _lib.check(L.mg_preprocess_forward(
-            ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales), ptr(sh_dc),
-            ptr(sh_rest), _lib.SH_SPLIT, ptr(self.opac), byref, self.sh_degree, n, ptr(b.uv),
-            ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color), s),
-            "preprocess_forward")
-        self.visibility_count().add_(b.valid)
-        self._end(ev)
-        ev = self._begin("binning")
-        ids, offsets, tiles_x = ext.bin_and_sort(b.uv, b.rxy, b.conic, self.opac, b.valid,
-                                                 b.depth, W, H, self.tile, workspace=b.bins)
+        tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
+        n_tiles = tiles_x * tiles_y
+        if b.ids.numel() < max(m, 1):
+            b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32, device=self.device)
+        if b.offsets is None or b.offsets.numel() != n_tiles + 1:
+            b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
+            b.order = torch.empty(n_tiles, dtype=torch.int32, device=self.device)
+            b.tile_work = torch.empty(n_tiles, dtype=torch.int32, device=self.device)
+        ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
+        if b.emit.numel() < ebytes:
+            b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8, device=self.device)
+        ev = self._begin("bin_emit")
+        _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), n, m, W,
+                                 H, self.tile, ptr(st.prep), ptr(b.ids), ptr(b.offsets),
+                                 ptr(b.emit), b.emit.numel(), s), "bin_emit")
         self._end(ev)
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
         ev = self._begin("raster_fwd")
+        _lib.check(L.mg_tile_order(ptr(b.offsets), None, n_tiles, ptr(b.order), s), "tile_order")
         _lib.check(L.mg_rasterize_forward(
-            ptr(b.uv), ptr(b.conic), ptr(self.opac), ptr(b.color), ptr(ids), ptr(offsets), W, H,
-            self.tile, tiles_x, bgp, ptr(b.rgb), ptr(b.alpha), ptr(b.T), ptr(b.stop), s),
-            "rasterize_forward")
+            ptr(st.uv), ptr(st.conic), ptr(self.opac), ptr(st.color), ptr(b.ids), ptr(b.offsets),
+            W, H, self.tile, tiles_x, bgp, ptr(b.rgb), ptr(b.alpha), ptr(b.T), ptr(b.stop),
+            ptr(b.order), ptr(b.tile_work), s), "rasterize_forward")
         self._end(ev)
+        if self.stage_events is not None:
+            self.walked.append(b.tile_work.sum())
         ev = self._begin("loss")
         _lib.check(L.mg_l1_ssim_loss(
             ptr(b.rgb), ptr(target), ptr(self.window), H, W, self.w_l1, self.w_ssim, scale,
@@ -226,20 +283,35 @@ class Trainer:
         b.grad2d.zero_()
         self._end(ev)
         ev = self._begin("raster_bwd")
+        _lib.check(L.mg_tile_order(ptr(b.offsets), ptr(b.tile_work), n_tiles, ptr(b.order), s),
+                   "tile_order")
         _lib.check(L.mg_rasterize_backward(
-            ptr(b.uv), ptr(b.conic), ptr(self.opac), ptr(b.color), ptr(ids), ptr(offsets),
+            ptr(st.uv), ptr(st.conic), ptr(self.opac), ptr(st.color), ptr(b.ids), ptr(b.offsets),
             ptr(b.T), ptr(b.stop), ptr(b.grad_rgb), None, W, H, self.tile, tiles_x, bgp,
-            ptr(b.alpha), 0, n, ptr(b.grad2d), s), "rasterize_backward")
+            ptr(b.alpha), 0, n, ptr(b.grad2d), ptr(b.order), s), "rasterize_backward")
         self._end(ev)
         ev = self._begin("preprocess_bwd")
         _lib.check(L.mg_preprocess_backward_accumulate(
             ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales), ptr(self.opac),
-            ptr(sh_dc), ptr(sh_rest), ptr(b.grad2d), ptr(b.valid), byref, self.sh_degree, n,
-            ptr(self.grad("means")), ptr(self.grad("quats")), ptr(self.grad("log_scales")),
-            ptr(self.grad("logit_opac")), ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")), s),
+            ptr(self.param("sh_dc")), ptr(self.param("sh_rest")), ptr(b.grad2d), ptr(st.valid),
+            _lib.C.byref(cam), self.sh_degree, n, ptr(self.grad("means")),
+            ptr(self.grad("quats")), ptr(self.grad("log_scales")), ptr(self.grad("logit_opac")),
+            ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")), s),
             "preprocess_backward_accumulate")
         self._end(ev)
-        return ViewStats(pairs=int(ids.numel()))
+        return ViewStats(pairs=m)
+
+    def forward_backward_views(self, views, targets, scale: float) -> list[ViewStats]:
+        """Render this rank's views, adding scale * each loss into self.loss
+        and scale * each parameter gradient into self.G. One device->host
+        read per call (all views' pair totals)."""
+        if len(views) > self._totals.numel():
+            self._totals = torch.zeros(len(views), dtype=torch.int64, device=self.device)
+        for v, view in enumerate(views):
+            self._project_and_prepare(v, view)
+        totals = self._totals[:len(views)].tolist()
+        return [self._render_and_backprop(v, view, t, int(m), scale)
+                for v, (view, t, m) in enumerate(zip(views, targets, totals))]
 
     def optimizer_step(self) -> None:
         self.step_count += 1
@@ -266,8 +338,7 @@ class Trainer:
         self.G.zero_()
         self.loss.zero_()
         self._end(ev)
-        self.last_stats = [self.forward_backward_view(v, t, 1.0 / gb)
-                           for v, t in zip(views, targets)]
+        self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb)
         if world > 1:
             ev = self._begin("allreduce")
             dp.exchange(self.G, self.loss, self.group)
@@ -297,9 +368,10 @@ class Trainer:
             total += 16 * M * math.ceil(math.log2(max(2, (v.width // self.tile + 1)
                                                        * (v.height // self.tile + 1))) / 8)
             total += 4 * M                          # ranges
-            total += 40 * M + 24 * P                # raster fwd
+            Wk = st.walked if st.walked else M
+            total += 40 * Wk + 24 * P               # raster fwd (walked entries)
             total += 40 * P + 36 * P                # fused loss (2 kernels)
-            total += 40 * M + 24 * P + 48 * n       # raster bwd (+ record)
+            total += 40 * Wk + 24 * P + 48 * n      # raster bwd (+ record)
             total += (44 + 48 + 192) * n + 236 * 2 * n  # preprocess bwd (+ RMW grads)
         total += 28 * FLOATS_PER_GAUSSIAN * nv + 8 * n   # selective Adam
         return total

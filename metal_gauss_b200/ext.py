@@ -219,11 +219,22 @@ def bin_and_sort(uv, rxy, conic, opacity, valid, depth, W, H, tile, workspace=No
 
 # ------------------------------------------------------------------ raster
 
+def tile_order(tile_offsets: torch.Tensor, work: torch.Tensor | None = None) -> torch.Tensor:
+    """Tile ids heaviest first: by `work` (e.g. the forward's tile walk
+    lengths) when given, else by list length."""
+    n_tiles = tile_offsets.numel() - 1
+    order = torch.empty(n_tiles, dtype=torch.int32, device=tile_offsets.device)
+    _lib.call("mg_tile_order", ptr(tile_offsets), ptr(work), n_tiles, ptr(order), _lib.stream())
+    return order
+
+
 def rasterize_forward(uv, conic, opacity, color, gauss_ids, tile_offsets, W, H, tile, tiles_x,
-                      background=None):
+                      background=None, tile_work_out=None):
     """-> [rgb (H,W,3), alpha (H,W), T (H,W), n_contrib (H,W) int32 stop index]
     (rasterize.mm:79-113). `background` (3 floats) folds the reference's
-    blend (metal_backend.py:539-541) into the kernel."""
+    blend (metal_backend.py:539-541) into the kernel. Tiles run heaviest
+    first; `tile_work_out` (n_tiles int32), when given, receives each tile's
+    walk length for ordering the backward."""
     for t, w in ((uv, "uv"), (conic, "conic"), (opacity, "opacity"), (color, "color")):
         _check(t, w)
     _check(gauss_ids, "gauss_ids", torch.int32)
@@ -233,29 +244,33 @@ def rasterize_forward(uv, conic, opacity, color, gauss_ids, tile_offsets, W, H, 
     T = _empty((H, W), uv)
     stop = _empty((H, W), uv, torch.int32)
     bg = None if background is None else (_lib.C.c_float * 3)(*[float(x) for x in background])
+    order = tile_order(tile_offsets)
     _lib.call("mg_rasterize_forward", ptr(uv), ptr(conic), ptr(opacity), ptr(color),
               ptr(gauss_ids), ptr(tile_offsets), W, H, tile, tiles_x,
               None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p), ptr(rgb), ptr(alpha),
-              ptr(T), ptr(stop), _lib.stream())
+              ptr(T), ptr(stop), ptr(order), ptr(tile_work_out), _lib.stream())
     return [rgb, alpha, T, stop]
 
 
 def rasterize_backward_packed(uv, conic, opacity, color, gauss_ids, tile_offsets, final_T,
                               n_contrib, grad_rgb, grad_alpha, W, H, tile, tiles_x,
-                              want_absgrad, background=None, alpha=None, grad2d=None):
+                              want_absgrad, background=None, alpha=None, grad2d=None,
+                              tile_work=None):
     """Backward into the packed (N, 12) record; accumulates into `grad2d` when
-    given, else into a fresh zeroed one. Returns grad2d."""
+    given, else into a fresh zeroed one. Tiles run heaviest first, by the
+    forward's `tile_work` when given, else by list length. Returns grad2d."""
     n = uv.shape[0]
     if grad2d is None:
         grad2d = torch.zeros((n, G2D_STRIDE), dtype=F32, device=uv.device)
     grad_rgb = grad_rgb.contiguous()
     grad_alpha = None if grad_alpha is None else grad_alpha.contiguous()
     bg = None if background is None else (_lib.C.c_float * 3)(*[float(x) for x in background])
+    order = tile_order(tile_offsets, tile_work)
     _lib.call("mg_rasterize_backward", ptr(uv), ptr(conic), ptr(opacity), ptr(color),
               ptr(gauss_ids), ptr(tile_offsets), ptr(final_T), ptr(n_contrib), ptr(grad_rgb),
               ptr(grad_alpha), W, H, tile, tiles_x,
               None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p), ptr(alpha),
-              int(bool(want_absgrad)), n, ptr(grad2d), _lib.stream())
+              int(bool(want_absgrad)), n, ptr(grad2d), ptr(order), _lib.stream())
     return grad2d
 
 
