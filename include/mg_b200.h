@@ -136,7 +136,24 @@ mg_status mg_preprocess_backward_accumulate(
     const float* grad2d, const int32_t* valid, const mg_camera* cam,
     int32_t sh_degree, int64_t n, float* d_means, float* d_quats,
     float* d_log_scales, float* d_logit_opac, float* d_sh_dc,
-    float* d_sh_rest, mg_stream_t stream);
+    float* d_sh_rest, const float* color, float* dpre_out,
+    mg_stream_t stream);
+
+/* Deferred SH gradient of a batch of views, once per step. With dpre_out
+ * given, mg_preprocess_backward_accumulate skips its SH branch and instead
+ * writes dpre_out (N,3) = the view's colour gradient where the forward colour
+ * `color` is > 0 (the ReLU gate of preprocess.metal:256-262; colour > 0 iff the
+ * pre-clamp colour is > 0). This entry point then evaluates the SH adjoint of
+ * all n_views views together: d_sh (split layout, OVERWRITTEN) = sum over
+ * views of B(dir_v) x dpre_v, and d_means += the view-direction term, reading
+ * the coefficients once instead of once per view. cam_centers: n_views x 3
+ * host floats; dpre: (n_views, N, 3) device; n_views <= 64. */
+mg_status mg_sh_backward_views(const float* means, const float* sh_dc,
+                               const float* sh_rest, int32_t sh_degree,
+                               int64_t n, const float* cam_centers,
+                               const float* dpre, int32_t n_views,
+                               float* d_means, float* d_sh_dc,
+                               float* d_sh_rest, mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Binning: exact ellipse-vs-tile test, keys, sort, per-tile ranges         */

@@ -71,7 +71,8 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
                            float* __restrict__ d_sh_dc, float* __restrict__ d_sh_rest,
                            int fused, int contiguous_rest,
                            const float* __restrict__ opac, const float* __restrict__ d_opac,
-                           int64_t d_opac_stride, float* __restrict__ d_logit) {
+                           int64_t d_opac_stride, float* __restrict__ d_logit,
+                           const float* __restrict__ color, float* __restrict__ dpre_out) {
     __shared__ float s_sh[kBwdBlock / 32][32 * kRowBlock];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
@@ -84,7 +85,21 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
     float dmx = 0.f, dmy = 0.f, dmz = 0.f;
 
     // ---------------------------------------------------------- SH branch
-    const bool do_sh = sh_degree >= 0 && d_color != nullptr && sh_dc != nullptr;
+    if (kAccum && dpre_out != nullptr) {
+        // deferred: only the ReLU-gated colour gradient, for mg_sh_backward_views
+        if (in) {
+            float3 d = make_float3(0.f, 0.f, 0.f);
+            if (d_color != nullptr) {
+                const float* dc = d_color + g * d_color_stride;
+                d = make_float3(color[3 * g] > 0.f ? dc[0] : 0.f,
+                                color[3 * g + 1] > 0.f ? dc[1] : 0.f,
+                                color[3 * g + 2] > 0.f ? dc[2] : 0.f);
+            }
+            dpre_out[3 * g] = d.x; dpre_out[3 * g + 1] = d.y; dpre_out[3 * g + 2] = d.z;
+        }
+    }
+    const bool do_sh = sh_degree >= 0 && d_color != nullptr && sh_dc != nullptr &&
+                       !(kAccum && dpre_out != nullptr);
     if (do_sh) {
         const ShBlock blk{s_sh[wib], fused != 0};
         const int nb = (sh_degree + 1) * (sh_degree + 1);
@@ -340,6 +355,83 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
     }
 }
 
+constexpr int kMaxViews = 64;
+struct ViewCentres {
+    float c[kMaxViews][3];
+};
+
+// Deferred SH adjoint over all views of a step: per Gaussian, the
+// coefficients are staged once (per warp, as in the per-view kernel), the
+// gradient rows are summed over the views in registers and written once.
+__global__ void __launch_bounds__(kBwdBlock)
+sh_backward_views_kernel(const float* __restrict__ means, const float* __restrict__ sh_dc,
+                         const float* __restrict__ sh_rest, int sh_degree, int64_t n,
+                         ViewCentres centres, const float* __restrict__ dpre, int n_views,
+                         float* __restrict__ d_means, float* __restrict__ d_sh_dc,
+                         float* __restrict__ d_sh_rest) {
+    __shared__ float s_sh[kBwdBlock / 32][32 * 45];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
+    const int64_t g0 = g - lane;
+    const bool in = g < n;
+    const int64_t warp_n = min((int64_t)32, n - g0);
+    float* blk = s_sh[wib];
+    const int total = (int)max((int64_t)0, warp_n) * 45;
+    for (int i = lane; i < total; i += 32) blk[i] = __ldg(sh_rest + g0 * 45 + i);
+    __syncwarp();
+    const int nb = (sh_degree + 1) * (sh_degree + 1);
+    float acc[16][3];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = 0.f;
+    float dmx = 0.f, dmy = 0.f, dmz = 0.f;
+    if (in) {
+        const float mx = means[3 * g], my = means[3 * g + 1], mz = means[3 * g + 2];
+        const float* dc = sh_dc + 3 * g;
+        const float* rest = blk + lane * 45;
+        for (int v = 0; v < n_views; ++v) {
+            const float* dp = dpre + ((int64_t)v * n + g) * 3;
+            const float er = dp[0], eg = dp[1], eb = dp[2];
+            if (er == 0.f && eg == 0.f && eb == 0.f) continue;
+            const float dvx = mx - centres.c[v][0], dvy = my - centres.c[v][1],
+                        dvz = mz - centres.c[v][2];
+            const float len = fmaxf(sqrtf(dvx * dvx + dvy * dvy + dvz * dvz), 1e-12f);
+            const float x = dvx / len, y = dvy / len, z = dvz / len;
+            float B[16];
+            sh_basis(sh_degree, x, y, z, B);
+            float ddx = 0.f, ddy = 0.f, ddz = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (i < nb) {
+                    const float* row = i == 0 ? dc : rest + (i - 1) * 3;
+                    acc[i][0] += B[i] * er; acc[i][1] += B[i] * eg; acc[i][2] += B[i] * eb;
+                    float gx, gy, gz;
+                    sh_basis_grad(i, x, y, z, gx, gy, gz);
+                    const float k = row[0] * er + row[1] * eg + row[2] * eb;
+                    ddx += gx * k; ddy += gy * k; ddz += gz * k;
+                }
+            }
+            const float dd = x * ddx + y * ddy + z * ddz;
+            dmx += (ddx - x * dd) / len;
+            dmy += (ddy - y * dd) / len;
+            dmz += (ddz - z * dd) / len;
+        }
+        if (dmx != 0.f || dmy != 0.f || dmz != 0.f) {
+            d_means[3 * g] += dmx; d_means[3 * g + 1] += dmy; d_means[3 * g + 2] += dmz;
+        }
+        d_sh_dc[3 * g] = acc[0][0]; d_sh_dc[3 * g + 1] = acc[0][1]; d_sh_dc[3 * g + 2] = acc[0][2];
+    }
+    __syncwarp();
+    if (in) {
+#pragma unroll
+        for (int i = 1; i < 16; ++i) {
+            float* r = blk + lane * 45 + (i - 1) * 3;
+            r[0] = acc[i][0]; r[1] = acc[i][1]; r[2] = acc[i][2];
+        }
+    }
+    __syncwarp();
+    for (int i = lane; i < total; i += 32) d_sh_rest[g0 * 45 + i] = blk[i];
+}
+
 }  // namespace
 
 }  // namespace mg
@@ -378,7 +470,7 @@ extern "C" mg_status mg_preprocess_backward(
                                         reinterpret_cast<cudaStream_t>(stream)>>>(
         means, quats, scales, sh_dc, sh_rest, shl, d_uv, d_uv_stride, d_conic, d_conic_stride,
         d_color, d_color_stride, valid, P, sh_degree, n, d_means, d_quats, d_scales, d_sh_dc,
-        d_sh_rest, fused ? 1 : 0, split ? 1 : 0, nullptr, nullptr, 0, nullptr);
+        d_sh_rest, fused ? 1 : 0, split ? 1 : 0, nullptr, nullptr, 0, nullptr, nullptr, nullptr);
     return check_launch("preprocess_backward");
 }
 
@@ -387,7 +479,7 @@ extern "C" mg_status mg_preprocess_backward_accumulate(
     const float* sh_dc, const float* sh_rest, const float* grad2d, const int32_t* valid,
     const mg_camera* cam, int32_t sh_degree, int64_t n, float* d_means, float* d_quats,
     float* d_log_scales, float* d_logit_opac, float* d_sh_dc, float* d_sh_rest,
-    mg_stream_t stream) {
+    const float* color, float* dpre_out, mg_stream_t stream) {
     MG_REQUIRE(cam != nullptr, "preprocess_backward_accumulate: null camera");
     MG_REQUIRE(sh_degree <= 3, "preprocess_backward_accumulate: sh_degree must be <= 3");
     if (n == 0) return MG_OK;
@@ -397,8 +489,11 @@ extern "C" mg_status mg_preprocess_backward_accumulate(
     MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u &&
                    (reinterpret_cast<uintptr_t>(d_quats) & 15u) == 0u,
                "preprocess_backward_accumulate: quats must be 16-byte aligned");
+    const bool deferred = dpre_out != nullptr;
     const bool with_sh = sh_degree >= 0 && sh_dc != nullptr;
-    if (with_sh)
+    if (deferred)
+        MG_REQUIRE(color != nullptr, "preprocess_backward_accumulate: deferred SH needs color");
+    else if (with_sh)
         MG_REQUIRE(sh_rest && d_sh_dc && d_sh_rest,
                    "preprocess_backward_accumulate: null SH pointer");
     const CamParams P = make_cam_params(*cam);
@@ -406,8 +501,28 @@ extern "C" mg_status mg_preprocess_backward_accumulate(
                                        reinterpret_cast<cudaStream_t>(stream)>>>(
         means, quats, scales, with_sh ? sh_dc : nullptr, sh_rest, SH_SPLIT_LAYOUT,
         grad2d + MG_G2D_UV, MG_G2D_STRIDE, grad2d + MG_G2D_CONIC, MG_G2D_STRIDE,
-        with_sh ? grad2d + MG_G2D_COLOR : nullptr, MG_G2D_STRIDE, valid, P,
+        (with_sh || deferred) ? grad2d + MG_G2D_COLOR : nullptr, MG_G2D_STRIDE, valid, P,
         with_sh ? sh_degree : -1, n, d_means, d_quats, d_log_scales, d_sh_dc, d_sh_rest, 0, 1,
-        opacities, grad2d + MG_G2D_OPACITY, MG_G2D_STRIDE, d_logit_opac);
+        opacities, grad2d + MG_G2D_OPACITY, MG_G2D_STRIDE, d_logit_opac, color, dpre_out);
     return check_launch("preprocess_backward_accumulate");
+}
+
+extern "C" mg_status mg_sh_backward_views(const float* means, const float* sh_dc,
+                                          const float* sh_rest, int32_t sh_degree, int64_t n,
+                                          const float* cam_centers, const float* dpre,
+                                          int32_t n_views, float* d_means, float* d_sh_dc,
+                                          float* d_sh_rest, mg_stream_t stream) {
+    MG_REQUIRE(n_views >= 0 && n_views <= kMaxViews, "sh_backward_views: at most 64 views");
+    MG_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_backward_views: sh_degree must be 0..3");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(means && sh_dc && sh_rest && d_means && d_sh_dc && d_sh_rest &&
+                   (n_views == 0 || (cam_centers && dpre)),
+               "sh_backward_views: null pointer");
+    ViewCentres c;
+    for (int v = 0; v < n_views; ++v)
+        for (int k = 0; k < 3; ++k) c.c[v][k] = cam_centers[3 * v + k];
+    sh_backward_views_kernel<<<ceil_div(n, kBwdBlock), kBwdBlock, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(
+        means, sh_dc, sh_rest, sh_degree, n, c, dpre, n_views, d_means, d_sh_dc, d_sh_rest);
+    return check_launch("sh_backward_views");
 }

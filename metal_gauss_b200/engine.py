@@ -137,6 +137,8 @@ class Trainer:
         self.window.copy_(w / w.sum())
         self._bufs: dict[tuple[int, int], _ImageBuffers] = {}
         self._states: list[_ViewState] = []
+        # per-view ReLU-gated colour gradients for the deferred SH pass
+        self._dpre = torch.empty(0, dtype=torch.float32, device=self.device)
         self._totals = torch.zeros(64, dtype=torch.int64, device=self.device)
         self._cams: dict[int, _lib.Camera] = {}
         self.last_stats: list[ViewStats] = []
@@ -296,8 +298,8 @@ class Trainer:
             ptr(self.param("sh_dc")), ptr(self.param("sh_rest")), ptr(b.grad2d), ptr(st.valid),
             _lib.C.byref(cam), self.sh_degree, n, ptr(self.grad("means")),
             ptr(self.grad("quats")), ptr(self.grad("log_scales")), ptr(self.grad("logit_opac")),
-            ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")), s),
-            "preprocess_backward_accumulate")
+            ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")), ptr(st.color),
+            ptr(self._dpre[v]), s), "preprocess_backward_accumulate")
         self._end(ev)
         return ViewStats(pairs=m)
 
@@ -305,13 +307,30 @@ class Trainer:
         """Render this rank's views, adding scale * each loss into self.loss
         and scale * each parameter gradient into self.G. One device->host
         read per call (all views' pair totals)."""
-        if len(views) > self._totals.numel():
-            self._totals = torch.zeros(len(views), dtype=torch.int64, device=self.device)
+        V = len(views)
+        if V > self._totals.numel():
+            self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
+        if self._dpre.shape[:1] != (V,) or self._dpre.numel() != V * self.n * 3:
+            self._dpre = torch.empty(V, self.n, 3, dtype=torch.float32, device=self.device)
         for v, view in enumerate(views):
             self._project_and_prepare(v, view)
-        totals = self._totals[:len(views)].tolist()
-        return [self._render_and_backprop(v, view, t, int(m), scale)
-                for v, (view, t, m) in enumerate(zip(views, targets, totals))]
+        totals = self._totals[:V].tolist()
+        stats = [self._render_and_backprop(v, view, t, int(m), scale)
+                 for v, (view, t, m) in enumerate(zip(views, targets, totals))]
+        # the SH adjoint of all views at once: coefficients read once, gradient
+        # rows written once
+        centres = (_lib.C.c_float * (3 * V))()
+        for v, view in enumerate(views):
+            cc = self._camera(view).cam_center
+            centres[3 * v:3 * v + 3] = [cc[0], cc[1], cc[2]]
+        ev = self._begin("sh_bwd")
+        _lib.call("mg_sh_backward_views", ptr(self.param("means")), ptr(self.param("sh_dc")),
+                  ptr(self.param("sh_rest")), self.sh_degree, self.n,
+                  _lib.C.cast(centres, _lib.C.c_void_p), ptr(self._dpre), V,
+                  ptr(self.grad("means")), ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")),
+                  _lib.stream())
+        self._end(ev)
+        return stats
 
     def optimizer_step(self) -> None:
         self.step_count += 1
