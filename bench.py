@@ -74,7 +74,7 @@ def dist_setup():
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
     return rank, world, local
@@ -352,7 +352,7 @@ def run_ours(args, rank, world, local):
             "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches),
             "clocks": clk,
         }
-        print(json.dumps(out), flush=True)
+        emit(out)
 
 
 # ----------------------------------------------------------- CPU (oracle)
@@ -452,7 +452,7 @@ def run_reference(args, rank, world):
             break
     step_s = float(np.mean(times))
     value = 1.0 / step_s
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "steps/s",
         "n_gpus": world, "steps": done, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 1),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -467,10 +467,28 @@ def run_reference(args, rank, world):
                          "cpu_model": _cpu_model()},
         "e2e": {"value": round(value, 5), "unit": "steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
+
+
+_JSON_FD = None
+
+
+def emit(obj: dict) -> None:
+    """Write the one result line to the process's original stdout (libraries
+    such as NCCL print banners to stdout, which is sent to stderr instead)."""
+    line = (json.dumps(obj) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, line)
 
 
 def main():
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse()
     rank, world, local = dist_setup()
     try:

@@ -342,13 +342,17 @@ mg_status mg_selective_adam_advance_steps(float* steps, const uint8_t* visible,
  * torch.optim.Adam at scalar step `step` (adam.metal:25-42). Otherwise it is
  * SelectiveAdam (selective_adam.py:116-186): only rows r with
  * visible_count[r] > 0 are updated, with the shared per-row step count
- * steps[r] + 1, and steps is advanced for those rows afterwards. At most
- * MG_MAX_ADAM_SEGMENTS segments. */
+ * steps[r] + 1, and steps is advanced for those rows (all `rows` of them)
+ * afterwards. A segment may cover only an element range (a data-parallel
+ * rank's chunk of the flat buffer; the row of element e is e / width). At
+ * most MG_MAX_ADAM_SEGMENTS segments. */
 #define MG_MAX_ADAM_SEGMENTS 8
 typedef struct mg_adam_segment {
-    int64_t offset;
-    int32_t width;
+    int64_t offset;      /* first element of the segment's row 0          */
+    int32_t width;       /* elements per row                               */
     float lr;
+    int64_t elem_begin;  /* update elements [elem_begin, elem_end) of the  */
+    int64_t elem_end;    /* segment; elem_end == 0 means all rows * width  */
 } mg_adam_segment;
 mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
                         int64_t rows, const mg_adam_segment* segments,

@@ -35,7 +35,8 @@ class ShLayout(C.Structure):
 
 
 class AdamSegment(C.Structure):
-    _fields_ = [("offset", C.c_int64), ("width", C.c_int32), ("lr", C.c_float)]
+    _fields_ = [("offset", C.c_int64), ("width", C.c_int32), ("lr", C.c_float),
+                ("elem_begin", C.c_int64), ("elem_end", C.c_int64)]
 
 
 SH_FUSED = ShLayout(16, 16, 1, 0)

@@ -65,6 +65,8 @@ __global__ void advance_steps_kernel(float* __restrict__ steps,
 
 struct AdamSegments {
     int64_t offset[MG_MAX_ADAM_SEGMENTS];
+    int64_t begin[MG_MAX_ADAM_SEGMENTS];
+    int64_t count[MG_MAX_ADAM_SEGMENTS];
     int32_t width[MG_MAX_ADAM_SEGMENTS];
     float lr[MG_MAX_ADAM_SEGMENTS];
 };
@@ -78,12 +80,13 @@ __global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict
                                   float w2, const float* __restrict__ vis,
                                   const float* __restrict__ steps, float bc1, float sqrt_bc2) {
     const int s = blockIdx.y;
-    const int64_t off = segs.offset[s];
+    const int64_t off = segs.offset[s], first = segs.begin[s];
     const int width = segs.width[s];
     const float lr = segs.lr[s];
-    const int64_t count = rows * width;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count;
-         e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t count = segs.count[s];
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count;
+         k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e = first + k;  // element within the segment
         const int64_t i = off + e;
         const float gi = g[i];
         if (vis != nullptr) {
@@ -169,29 +172,40 @@ extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
                                    const mg_adam_segment* segments, int32_t n_segments,
                                    float b1, float b2, float eps, const float* visible_count,
                                    float* steps, int64_t step, mg_stream_t stream) {
-    MG_REQUIRE(n_segments > 0 && n_segments <= MG_MAX_ADAM_SEGMENTS && segments != nullptr,
-               "adam_multi: 1..MG_MAX_ADAM_SEGMENTS segments");
+    MG_REQUIRE(n_segments >= 0 && n_segments <= MG_MAX_ADAM_SEGMENTS &&
+                   (n_segments == 0 || segments != nullptr),
+               "adam_multi: 0..MG_MAX_ADAM_SEGMENTS segments");
     MG_REQUIRE(p && g && m && v, "adam_multi: null pointer");
     MG_REQUIRE(visible_count == nullptr || steps != nullptr, "adam_multi: selective mode needs steps");
     MG_REQUIRE(visible_count != nullptr || step >= 1, "adam_multi: dense mode needs step >= 1");
     if (rows == 0) return MG_OK;
     AdamSegments segs;
-    int max_w = 1;
+    int64_t max_count = 1;
     for (int s = 0; s < n_segments; ++s) {
-        MG_REQUIRE(segments[s].width > 0 && segments[s].offset >= 0, "adam_multi: bad segment");
-        segs.offset[s] = segments[s].offset;
-        segs.width[s] = segments[s].width;
-        segs.lr[s] = segments[s].lr;
-        max_w = std::max(max_w, (int)segments[s].width);
+        const mg_adam_segment& g = segments[s];
+        MG_REQUIRE(g.width > 0 && g.offset >= 0, "adam_multi: bad segment");
+        const int64_t full = rows * (int64_t)g.width;
+        const int64_t b = g.elem_end > 0 ? g.elem_begin : 0;
+        const int64_t e = g.elem_end > 0 ? g.elem_end : full;
+        MG_REQUIRE(0 <= b && b <= e && e <= full, "adam_multi: element range outside the segment");
+        segs.offset[s] = g.offset;
+        segs.begin[s] = b;
+        segs.count[s] = e - b;
+        segs.width[s] = g.width;
+        segs.lr[s] = g.lr;
+        max_count = std::max(max_count, e - b);
     }
     const double bc1 = visible_count ? 1.0 : 1.0 - std::pow((double)b1, (double)step);
     const double sq = visible_count ? 1.0 : std::sqrt(1.0 - std::pow((double)b2, (double)step));
     const float w1 = (float)(1.0 - (double)b1), w2 = (float)(1.0 - (double)b2);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int gx = (int)std::min<int64_t>((rows * max_w + 255) / 256, 148 * 8);
-    adam_multi_kernel<<<dim3(std::max(gx, 1), n_segments), 256, 0, st>>>(
-        p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, (float)bc1, (float)sq);
-    MG_TRY(check_launch("adam_multi"));
+    const int gx = (int)std::min<int64_t>((max_count + 255) / 256, 148 * 8);
+    if (n_segments > 0) {
+        adam_multi_kernel<<<dim3(std::max(gx, 1), n_segments), 256, 0, st>>>(
+            p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, (float)bc1,
+            (float)sq);
+        MG_TRY(check_launch("adam_multi"));
+    }
     if (visible_count) {
         advance_steps_count_kernel<<<ceil_div(rows, 256), 256, 0, st>>>(steps, visible_count, rows);
         return check_launch("adam_multi steps");

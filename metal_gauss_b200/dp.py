@@ -45,3 +45,53 @@ def exchange(flat_grad: torch.Tensor, loss: torch.Tensor, group=None) -> None:
     import torch.distributed as dist
     dist.all_reduce(flat_grad, op=dist.ReduceOp.SUM, group=group)
     dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=group)
+
+
+def rank(group=None) -> int:
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group)
+    return 0
+
+
+def shard_rows(n_pad: int, rank_: int, world: int) -> tuple[int, int]:
+    """Row range [lo, hi) of the Gaussians whose optimizer state this rank
+    owns; n_pad is a multiple of world."""
+    per = n_pad // world
+    return rank_ * per, (rank_ + 1) * per
+
+
+def reduce_scatter_segment(seg: torch.Tensor, group=None) -> None:
+    """Sum a (rows x width) segment over ranks, leaving rank r's row shard
+    summed in place (other rows are left undefined). NCCL does it as an
+    in-place reduce-scatter; gloo (CPU tests), which has none, as an
+    all-reduce."""
+    import torch.distributed as dist
+    world = world_size(group)
+    if world == 1:
+        return
+    if dist.get_backend(group) == "nccl":
+        chunk = seg.numel() // world
+        r = rank(group)
+        dist.reduce_scatter_tensor(seg[r * chunk:(r + 1) * chunk], seg, group=group)
+    else:
+        dist.all_reduce(seg, group=group)
+
+
+def all_gather_segment(seg: torch.Tensor, group=None) -> None:
+    """Every rank's row shard of a segment, gathered in place on all ranks."""
+    import torch.distributed as dist
+    world = world_size(group)
+    if world == 1:
+        return
+    chunk = seg.numel() // world
+    r = rank(group)
+    dist.all_gather_into_tensor(seg, seg[r * chunk:(r + 1) * chunk].clone()
+                                if dist.get_backend(group) != "nccl"
+                                else seg[r * chunk:(r + 1) * chunk], group=group)
+
+
+def all_reduce_(t: torch.Tensor, group=None) -> None:
+    import torch.distributed as dist
+    if world_size(group) > 1:
+        dist.all_reduce(t, group=group)

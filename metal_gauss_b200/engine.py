@@ -98,9 +98,17 @@ class Trainer:
                  background=(0.0, 0.0, 0.0), lrs: dict | None = None, w_l1: float = 0.8,
                  w_ssim: float = 0.2, selective: bool = True, near: float = 0.01,
                  far: float = 100.0, max_radius_frac: float = 1.0, group=None,
-                 betas=(0.9, 0.999), eps: float = 1e-15):
+                 betas=(0.9, 0.999), eps: float = 1e-15, shard_optimizer: bool | None = None):
         self.device = torch.device(device)
         self.n = n = int(params["means"].shape[0])
+        self.world = dp.world_size(group)
+        self.rank = dp.rank(group)
+        # ZeRO-1: with several ranks each one owns the optimizer state of a
+        # contiguous range of Gaussian rows (gradient reduce-scatter, Adam on
+        # the shard, parameter all-gather); rows are padded to a multiple of
+        # the world size so every segment splits into equal row shards
+        self.shard_optimizer = (self.world > 1) if shard_optimizer is None else shard_optimizer
+        self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
             else tuple(float(b) for b in background)
@@ -117,20 +125,26 @@ class Trainer:
         off = 0
         for name, w in SEGMENTS:
             self.offsets[name] = off
-            off += (w * n + 63) // 64 * 64
-        self.vis_offset = off
-        self.P = torch.zeros(off, **f32)
-        self.G = torch.zeros(off + n, **f32)
-        self.M = torch.zeros(off, **f32)
-        self.V = torch.zeros(off, **f32)
-        self.steps = torch.zeros(n, **f32)
+            off += (w * self.n_pad + 63) // 64 * 64
+        # parameter region padded so it splits into equal 64-float-aligned
+        # chunks, one per rank (the unit of the reduce-scatter / all-gather)
+        unit = 64 * self.world
+        self.p_total = -(-off // unit) * unit
+        self.vis_offset = self.p_total
+        # gradient buffer: parameter region | visibility counts | loss
+        self.loss_offset = self.vis_offset + self.n_pad
+        self.P = torch.zeros(self.p_total, **f32)
+        self.G = torch.zeros(self.loss_offset + 64, **f32)
+        self.M = torch.zeros(self.p_total, **f32)
+        self.V = torch.zeros(self.p_total, **f32)
+        self.steps = torch.zeros(self.n_pad, **f32)
         self.step_count = 0
         for name, _ in SEGMENTS:
             self.param(name).copy_(params[name].to(self.device, torch.float32).reshape(
                 (n,) + SHAPES[name]))
         self.scales = torch.empty(n, 3, **f32)
         self.opac = torch.empty(n, **f32)
-        self.loss = torch.zeros(1, **f32)
+        self.loss = self.G[self.loss_offset:self.loss_offset + 1]
         self.window = torch.empty(11, **f32)
         x = torch.arange(11, dtype=torch.float32) - 5
         w = torch.exp(-x ** 2 / (2 * 1.5 ** 2))
@@ -186,6 +200,14 @@ class Trainer:
 
     def visibility_count(self) -> torch.Tensor:
         return self.G[self.vis_offset:self.vis_offset + self.n]
+
+    def _segment(self, buf: torch.Tensor, name: str) -> torch.Tensor:
+        """A whole padded segment (n_pad rows) of a flat buffer."""
+        if name == "visibility":
+            return buf[self.vis_offset:self.vis_offset + self.n_pad]
+        w = dict(SEGMENTS)[name]
+        o = self.offsets[name]
+        return buf[o:o + w * self.n_pad]
 
     def state_dict(self) -> dict:
         return {name: self.param(name).detach().clone() for name, _ in SEGMENTS}
@@ -333,15 +355,34 @@ class Trainer:
         return stats
 
     def optimizer_step(self) -> None:
+        """Adam over this rank's share: every element, or under ZeRO-1 the
+        rank's contiguous chunk of the flat parameter region (segments clipped
+        to it; a chunk may start or end inside a row)."""
         self.step_count += 1
-        segs = (_lib.AdamSegment * len(SEGMENTS))(
-            *[_lib.AdamSegment(self.offsets[name], w, self.lrs[name]) for name, w in SEGMENTS])
+        if self.shard_optimizer:
+            chunk = self.p_total // self.world
+            c_lo, c_hi = self.rank * chunk, (self.rank + 1) * chunk
+        else:
+            c_lo, c_hi = 0, self.p_total
+        segs = []
+        for name, w in SEGMENTS:
+            o = self.offsets[name]
+            b = max(c_lo, o) - o
+            e = min(c_hi, o + w * self.n) - o
+            if e > b:
+                segs.append(_lib.AdamSegment(o, w, self.lrs[name], b, e))
         b1, b2 = self.betas
         vis = self.visibility_count() if self.selective else None
         ev = self._begin("adam")
-        _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
-                  segs, len(SEGMENTS), b1, b2, self.eps, ptr(vis), ptr(self.steps),
-                  self.step_count, _lib.stream())
+        if segs:
+            arr = (_lib.AdamSegment * len(segs))(*segs)
+            _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
+                      arr, len(segs), b1, b2, self.eps, ptr(vis), ptr(self.steps),
+                      self.step_count, _lib.stream())
+        elif vis is not None:  # no elements here: still advance the shared step counts
+            _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
+                      (_lib.AdamSegment * 1)(_lib.AdamSegment(0, 1, 0.0, 0, 0)), 0, b1, b2,
+                      self.eps, ptr(vis), ptr(self.steps), self.step_count, _lib.stream())
         self._end(ev)
 
     def train_step(self, views, targets, global_batch: int | None = None) -> torch.Tensor:
@@ -358,9 +399,19 @@ class Trainer:
         self.loss.zero_()
         self._end(ev)
         self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb)
+        if world > 1 and self.shard_optimizer:
+            ev = self._begin("reduce_scatter")
+            dp.all_reduce_(self.G[self.vis_offset:], self.group)     # visibility + loss
+            dp.reduce_scatter_segment(self.G[:self.p_total], self.group)
+            self._end(ev)
+            self.optimizer_step()
+            ev = self._begin("all_gather")
+            dp.all_gather_segment(self.P, self.group)
+            self._end(ev)
+            return self.loss
         if world > 1:
             ev = self._begin("allreduce")
-            dp.exchange(self.G, self.loss, self.group)
+            dp.all_reduce_(self.G, self.group)
             self._end(ev)
         self.optimizer_step()
         return self.loss

@@ -129,3 +129,29 @@ def test_a_dead_rank_is_detected_by_its_peer(tmp_path):
         p.join(120)
     status = (tmp_path / "status.txt").read_text()
     assert status.startswith("error"), status
+
+
+def _shard_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    n_pad, width = 8, 3
+    g = torch.arange(n_pad * width, dtype=torch.float32) * (rank + 1)   # rank's gradient
+    p = torch.ones(n_pad * width)                                     # replicated params
+    dp.reduce_scatter_segment(g, None)
+    lo, hi = dp.shard_rows(n_pad, rank, world)
+    p[lo * width:hi * width] -= 0.5 * g[lo * width:hi * width]        # update own shard only
+    dp.all_gather_segment(p, None)
+    torch.save(p, os.path.join(out_dir, f"p{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_sharded_update_matches_the_replicated_one(tmp_path):
+    """ZeRO-1 plumbing: reduce-scatter of a gradient segment, an update on
+    each rank's row shard, all-gather of the parameters."""
+    port = _free_port()
+    mp.start_processes(_shard_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    p0, p1 = torch.load(tmp_path / "p0.pt"), torch.load(tmp_path / "p1.pt")
+    ref = 1.0 - 0.5 * (torch.arange(24, dtype=torch.float32) * 3)     # sum over ranks 1 + 2
+    assert torch.equal(p0, p1) and torch.allclose(p0, ref)
