@@ -189,14 +189,16 @@ def stage_bytes(stage: str, n: int, walked: float, P: int, n_tiles: int,
     rasteriser only touches the list entries it walks (each tile's list up to
     its largest stop index), so those -- not all pairs -- are counted."""
     if stage == "raster_bwd":
-        # per walked entry: id (4) + gathered uv/conic/opacity/colour (36);
-        # per pixel: T, stop, dL/drgb (24); per visible Gaussian: its 48-byte
+        # per walked entry: id (4) + the 48-byte splat record; per pixel: T,
+        # stop, alpha, rgb, dL/drgb (36); per visible Gaussian: its 48-byte
         # gradient record
-        return 40.0 * walked + 24.0 * P + 48.0 * n_vis
+        return 52.0 * walked + 36.0 * P + 48.0 * n_vis
     if stage == "raster_fwd":
-        # per walked entry 40; per tile offsets + order + walk (12); per pixel
+        # per walked entry 52; per tile offsets + order + walk (12); per pixel
         # rgb, alpha, T, stop out (24)
-        return 40.0 * walked + 12.0 * n_tiles + 24.0 * P
+        return 52.0 * walked + 12.0 * n_tiles + 24.0 * P
+    if stage == "pack":
+        return (36.0 + 48.0) * n
     if stage == "preprocess_fwd":
         return (44.0 + 192.0 + 48.0) * n
     if stage == "preprocess_bwd":

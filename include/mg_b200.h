@@ -259,42 +259,66 @@ mg_status mg_bin_emit(
 /* Rasterisation                                                            */
 /* ------------------------------------------------------------------------ */
 
+/* The rasterisers read one 48-byte record per splat (12 floats, 16-byte
+ * aligned), packed from the reference's separate uv / conic / opacity /
+ * colour arrays by mg_pack_splats. The record layout is private to the
+ * library. */
+#define MG_SPLAT_FLOATS 12
+#define MG_SPLAT_BYTES 48
+
+/* List entries between two forward checkpoints; the backward splits every
+ * warp block's walk into segments of this many entries. */
+#define MG_RASTER_SEGMENT 256
+
+/* Packs n splats into `splats` (n * MG_SPLAT_BYTES, 16-byte aligned). The
+ * reference's rasterize_forward / rasterize_backward (rasterize.mm:79-194)
+ * take uv (N,2), conic (N,3), opacity (N,), color (N,3); a caller of this ABI
+ * packs them once per view and hands the record array to both passes. */
+mg_status mg_pack_splats(const float* uv, const float* conic, const float* opacity,
+                         const float* color, int64_t n, void* splats, mg_stream_t stream);
+
+/* Bytes of rasteriser scratch for one view of width x height with `m`
+ * (tile, splat) pairs: work counters, the tile order, per-warp-block walk
+ * lengths, the backward's work items and the forward's checkpoints. */
+size_t mg_raster_scratch_bytes(int32_t width, int32_t height, int32_t tile, int64_t m);
+
 /* Replaces rasterize_forward (rasterize.mm:79-113; rasterize.metal:61-167).
- * One CTA per tile, tile in {8, 12, 16, 32}. Outputs rgb (H,W,3),
+ * splats from mg_pack_splats, gauss_ids / tile_offsets from binning with m =
+ * tile_offsets[n_tiles] pairs, tile in {8, 12, 16, 32}. Outputs rgb (H,W,3),
  * alpha (H,W), final transmittance T (H,W), stop index (H,W) int32.
  * background: NULL, or 3 host floats blended as rgb + max(1-alpha,0)*bg,
- * which is metal_backend.py:539-541 folded into the kernel.
- * tile_order (optional, n_tiles ids from mg_tile_order) is the order in which
- * CTAs take tiles -- heaviest first, so long tiles do not form the tail.
- * tile_work (optional, n_tiles ints) receives each tile's walk length, the
- * largest stop index minus the tile's first index: the backward's cost. */
+ * which is metal_backend.py:539-541 folded into the kernel. tile_work
+ * (optional, n_tiles ints) receives each tile's walk length, the largest stop
+ * index minus the tile's first index. scratch (mg_raster_scratch_bytes,
+ * 16-byte aligned) receives the state the backward of the same view reads
+ * when called with segmented = 1; keep it unchanged until then. */
 mg_status mg_rasterize_forward(
-    const float* uv, const float* conic, const float* opacity,
-    const float* color, const int32_t* gauss_ids, const int32_t* tile_offsets,
+    const void* splats, const int32_t* gauss_ids, const int32_t* tile_offsets, int64_t m,
     int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
     const float* background, float* out_rgb, float* out_alpha, float* out_T,
-    int32_t* out_stop, const int32_t* tile_order, int32_t* tile_work,
+    int32_t* out_stop, int32_t* tile_work, void* scratch, size_t scratch_bytes,
     mg_stream_t stream);
 
 /* Replaces rasterize_backward (rasterize.mm:147-194; rasterize.metal:
  * 173-340). grad2d (N, MG_G2D_STRIDE) is ACCUMULATED into (zero it first for
  * a fresh gradient). background as in the forward: the blend's adjoint is
- * applied in-kernel, which needs the forward's alpha (H,W) (ignored when
- * background is NULL; grad_alpha may then also be NULL for zero).
- * want_absgrad adds per-pixel |d uv| into MG_G2D_ABSUV. tile_order is
- * optional, as in the forward (order the tiles by the forward's tile_work).
- */
+ * applied in-kernel, which needs the forward's alpha (H,W) (grad_alpha may be
+ * NULL for zero). want_absgrad adds per-pixel |d uv| into MG_G2D_ABSUV.
+ * segmented = 1: `scratch` is the one the forward of this view filled; each
+ * warp block's walk is split into MG_RASTER_SEGMENT-entry segments that start
+ * from the forward's checkpoints (needs out_rgb and out_alpha of that
+ * forward). segmented = 0: scratch is workspace only and every block walks
+ * its whole list (out_rgb unused; out_alpha only with a background). */
 mg_status mg_rasterize_backward(
-    const float* uv, const float* conic, const float* opacity,
-    const float* color, const int32_t* gauss_ids, const int32_t* tile_offsets,
-    const float* final_T, const int32_t* stop, const float* grad_rgb,
-    const float* grad_alpha, int32_t width, int32_t height, int32_t tile,
-    int32_t tiles_x, const float* background, const float* alpha,
-    int32_t want_absgrad, int64_t n, float* grad2d, const int32_t* tile_order,
-    mg_stream_t stream);
+    const void* splats, const int32_t* gauss_ids, const int32_t* tile_offsets, int64_t m,
+    const float* out_rgb, const float* out_alpha, const float* final_T,
+    const int32_t* stop, const float* grad_rgb, const float* grad_alpha,
+    int32_t width, int32_t height, int32_t tile, int32_t tiles_x,
+    const float* background, int32_t want_absgrad, int64_t n, float* grad2d,
+    int32_t segmented, void* scratch, size_t scratch_bytes, mg_stream_t stream);
 
-/* Tile ids ordered by decreasing work, for the rasteriser's tile_order:
- * work[t] when `work` is given (e.g. the forward's tile_work), else the list
+/* Tile ids ordered by decreasing work: work[t] when `work` is given (e.g.
+ * the forward's tile_work), else the list
  * length tile_offsets[t+1] - tile_offsets[t]. Bucketed by powers of two
  * (order inside a bucket is unspecified; results do not depend on it). */
 mg_status mg_tile_order(const int32_t* tile_offsets, const int32_t* work,

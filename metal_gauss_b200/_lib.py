@@ -20,6 +20,8 @@ LIB_PATH = build_native.LIB
 
 G2D_STRIDE = 12
 G2D_UV, G2D_OPACITY, G2D_ABSUV, G2D_CONIC, G2D_COLOR = 0, 2, 3, 4, 8
+SPLAT_FLOATS = 12        # MG_SPLAT_FLOATS: one packed splat record
+RASTER_SEGMENT = 256     # MG_RASTER_SEGMENT
 
 
 class Camera(C.Structure):
@@ -69,10 +71,12 @@ SIGNATURES = {
     "mg_bin_prepare": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp, sz, vp]),
     "mg_bin_emit_scratch_bytes": (sz, [i64, i64, i32]),
     "mg_bin_emit": (i32, [vp, vp, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
-    "mg_rasterize_forward": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp,
-                                   vp, vp, vp, vp]),
-    "mg_rasterize_backward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
-                                    vp, vp, i32, i64, vp, vp, vp]),
+    "mg_pack_splats": (i32, [vp, vp, vp, vp, i64, vp, vp]),
+    "mg_raster_scratch_bytes": (sz, [i32, i32, i32, i64]),
+    "mg_rasterize_forward": (i32, [vp, vp, vp, i64, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,
+                                   vp, sz, vp]),
+    "mg_rasterize_backward": (i32, [vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
+                                    vp, i32, i64, vp, i32, vp, sz, vp]),
     "mg_tile_order": (i32, [vp, vp, i32, vp, vp]),
     "mg_pack_intersections": (i32, [vp, vp, vp, vp, vp, i64, vp, vp, vp, vp]),
     "mg_adam_step": (i32, [vp, vp, vp, vp, i64, f32, f32, f32, f32, f32, f32, vp]),

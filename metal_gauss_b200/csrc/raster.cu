@@ -1,128 +1,115 @@
 // Tile rasterisation, forward and backward (rasterize.metal:61-340).
 //
-// One CTA per screen tile; full 8x4 pixel blocks per warp when the tile side
-// is a multiple of 8 (compact warps reach fewer Gaussians), otherwise
-// row-major pixels with the CTA padded to whole warps.
+// Splat records. Before rasterising, each splat is packed into one 48-byte
+// record (mg_pack_splats): centre, the conic pre-scaled so the exponent is
+// A dx^2 + B dx dy + C dy^2 (A = -ca/2, B = -cb, C = -cc/2 are exact power-of-
+// two scalings), opacity, colour and the constants of the rectangle cull. A
+// list entry then costs three 16-byte loads instead of eight scalar gathers.
 //
-// Every warp walks the tile's depth-sorted list ON ITS OWN, 32 entries at a
-// time: each lane gathers one entry into warp-private shared memory and tests
-// it against the warp's rectangle of pixel centres (the minimum of the conic's
-// quadratic form over the rectangle against 2 ln(255 op), the reference's
-// per-simdgroup cull, rasterize.metal:13-38); the warp then evaluates only the
-// live entries (a ballot mask) and leaves the list as soon as its own 32
-// pixels are done. There is no CTA barrier inside the walk, so a warp never
-// waits for a slower one. Tiles are taken in a caller-given order (heaviest
-// first, mg_tile_order) so long tiles do not form the kernel's tail.
+// Work units. A tile's pixels are split into warp blocks of 32 pixels (8x4
+// when the tile side is a multiple of 8, else row-major pixels padded to whole
+// warps). Both kernels are persistent: every warp takes work items from a
+// device counter until the list is exhausted, so a warp that finishes early
+// takes more work instead of idling behind a slow one.
 //
-// Forward: front to back, alpha = min(0.999, op exp(power)), skip power > 0
-// or alpha < 1/255, stop a pixel once T < 1e-4 and record the stop INDEX.
+// Walk. A warp walks its tile's depth-sorted list 32 entries (a chunk) at a
+// time. The records of the next chunk are copied into the warp's shared-memory
+// double buffer with cp.async while the current chunk is processed, and the
+// list ids two chunks ahead are loaded into registers, so one chunk's gather
+// latency overlaps the previous chunk's arithmetic. Each lane tests its entry
+// against the warp's rectangle of pixel centres (the reference's per-simdgroup
+// cull, rasterize.metal:13-38, done as the largest exponent over the rectangle
+// against -ln(255 op) with a margin); the warp then evaluates only the live
+// entries (a ballot mask).
 //
-// Backward: back to front from the warp's largest stop index, recovering T
-// by division. Per live entry the warp reduces its 32 pixels' contributions
-// with a 16-slot butterfly reduce-scatter (16 shuffles for all components
-// instead of 5 per component) and three lanes add the 48-byte gradient record
-// to global memory with three 16-byte vector atomics.
+// Forward, front to back: alpha = min(0.999, op exp(power)), skip power > 0 or
+// alpha < 1/255, stop a pixel once T < 1e-4 and record the stop INDEX. Live
+// entries are taken two at a time: both exponentials are evaluated before
+// either blend, so their latencies overlap, and the blends stay in list order.
+// Every MG_RASTER_SEGMENT entries of a tile's list the forward stores each
+// pixel's running state (T, accumulated rgb, accumulated alpha): a checkpoint.
+//
+// Backward, back to front: work items are (warp block, segment) pairs, a
+// segment being MG_RASTER_SEGMENT consecutive entries of the block's walk,
+// longest first. A segment starts from the checkpoint at its upper end (T
+// there; the colour behind it is the final colour minus the checkpointed one),
+// so a long list is split over many warps instead of forming the kernel's
+// tail. Per live entry the warp reduces its 32 pixels' contributions with a
+// 16-slot butterfly reduce-scatter and three lanes add the 48-byte gradient
+// record to global memory with 16-byte vector atomics.
+#include <mutex>
+#include <unordered_map>
+
 #include "kernels.cuh"
 
 namespace mg {
 
 namespace {
 
-// One list entry as a warp stages it (36 B: two 16-byte and one 4-byte
-// shared-memory words).
-struct StagedGauss {
-    float u, v, op, ca;
-    float cb, cc, r, g;
-    float b;
-};
+constexpr int kSeg = MG_RASTER_SEGMENT;
+static_assert(kSeg % 32 == 0 && (kSeg & (kSeg - 1)) == 0,
+              "segments are a power of two number of whole chunks");
+constexpr int kRasterWarps = 4;  // warps per CTA of the persistent kernels
 
-// Quadratic form and alpha for one (pixel, Gaussian) pair. Shared by the
-// forward and the backward and written with explicitly rounded operations, so
-// both passes take bit-identical blend decisions.
-__device__ __forceinline__ float pair_power(float dx, float dy, float ca, float cb,
-                                            float cc) {
-    const float q = __fmaf_rn(ca, __fmul_rn(dx, dx),
-                              __fmaf_rn(__fmul_rn(2.0f, cb), __fmul_rn(dx, dy),
-                                        __fmul_rn(cc, __fmul_rn(dy, dy))));
-    return __fmul_rn(-0.5f, q);
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// ---------------------------------------------------------------- records
+
+__global__ void pack_splats_kernel(const float2* __restrict__ uv,
+                                   const float* __restrict__ conic,
+                                   const float* __restrict__ opacity,
+                                   const float* __restrict__ color, int64_t n,
+                                   float4* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float2 m = uv[i];
+    const float ca = conic[3 * i], cb = conic[3 * i + 1], cc = conic[3 * i + 2];
+    const float op = opacity[i];
+    const float oa = 255.0f * op;
+    // live iff max exponent over a rectangle > pthr; -ln(255 op) is the exact
+    // bound (alpha >= 1/255), widened by a relative and an absolute margin
+    const float pthr = oa > 1.0f ? -(logf(oa) * 1.0001f + 5e-5f) : __int_as_float(0x7f800000);
+    out[3 * i] = make_float4(m.x, m.y, -0.5f * ca, -cb);
+    out[3 * i + 1] = make_float4(-0.5f * cc, op, color[3 * i], color[3 * i + 1]);
+    out[3 * i + 2] = make_float4(color[3 * i + 2], cb / fmaxf(ca, 1e-12f),
+                                 cb / fmaxf(cc, 1e-12f), pthr);
 }
 
-__device__ __forceinline__ float pair_gauss(float power) { return __expf(power); }
+// Exponent of one (pixel, splat) pair with explicitly rounded operations, so
+// the forward and the backward take bit-identical blend decisions.
+__device__ __forceinline__ float pair_power(float dx, float dy, float A, float B, float C) {
+    return __fmaf_rn(A, __fmul_rn(dx, dx),
+                     __fmaf_rn(B, __fmul_rn(dx, dy), __fmul_rn(C, __fmul_rn(dy, dy))));
+}
 
-// Minimum of the conic's quadratic form over a rectangle (binning.metal:25-44),
-// in ordinary fast arithmetic: it only decides a conservative skip.
-__device__ __forceinline__ float min_q_rect_fast(float mux, float muy, float ca, float cb,
-                                                 float cc, float x0, float x1, float y0,
-                                                 float y1) {
-    if (mux >= x0 && mux <= x1 && muy >= y0 && muy <= y1) return 0.0f;
-    const float a = fmaxf(ca, 1e-12f), c = fmaxf(cc, 1e-12f);
-    const float ia = 1.0f / a, ic = 1.0f / c;
-    float best = __int_as_float(0x7f800000);
+// Is the record live for a warp whose pixel centres span [x0,x1] x [y0,y1]?
+// The largest exponent over the rectangle (binning.metal:25-44 for the
+// quadratic form's minimum): at the centre when it lies inside, else on an
+// edge at the clamped stationary point. q0 = {u, v, A, B}, C, q2 = {b, kx,
+// ky, pthr} with kx = cb/ca, ky = cb/cc.
+__device__ __forceinline__ bool rect_live(const float4 q0, const float C, const float4 q2,
+                                          float x0, float x1, float y0, float y1) {
+    const float u = q0.x, v = q0.y, A = q0.z, B = q0.w;
+    const float kx = q2.y, ky = q2.z, pthr = q2.w;
+    if (!(pthr < 0.0f)) return false;  // opacity at most 1/255
+    if (u >= x0 && u <= x1 && v >= y0 && v <= y1) return true;
+    float best = -3.0e38f;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-        const float yc = e == 0 ? y0 : y1;
-        const float ey = yc - muy;
-        const float ex = fminf(fmaxf(mux - cb * ey * ia, x0), x1) - mux;
-        best = fminf(best, a * ex * ex + 2.0f * cb * ex * ey + c * ey * ey);
+        const float ey = (e == 0 ? y0 : y1) - v;
+        const float ex = fminf(fmaxf(u - kx * ey, x0), x1) - u;
+        best = fmaxf(best, A * ex * ex + B * ex * ey + C * ey * ey);
     }
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-        const float xc = e == 0 ? x0 : x1;
-        const float ex = xc - mux;
-        const float ey = fminf(fmaxf(muy - cb * ex * ic, y0), y1) - muy;
-        best = fminf(best, a * ex * ex + 2.0f * cb * ex * ey + c * ey * ey);
+        const float ex = (e == 0 ? x0 : x1) - u;
+        const float ey = fminf(fmaxf(v - ky * ex, y0), y1) - v;
+        best = fmaxf(best, A * ex * ex + B * ex * ey + C * ey * ey);
     }
-    return best;
+    return best > pthr;
 }
 
-
-
-__device__ __forceinline__ StagedGauss stage_one(const float2* __restrict__ uv,
-                                                 const float* __restrict__ conic,
-                                                 const float* __restrict__ opacity,
-                                                 const float* __restrict__ color, int g) {
-    const float2 m = uv[g];
-    StagedGauss s;
-    s.u = m.x; s.v = m.y; s.op = opacity[g];
-    s.ca = conic[3 * g]; s.cb = conic[3 * g + 1]; s.cc = conic[3 * g + 2];
-    s.r = color[3 * g]; s.g = color[3 * g + 1]; s.b = color[3 * g + 2];
-    return s;
-}
-
-// Warp-private staging slots: float4 {u, v, op, ca}, float4 {cb, cc, r, g},
-// float b.
-struct WarpSlots {
-    float4 a[32];
-    float4 c[32];
-    float b[32];
-    int32_t id[32];
-    __device__ __forceinline__ void put(int k, const StagedGauss& s, int gid) {
-        a[k] = make_float4(s.u, s.v, s.op, s.ca);
-        c[k] = make_float4(s.cb, s.cc, s.r, s.g);
-        b[k] = s.b;
-        id[k] = gid;
-    }
-    __device__ __forceinline__ StagedGauss get(int k) const {
-        const float4 x = a[k], y = c[k];
-        StagedGauss s;
-        s.u = x.x; s.v = x.y; s.op = x.z; s.ca = x.w;
-        s.cb = y.x; s.cc = y.y; s.r = y.z; s.g = y.w;
-        s.b = b[k];
-        return s;
-    }
-};
-
-// Is this entry live for a warp whose pixel centres span [x0,x1] x [y0,y1]?
-__device__ __forceinline__ bool live_for_rect(const StagedGauss& g, float x0, float x1,
-                                              float y0, float y1) {
-    const float oa = 255.0f * g.op;
-    if (oa <= 1.0f || x0 > x1) return false;
-    const float thr = 2.0f * __logf(oa) * 1.0001f + 1e-4f;
-    return min_q_rect_fast(g.u, g.v, g.ca, g.cb, g.cc, x0, x1, y0, y1) < thr;
-}
-
-// Bounding rectangle of the warp's in-image pixel centres, in every lane
-// (x0 > x1 when the warp has no pixel in the image).
+// Bounding rectangle of the warp's in-image pixel centres, in every lane.
 __device__ __forceinline__ void warp_rect(bool inimg, float fx, float fy, float& x0, float& x1,
                                           float& y0, float& y1) {
     x0 = inimg ? fx : 3.0e38f; x1 = inimg ? fx : -3.0e38f;
@@ -136,114 +123,196 @@ __device__ __forceinline__ void warp_rect(bool inimg, float fx, float fy, float&
     }
 }
 
-// Work split: a tile's pixels are 8x4 warp blocks (row-major pixels padded
-// to whole warps when the side is not a multiple of 8). Warps walk the list
-// independently, so a CTA is only a scheduling unit: two warps (an 8x8
-// sub-block) per CTA when the side is a multiple of 8, which lets finished
-// sub-blocks free their registers while a slow one is still walking.
+// ---------------------------------------------------------------- staging
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// A warp's double-buffered chunk of records: q[buffer][word][entry], so a
+// lane's three copies land in consecutive 16-byte words of three rows and an
+// entry is read back as three broadcast loads.
+struct WarpStage {
+    float4 q[2][3][32];
+    int32_t id[2][32];
+    __device__ __forceinline__ void fetch(int buf, int lane, const float4* splats, int gid,
+                                          bool keep_id) {
+        const float4* src = splats + 3 * (int64_t)gid;
+        cp_async16(&q[buf][0][lane], src);
+        cp_async16(&q[buf][1][lane], src + 1);
+        cp_async16(&q[buf][2][lane], src + 2);
+        if (keep_id) id[buf][lane] = gid;
+    }
+};
+
+// Pixels of a tile in warp blocks: 8x4 when the side is a multiple of 8,
+// otherwise row-major with the last block padded.
 template <int TILE>
-struct TileGeom {
+struct Blocks {
     static constexpr int kPix = TILE * TILE;
-    static constexpr int kTileWarps = (kPix + 31) / 32;
-    static constexpr int kWarps = (TILE % 8 == 0) ? 2 : kTileWarps;  // per CTA
-    static constexpr int kThreads = kWarps * 32;
-    static constexpr int kCtasPerTile = kTileWarps / kWarps;
-    // pixel of lane `lane` in warp `wt` (0 .. kTileWarps-1) of the tile
-    __device__ __forceinline__ static void pixel(int wt, int lane, int& lx, int& ly) {
+    static constexpr int kCount = (kPix + 31) / 32;
+    static constexpr int kPixPad = kCount * 32;  // pixel slots of a checkpoint
+    __device__ __forceinline__ static void pixel(int wb, int lane, int& lx, int& ly) {
         if (TILE % 8 == 0) {
             const int bx = TILE / 8;
-            lx = (wt % bx) * 8 + (lane & 7);
-            ly = (wt / bx) * 4 + (lane >> 3);
+            lx = (wb % bx) * 8 + (lane & 7);
+            ly = (wb / bx) * 4 + (lane >> 3);
         } else {
-            const int t = wt * 32 + lane;
-            if (t < kPix) {
-                lx = t % TILE;
-                ly = t / TILE;
-            } else {
-                lx = TILE;  // padding thread, outside the tile
-                ly = TILE;
-            }
+            const int t = wb * 32 + lane;
+            lx = t < kPix ? t % TILE : TILE;  // padding lanes sit outside the tile
+            ly = t < kPix ? t / TILE : TILE;
         }
     }
 };
 
+// Checkpoint slot of boundary j (1-based: the state before entry start + j *
+// kSeg) of the tile whose list starts at `start`. Slots of consecutive tiles
+// never overlap and stay below m / kSeg + n_tiles.
+__device__ __forceinline__ int64_t ckpt_slot(int start, int tile_id, int j) {
+    return (int64_t)(start / kSeg) + tile_id + j - 1;
+}
+
+__device__ __forceinline__ int pull_item(int32_t* counter, int lane) {
+    int item = 0;
+    if (lane == 0) item = atomicAdd(counter, 1);
+    return __shfl_sync(0xffffffffu, item, 0);
+}
+
+// ---------------------------------------------------------------- forward
+
 template <int TILE>
-__global__ void __launch_bounds__(TileGeom<TILE>::kThreads)
-raster_forward_kernel(const float2* __restrict__ uv, const float* __restrict__ conic,
-                      const float* __restrict__ opacity, const float* __restrict__ color,
-                      const int32_t* __restrict__ ids,
+__global__ void __launch_bounds__(kRasterWarps * 32)
+raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ ids,
                       const int32_t* __restrict__ offsets, int W, int H, int tiles_x,
-                      int has_bg, float bg_r, float bg_g, float bg_b,
+                      int n_tiles, int has_bg, float bg_r, float bg_g, float bg_b,
                       float* __restrict__ out_rgb, float* __restrict__ out_alpha,
                       float* __restrict__ out_T, int32_t* __restrict__ out_stop,
-                      const int32_t* __restrict__ tile_order, int32_t* __restrict__ tile_work) {
-    using G = TileGeom<TILE>;
-    __shared__ WarpSlots s_w[G::kWarps];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int slot = blockIdx.x / G::kCtasPerTile;
-    const int tile_id = tile_order ? tile_order[slot] : slot;
-    const int tx = tile_id % tiles_x, ty = tile_id / tiles_x;
-    int lx, ly;
-    G::pixel((blockIdx.x % G::kCtasPerTile) * G::kWarps + warp, lane, lx, ly);
-    const bool in_tile = lx < TILE && ly < TILE;
-    const int px = tx * TILE + lx, py = ty * TILE + ly;
-    const bool inimg = in_tile && px < W && py < H;
-    const int start = offsets[tile_id], end = offsets[tile_id + 1];
-    const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-    float rx0, rx1, ry0, ry1;
-    warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
-    WarpSlots& slots = s_w[warp];
+                      const int32_t* __restrict__ order, int32_t* __restrict__ counter,
+                      int32_t* __restrict__ block_work, int32_t* __restrict__ tile_work,
+                      float* __restrict__ ckpt, int m_cap, int32_t* __restrict__ err) {
+    using G = Blocks<TILE>;
+    __shared__ WarpStage s_stage[kRasterWarps];
+    const int lane = threadIdx.x & 31;
+    WarpStage& st = s_stage[threadIdx.x >> 5];
+    const int n_items = n_tiles * G::kCount;
 
-    float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f, aa = 0.0f;
-    int stop = start;
-    bool done = !inimg;
-    bool warp_done = __all_sync(0xffffffffu, done);
-    for (int base = start; base < end && !warp_done; base += 32) {
-        const int i = base + lane;
-        bool lv = false;
-        if (i < end) {
-            const StagedGauss sg = stage_one(uv, conic, opacity, color, ids[i]);
-            lv = live_for_rect(sg, rx0, rx1, ry0, ry1);
-            if (lv) slots.put(lane, sg, 0);
+    for (int item = pull_item(counter, lane); item < n_items; item = pull_item(counter, lane)) {
+        const int tile_id = order[item / G::kCount];
+        const int wb = item % G::kCount;
+        int lx, ly;
+        G::pixel(wb, lane, lx, ly);
+        const int px = (tile_id % tiles_x) * TILE + lx, py = (tile_id / tiles_x) * TILE + ly;
+        const bool inimg = lx < TILE && ly < TILE && px < W && py < H;
+        const int start = offsets[tile_id];
+        int end = offsets[tile_id + 1];
+        if (end > m_cap) {  // lists beyond the sized pair count: report, render nothing
+            if (lane == 0) record_device_error(err, DEV_ERR_INDEX);
+            end = start;
         }
-        uint32_t live = __ballot_sync(0xffffffffu, lv);
-        __syncwarp();
-        while (live) {
-            const int k = __ffs(live) - 1;  // front to back
-            live &= live - 1;
-            if (done) continue;
-            const StagedGauss sj = slots.get(k);
-            const float power = pair_power(fx - sj.u, fy - sj.v, sj.ca, sj.cb, sj.cc);
-            if (power > 0.0f) continue;
-            const float alpha = fminf(0.999f, sj.op * pair_gauss(power));
-            if (alpha < 1.0f / 255.0f) continue;
-            const float w = alpha * T;
-            ar += w * sj.r; ag += w * sj.g; ab += w * sj.b;
-            aa += w;
-            T *= (1.0f - alpha);
-            stop = base + k + 1;
-            if (T < 1e-4f) done = true;
+        const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
+
+        float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f, aa = 0.0f;
+        int stop = start;
+        bool done = !inimg;
+        if (start < end && !__all_sync(0xffffffffu, done)) {
+            float rx0, rx1, ry0, ry1;
+            warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
+            float* ck = ckpt + wb * 32 + lane;
+            if (start + lane < end) st.fetch(0, lane, splats, ids[start + lane], false);
+            cp_async_commit();
+            int gid_next = start + 32 + lane < end ? ids[start + 32 + lane] : 0;
+            int buf = 0;
+            for (int base = start;; base += 32) {
+                const int nb = base + 32;
+                // buffer buf^1 was released by the previous chunk's last vote
+                if (nb + lane < end) st.fetch(buf ^ 1, lane, splats, gid_next, false);
+                cp_async_commit();
+                const int gid_after = nb + 32 + lane < end ? ids[nb + 32 + lane] : 0;
+                if (base != start && ((base - start) & (kSeg - 1)) == 0) {
+                    float* c = ck + ckpt_slot(start, tile_id, (base - start) / kSeg) * 5 *
+                                        G::kPixPad;
+                    c[0] = T;
+                    c[G::kPixPad] = ar;
+                    c[2 * G::kPixPad] = ag;
+                    c[3 * G::kPixPad] = ab;
+                    c[4 * G::kPixPad] = aa;
+                }
+                cp_async_wait<1>();
+                __syncwarp();
+                const bool lv = base + lane < end &&
+                                rect_live(st.q[buf][0][lane], st.q[buf][1][lane].x,
+                                          st.q[buf][2][lane], rx0, rx1, ry0, ry1);
+                uint32_t live = __ballot_sync(0xffffffffu, lv);
+                while (live) {
+                    const int k1 = __ffs(live) - 1;
+                    live &= live - 1;
+                    const bool two = live != 0u;
+                    const int k2 = two ? __ffs(live) - 1 : k1;
+                    live &= live - 1;
+                    const float4 a1 = st.q[buf][0][k1], b1 = st.q[buf][1][k1];
+                    const float c1 = st.q[buf][2][k1].x;
+                    const float4 a2 = st.q[buf][0][k2], b2 = st.q[buf][1][k2];
+                    const float c2 = st.q[buf][2][k2].x;
+                    const float p1 = pair_power(fx - a1.x, fy - a1.y, a1.z, a1.w, b1.x);
+                    const float p2 = pair_power(fx - a2.x, fy - a2.y, a2.z, a2.w, b2.x);
+                    const float al1 = fminf(0.999f, b1.y * __expf(p1));
+                    const float al2 = fminf(0.999f, b2.y * __expf(p2));
+                    if (!done && p1 <= 0.0f && al1 >= 1.0f / 255.0f) {
+                        const float w = al1 * T;
+                        ar += w * b1.z; ag += w * b1.w; ab += w * c1;
+                        aa += w;
+                        T *= (1.0f - al1);
+                        stop = base + k1 + 1;
+                        done = T < 1e-4f;
+                    }
+                    if (two && !done && p2 <= 0.0f && al2 >= 1.0f / 255.0f) {
+                        const float w = al2 * T;
+                        ar += w * b2.z; ag += w * b2.w; ab += w * c2;
+                        aa += w;
+                        T *= (1.0f - al2);
+                        stop = base + k2 + 1;
+                        done = T < 1e-4f;
+                    }
+                    if (__all_sync(0xffffffffu, done)) break;
+                }
+                const bool all_done = __all_sync(0xffffffffu, done);  // releases buffer buf
+                if (all_done || nb >= end) break;
+                buf ^= 1;
+                gid_next = gid_after;
+            }
+            cp_async_wait<0>();
+            __syncwarp();
         }
-        warp_done = __all_sync(0xffffffffu, done);
-        __syncwarp();  // slots are rewritten by the next chunk
+        const int walk = __reduce_max_sync(0xffffffffu, stop) - start;
+        if (lane == 0) {
+            block_work[tile_id * G::kCount + wb] = walk;
+            if (tile_work && walk > 0) atomicMax(&tile_work[tile_id], walk);
+        }
+        if (inimg) {
+            const int64_t o = (int64_t)py * W + px;
+            if (has_bg) {
+                const float k = fmaxf(1.0f - aa, 0.0f);
+                ar = ar + k * bg_r; ag = ag + k * bg_g; ab = ab + k * bg_b;
+            }
+            out_rgb[3 * o + 0] = ar;
+            out_rgb[3 * o + 1] = ag;
+            out_rgb[3 * o + 2] = ab;
+            out_alpha[o] = aa;
+            out_T[o] = T;
+            out_stop[o] = stop;
+        }
     }
-    if (tile_work) {  // zeroed by the launcher; the tile's walk = max stop - start
-        const int ws = __reduce_max_sync(0xffffffffu, stop) - start;
-        if (lane == 0 && ws > 0) atomicMax(&tile_work[tile_id], ws);
-    }
-    if (!inimg) return;
-    const int64_t o = (int64_t)py * W + px;
-    if (has_bg) {
-        const float k = fmaxf(1.0f - aa, 0.0f);
-        ar = ar + k * bg_r; ag = ag + k * bg_g; ab = ab + k * bg_b;
-    }
-    out_rgb[3 * o + 0] = ar;
-    out_rgb[3 * o + 1] = ag;
-    out_rgb[3 * o + 2] = ab;
-    out_alpha[o] = aa;
-    out_T[o] = T;
-    out_stop[o] = stop;
 }
+
+// ---------------------------------------------------------------- backward
 
 // 16-slot butterfly reduce-scatter across the warp: on return, lanes 2s and
 // 2s+1 hold the warp sum of slot s.
@@ -278,124 +347,247 @@ __device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
     return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
-template <int TILE>
-__global__ void __launch_bounds__(TileGeom<TILE>::kThreads)
-raster_backward_kernel(const float2* __restrict__ uv, const float* __restrict__ conic,
-                       const float* __restrict__ opacity, const float* __restrict__ color,
-                       const int32_t* __restrict__ ids,
-                       const int32_t* __restrict__ offsets,
-                       const float* __restrict__ final_T,
+// kSegmented: items are (block, segment) pairs and segments start from the
+// forward's checkpoints; otherwise one item per block walks the whole list
+// from the pixels' stop indices (no forward state needed).
+template <int TILE, bool kSegmented>
+__global__ void __launch_bounds__(kRasterWarps * 32)
+raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ ids,
+                       const int32_t* __restrict__ offsets, const float* __restrict__ out_rgb,
+                       const float* __restrict__ out_alpha, const float* __restrict__ final_T,
                        const int32_t* __restrict__ stop_idx,
                        const float* __restrict__ grad_rgb,
                        const float* __restrict__ grad_alpha, int W, int H, int tiles_x,
-                       int has_bg, float bg_r, float bg_g, float bg_b,
-                       const float* __restrict__ alpha_fwd, int want_absgrad,
-                       float* __restrict__ grad2d, const int32_t* __restrict__ tile_order) {
-    using G = TileGeom<TILE>;
-    __shared__ WarpSlots s_w[G::kWarps];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int slot = blockIdx.x / G::kCtasPerTile;
-    const int tile_id = tile_order ? tile_order[slot] : slot;
-    const int tx = tile_id % tiles_x, ty = tile_id / tiles_x;
-    int lx, ly;
-    G::pixel((blockIdx.x % G::kCtasPerTile) * G::kWarps + warp, lane, lx, ly);
-    const bool in_tile = lx < TILE && ly < TILE;
-    const int px = tx * TILE + lx, py = ty * TILE + ly;
-    const bool inimg = in_tile && px < W && py < H;
-    const int start = offsets[tile_id];
-    const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-    const int64_t o = inimg ? (int64_t)py * W + px : 0;
+                       int has_bg, float bg_r, float bg_g, float bg_b, int want_absgrad,
+                       float* __restrict__ grad2d, const int2* __restrict__ items,
+                       int32_t* __restrict__ counters, const float* __restrict__ ckpt,
+                       int m_cap, int32_t* __restrict__ err) {
+    using G = Blocks<TILE>;
+    __shared__ WarpStage s_stage[kRasterWarps];
+    const int lane = threadIdx.x & 31;
+    WarpStage& st = s_stage[threadIdx.x >> 5];
+    const int n_items = counters[2];
 
-    float T = inimg ? final_T[o] : 1.0f;
-    const int my_stop = inimg ? stop_idx[o] : start;
-    float gr = 0.f, gg = 0.f, gb = 0.f, ga = 0.f;
-    if (inimg) {
-        gr = grad_rgb[3 * o]; gg = grad_rgb[3 * o + 1]; gb = grad_rgb[3 * o + 2];
-        ga = grad_alpha ? grad_alpha[o] : 0.0f;
-        // rgb_out = rgb + max(1 - alpha, 0) * bg  =>  d alpha -= <d rgb, bg>
-        if (has_bg && 1.0f - alpha_fwd[o] >= 0.0f) ga -= gr * bg_r + gg * bg_g + gb * bg_b;
-    }
-    const int warp_stop = __reduce_max_sync(0xffffffffu, my_stop);
-    if (warp_stop <= start) return;  // this warp blended nothing
-    float rx0, rx1, ry0, ry1;
-    warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
-    WarpSlots& slots = s_w[warp];
-
-    float sr = 0.f, sg = 0.f, sb = 0.f, sa = 0.f;  // suffix colour / alpha
-    for (int cbase = start + ((warp_stop - 1 - start) >> 5) * 32; cbase >= start; cbase -= 32) {
-        const int i = cbase + lane;
-        bool lv = false;
-        if (i < warp_stop) {
-            const int gid = ids[i];
-            const StagedGauss st = stage_one(uv, conic, opacity, color, gid);
-            lv = live_for_rect(st, rx0, rx1, ry0, ry1);
-            if (lv) slots.put(lane, st, gid);
+    for (int item = pull_item(counters + 1, lane); item < n_items;
+         item = pull_item(counters + 1, lane)) {
+        const int2 it = items[item];
+        const int tile_id = it.x / G::kCount, wb = it.x % G::kCount, seg = it.y;
+        int lx, ly;
+        G::pixel(wb, lane, lx, ly);
+        const int px = (tile_id % tiles_x) * TILE + lx, py = (tile_id / tiles_x) * TILE + ly;
+        const bool inimg = lx < TILE && ly < TILE && px < W && py < H;
+        const int start = offsets[tile_id], end = offsets[tile_id + 1];
+        if (end > m_cap) {
+            if (lane == 0) record_device_error(err, DEV_ERR_INDEX);
+            continue;
         }
-        uint32_t live = __ballot_sync(0xffffffffu, lv);
-        __syncwarp();
-        while (live) {
-            const int k = 31 - __clz(live);  // back to front
-            live &= ~(1u << k);
-            const StagedGauss s = slots.get(k);
-            const float dx = fx - s.u, dy = fy - s.v;
-            const float power = pair_power(dx, dy, s.ca, s.cb, s.cc);
-            const float gauss = pair_gauss(fminf(power, 0.0f));
-            const float alpha_raw = s.op * gauss;
-            const bool clamped = alpha_raw > 0.999f;
-            const float alpha = fminf(0.999f, alpha_raw);
-            const bool active = inimg && (cbase + k < my_stop) && (power <= 0.0f) &&
-                                (alpha >= 1.0f / 255.0f);
-            const uint32_t act = __ballot_sync(0xffffffffu, active);
-            if (act == 0u) continue;
-            float v[16];
+        const int seg_lo = start + seg * kSeg;
+        const int seg_top = kSegmented ? min(seg_lo + kSeg, end) : end;
+        const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
+        const int64_t o = inimg ? (int64_t)py * W + px : 0;
+
+        float T = 1.0f, sr = 0.f, sg = 0.f, sb = 0.f, sa = 0.f;  // suffix colour / alpha
+        float gr = 0.f, gg = 0.f, gb = 0.f, ga = 0.f;
+        int my_stop = start;
+        if (inimg) {
+            my_stop = stop_idx[o];
+            gr = grad_rgb[3 * o]; gg = grad_rgb[3 * o + 1]; gb = grad_rgb[3 * o + 2];
+            ga = grad_alpha ? grad_alpha[o] : 0.0f;
+            const float a_fin = (has_bg || kSegmented) ? out_alpha[o] : 0.0f;
+            const float kbg = fmaxf(1.0f - a_fin, 0.0f);
+            // rgb_out = rgb + max(1 - alpha, 0) * bg  =>  d alpha -= <d rgb, bg>
+            if (has_bg && 1.0f - a_fin >= 0.0f) ga -= gr * bg_r + gg * bg_g + gb * bg_b;
+            if (kSegmented && my_stop > seg_lo + kSeg) {
+                const float* c = ckpt + ckpt_slot(start, tile_id, seg + 1) * 5 * G::kPixPad +
+                                 wb * 32 + lane;
+                float cr = out_rgb[3 * o], cg = out_rgb[3 * o + 1], cbl = out_rgb[3 * o + 2];
+                if (has_bg) { cr -= kbg * bg_r; cg -= kbg * bg_g; cbl -= kbg * bg_b; }
+                T = c[0];
+                sr = cr - c[G::kPixPad];
+                sg = cg - c[2 * G::kPixPad];
+                sb = cbl - c[3 * G::kPixPad];
+                sa = a_fin - c[4 * G::kPixPad];
+            } else {
+                T = final_T[o];
+            }
+        }
+        const int hi = inimg ? min(my_stop, seg_top) : seg_lo;
+        const int warp_hi = __reduce_max_sync(0xffffffffu, hi);
+        if (warp_hi <= seg_lo) continue;
+        float rx0, rx1, ry0, ry1;
+        warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
+
+        // chunks are aligned to the list start; seg_lo is a chunk boundary
+        int cbase = start + ((warp_hi - 1 - start) >> 5) * 32;
+        if (cbase + lane < warp_hi) st.fetch(0, lane, splats, ids[cbase + lane], true);
+        cp_async_commit();
+        int gid_next = cbase - 32 >= seg_lo ? ids[cbase - 32 + lane] : 0;
+        int buf = 0;
+        for (;;) {
+            const int nb = cbase - 32;
+            if (nb >= seg_lo) st.fetch(buf ^ 1, lane, splats, gid_next, true);
+            cp_async_commit();
+            const int gid_after = nb - 32 >= seg_lo ? ids[nb - 32 + lane] : 0;
+            cp_async_wait<1>();
+            __syncwarp();
+            const bool lv = cbase + lane < warp_hi &&
+                            rect_live(st.q[buf][0][lane], st.q[buf][1][lane].x,
+                                      st.q[buf][2][lane], rx0, rx1, ry0, ry1);
+            uint32_t live = __ballot_sync(0xffffffffu, lv);
+            while (live) {
+                const int k = 31 - __clz(live);  // back to front
+                live &= ~(1u << k);
+                const float4 a = st.q[buf][0][k], b4 = st.q[buf][1][k];
+                const float cbk = st.q[buf][2][k].x;
+                const float dx = fx - a.x, dy = fy - a.y;
+                const float power = pair_power(dx, dy, a.z, a.w, b4.x);
+                const float gauss = __expf(fminf(power, 0.0f));
+                const float alpha_raw = b4.y * gauss;
+                const bool clamped = alpha_raw > 0.999f;
+                const float alpha = fminf(0.999f, alpha_raw);
+                const bool active = inimg && (cbase + k < my_stop) && (power <= 0.0f) &&
+                                    (alpha >= 1.0f / 255.0f);
+                const uint32_t act = __ballot_sync(0xffffffffu, active);
+                if (act == 0u) continue;
+                float v[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) v[q] = 0.0f;
-            if (active) {
-                const float inv = __frcp_rn(fmaxf(1.0f - alpha, 1e-8f));
-                T = T * inv;
-                const float w = alpha * T;
-                v[8] = w * gr; v[9] = w * gg; v[10] = w * gb;
-                const float dL_dalpha = (gr * (T * s.r - sr * inv) + gg * (T * s.g - sg * inv) +
-                                         gb * (T * s.b - sb * inv)) +
-                                        ga * (T - sa * inv);
-                sr += alpha * T * s.r; sg += alpha * T * s.g; sb += alpha * T * s.b;
-                sa += alpha * T;
-                if (!clamped) {
-                    const float dp = dL_dalpha * s.op * gauss;
-                    v[2] = dL_dalpha * gauss;
-                    const float dux = dp * (s.ca * dx + s.cb * dy);
-                    const float duy = dp * (s.cb * dx + s.cc * dy);
-                    v[0] = dux; v[1] = duy;
-                    v[4] = dp * (-0.5f * dx * dx);
-                    v[5] = dp * (-1.0f * dx * dy);
-                    v[6] = dp * (-0.5f * dy * dy);
-                    if (want_absgrad) v[3] = sqrtf(dux * dux + duy * duy);
-                }
-            }
-            if (__popc(act) <= 2) {
-                // few contributing pixels: each adds its own record (the warp
-                // reduction costs more instructions than two sets of atomics)
+                for (int q = 0; q < 16; ++q) v[q] = 0.0f;
                 if (active) {
-                    float4* dst =
-                        reinterpret_cast<float4*>(grad2d + (int64_t)slots.id[k] * MG_G2D_STRIDE);
-                    atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
-                    if (v[4] != 0.f || v[5] != 0.f || v[6] != 0.f)
-                        atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
-                    atomicAdd(dst + 2, make_float4(v[8], v[9], v[10], 0.f));
+                    const float om = fmaxf(1.0f - alpha, 1e-8f);
+                    // segments bound the recovery chain to kSeg divisions
+                    const float inv = kSegmented ? __fdividef(1.0f, om) : __frcp_rn(om);
+                    T = T * inv;
+                    const float w = alpha * T;
+                    v[8] = w * gr; v[9] = w * gg; v[10] = w * gb;
+                    const float dL_dalpha =
+                        (gr * (T * b4.z - sr * inv) + gg * (T * b4.w - sg * inv) +
+                         gb * (T * cbk - sb * inv)) +
+                        ga * (T - sa * inv);
+                    sr += w * b4.z; sg += w * b4.w; sb += w * cbk;
+                    sa += w;
+                    if (!clamped) {
+                        const float dp = dL_dalpha * b4.y * gauss;
+                        v[2] = dL_dalpha * gauss;
+                        // d power / d u = ca dx + cb dy = -(2A dx + B dy)
+                        const float dux = -dp * (2.0f * a.z * dx + a.w * dy);
+                        const float duy = -dp * (a.w * dx + 2.0f * b4.x * dy);
+                        v[0] = dux; v[1] = duy;
+                        v[4] = dp * (-0.5f * dx * dx);
+                        v[5] = dp * (-1.0f * dx * dy);
+                        v[6] = dp * (-0.5f * dy * dy);
+                        if (want_absgrad) v[3] = sqrtf(dux * dux + duy * duy);
+                    }
                 }
-                continue;
+                float4* dst =
+                    reinterpret_cast<float4*>(grad2d + (int64_t)st.id[buf][k] * MG_G2D_STRIDE);
+                if (__popc(act) <= 2) {
+                    // few contributing pixels: each adds its own record (the
+                    // warp reduction costs more than two sets of atomics)
+                    if (active) {
+                        atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
+                        if (v[4] != 0.f || v[5] != 0.f || v[6] != 0.f)
+                            atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
+                        atomicAdd(dst + 2, make_float4(v[8], v[9], v[10], 0.f));
+                    }
+                    continue;
+                }
+                // lanes 2s, 2s+1 hold slot s; lanes 0, 8, 16 gather slots 0-3, 4-7, 8-11
+                const float r = reduce_scatter16(v, lane);
+                const float r1 = __shfl_down_sync(0xffffffffu, r, 2);
+                const float r2 = __shfl_down_sync(0xffffffffu, r, 4);
+                const float r3 = __shfl_down_sync(0xffffffffu, r, 6);
+                if ((lane & 7) == 0 && lane < 24 &&
+                    (r != 0.f || r1 != 0.f || r2 != 0.f || r3 != 0.f))
+                    atomicAdd(dst + (lane >> 3), make_float4(r, r1, r2, r3));
             }
-            // lanes 2s, 2s+1 hold slot s; lanes 0, 8, 16 gather slots 0-3, 4-7, 8-11
-            const float r = reduce_scatter16(v, lane);
-            const float r1 = __shfl_down_sync(0xffffffffu, r, 2);
-            const float r2 = __shfl_down_sync(0xffffffffu, r, 4);
-            const float r3 = __shfl_down_sync(0xffffffffu, r, 6);
-            if ((lane & 7) == 0 && lane < 24 && (r != 0.f || r1 != 0.f || r2 != 0.f || r3 != 0.f)) {
-                float4* dst = reinterpret_cast<float4*>(grad2d + (int64_t)slots.id[k] * MG_G2D_STRIDE);
-                atomicAdd(dst + (lane >> 3), make_float4(r, r1, r2, r3));
-            }
+            __syncwarp();  // buffer buf is refilled two chunks on
+            if (nb < seg_lo) break;
+            cbase = nb;
+            buf ^= 1;
+            gid_next = gid_after;
         }
-        __syncwarp();  // slots are rewritten by the next chunk
+        cp_async_wait<0>();
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------- ordering
+
+// Longest-first tile order: a one-CTA counting sort of the tiles by the
+// bucket floor(log2(work)) + 1, heaviest bucket first. Optionally zeroes a
+// work counter and a per-tile array for the kernel that follows.
+__global__ void __launch_bounds__(1024)
+tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ work,
+                  int n_tiles, int32_t* __restrict__ order, int32_t* __restrict__ zero_word,
+                  int32_t* __restrict__ zero_tiles) {
+    __shared__ int s_count[33];
+    __shared__ int s_cursor[33];
+    const int tid = threadIdx.x;
+    if (tid < 33) s_count[tid] = 0;
+    if (tid == 0 && zero_word) *zero_word = 0;
+    __syncthreads();
+    for (int t = tid; t < n_tiles; t += 1024) {
+        const int w = work ? work[t] : offsets[t + 1] - offsets[t];
+        const int b = w > 0 ? 32 - __clz(w) : 0;  // 0..31
+        atomicAdd(&s_count[31 - b], 1);            // heaviest bucket first
+        if (zero_tiles) zero_tiles[t] = 0;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int b = 0; b < 33; ++b) { s_cursor[b] = run; run += s_count[b]; }
+    }
+    __syncthreads();
+    for (int t = tid; t < n_tiles; t += 1024) {
+        const int w = work ? work[t] : offsets[t + 1] - offsets[t];
+        const int b = w > 0 ? 32 - __clz(w) : 0;
+        order[atomicAdd(&s_cursor[31 - b], 1)] = t;
+    }
+}
+
+// Backward work items, longest first: with segments (seg > 0), each block's
+// walk becomes floor(walk / seg) whole segments (bucket 0) plus one partial
+// segment in bucket clz(length) (longer partials first); without, one item
+// per block with a non-empty list, bucketed by its list length. One CTA; also
+// zeroes the backward's pull counter and publishes the item count.
+__global__ void __launch_bounds__(1024)
+backward_items_kernel(const int32_t* __restrict__ offsets,
+                      const int32_t* __restrict__ block_work, int n_tiles, int blocks_per_tile,
+                      int seg, int2* __restrict__ items, int32_t* __restrict__ counters) {
+    __shared__ int s_count[33];
+    __shared__ int s_cursor[33];
+    const int tid = threadIdx.x;
+    const int n_blocks = n_tiles * blocks_per_tile;
+    if (tid < 33) s_count[tid] = 0;
+    __syncthreads();
+    for (int b = tid; b < n_blocks; b += 1024) {
+        const int t = b / blocks_per_tile;
+        const int w = block_work ? block_work[b] : offsets[t + 1] - offsets[t];
+        if (w <= 0) continue;
+        const int full = seg > 0 ? w / seg : 0;
+        const int rem = w - full * seg;
+        if (full) atomicAdd(&s_count[0], full);
+        if (rem) atomicAdd(&s_count[__clz(rem)], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int k = 0; k < 33; ++k) { s_cursor[k] = run; run += s_count[k]; }
+        counters[1] = 0;
+        counters[2] = run;
+    }
+    __syncthreads();
+    for (int b = tid; b < n_blocks; b += 1024) {
+        const int t = b / blocks_per_tile;
+        const int w = block_work ? block_work[b] : offsets[t + 1] - offsets[t];
+        if (w <= 0) continue;
+        const int full = seg > 0 ? w / seg : 0;
+        const int rem = w - full * seg;
+        if (full) {
+            const int at = atomicAdd(&s_cursor[0], full);
+            for (int s = 0; s < full; ++s) items[at + s] = make_int2(b, s);
+        }
+        if (rem) items[atomicAdd(&s_cursor[__clz(rem)], 1)] = make_int2(b, full);
     }
 }
 
@@ -418,65 +610,116 @@ __global__ void pack_intersections_kernel(const float2* __restrict__ uv,
     p_rgb[3 * i + 2] = color[3 * g + 2];
 }
 
-// Longest-first tile order: a one-CTA counting sort of the tiles by the
-// bucket floor(log2(work)) + 1, heaviest bucket first.
-__global__ void __launch_bounds__(1024)
-tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ work,
-                  int n_tiles, int32_t* __restrict__ order) {
-    __shared__ int s_count[33];
-    __shared__ int s_cursor[33];
-    const int tid = threadIdx.x;
-    if (tid < 33) s_count[tid] = 0;
-    __syncthreads();
-    for (int t = tid; t < n_tiles; t += 1024) {
-        const int w = work ? work[t] : offsets[t + 1] - offsets[t];
-        const int b = w > 0 ? 32 - __clz(w) : 0;       // 0..31
-        atomicAdd(&s_count[31 - b], 1);                // heaviest bucket first
-    }
-    __syncthreads();
-    if (tid == 0) {
-        int run = 0;
-        for (int b = 0; b < 33; ++b) { s_cursor[b] = run; run += s_count[b]; }
-    }
-    __syncthreads();
-    for (int t = tid; t < n_tiles; t += 1024) {
-        const int w = work ? work[t] : offsets[t + 1] - offsets[t];
-        const int b = w > 0 ? 32 - __clz(w) : 0;
-        order[atomicAdd(&s_cursor[31 - b], 1)] = t;
-    }
+// ---------------------------------------------------------------- host side
+
+int blocks_per_tile(int tile) { return (tile * tile + 31) / 32; }
+
+// Scratch shared by one view's forward and backward.
+struct RasterScratch {
+    int32_t* counters;    // [0] forward pull, [1] backward pull, [2] backward item count
+    int32_t* order;       // n_tiles, longest list first
+    int32_t* block_work;  // n_blocks walk lengths (forward)
+    int2* items;          // backward work items
+    float* ckpt;          // checkpoint slots x 5 x pixel slots
+    size_t bytes;
+};
+
+RasterScratch carve_raster(void* base, int W, int H, int tile, int64_t m) {
+    const int64_t tiles_x = (W + tile - 1) / tile, tiles_y = (H + tile - 1) / tile;
+    const int64_t n_tiles = tiles_x * tiles_y;
+    const int bpt = blocks_per_tile(tile);
+    const int64_t n_blocks = n_tiles * bpt;
+    const int64_t m1 = std::max<int64_t>(m, 1);
+    // sum over blocks of ceil(walk / kSeg) <= n_blocks + bpt * m / kSeg
+    const int64_t n_items = n_blocks + (int64_t)bpt * ((m1 + kSeg - 1) / kSeg);
+    const int64_t slots = m1 / kSeg + n_tiles;
+    RasterScratch s;
+    char* p = static_cast<char*>(base);
+    s.counters = reinterpret_cast<int32_t*>(p); p += 256;
+    s.order = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * n_tiles);
+    s.block_work = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * n_blocks);
+    s.items = reinterpret_cast<int2*>(p); p += align256(sizeof(int2) * n_items);
+    s.ckpt = reinterpret_cast<float*>(p);
+    p += align256(sizeof(float) * (size_t)slots * 5 * (size_t)bpt * 32);
+    s.bytes = (size_t)(p - static_cast<char*>(base));
+    return s;
+}
+
+// CTAs that fit on the device at once, per (kernel, device).
+int persistent_grid(const void* kernel, int threads) {
+    static std::mutex mu;
+    static std::unordered_map<uint64_t, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const uint64_t key = (reinterpret_cast<uint64_t>(kernel) << 6) ^ (uint64_t)dev;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int per_sm = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 0;
+    const int grid = std::max(per_sm, 1) * sms;
+    cache[key] = grid;
+    return grid;
 }
 
 template <int TILE>
-mg_status launch_fwd(const float* uv, const float* conic, const float* opacity,
-                     const float* color, const int32_t* ids, const int32_t* offsets, int W,
+mg_status launch_fwd(const float4* splats, const int32_t* ids, const int32_t* offsets, int W,
                      int H, int tiles_x, int tiles_y, const float* bg, float* rgb,
-                     float* alpha, float* T, int32_t* stop, const int32_t* order,
-                     int32_t* work, cudaStream_t stream) {
+                     float* alpha, float* T, int32_t* stop, int32_t* tile_work,
+                     const RasterScratch& sc, int m_cap, cudaStream_t stream) {
     const int n_tiles = tiles_x * tiles_y;
-    if (work && cudaMemsetAsync(work, 0, sizeof(int32_t) * n_tiles, stream) != cudaSuccess)
-        return check_launch("rasterize_forward tile_work memset");
-    raster_forward_kernel<TILE><<<n_tiles * TileGeom<TILE>::kCtasPerTile,
-                                  TileGeom<TILE>::kThreads, 0, stream>>>(
-        reinterpret_cast<const float2*>(uv), conic, opacity, color, ids, offsets, W, H,
-        tiles_x, bg != nullptr, bg ? bg[0] : 0.f, bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, rgb,
-        alpha, T, stop, order, work);
+    tile_order_kernel<<<1, 1024, 0, stream>>>(offsets, nullptr, n_tiles, sc.order, sc.counters,
+                                              tile_work);
+    MG_TRY(check_launch("rasterize_forward order"));
+    const void* k = reinterpret_cast<const void*>(&raster_forward_kernel<TILE>);
+    const int grid = persistent_grid(k, kRasterWarps * 32);
+    if (grid <= 0) return check_launch("rasterize_forward occupancy");
+    raster_forward_kernel<TILE><<<grid, kRasterWarps * 32, 0, stream>>>(
+        splats, ids, offsets, W, H, tiles_x, n_tiles, bg != nullptr, bg ? bg[0] : 0.f,
+        bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, rgb, alpha, T, stop, sc.order, sc.counters,
+        sc.block_work, tile_work, sc.ckpt, m_cap, device_error_word());
     return check_launch("rasterize_forward");
 }
 
+template <int TILE, bool kSegmented>
+mg_status launch_bwd_mode(const float4* splats, const int32_t* ids, const int32_t* offsets,
+                          const float* rgb, const float* alpha, const float* final_T,
+                          const int32_t* stop, const float* grad_rgb, const float* grad_alpha,
+                          int W, int H, int tiles_x, int tiles_y, const float* bg,
+                          int want_absgrad, float* grad2d, const RasterScratch& sc,
+                          int m_cap, cudaStream_t stream) {
+    const int n_tiles = tiles_x * tiles_y;
+    backward_items_kernel<<<1, 1024, 0, stream>>>(offsets, kSegmented ? sc.block_work : nullptr,
+                                                  n_tiles, Blocks<TILE>::kCount,
+                                                  kSegmented ? kSeg : 0, sc.items, sc.counters);
+    MG_TRY(check_launch("rasterize_backward items"));
+    const void* k = reinterpret_cast<const void*>(&raster_backward_kernel<TILE, kSegmented>);
+    const int grid = persistent_grid(k, kRasterWarps * 32);
+    if (grid <= 0) return check_launch("rasterize_backward occupancy");
+    raster_backward_kernel<TILE, kSegmented><<<grid, kRasterWarps * 32, 0, stream>>>(
+        splats, ids, offsets, rgb, alpha, final_T, stop, grad_rgb, grad_alpha, W, H, tiles_x,
+        bg != nullptr, bg ? bg[0] : 0.f, bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, want_absgrad,
+        grad2d, sc.items, sc.counters, sc.ckpt, m_cap, device_error_word());
+    return check_launch("rasterize_backward");
+}
+
 template <int TILE>
-mg_status launch_bwd(const float* uv, const float* conic, const float* opacity,
-                     const float* color, const int32_t* ids, const int32_t* offsets,
+mg_status launch_bwd(bool segmented, const float4* splats, const int32_t* ids,
+                     const int32_t* offsets, const float* rgb, const float* alpha,
                      const float* final_T, const int32_t* stop, const float* grad_rgb,
                      const float* grad_alpha, int W, int H, int tiles_x, int tiles_y,
-                     const float* bg, const float* alpha, int want_absgrad, float* grad2d,
-                     const int32_t* order, cudaStream_t stream) {
-    const int n_tiles = tiles_x * tiles_y;
-    raster_backward_kernel<TILE><<<n_tiles * TileGeom<TILE>::kCtasPerTile,
-                                   TileGeom<TILE>::kThreads, 0, stream>>>(
-        reinterpret_cast<const float2*>(uv), conic, opacity, color, ids, offsets, final_T,
-        stop, grad_rgb, grad_alpha, W, H, tiles_x, bg != nullptr, bg ? bg[0] : 0.f,
-        bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, alpha, want_absgrad, grad2d, order);
-    return check_launch("rasterize_backward");
+                     const float* bg, int want_absgrad, float* grad2d, const RasterScratch& sc,
+                     int m_cap, cudaStream_t stream) {
+    if (segmented)
+        return launch_bwd_mode<TILE, true>(splats, ids, offsets, rgb, alpha, final_T, stop,
+                                           grad_rgb, grad_alpha, W, H, tiles_x, tiles_y, bg,
+                                           want_absgrad, grad2d, sc, m_cap, stream);
+    return launch_bwd_mode<TILE, false>(splats, ids, offsets, rgb, alpha, final_T, stop,
+                                        grad_rgb, grad_alpha, W, H, tiles_x, tiles_y, bg,
+                                        want_absgrad, grad2d, sc, m_cap, stream);
 }
 
 mg_status check_tile(int tile) {
@@ -493,53 +736,93 @@ mg_status check_tile(int tile) {
 
 using namespace mg;
 
-extern "C" mg_status mg_rasterize_forward(const float* uv, const float* conic,
-                                          const float* opacity, const float* color,
-                                          const int32_t* gauss_ids,
-                                          const int32_t* tile_offsets, int32_t width,
-                                          int32_t height, int32_t tile, int32_t tiles_x,
-                                          const float* background, float* out_rgb,
-                                          float* out_alpha, float* out_T,
-                                          int32_t* out_stop, const int32_t* tile_order,
-                                          int32_t* tile_work, mg_stream_t stream) {
+extern "C" size_t mg_raster_scratch_bytes(int32_t width, int32_t height, int32_t tile,
+                                          int64_t m) {
+    if (width <= 0 || height <= 0 || tile <= 0 || m < 0) return 0;
+    return carve_raster(nullptr, width, height, tile, m).bytes;
+}
+
+extern "C" mg_status mg_pack_splats(const float* uv, const float* conic, const float* opacity,
+                                    const float* color, int64_t n, void* splats,
+                                    mg_stream_t stream) {
+    MG_REQUIRE(n >= 0, "pack_splats: negative count");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(uv && conic && opacity && color && splats, "pack_splats: null pointer");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(splats) & 15u) == 0u,
+               "pack_splats: splats must be 16-byte aligned");
+    pack_splats_kernel<<<ceil_div(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float2*>(uv), conic, opacity, color, n,
+        static_cast<float4*>(splats));
+    return check_launch("pack_splats");
+}
+
+extern "C" mg_status mg_rasterize_forward(const void* splats, const int32_t* gauss_ids,
+                                          const int32_t* tile_offsets, int64_t m,
+                                          int32_t width, int32_t height, int32_t tile,
+                                          int32_t tiles_x, const float* background,
+                                          float* out_rgb, float* out_alpha, float* out_T,
+                                          int32_t* out_stop, int32_t* tile_work,
+                                          void* scratch, size_t scratch_bytes,
+                                          mg_stream_t stream) {
     MG_TRY(check_tile(tile));
     MG_REQUIRE(width > 0 && height > 0, "rasterize_forward: empty image");
     const int tiles_y = (height + tile - 1) / tile;
     MG_REQUIRE(tiles_x == (width + tile - 1) / tile, "rasterize_forward: tiles_x mismatch");
-    MG_REQUIRE(tile_offsets && out_rgb && out_alpha && out_T && out_stop,
+    MG_REQUIRE(tile_offsets && out_rgb && out_alpha && out_T && out_stop && scratch,
                "rasterize_forward: null pointer");
+    MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 31), "rasterize_forward: pair count out of range");
+    MG_REQUIRE(m == 0 || (splats && gauss_ids), "rasterize_forward: null splats or ids");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(splats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(scratch) & 15u) == 0u,
+               "rasterize_forward: splats and scratch must be 16-byte aligned");
+    const RasterScratch sc = carve_raster(scratch, width, height, tile, m);
+    MG_REQUIRE(scratch_bytes >= sc.bytes,
+               "rasterize_forward: scratch too small (mg_raster_scratch_bytes)");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const float4* sp = static_cast<const float4*>(splats);
     switch (tile) {
-        case 8: return launch_fwd<8>(uv, conic, opacity, color, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_order, tile_work, s);
-        case 12: return launch_fwd<12>(uv, conic, opacity, color, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_order, tile_work, s);
-        case 16: return launch_fwd<16>(uv, conic, opacity, color, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_order, tile_work, s);
-        default: return launch_fwd<32>(uv, conic, opacity, color, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_order, tile_work, s);
+        case 8: return launch_fwd<8>(sp, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_work, sc, (int)m, s);
+        case 12: return launch_fwd<12>(sp, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_work, sc, (int)m, s);
+        case 16: return launch_fwd<16>(sp, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_work, sc, (int)m, s);
+        default: return launch_fwd<32>(sp, gauss_ids, tile_offsets, width, height, tiles_x, tiles_y, background, out_rgb, out_alpha, out_T, out_stop, tile_work, sc, (int)m, s);
     }
 }
 
 extern "C" mg_status mg_rasterize_backward(
-    const float* uv, const float* conic, const float* opacity, const float* color,
-    const int32_t* gauss_ids, const int32_t* tile_offsets, const float* final_T,
-    const int32_t* stop, const float* grad_rgb, const float* grad_alpha, int32_t width,
-    int32_t height, int32_t tile, int32_t tiles_x, const float* background,
-    const float* alpha, int32_t want_absgrad, int64_t n, float* grad2d,
-    const int32_t* tile_order, mg_stream_t stream) {
+    const void* splats, const int32_t* gauss_ids, const int32_t* tile_offsets, int64_t m,
+    const float* out_rgb, const float* out_alpha, const float* final_T, const int32_t* stop,
+    const float* grad_rgb, const float* grad_alpha, int32_t width, int32_t height,
+    int32_t tile, int32_t tiles_x, const float* background, int32_t want_absgrad, int64_t n,
+    float* grad2d, int32_t segmented, void* scratch, size_t scratch_bytes,
+    mg_stream_t stream) {
     MG_TRY(check_tile(tile));
     MG_REQUIRE(width > 0 && height > 0, "rasterize_backward: empty image");
     const int tiles_y = (height + tile - 1) / tile;
     MG_REQUIRE(tiles_x == (width + tile - 1) / tile, "rasterize_backward: tiles_x mismatch");
-    MG_REQUIRE(final_T && stop && grad_rgb && tile_offsets, "rasterize_backward: null pointer");
-    MG_REQUIRE(background == nullptr || alpha != nullptr,
+    MG_REQUIRE(final_T && stop && grad_rgb && tile_offsets && scratch,
+               "rasterize_backward: null pointer");
+    MG_REQUIRE(background == nullptr || out_alpha != nullptr,
                "rasterize_backward: the background blend needs the forward alpha");
-    MG_REQUIRE((reinterpret_cast<uintptr_t>(grad2d) & 15u) == 0u,
-               "rasterize_backward: grad2d must be 16-byte aligned");
-    if (n == 0) return MG_OK;
+    MG_REQUIRE(!segmented || (out_rgb && out_alpha),
+               "rasterize_backward: segments need the forward's rgb and alpha");
+    MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 31), "rasterize_backward: pair count out of range");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(grad2d) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(splats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(scratch) & 15u) == 0u,
+               "rasterize_backward: grad2d, splats and scratch must be 16-byte aligned");
+    if (n == 0 || m == 0) return MG_OK;
+    MG_REQUIRE(splats && gauss_ids && grad2d, "rasterize_backward: null splats, ids or grad2d");
+    const RasterScratch sc = carve_raster(scratch, width, height, tile, m);
+    MG_REQUIRE(scratch_bytes >= sc.bytes,
+               "rasterize_backward: scratch too small (mg_raster_scratch_bytes)");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const float4* sp = static_cast<const float4*>(splats);
+    const bool seg = segmented != 0;
     switch (tile) {
-        case 8: return launch_bwd<8>(uv, conic, opacity, color, gauss_ids, tile_offsets, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, alpha, want_absgrad, grad2d, tile_order, s);
-        case 12: return launch_bwd<12>(uv, conic, opacity, color, gauss_ids, tile_offsets, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, alpha, want_absgrad, grad2d, tile_order, s);
-        case 16: return launch_bwd<16>(uv, conic, opacity, color, gauss_ids, tile_offsets, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, alpha, want_absgrad, grad2d, tile_order, s);
-        default: return launch_bwd<32>(uv, conic, opacity, color, gauss_ids, tile_offsets, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, alpha, want_absgrad, grad2d, tile_order, s);
+        case 8: return launch_bwd<8>(seg, sp, gauss_ids, tile_offsets, out_rgb, out_alpha, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, want_absgrad, grad2d, sc, (int)m, s);
+        case 12: return launch_bwd<12>(seg, sp, gauss_ids, tile_offsets, out_rgb, out_alpha, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, want_absgrad, grad2d, sc, (int)m, s);
+        case 16: return launch_bwd<16>(seg, sp, gauss_ids, tile_offsets, out_rgb, out_alpha, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, want_absgrad, grad2d, sc, (int)m, s);
+        default: return launch_bwd<32>(seg, sp, gauss_ids, tile_offsets, out_rgb, out_alpha, final_T, stop, grad_rgb, grad_alpha, width, height, tiles_x, tiles_y, background, want_absgrad, grad2d, sc, (int)m, s);
     }
 }
 
@@ -548,7 +831,7 @@ extern "C" mg_status mg_tile_order(const int32_t* tile_offsets, const int32_t* w
     MG_REQUIRE(n_tiles > 0 && order != nullptr, "tile_order: bad arguments");
     MG_REQUIRE(work != nullptr || tile_offsets != nullptr, "tile_order: no work measure");
     tile_order_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        tile_offsets, work, n_tiles, order);
+        tile_offsets, work, n_tiles, order, nullptr, nullptr);
     return check_launch("tile_order");
 }
 

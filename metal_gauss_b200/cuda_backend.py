@@ -87,11 +87,15 @@ class _RasterizeCUDA(torch.autograd.Function):
     def forward(ctx, uv, conic, opacity, color, gauss_ids, tile_offsets, W, H, tile, tiles_x,
                 absgrad_out=None, background=None):
         args = [t.contiguous() for t in (uv, conic, opacity, color)]
-        work = torch.empty(tile_offsets.numel() - 1, dtype=torch.int32, device=uv.device)
+        state = []
         rgb, alpha, T, ncontrib = ext.rasterize_forward(*args, gauss_ids, tile_offsets, W, H,
                                                         tile, tiles_x, background=background,
-                                                        tile_work_out=work)
-        ctx.save_for_backward(*args, gauss_ids, tile_offsets, T, ncontrib, alpha, work)
+                                                        state_out=state)
+        # the packed records and checkpoints let the backward split long
+        # walks into segments; rgb and alpha are saved so in-place edits of
+        # the outputs are caught by autograd's version check
+        ctx.save_for_backward(*args, gauss_ids, tile_offsets, T, ncontrib, alpha, rgb)
+        ctx.state = state[0]
         ctx.dims = (W, H, tile, tiles_x)
         ctx.absgrad_out = absgrad_out
         ctx.background = background
@@ -100,7 +104,7 @@ class _RasterizeCUDA(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_rgb, grad_alpha):
         (uv, conic, opacity, color, gauss_ids, tile_offsets, T, ncontrib, alpha,
-         work) = ctx.saved_tensors
+         rgb) = ctx.saved_tensors
         W, H, tile, tiles_x = ctx.dims
         if grad_rgb is None:
             grad_rgb = torch.zeros(H, W, 3, device=uv.device)
@@ -108,7 +112,8 @@ class _RasterizeCUDA(torch.autograd.Function):
         g = ext.rasterize_backward_packed(uv, conic, opacity, color, gauss_ids, tile_offsets, T,
                                           ncontrib, grad_rgb, grad_alpha, W, H, tile, tiles_x,
                                           want_abs, background=ctx.background, alpha=alpha,
-                                          tile_work=work)
+                                          state=ctx.state, rgb=rgb)
+        ctx.state = None
         if want_abs:
             ctx.absgrad_out[:g.shape[0]] += g[:, G2D_ABSUV]
         return (g[:, 0:2], g[:, 4:7], g[:, 2], g[:, 8:11]) + (None,) * 8

@@ -66,8 +66,9 @@ class _ImageBuffers:
         self.grad_rgb = torch.empty(H, W, 3, **f32)
         nbytes = _lib.load().mg_l1_ssim_scratch_bytes(H, W)
         self.loss_scratch = torch.empty(nbytes, dtype=torch.uint8, device=device)
-        self.order = None
         self.tile_work = None
+        self.splats = torch.empty(n, _lib.SPLAT_FLOATS, **f32)
+        self.raster = torch.empty(0, dtype=torch.uint8, device=device)
         self.ids = torch.empty(0, dtype=torch.int32, device=device)
         self.offsets = None
         self.emit = torch.empty(0, dtype=torch.uint8, device=device)
@@ -278,8 +279,11 @@ class Trainer:
             b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32, device=self.device)
         if b.offsets is None or b.offsets.numel() != n_tiles + 1:
             b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
-            b.order = torch.empty(n_tiles, dtype=torch.int32, device=self.device)
             b.tile_work = torch.empty(n_tiles, dtype=torch.int32, device=self.device)
+        rbytes = L.mg_raster_scratch_bytes(W, H, self.tile, m)
+        if b.raster.numel() < rbytes:
+            b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
+                                   device=self.device)
         ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
         if b.emit.numel() < ebytes:
             b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8, device=self.device)
@@ -290,15 +294,20 @@ class Trainer:
         self._end(ev)
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
-        ev = self._begin("raster_fwd")
-        _lib.check(L.mg_tile_order(ptr(b.offsets), None, n_tiles, ptr(b.order), s), "tile_order")
-        _lib.check(L.mg_rasterize_forward(
-            ptr(st.uv), ptr(st.conic), ptr(self.opac), ptr(st.color), ptr(b.ids), ptr(b.offsets),
-            W, H, self.tile, tiles_x, bgp, ptr(b.rgb), ptr(b.alpha), ptr(b.T), ptr(b.stop),
-            ptr(b.order), ptr(b.tile_work), s), "rasterize_forward")
+        ev = self._begin("pack")
+        _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(self.opac), ptr(st.color), n,
+                                    ptr(b.splats), s), "pack_splats")
         self._end(ev)
-        if self.stage_events is not None:
-            self.walked.append(b.tile_work.sum())
+        # tile walk lengths only when the instrumented pass asks for them
+        work = b.tile_work if self.stage_events is not None else None
+        ev = self._begin("raster_fwd")
+        _lib.check(L.mg_rasterize_forward(
+            ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, W, H, self.tile, tiles_x, bgp,
+            ptr(b.rgb), ptr(b.alpha), ptr(b.T), ptr(b.stop), ptr(work), ptr(b.raster),
+            b.raster.numel(), s), "rasterize_forward")
+        self._end(ev)
+        if work is not None:
+            self.walked.append(work.sum())
         ev = self._begin("loss")
         _lib.check(L.mg_l1_ssim_loss(
             ptr(b.rgb), ptr(target), ptr(self.window), H, W, self.w_l1, self.w_ssim, scale,
@@ -307,12 +316,10 @@ class Trainer:
         b.grad2d.zero_()
         self._end(ev)
         ev = self._begin("raster_bwd")
-        _lib.check(L.mg_tile_order(ptr(b.offsets), ptr(b.tile_work), n_tiles, ptr(b.order), s),
-                   "tile_order")
         _lib.check(L.mg_rasterize_backward(
-            ptr(st.uv), ptr(st.conic), ptr(self.opac), ptr(st.color), ptr(b.ids), ptr(b.offsets),
-            ptr(b.T), ptr(b.stop), ptr(b.grad_rgb), None, W, H, self.tile, tiles_x, bgp,
-            ptr(b.alpha), 0, n, ptr(b.grad2d), ptr(b.order), s), "rasterize_backward")
+            ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, ptr(b.rgb), ptr(b.alpha), ptr(b.T),
+            ptr(b.stop), ptr(b.grad_rgb), None, W, H, self.tile, tiles_x, bgp, 0, n,
+            ptr(b.grad2d), 1, ptr(b.raster), b.raster.numel(), s), "rasterize_backward")
         self._end(ev)
         ev = self._begin("preprocess_bwd")
         _lib.check(L.mg_preprocess_backward_accumulate(
@@ -439,9 +446,10 @@ class Trainer:
                                                        * (v.height // self.tile + 1))) / 8)
             total += 4 * M                          # ranges
             Wk = st.walked if st.walked else M
-            total += 40 * Wk + 24 * P               # raster fwd (walked entries)
+            total += (36 + 48) * n                  # pack splat records
+            total += 52 * Wk + 24 * P               # raster fwd (walked id + record)
             total += 40 * P + 36 * P                # fused loss (2 kernels)
-            total += 40 * Wk + 24 * P + 48 * n      # raster bwd (+ record)
+            total += 52 * Wk + 36 * P + 48 * n      # raster bwd (+ gradient record)
             total += (44 + 48 + 192) * n + 236 * 2 * n  # preprocess bwd (+ RMW grads)
         total += 28 * FLOATS_PER_GAUSSIAN * nv + 8 * n   # selective Adam
         return total

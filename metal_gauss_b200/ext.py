@@ -228,13 +228,50 @@ def tile_order(tile_offsets: torch.Tensor, work: torch.Tensor | None = None) -> 
     return order
 
 
+class RasterState:
+    """What one view's forward leaves for its backward: the packed splat
+    records and the rasteriser scratch (walk lengths, checkpoints)."""
+
+    def __init__(self, splats: torch.Tensor, scratch: torch.Tensor, m: int, W: int, H: int,
+                 tile: int):
+        self.splats, self.scratch, self.m = splats, scratch, m
+        self.W, self.H, self.tile = W, H, tile
+
+
+def pack_splats(uv, conic, opacity, color) -> torch.Tensor:
+    """(N, 12) packed records the rasterisers read (mg_pack_splats)."""
+    for t, w in ((uv, "uv"), (conic, "conic"), (opacity, "opacity"), (color, "color")):
+        _check(t, w)
+    n = uv.shape[0]
+    splats = _empty((n, _lib.SPLAT_FLOATS), uv)
+    _lib.call("mg_pack_splats", ptr(uv), ptr(conic), ptr(opacity), ptr(color), n, ptr(splats),
+              _lib.stream())
+    return splats
+
+
+def raster_scratch(W: int, H: int, tile: int, m: int, device) -> torch.Tensor:
+    nbytes = _lib.load().mg_raster_scratch_bytes(W, H, tile, m)
+    if nbytes == 0:
+        raise RuntimeError(f"rasteriser scratch: bad size arguments W={W} H={H} tile={tile} "
+                           f"m={m}")
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def _bg_arg(background):
+    if background is None:
+        return None, None
+    bg = (_lib.C.c_float * 3)(*[float(x) for x in background])
+    return bg, _lib.C.cast(bg, _lib.C.c_void_p)
+
+
 def rasterize_forward(uv, conic, opacity, color, gauss_ids, tile_offsets, W, H, tile, tiles_x,
-                      background=None, tile_work_out=None):
+                      background=None, tile_work_out=None, state_out: list | None = None):
     """-> [rgb (H,W,3), alpha (H,W), T (H,W), n_contrib (H,W) int32 stop index]
     (rasterize.mm:79-113). `background` (3 floats) folds the reference's
-    blend (metal_backend.py:539-541) into the kernel. Tiles run heaviest
-    first; `tile_work_out` (n_tiles int32), when given, receives each tile's
-    walk length for ordering the backward."""
+    blend (metal_backend.py:539-541) into the kernel. `tile_work_out`
+    (n_tiles int32), when given, receives each tile's walk length. When
+    `state_out` is a list, the view's RasterState is appended to it for
+    rasterize_backward_packed."""
     for t, w in ((uv, "uv"), (conic, "conic"), (opacity, "opacity"), (color, "color")):
         _check(t, w)
     _check(gauss_ids, "gauss_ids", torch.int32)
@@ -243,34 +280,48 @@ def rasterize_forward(uv, conic, opacity, color, gauss_ids, tile_offsets, W, H, 
     alpha = _empty((H, W), uv)
     T = _empty((H, W), uv)
     stop = _empty((H, W), uv, torch.int32)
-    bg = None if background is None else (_lib.C.c_float * 3)(*[float(x) for x in background])
-    order = tile_order(tile_offsets)
-    _lib.call("mg_rasterize_forward", ptr(uv), ptr(conic), ptr(opacity), ptr(color),
-              ptr(gauss_ids), ptr(tile_offsets), W, H, tile, tiles_x,
-              None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p), ptr(rgb), ptr(alpha),
-              ptr(T), ptr(stop), ptr(order), ptr(tile_work_out), _lib.stream())
+    m = gauss_ids.numel()  # the lists index into gauss_ids: no host read needed
+    splats = pack_splats(uv, conic, opacity, color)
+    scratch = raster_scratch(W, H, tile, m, uv.device)
+    _bg, bgp = _bg_arg(background)
+    _lib.call("mg_rasterize_forward", ptr(splats), ptr(gauss_ids), ptr(tile_offsets), m, W, H,
+              tile, tiles_x, bgp, ptr(rgb), ptr(alpha), ptr(T), ptr(stop), ptr(tile_work_out),
+              ptr(scratch), scratch.numel(), _lib.stream())
+    if state_out is not None:
+        state_out.append(RasterState(splats, scratch, m, W, H, tile))
     return [rgb, alpha, T, stop]
 
 
 def rasterize_backward_packed(uv, conic, opacity, color, gauss_ids, tile_offsets, final_T,
                               n_contrib, grad_rgb, grad_alpha, W, H, tile, tiles_x,
                               want_absgrad, background=None, alpha=None, grad2d=None,
-                              tile_work=None):
+                              state: RasterState | None = None, rgb=None):
     """Backward into the packed (N, 12) record; accumulates into `grad2d` when
-    given, else into a fresh zeroed one. Tiles run heaviest first, by the
-    forward's `tile_work` when given, else by list length. Returns grad2d."""
+    given, else into a fresh zeroed one. With the forward's `state` (and its
+    `rgb`, `alpha`), long walks are split into segments that start from the
+    forward's checkpoints; without, every warp block walks its whole list.
+    Returns grad2d."""
     n = uv.shape[0]
     if grad2d is None:
         grad2d = torch.zeros((n, G2D_STRIDE), dtype=F32, device=uv.device)
     grad_rgb = grad_rgb.contiguous()
     grad_alpha = None if grad_alpha is None else grad_alpha.contiguous()
-    bg = None if background is None else (_lib.C.c_float * 3)(*[float(x) for x in background])
-    order = tile_order(tile_offsets, tile_work)
-    _lib.call("mg_rasterize_backward", ptr(uv), ptr(conic), ptr(opacity), ptr(color),
-              ptr(gauss_ids), ptr(tile_offsets), ptr(final_T), ptr(n_contrib), ptr(grad_rgb),
-              ptr(grad_alpha), W, H, tile, tiles_x,
-              None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p), ptr(alpha),
-              int(bool(want_absgrad)), n, ptr(grad2d), ptr(order), _lib.stream())
+    _bg, bgp = _bg_arg(background)
+    segmented = state is not None
+    if segmented:
+        if rgb is None or alpha is None:
+            raise RuntimeError("rasterize_backward: the forward state needs its rgb and alpha")
+        if (state.W, state.H, state.tile) != (W, H, tile):
+            raise RuntimeError("rasterize_backward: forward state is for another view")
+        splats, scratch, m = state.splats, state.scratch, state.m
+    else:
+        m = gauss_ids.numel()
+        splats = pack_splats(uv, conic, opacity, color)
+        scratch = raster_scratch(W, H, tile, m, uv.device)
+    _lib.call("mg_rasterize_backward", ptr(splats), ptr(gauss_ids), ptr(tile_offsets), m,
+              ptr(rgb) if segmented else None, ptr(alpha), ptr(final_T), ptr(n_contrib),
+              ptr(grad_rgb), ptr(grad_alpha), W, H, tile, tiles_x, bgp, int(bool(want_absgrad)),
+              n, ptr(grad2d), int(segmented), ptr(scratch), scratch.numel(), _lib.stream())
     return grad2d
 
 

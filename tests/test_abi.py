@@ -43,3 +43,8 @@ def test_scratch_queries_need_no_device():
     assert lib.mg_bin_prepare_scratch_bytes(1000) > 4 * 1000
     assert lib.mg_bin_emit_scratch_bytes(1000, 5000, 2500) > 4 * 5000
     assert lib.mg_l1_ssim_scratch_bytes(64, 64) >= 9 * 64 * 64 * 4
+    # counters + tile order + block walks + items + checkpoints (5 floats per
+    # pixel slot per MG_RASTER_SEGMENT entries)
+    rb = lib.mg_raster_scratch_bytes(800, 800, 16, 10_000_000)
+    assert rb >= 4 * 5 * 256 * (10_000_000 // _lib.RASTER_SEGMENT)
+    assert lib.mg_raster_scratch_bytes(0, 800, 16, 10) == 0

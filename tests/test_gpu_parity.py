@@ -228,17 +228,14 @@ def _oracle_scene(n, W, H, seed, deg=3, tile=16):
     return pre, opac, ids, off
 
 
-@pytest.mark.parametrize("tile", [8, 12, 16, 32])
-def test_rasterize_forward_and_backward_match_oracle(cuda, tile):
-    W, H = 200, 130
-    pre, opac, ids, off = _oracle_scene(6000, W, H, 2, tile=tile)
-    bg = np.array([0.2, 0.5, 1.0], np.float32)
+def _raster_vs_oracle(pre, opac, ids, off, W, H, tile, bg, segmented, grad_tol):
     r_rgb, r_alpha, r_T, r_stop = oracle.rasterize_forward(pre["uv"], pre["conic"], opac,
                                                            pre["color"], ids, off, W, H, tile, bg)
     tx = math.ceil(W / tile)
     args = [T(pre["uv"]), T(pre["conic"]), T(opac), T(pre["color"])]
+    state = [] if segmented else None
     rgb, alpha, Tt, stop = ext.rasterize_forward(*args, T(ids), T(off), W, H, tile, tx,
-                                                 background=bg)
+                                                 background=bg, state_out=state)
     assert np.abs(N(rgb) - r_rgb).max() < IMG_TOL
     assert np.abs(N(alpha) - r_alpha).max() < IMG_TOL
     assert (N(stop) == r_stop).mean() > 0.999
@@ -248,10 +245,48 @@ def test_rasterize_forward_and_backward_match_oracle(cuda, tile):
     ref = oracle.rasterize_backward(pre["uv"], pre["conic"], opac, pre["color"], ids, off, r_T,
                                     r_stop, grgb, ga, W, H, tile, bg, r_alpha, True)
     got = N(ext.rasterize_backward_packed(*args, T(ids), T(off), Tt, stop, T(grgb), T(ga), W, H,
-                                          tile, tx, True, background=bg, alpha=alpha))
+                                          tile, tx, True, background=bg, alpha=alpha,
+                                          state=state[0] if segmented else None, rgb=rgb))
     for sl, name in ((slice(0, 2), "uv"), (slice(2, 3), "opacity"), (slice(3, 4), "absgrad"),
                      (slice(4, 7), "conic"), (slice(8, 11), "color")):
-        assert rel_l2(got[:, sl], ref[:, sl]) < 1e-4, name
+        assert rel_l2(got[:, sl], ref[:, sl]) < grad_tol, name
+    assert ext.device_error() == 0
+    return r_stop - off[:-1].min()
+
+
+@pytest.mark.parametrize("segmented", [False, True])
+@pytest.mark.parametrize("tile", [8, 12, 16, 32])
+def test_rasterize_forward_and_backward_match_oracle(cuda, tile, segmented):
+    W, H = 200, 130
+    pre, opac, ids, off = _oracle_scene(6000, W, H, 2, tile=tile)
+    bg = np.array([0.2, 0.5, 1.0], np.float32)
+    _raster_vs_oracle(pre, opac, ids, off, W, H, tile, bg, segmented, 1e-4)
+
+
+@pytest.mark.parametrize("tile", [12, 16])
+def test_segmented_backward_on_long_lists(cuda, tile):
+    """Faint, wide splats: lists of 6-7k entries that few pixels finish
+    early, so the backward runs over twenty segments per warp block, each
+    started from a forward checkpoint, next to blocks whose pixels stop
+    inside a segment."""
+    W, H = 72, 56
+    g = np.random.default_rng(11)
+    n = 12000
+    means = np.stack([g.uniform(-1.2, 1.2, n), g.uniform(-0.9, 0.9, n),
+                      g.uniform(3.0, 6.0, n)], 1).astype(np.float32)
+    quats = g.standard_normal((n, 4)).astype(np.float32)
+    scales = (g.random((n, 3)) * 0.25 + 0.05).astype(np.float32)
+    opac = (g.random(n) * 0.03 + 0.006).astype(np.float32)
+    sh = (g.standard_normal((n, 16, 3)) * 0.3).astype(np.float32)
+    K = np.array([[60, 0, W / 2], [0, 60, H / 2], [0, 0, 1]], np.float32)
+    cam = oracle.camera(np.eye(4, dtype=np.float32), K, W, H)
+    pre = oracle.preprocess_forward(means, quats, scales, sh, None, opac, cam, 3)
+    ids, off, _ = oracle.build_tile_lists(pre["uv"], pre["rxy"], pre["conic"], opac, pre["valid"],
+                                          pre["depth"], W, H, tile)
+    lens = np.diff(off)
+    assert lens.max() > 8 * 256, "scene must produce lists spanning many segments"
+    for segmented in (False, True):
+        _raster_vs_oracle(pre, opac, ids, off, W, H, tile, None, segmented, 2e-4)
 
 
 # ------------------------------------------------- whole render vs torch_ref
