@@ -25,7 +25,8 @@
 // Forward, front to back: alpha = min(0.999, op exp(power)), skip power > 0 or
 // alpha < 1/255, stop a pixel once T < 1e-4 and record the stop INDEX. Live
 // entries are taken two at a time: both exponentials are evaluated before
-// either blend, so their latencies overlap, and the blends stay in list order.
+// either blend, so their latencies overlap, and the blends stay in list order
+// and branch per pixel, so a warp skips the blend when no pixel takes it.
 // Every MG_RASTER_SEGMENT entries of a tile's list the forward stores each
 // pixel's running state (T, accumulated rgb, accumulated alpha): a checkpoint.
 //
@@ -34,9 +35,12 @@
 // longest first. A segment starts from the checkpoint at its upper end (T
 // there; the colour behind it is the final colour minus the checkpointed one),
 // so a long list is split over many warps instead of forming the kernel's
-// tail. Per live entry the warp reduces its 32 pixels' contributions with a
-// 16-slot butterfly reduce-scatter and three lanes add the 48-byte gradient
-// record to global memory with 16-byte vector atomics.
+// tail. The colour and alpha behind an entry enter its gradient only through
+// their dot product with the pixel's output gradient, so a pixel carries one
+// running sum for them. Per live entry the warp reduces its 32 pixels'
+// contributions with a 10-slot butterfly reduce-scatter (12 shuffles) and
+// three lanes add the 48-byte gradient record to global memory with 16-byte
+// vector atomics.
 #include <mutex>
 #include <unordered_map>
 
@@ -137,12 +141,26 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// A warp's double-buffered chunk of records: q[buffer][word][entry], so a
-// lane's three copies land in consecutive 16-byte words of three rows and an
-// entry is read back as three broadcast loads.
+// Chunks in flight per warp: the records of chunk i + stages - 1 are copied
+// while chunk i is processed. The forward finds its records in L2 (packed
+// just before), so two stages suffice there; the backward starts a new walk
+// every segment and gains from a third.
+#ifndef MG_FWD_STAGES
+#define MG_FWD_STAGES 2
+#endif
+#ifndef MG_BWD_STAGES
+#define MG_BWD_STAGES 3
+#endif
+constexpr int kFwdStages = MG_FWD_STAGES;
+constexpr int kBwdStages = MG_BWD_STAGES;
+
+// A warp's ring of chunk buffers: q[buffer][word][entry], so a lane's three
+// copies land in consecutive 16-byte words of three rows and an entry is read
+// back as three broadcast loads.
+template <int kStages>
 struct WarpStage {
-    float4 q[2][3][32];
-    int32_t id[2][32];
+    float4 q[kStages][3][32];
+    int32_t id[kStages][32];
     __device__ __forceinline__ void fetch(int buf, int lane, const float4* splats, int gid,
                                           bool keep_id) {
         const float4* src = splats + 3 * (int64_t)gid;
@@ -199,9 +217,10 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                       int32_t* __restrict__ block_work, int32_t* __restrict__ tile_work,
                       float* __restrict__ ckpt, int m_cap, int32_t* __restrict__ err) {
     using G = Blocks<TILE>;
-    __shared__ WarpStage s_stage[kRasterWarps];
+    constexpr int kStages = kFwdStages;
+    __shared__ WarpStage<kStages> s_stage[kRasterWarps];
     const int lane = threadIdx.x & 31;
-    WarpStage& st = s_stage[threadIdx.x >> 5];
+    WarpStage<kStages>& st = s_stage[threadIdx.x >> 5];
     const int n_items = n_tiles * G::kCount;
 
     for (int item = pull_item(counter, lane); item < n_items; item = pull_item(counter, lane)) {
@@ -226,17 +245,32 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
             float rx0, rx1, ry0, ry1;
             warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
             float* ck = ckpt + wb * 32 + lane;
-            if (start + lane < end) st.fetch(0, lane, splats, ids[start + lane], false);
-            cp_async_commit();
-            int gid_next = start + 32 + lane < end ? ids[start + 32 + lane] : 0;
-            int buf = 0;
-            for (int base = start;; base += 32) {
-                const int nb = base + 32;
-                // buffer buf^1 was released by the previous chunk's last vote
-                if (nb + lane < end) st.fetch(buf ^ 1, lane, splats, gid_next, false);
+            const int n_chunks = (end - start + 31) >> 5;
+            // ids of the first kStages chunks (all loads in flight together),
+            // then the copies of the first kStages - 1
+            int gid[kStages];
+#pragma unroll
+            for (int c = 0; c < kStages; ++c) {
+                const int j = start + 32 * c + lane;
+                gid[c] = j < end ? ids[j] : -1;
+            }
+#pragma unroll
+            for (int c = 0; c < kStages - 1; ++c) {
+                if (gid[c] >= 0) st.fetch(c, lane, splats, gid[c], false);
                 cp_async_commit();
-                const int gid_after = nb + 32 + lane < end ? ids[nb + 32 + lane] : 0;
-                if (base != start && ((base - start) & (kSeg - 1)) == 0) {
+            }
+            int gid_next = gid[kStages - 1];
+            int buf = 0, ibuf = kStages - 1;  // buffers of chunk i and chunk i + kStages - 1
+            for (int ci = 0;; ++ci) {
+                const int base = start + 32 * ci;
+                // ibuf held chunk ci - 1, released by that chunk's last vote
+                if (gid_next >= 0) st.fetch(ibuf, lane, splats, gid_next, false);
+                cp_async_commit();
+                {
+                    const int j = base + 32 * kStages + lane;
+                    gid_next = j < end ? ids[j] : -1;
+                }
+                if (ci != 0 && ((base - start) & (kSeg - 1)) == 0) {
                     float* c = ck + ckpt_slot(start, tile_id, (base - start) / kSeg) * 5 *
                                         G::kPixPad;
                     c[0] = T;
@@ -245,7 +279,7 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                     c[3 * G::kPixPad] = ab;
                     c[4 * G::kPixPad] = aa;
                 }
-                cp_async_wait<1>();
+                cp_async_wait<kStages - 1>();
                 __syncwarp();
                 const bool lv = base + lane < end &&
                                 rect_live(st.q[buf][0][lane], st.q[buf][1][lane].x,
@@ -284,9 +318,9 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                     if (__all_sync(0xffffffffu, done)) break;
                 }
                 const bool all_done = __all_sync(0xffffffffu, done);  // releases buffer buf
-                if (all_done || nb >= end) break;
-                buf ^= 1;
-                gid_next = gid_after;
+                if (all_done || ci + 1 >= n_chunks) break;
+                buf = buf + 1 == kStages ? 0 : buf + 1;
+                ibuf = ibuf + 1 == kStages ? 0 : ibuf + 1;
             }
             cp_async_wait<0>();
             __syncwarp();
@@ -314,37 +348,50 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
 
 // ---------------------------------------------------------------- backward
 
-// 16-slot butterfly reduce-scatter across the warp: on return, lanes 2s and
-// 2s+1 hold the warp sum of slot s.
-__device__ __forceinline__ float reduce_scatter16(float (&v)[16], int lane) {
+// 10-slot butterfly reduce-scatter across the warp in 12 shuffles (5 + 3 + 2
+// + 1 exchanges, halving the slots a lane holds each round, padded where the
+// count is odd, then one plain add). On return lanes 2p and 2p+1 hold the
+// warp sum of slot s for (p, s) = (0,0) (1,1) (2,2) (4,3) (5,4) (8,5) (9,6)
+// (10,7) (12,8) (13,9); the other pairs hold padding zeros.
+__device__ __forceinline__ float reduce_scatter10(const float (&v)[10], int lane) {
+    const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4, h2 = lane & 2;
+    float u[5];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const bool hi = lane & 16;
-        const float send = hi ? v[k] : v[k + 8];
-        const float keep = hi ? v[k + 8] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    for (int k = 0; k < 5; ++k) {
+        const float send = h16 ? v[k] : v[k + 5];
+        const float keep = h16 ? v[k + 5] : v[k];
+        u[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const bool hi = lane & 8;
-        const float send = hi ? v[k] : v[k + 4];
-        const float keep = hi ? v[k + 4] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
+    float w[3];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        const bool hi = lane & 4;
-        const float send = hi ? v[k] : v[k + 2];
-        const float keep = hi ? v[k + 2] : v[k];
-        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        const float send = h8 ? u[k] : u[k + 3];
+        const float keep = h8 ? u[k + 3] : u[k];
+        w[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
     }
+    w[2] = (h8 ? 0.0f : u[2]) + __shfl_xor_sync(0xffffffffu, h8 ? u[2] : 0.0f, 8);
+    float x0, x1;
     {
-        const bool hi = lane & 2;
-        const float send = hi ? v[0] : v[1];
-        const float keep = hi ? v[1] : v[0];
-        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+        const float send = h4 ? w[0] : w[2];
+        const float keep = h4 ? w[2] : w[0];
+        x0 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
     }
-    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+    x1 = (h4 ? 0.0f : w[1]) + __shfl_xor_sync(0xffffffffu, h4 ? w[1] : 0.0f, 4);
+    const float send = h2 ? x0 : x1;
+    const float keep = h2 ? x1 : x0;
+    const float y = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    return y + __shfl_xor_sync(0xffffffffu, y, 1);
+}
+
+// Source lanes from which lanes 0, 1, 2 gather the float4 words of the
+// gradient record after reduce_scatter10 (slot s -> lane of its pair; lane 6
+// holds a padding zero).
+__device__ __forceinline__ void record_gather_lanes(int lane, int& s0, int& s1, int& s2,
+                                                    int& s3) {
+    s0 = lane == 0 ? 0 : lane == 1 ? 10 : lane == 2 ? 20 : lane;
+    s1 = lane == 0 ? 2 : lane == 1 ? 16 : lane == 2 ? 24 : lane;
+    s2 = lane == 0 ? 4 : lane == 1 ? 18 : lane == 2 ? 26 : lane;
+    s3 = lane == 0 ? 8 : lane <= 2 ? 6 : lane;
 }
 
 // kSegmented: items are (block, segment) pairs and segments start from the
@@ -363,10 +410,13 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                        int32_t* __restrict__ counters, const float* __restrict__ ckpt,
                        int m_cap, int32_t* __restrict__ err) {
     using G = Blocks<TILE>;
-    __shared__ WarpStage s_stage[kRasterWarps];
+    constexpr int kStages = kBwdStages;
+    __shared__ WarpStage<kStages> s_stage[kRasterWarps];
     const int lane = threadIdx.x & 31;
-    WarpStage& st = s_stage[threadIdx.x >> 5];
+    WarpStage<kStages>& st = s_stage[threadIdx.x >> 5];
     const int n_items = counters[2];
+    int g0, g1, g2, g3;
+    record_gather_lanes(lane, g0, g1, g2, g3);
 
     for (int item = pull_item(counters + 1, lane); item < n_items;
          item = pull_item(counters + 1, lane)) {
@@ -386,7 +436,9 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
         const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
         const int64_t o = inimg ? (int64_t)py * W + px : 0;
 
-        float T = 1.0f, sr = 0.f, sg = 0.f, sb = 0.f, sa = 0.f;  // suffix colour / alpha
+        // S = <d L / d (rgb, alpha), colour and alpha blended behind the
+        // current entry>: one running dot product instead of four suffix sums
+        float T = 1.0f, S = 0.0f;
         float gr = 0.f, gg = 0.f, gb = 0.f, ga = 0.f;
         int my_stop = start;
         if (inimg) {
@@ -403,10 +455,8 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                 float cr = out_rgb[3 * o], cg = out_rgb[3 * o + 1], cbl = out_rgb[3 * o + 2];
                 if (has_bg) { cr -= kbg * bg_r; cg -= kbg * bg_g; cbl -= kbg * bg_b; }
                 T = c[0];
-                sr = cr - c[G::kPixPad];
-                sg = cg - c[2 * G::kPixPad];
-                sb = cbl - c[3 * G::kPixPad];
-                sa = a_fin - c[4 * G::kPixPad];
+                S = gr * (cr - c[G::kPixPad]) + gg * (cg - c[2 * G::kPixPad]) +
+                    gb * (cbl - c[3 * G::kPixPad]) + ga * (a_fin - c[4 * G::kPixPad]);
             } else {
                 T = final_T[o];
             }
@@ -417,20 +467,31 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
         float rx0, rx1, ry0, ry1;
         warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
 
-        // chunks are aligned to the list start; seg_lo is a chunk boundary
-        int cbase = start + ((warp_hi - 1 - start) >> 5) * 32;
-        if (cbase + lane < warp_hi) st.fetch(0, lane, splats, ids[cbase + lane], true);
-        cp_async_commit();
-        int gid_next = cbase - 32 >= seg_lo ? ids[cbase - 32 + lane] : 0;
-        int buf = 0;
-        for (;;) {
-            const int nb = cbase - 32;
-            if (nb >= seg_lo) st.fetch(buf ^ 1, lane, splats, gid_next, true);
+        // chunks are aligned to the list start (seg_lo is a chunk boundary)
+        // and walked from the top one down: chunk c starts at top - 32 c
+        const int top = start + ((warp_hi - 1 - start) >> 5) * 32;
+        const int n_chunks = ((top - seg_lo) >> 5) + 1;
+        int gid[kStages];
+#pragma unroll
+        for (int c = 0; c < kStages; ++c) {
+            const int j = top - 32 * c + lane;
+            gid[c] = (c < n_chunks && j < warp_hi) ? ids[j] : -1;
+        }
+#pragma unroll
+        for (int c = 0; c < kStages - 1; ++c) {
+            if (gid[c] >= 0) st.fetch(c, lane, splats, gid[c], true);
             cp_async_commit();
-            const int gid_after = nb - 32 >= seg_lo ? ids[nb - 32 + lane] : 0;
-            cp_async_wait<1>();
+        }
+        int gid_next = gid[kStages - 1];
+        int buf = 0, ibuf = kStages - 1;
+        for (int ci = 0;; ++ci) {
+            const int base = top - 32 * ci;
+            if (gid_next >= 0) st.fetch(ibuf, lane, splats, gid_next, true);
+            cp_async_commit();
+            gid_next = ci + kStages < n_chunks ? ids[top - 32 * (ci + kStages) + lane] : -1;
+            cp_async_wait<kStages - 1>();
             __syncwarp();
-            const bool lv = cbase + lane < warp_hi &&
+            const bool lv = base + lane < warp_hi &&
                             rect_live(st.q[buf][0][lane], st.q[buf][1][lane].x,
                                       st.q[buf][2][lane], rx0, rx1, ry0, ry1);
             uint32_t live = __ballot_sync(0xffffffffu, lv);
@@ -443,41 +504,34 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                 const float power = pair_power(dx, dy, a.z, a.w, b4.x);
                 const float gauss = __expf(fminf(power, 0.0f));
                 const float alpha_raw = b4.y * gauss;
-                const bool clamped = alpha_raw > 0.999f;
                 const float alpha = fminf(0.999f, alpha_raw);
-                const bool active = inimg && (cbase + k < my_stop) && (power <= 0.0f) &&
+                const bool active = inimg && (base + k < my_stop) && (power <= 0.0f) &&
                                     (alpha >= 1.0f / 255.0f);
                 const uint32_t act = __ballot_sync(0xffffffffu, active);
                 if (act == 0u) continue;
-                float v[16];
-#pragma unroll
-                for (int q = 0; q < 16; ++q) v[q] = 0.0f;
-                if (active) {
-                    const float om = fmaxf(1.0f - alpha, 1e-8f);
-                    // segments bound the recovery chain to kSeg divisions
-                    const float inv = kSegmented ? __fdividef(1.0f, om) : __frcp_rn(om);
-                    T = T * inv;
-                    const float w = alpha * T;
-                    v[8] = w * gr; v[9] = w * gg; v[10] = w * gb;
-                    const float dL_dalpha =
-                        (gr * (T * b4.z - sr * inv) + gg * (T * b4.w - sg * inv) +
-                         gb * (T * cbk - sb * inv)) +
-                        ga * (T - sa * inv);
-                    sr += w * b4.z; sg += w * b4.w; sb += w * cbk;
-                    sa += w;
-                    if (!clamped) {
-                        const float dp = dL_dalpha * b4.y * gauss;
-                        v[2] = dL_dalpha * gauss;
-                        // d power / d u = ca dx + cb dy = -(2A dx + B dy)
-                        const float dux = -dp * (2.0f * a.z * dx + a.w * dy);
-                        const float duy = -dp * (a.w * dx + 2.0f * b4.x * dy);
-                        v[0] = dux; v[1] = duy;
-                        v[4] = dp * (-0.5f * dx * dx);
-                        v[5] = dp * (-1.0f * dx * dy);
-                        v[6] = dp * (-0.5f * dy * dy);
-                        if (want_absgrad) v[3] = sqrtf(dux * dux + duy * duy);
-                    }
-                }
+                // every lane evaluates; inactive lanes are masked to zero
+                const float om = fmaxf(1.0f - alpha, 1e-8f);
+                // segments bound the recovery chain to kSeg divisions
+                const float inv = kSegmented ? __fdividef(1.0f, om) : __frcp_rn(om);
+                const float Tn = T * inv;
+                const float q = gr * b4.z + gg * b4.w + gb * cbk + ga;
+                const float dL_dalpha = Tn * q - inv * S;
+                const float w = active ? alpha * Tn : 0.0f;
+                T = active ? Tn : T;
+                S += w * q;
+                // the 0.999 clamp cuts the gradient to opacity and position
+                const float dLg = (active && alpha_raw <= 0.999f) ? dL_dalpha * gauss : 0.0f;
+                const float dp = dLg * b4.y;
+                float v[10];
+                // d power / d u = ca dx + cb dy = -(2A dx + B dy)
+                v[0] = -dp * (2.0f * a.z * dx + a.w * dy);
+                v[1] = -dp * (a.w * dx + 2.0f * b4.x * dy);
+                v[2] = dLg;
+                v[3] = want_absgrad ? sqrtf(v[0] * v[0] + v[1] * v[1]) : 0.0f;
+                v[4] = dp * (-0.5f * dx * dx);
+                v[5] = dp * (-1.0f * dx * dy);
+                v[6] = dp * (-0.5f * dy * dy);
+                v[7] = w * gr; v[8] = w * gg; v[9] = w * gb;
                 float4* dst =
                     reinterpret_cast<float4*>(grad2d + (int64_t)st.id[buf][k] * MG_G2D_STRIDE);
                 if (__popc(act) <= 2) {
@@ -485,26 +539,23 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                     // warp reduction costs more than two sets of atomics)
                     if (active) {
                         atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
-                        if (v[4] != 0.f || v[5] != 0.f || v[6] != 0.f)
-                            atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
-                        atomicAdd(dst + 2, make_float4(v[8], v[9], v[10], 0.f));
+                        if (dp != 0.f) atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
+                        atomicAdd(dst + 2, make_float4(v[7], v[8], v[9], 0.f));
                     }
                     continue;
                 }
-                // lanes 2s, 2s+1 hold slot s; lanes 0, 8, 16 gather slots 0-3, 4-7, 8-11
-                const float r = reduce_scatter16(v, lane);
-                const float r1 = __shfl_down_sync(0xffffffffu, r, 2);
-                const float r2 = __shfl_down_sync(0xffffffffu, r, 4);
-                const float r3 = __shfl_down_sync(0xffffffffu, r, 6);
-                if ((lane & 7) == 0 && lane < 24 &&
-                    (r != 0.f || r1 != 0.f || r2 != 0.f || r3 != 0.f))
-                    atomicAdd(dst + (lane >> 3), make_float4(r, r1, r2, r3));
+                const float r = reduce_scatter10(v, lane);
+                const float r0 = __shfl_sync(0xffffffffu, r, g0);
+                const float r1 = __shfl_sync(0xffffffffu, r, g1);
+                const float r2 = __shfl_sync(0xffffffffu, r, g2);
+                const float r3 = __shfl_sync(0xffffffffu, r, g3);
+                if (lane < 3 && (r0 != 0.f || r1 != 0.f || r2 != 0.f || r3 != 0.f))
+                    atomicAdd(dst + lane, make_float4(r0, r1, r2, r3));
             }
-            __syncwarp();  // buffer buf is refilled two chunks on
-            if (nb < seg_lo) break;
-            cbase = nb;
-            buf ^= 1;
-            gid_next = gid_after;
+            __syncwarp();  // buffer buf is refilled kStages - 1 chunks on
+            if (ci + 1 >= n_chunks) break;
+            buf = buf + 1 == kStages ? 0 : buf + 1;
+            ibuf = ibuf + 1 == kStages ? 0 : ibuf + 1;
         }
         cp_async_wait<0>();
         __syncwarp();
@@ -513,81 +564,116 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
 
 // ---------------------------------------------------------------- ordering
 
-// Longest-first tile order: a one-CTA counting sort of the tiles by the
-// bucket floor(log2(work)) + 1, heaviest bucket first. Optionally zeroes a
-// work counter and a per-tile array for the kernel that follows.
+// Inclusive prefix sum across the warp.
+__device__ __forceinline__ int warp_incl_scan(int x, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+    }
+    return x;
+}
+
+// One-CTA counting sort into K classes, class K-1 first. Each thread owns
+// the elements tid, tid + 1024, ... and counts them per class in registers;
+// per class, every warp scans its lanes' counts and reserves its range with
+// one shared-memory atomic, so there is no per-element atomic. Returns, per
+// class, this thread's first output position.
+template <int K>
+__device__ __forceinline__ void class_positions(const int (&cnt)[K], int (&pos)[K], int lane,
+                                                int* s_total /* [K], zeroed */) {
+    int wbase[K], excl[K];
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        const int incl = warp_incl_scan(cnt[c], lane);
+        const int wtot = __shfl_sync(0xffffffffu, incl, 31);
+        int b = 0;
+        if (lane == 31 && wtot > 0) b = atomicAdd(&s_total[c], wtot);
+        wbase[c] = __shfl_sync(0xffffffffu, b, 31);
+        excl[c] = incl - cnt[c];
+    }
+    __syncthreads();  // class totals complete
+    int run = 0;
+#pragma unroll
+    for (int c = K - 1; c >= 0; --c) {
+        pos[c] = run + wbase[c] + excl[c];
+        run += s_total[c];
+    }
+}
+
+constexpr int kOrderClasses = 8;
+
+// Length class of a tile: floor(log2(len)) - 6 clamped to [0, 7].
+__device__ __forceinline__ int length_class(int w) {
+    if (w <= 0) return 0;
+    return min(kOrderClasses - 1, max(0, (31 - __clz(w)) - 6));
+}
+
+// Longest-first tile order by list-length class (order inside a class is
+// unspecified). Optionally zeroes a work counter and a per-tile array for the
+// kernel that follows.
 __global__ void __launch_bounds__(1024)
 tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ work,
                   int n_tiles, int32_t* __restrict__ order, int32_t* __restrict__ zero_word,
                   int32_t* __restrict__ zero_tiles) {
-    __shared__ int s_count[33];
-    __shared__ int s_cursor[33];
-    const int tid = threadIdx.x;
-    if (tid < 33) s_count[tid] = 0;
+    __shared__ int s_total[kOrderClasses];
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < kOrderClasses) s_total[tid] = 0;
     if (tid == 0 && zero_word) *zero_word = 0;
     __syncthreads();
+    int cnt[kOrderClasses], pos[kOrderClasses];
+#pragma unroll
+    for (int c = 0; c < kOrderClasses; ++c) cnt[c] = 0;
     for (int t = tid; t < n_tiles; t += 1024) {
-        const int w = work ? work[t] : offsets[t + 1] - offsets[t];
-        const int b = w > 0 ? 32 - __clz(w) : 0;  // 0..31
-        atomicAdd(&s_count[31 - b], 1);            // heaviest bucket first
+        const int cls = length_class(work ? work[t] : offsets[t + 1] - offsets[t]);
+#pragma unroll
+        for (int c = 0; c < kOrderClasses; ++c) cnt[c] += cls == c;
         if (zero_tiles) zero_tiles[t] = 0;
     }
-    __syncthreads();
-    if (tid == 0) {
-        int run = 0;
-        for (int b = 0; b < 33; ++b) { s_cursor[b] = run; run += s_count[b]; }
-    }
-    __syncthreads();
+    class_positions<kOrderClasses>(cnt, pos, lane, s_total);
     for (int t = tid; t < n_tiles; t += 1024) {
-        const int w = work ? work[t] : offsets[t + 1] - offsets[t];
-        const int b = w > 0 ? 32 - __clz(w) : 0;
-        order[atomicAdd(&s_cursor[31 - b], 1)] = t;
+        const int cls = length_class(work ? work[t] : offsets[t + 1] - offsets[t]);
+#pragma unroll
+        for (int c = 0; c < kOrderClasses; ++c)
+            if (cls == c) order[pos[c]++] = t;
     }
 }
 
-// Backward work items, longest first: with segments (seg > 0), each block's
-// walk becomes floor(walk / seg) whole segments (bucket 0) plus one partial
-// segment in bucket clz(length) (longer partials first); without, one item
-// per block with a non-empty list, bucketed by its list length. One CTA; also
-// zeroes the backward's pull counter and publishes the item count.
+// Backward work items: with segments (seg > 0), each block's walk becomes
+// floor(walk / seg) whole segments plus one partial segment, whole segments
+// first (every item is at most one segment, so the order inside a class does
+// not form a tail); without, one item per block with a non-empty list. One
+// CTA; also zeroes the backward's pull counter and publishes the item count.
 __global__ void __launch_bounds__(1024)
 backward_items_kernel(const int32_t* __restrict__ offsets,
                       const int32_t* __restrict__ block_work, int n_tiles, int blocks_per_tile,
                       int seg, int2* __restrict__ items, int32_t* __restrict__ counters) {
-    __shared__ int s_count[33];
-    __shared__ int s_cursor[33];
-    const int tid = threadIdx.x;
+    __shared__ int s_total[2];
+    const int tid = threadIdx.x, lane = tid & 31;
     const int n_blocks = n_tiles * blocks_per_tile;
-    if (tid < 33) s_count[tid] = 0;
+    if (tid < 2) s_total[tid] = 0;
     __syncthreads();
+    int cnt[2] = {0, 0}, pos[2];  // [0] partial segments, [1] whole segments
     for (int b = tid; b < n_blocks; b += 1024) {
         const int t = b / blocks_per_tile;
         const int w = block_work ? block_work[b] : offsets[t + 1] - offsets[t];
         if (w <= 0) continue;
         const int full = seg > 0 ? w / seg : 0;
-        const int rem = w - full * seg;
-        if (full) atomicAdd(&s_count[0], full);
-        if (rem) atomicAdd(&s_count[__clz(rem)], 1);
+        cnt[1] += full;
+        cnt[0] += w - full * seg > 0;
     }
-    __syncthreads();
+    class_positions<2>(cnt, pos, lane, s_total);
     if (tid == 0) {
-        int run = 0;
-        for (int k = 0; k < 33; ++k) { s_cursor[k] = run; run += s_count[k]; }
         counters[1] = 0;
-        counters[2] = run;
+        counters[2] = s_total[0] + s_total[1];
     }
-    __syncthreads();
     for (int b = tid; b < n_blocks; b += 1024) {
         const int t = b / blocks_per_tile;
         const int w = block_work ? block_work[b] : offsets[t + 1] - offsets[t];
         if (w <= 0) continue;
         const int full = seg > 0 ? w / seg : 0;
-        const int rem = w - full * seg;
-        if (full) {
-            const int at = atomicAdd(&s_cursor[0], full);
-            for (int s = 0; s < full; ++s) items[at + s] = make_int2(b, s);
-        }
-        if (rem) items[atomicAdd(&s_cursor[__clz(rem)], 1)] = make_int2(b, full);
+        for (int k = 0; k < full; ++k) items[pos[1]++] = make_int2(b, k);
+        if (w - full * seg > 0) items[pos[0]++] = make_int2(b, full);
     }
 }
 
