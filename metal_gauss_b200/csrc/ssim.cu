@@ -111,61 +111,124 @@ __global__ void ssim_chain_backward_kernel(const float* __restrict__ x, const fl
 }
 
 // ------------------------------------------------------- fused training loss
+//
+// Tiles of kLW x kLH outputs per 256-thread block (32 x 8 threads); one colour
+// channel at a time. The block stages its inputs with the 5-pixel halo, then
+//  * horizontal pass: each thread produces 4 adjacent columns of one staged
+//    row from 14 inputs held in registers (16-byte shared loads; products
+//    such as x*x formed once per input, not once per tap);
+//  * vertical pass: each thread produces kLRows adjacent rows of one column
+//    from kLRows + 10 horizontally blurred rows.
 
-constexpr int kLT = 16;               // output tile side
-constexpr int kLH = kLT + 2 * kR;     // staged side with halo (26)
+constexpr int kLW = 32;              // output tile width (one warp of columns)
+constexpr int kLH = 24;              // output tile height
+constexpr int kLRows = kLH / 8;      // output rows per thread in the vertical pass
+constexpr int kSW = kLW + 2 * kR;    // staged width (42)
+constexpr int kSH = kLH + 2 * kR;    // staged height (34)
+constexpr int kSP = 44;              // staged row pitch: 16-byte rows, banks staggered
+constexpr int kHItems = kSH * (kLW / 4);  // horizontal work items (row, 4-column group)
+
+// 16 staged values from column 4g of a row (only the first 14 are used).
+__device__ __forceinline__ void load16(const float* row, int g, float (&v)[16]) {
+    const float4* r = reinterpret_cast<const float4*>(row) + g;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float4 t = r[k];
+        v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+    }
+}
+
+// Stages channel c of `src` (H, W, 3) around the tile at (ox, oy), zero outside.
+__device__ __forceinline__ void stage_channel(const float* __restrict__ src, int c, int W, int H,
+                                              int ox, int oy, float (*dst)[kSP]) {
+    for (int ly = threadIdx.y; ly < kSH; ly += 8) {
+        const int gy = oy + ly - kR;
+        for (int lx = threadIdx.x; lx < kSP; lx += 32) {
+            const int gx = ox + lx - kR;
+            const bool ok = lx < kSW && gx >= 0 && gx < W && gy >= 0 && gy < H;
+            dst[ly][lx] = ok ? src[((int64_t)gy * W + gx) * 3 + c] : 0.f;
+        }
+    }
+}
 
 // Kernel 1: moments -> SSIM, its adjoint maps and the loss partial sums.
-__global__ void __launch_bounds__(kLT * kLT)
+#ifndef MG_LOSS_MIN_BLOCKS
+#define MG_LOSS_MIN_BLOCKS 6
+#endif
+// Six blocks per SM keep an 800 x 800 image (850 tiles) in one wave.
+__global__ void __launch_bounds__(256, MG_LOSS_MIN_BLOCKS)
 loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
                     const float* __restrict__ win, int W, int H, float g_ssim,
                     float* __restrict__ adj, float* __restrict__ partial) {
-    __shared__ float c_win[11];
-    __shared__ float s_x[kLH][kLH + 1], s_y[kLH][kLH + 1];
-    __shared__ float s_h[5][kLH][kLT + 1];
-    __shared__ float s_red[2][kLT * kLT / 32];
-    const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * kLT + tx;
-    const int ox = blockIdx.x * kLT, oy = blockIdx.y * kLT;
-    const int px = ox + tx, py = oy + ty;
-    const bool in = px < W && py < H;
+    __shared__ __align__(16) float s_x[kSH][kSP];
+    __shared__ __align__(16) float s_y[kSH][kSP];
+    __shared__ __align__(16) float s_h[5][kSH][kLW];
+    __shared__ float s_red[2][8];
+    const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * 32 + tx;
+    const int ox = blockIdx.x * kLW, oy = blockIdx.y * kLH;
     const int64_t npix = (int64_t)W * H;
-    if (tid < 11) c_win[tid] = win[tid];  // published by the first barrier below
+    float wk[11];
+#pragma unroll
+    for (int k = 0; k < 11; ++k) wk[k] = win[k];
     float sum_s = 0.f, sum_l1 = 0.f;
     for (int c = 0; c < 3; ++c) {
-        for (int i = tid; i < kLH * kLH; i += kLT * kLT) {
-            const int ly = i / kLH, lx = i % kLH;
-            const int gx = ox + lx - kR, gy = oy + ly - kR;
-            const bool ok = gx >= 0 && gx < W && gy >= 0 && gy < H;
-            const int64_t o = ((int64_t)gy * W + gx) * 3 + c;
-            s_x[ly][lx] = ok ? x[o] : 0.f;
-            s_y[ly][lx] = ok ? y[o] : 0.f;
-        }
+        stage_channel(x, c, W, H, ox, oy, s_x);
+        stage_channel(y, c, W, H, ox, oy, s_y);
         __syncthreads();
-        // horizontal pass over all kLH rows, kLT output columns
-        for (int i = tid; i < kLH * kLT; i += kLT * kLT) {
-            const int ly = i / kLT, lx = i % kLT;
-            float a0 = 0, a1 = 0, a2 = 0, a3 = 0, a4 = 0;
+        for (int it = tid; it < kHItems; it += 256) {
+            const int row = it >> 3, g = it & 7;
+            float xv[16], yv[16];
+            load16(s_x[row], g, xv);
+            load16(s_y[row], g, yv);
+            float acc[5][4];
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float wk = c_win[k];
-                const float xv = s_x[ly][lx + k], yv = s_y[ly][lx + k];
-                a0 += wk * xv; a1 += wk * yv;
-                a2 += wk * xv * xv; a3 += wk * yv * yv; a4 += wk * xv * yv;
+            for (int q = 0; q < 5; ++q)
+#pragma unroll
+                for (int p = 0; p < 4; ++p) acc[q][p] = 0.f;
+#pragma unroll
+            for (int j = 0; j < 14; ++j) {
+                const float a = xv[j], b = yv[j];
+                const float v5[5] = {a, b, a * a, b * b, a * b};
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const int k = j - p;
+                    if (k < 0 || k > 10) continue;
+#pragma unroll
+                    for (int q = 0; q < 5; ++q) acc[q][p] += wk[k] * v5[q];
+                }
             }
-            s_h[0][ly][lx] = a0; s_h[1][ly][lx] = a1; s_h[2][ly][lx] = a2;
-            s_h[3][ly][lx] = a3; s_h[4][ly][lx] = a4;
+#pragma unroll
+            for (int q = 0; q < 5; ++q)
+                reinterpret_cast<float4*>(s_h[q][row])[g] =
+                    make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
         }
         __syncthreads();
-        float m[5] = {0, 0, 0, 0, 0};
+        float m[5][kLRows];
 #pragma unroll
-        for (int k = 0; k < 11; ++k) {
-            const float wk = c_win[k];
+        for (int q = 0; q < 5; ++q)
 #pragma unroll
-            for (int q = 0; q < 5; ++q) m[q] += wk * s_h[q][ty + k][tx];
+            for (int p = 0; p < kLRows; ++p) m[q][p] = 0.f;
+#pragma unroll
+        for (int j = 0; j < kLRows + 10; ++j) {
+            float hv[5];
+#pragma unroll
+            for (int q = 0; q < 5; ++q) hv[q] = s_h[q][ty * kLRows + j][tx];
+#pragma unroll
+            for (int p = 0; p < kLRows; ++p) {
+                const int k = j - p;
+                if (k < 0 || k > 10) continue;
+#pragma unroll
+                for (int q = 0; q < 5; ++q) m[q][p] += wk[k] * hv[q];
+            }
         }
-        if (in) {
-            const float MX = m[0], MY = m[1];
-            const float sxx = m[2] - MX * MX, syy = m[3] - MY * MY, sxy = m[4] - MX * MY;
+        const int px = ox + tx;
+#pragma unroll
+        for (int p = 0; p < kLRows; ++p) {
+            const int ly = ty * kLRows + p, py = oy + ly;
+            if (px >= W || py >= H) continue;
+            const float MX = m[0][p], MY = m[1][p];
+            const float sxx = m[2][p] - MX * MX, syy = m[3][p] - MY * MY;
+            const float sxy = m[4][p] - MX * MY;
             const float A = 2.0f * MX * MY + kC1, B = 2.0f * sxy + kC2;
             const float C = MX * MX + MY * MY + kC1, D = sxx + syy + kC2;
             const float invCD = 1.0f / (C * D);
@@ -176,20 +239,19 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
             adj[(3 * c + 1) * npix + o] = g_ssim * dD;
             adj[(3 * c + 2) * npix + o] = g_ssim * (2.0f * dB);
             sum_s += S;
-            sum_l1 += fabsf(s_x[ty + kR][tx + kR] - s_y[ty + kR][tx + kR]);
+            sum_l1 += fabsf(s_x[ly + kR][tx + kR] - s_y[ly + kR][tx + kR]);
         }
-        __syncthreads();
+        __syncthreads();  // the next channel restages s_x, s_y, s_h
     }
-    // block partial sums of S and |x - y|
     for (int o = 16; o > 0; o >>= 1) {
         sum_s += __shfl_xor_sync(0xffffffffu, sum_s, o);
         sum_l1 += __shfl_xor_sync(0xffffffffu, sum_l1, o);
     }
-    if ((tid & 31) == 0) { s_red[0][tid >> 5] = sum_s; s_red[1][tid >> 5] = sum_l1; }
+    if (tx == 0) { s_red[0][ty] = sum_s; s_red[1][ty] = sum_l1; }
     __syncthreads();
     if (tid == 0) {
         float a = 0.f, b = 0.f;
-        for (int i = 0; i < kLT * kLT / 32; ++i) { a += s_red[0][i]; b += s_red[1][i]; }
+        for (int i = 0; i < 8; ++i) { a += s_red[0][i]; b += s_red[1][i]; }
         const int64_t blk = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
         partial[2 * blk + 0] = a;
         partial[2 * blk + 1] = b;
@@ -197,54 +259,80 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
 }
 
 // Kernel 2: blur the adjoint maps back and apply the chain rule + L1 term.
-__global__ void __launch_bounds__(kLT * kLT)
+__global__ void __launch_bounds__(256, 6)
 loss_grad_kernel(const float* __restrict__ x, const float* __restrict__ y,
                  const float* __restrict__ adj, const float* __restrict__ win, int W, int H,
                  float g_l1, float* __restrict__ grad_x) {
-    __shared__ float c_win[11];
-    __shared__ float s_a[3][kLH][kLH + 1];
-    __shared__ float s_h[3][kLH][kLT + 1];
-    const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * kLT + tx;
-    const int ox = blockIdx.x * kLT, oy = blockIdx.y * kLT;
-    const int px = ox + tx, py = oy + ty;
-    const bool in = px < W && py < H;
+    __shared__ __align__(16) float s_a[3][kSH][kSP];
+    __shared__ __align__(16) float s_h[3][kSH][kLW];
+    const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * 32 + tx;
+    const int ox = blockIdx.x * kLW, oy = blockIdx.y * kLH;
     const int64_t npix = (int64_t)W * H;
-    if (tid < 11) c_win[tid] = win[tid];  // published by the first barrier below
+    float wk[11];
+#pragma unroll
+    for (int k = 0; k < 11; ++k) wk[k] = win[k];
     for (int c = 0; c < 3; ++c) {
-        for (int i = tid; i < kLH * kLH; i += kLT * kLT) {
-            const int ly = i / kLH, lx = i % kLH;
-            const int gx = ox + lx - kR, gy = oy + ly - kR;
-            const bool ok = gx >= 0 && gx < W && gy >= 0 && gy < H;
-            const int64_t o = (int64_t)gy * W + gx;
+        for (int ly = ty; ly < kSH; ly += 8) {
+            const int gy = oy + ly - kR;
+            for (int lx = tx; lx < kSP; lx += 32) {
+                const int gx = ox + lx - kR;
+                const bool ok = lx < kSW && gx >= 0 && gx < W && gy >= 0 && gy < H;
+                const int64_t o = (int64_t)gy * W + gx;
 #pragma unroll
-            for (int q = 0; q < 3; ++q) s_a[q][ly][lx] = ok ? adj[(3 * c + q) * npix + o] : 0.f;
-        }
-        __syncthreads();
-        for (int i = tid; i < kLH * kLT; i += kLT * kLT) {
-            const int ly = i / kLT, lx = i % kLT;
-            float a0 = 0, a1 = 0, a2 = 0;
-#pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float wk = c_win[k];
-                a0 += wk * s_a[0][ly][lx + k]; a1 += wk * s_a[1][ly][lx + k];
-                a2 += wk * s_a[2][ly][lx + k];
+                for (int q = 0; q < 3; ++q)
+                    s_a[q][ly][lx] = ok ? adj[(3 * c + q) * npix + o] : 0.f;
             }
-            s_h[0][ly][lx] = a0; s_h[1][ly][lx] = a1; s_h[2][ly][lx] = a2;
         }
         __syncthreads();
-        float b0 = 0, b1 = 0, b2 = 0;
+        for (int it = tid; it < kHItems; it += 256) {
+            const int row = it >> 3, g = it & 7;
+            float acc[3][4];
 #pragma unroll
-        for (int k = 0; k < 11; ++k) {
-            const float wk = c_win[k];
-            b0 += wk * s_h[0][ty + k][tx]; b1 += wk * s_h[1][ty + k][tx];
-            b2 += wk * s_h[2][ty + k][tx];
+            for (int q = 0; q < 3; ++q) {
+                float v[16];
+                load16(s_a[q][row], g, v);
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    float a = 0.f;
+#pragma unroll
+                    for (int k = 0; k < 11; ++k) a += wk[k] * v[p + k];
+                    acc[q][p] = a;
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 3; ++q)
+                reinterpret_cast<float4*>(s_h[q][row])[g] =
+                    make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
         }
-        if (in) {
+        __syncthreads();
+        float b[3][kLRows];
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+#pragma unroll
+            for (int p = 0; p < kLRows; ++p) b[q][p] = 0.f;
+#pragma unroll
+        for (int j = 0; j < kLRows + 10; ++j) {
+            float hv[3];
+#pragma unroll
+            for (int q = 0; q < 3; ++q) hv[q] = s_h[q][ty * kLRows + j][tx];
+#pragma unroll
+            for (int p = 0; p < kLRows; ++p) {
+                const int k = j - p;
+                if (k < 0 || k > 10) continue;
+#pragma unroll
+                for (int q = 0; q < 3; ++q) b[q][p] += wk[k] * hv[q];
+            }
+        }
+        const int px = ox + tx;
+#pragma unroll
+        for (int p = 0; p < kLRows; ++p) {
+            const int py = oy + ty * kLRows + p;
+            if (px >= W || py >= H) continue;
             const int64_t o = ((int64_t)py * W + px) * 3 + c;
             const float xv = x[o], yv = y[o];
             const float diff = xv - yv;
             const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
-            grad_x[o] = b0 + 2.0f * xv * b1 + yv * b2 + g_l1 * sgn;
+            grad_x[o] = b[0][p] + 2.0f * xv * b[1][p] + yv * b[2][p] + g_l1 * sgn;
         }
         __syncthreads();
     }
@@ -334,8 +422,10 @@ extern "C" mg_status mg_ssim_chain_backward(const float* x, const float* y,
     return check_launch("ssim_chain_backward");
 }
 
+static dim3 loss_grid(int W, int H) { return dim3((W + kLW - 1) / kLW, (H + kLH - 1) / kLH, 1); }
+
 extern "C" size_t mg_l1_ssim_scratch_bytes(int32_t height, int32_t width) {
-    const dim3 g = grid2d(width, height, kLT);
+    const dim3 g = loss_grid(width, height);
     const size_t adj = sizeof(float) * 9 * (size_t)height * width;
     const size_t part = sizeof(float) * 2 * (size_t)g.x * g.y;
     return ((adj + 255) & ~(size_t)255) + ((part + 255) & ~(size_t)255);
@@ -350,17 +440,17 @@ extern "C" mg_status mg_l1_ssim_loss(const float* x, const float* y, const float
     MG_REQUIRE(scratch && scratch_bytes >= mg_l1_ssim_scratch_bytes(height, width),
                "l1_ssim_loss: scratch buffer too small");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const dim3 g = grid2d(width, height, kLT);
+    const dim3 g = loss_grid(width, height);
     const int64_t npix = (int64_t)height * width;
     float* adj = static_cast<float*>(scratch);
     float* partial = reinterpret_cast<float*>(static_cast<char*>(scratch) +
                                               ((sizeof(float) * 9 * npix + 255) & ~(size_t)255));
     const float inv_n = 1.0f / (float)(3 * npix);
     // d loss / d S_p = -scale * w_ssim / n ; d loss / d x = scale * w_l1 * sign / n
-    loss_moments_kernel<<<g, dim3(kLT, kLT), 0, s>>>(x, y, w, width, height,
+    loss_moments_kernel<<<g, dim3(32, 8), 0, s>>>(x, y, w, width, height,
                                                      -scale * w_ssim * inv_n, adj, partial);
     MG_TRY(check_launch("l1_ssim_loss moments"));
-    loss_grad_kernel<<<g, dim3(kLT, kLT), 0, s>>>(x, y, adj, w, width, height,
+    loss_grad_kernel<<<g, dim3(32, 8), 0, s>>>(x, y, adj, w, width, height,
                                                   scale * w_l1 * inv_n, grad_x);
     MG_TRY(check_launch("l1_ssim_loss grad"));
     loss_finish_kernel<<<1, 256, 0, s>>>(partial, (int)(g.x * g.y), w_l1, w_ssim, scale,
