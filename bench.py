@@ -24,6 +24,7 @@ import argparse
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -210,6 +211,25 @@ def stage_bytes(stage: str, n: int, walked: float, P: int, n_tiles: int,
     return 0.0
 
 
+TRAFFIC_PROFILE = ROOT / "profiles" / "raster_cfg3_1view.md"
+
+
+def profiled_traffic(kernel: str, args):
+    """DRAM bytes (read + write) per launch of `kernel`, from the committed
+    ncu capture of one view of the default workload, or (None, reason) when
+    this run is not that workload or the capture has no figure for it."""
+    if (args.n_gaussians, args.width, args.height) != (1_000_000, 800, 800):
+        return None, "no capture for this workload size"
+    try:
+        text = TRAFFIC_PROFILE.read_text()
+    except OSError:
+        return None, "capture summary missing"
+    for name, val in re.findall(r"<!-- traffic_bytes_per_launch (\S+) (\d+) -->", text):
+        if name == kernel:
+            return int(val), f"{TRAFFIC_PROFILE.relative_to(ROOT)} (ncu --set full, one view)"
+    return None, f"no capture of {kernel}"
+
+
 # ---------------------------------------------------------------- our arm
 
 def run_ours(args, rank, world, local):
@@ -283,10 +303,12 @@ def run_ours(args, rank, world, local):
     dom_bytes = stage_bytes(dom, n, walked, P, n_tiles, n_vis_view)
     peaks = measured_peaks()
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    traffic, traffic_src = profiled_traffic(dom, args)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "peak_source": peaks["source"], "traffic": None,
+                "peak_source": peaks["source"], "traffic": traffic,
+                "traffic_source": traffic_src,
                 "bytes_per_launch": dom_bytes, "avg_launch_ms": round(dom_ms, 4),
                 "launches_timed": len(dom_times)}
 
