@@ -32,7 +32,8 @@
 //
 // Backward, back to front: work items are (warp block, segment) pairs, a
 // segment being MG_RASTER_SEGMENT consecutive entries of the block's walk,
-// longest first. A segment starts from the checkpoint at its upper end (T
+// which the forward appends as it finishes each block. A segment starts from
+// the checkpoint at its upper end (T
 // there; the colour behind it is the final colour minus the checkpointed one),
 // so a long list is split over many warps instead of forming the kernel's
 // tail. The colour and alpha behind an entry enter its gradient only through
@@ -215,7 +216,8 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                       float* __restrict__ out_T, int32_t* __restrict__ out_stop,
                       const int32_t* __restrict__ order, int32_t* __restrict__ counter,
                       int32_t* __restrict__ block_work, int32_t* __restrict__ tile_work,
-                      float* __restrict__ ckpt, int m_cap, int32_t* __restrict__ err) {
+                      float* __restrict__ ckpt, int2* __restrict__ items, int m_cap,
+                      int32_t* __restrict__ err) {
     using G = Blocks<TILE>;
     constexpr int kStages = kFwdStages;
     __shared__ WarpStage<kStages> s_stage[kRasterWarps];
@@ -326,10 +328,19 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
             __syncwarp();
         }
         const int walk = __reduce_max_sync(0xffffffffu, stop) - start;
+        // the backward's work items for this block: one per MG_RASTER_SEGMENT
+        // entries of its walk (appended in completion order; every item is at
+        // most one segment, so their order forms no tail)
+        const int nseg = (walk + kSeg - 1) / kSeg;
+        int ibase = 0;
         if (lane == 0) {
             block_work[tile_id * G::kCount + wb] = walk;
             if (tile_work && walk > 0) atomicMax(&tile_work[tile_id], walk);
+            if (nseg > 0) ibase = atomicAdd(&counter[2], nseg);
         }
+        ibase = __shfl_sync(0xffffffffu, ibase, 0);
+        for (int sgi = lane; sgi < nseg; sgi += 32)
+            items[ibase + sgi] = make_int2(tile_id * G::kCount + wb, sgi);
         if (inimg) {
             const int64_t o = (int64_t)py * W + px;
             if (has_bg) {
@@ -619,7 +630,7 @@ tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict
     __shared__ int s_total[kOrderClasses];
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid < kOrderClasses) s_total[tid] = 0;
-    if (tid == 0 && zero_word) *zero_word = 0;
+    if (tid < 4 && zero_word) zero_word[tid] = 0;  // a kernel's work counters
     __syncthreads();
     int cnt[kOrderClasses], pos[kOrderClasses];
 #pragma unroll
@@ -639,11 +650,12 @@ tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict
     }
 }
 
-// Backward work items: with segments (seg > 0), each block's walk becomes
-// floor(walk / seg) whole segments plus one partial segment, whole segments
-// first (every item is at most one segment, so the order inside a class does
-// not form a tail); without, one item per block with a non-empty list. One
-// CTA; also zeroes the backward's pull counter and publishes the item count.
+// Backward work items when there is no forward state (the segmented
+// backward's items are appended by the forward itself): one item per block
+// with a non-empty list, longest list first; with seg > 0 each block's walk
+// would instead become floor(walk / seg) whole segments plus one partial
+// segment, whole segments first. One CTA; also zeroes the backward's pull
+// counter and publishes the item count.
 __global__ void __launch_bounds__(1024)
 backward_items_kernel(const int32_t* __restrict__ offsets,
                       const int32_t* __restrict__ block_work, int n_tiles, int blocks_per_tile,
@@ -766,7 +778,7 @@ mg_status launch_fwd(const float4* splats, const int32_t* ids, const int32_t* of
     raster_forward_kernel<TILE><<<grid, kRasterWarps * 32, 0, stream>>>(
         splats, ids, offsets, W, H, tiles_x, n_tiles, bg != nullptr, bg ? bg[0] : 0.f,
         bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, rgb, alpha, T, stop, sc.order, sc.counters,
-        sc.block_work, tile_work, sc.ckpt, m_cap, device_error_word());
+        sc.block_work, tile_work, sc.ckpt, sc.items, m_cap, device_error_word());
     return check_launch("rasterize_forward");
 }
 
@@ -778,10 +790,17 @@ mg_status launch_bwd_mode(const float4* splats, const int32_t* ids, const int32_
                           int want_absgrad, float* grad2d, const RasterScratch& sc,
                           int m_cap, cudaStream_t stream) {
     const int n_tiles = tiles_x * tiles_y;
-    backward_items_kernel<<<1, 1024, 0, stream>>>(offsets, kSegmented ? sc.block_work : nullptr,
-                                                  n_tiles, Blocks<TILE>::kCount,
-                                                  kSegmented ? kSeg : 0, sc.items, sc.counters);
-    MG_TRY(check_launch("rasterize_backward items"));
+    if (kSegmented) {
+        // the forward of this view appended the items and their count; only
+        // the pull counter starts over (a second backward reuses the items)
+        if (cudaMemsetAsync(sc.counters + 1, 0, sizeof(int32_t), stream) != cudaSuccess)
+            return check_launch("rasterize_backward counter");
+    } else {
+        backward_items_kernel<<<1, 1024, 0, stream>>>(offsets, nullptr, n_tiles,
+                                                      Blocks<TILE>::kCount, 0, sc.items,
+                                                      sc.counters);
+        MG_TRY(check_launch("rasterize_backward items"));
+    }
     const void* k = reinterpret_cast<const void*>(&raster_backward_kernel<TILE, kSegmented>);
     const int grid = persistent_grid(k, kRasterWarps * 32);
     if (grid <= 0) return check_launch("rasterize_backward occupancy");

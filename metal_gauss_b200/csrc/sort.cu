@@ -28,6 +28,7 @@ constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kHistPrivatePasses = 4;  // per-warp histogram copies up to this many passes
 
 template <typename K> struct SortTraits;
 template <> struct SortTraits<uint32_t> { static constexpr int kItems = 16; };
@@ -84,22 +85,29 @@ template <typename K>
 __global__ void __launch_bounds__(kSortThreads)
 radix_histogram_kernel(const K* __restrict__ keys, int64_t n, int bits, int passes,
                        uint32_t* __restrict__ hist) {
-    __shared__ uint32_t s_hist[8][kRadix];
-    for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads)
-        s_hist[i / kRadix][i % kRadix] = 0u;
+    // One counter set per warp (keys with few distinct digits, such as the
+    // high bits of tile ids, would otherwise serialise every warp of the
+    // block on the same shared-memory words), when they fit.
+    extern __shared__ uint32_t s_hist[];
+    const bool per_warp = passes <= kHistPrivatePasses;
+    const int sets = per_warp ? kSortWarps : 1;
+    const int words = sets * passes * kRadix;
+    for (int i = threadIdx.x; i < words; i += kSortThreads) s_hist[i] = 0u;
     __syncthreads();
+    uint32_t* mine = s_hist + (per_warp ? (threadIdx.x >> 5) * passes * kRadix : 0);
     for (int64_t i = (int64_t)blockIdx.x * kSortThreads + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * kSortThreads) {
         const K k = keys[i];
         for (int p = 0; p < passes; ++p) {
             const int shift = p * kRadixBits;
             const int db = min(kRadixBits, bits - shift);
-            atomicAdd(&s_hist[p][digit_of(k, shift, (1u << db) - 1u)], 1u);
+            atomicAdd(&mine[p * kRadix + digit_of(k, shift, (1u << db) - 1u)], 1u);
         }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) {
-        const uint32_t c = s_hist[i / kRadix][i % kRadix];
+        uint32_t c = 0u;
+        for (int w = 0; w < sets; ++w) c += s_hist[w * passes * kRadix + i];
         if (c) atomicAdd(&hist[i], c);
     }
 }
@@ -387,6 +395,32 @@ __global__ void tile_ranges_kernel(const uint32_t* __restrict__ tiles,
         for (int64_t tt = t + 1; tt <= n_tiles; ++tt) offsets[tt] = (int32_t)m;
 }
 
+// Same as tile_ranges_kernel for 32-bit tile ids on a 16-byte boundary: each
+// thread reads four consecutive ids with one vector load.
+__global__ void tile_ranges4_kernel(const uint32_t* __restrict__ tiles, int64_t m, int n_tiles,
+                                    int32_t* __restrict__ offsets) {
+    const int64_t i0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+    if (i0 >= m) return;
+    uint32_t t[4];
+    if (i0 + 3 < m) {
+        const uint4 v = reinterpret_cast<const uint4*>(tiles)[i0 >> 2];
+        t[0] = v.x; t[1] = v.y; t[2] = v.z; t[3] = v.w;
+    } else {
+        for (int k = 0; k < 4; ++k) t[k] = i0 + k < m ? tiles[i0 + k] : 0u;
+    }
+    int64_t prev = i0 == 0 ? -1 : min((int64_t)tiles[i0 - 1], (int64_t)n_tiles);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int64_t i = i0 + k;
+        if (i >= m) break;
+        const int64_t tk = min((int64_t)t[k], (int64_t)n_tiles);
+        for (int64_t tt = prev + 1; tt <= tk; ++tt) offsets[tt] = (int32_t)i;
+        if (i == m - 1)
+            for (int64_t tt = tk + 1; tt <= n_tiles; ++tt) offsets[tt] = (int32_t)m;
+        prev = tk;
+    }
+}
+
 }  // namespace
 
 size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes) {
@@ -411,7 +445,9 @@ mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_
         return check_launch("sort scratch memset");
 
     const int hist_blocks = std::min<int64_t>((n + 4095) / 4096, 148 * 4);
-    radix_histogram_kernel<K><<<std::max(1, hist_blocks), kSortThreads, 0, stream>>>(
+    const size_t hist_smem = sizeof(uint32_t) * kRadix * s.passes *
+                             (s.passes <= kHistPrivatePasses ? kSortWarps : 1);
+    radix_histogram_kernel<K><<<std::max(1, hist_blocks), kSortThreads, hist_smem, stream>>>(
         keys, n, bits, s.passes, s.hist);
     MG_TRY(check_launch("radix_histogram"));
     radix_offsets_kernel<<<s.passes, kRadix, 0, stream>>>(s.hist);
@@ -472,6 +508,11 @@ mg_status launch_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64, i
             cudaSuccess)
             return check_launch("tile_ranges memset");
         return MG_OK;
+    }
+    if (keys64 == nullptr && (reinterpret_cast<uintptr_t>(tile_ids) & 15u) == 0u) {
+        tile_ranges4_kernel<<<ceil_div((m + 3) / 4, 256), 256, 0, stream>>>(tile_ids, m, n_tiles,
+                                                                          offsets);
+        return check_launch("tile_ranges");
     }
     tile_ranges_kernel<<<ceil_div(m, 256), 256, 0, stream>>>(tile_ids, keys64, m, n_tiles,
                                                              offsets);
