@@ -34,6 +34,7 @@ struct PrepareScratch {
     uint32_t* dkeys_alt;
     uint32_t* dvals_alt;
     uint32_t* offsets;
+    uint4* recs;  // per Gaussian: the count walk's pass mask and rectangle
     void* sort;
     size_t sort_bytes;
     void* scan;
@@ -50,6 +51,8 @@ PrepareScratch carve_prepare(const void* base, int64_t n) {
     s.dkeys_alt = reinterpret_cast<uint32_t*>(p); p += arr;
     s.dvals_alt = reinterpret_cast<uint32_t*>(p); p += arr;
     s.offsets = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.recs = reinterpret_cast<uint4*>(p);
+    p += align256(sizeof(uint4) * (size_t)std::max<int64_t>(n, 1));
     s.sort_bytes = align256(radix_sort_scratch_bytes(n, 32, 4));
     s.sort = p; p += s.sort_bytes;
     s.scan = p; p += align256(scan_scratch_bytes(n));
@@ -236,7 +239,7 @@ extern "C" mg_status mg_bin_prepare(const float* uv, const float* rxy, const flo
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
     MG_TRY(launch_bin_count_depth(uv, rxy, conic, opacity, valid, depth, n, width, height, tile,
-                                  tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, st));
+                                  tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, s.recs, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, n, 32, s.sort,
                                       s.sort_bytes, &in_alt, st));
@@ -270,7 +273,7 @@ extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float*
     const PrepareScratch p = carve_prepare(prepare_scratch, n);
     uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
     MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m, width,
-                           height, tile, tiles_x, tiles_y, e.pair_tiles, ids, st));
+                           height, tile, tiles_x, tiles_y, p.recs, e.pair_tiles, ids, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m,
                                       tile_bits(n_tiles), e.sort, e.sort_bytes, &in_alt, st));

@@ -27,12 +27,13 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
                                  const float* opacity, const int32_t* valid,
                                  const float* depth, int64_t n, int W, int H, int tile,
                                  int tiles_x, int tiles_y, uint32_t* counts,
-                                 uint32_t* dkeys, uint32_t* dvals, cudaStream_t stream);
+                                 uint32_t* dkeys, uint32_t* dvals, uint4* recs,
+                                 cudaStream_t stream);
 mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const float* opacity, const uint32_t* sorted_gid,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
-                          uint32_t* pair_tiles, uint32_t* pair_ids,
+                          const uint4* recs, uint32_t* pair_tiles, uint32_t* pair_ids,
                           cudaStream_t stream);
 
 // sort.cu

@@ -119,16 +119,24 @@ preprocess_forward_kernel(const float* __restrict__ means,
 
 // Walk the Gaussian's clamped tile rectangle row-major and count (or emit)
 // the tiles that pass the exact ellipse test (binning.metal:46-90).
+// With `rec` given (count walks), the walk also leaves a record of its
+// decisions: rectangles of at most 64 tiles get the pass mask over the
+// rectangle in row-major order plus the rectangle itself, so the emission
+// can expand the mask instead of testing every tile again.
 template <bool kEmit64, bool kEmitPair>
 __device__ __forceinline__ uint32_t bin_walk(
     float mux, float muy, float rx, float ry, float ca, float cb, float cc,
     float op, uint32_t dbits, int tile, int tiles_x, int tiles_y, int W, int H,
     uint64_t* keys, int32_t* ids, uint32_t* pair_tiles, uint32_t* pair_ids,
-    int64_t write_at, uint32_t cap, int32_t gid) {
+    int64_t write_at, uint32_t cap, int32_t gid, uint4* rec = nullptr) {
     const TileRect tr = tile_rect(mux, muy, rx, ry, tile, tiles_x, tiles_y);
     const float oa = 255.0f * op;
     if (oa <= 1.0f) return 0u;
     const float thr = 2.0f * log_f32_via_f64(oa);
+    const int rw = tr.x1 - tr.x0 + 1, rh = tr.y1 - tr.y0 + 1;
+    const bool masked = rec != nullptr && rw * rh <= 64;
+    uint64_t mask = 0ull;
+    int bit = 0;
     uint32_t cnt = 0u;
     for (int ty = tr.y0; ty <= tr.y1; ++ty) {
         const float y0 = (float)(ty * tile);
@@ -136,7 +144,9 @@ __device__ __forceinline__ uint32_t bin_walk(
         for (int tx = tr.x0; tx <= tr.x1; ++tx) {
             const float x0 = (float)(tx * tile);
             const float x1 = fminf((float)((tx + 1) * tile), (float)W);
+            const int b = bit++;
             if (min_q_over_rect(mux, muy, ca, cb, cc, x0, x1, y0, y1) >= thr) continue;
+            if (masked) mask |= 1ull << b;
             if (kEmit64 || kEmitPair) {
                 if (cnt < cap) {
                     const uint32_t tid = (uint32_t)(ty * tiles_x + tx);
@@ -152,6 +162,10 @@ __device__ __forceinline__ uint32_t bin_walk(
             ++cnt;
         }
     }
+    if (rec)  // width 0 marks a rectangle the emission must walk again
+        *rec = make_uint4((uint32_t)mask, (uint32_t)(mask >> 32),
+                          (uint32_t)tr.x0 | ((uint32_t)tr.y0 << 16),
+                          masked ? ((uint32_t)rw | ((uint32_t)rh << 16)) : 0u);
     return cnt;
 }
 
@@ -210,7 +224,8 @@ __global__ void bin_count_depth_kernel(const float2* __restrict__ uv,
                                        int W, int H, int tile, int tiles_x,
                                        int tiles_y, uint32_t* __restrict__ counts,
                                        uint32_t* __restrict__ dkeys,
-                                       uint32_t* __restrict__ dvals) {
+                                       uint32_t* __restrict__ dvals,
+                                       uint4* __restrict__ recs) {
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n) return;
     uint32_t c = 0u;
@@ -219,7 +234,7 @@ __global__ void bin_count_depth_kernel(const float2* __restrict__ uv,
         c = bin_walk<false, false>(mu.x, mu.y, r.x, r.y, conic[3 * g], conic[3 * g + 1],
                                    conic[3 * g + 2], opacity[g], 0u, tile, tiles_x,
                                    tiles_y, W, H, nullptr, nullptr, nullptr, nullptr,
-                                   0, 0u, 0);
+                                   0, 0u, 0, recs + g);
     }
     counts[g] = c;
     dkeys[g] = c > 0u ? __float_as_uint(depth[g]) : 0xffffffffu;
@@ -237,7 +252,8 @@ __global__ void bin_emit_kernel(const float2* __restrict__ uv,
                                 const uint32_t* __restrict__ counts,
                                 const uint32_t* __restrict__ offsets, int64_t n,
                                 int64_t m, int W, int H, int tile, int tiles_x,
-                                int tiles_y, uint32_t* __restrict__ pair_tiles,
+                                int tiles_y, const uint4* __restrict__ recs,
+                                uint32_t* __restrict__ pair_tiles,
                                 uint32_t* __restrict__ pair_ids) {
     const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
@@ -246,6 +262,30 @@ __global__ void bin_emit_kernel(const float2* __restrict__ uv,
     if (cnt == 0u) return;
     const int64_t at = offsets[s];
     if (at + cnt > m) return;
+    const uint4 rec = recs[g];
+    const uint32_t rw = rec.w & 0xffffu, rh = rec.w >> 16;
+    if (rw != 0u) {
+        // the count walk's decisions: row-major bits over the rectangle
+        uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
+        const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
+        const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
+        uint32_t k = 0u;
+        for (uint32_t r = 0; r < rh && mask; ++r) {
+            uint64_t row = mask & row_bits;
+            mask >>= rw;
+            const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
+            while (row) {
+                const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
+                row &= row - 1ull;
+                if (k < cnt) {
+                    pair_tiles[at + k] = trow + b;
+                    pair_ids[at + k] = g;
+                }
+                ++k;
+            }
+        }
+        return;
+    }
     const float2 mu = uv[g], r = rxy[g];
     bin_walk<false, true>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
                           conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
@@ -299,11 +339,12 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
                                  const float* opacity, const int32_t* valid,
                                  const float* depth, int64_t n, int W, int H, int tile,
                                  int tiles_x, int tiles_y, uint32_t* counts,
-                                 uint32_t* dkeys, uint32_t* dvals, cudaStream_t stream) {
+                                 uint32_t* dkeys, uint32_t* dvals, uint4* recs,
+                                 cudaStream_t stream) {
     if (n == 0) return MG_OK;
     bin_count_depth_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
-        opacity, valid, depth, n, W, H, tile, tiles_x, tiles_y, counts, dkeys, dvals);
+        opacity, valid, depth, n, W, H, tile, tiles_x, tiles_y, counts, dkeys, dvals, recs);
     return check_launch("bin_count_depth");
 }
 
@@ -311,13 +352,13 @@ mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const float* opacity, const uint32_t* sorted_gid,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
-                          uint32_t* pair_tiles, uint32_t* pair_ids,
+                          const uint4* recs, uint32_t* pair_tiles, uint32_t* pair_ids,
                           cudaStream_t stream) {
     if (n == 0 || m == 0) return MG_OK;
     bin_emit_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
         opacity, sorted_gid, counts, offsets, n, m, W, H, tile, tiles_x, tiles_y,
-        pair_tiles, pair_ids);
+        recs, pair_tiles, pair_ids);
     return check_launch("bin_emit");
 }
 

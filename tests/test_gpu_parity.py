@@ -194,6 +194,31 @@ def test_binning_end_to_end_bit_exact_at_scale(cuda):
     assert np.array_equal(N(off), r_off)
 
 
+@pytest.mark.parametrize("tile", [8, 16])
+def test_binning_mixes_recorded_and_rewalked_rectangles(cuda, tile):
+    """The emission expands the count walk's recorded decisions for tile
+    rectangles of at most 64 tiles and walks larger ones again; a scene with
+    both, against the oracle."""
+    W, H = 400, 300
+    means, quats, scales, opac, _, K = random_scene(20_000, 5, W, H)
+    g = np.random.default_rng(6)
+    big = g.random(scales.shape[0]) < 0.05
+    scales[big] *= 8.0
+    vm = np.eye(4, dtype=np.float32)
+    cam = oracle.camera(vm, K, W, H)
+    ref = oracle.preprocess_forward(means, quats, scales, None, None, opac, cam, -1)
+    r_ids, r_off, _ = oracle.build_tile_lists(ref["uv"], ref["rxy"], ref["conic"], opac,
+                                              ref["valid"], ref["depth"], W, H, tile)
+    side = (2 * ref["rxy"] / tile + 1)[ref["valid"] != 0]
+    span = side[:, 0] * side[:, 1]
+    assert (span > 100).sum() > 50 and (span < 30).sum() > 1000  # both kinds present
+    o = ext.preprocess_forward(T(means), T(quats), T(scales), None, None, T(opac),
+                               *cam_args(K, vm, W, H), -1)
+    ids, off, _ = ext.bin_and_sort(o[0], o[3], o[1], T(opac), o[4], o[2], W, H, tile)
+    assert np.array_equal(N(ids), r_ids)
+    assert np.array_equal(N(off), r_off)
+
+
 def test_binning_of_an_empty_and_an_invisible_scene(cuda):
     W, H = 64, 64
     ids, off, tx = ext.bin_and_sort(*(torch.zeros(0, k, device="cuda") for k in (2, 2, 3)),
