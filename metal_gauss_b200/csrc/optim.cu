@@ -73,7 +73,11 @@ struct AdamSegments {
 
 // One launch over every segment (blockIdx.y). Selective mode (vis != null)
 // follows selective_adam_kernel's arithmetic with the shared per-row step
-// count; dense mode follows adam_kernel's.
+// count; dense mode follows adam_kernel's. Each thread updates four
+// consecutive elements (16-byte accesses when they are aligned); their rows
+// are tracked incrementally, and a row's bias correction is computed once
+// per thread however many of its elements the thread holds (sh_rest rows
+// have 45), instead of once per element.
 __global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict__ g,
                                   float* __restrict__ m, float* __restrict__ v, int64_t rows,
                                   AdamSegments segs, float b1, float b2, float eps, float w1,
@@ -84,31 +88,91 @@ __global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict
     const int width = segs.width[s];
     const float lr = segs.lr[s];
     const int64_t count = segs.count[s];
-    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count;
-         k += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e = first + k;  // element within the segment
-        const int64_t i = off + e;
-        const float gi = g[i];
-        if (vis != nullptr) {
-            const int64_t r = e / width;
-            if (!(vis[r] > 0.0f)) continue;
-            const float k = __fadd_rn(steps[r], 1.0f);
-            const float c1 = __fsub_rn(1.0f, powf(b1, k));
-            const float c2 = __fsub_rn(1.0f, powf(b2, k));
-            const float step_size = __fmul_rn(lr, __fdiv_rn(__fsqrt_rn(c2), c1));
-            const float mi = __fadd_rn(__fmul_rn(m[i], b1), __fmul_rn(gi, w1));
-            const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(gi, gi), w2));
-            m[i] = mi;
-            v[i] = vi;
-            p[i] = __fsub_rn(p[i], __fdiv_rn(__fmul_rn(step_size, mi), __fadd_rn(__fsqrt_rn(vi), eps)));
+    for (int64_t k0 = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); k0 < count;
+         k0 += 4 * (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e0 = first + k0;  // element within the segment
+        const int64_t i0 = off + e0;
+        const int nk = (int)min((int64_t)4, count - k0);
+        const bool vec = nk == 4 && (i0 & 3) == 0;
+        float gv[4], mv[4], vv[4], pv[4];
+        if (vec) {
+            const float4 a = *reinterpret_cast<const float4*>(g + i0);
+            const float4 b = *reinterpret_cast<const float4*>(m + i0);
+            const float4 c = *reinterpret_cast<const float4*>(v + i0);
+            const float4 d = *reinterpret_cast<const float4*>(p + i0);
+            gv[0] = a.x; gv[1] = a.y; gv[2] = a.z; gv[3] = a.w;
+            mv[0] = b.x; mv[1] = b.y; mv[2] = b.z; mv[3] = b.w;
+            vv[0] = c.x; vv[1] = c.y; vv[2] = c.z; vv[3] = c.w;
+            pv[0] = d.x; pv[1] = d.y; pv[2] = d.z; pv[3] = d.w;
         } else {
-            float mi = m[i];
-            mi = __fadd_rn(mi, __fmul_rn(1.0f - b1, __fsub_rn(gi, mi)));
-            const float vi = __fadd_rn(__fmul_rn(v[i], b2), __fmul_rn(__fmul_rn(1.0f - b2, gi), gi));
-            m[i] = mi;
-            v[i] = vi;
-            const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), sqrt_bc2), eps);
-            p[i] = __fadd_rn(p[i], __fdiv_rn(__fmul_rn(-(lr / bc1), mi), denom));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bool in = j < nk;
+                gv[j] = in ? g[i0 + j] : 0.f;
+                mv[j] = in ? m[i0 + j] : 0.f;
+                vv[j] = in ? v[i0 + j] : 0.f;
+                pv[j] = in ? p[i0 + j] : 0.f;
+            }
+        }
+        if (vis != nullptr) {
+            int64_t r = e0 / width;
+            int c = (int)(e0 - r * width);
+            int64_t r_done = -1;
+            bool live = false;
+            float step_size = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j < nk) {
+                    if (r != r_done) {
+                        r_done = r;
+                        live = vis[r] > 0.0f;
+                        if (live) {
+                            const float k = __fadd_rn(steps[r], 1.0f);
+                            const float c1 = __fsub_rn(1.0f, powf(b1, k));
+                            const float c2 = __fsub_rn(1.0f, powf(b2, k));
+                            step_size = __fmul_rn(lr, __fdiv_rn(__fsqrt_rn(c2), c1));
+                        }
+                    }
+                    if (live) {
+                        const float gi = gv[j];
+                        const float mi = __fadd_rn(__fmul_rn(mv[j], b1), __fmul_rn(gi, w1));
+                        const float vi =
+                            __fadd_rn(__fmul_rn(vv[j], b2), __fmul_rn(__fmul_rn(gi, gi), w2));
+                        mv[j] = mi;
+                        vv[j] = vi;
+                        pv[j] = __fsub_rn(pv[j], __fdiv_rn(__fmul_rn(step_size, mi),
+                                                           __fadd_rn(__fsqrt_rn(vi), eps)));
+                    }
+                    if (++c == width) { c = 0; ++r; }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float gi = gv[j];
+                float mi = mv[j];
+                mi = __fadd_rn(mi, __fmul_rn(1.0f - b1, __fsub_rn(gi, mi)));
+                const float vi =
+                    __fadd_rn(__fmul_rn(vv[j], b2), __fmul_rn(__fmul_rn(1.0f - b2, gi), gi));
+                mv[j] = mi;
+                vv[j] = vi;
+                const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vi), sqrt_bc2), eps);
+                pv[j] = __fadd_rn(pv[j], __fdiv_rn(__fmul_rn(-(lr / bc1), mi), denom));
+            }
+        }
+        if (vec) {
+            *reinterpret_cast<float4*>(m + i0) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+            *reinterpret_cast<float4*>(v + i0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            *reinterpret_cast<float4*>(p + i0) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (j < nk) {
+                    m[i0 + j] = mv[j];
+                    v[i0 + j] = vv[j];
+                    p[i0 + j] = pv[j];
+                }
+            }
         }
     }
 }
@@ -199,7 +263,7 @@ extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
     const double sq = visible_count ? 1.0 : std::sqrt(1.0 - std::pow((double)b2, (double)step));
     const float w1 = (float)(1.0 - (double)b1), w2 = (float)(1.0 - (double)b2);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int gx = (int)std::min<int64_t>((max_count + 255) / 256, 148 * 8);
+    const int gx = (int)std::min<int64_t>((max_count + 1023) / 1024, 148 * 8);
     if (n_segments > 0) {
         adam_multi_kernel<<<dim3(std::max(gx, 1), n_segments), 256, 0, st>>>(
             p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, (float)bc1,
