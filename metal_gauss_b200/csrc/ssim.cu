@@ -112,8 +112,9 @@ __global__ void ssim_chain_backward_kernel(const float* __restrict__ x, const fl
 
 // ------------------------------------------------------- fused training loss
 //
-// Tiles of kLW x kLH outputs per 256-thread block (32 x 8 threads); one colour
-// channel at a time. The block stages its inputs with the 5-pixel halo, then
+// Tiles of kLW x kLH outputs per 256-thread block (32 x 8 threads), one colour
+// channel per block (blockIdx.z). The block stages its inputs with the 5-pixel
+// halo, then
 //  * horizontal pass: each thread produces 4 adjacent columns of one staged
 //    row from 14 inputs held in registers (16-byte shared loads; products
 //    such as x*x formed once per input, not once per tap);
@@ -171,7 +172,8 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
 #pragma unroll
     for (int k = 0; k < 11; ++k) wk[k] = win[k];
     float sum_s = 0.f, sum_l1 = 0.f;
-    for (int c = 0; c < 3; ++c) {
+    {
+        const int c = blockIdx.z;  // one colour channel per block
         stage_channel(x, c, W, H, ox, oy, s_x);
         stage_channel(y, c, W, H, ox, oy, s_y);
         __syncthreads();
@@ -241,7 +243,7 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
             sum_s += S;
             sum_l1 += fabsf(s_x[ly + kR][tx + kR] - s_y[ly + kR][tx + kR]);
         }
-        __syncthreads();  // the next channel restages s_x, s_y, s_h
+        __syncthreads();  // s_x, s_y hold the L1 term's inputs until here
     }
     for (int o = 16; o > 0; o >>= 1) {
         sum_s += __shfl_xor_sync(0xffffffffu, sum_s, o);
@@ -252,7 +254,8 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
     if (tid == 0) {
         float a = 0.f, b = 0.f;
         for (int i = 0; i < 8; ++i) { a += s_red[0][i]; b += s_red[1][i]; }
-        const int64_t blk = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+        const int64_t blk =
+            ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
         partial[2 * blk + 0] = a;
         partial[2 * blk + 1] = b;
     }
@@ -271,7 +274,8 @@ loss_grad_kernel(const float* __restrict__ x, const float* __restrict__ y,
     float wk[11];
 #pragma unroll
     for (int k = 0; k < 11; ++k) wk[k] = win[k];
-    for (int c = 0; c < 3; ++c) {
+    {
+        const int c = blockIdx.z;  // one colour channel per block
         for (int ly = ty; ly < kSH; ly += 8) {
             const int gy = oy + ly - kR;
             for (int lx = tx; lx < kSP; lx += 32) {
@@ -422,12 +426,12 @@ extern "C" mg_status mg_ssim_chain_backward(const float* x, const float* y,
     return check_launch("ssim_chain_backward");
 }
 
-static dim3 loss_grid(int W, int H) { return dim3((W + kLW - 1) / kLW, (H + kLH - 1) / kLH, 1); }
+static dim3 loss_grid(int W, int H) { return dim3((W + kLW - 1) / kLW, (H + kLH - 1) / kLH, 3); }
 
 extern "C" size_t mg_l1_ssim_scratch_bytes(int32_t height, int32_t width) {
     const dim3 g = loss_grid(width, height);
     const size_t adj = sizeof(float) * 9 * (size_t)height * width;
-    const size_t part = sizeof(float) * 2 * (size_t)g.x * g.y;
+    const size_t part = sizeof(float) * 2 * (size_t)g.x * g.y * g.z;
     return ((adj + 255) & ~(size_t)255) + ((part + 255) & ~(size_t)255);
 }
 
@@ -453,7 +457,7 @@ extern "C" mg_status mg_l1_ssim_loss(const float* x, const float* y, const float
     loss_grad_kernel<<<g, dim3(32, 8), 0, s>>>(x, y, adj, w, width, height,
                                                   scale * w_l1 * inv_n, grad_x);
     MG_TRY(check_launch("l1_ssim_loss grad"));
-    loss_finish_kernel<<<1, 256, 0, s>>>(partial, (int)(g.x * g.y), w_l1, w_ssim, scale,
+    loss_finish_kernel<<<1, 256, 0, s>>>(partial, (int)(g.x * g.y * g.z), w_l1, w_ssim, scale,
                                          inv_n, loss_dev);
     return check_launch("l1_ssim_loss finish");
 }
