@@ -240,18 +240,27 @@ mg_status mg_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64,
  *     and extracts the per-tile ranges.
  * The result equals a stable sort on (tile_id << 32 | depth_bits) keys
  * emitted in Gaussian order: within a tile, front to back, equal depths by
- * Gaussian index. Scratch sizes come from the two queries. */
-size_t mg_bin_prepare_scratch_bytes(int64_t n);
+ * Gaussian index. Scratch sizes come from the two queries.
+ *
+ * saturation_cut = 1 (both calls, the same value) drops, per tile, the pairs
+ * behind the depth at which Gaussians covering the whole tile have provably
+ * driven every pixel's transmittance below the rasteriser's 1e-4 stop
+ * (a lower bound of their alpha over the tile's pixel centres, summed as
+ * optical depth over 64 log-spaced depth bins, with a margin). The lists are
+ * then a front-to-back prefix of the full ones: rasterisation results are
+ * unchanged, but the lists no longer equal the reference's. 0 gives the
+ * reference's lists. */
+size_t mg_bin_prepare_scratch_bytes(int64_t n, int32_t n_tiles);
 mg_status mg_bin_prepare(
     const float* uv, const float* rxy, const float* conic,
     const float* opacity, const int32_t* valid, const float* depth, int64_t n,
-    int32_t width, int32_t height, int32_t tile, int64_t* total_dev,
-    void* scratch, size_t scratch_bytes, mg_stream_t stream);
+    int32_t width, int32_t height, int32_t tile, int32_t saturation_cut,
+    int64_t* total_dev, void* scratch, size_t scratch_bytes, mg_stream_t stream);
 size_t mg_bin_emit_scratch_bytes(int64_t n, int64_t m, int32_t n_tiles);
 mg_status mg_bin_emit(
     const float* uv, const float* rxy, const float* conic,
     const float* opacity, int64_t n, int64_t m,
-    int32_t width, int32_t height, int32_t tile,
+    int32_t width, int32_t height, int32_t tile, int32_t saturation_cut,
     const void* prepare_scratch, int32_t* gauss_ids, int32_t* tile_offsets,
     void* scratch, size_t scratch_bytes, mg_stream_t stream);
 

@@ -67,10 +67,11 @@ SIGNATURES = {
     "mg_sort_pairs_u64": (i32, [vp, vp, vp, vp, i64, i32, vp, sz, vp]),
     "mg_sort_pairs_u32_noalloc": (i32, [vp, vp, i64, i32, vp]),
     "mg_tile_ranges": (i32, [vp, vp, i64, i32, vp, vp]),
-    "mg_bin_prepare_scratch_bytes": (sz, [i64]),
-    "mg_bin_prepare": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp, sz, vp]),
+    "mg_bin_prepare_scratch_bytes": (sz, [i64, i32]),
+    "mg_bin_prepare": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, vp, vp, sz, vp]),
     "mg_bin_emit_scratch_bytes": (sz, [i64, i64, i32]),
-    "mg_bin_emit": (i32, [vp, vp, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
+    "mg_bin_emit": (i32, [vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp, vp, sz,
+                          vp]),
     "mg_pack_splats": (i32, [vp, vp, vp, vp, i64, vp, vp]),
     "mg_raster_scratch_bytes": (sz, [i32, i32, i32, i64]),
     "mg_rasterize_forward": (i32, [vp, vp, vp, i64, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,

@@ -35,13 +35,17 @@ struct PrepareScratch {
     uint32_t* dvals_alt;
     uint32_t* offsets;
     uint4* recs;  // per Gaussian: the count walk's pass mask and rectangle
+    uint32_t* cut_range;  // saturation cut: depth range words, then the histogram
+    uint32_t* cut_hist;
+    int32_t* cutoff;
+    size_t cut_zero_bytes;  // range words + histogram, zeroed per call
     void* sort;
     size_t sort_bytes;
     void* scan;
     size_t total;
 };
 
-PrepareScratch carve_prepare(const void* base, int64_t n) {
+PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles) {
     PrepareScratch s;
     char* p = const_cast<char*>(static_cast<const char*>(base));
     const size_t arr = align256(sizeof(uint32_t) * (size_t)std::max<int64_t>(n, 1));
@@ -53,6 +57,12 @@ PrepareScratch carve_prepare(const void* base, int64_t n) {
     s.offsets = reinterpret_cast<uint32_t*>(p); p += arr;
     s.recs = reinterpret_cast<uint4*>(p);
     p += align256(sizeof(uint4) * (size_t)std::max<int64_t>(n, 1));
+    s.cut_range = reinterpret_cast<uint32_t*>(p);
+    s.cut_hist = s.cut_range + 64;  // keeps the histogram 256-byte aligned
+    s.cut_zero_bytes = sizeof(uint32_t) * (64 + (size_t)std::max(n_tiles, 1) * kSaturationBins);
+    p += align256(s.cut_zero_bytes);
+    s.cutoff = reinterpret_cast<int32_t*>(p);
+    p += align256(sizeof(int32_t) * (size_t)std::max(n_tiles, 1));
     s.sort_bytes = align256(radix_sort_scratch_bytes(n, 32, 4));
     s.sort = p; p += s.sort_bytes;
     s.scan = p; p += align256(scan_scratch_bytes(n));
@@ -224,22 +234,31 @@ extern "C" mg_status mg_tile_ranges(const uint32_t* tile_ids, const uint64_t* ke
                               reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" size_t mg_bin_prepare_scratch_bytes(int64_t n) { return carve_prepare(nullptr, n).total; }
+extern "C" size_t mg_bin_prepare_scratch_bytes(int64_t n, int32_t n_tiles) {
+    if (n < 0 || n_tiles <= 0) return 0;
+    return carve_prepare(nullptr, n, n_tiles).total;
+}
 
 extern "C" mg_status mg_bin_prepare(const float* uv, const float* rxy, const float* conic,
                                     const float* opacity, const int32_t* valid,
                                     const float* depth, int64_t n, int32_t width, int32_t height,
-                                    int32_t tile, int64_t* total_dev, void* scratch,
-                                    size_t scratch_bytes, mg_stream_t stream) {
+                                    int32_t tile, int32_t saturation_cut, int64_t* total_dev,
+                                    void* scratch, size_t scratch_bytes, mg_stream_t stream) {
     MG_REQUIRE(tile > 0 && width > 0 && height > 0, "bin_prepare: bad tiling");
     MG_REQUIRE(total_dev != nullptr, "bin_prepare: null total");
     MG_REQUIRE(n < (int64_t)1 << 30, "bin_prepare: more than 2^30 Gaussians");
-    const PrepareScratch s = carve_prepare(scratch, n);
+    const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
+    const PrepareScratch s = carve_prepare(scratch, n, tiles_x * tiles_y);
     MG_REQUIRE(scratch != nullptr && scratch_bytes >= s.total, "bin_prepare: scratch too small");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
+    if (saturation_cut &&
+        cudaMemsetAsync(s.cut_range, 0, s.cut_zero_bytes, st) != cudaSuccess)
+        return check_launch("bin_prepare cut memset");
     MG_TRY(launch_bin_count_depth(uv, rxy, conic, opacity, valid, depth, n, width, height, tile,
-                                  tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, s.recs, st));
+                                  tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, s.recs,
+                                  saturation_cut ? s.cut_range : nullptr,
+                                  saturation_cut ? s.cut_hist : nullptr,
+                                  saturation_cut ? s.cutoff : nullptr, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, n, 32, s.sort,
                                       s.sort_bytes, &in_alt, st));
@@ -257,9 +276,10 @@ extern "C" size_t mg_bin_emit_scratch_bytes(int64_t n, int64_t m, int32_t n_tile
 
 extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float* conic,
                                  const float* opacity, int64_t n, int64_t m, int32_t width,
-                                 int32_t height, int32_t tile, const void* prepare_scratch,
-                                 int32_t* gauss_ids, int32_t* tile_offsets, void* scratch,
-                                 size_t scratch_bytes, mg_stream_t stream) {
+                                 int32_t height, int32_t tile, int32_t saturation_cut,
+                                 const void* prepare_scratch, int32_t* gauss_ids,
+                                 int32_t* tile_offsets, void* scratch, size_t scratch_bytes,
+                                 mg_stream_t stream) {
     MG_REQUIRE(tile > 0 && width > 0 && height > 0, "bin_emit: bad tiling");
     MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 31), "bin_emit: pair count exceeds 2^31");
     MG_REQUIRE(prepare_scratch != nullptr && tile_offsets != nullptr, "bin_emit: null pointer");
@@ -270,10 +290,11 @@ extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float*
     MG_REQUIRE(gauss_ids != nullptr, "bin_emit: null gauss_ids");
     const EmitScratch e = carve_emit(scratch, m, n_tiles);
     MG_REQUIRE(scratch != nullptr && scratch_bytes >= e.total, "bin_emit: scratch too small");
-    const PrepareScratch p = carve_prepare(prepare_scratch, n);
+    const PrepareScratch p = carve_prepare(prepare_scratch, n, n_tiles);
     uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
     MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m, width,
-                           height, tile, tiles_x, tiles_y, p.recs, e.pair_tiles, ids, st));
+                           height, tile, tiles_x, tiles_y, p.recs,
+                           saturation_cut ? p.cutoff : nullptr, e.pair_tiles, ids, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m,
                                       tile_bits(n_tiles), e.sort, e.sort_bytes, &in_alt, st));

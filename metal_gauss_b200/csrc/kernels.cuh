@@ -28,13 +28,17 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
                                  const float* depth, int64_t n, int W, int H, int tile,
                                  int tiles_x, int tiles_y, uint32_t* counts,
                                  uint32_t* dkeys, uint32_t* dvals, uint4* recs,
+                                 uint32_t* cut_range, uint32_t* cut_hist, int32_t* cutoff,
                                  cudaStream_t stream);
+// Saturation-cut histogram bins per tile (cut_hist holds n_tiles of them;
+// cut_range two zeroed words before the call; see preprocess_fwd.cu).
+constexpr int kSaturationBins = 64;
 mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const float* opacity, const uint32_t* sorted_gid,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
-                          const uint4* recs, uint32_t* pair_tiles, uint32_t* pair_ids,
-                          cudaStream_t stream);
+                          const uint4* recs, const int32_t* cutoff, uint32_t* pair_tiles,
+                          uint32_t* pair_ids, cudaStream_t stream);
 
 // sort.cu
 // Sorts in place between (keys, vals) and (keys_alt, vals_alt); returns in

@@ -7,6 +7,8 @@
 // 128-byte segments. SH rows are 48 B (fused) or 12 B + 180 B (split): a warp
 // stages its 32 Gaussians' coefficient block through shared memory with
 // coalesced loads and each thread then reads its own row from there.
+#include <algorithm>
+
 #include "exact_math.cuh"
 #include "kernels.cuh"
 
@@ -119,22 +121,90 @@ preprocess_forward_kernel(const float* __restrict__ means,
 
 // Walk the Gaussian's clamped tile rectangle row-major and count (or emit)
 // the tiles that pass the exact ellipse test (binning.metal:46-90).
+// Saturation cut (engine binning). A tile's pairs behind the depth at which
+// Gaussians that cover the whole tile have certainly driven every pixel's
+// transmittance below the rasteriser's 1e-4 stop are never read by either
+// pass, so they need not be emitted or sorted. Per tile, a histogram over
+// kCutBins log-spaced depth bins accumulates each covering Gaussian's optical
+// depth -ln(1 - alpha_lb), alpha_lb being a lower bound of its alpha at every
+// pixel centre of the tile; the cutoff bin is the first where the running sum
+// reaches ln(1e4) + 1 (T <= 3.7e-5 with a margin for float rounding), and
+// pairs in later bins are dropped. Kept pairs are a depth-order prefix of
+// each tile's list, so images and gradients are unchanged.
+constexpr int kCutBins = kSaturationBins;
+constexpr float kCutOdScale = 1048576.0f;  // optical depth quantum 2^-20
+constexpr uint32_t kCutNeed = 10707140u;   // (ln(1e4) + 1) * 2^20, rounded up
+
+struct CutArgs {
+    uint32_t* hist;          // count walks: n_tiles * kCutBins optical depths
+    const int32_t* cutoff;   // filtering walks: per-tile last kept bin
+    int bin;                 // this Gaussian's depth bin
+};
+
+// Depth bin of a Gaussian: log-spaced over the view's depth range, given as
+// the bit patterns of the smallest and largest visible depth.
+__device__ __forceinline__ int cut_bin(float depth, uint32_t dmin_bits, uint32_t dmax_bits) {
+    const float lo = __logf(__uint_as_float(dmin_bits));
+    const float hi = __logf(__uint_as_float(dmax_bits));
+    const float inv = (float)kCutBins / fmaxf(hi - lo, 1e-6f);
+    const int b = (int)((__logf(depth) - lo) * inv);
+    return min(max(b, 0), kCutBins - 1);
+}
+
+// Quantised lower bound of the optical depth -ln(1 - alpha) that a Gaussian
+// adds at every pixel centre [x0+.5, x1-.5] x [y0+.5, y1-.5] of a tile, or 0
+// when it may fall under 1/255 somewhere (then some pixel can skip it). The
+// conic's quadratic form is convex, so it is largest at a corner; a corner
+// at or past the 1/255 threshold `thr` (the pass test's) ends the search.
+// The bound only decides how much of a list is kept, never a blend: fast
+// exp/log with a 1e-3 margin on alpha and another on the optical depth.
+__device__ __forceinline__ uint32_t tile_optical_depth(float mux, float muy, float ca,
+                                                       float cb, float cc, float op, float thr,
+                                                       float x0, float x1, float y0,
+                                                       float y1) {
+    float qmax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float dx = ((e & 1) ? x1 - 0.5f : x0 + 0.5f) - mux;
+        const float dy = ((e & 2) ? y1 - 0.5f : y0 + 0.5f) - muy;
+        const float q = __fmaf_rn(ca * dx, dx, __fmaf_rn(2.0f * cb * dx, dy, cc * dy * dy));
+        if (q >= thr) return 0u;
+        qmax = fmaxf(qmax, q);
+    }
+    const float alb = fminf(op * __expf(-0.5f * qmax) * 0.999f, 0.999f);
+    if (alb < 1.0f / 255.0f) return 0u;
+    return (uint32_t)(-__logf(1.0f - alb) * (0.999f * kCutOdScale));
+}
+
 // With `rec` given (count walks), the walk also leaves a record of its
 // decisions: rectangles of at most 64 tiles get the pass mask over the
-// rectangle in row-major order plus the rectangle itself, so the emission
-// can expand the mask instead of testing every tile again.
-template <bool kEmit64, bool kEmitPair>
+// rectangle in row-major order plus the rectangle itself (and the Gaussian's
+// depth bin), so the emission can expand the mask instead of testing every
+// tile again. kCut: 1 adds covering Gaussians to the saturation histogram,
+// 2 keeps only tiles whose cutoff bin is not before the Gaussian's bin.
+template <bool kEmit64, bool kEmitPair, int kCut = 0>
 __device__ __forceinline__ uint32_t bin_walk(
     float mux, float muy, float rx, float ry, float ca, float cb, float cc,
     float op, uint32_t dbits, int tile, int tiles_x, int tiles_y, int W, int H,
     uint64_t* keys, int32_t* ids, uint32_t* pair_tiles, uint32_t* pair_ids,
-    int64_t write_at, uint32_t cap, int32_t gid, uint4* rec = nullptr) {
+    int64_t write_at, uint32_t cap, int32_t gid, uint4* rec = nullptr,
+    CutArgs cut = CutArgs{nullptr, nullptr, 0}) {
     const TileRect tr = tile_rect(mux, muy, rx, ry, tile, tiles_x, tiles_y);
     const float oa = 255.0f * op;
     if (oa <= 1.0f) return 0u;
     const float thr = 2.0f * log_f32_via_f64(oa);
     const int rw = tr.x1 - tr.x0 + 1, rh = tr.y1 - tr.y0 + 1;
     const bool masked = rec != nullptr && rw * rh <= 64;
+    // a tile fits in the 1/255 ellipse {q < thr} only if its inscribed circle
+    // does: the ellipse's smaller semi-axis sqrt(thr / lambda_max(conic))
+    // must reach half the side, lambda_max <= 4 thr / (tile - 1)^2
+    bool can_cover = false;
+    if (kCut == 1) {
+        const float half_tr = 0.5f * (ca + cc);
+        const float lmax = half_tr + sqrtf(fmaxf(half_tr * half_tr - (ca * cc - cb * cb), 0.0f));
+        const float side = (float)(tile - 1);
+        can_cover = lmax * side * side <= 4.0f * thr * 1.001f;
+    }
     uint64_t mask = 0ull;
     int bit = 0;
     uint32_t cnt = 0u;
@@ -147,6 +217,12 @@ __device__ __forceinline__ uint32_t bin_walk(
             const int b = bit++;
             if (min_q_over_rect(mux, muy, ca, cb, cc, x0, x1, y0, y1) >= thr) continue;
             if (masked) mask |= 1ull << b;
+            if (kCut == 1 && can_cover) {
+                const uint32_t q =
+                    tile_optical_depth(mux, muy, ca, cb, cc, op, thr, x0, x1, y0, y1);
+                if (q) atomicAdd(&cut.hist[(ty * tiles_x + tx) * kCutBins + cut.bin], q);
+            }
+            if (kCut == 2 && cut.cutoff[ty * tiles_x + tx] < cut.bin) continue;
             if (kEmit64 || kEmitPair) {
                 if (cnt < cap) {
                     const uint32_t tid = (uint32_t)(ty * tiles_x + tx);
@@ -165,7 +241,8 @@ __device__ __forceinline__ uint32_t bin_walk(
     if (rec)  // width 0 marks a rectangle the emission must walk again
         *rec = make_uint4((uint32_t)mask, (uint32_t)(mask >> 32),
                           (uint32_t)tr.x0 | ((uint32_t)tr.y0 << 16),
-                          masked ? ((uint32_t)rw | ((uint32_t)rh << 16)) : 0u);
+                          (masked ? ((uint32_t)rw | ((uint32_t)rh << 8)) : 0u) |
+                              ((uint32_t)cut.bin << 16));
     return cnt;
 }
 
@@ -225,16 +302,26 @@ __global__ void bin_count_depth_kernel(const float2* __restrict__ uv,
                                        int tiles_y, uint32_t* __restrict__ counts,
                                        uint32_t* __restrict__ dkeys,
                                        uint32_t* __restrict__ dvals,
-                                       uint4* __restrict__ recs) {
+                                       uint4* __restrict__ recs,
+                                       const uint32_t* __restrict__ range,
+                                       uint32_t* __restrict__ hist) {
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n) return;
     uint32_t c = 0u;
     if (valid[g] != 0) {
         const float2 mu = uv[g], r = rxy[g];
-        c = bin_walk<false, false>(mu.x, mu.y, r.x, r.y, conic[3 * g], conic[3 * g + 1],
-                                   conic[3 * g + 2], opacity[g], 0u, tile, tiles_x,
-                                   tiles_y, W, H, nullptr, nullptr, nullptr, nullptr,
-                                   0, 0u, 0, recs + g);
+        if (hist) {
+            const CutArgs cut{hist, nullptr, cut_bin(depth[g], ~range[0], range[1])};
+            c = bin_walk<false, false, 1>(mu.x, mu.y, r.x, r.y, conic[3 * g],
+                                          conic[3 * g + 1], conic[3 * g + 2], opacity[g],
+                                          0u, tile, tiles_x, tiles_y, W, H, nullptr, nullptr,
+                                          nullptr, nullptr, 0, 0u, 0, recs + g, cut);
+        } else {
+            c = bin_walk<false, false>(mu.x, mu.y, r.x, r.y, conic[3 * g], conic[3 * g + 1],
+                                       conic[3 * g + 2], opacity[g], 0u, tile, tiles_x,
+                                       tiles_y, W, H, nullptr, nullptr, nullptr, nullptr,
+                                       0, 0u, 0, recs + g);
+        }
     }
     counts[g] = c;
     dkeys[g] = c > 0u ? __float_as_uint(depth[g]) : 0xffffffffu;
@@ -253,6 +340,7 @@ __global__ void bin_emit_kernel(const float2* __restrict__ uv,
                                 const uint32_t* __restrict__ offsets, int64_t n,
                                 int64_t m, int W, int H, int tile, int tiles_x,
                                 int tiles_y, const uint4* __restrict__ recs,
+                                const int32_t* __restrict__ cutoff,
                                 uint32_t* __restrict__ pair_tiles,
                                 uint32_t* __restrict__ pair_ids) {
     const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -263,7 +351,8 @@ __global__ void bin_emit_kernel(const float2* __restrict__ uv,
     const int64_t at = offsets[s];
     if (at + cnt > m) return;
     const uint4 rec = recs[g];
-    const uint32_t rw = rec.w & 0xffffu, rh = rec.w >> 16;
+    const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
+    const int gbin = (int)((rec.w >> 16) & 0xffu);
     if (rw != 0u) {
         // the count walk's decisions: row-major bits over the rectangle
         uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
@@ -277,6 +366,7 @@ __global__ void bin_emit_kernel(const float2* __restrict__ uv,
             while (row) {
                 const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
                 row &= row - 1ull;
+                if (cutoff && cutoff[trow + b] < gbin) continue;
                 if (k < cnt) {
                     pair_tiles[at + k] = trow + b;
                     pair_ids[at + k] = g;
@@ -287,10 +377,124 @@ __global__ void bin_emit_kernel(const float2* __restrict__ uv,
         return;
     }
     const float2 mu = uv[g], r = rxy[g];
-    bin_walk<false, true>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
-                          conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
-                          opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
-                          nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g);
+    if (cutoff)
+        bin_walk<false, true, 2>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
+                                 conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
+                                 opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
+                                 nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g, nullptr,
+                                 CutArgs{nullptr, cutoff, gbin});
+    else
+        bin_walk<false, true>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
+                              conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
+                              opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
+                              nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g);
+}
+
+// Saturation cut, step 1: the view's visible depth range as bit patterns
+// (range[0] holds the complement of the smallest, so both are maxima over
+// zero-initialised words).
+__global__ void __launch_bounds__(256)
+bin_depth_range_kernel(const int32_t* __restrict__ valid, const float* __restrict__ depth,
+                       int64_t n, uint32_t* __restrict__ range) {
+    __shared__ uint32_t s_lo[8], s_hi[8];
+    uint32_t lo = 0u, hi = 0u;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n;
+         g += (int64_t)gridDim.x * blockDim.x) {
+        if (valid[g] != 0) {
+            const uint32_t bits = __float_as_uint(depth[g]);  // positive depths
+            lo = max(lo, ~bits);
+            hi = max(hi, bits);
+        }
+    }
+    lo = __reduce_max_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { s_lo[warp] = lo; s_hi[warp] = hi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+            lo = max(lo, s_lo[w]);
+            hi = max(hi, s_hi[w]);
+        }
+        if (hi != 0u) {  // one pair of atomics per block
+            atomicMax(&range[0], lo);
+            atomicMax(&range[1], hi);
+        }
+    }
+}
+
+// Saturation cut, step 2: per tile, the first depth bin whose running optical
+// depth reaches kCutNeed (the last bin when none does).
+__global__ void bin_cutoff_kernel(const uint32_t* __restrict__ hist, int n_tiles,
+                                  int32_t* __restrict__ cutoff) {
+    static_assert(kCutBins == 64, "two bins per lane");
+    const int t = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= n_tiles) return;  // whole warps
+    const uint2 h = reinterpret_cast<const uint2*>(hist + (int64_t)t * kCutBins)[lane];
+    // inclusive running sums of bins 2*lane and 2*lane + 1
+    unsigned long long a = h.x, b = (unsigned long long)h.x + h.y, incl = b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    const unsigned long long before = incl - b;
+    a += before;
+    b += before;
+    const uint32_t hit_a = __ballot_sync(0xffffffffu, a >= kCutNeed);
+    const uint32_t hit_b = __ballot_sync(0xffffffffu, b >= kCutNeed);
+    if (lane == 0) {
+        int cut = kCutBins - 1;
+        if (hit_a | hit_b) {
+            const int la = hit_a ? __ffs(hit_a) - 1 : 64, lb = hit_b ? __ffs(hit_b) - 1 : 64;
+            cut = min(2 * la, 2 * lb + 1);
+        }
+        cutoff[t] = cut;
+    }
+}
+
+// Saturation cut, step 3: per Gaussian, the pairs that survive the cut (its
+// count and depth key are rewritten; the emission keeps the same pairs).
+__global__ void bin_recount_kernel(const float2* __restrict__ uv,
+                                   const float2* __restrict__ rxy,
+                                   const float* __restrict__ conic,
+                                   const float* __restrict__ opacity,
+                                   const float* __restrict__ depth, int64_t n, int W, int H,
+                                   int tile, int tiles_x, int tiles_y,
+                                   const uint4* __restrict__ recs,
+                                   const int32_t* __restrict__ cutoff,
+                                   uint32_t* __restrict__ counts,
+                                   uint32_t* __restrict__ dkeys) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n || counts[g] == 0u) return;
+    const uint4 rec = recs[g];
+    const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
+    const int gbin = (int)((rec.w >> 16) & 0xffu);
+    uint32_t kept = 0u;
+    if (rw != 0u) {
+        uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
+        const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
+        const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
+        for (uint32_t r = 0; r < rh && mask; ++r) {
+            uint64_t row = mask & row_bits;
+            mask >>= rw;
+            const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
+            while (row) {
+                const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
+                row &= row - 1ull;
+                kept += cutoff[trow + b] >= gbin;
+            }
+        }
+    } else {
+        const float2 mu = uv[g], r = rxy[g];
+        kept = bin_walk<false, false, 2>(mu.x, mu.y, r.x, r.y, conic[3 * g], conic[3 * g + 1],
+                                         conic[3 * g + 2], opacity[g], 0u, tile, tiles_x,
+                                         tiles_y, W, H, nullptr, nullptr, nullptr, nullptr, 0,
+                                         0u, 0, nullptr, CutArgs{nullptr, cutoff, gbin});
+    }
+    counts[g] = kept;
+    if (kept == 0u) dkeys[g] = 0xffffffffu;
 }
 
 }  // namespace
@@ -340,25 +544,42 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
                                  const float* depth, int64_t n, int W, int H, int tile,
                                  int tiles_x, int tiles_y, uint32_t* counts,
                                  uint32_t* dkeys, uint32_t* dvals, uint4* recs,
+                                 uint32_t* cut_range, uint32_t* cut_hist, int32_t* cutoff,
                                  cudaStream_t stream) {
     if (n == 0) return MG_OK;
+    const bool cut = cut_hist != nullptr;
+    if (cut) {
+        bin_depth_range_kernel<<<std::min(ceil_div(n, 256), 148 * 4), 256, 0, stream>>>(
+            valid, depth, n, cut_range);
+        MG_TRY(check_launch("bin_depth_range"));
+    }
     bin_count_depth_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
-        opacity, valid, depth, n, W, H, tile, tiles_x, tiles_y, counts, dkeys, dvals, recs);
-    return check_launch("bin_count_depth");
+        opacity, valid, depth, n, W, H, tile, tiles_x, tiles_y, counts, dkeys, dvals, recs,
+        cut_range, cut_hist);
+    MG_TRY(check_launch("bin_count_depth"));
+    if (!cut) return MG_OK;
+    const int n_tiles = tiles_x * tiles_y;
+    bin_cutoff_kernel<<<ceil_div((int64_t)n_tiles * 32, 256), 256, 0, stream>>>(cut_hist, n_tiles,
+                                                                             cutoff);
+    MG_TRY(check_launch("bin_cutoff"));
+    bin_recount_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+        reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
+        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, counts, dkeys);
+    return check_launch("bin_recount");
 }
 
 mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const float* opacity, const uint32_t* sorted_gid,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
-                          const uint4* recs, uint32_t* pair_tiles, uint32_t* pair_ids,
-                          cudaStream_t stream) {
+                          const uint4* recs, const int32_t* cutoff, uint32_t* pair_tiles,
+                          uint32_t* pair_ids, cudaStream_t stream) {
     if (n == 0 || m == 0) return MG_OK;
     bin_emit_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
         opacity, sorted_gid, counts, offsets, n, m, W, H, tile, tiles_x, tiles_y,
-        recs, pair_tiles, pair_ids);
+        recs, cutoff, pair_tiles, pair_ids);
     return check_launch("bin_emit");
 }
 

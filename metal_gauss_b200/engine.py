@@ -86,8 +86,14 @@ class _ViewState:
         self.rxy = torch.empty(n, 2, **f32)
         self.valid = torch.empty(n, dtype=torch.int32, device=device)
         self.color = torch.empty(n, 3, **f32)
-        nbytes = _lib.load().mg_bin_prepare_scratch_bytes(n)
-        self.prep = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self.n = n
+        self.prep = torch.empty(0, dtype=torch.uint8, device=device)
+
+    def prep_scratch(self, n_tiles: int) -> torch.Tensor:
+        nbytes = _lib.load().mg_bin_prepare_scratch_bytes(self.n, n_tiles)
+        if self.prep.numel() < nbytes:
+            self.prep = torch.empty(nbytes, dtype=torch.uint8, device=self.prep.device)
+        return self.prep
 
 
 class Trainer:
@@ -99,7 +105,8 @@ class Trainer:
                  background=(0.0, 0.0, 0.0), lrs: dict | None = None, w_l1: float = 0.8,
                  w_ssim: float = 0.2, selective: bool = True, near: float = 0.01,
                  far: float = 100.0, max_radius_frac: float = 1.0, group=None,
-                 betas=(0.9, 0.999), eps: float = 1e-15, shard_optimizer: bool | None = None):
+                 betas=(0.9, 0.999), eps: float = 1e-15, shard_optimizer: bool | None = None,
+                 saturation_cut: bool = True):
         self.device = torch.device(device)
         self.n = n = int(params["means"].shape[0])
         self.world = dp.world_size(group)
@@ -109,6 +116,10 @@ class Trainer:
         # the shard, parameter all-gather); rows are padded to a multiple of
         # the world size so every segment splits into equal row shards
         self.shard_optimizer = (self.world > 1) if shard_optimizer is None else shard_optimizer
+        # drop each tile's pairs behind the depth where covering Gaussians
+        # provably saturate every pixel (mg_bin_prepare): same images and
+        # gradients, fewer pairs to emit and sort
+        self.saturation_cut = int(bool(saturation_cut))
         self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
@@ -256,10 +267,11 @@ class Trainer:
         self.visibility_count().add_(st.valid)
         self._end(ev)
         ev = self._begin("bin_prepare")
+        prep = st.prep_scratch(-(-view.width // self.tile) * -(-view.height // self.tile))
         _lib.check(L.mg_bin_prepare(
             ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), ptr(st.valid), ptr(st.depth),
-            self.n, view.width, view.height, self.tile, ptr(self._totals[v:v + 1]), ptr(st.prep),
-            st.prep.numel(), s), "bin_prepare")
+            self.n, view.width, view.height, self.tile, self.saturation_cut,
+            ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(), s), "bin_prepare")
         self._end(ev)
 
     def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
@@ -289,7 +301,8 @@ class Trainer:
             b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8, device=self.device)
         ev = self._begin("bin_emit")
         _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), n, m, W,
-                                 H, self.tile, ptr(st.prep), ptr(b.ids), ptr(b.offsets),
+                                 H, self.tile, self.saturation_cut, ptr(st.prep), ptr(b.ids),
+                                 ptr(b.offsets),
                                  ptr(b.emit), b.emit.numel(), s), "bin_emit")
         self._end(ev)
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)

@@ -201,18 +201,18 @@ def bin_and_sort(uv, rxy, conic, opacity, valid, depth, W, H, tile, workspace=No
                 torch.zeros(tx * ty + 1, dtype=torch.int32, device=dev), tx)
     ws = workspace or _default_ws.setdefault(dev.index or 0, BinWorkspace())
     L = _lib.load()
-    pbytes = L.mg_bin_prepare_scratch_bytes(n)
+    pbytes = L.mg_bin_prepare_scratch_bytes(n, tx * ty)
     prep = ws.get("prep", pbytes, dev)
     total_dev = ws.get("total", 8, dev)
     s = _lib.stream()
     _lib.call("mg_bin_prepare", ptr(uv), ptr(rxy), ptr(conic), ptr(opacity), ptr(valid),
-              ptr(depth), n, W, H, tile, ptr(total_dev), ptr(prep), prep.numel(), s)
+              ptr(depth), n, W, H, tile, 0, ptr(total_dev), ptr(prep), prep.numel(), s)
     m = int(total_dev[:8].view(torch.int64).item())
     gauss_ids = torch.empty(m, dtype=torch.int32, device=dev)
     offsets = torch.empty(tx * ty + 1, dtype=torch.int32, device=dev)
     ebytes = L.mg_bin_emit_scratch_bytes(n, m, tx * ty)
     emit = ws.get("emit", ebytes, dev)
-    _lib.call("mg_bin_emit", ptr(uv), ptr(rxy), ptr(conic), ptr(opacity), n, m, W, H, tile,
+    _lib.call("mg_bin_emit", ptr(uv), ptr(rxy), ptr(conic), ptr(opacity), n, m, W, H, tile, 0,
               ptr(prep), ptr(gauss_ids), ptr(offsets), ptr(emit), emit.numel(), s)
     return gauss_ids, offsets, tx
 

@@ -40,7 +40,7 @@ def test_version_and_error_string():
 def test_scratch_queries_need_no_device():
     lib = _lib.load()
     assert lib.mg_sort_scratch_bytes(1 << 20, 32, 4) > 0
-    assert lib.mg_bin_prepare_scratch_bytes(1000) > 4 * 1000
+    assert lib.mg_bin_prepare_scratch_bytes(1000, 2500) > 4 * 1000 + 64 * 4 * 2500
     assert lib.mg_bin_emit_scratch_bytes(1000, 5000, 2500) > 4 * 5000
     assert lib.mg_l1_ssim_scratch_bytes(64, 64) >= 9 * 64 * 64 * 4
     # counters + tile order + block walks + items + checkpoints (5 floats per
