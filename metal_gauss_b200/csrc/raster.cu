@@ -38,10 +38,11 @@
 // so a long list is split over many warps instead of forming the kernel's
 // tail. The colour and alpha behind an entry enter its gradient only through
 // their dot product with the pixel's output gradient, so a pixel carries one
-// running sum for them. Per live entry the warp reduces its 32 pixels'
-// contributions with a 10-slot butterfly reduce-scatter (12 shuffles) and
-// three lanes add the 48-byte gradient record to global memory with 16-byte
-// vector atomics.
+// running sum for them. A live entry to which at most 16 of the warp's
+// pixels contribute is added as per-pixel 16-byte vector atomics; otherwise
+// the warp reduces its 32 pixels' contributions with a 10-slot butterfly
+// reduce-scatter (12 shuffles) and three lanes add the 48-byte gradient record
+// with three vector atomics (the crossover measured on B200).
 #include <mutex>
 #include <unordered_map>
 
@@ -153,6 +154,12 @@ __device__ __forceinline__ void cp_async_wait() {
 #define MG_BWD_STAGES 3
 #endif
 constexpr int kFwdStages = MG_FWD_STAGES;
+#ifndef MG_BWD_DIRECT_MAX
+#define MG_BWD_DIRECT_MAX 16
+#endif
+// Up to this many contributing pixels, a live entry's gradient goes out as
+// per-pixel vector atomics instead of through the warp reduction.
+constexpr int kBwdDirectMax = MG_BWD_DIRECT_MAX;
 constexpr int kBwdStages = MG_BWD_STAGES;
 
 // A warp's ring of chunk buffers: q[buffer][word][entry], so a lane's three
@@ -545,9 +552,9 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                 v[7] = w * gr; v[8] = w * gg; v[9] = w * gb;
                 float4* dst =
                     reinterpret_cast<float4*>(grad2d + (int64_t)st.id[buf][k] * MG_G2D_STRIDE);
-                if (__popc(act) <= 2) {
+                if (__popc(act) <= kBwdDirectMax) {
                     // few contributing pixels: each adds its own record (the
-                    // warp reduction costs more than two sets of atomics)
+                    // warp reduction costs more than a few sets of atomics)
                     if (active) {
                         atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
                         if (dp != 0.f) atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
