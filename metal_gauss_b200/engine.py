@@ -10,18 +10,19 @@ ranks when torch.distributed is initialised:
     storage form, 59 floats per Gaussian, as consecutive segments
     means (N,3) | quats (N,4) | log_scales (N,3) | logit_opac (N,) |
     sh_dc (N,1,3) | sh_rest (N,15,3);
-  * the gradient buffer has the same segments plus one more: the number of
-    views in which each Gaussian was visible, so a SINGLE collective
-    (NCCL all-reduce over NVLink) sums the gradients and forms the union
-    visibility mask that selective Adam needs;
+  * the gradient buffer has the same segments plus the number of views in
+    which each Gaussian was visible and the loss;
   * per view: preprocess -> binning (device sort) -> raster forward -> fused
     loss -> raster backward (packed gradient record) -> preprocess backward
     that ADDS into the flat gradient with the exp/sigmoid chain applied;
   * the loss of a batch is the mean over its views, so each view's
     gradient is scaled by 1 / (global batch).
 
-The parameters are replicated on every rank and stay bit-identical: all
-ranks apply the same Adam update to the same all-reduced gradient.
+With several ranks the optimizer is sharded (ZeRO-1): the visibility counts
+and the loss are all-reduced, the parameter gradient is reduce-scattered so
+each rank holds the summed gradient of its own chunk, each rank runs Adam on
+that chunk only, and the updated parameters are all-gathered, so every rank
+again holds the full, identical parameter set for the next step.
 """
 
 from __future__ import annotations
@@ -209,6 +210,18 @@ class Trainer:
 
     def grad(self, name: str) -> torch.Tensor:
         return self._view(self.G, name)
+
+    def parameters(self) -> dict:
+        """The current parameters in the trainer's storage form (views into
+        the flat device buffer): means, quats, log_scales, logit_opac,
+        sh_dc (N,1,3), sh_rest (N,15,3)."""
+        return {name: self.param(name) for name, _ in SEGMENTS}
+
+    def export_ply(self, path, filter_3d=None) -> None:
+        """Write the current model as an INRIA-convention .ply, the file the
+        reference's `train.export_ply` writes (see `metal_gauss_b200.ply`)."""
+        from .ply import export_ply
+        export_ply(self.parameters(), path, filter_3d=filter_3d)
 
     def visibility_count(self) -> torch.Tensor:
         return self.G[self.vis_offset:self.vis_offset + self.n]
@@ -466,3 +479,47 @@ class Trainer:
             total += (44 + 48 + 192) * n + 236 * 2 * n  # preprocess bwd (+ RMW grads)
         total += 28 * FLOATS_PER_GAUSSIAN * nv + 8 * n   # selective Adam
         return total
+
+
+def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: int = 0,
+        lr_means_end: float | None = None, sh_warmup: int = 0, callback=None) -> list[float]:
+    """The reference's training loop (train.py:311-366) over batches of views.
+
+    Views are drawn in epoch permutations (numpy's default_rng(seed), a new
+    permutation whenever one is used up), `batch` per step; the means learning
+    rate decays geometrically from its initial value to `lr_means_end` over
+    `steps`; with `sh_warmup`, the SH degree grows by one band every
+    `sh_warmup` steps up to 3. Densification, the appearance model and the
+    opacity/scale regularisers are not part of this loop. `targets` are
+    (H, W, 3) uint8 or float images, moved to the device per step; returns the
+    per-step losses (one host read per step). With several ranks every rank
+    draws the same batches and renders its own share of each."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(len(views))
+    oi = 0
+    lr0 = trainer.lrs["means"]
+    decay = 1.0 if lr_means_end is None else (lr_means_end / max(lr0, 1e-12)) ** (1.0 / steps)
+    rank_views = dp.shard(list(range(batch)), trainer.rank, trainer.world)
+    losses = []
+    for step in range(1, steps + 1):
+        idx = []
+        while len(idx) < batch:
+            if oi >= len(order):
+                order = rng.permutation(len(views))
+                oi = 0
+            idx.append(int(order[oi]))
+            oi += 1
+        trainer.lrs["means"] = lr0 * decay ** step
+        trainer.sh_degree = min(3, step // sh_warmup) if sh_warmup else 3
+        mine = [idx[i] for i in rank_views]
+        ts = []
+        for i in mine:
+            t = targets[i]
+            t = torch.as_tensor(t).to(trainer.device, non_blocking=True)
+            ts.append(t.float().div_(255.0) if t.dtype == torch.uint8 else t.float())
+        losses.append(float(trainer.train_step([views[i] for i in mine], ts, batch)))
+        if callback is not None:
+            callback(step, losses[-1])
+    return losses
+

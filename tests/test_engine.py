@@ -118,3 +118,30 @@ def test_saturation_cut_changes_nothing_but_the_pair_count(cuda):
         assert rel_l2(cut.grad(name).cpu().numpy(), full.grad(name).cpu().numpy()) < 1e-5, name
         assert rel_l2(cut.param(name).cpu().numpy(), full.param(name).cpu().numpy()) < 1e-6, name
     assert torch.equal(cut.visibility_count(), full.visibility_count())
+
+
+def test_trainer_exports_its_parameters_as_ply(cuda, tmp_path):
+    from metal_gauss_b200 import ply
+    p, views, targets = _setup(5)
+    tr = Trainer(p, cuda, sh_degree=3)
+    tr.train_step(views[:1], [torch.from_numpy(targets[0]).cuda()], 1)
+    tr.export_ply(tmp_path / "model.ply")
+    q = ply.read_ply(tmp_path / "model.ply")
+    for name, _ in SEGMENTS:
+        assert torch.equal(q[name], tr.param(name).cpu()), name
+
+
+def test_fit_runs_the_reference_loop_over_batches(cuda):
+    """engine.fit: epoch permutations of the views, batches of 2, the means
+    learning rate decaying to its end value, SH bands warming up."""
+    from metal_gauss_b200.engine import fit
+    p, views, targets = _setup(13)
+    tr = Trainer(p, cuda, sh_degree=3, lrs={"means": 1e-3})
+    u8 = [np.clip(t * 255, 0, 255).astype(np.uint8) for t in targets]
+    seen = []
+    losses = fit(tr, views, u8, steps=6, batch=2, lr_means_end=1e-4, sh_warmup=2,
+                 callback=lambda step, loss: seen.append((step, tr.sh_degree, tr.lrs["means"])))
+    assert len(losses) == 6 and all(np.isfinite(losses))
+    assert losses[-1] < losses[0]
+    assert [d for _, d, _ in seen] == [0, 1, 1, 2, 2, 3]
+    assert abs(seen[-1][2] - 1e-4) < 1e-9
