@@ -308,6 +308,18 @@ mg_status mg_rasterize_forward(
     int32_t* out_stop, int32_t* tile_work, void* scratch, size_t scratch_bytes,
     mg_stream_t stream);
 
+/* out_T and out_stop may both be NULL: a forward-only render (the viewer's
+ * and render_path's callers, viewer.py:477-485), which writes neither them
+ * nor the backward's checkpoints; the scratch is then only workspace. */
+
+/* Mip-Splatting's 2D antialias compensation of opacity, applied before
+ * binning as metal_backend.py:506-511 does: out[i] = opacity[i] *
+ * sqrt(clamp(det_before / det_after, 0, 1)) with det_before the determinant
+ * of the 2D covariance before the `blur` (0.3 px) dilation, recovered from
+ * the dilated conic (metal_backend.py:367-393). */
+mg_status mg_antialias_opacity(const float* conic, const float* opacity, int64_t n,
+                               float blur, float* out, mg_stream_t stream);
+
 /* Replaces rasterize_backward (rasterize.mm:147-194; rasterize.metal:
  * 173-340). grad2d (N, MG_G2D_STRIDE) is ACCUMULATED into (zero it first for
  * a fresh gradient). background as in the forward: the blend's adjoint is

@@ -7,7 +7,9 @@ Drop-in surface (same names and semantics as the reference's modules):
   FusedAdam, SelectiveAdam   metal_gauss.fused_adam / selective_adam
   ssim, gaussian_kernel      train.ssim / train._gaussian_kernel
 Batched multi-view training (one process per GPU, NCCL gradient exchange):
-  engine.Trainer
+  engine.Trainer, engine.fit
+Forward-only rendering of many views (viewer / camera paths):
+  renderer.Renderer
 """
 
 from .api import BACKENDS, render

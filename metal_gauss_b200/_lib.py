@@ -73,6 +73,7 @@ SIGNATURES = {
     "mg_bin_emit": (i32, [vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp, vp, sz,
                           vp]),
     "mg_pack_splats": (i32, [vp, vp, vp, vp, i64, vp, vp]),
+    "mg_antialias_opacity": (i32, [vp, vp, i64, f32, vp, vp]),
     "mg_raster_scratch_bytes": (sz, [i32, i32, i32, i64]),
     "mg_rasterize_forward": (i32, [vp, vp, vp, i64, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,
                                    vp, sz, vp]),

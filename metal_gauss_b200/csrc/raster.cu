@@ -253,7 +253,7 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
         if (start < end && !__all_sync(0xffffffffu, done)) {
             float rx0, rx1, ry0, ry1;
             warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
-            float* ck = ckpt + wb * 32 + lane;
+            float* ck = ckpt ? ckpt + wb * 32 + lane : nullptr;  // null: forward only
             const int n_chunks = (end - start + 31) >> 5;
             // ids of the first kStages chunks (all loads in flight together),
             // then the copies of the first kStages - 1
@@ -279,7 +279,7 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                     const int j = base + 32 * kStages + lane;
                     gid_next = j < end ? ids[j] : -1;
                 }
-                if (ci != 0 && ((base - start) & (kSeg - 1)) == 0) {
+                if (ck && ci != 0 && ((base - start) & (kSeg - 1)) == 0) {
                     float* c = ck + ckpt_slot(start, tile_id, (base - start) / kSeg) * 5 *
                                         G::kPixPad;
                     c[0] = T;
@@ -343,11 +343,12 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
         if (lane == 0) {
             block_work[tile_id * G::kCount + wb] = walk;
             if (tile_work && walk > 0) atomicMax(&tile_work[tile_id], walk);
-            if (nseg > 0) ibase = atomicAdd(&counter[2], nseg);
+            if (items && nseg > 0) ibase = atomicAdd(&counter[2], nseg);
         }
         ibase = __shfl_sync(0xffffffffu, ibase, 0);
-        for (int sgi = lane; sgi < nseg; sgi += 32)
-            items[ibase + sgi] = make_int2(tile_id * G::kCount + wb, sgi);
+        if (items)
+            for (int sgi = lane; sgi < nseg; sgi += 32)
+                items[ibase + sgi] = make_int2(tile_id * G::kCount + wb, sgi);
         if (inimg) {
             const int64_t o = (int64_t)py * W + px;
             if (has_bg) {
@@ -358,8 +359,10 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
             out_rgb[3 * o + 1] = ag;
             out_rgb[3 * o + 2] = ab;
             out_alpha[o] = aa;
-            out_T[o] = T;
-            out_stop[o] = stop;
+            if (out_T) {  // the backward's inputs; absent in forward-only renders
+                out_T[o] = T;
+                out_stop[o] = stop;
+            }
         }
     }
 }
@@ -715,6 +718,21 @@ __global__ void pack_intersections_kernel(const float2* __restrict__ uv,
     p_rgb[3 * i + 2] = color[3 * g + 2];
 }
 
+// Mip-Splatting opacity compensation (metal_backend.py:367-393): the 2D
+// covariance before the 0.3 px blur, recovered from the blurred conic, gives
+// op * sqrt(clamp(det_before / det_after, 0, 1)).
+__global__ void antialias_opacity_kernel(const float* __restrict__ conic,
+                                         const float* __restrict__ opacity, int64_t n,
+                                         float blur, float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float cxx = conic[3 * i], cxy = conic[3 * i + 1], cyy = conic[3 * i + 2];
+    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
+    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
+    const float det_before = (a - blur) * (c - blur) - b * b;
+    out[i] = opacity[i] * sqrtf(fminf(fmaxf(det_before, 0.0f) / det_after, 1.0f));
+}
+
 // ---------------------------------------------------------------- host side
 
 int blocks_per_tile(int tile) { return (tile * tile + 31) / 32; }
@@ -785,7 +803,8 @@ mg_status launch_fwd(const float4* splats, const int32_t* ids, const int32_t* of
     raster_forward_kernel<TILE><<<grid, kRasterWarps * 32, 0, stream>>>(
         splats, ids, offsets, W, H, tiles_x, n_tiles, bg != nullptr, bg ? bg[0] : 0.f,
         bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, rgb, alpha, T, stop, sc.order, sc.counters,
-        sc.block_work, tile_work, sc.ckpt, sc.items, m_cap, device_error_word());
+        sc.block_work, tile_work, T ? sc.ckpt : nullptr, T ? sc.items : nullptr, m_cap,
+        device_error_word());
     return check_launch("rasterize_forward");
 }
 
@@ -880,8 +899,10 @@ extern "C" mg_status mg_rasterize_forward(const void* splats, const int32_t* gau
     MG_REQUIRE(width > 0 && height > 0, "rasterize_forward: empty image");
     const int tiles_y = (height + tile - 1) / tile;
     MG_REQUIRE(tiles_x == (width + tile - 1) / tile, "rasterize_forward: tiles_x mismatch");
-    MG_REQUIRE(tile_offsets && out_rgb && out_alpha && out_T && out_stop && scratch,
+    MG_REQUIRE(tile_offsets && out_rgb && out_alpha && scratch,
                "rasterize_forward: null pointer");
+    MG_REQUIRE((out_T == nullptr) == (out_stop == nullptr),
+               "rasterize_forward: give both out_T and out_stop, or neither (forward only)");
     MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 31), "rasterize_forward: pair count out of range");
     MG_REQUIRE(m == 0 || (splats && gauss_ids), "rasterize_forward: null splats or ids");
     MG_REQUIRE((reinterpret_cast<uintptr_t>(splats) & 15u) == 0u &&
@@ -958,4 +979,14 @@ extern "C" mg_status mg_pack_intersections(const float* uv, const float* conic,
         reinterpret_cast<const float2*>(uv), conic, opacity, color, gauss_ids, m, p_xy_opac,
         p_conic, p_rgb);
     return check_launch("pack_intersections");
+}
+
+extern "C" mg_status mg_antialias_opacity(const float* conic, const float* opacity, int64_t n,
+                                          float blur, float* out, mg_stream_t stream) {
+    MG_REQUIRE(n >= 0, "antialias_opacity: negative count");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(conic && opacity && out, "antialias_opacity: null pointer");
+    antialias_opacity_kernel<<<ceil_div(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        conic, opacity, n, blur, out);
+    return check_launch("antialias_opacity");
 }

@@ -1,0 +1,159 @@
+"""Forward-only rendering of many views on one GPU.
+
+The reference's viewer and camera-path renderer call `render` under
+`torch.no_grad()` view after view (viewer.py:477-485, render_path.py:
+440-456). This renderer keeps the Gaussians resident in the form the kernels
+read and, per view, runs the projection with SH colour, the antialias
+opacity compensation when asked for (metal_backend.py:506-511), the binning
+with the saturation cut, the packing and a forward-only rasterisation that
+writes no transmittance, stop indices or checkpoints and keeps no autograd
+state. Views are processed in batches with one host read per batch (the pair
+totals of all its views).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import ptr
+from .engine import _ViewState
+
+
+class _FrameBuffers:
+    """Per-resolution scratch of the forward-only path (no transmittance,
+    stop indices, gradients or loss scratch)."""
+
+    def __init__(self, n: int, device):
+        self.splats = torch.empty(n, _lib.SPLAT_FLOATS, dtype=torch.float32, device=device)
+        self.raster = torch.empty(0, dtype=torch.uint8, device=device)
+        self.ids = torch.empty(0, dtype=torch.int32, device=device)
+        self.offsets = None
+        self.emit = torch.empty(0, dtype=torch.uint8, device=device)
+
+
+class Renderer:
+    """`params` in the trainer's storage form (means, quats, log_scales,
+    logit_opac, sh_dc (N,1,3), sh_rest (N,15,3)); activations are applied
+    once here."""
+
+    def __init__(self, params: dict, device="cuda", *, sh_degree: int = 3, tile: int = 16,
+                 background=(0.0, 0.0, 0.0), antialias: bool = False, near: float = 0.01,
+                 far: float = 100.0, max_radius_frac: float = 1.0, saturation_cut: bool = True,
+                 batch: int = 8):
+        self.device = torch.device(device)
+        f32 = dict(dtype=torch.float32, device=self.device)
+        self.n = n = int(params["means"].shape[0])
+        self.means = params["means"].to(**f32).reshape(n, 3).contiguous()
+        self.quats = params["quats"].to(**f32).reshape(n, 4).contiguous()
+        self.scales = torch.exp(params["log_scales"].to(**f32)).reshape(n, 3).contiguous()
+        self.opac = torch.sigmoid(params["logit_opac"].to(**f32)).reshape(n).contiguous()
+        self.sh_dc = params["sh_dc"].to(**f32).reshape(n, 1, 3).contiguous()
+        self.sh_rest = params["sh_rest"].to(**f32).reshape(n, 15, 3).contiguous()
+        self.sh_degree, self.tile = sh_degree, tile
+        self.antialias = antialias
+        self.near, self.far, self.max_radius_frac = near, far, max_radius_frac
+        self.saturation_cut = int(bool(saturation_cut))
+        self.background = None if background is None or all(b == 0 for b in background) \
+            else tuple(float(b) for b in background)
+        self.batch = batch
+        self._states: list[_ViewState] = []
+        self._bufs: dict = {}
+        # per-view opacity after the antialias compensation
+        self._opac_view: list[torch.Tensor] = []
+        self._totals = torch.zeros(batch, dtype=torch.int64, device=self.device)
+
+    def _camera(self, view) -> _lib.Camera:
+        vm = view.viewmat.to(torch.float32)
+        K = view.K
+        cc = -vm[:3, :3].T @ vm[:3, 3]
+        return _lib.make_camera(vm, float(K[0, 0]), float(K[1, 1]), float(K[0, 2]),
+                                float(K[1, 2]), view.width, view.height, self.near, self.far, 0.3,
+                                self.max_radius_frac * max(view.width, view.height), cc)
+
+    def _state(self, v: int) -> _ViewState:
+        while len(self._states) <= v:
+            self._states.append(_ViewState(self.n, self.device))
+            if self.antialias:
+                self._opac_view.append(torch.empty(self.n, dtype=torch.float32,
+                                                   device=self.device))
+        return self._states[v]
+
+    def _opacity(self, v: int) -> torch.Tensor:
+        return self._opac_view[v] if self.antialias else self.opac
+
+    def _buffers(self, W: int, H: int) -> _FrameBuffers:
+        b = self._bufs.get((W, H))
+        if b is None:
+            b = _FrameBuffers(self.n, self.device)
+            self._bufs[(W, H)] = b
+        return b
+
+    def render(self, views) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        """[(rgb (H,W,3), alpha (H,W))] device tensors, one pair per view."""
+        out = []
+        for i in range(0, len(views), self.batch):
+            out += self._render_batch(views[i:i + self.batch])
+        return out
+
+    def _render_batch(self, views):
+        L = _lib.load()
+        s = _lib.stream()
+        n = self.n
+        cams = [self._camera(v) for v in views]
+        for v, (view, cam) in enumerate(zip(views, cams)):
+            st = self._state(v)
+            opac = self._opacity(v)
+            _lib.check(L.mg_preprocess_forward(
+                ptr(self.means), ptr(self.quats), ptr(self.scales), ptr(self.sh_dc),
+                ptr(self.sh_rest), _lib.SH_SPLIT, ptr(self.opac), _lib.C.byref(cam),
+                self.sh_degree, n, ptr(st.uv), ptr(st.conic), ptr(st.depth), ptr(st.rxy),
+                ptr(st.valid), ptr(st.color), s), "preprocess_forward")
+            if self.antialias:
+                # before binning, as the reference does: the exact tile test
+                # then uses the opacity that is composited
+                _lib.check(L.mg_antialias_opacity(ptr(st.conic), ptr(self.opac), n, 0.3,
+                                                  ptr(opac), s), "antialias_opacity")
+            tiles = -(-view.width // self.tile) * -(-view.height // self.tile)
+            prep = st.prep_scratch(tiles)
+            _lib.check(L.mg_bin_prepare(
+                ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), ptr(st.valid),
+                ptr(st.depth), n, view.width, view.height, self.tile, self.saturation_cut,
+                ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(), s), "bin_prepare")
+        totals = self._totals[:len(views)].tolist()
+        bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
+        bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
+        out = []
+        for v, (view, m) in enumerate(zip(views, totals)):
+            st = self._states[v]
+            opac = self._opacity(v)
+            W, H, m = view.width, view.height, int(m)
+            b = self._buffers(W, H)
+            tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
+            n_tiles = tiles_x * tiles_y
+            if b.ids.numel() < max(m, 1):
+                b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32, device=self.device)
+            if b.offsets is None or b.offsets.numel() != n_tiles + 1:
+                b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
+            ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
+            if b.emit.numel() < ebytes:
+                b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
+                                     device=self.device)
+            rbytes = L.mg_raster_scratch_bytes(W, H, self.tile, m)
+            if b.raster.numel() < rbytes:
+                b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
+                                       device=self.device)
+            _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), n, m,
+                                     W, H, self.tile, self.saturation_cut, ptr(st.prep),
+                                     ptr(b.ids), ptr(b.offsets), ptr(b.emit), b.emit.numel(),
+                                     s), "bin_emit")
+            _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(opac), ptr(st.color),
+                                        n, ptr(b.splats), s), "pack_splats")
+            rgb = torch.empty(H, W, 3, dtype=torch.float32, device=self.device)
+            alpha = torch.empty(H, W, dtype=torch.float32, device=self.device)
+            _lib.check(L.mg_rasterize_forward(
+                ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, W, H, self.tile, tiles_x, bgp,
+                ptr(rgb), ptr(alpha), None, None, None, ptr(b.raster), b.raster.numel(), s),
+                "rasterize_forward")
+            out.append((rgb, alpha))
+        return out
