@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--dense-adam", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=120.0)
+    ap.add_argument("--render", action="store_true",
+                    help="forward-only render throughput on cfg4 (3M heavy-tailed Gaussians, "
+                         "1920x1080, antialias, 256 orbit views) instead of the training step")
     return ap.parse_args()
 
 
@@ -379,6 +382,65 @@ def run_ours(args, rank, world, local):
         emit(out)
 
 
+def run_render(args, rank, world, local):
+    """Forward-only frames/s on cfg4 through renderer.Renderer: each rank
+    renders its share of the 256 orbit views (weak in views per rank, no
+    collective); one step = every view once. `e2e` adds the device->host copy
+    of each frame (rgb + alpha, float32) into pinned memory."""
+    from metal_gauss_b200 import _lib, scenes
+    from metal_gauss_b200.renderer import Renderer
+
+    dev = torch.device("cuda", local)
+    p, views, spec = scenes.config("cfg4", seed=0)
+    mine = views[rank::world]
+    r = Renderer(p, dev, sh_degree=spec["sh_degree"], antialias=spec["antialias"],
+                 background=spec["background"], batch=spec["batch"])
+    for _ in range(max(args.warmup, 3)):
+        r.render(mine[:spec["batch"]])
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 3))
+    L = _lib.load()
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        launches0 = L.mg_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            out = r.render(mine)
+            del out
+        e1.record()
+        torch.cuda.synchronize()
+        launches = (L.mg_launch_count() - launches0) // steps
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    W, H = views[0].width, views[0].height
+    host = [torch.empty(H, W, 4, dtype=torch.float32).pin_memory() for _ in range(2)]
+    barrier(world)
+    e0.record()
+    for k, (rgb, alpha) in enumerate(r.render(mine)):
+        host[k % 2][..., :3].copy_(rgb, non_blocking=True)
+        host[k % 2][..., 3].copy_(alpha, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    if rank == 0:
+        frames = len(views)
+        emit({
+            "metric": "render frames/s (forward only) at 1920x1080, 3M Gaussians, antialias",
+            "value": round(1000.0 * frames / ms, 2), "unit": "frames/s", "n_gpus": world,
+            "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 3),
+            "ms_per_frame": round(ms / frames, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg4: 3M heavy-tailed Gaussians, SH3, 1920x1080, fov 60, "
+                                   "antialias, 256 orbit views per step sharded over the GPUs",
+                       "batch_views": spec["batch"],
+                       "l2": "no flush: Gaussians (3M x 236 B) larger than L2"},
+            "e2e": {"value": round(1000.0 * frames / e_ms, 2), "unit": "frames/s",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": frames * W * H * 16,
+                    "api": "metal_gauss_b200.renderer.Renderer.render"},
+            "gpu_launches": int(launches), "clocks": clocks.summary(),
+        })
+
+
 # ----------------------------------------------------------- CPU (oracle)
 
 def cpu_view_step(op, params_np, view, target, batch, selective_state=None):
@@ -518,6 +580,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.render:
+            run_render(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:
