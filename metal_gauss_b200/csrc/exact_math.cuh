@@ -188,6 +188,65 @@ __device__ __forceinline__ float min_q_over_rect(float mux, float muy, float ca,
     return best;
 }
 
+// min_q_over_rect evaluated tile after tile along a row-major walk of a grid
+// of tile rectangles. The terms that depend only on one row edge (y) or one
+// column edge (x) -- among them the two divisions per edge -- are computed
+// once per edge and shared by the tiles on either side of it. Each value is
+// produced by the same operations on the same operands as min_q_over_rect,
+// so the minima are bit-identical; only repeated work is removed.
+struct RowEdge {
+    float y, ey, s, tc;  // y, y - mu_y, b (y - mu_y) / a, c (y - mu_y)^2
+};
+struct ColEdge {
+    float x, ex, s, ta;  // x, x - mu_x, b (x - mu_x) / c, a (x - mu_x)^2
+};
+struct RectQuadratic {
+    float mux, muy, a, b, b2, c;
+    __device__ __forceinline__ RectQuadratic(float mux_, float muy_, float ca, float cb,
+                                             float ccz)
+        : mux(mux_), muy(muy_), a(fmaxf(ca, 1e-12f)), b(cb), b2(2.0f * cb),
+          c(fmaxf(ccz, 1e-12f)) {}
+    __device__ __forceinline__ RowEdge row_edge(float y) const {
+        RowEdge e;
+        e.y = y;
+        e.ey = y - muy;
+        e.s = (b * e.ey) / a;
+        e.tc = (c * e.ey) * e.ey;
+        return e;
+    }
+    __device__ __forceinline__ ColEdge col_edge(float x) const {
+        ColEdge e;
+        e.x = x;
+        e.ex = x - mux;
+        e.s = (b * e.ex) / c;
+        e.ta = (a * e.ex) * e.ex;
+        return e;
+    }
+    // min_q_over_rect(mux, muy, ca, cb, ccz, l.x, r.x, t.y, bt.y)
+    __device__ __forceinline__ float min_q(const ColEdge& l, const ColEdge& r, const RowEdge& t,
+                                           const RowEdge& bt) const {
+        if (mux >= l.x && mux <= r.x && muy >= t.y && muy <= bt.y) return 0.0f;
+        float best = __int_as_float(0x7f800000);
+        {
+            const float ex = clampf(mux - t.s, l.x, r.x) - mux;
+            best = fminf(best, (((a * ex) * ex) + ((b2 * ex) * t.ey)) + t.tc);
+        }
+        {
+            const float ex = clampf(mux - bt.s, l.x, r.x) - mux;
+            best = fminf(best, (((a * ex) * ex) + ((b2 * ex) * bt.ey)) + bt.tc);
+        }
+        {
+            const float ey = clampf(muy - l.s, t.y, bt.y) - muy;
+            best = fminf(best, (l.ta + ((b2 * l.ex) * ey)) + ((c * ey) * ey));
+        }
+        {
+            const float ey = clampf(muy - r.s, t.y, bt.y) - muy;
+            best = fminf(best, (r.ta + ((b2 * r.ex) * ey)) + ((c * ey) * ey));
+        }
+        return best;
+    }
+};
+
 // Tile rectangle clamped to the grid, from the SnugBox extents
 // (binning.metal:59-64).
 struct TileRect {

@@ -131,6 +131,11 @@ preprocess_forward_kernel(const float* __restrict__ means,
 // reaches ln(1e4) + 1 (T <= 3.7e-5 with a margin for float rounding), and
 // pairs in later bins are dropped. Kept pairs are a depth-order prefix of
 // each tile's list, so images and gradients are unchanged.
+// Resident 256-thread CTAs per SM the binning walks' register budget is held
+// to (0: none).
+#ifndef MG_BIN_MIN_CTAS
+#define MG_BIN_MIN_CTAS 4
+#endif
 constexpr int kCutBins = kSaturationBins;
 constexpr float kCutOdScale = 1048576.0f;  // optical depth quantum 2^-20
 constexpr uint32_t kCutNeed = 10707140u;   // (ln(1e4) + 1) * 2^20, rounded up
@@ -208,14 +213,20 @@ __device__ __forceinline__ uint32_t bin_walk(
     uint64_t mask = 0ull;
     int bit = 0;
     uint32_t cnt = 0u;
+    // inside the rectangle a tile's bottom (right) edge is the next row's
+    // top (next tile's left) edge: (ty + 1) * tile < H there
+    const RectQuadratic rq(mux, muy, ca, cb, cc);
+    RowEdge top = rq.row_edge((float)(tr.y0 * tile));
     for (int ty = tr.y0; ty <= tr.y1; ++ty) {
-        const float y0 = (float)(ty * tile);
-        const float y1 = fminf((float)((ty + 1) * tile), (float)H);
+        const RowEdge bottom = rq.row_edge(fminf((float)((ty + 1) * tile), (float)H));
+        const float y0 = top.y, y1 = bottom.y;
+        ColEdge right = rq.col_edge((float)(tr.x0 * tile));
         for (int tx = tr.x0; tx <= tr.x1; ++tx) {
-            const float x0 = (float)(tx * tile);
-            const float x1 = fminf((float)((tx + 1) * tile), (float)W);
+            const ColEdge left = right;
+            right = rq.col_edge(fminf((float)((tx + 1) * tile), (float)W));
+            const float x0 = left.x, x1 = right.x;
             const int b = bit++;
-            if (min_q_over_rect(mux, muy, ca, cb, cc, x0, x1, y0, y1) >= thr) continue;
+            if (rq.min_q(left, right, top, bottom) >= thr) continue;
             if (masked) mask |= 1ull << b;
             if (kCut == 1 && can_cover) {
                 const uint32_t q =
@@ -237,6 +248,7 @@ __device__ __forceinline__ uint32_t bin_walk(
             }
             ++cnt;
         }
+        top = bottom;
     }
     if (rec)  // width 0 marks a rectangle the emission must walk again
         *rec = make_uint4((uint32_t)mask, (uint32_t)(mask >> 32),
@@ -292,7 +304,7 @@ __global__ void bin_write_kernel(const float2* __restrict__ uv,
 // Gaussians that claim no tile get key 0xffffffff and sort behind every
 // positive depth (valid depths are > near > 0, whose bit patterns are below
 // 0x7f800000).
-__global__ void bin_count_depth_kernel(const float2* __restrict__ uv,
+__global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(const float2* __restrict__ uv,
                                        const float2* __restrict__ rxy,
                                        const float* __restrict__ conic,
                                        const float* __restrict__ opacity,
@@ -331,7 +343,7 @@ __global__ void bin_count_depth_kernel(const float2* __restrict__ uv,
 // Stage B: emit every (tile, Gaussian) pair with Gaussians in depth order.
 // offsets are the exclusive scan of the counts in that order; each thread
 // writes at most its own count so a disagreement can never overrun.
-__global__ void bin_emit_kernel(const float2* __restrict__ uv,
+__global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const float2* __restrict__ uv,
                                 const float2* __restrict__ rxy,
                                 const float* __restrict__ conic,
                                 const float* __restrict__ opacity,
@@ -456,7 +468,7 @@ __global__ void bin_cutoff_kernel(const uint32_t* __restrict__ hist, int n_tiles
 
 // Saturation cut, step 3: per Gaussian, the pairs that survive the cut (its
 // count and depth key are rewritten; the emission keeps the same pairs).
-__global__ void bin_recount_kernel(const float2* __restrict__ uv,
+__global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const float2* __restrict__ uv,
                                    const float2* __restrict__ rxy,
                                    const float* __restrict__ conic,
                                    const float* __restrict__ opacity,

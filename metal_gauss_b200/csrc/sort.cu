@@ -31,7 +31,10 @@ constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kHistPrivatePasses = 4;  // per-warp histogram copies up to this many passes
 
 template <typename K> struct SortTraits;
-template <> struct SortTraits<uint32_t> { static constexpr int kItems = 16; };
+#ifndef MG_SORT_ITEMS32
+#define MG_SORT_ITEMS32 16
+#endif
+template <> struct SortTraits<uint32_t> { static constexpr int kItems = MG_SORT_ITEMS32; };
 template <> struct SortTraits<uint64_t> { static constexpr int kItems = 10; };
 
 template <typename K>
@@ -41,6 +44,10 @@ constexpr uint32_t kFlagAgg = 1u << 30;
 constexpr uint32_t kFlagInc = 2u << 30;
 constexpr uint32_t kCountMask = (1u << 30) - 1u;
 constexpr uint32_t kLookbackSpinLimit = 1u << 22;
+#ifndef MG_SORT_LOOKBACK
+#define MG_SORT_LOOKBACK 4
+#endif
+constexpr int kLookback = MG_SORT_LOOKBACK;  // predecessor words read per round trip
 
 struct SortScratch {
     uint32_t* hist;           // passes x 256: histogram, then exclusive offsets
@@ -219,24 +226,36 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     }
     sm.local_start[d] -= tile_count;
 
-    // Decoupled look-back over previous tiles for this digit.
+    // Decoupled look-back over previous tiles for this digit, kLookback
+    // predecessors per round trip (independent loads): aggregates are added
+    // up to the first inclusive prefix; a word not yet published ends the
+    // round and is read again.
     uint32_t excl = 0u;
     if (tile > 0) {
         int64_t t = (int64_t)tile - 1;
         uint32_t spins = 0u;
-        while (t >= 0) {
-            const uint32_t s = *(volatile uint32_t*)(status + t * kRadix + d);
-            const uint32_t flag = s & ~kCountMask;
-            if (flag == 0u) {
-                if (++spins > kLookbackSpinLimit) {
-                    record_device_error(err_word, DEV_ERR_SORT_LOOKBACK_TIMEOUT);
-                    break;
-                }
-                continue;
+        for (;;) {
+            uint32_t sv[kLookback];
+#pragma unroll
+            for (int k = 0; k < kLookback; ++k)  // tile 0 is inclusive: never read past it
+                sv[k] = t - k >= 0
+                            ? (uint32_t)*(volatile uint32_t*)(status + (t - k) * kRadix + d)
+                            : (uint32_t)kFlagInc;
+            int k = 0;
+            bool found = false;
+#pragma unroll
+            for (; k < kLookback; ++k) {
+                const uint32_t flag = sv[k] & ~kCountMask;
+                if (flag == 0u) break;
+                excl += sv[k] & kCountMask;
+                if (flag == kFlagInc) { found = true; break; }
             }
-            excl += s & kCountMask;
-            if (flag == kFlagInc) break;
-            --t;
+            if (found) break;
+            if (k == 0 && ++spins > kLookbackSpinLimit) {
+                record_device_error(err_word, DEV_ERR_SORT_LOOKBACK_TIMEOUT);
+                break;
+            }
+            t -= k;
         }
         atomicExch(my_status, kFlagInc | ((excl + tile_count) & kCountMask));
     }
