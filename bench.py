@@ -187,11 +187,13 @@ from metal_gauss_b200.dp import batch_indices, shard  # noqa: E402
 # ---------------------------------------------------------- algorithmic bytes
 
 def stage_bytes(stage: str, n: int, walked: float, P: int, n_tiles: int,
-                n_vis: float) -> float:
-    """Compulsory HBM bytes of one launch of a stage (per view), from the
-    dataflow: every input read once, every output written once. The
-    rasteriser only touches the list entries it walks (each tile's list up to
-    its largest stop index), so those -- not all pairs -- are counted."""
+                n_vis: float, views: int = 1) -> float:
+    """Compulsory HBM bytes of one launch of a stage, from the dataflow:
+    every input read once, every output written once. Raster, pack and loss
+    launches are per view; the two preprocess stages are one launch for the
+    `views` views of a step. The rasteriser only touches the list entries it
+    walks (each tile's list up to its largest stop index), so those -- not all
+    pairs -- are counted."""
     if stage == "raster_bwd":
         # per walked entry: id (4) + the 48-byte splat record; per pixel: T,
         # stop, alpha, rgb, dL/drgb (36); per visible Gaussian: its 48-byte
@@ -204,9 +206,12 @@ def stage_bytes(stage: str, n: int, walked: float, P: int, n_tiles: int,
     if stage == "pack":
         return (36.0 + 48.0) * n
     if stage == "preprocess_fwd":
-        return (44.0 + 192.0 + 48.0) * n
+        # parameters + SH rows once, 48 B of outputs per view, visibility RMW
+        return (44.0 + 192.0 + 8.0) * n + 48.0 * views * n
     if stage == "preprocess_bwd":
-        return (44.0 + 48.0 + 192.0 + 4.0 + 2 * 236.0) * n
+        # parameters once; per view gradient record, valid, colour, gated
+        # colour gradient; one read-modify-write of 11 gradient floats
+        return 44.0 * n + 76.0 * views * n + 88.0 * n
     if stage == "loss":
         return 40.0 * P + 36.0 * P
     if stage == "adam":
@@ -303,7 +308,7 @@ def run_ours(args, rank, world, local):
     n_tiles = math.ceil(args.width / 16) * math.ceil(args.height / 16)
     m_avg = float(np.mean(pairs)) if pairs else 0.0
     dom_ms = float(np.mean(dom_times)) if dom_times else float(np.mean(singles[dom]))
-    dom_bytes = stage_bytes(dom, n, walked, P, n_tiles, n_vis_view)
+    dom_bytes = stage_bytes(dom, n, walked, P, n_tiles, n_vis_view, B // world)
     peaks = measured_peaks()
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
     traffic, traffic_src = profiled_traffic(dom, args)

@@ -102,6 +102,22 @@ mg_status mg_preprocess_forward(
     float* uv, float* conic, float* depth, float* rxy, int32_t* valid,
     float* color, mg_stream_t stream);
 
+/* Training-engine form of mg_preprocess_forward for the views of one batch
+ * (same math per view, preprocess.metal:114-221): each Gaussian's
+ * parameters and SH rows are read once and projected and coloured for all
+ * n_views cameras `cams`. View v's outputs start at row v * view_stride
+ * (view_stride >= n) of uv, conic, depth, rxy, valid and color, laid out as
+ * in mg_preprocess_forward. With `visibility` given, the number of views in
+ * which a Gaussian is valid is ADDED to visibility[g] (float). No reference
+ * counterpart: the reference projects one camera per call. */
+mg_status mg_preprocess_forward_views(
+    const float* means, const float* quats, const float* scales,
+    const float* sh_dc, const float* sh_rest, mg_sh_layout shl,
+    const float* opacities, const mg_camera* cams, int32_t n_views,
+    int32_t sh_degree, int64_t n, int64_t view_stride, float* uv, float* conic,
+    float* depth, float* rxy, int32_t* valid, float* color, float* visibility,
+    mg_stream_t stream);
+
 /* Replaces preprocess_backward (rasterize.mm:286-327, kernel
  * preprocess.metal:223-411). The incoming gradients are read through row
  * strides (in floats) so they may point into a packed MG_G2D record
@@ -138,6 +154,22 @@ mg_status mg_preprocess_backward_accumulate(
     float* d_log_scales, float* d_logit_opac, float* d_sh_dc,
     float* d_sh_rest, const float* color, float* dpre_out,
     mg_stream_t stream);
+
+/* The projection half of mg_preprocess_backward_accumulate (deferred SH
+ * form, preprocess.metal:265-411) for the views of one batch: per Gaussian
+ * the parameters are read once and the views' adjoints are summed before
+ * they are ADDED to d_means, d_quats, d_log_scales and d_logit_opac
+ * (activation chain as in mg_preprocess_backward_accumulate). View v's
+ * grad2d records (MG_G2D_STRIDE floats), valid flags and forward colours
+ * start at row v * view_stride; dpre_out row v * view_stride + g receives
+ * view v's colour gradient gated by colour > 0, the input of
+ * mg_sh_backward_views. No reference counterpart. */
+mg_status mg_preprocess_backward_views(
+    const float* means, const float* quats, const float* scales,
+    const float* opacities, const float* grad2d, const int32_t* valid,
+    const float* color, const mg_camera* cams, int32_t n_views, int64_t n,
+    int64_t view_stride, float* d_means, float* d_quats, float* d_log_scales,
+    float* d_logit_opac, float* dpre_out, mg_stream_t stream);
 
 /* Deferred SH gradient of a batch of views, once per step. With dpre_out
  * given, mg_preprocess_backward_accumulate skips its SH branch and instead

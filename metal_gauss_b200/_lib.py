@@ -59,6 +59,10 @@ SIGNATURES = {
     "mg_preprocess_backward_accumulate": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, CAM, i32, i64,
                                                 vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "mg_sh_backward_views": (i32, [vp, vp, vp, i32, i64, vp, vp, i32, vp, vp, vp, vp]),
+    "mg_preprocess_forward_views": (i32, [vp, vp, vp, vp, vp, ShLayout, vp, vp, i32, i32, i64,
+                                          i64, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "mg_preprocess_backward_views": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i64, i64, vp,
+                                           vp, vp, vp, vp, vp]),
     "mg_bin_count": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]),
     "mg_bin_write": (i32, [vp, vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32, vp, vp,
                            vp]),

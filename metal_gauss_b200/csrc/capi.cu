@@ -167,6 +167,37 @@ extern "C" mg_status mg_preprocess_forward(const float* means, const float* quat
                                      reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" mg_status mg_preprocess_forward_views(
+    const float* means, const float* quats, const float* scales, const float* sh_dc,
+    const float* sh_rest, mg_sh_layout shl, const float* opacities, const mg_camera* cams,
+    int32_t n_views, int32_t sh_degree, int64_t n, int64_t view_stride, float* uv, float* conic,
+    float* depth, float* rxy, int32_t* valid, float* color, float* visibility,
+    mg_stream_t stream) {
+    MG_REQUIRE(n_views >= 0, "preprocess_forward_views: negative view count");
+    MG_REQUIRE(sh_degree <= 3, "preprocess_forward_views: sh_degree must be <= 3");
+    if (n == 0 || n_views == 0) return MG_OK;
+    MG_REQUIRE(cams != nullptr, "preprocess_forward_views: null cameras");
+    MG_REQUIRE(view_stride >= n, "preprocess_forward_views: view_stride below n");
+    for (int v = 0; v < n_views; ++v)
+        MG_REQUIRE(cams[v].width > 0 && cams[v].height > 0,
+                   "preprocess_forward_views: empty image");
+    MG_REQUIRE(means && quats && scales && opacities && uv && conic && depth && rxy && valid,
+               "preprocess_forward_views: null pointer");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u,
+               "preprocess_forward_views: quats must be 16-byte aligned");
+    if (sh_degree >= 0 && sh_dc != nullptr) {
+        const bool fused = shl.stride_dc == 16 && shl.stride_rest == 16 && shl.offset_rest == 1;
+        const bool split = shl.stride_dc == 1 && shl.stride_rest == 15 && shl.offset_rest == 0;
+        MG_REQUIRE(fused || split, "SH must be either one (N,16,3) tensor or (N,1,3)+(N,15,3)");
+        MG_REQUIRE(sh_rest != nullptr && color != nullptr,
+                   "preprocess_forward_views: null SH pointer");
+    }
+    return launch_preprocess_forward_views(means, quats, scales, sh_dc, sh_rest, shl, opacities,
+                                           cams, n_views, sh_degree, n, view_stride, uv, conic,
+                                           depth, rxy, valid, color, visibility,
+                                           reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" mg_status mg_bin_count(const float* uv, const float* rxy, const float* conic,
                                   const float* opacity, const int32_t* valid, int64_t n,
                                   int32_t width, int32_t height, int32_t tile, int32_t tiles_x,

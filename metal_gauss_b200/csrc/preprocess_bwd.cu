@@ -52,6 +52,136 @@ struct ShBlock {
     }
 };
 
+// Projection adjoint of one valid Gaussian for one camera (preprocess.metal:
+// 265-411): the incoming uv and conic gradients are carried through the conic
+// inverse, the EWA covariance J W Sigma W^T J^T (with the Jacobian's clamp
+// routing to zc), Sigma = R S S^T R^T and the quaternion normalisation.
+// Adds the mean gradient into dmx/dmy/dmz; returns d scales and d quat.
+__device__ __forceinline__ void projection_adjoint(const CamParams& P, float mx, float my,
+                                                   float mz, const float4 q4, const float (&s)[3],
+                                                   float dux, float duy, float dcx, float dcy,
+                                                   float dcz, float& dmx, float& dmy,
+                                                   float& dmz, float (&ds)[3], float4& dq) {
+    const float fx = P.fx, fy = P.fy;
+    const float pcx = P.R0.x * mx + P.R0.y * my + P.R0.z * mz + P.R0.w;
+    const float pcy = P.R1.x * mx + P.R1.y * my + P.R1.z * mz + P.R1.w;
+    const float pcz = P.R2.x * mx + P.R2.y * my + P.R2.z * mz + P.R2.w;
+    const float z = pcz, zc = fmaxf(z, P.near_plane);
+    const float izc = 1.0f / zc, izc2 = izc * izc;
+    const float lim_x = 1.3f * (0.5f * (float)P.W / fx);
+    const float lim_y = 1.3f * (0.5f * (float)P.H / fy);
+    const float txn = pcx / zc, tyn = pcy / zc;
+    const bool clx = (txn < -lim_x) || (txn > lim_x);
+    const bool cly = (tyn < -lim_y) || (tyn > lim_y);
+    const float tx = clampf(txn, -lim_x, lim_x) * zc;
+    const float ty = clampf(tyn, -lim_y, lim_y) * zc;
+    const float qn = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+    const float qd = fmaxf(qn, 1e-12f);
+    const float w = q4.x / qd, x = q4.y / qd, y = q4.z / qd, zq = q4.w / qd;
+    float R[3][3];
+    R[0][0] = 1.f - 2.f * (y * y + zq * zq); R[0][1] = 2.f * (x * y - w * zq); R[0][2] = 2.f * (x * zq + w * y);
+    R[1][0] = 2.f * (x * y + w * zq); R[1][1] = 1.f - 2.f * (x * x + zq * zq); R[1][2] = 2.f * (y * zq - w * x);
+    R[2][0] = 2.f * (x * zq - w * y); R[2][1] = 2.f * (y * zq + w * x); R[2][2] = 1.f - 2.f * (x * x + y * y);
+
+    float M[3][3], S[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) M[i][j] = R[i][j] * s[j];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) S[i][j] = M[i][0] * M[j][0] + M[i][1] * M[j][1] + M[i][2] * M[j][2];
+
+    const float Rw[3][3] = {{P.R0.x, P.R0.y, P.R0.z}, {P.R1.x, P.R1.y, P.R1.z},
+                            {P.R2.x, P.R2.y, P.R2.z}};
+    const float J0x = fx * izc, J0z = -fx * tx * izc2;
+    const float J1y = fy * izc, J1z = -fy * ty * izc2;
+    float T0[3], T1[3], ST0[3], ST1[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        T0[k] = J0x * Rw[0][k] + J0z * Rw[2][k];
+        T1[k] = J1y * Rw[1][k] + J1z * Rw[2][k];
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        ST0[i] = S[i][0] * T0[0] + S[i][1] * T0[1] + S[i][2] * T0[2];
+        ST1[i] = S[i][0] * T1[0] + S[i][1] * T1[1] + S[i][2] * T1[2];
+    }
+    const float a = T0[0] * ST0[0] + T0[1] * ST0[1] + T0[2] * ST0[2] + P.blur;
+    const float b = T0[0] * ST1[0] + T0[1] * ST1[1] + T0[2] * ST1[2];
+    const float c = T1[0] * ST1[0] + T1[1] * ST1[1] + T1[2] * ST1[2] + P.blur;
+    const float det = a * c - b * b;
+    const float dets = fmaxf(det, 1e-12f);
+    const float id = 1.0f / dets;
+    const float ddet = -(dcx * c - dcy * b + dcz * a) * id * id;
+    float da = dcz * id + ddet * c;
+    float db = -dcy * id - 2.0f * ddet * b;
+    float dc = dcx * id + ddet * a;
+    if (det <= 1e-12f) { da = db = dc = 0.f; }
+
+    // dSigma (unsymmetrised) = da T0 T0^T + db T0 T1^T + dc T1 T1^T
+    float dS[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+            dS[i][j] = da * T0[i] * T0[j] + db * T0[i] * T1[j] + dc * T1[i] * T1[j];
+    float dT0[3], dT1[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        dT0[k] = 2.0f * (da * ST0[k]) + db * ST1[k];
+        dT1[k] = 2.0f * (dc * ST1[k]) + db * ST0[k];
+    }
+    float dJ0[3], dJ1[3];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        dJ0[r] = dT0[0] * Rw[r][0] + dT0[1] * Rw[r][1] + dT0[2] * Rw[r][2];
+        dJ1[r] = dT1[0] * Rw[r][0] + dT1[1] * Rw[r][1] + dT1[2] * Rw[r][2];
+    }
+    const float dtx = -fx * izc2 * dJ0[2];
+    const float dty = -fy * izc2 * dJ1[2];
+    float dzc = -fx * izc2 * dJ0[0] - fy * izc2 * dJ1[1] +
+                2.0f * fx * tx * izc2 * izc * dJ0[2] + 2.0f * fy * ty * izc2 * izc * dJ1[2];
+    float dpx = fx * izc * dux;
+    float dpy = fy * izc * duy;
+    dzc += -fx * pcx * izc2 * dux - fy * pcy * izc2 * duy;
+    if (!clx) dpx += dtx; else dzc += dtx * (tx * izc);
+    if (!cly) dpy += dty; else dzc += dty * (ty * izc);
+    const float dpz = (z > P.near_plane) ? dzc : 0.0f;
+    dmx += Rw[0][0] * dpx + Rw[1][0] * dpy + Rw[2][0] * dpz;
+    dmy += Rw[0][1] * dpx + Rw[1][1] * dpy + Rw[2][1] * dpz;
+    dmz += Rw[0][2] * dpx + Rw[1][2] * dpy + Rw[2][2] * dpz;
+
+    // dM = 2 sym(dSigma) M
+    float dM[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) acc += 0.5f * (dS[i][k] + dS[k][i]) * M[k][j];
+            dM[i][j] = 2.0f * acc;
+        }
+    const float ds0 = dM[0][0] * R[0][0] + dM[1][0] * R[1][0] + dM[2][0] * R[2][0];
+    const float ds1 = dM[0][1] * R[0][1] + dM[1][1] * R[1][1] + dM[2][1] * R[2][1];
+    const float ds2 = dM[0][2] * R[0][2] + dM[1][2] * R[1][2] + dM[2][2] * R[2][2];
+    ds[0] = ds0; ds[1] = ds1; ds[2] = ds2;
+    float G[3][3];  // dL/dR
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) G[i][j] = dM[i][j] * s[j];
+    const float dw = 2.f * (x * (G[2][1] - G[1][2]) + y * (G[0][2] - G[2][0]) + zq * (G[1][0] - G[0][1]));
+    const float dqx = 2.f * (w * (G[2][1] - G[1][2]) + y * (G[1][0] + G[0][1]) + zq * (G[2][0] + G[0][2]) - 2.f * x * (G[1][1] + G[2][2]));
+    const float dqy = 2.f * (w * (G[0][2] - G[2][0]) + x * (G[1][0] + G[0][1]) + zq * (G[2][1] + G[1][2]) - 2.f * y * (G[0][0] + G[2][2]));
+    const float dqz = 2.f * (w * (G[1][0] - G[0][1]) + x * (G[2][0] + G[0][2]) + y * (G[2][1] + G[1][2]) - 2.f * zq * (G[0][0] + G[1][1]));
+    const float qdot = w * dw + x * dqx + y * dqy + zq * dqz;
+    dq = make_float4((dw - w * qdot) / qd, (dqx - x * qdot) / qd, (dqy - y * qdot) / qd,
+                     (dqz - zq * qdot) / qd);
+}
+
 // kAccum = false: the reference bridge's semantics (every output overwritten).
 // kAccum = true: the training engine's form -- gradients are ADDED, the
 // activation chain is applied (d_log_scales = d_scales * scales, d_logit =
@@ -196,141 +326,25 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
 
     // --------------------------------------------------- projection branch
     if (valid[g] != 0) {
-        const float fx = P.fx, fy = P.fy;
-        const float pcx = P.R0.x * mx + P.R0.y * my + P.R0.z * mz + P.R0.w;
-        const float pcy = P.R1.x * mx + P.R1.y * my + P.R1.z * mz + P.R1.w;
-        const float pcz = P.R2.x * mx + P.R2.y * my + P.R2.z * mz + P.R2.w;
-        const float z = pcz, zc = fmaxf(z, P.near_plane);
-        const float izc = 1.0f / zc, izc2 = izc * izc;
-        const float lim_x = 1.3f * (0.5f * (float)P.W / fx);
-        const float lim_y = 1.3f * (0.5f * (float)P.H / fy);
-        const float txn = pcx / zc, tyn = pcy / zc;
-        const bool clx = (txn < -lim_x) || (txn > lim_x);
-        const bool cly = (tyn < -lim_y) || (tyn > lim_y);
-        const float tx = clampf(txn, -lim_x, lim_x) * zc;
-        const float ty = clampf(tyn, -lim_y, lim_y) * zc;
-
         const float4 q4 = reinterpret_cast<const float4*>(quats)[g];
-        const float qn = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
-        const float qd = fmaxf(qn, 1e-12f);
-        const float w = q4.x / qd, x = q4.y / qd, y = q4.z / qd, zq = q4.w / qd;
-        float R[3][3];
-        R[0][0] = 1.f - 2.f * (y * y + zq * zq); R[0][1] = 2.f * (x * y - w * zq); R[0][2] = 2.f * (x * zq + w * y);
-        R[1][0] = 2.f * (x * y + w * zq); R[1][1] = 1.f - 2.f * (x * x + zq * zq); R[1][2] = 2.f * (y * zq - w * x);
-        R[2][0] = 2.f * (x * zq - w * y); R[2][1] = 2.f * (y * zq + w * x); R[2][2] = 1.f - 2.f * (x * x + y * y);
         const float s[3] = {scales[3 * g], scales[3 * g + 1], scales[3 * g + 2]};
-        float M[3][3], S[3][3];
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-            for (int j = 0; j < 3; ++j) M[i][j] = R[i][j] * s[j];
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-            for (int j = 0; j < 3; ++j) S[i][j] = M[i][0] * M[j][0] + M[i][1] * M[j][1] + M[i][2] * M[j][2];
-
-        const float Rw[3][3] = {{P.R0.x, P.R0.y, P.R0.z}, {P.R1.x, P.R1.y, P.R1.z},
-                                {P.R2.x, P.R2.y, P.R2.z}};
-        const float J0x = fx * izc, J0z = -fx * tx * izc2;
-        const float J1y = fy * izc, J1z = -fy * ty * izc2;
-        float T0[3], T1[3], ST0[3], ST1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            T0[k] = J0x * Rw[0][k] + J0z * Rw[2][k];
-            T1[k] = J1y * Rw[1][k] + J1z * Rw[2][k];
-        }
-#pragma unroll
-        for (int i = 0; i < 3; ++i) {
-            ST0[i] = S[i][0] * T0[0] + S[i][1] * T0[1] + S[i][2] * T0[2];
-            ST1[i] = S[i][0] * T1[0] + S[i][1] * T1[1] + S[i][2] * T1[2];
-        }
-        const float a = T0[0] * ST0[0] + T0[1] * ST0[1] + T0[2] * ST0[2] + P.blur;
-        const float b = T0[0] * ST1[0] + T0[1] * ST1[1] + T0[2] * ST1[2];
-        const float c = T1[0] * ST1[0] + T1[1] * ST1[1] + T1[2] * ST1[2] + P.blur;
-        const float det = a * c - b * b;
-        const float dets = fmaxf(det, 1e-12f);
-        const float id = 1.0f / dets;
-
-        const float dcx = d_conic[g * d_conic_stride];
-        const float dcy = d_conic[g * d_conic_stride + 1];
-        const float dcz = d_conic[g * d_conic_stride + 2];
-        const float ddet = -(dcx * c - dcy * b + dcz * a) * id * id;
-        float da = dcz * id + ddet * c;
-        float db = -dcy * id - 2.0f * ddet * b;
-        float dc = dcx * id + ddet * a;
-        if (det <= 1e-12f) { da = db = dc = 0.f; }
-
-        // dSigma (unsymmetrised) = da T0 T0^T + db T0 T1^T + dc T1 T1^T
-        float dS[3][3];
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-            for (int j = 0; j < 3; ++j)
-                dS[i][j] = da * T0[i] * T0[j] + db * T0[i] * T1[j] + dc * T1[i] * T1[j];
-        float dT0[3], dT1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            dT0[k] = 2.0f * (da * ST0[k]) + db * ST1[k];
-            dT1[k] = 2.0f * (dc * ST1[k]) + db * ST0[k];
-        }
-        float dJ0[3], dJ1[3];
-#pragma unroll
-        for (int r = 0; r < 3; ++r) {
-            dJ0[r] = dT0[0] * Rw[r][0] + dT0[1] * Rw[r][1] + dT0[2] * Rw[r][2];
-            dJ1[r] = dT1[0] * Rw[r][0] + dT1[1] * Rw[r][1] + dT1[2] * Rw[r][2];
-        }
-        const float dtx = -fx * izc2 * dJ0[2];
-        const float dty = -fy * izc2 * dJ1[2];
-        float dzc = -fx * izc2 * dJ0[0] - fy * izc2 * dJ1[1] +
-                    2.0f * fx * tx * izc2 * izc * dJ0[2] + 2.0f * fy * ty * izc2 * izc * dJ1[2];
-        const float dux = d_uv[g * d_uv_stride], duy = d_uv[g * d_uv_stride + 1];
-        float dpx = fx * izc * dux;
-        float dpy = fy * izc * duy;
-        dzc += -fx * pcx * izc2 * dux - fy * pcy * izc2 * duy;
-        if (!clx) dpx += dtx; else dzc += dtx * (tx * izc);
-        if (!cly) dpy += dty; else dzc += dty * (ty * izc);
-        const float dpz = (z > P.near_plane) ? dzc : 0.0f;
-        dmx += Rw[0][0] * dpx + Rw[1][0] * dpy + Rw[2][0] * dpz;
-        dmy += Rw[0][1] * dpx + Rw[1][1] * dpy + Rw[2][1] * dpz;
-        dmz += Rw[0][2] * dpx + Rw[1][2] * dpy + Rw[2][2] * dpz;
-
-        // dM = 2 sym(dSigma) M
-        float dM[3][3];
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                float acc = 0.f;
-#pragma unroll
-                for (int k = 0; k < 3; ++k) acc += 0.5f * (dS[i][k] + dS[k][i]) * M[k][j];
-                dM[i][j] = 2.0f * acc;
-            }
-        const float ds0 = dM[0][0] * R[0][0] + dM[1][0] * R[1][0] + dM[2][0] * R[2][0];
-        const float ds1 = dM[0][1] * R[0][1] + dM[1][1] * R[1][1] + dM[2][1] * R[2][1];
-        const float ds2 = dM[0][2] * R[0][2] + dM[1][2] * R[1][2] + dM[2][2] * R[2][2];
+        float ds[3];
+        float4 dq;
+        projection_adjoint(P, mx, my, mz, q4, s, d_uv[g * d_uv_stride],
+                           d_uv[g * d_uv_stride + 1], d_conic[g * d_conic_stride],
+                           d_conic[g * d_conic_stride + 1], d_conic[g * d_conic_stride + 2],
+                           dmx, dmy, dmz, ds, dq);
         if (kAccum) {  // d log s = d s * s
-            d_scales[3 * g + 0] += ds0 * s[0];
-            d_scales[3 * g + 1] += ds1 * s[1];
-            d_scales[3 * g + 2] += ds2 * s[2];
+            d_scales[3 * g + 0] += ds[0] * s[0];
+            d_scales[3 * g + 1] += ds[1] * s[1];
+            d_scales[3 * g + 2] += ds[2] * s[2];
             const float op = opac[g];
             d_logit[g] += d_opac[g * d_opac_stride] * (op * (1.0f - op));
         } else {
-            d_scales[3 * g + 0] = ds0;
-            d_scales[3 * g + 1] = ds1;
-            d_scales[3 * g + 2] = ds2;
+            d_scales[3 * g + 0] = ds[0];
+            d_scales[3 * g + 1] = ds[1];
+            d_scales[3 * g + 2] = ds[2];
         }
-        float G[3][3];  // dL/dR
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-            for (int j = 0; j < 3; ++j) G[i][j] = dM[i][j] * s[j];
-        const float dw = 2.f * (x * (G[2][1] - G[1][2]) + y * (G[0][2] - G[2][0]) + zq * (G[1][0] - G[0][1]));
-        const float dqx = 2.f * (w * (G[2][1] - G[1][2]) + y * (G[1][0] + G[0][1]) + zq * (G[2][0] + G[0][2]) - 2.f * x * (G[1][1] + G[2][2]));
-        const float dqy = 2.f * (w * (G[0][2] - G[2][0]) + x * (G[1][0] + G[0][1]) + zq * (G[2][1] + G[1][2]) - 2.f * y * (G[0][0] + G[2][2]));
-        const float dqz = 2.f * (w * (G[1][0] - G[0][1]) + x * (G[2][0] + G[0][2]) + y * (G[2][1] + G[1][2]) - 2.f * zq * (G[0][0] + G[1][1]));
-        const float qdot = w * dw + x * dqx + y * dqy + zq * dqz;
-        const float4 dq = make_float4((dw - w * qdot) / qd, (dqx - x * qdot) / qd,
-                                      (dqy - y * qdot) / qd, (dqz - zq * qdot) / qd);
         float4* dqp = reinterpret_cast<float4*>(d_quats) + g;
         if (kAccum) {
             const float4 o = *dqp;
@@ -353,6 +367,70 @@ preprocess_backward_kernel(const float* __restrict__ means, const float* __restr
         d_means[3 * g + 1] = dmy;
         d_means[3 * g + 2] = dmz;
     }
+}
+
+constexpr int kMaxViewsPerLaunch = 16;
+struct ViewCams {
+    CamParams c[kMaxViewsPerLaunch];
+};
+
+// The projection half of preprocess_backward_kernel<true> (deferred SH) for
+// several cameras at once: a Gaussian's parameters are read once, its
+// per-view adjoints are summed in registers in view order and added into the
+// gradient rows once, and each view's ReLU-gated colour gradient goes to
+// dpre[v * view_stride + g] for sh_backward_views_kernel. View v's grad2d
+// records, valid flags and forward colours start at v * view_stride rows.
+__global__ void __launch_bounds__(kBwdBlock)
+preprocess_backward_views_kernel(const float* __restrict__ means,
+                                 const float* __restrict__ quats,
+                                 const float* __restrict__ scales,
+                                 const float* __restrict__ opac,
+                                 const float* __restrict__ grad2d,
+                                 const int32_t* __restrict__ valid,
+                                 const float* __restrict__ color, ViewCams cams, int n_views,
+                                 int64_t n, int64_t view_stride, float* __restrict__ d_means,
+                                 float* __restrict__ d_quats, float* __restrict__ d_log_scales,
+                                 float* __restrict__ d_logit, float* __restrict__ dpre) {
+    const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
+    if (g >= n) return;
+    const float mx = means[3 * g], my = means[3 * g + 1], mz = means[3 * g + 2];
+    const float4 q4 = reinterpret_cast<const float4*>(quats)[g];
+    const float s[3] = {scales[3 * g], scales[3 * g + 1], scales[3 * g + 2]};
+    const float op = opac[g];
+    float dmx = 0.f, dmy = 0.f, dmz = 0.f, dl = 0.f;
+    float dls[3] = {0.f, 0.f, 0.f};
+    float4 dqa = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool any = false;
+    for (int v = 0; v < n_views; ++v) {
+        const int64_t o = (int64_t)v * view_stride + g;
+        const float* r = grad2d + o * MG_G2D_STRIDE;
+        dpre[3 * o + 0] = color[3 * o + 0] > 0.f ? r[MG_G2D_COLOR + 0] : 0.f;
+        dpre[3 * o + 1] = color[3 * o + 1] > 0.f ? r[MG_G2D_COLOR + 1] : 0.f;
+        dpre[3 * o + 2] = color[3 * o + 2] > 0.f ? r[MG_G2D_COLOR + 2] : 0.f;
+        if (valid[o] == 0) continue;
+        float ds[3];
+        float4 dq;
+        projection_adjoint(cams.c[v], mx, my, mz, q4, s, r[MG_G2D_UV], r[MG_G2D_UV + 1],
+                           r[MG_G2D_CONIC], r[MG_G2D_CONIC + 1], r[MG_G2D_CONIC + 2], dmx, dmy,
+                           dmz, ds, dq);
+        dls[0] += ds[0] * s[0];
+        dls[1] += ds[1] * s[1];
+        dls[2] += ds[2] * s[2];
+        dl += r[MG_G2D_OPACITY] * (op * (1.0f - op));
+        dqa = make_float4(dqa.x + dq.x, dqa.y + dq.y, dqa.z + dq.z, dqa.w + dq.w);
+        any = true;
+    }
+    if (!any) return;
+    d_means[3 * g + 0] += dmx;
+    d_means[3 * g + 1] += dmy;
+    d_means[3 * g + 2] += dmz;
+    float4* dqp = reinterpret_cast<float4*>(d_quats) + g;
+    const float4 oq = *dqp;
+    *dqp = make_float4(oq.x + dqa.x, oq.y + dqa.y, oq.z + dqa.z, oq.w + dqa.w);
+    d_log_scales[3 * g + 0] += dls[0];
+    d_log_scales[3 * g + 1] += dls[1];
+    d_log_scales[3 * g + 2] += dls[2];
+    d_logit[g] += dl;
 }
 
 constexpr int kMaxViews = 64;
@@ -505,6 +583,36 @@ extern "C" mg_status mg_preprocess_backward_accumulate(
         with_sh ? sh_degree : -1, n, d_means, d_quats, d_log_scales, d_sh_dc, d_sh_rest, 0, 1,
         opacities, grad2d + MG_G2D_OPACITY, MG_G2D_STRIDE, d_logit_opac, color, dpre_out);
     return check_launch("preprocess_backward_accumulate");
+}
+
+extern "C" mg_status mg_preprocess_backward_views(
+    const float* means, const float* quats, const float* scales, const float* opacities,
+    const float* grad2d, const int32_t* valid, const float* color, const mg_camera* cams,
+    int32_t n_views, int64_t n, int64_t view_stride, float* d_means, float* d_quats,
+    float* d_log_scales, float* d_logit_opac, float* dpre_out, mg_stream_t stream) {
+    MG_REQUIRE(n_views >= 0, "preprocess_backward_views: negative view count");
+    if (n == 0 || n_views == 0) return MG_OK;
+    MG_REQUIRE(cams != nullptr, "preprocess_backward_views: null cameras");
+    MG_REQUIRE(view_stride >= n, "preprocess_backward_views: view_stride below n");
+    MG_REQUIRE(means && quats && scales && opacities && grad2d && valid && color && d_means &&
+                   d_quats && d_log_scales && d_logit_opac && dpre_out,
+               "preprocess_backward_views: null pointer");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(d_quats) & 15u) == 0u,
+               "preprocess_backward_views: quats must be 16-byte aligned");
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    for (int v0 = 0; v0 < n_views; v0 += kMaxViewsPerLaunch) {
+        const int nv = n_views - v0 < kMaxViewsPerLaunch ? n_views - v0 : kMaxViewsPerLaunch;
+        ViewCams vc;
+        for (int k = 0; k < nv; ++k) vc.c[k] = make_cam_params(cams[v0 + k]);
+        const int64_t o = (int64_t)v0 * view_stride;
+        preprocess_backward_views_kernel<<<ceil_div(n, kBwdBlock), kBwdBlock, 0, st>>>(
+            means, quats, scales, opacities, grad2d + o * MG_G2D_STRIDE, valid + o,
+            color + 3 * o, vc, nv, n, view_stride, d_means, d_quats, d_log_scales,
+            d_logit_opac, dpre_out + 3 * o);
+        MG_TRY(check_launch("preprocess_backward_views"));
+    }
+    return MG_OK;
 }
 
 extern "C" mg_status mg_sh_backward_views(const float* means, const float* sh_dc,

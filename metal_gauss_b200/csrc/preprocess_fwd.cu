@@ -40,6 +40,32 @@ __device__ __forceinline__ void stage_rows(const float* __restrict__ src,
     }
 }
 
+// SH colour of one Gaussian seen along (dvx, dvy, dvz) (mean minus camera
+// centre): DC row from global memory, rows 1.. from the warp's staged block,
+// +0.5 and the clamp at 0 (preprocess.metal:203-221).
+__device__ __forceinline__ float3 sh_colour(int sh_degree, int nb, float dvx, float dvy,
+                                            float dvz, const float* __restrict__ dc,
+                                            const float* rest) {
+    const float len = sqrtf((dvx * dvx + dvy * dvy) + dvz * dvz);
+    const float invn = 1.0f / fmaxf(len, 1e-12f);
+    float B[16];
+    sh_basis(sh_degree, dvx * invn, dvy * invn, dvz * invn, B);
+    float r = 0.0f, gg = 0.0f, bb = 0.0f;
+    r = r + B[0] * dc[0];
+    gg = gg + B[0] * dc[1];
+    bb = bb + B[0] * dc[2];
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+        if (i < nb) {
+            r = r + B[i] * rest[(i - 1) * 3 + 0];
+            gg = gg + B[i] * rest[(i - 1) * 3 + 1];
+            bb = bb + B[i] * rest[(i - 1) * 3 + 2];
+        }
+    }
+    r = r + 0.5f; gg = gg + 0.5f; bb = bb + 0.5f;
+    return make_float3(fmaxf(r, 0.0f), fmaxf(gg, 0.0f), fmaxf(bb, 0.0f));
+}
+
 __global__ void __launch_bounds__(kPreBlock)
 preprocess_forward_kernel(const float* __restrict__ means,
                           const float* __restrict__ quats,
@@ -94,29 +120,89 @@ preprocess_forward_kernel(const float* __restrict__ means,
         out_color[3 * g + 2] = 0.0f;
         return;
     }
-    const float dvx = mx - P.ccx, dvy = my - P.ccy, dvz = mz - P.ccz;
-    const float len = sqrtf((dvx * dvx + dvy * dvy) + dvz * dvz);
-    const float invn = 1.0f / fmaxf(len, 1e-12f);
-    float B[16];
-    sh_basis(sh_degree, dvx * invn, dvy * invn, dvz * invn, B);
-    const float* dc = sh_dc + g * (int64_t)shl.stride_dc * 3;
-    float r = 0.0f, gg = 0.0f, bb = 0.0f;
-    r = r + B[0] * dc[0];
-    gg = gg + B[0] * dc[1];
-    bb = bb + B[0] * dc[2];
-    const float* rest = s_rest[wib] + lane * (nb - 1) * 3;
-#pragma unroll
-    for (int i = 1; i < 16; ++i) {
-        if (i < nb) {
-            r = r + B[i] * rest[(i - 1) * 3 + 0];
-            gg = gg + B[i] * rest[(i - 1) * 3 + 1];
-            bb = bb + B[i] * rest[(i - 1) * 3 + 2];
-        }
+    const float3 col = sh_colour(sh_degree, nb, mx - P.ccx, my - P.ccy, mz - P.ccz,
+                                 sh_dc + g * (int64_t)shl.stride_dc * 3,
+                                 s_rest[wib] + lane * (nb - 1) * 3);
+    out_color[3 * g + 0] = col.x;
+    out_color[3 * g + 1] = col.y;
+    out_color[3 * g + 2] = col.z;
+}
+
+constexpr int kMaxViewsPerLaunch = 16;
+struct ViewCams {
+    CamParams c[kMaxViewsPerLaunch];
+};
+
+// preprocess_forward_kernel for several cameras at once: a Gaussian's
+// parameters and SH rows are read (and staged) once and projected and
+// coloured for every view; view v's outputs start at v * view_stride. With
+// `vis` given, each Gaussian's count of views where it is valid is added to
+// vis[g]. Per view the arithmetic is that of the single-view kernel.
+__global__ void __launch_bounds__(kPreBlock)
+preprocess_forward_views_kernel(const float* __restrict__ means,
+                                const float* __restrict__ quats,
+                                const float* __restrict__ scales,
+                                const float* __restrict__ sh_dc,
+                                const float* __restrict__ sh_rest, mg_sh_layout shl,
+                                const float* __restrict__ opacities, ViewCams cams,
+                                int n_views, int sh_degree, int64_t n, int64_t view_stride,
+                                float2* __restrict__ out_uv, float* __restrict__ out_conic,
+                                float* __restrict__ out_depth, float2* __restrict__ out_rxy,
+                                int32_t* __restrict__ out_valid,
+                                float* __restrict__ out_color, float* __restrict__ vis) {
+    __shared__ float s_rest[kPreBlock / 32][32 * 15 * 3];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t g = (int64_t)blockIdx.x * kPreBlock + threadIdx.x;
+    const int64_t g0 = g - lane;
+    const bool in = g < n;
+    const bool colour = sh_degree >= 0 && sh_dc != nullptr;
+    const int nb = (sh_degree + 1) * (sh_degree + 1);
+
+    float mx = 0.f, my = 0.f, mz = 0.f, sx = 0.f, sy = 0.f, sz = 0.f, op = 0.f;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (in) {
+        mx = means[3 * g + 0]; my = means[3 * g + 1]; mz = means[3 * g + 2];
+        q = __ldg(reinterpret_cast<const float4*>(quats) + g);
+        sx = scales[3 * g + 0]; sy = scales[3 * g + 1]; sz = scales[3 * g + 2];
+        op = opacities[g];
     }
-    r = r + 0.5f; gg = gg + 0.5f; bb = bb + 0.5f;
-    out_color[3 * g + 0] = fmaxf(r, 0.0f);
-    out_color[3 * g + 1] = fmaxf(gg, 0.0f);
-    out_color[3 * g + 2] = fmaxf(bb, 0.0f);
+    bool staged = false;  // warp-uniform: the SH rows are staged at first use
+    int visible = 0;
+    for (int v = 0; v < n_views; ++v) {
+        const CamParams& P = cams.c[v];
+        const int64_t o = (int64_t)v * view_stride + g;
+        Projected pr;
+        pr.ok = false;
+        if (in) {
+            pr = project_one(P, mx, my, mz, q.x, q.y, q.z, q.w, sx, sy, sz, op);
+            out_uv[o] = make_float2(pr.u, pr.v);
+            out_conic[3 * o + 0] = pr.ca;
+            out_conic[3 * o + 1] = pr.cb;
+            out_conic[3 * o + 2] = pr.cc;
+            out_depth[o] = pr.z;
+            out_rxy[o] = make_float2(pr.rx, pr.ry);
+            out_valid[o] = pr.ok ? 1 : 0;
+            visible += pr.ok ? 1 : 0;
+        }
+        if (!colour) continue;
+        const unsigned any_ok = __ballot_sync(0xffffffffu, in && pr.ok);
+        if (!staged && any_ok != 0u && nb > 1) {
+            stage_rows(sh_rest, g0, n, shl.stride_rest, shl.offset_rest, nb - 1, s_rest[wib],
+                       lane);
+            __syncwarp();
+            staged = true;
+        }
+        if (!in) continue;
+        float3 col = make_float3(0.f, 0.f, 0.f);
+        if (pr.ok)
+            col = sh_colour(sh_degree, nb, mx - P.ccx, my - P.ccy, mz - P.ccz,
+                            sh_dc + g * (int64_t)shl.stride_dc * 3,
+                            s_rest[wib] + lane * (nb - 1) * 3);
+        out_color[3 * o + 0] = col.x;
+        out_color[3 * o + 1] = col.y;
+        out_color[3 * o + 2] = col.z;
+    }
+    if (vis != nullptr && in && visible > 0) vis[g] += (float)visible;
 }
 
 // Walk the Gaussian's clamped tile rectangle row-major and count (or emit)
@@ -525,6 +611,30 @@ mg_status launch_preprocess_forward(const float* means, const float* quats,
         reinterpret_cast<float2*>(uv), conic, depth, reinterpret_cast<float2*>(rxy),
         valid, color);
     return check_launch("preprocess_forward");
+}
+
+mg_status launch_preprocess_forward_views(const float* means, const float* quats,
+                                          const float* scales, const float* sh_dc,
+                                          const float* sh_rest, mg_sh_layout shl,
+                                          const float* opacities, const mg_camera* cams,
+                                          int n_views, int sh_degree, int64_t n,
+                                          int64_t view_stride, float* uv, float* conic,
+                                          float* depth, float* rxy, int32_t* valid,
+                                          float* color, float* vis, cudaStream_t stream) {
+    if (n == 0) return MG_OK;
+    for (int v0 = 0; v0 < n_views; v0 += kMaxViewsPerLaunch) {
+        const int nv = std::min(kMaxViewsPerLaunch, n_views - v0);
+        ViewCams vc;
+        for (int k = 0; k < nv; ++k) vc.c[k] = make_cam_params(cams[v0 + k]);
+        const int64_t o = (int64_t)v0 * view_stride;
+        preprocess_forward_views_kernel<<<ceil_div(n, kPreBlock), kPreBlock, 0, stream>>>(
+            means, quats, scales, sh_dc, sh_rest, shl, opacities, vc, nv, sh_degree, n,
+            view_stride, reinterpret_cast<float2*>(uv) + o, conic + 3 * o, depth + o,
+            reinterpret_cast<float2*>(rxy) + o, valid + o, color ? color + 3 * o : nullptr,
+            vis);
+        MG_TRY(check_launch("preprocess_forward_views"));
+    }
+    return MG_OK;
 }
 
 mg_status launch_bin_count(const float* uv, const float* rxy, const float* conic,

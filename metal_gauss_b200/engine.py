@@ -59,7 +59,6 @@ class _ImageBuffers:
 
     def __init__(self, n: int, W: int, H: int, device):
         f32 = dict(dtype=torch.float32, device=device)
-        self.grad2d = torch.empty(n, G2D_STRIDE, **f32)
         self.rgb = torch.empty(H, W, 3, **f32)
         self.alpha = torch.empty(H, W, **f32)
         self.T = torch.empty(H, W, **f32)
@@ -75,26 +74,48 @@ class _ImageBuffers:
         self.emit = torch.empty(0, dtype=torch.uint8, device=device)
 
 
-class _ViewState:
-    """Per-view projection outputs and binning scratch, alive from phase A
-    (projection + binning preparation of every view) to phase B."""
+class _ViewBatch:
+    """View-major projection outputs (and, for training, raster gradient
+    records and gated colour gradients) of up to `cap` views: row v * n + g
+    belongs to Gaussian g in view v, so one multi-view launch fills or reads
+    every view of a batch."""
 
-    def __init__(self, n: int, device):
+    def __init__(self, n: int, cap: int, device, grads: bool = True):
         f32 = dict(dtype=torch.float32, device=device)
-        self.uv = torch.empty(n, 2, **f32)
-        self.conic = torch.empty(n, 3, **f32)
-        self.depth = torch.empty(n, **f32)
-        self.rxy = torch.empty(n, 2, **f32)
-        self.valid = torch.empty(n, dtype=torch.int32, device=device)
-        self.color = torch.empty(n, 3, **f32)
-        self.n = n
+        self.n, self.cap = n, cap
+        self.uv = torch.empty(cap, n, 2, **f32)
+        self.conic = torch.empty(cap, n, 3, **f32)
+        self.depth = torch.empty(cap, n, **f32)
+        self.rxy = torch.empty(cap, n, 2, **f32)
+        self.valid = torch.empty(cap, n, dtype=torch.int32, device=device)
+        self.color = torch.empty(cap, n, 3, **f32)
+        self.grad2d = torch.empty(cap, n, G2D_STRIDE, **f32) if grads else None
+        self.dpre = torch.empty(cap, n, 3, **f32) if grads else None
+
+
+class _ViewState:
+    """View v's slice of a _ViewBatch plus its binning scratch, alive from
+    phase A (projection + binning preparation of every view) to phase B."""
+
+    def __init__(self, batch: _ViewBatch, v: int, device):
+        self.n = batch.n
         self.prep = torch.empty(0, dtype=torch.uint8, device=device)
+        self.bind(batch, v)
+
+    def bind(self, batch: _ViewBatch, v: int) -> None:
+        self.uv, self.conic, self.depth = batch.uv[v], batch.conic[v], batch.depth[v]
+        self.rxy, self.valid, self.color = batch.rxy[v], batch.valid[v], batch.color[v]
+        self.grad2d = None if batch.grad2d is None else batch.grad2d[v]
 
     def prep_scratch(self, n_tiles: int) -> torch.Tensor:
         nbytes = _lib.load().mg_bin_prepare_scratch_bytes(self.n, n_tiles)
         if self.prep.numel() < nbytes:
             self.prep = torch.empty(nbytes, dtype=torch.uint8, device=self.prep.device)
         return self.prep
+
+
+def _views_array(cams: list) -> "_lib.C.Array":
+    return (_lib.Camera * len(cams))(*cams)
 
 
 class Trainer:
@@ -163,9 +184,8 @@ class Trainer:
         w = torch.exp(-x ** 2 / (2 * 1.5 ** 2))
         self.window.copy_(w / w.sum())
         self._bufs: dict[tuple[int, int], _ImageBuffers] = {}
+        self._batch: _ViewBatch | None = None
         self._states: list[_ViewState] = []
-        # per-view ReLU-gated colour gradients for the deferred SH pass
-        self._dpre = torch.empty(0, dtype=torch.float32, device=self.device)
         self._totals = torch.zeros(64, dtype=torch.int64, device=self.device)
         self._cams: dict[int, _lib.Camera] = {}
         self.last_stats: list[ViewStats] = []
@@ -259,26 +279,39 @@ class Trainer:
             self._bufs[(W, H)] = b
         return b
 
+    def _ensure_views(self, V: int) -> None:
+        """View-major buffers for V views (grown, never shrunk)."""
+        if self._batch is None or self._batch.cap < V:
+            self._batch = _ViewBatch(self.n, V, self.device)
+            for v, st in enumerate(self._states):
+                st.bind(self._batch, v)
+        while len(self._states) < V:
+            self._states.append(_ViewState(self._batch, len(self._states), self.device))
+
     def _state(self, v: int) -> _ViewState:
-        while len(self._states) <= v:
-            self._states.append(_ViewState(self.n, self.device))
         return self._states[v]
 
-    def _project_and_prepare(self, v: int, view) -> None:
-        """Phase A for view v: projection + SH colour, visibility count, tile
-        counts, depth sort and the scan that yields the view's pair total."""
+    def _project_views(self, views) -> None:
+        """Phase A, first half: projection + SH colour of every view in one
+        launch (parameters and SH rows read once), adding each Gaussian's
+        count of valid views to the visibility count."""
+        b = self._batch
+        cams = _views_array([self._camera(view) for view in views])
+        ev = self._begin("preprocess_fwd")
+        _lib.call("mg_preprocess_forward_views", ptr(self.param("means")),
+                  ptr(self.param("quats")), ptr(self.scales), ptr(self.param("sh_dc")),
+                  ptr(self.param("sh_rest")), _lib.SH_SPLIT, ptr(self.opac),
+                  _lib.C.cast(cams, _lib.C.c_void_p), len(views), self.sh_degree, self.n, self.n,
+                  ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color),
+                  ptr(self.visibility_count()), _lib.stream())
+        self._end(ev)
+
+    def _prepare(self, v: int, view) -> None:
+        """Phase A, second half, for view v: tile counts, depth sort and the
+        scan that yields the view's pair total."""
         L = _lib.load()
         s = _lib.stream()
         st = self._state(v)
-        cam = self._camera(view)
-        ev = self._begin("preprocess_fwd")
-        _lib.check(L.mg_preprocess_forward(
-            ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales),
-            ptr(self.param("sh_dc")), ptr(self.param("sh_rest")), _lib.SH_SPLIT, ptr(self.opac),
-            _lib.C.byref(cam), self.sh_degree, self.n, ptr(st.uv), ptr(st.conic), ptr(st.depth),
-            ptr(st.rxy), ptr(st.valid), ptr(st.color), s), "preprocess_forward")
-        self.visibility_count().add_(st.valid)
-        self._end(ev)
         ev = self._begin("bin_prepare")
         prep = st.prep_scratch(-(-view.width // self.tile) * -(-view.height // self.tile))
         _lib.check(L.mg_bin_prepare(
@@ -290,14 +323,13 @@ class Trainer:
     def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
                              scale: float) -> ViewStats:
         """Phase B for view v (its pair total m known on the host): pair
-        emission and tile sort, raster forward, fused loss, raster backward,
-        and the preprocess backward that adds into the flat gradient."""
+        emission and tile sort, raster forward, fused loss and raster
+        backward into the view's gradient records."""
         L = _lib.load()
         s = _lib.stream()
         W, H, n = view.width, view.height, self.n
         st = self._state(v)
         b = self._buffers(W, H)
-        cam = self._camera(view)
         tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
         n_tiles = tiles_x * tiles_y
         if b.ids.numel() < max(m, 1):
@@ -339,22 +371,13 @@ class Trainer:
             ptr(b.rgb), ptr(target), ptr(self.window), H, W, self.w_l1, self.w_ssim, scale,
             ptr(b.grad_rgb), ptr(self.loss), ptr(b.loss_scratch), b.loss_scratch.numel(), s),
             "l1_ssim_loss")
-        b.grad2d.zero_()
+        st.grad2d.zero_()
         self._end(ev)
         ev = self._begin("raster_bwd")
         _lib.check(L.mg_rasterize_backward(
             ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, ptr(b.rgb), ptr(b.alpha), ptr(b.T),
             ptr(b.stop), ptr(b.grad_rgb), None, W, H, self.tile, tiles_x, bgp, 0, n,
-            ptr(b.grad2d), 1, ptr(b.raster), b.raster.numel(), s), "rasterize_backward")
-        self._end(ev)
-        ev = self._begin("preprocess_bwd")
-        _lib.check(L.mg_preprocess_backward_accumulate(
-            ptr(self.param("means")), ptr(self.param("quats")), ptr(self.scales), ptr(self.opac),
-            ptr(self.param("sh_dc")), ptr(self.param("sh_rest")), ptr(b.grad2d), ptr(st.valid),
-            _lib.C.byref(cam), self.sh_degree, n, ptr(self.grad("means")),
-            ptr(self.grad("quats")), ptr(self.grad("log_scales")), ptr(self.grad("logit_opac")),
-            ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")), ptr(st.color),
-            ptr(self._dpre[v]), s), "preprocess_backward_accumulate")
+            ptr(st.grad2d), 1, ptr(b.raster), b.raster.numel(), s), "rasterize_backward")
         self._end(ev)
         return ViewStats(pairs=m)
 
@@ -365,15 +388,25 @@ class Trainer:
         V = len(views)
         if V > self._totals.numel():
             self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
-        if self._dpre.shape[:1] != (V,) or self._dpre.numel() != V * self.n * 3:
-            self._dpre = torch.empty(V, self.n, 3, dtype=torch.float32, device=self.device)
+        self._ensure_views(V)
+        self._project_views(views)
         for v, view in enumerate(views):
-            self._project_and_prepare(v, view)
+            self._prepare(v, view)
         totals = self._totals[:V].tolist()
         stats = [self._render_and_backprop(v, view, t, int(m), scale)
                  for v, (view, t, m) in enumerate(zip(views, targets, totals))]
-        # the SH adjoint of all views at once: coefficients read once, gradient
-        # rows written once
+        # the projection adjoint of all views at once (parameters read and
+        # gradient rows updated once), then the SH adjoint likewise
+        b = self._batch
+        cams = _views_array([self._camera(view) for view in views])
+        ev = self._begin("preprocess_bwd")
+        _lib.call("mg_preprocess_backward_views", ptr(self.param("means")),
+                  ptr(self.param("quats")), ptr(self.scales), ptr(self.opac), ptr(b.grad2d),
+                  ptr(b.valid), ptr(b.color), _lib.C.cast(cams, _lib.C.c_void_p), V, self.n,
+                  self.n, ptr(self.grad("means")), ptr(self.grad("quats")),
+                  ptr(self.grad("log_scales")), ptr(self.grad("logit_opac")), ptr(b.dpre),
+                  _lib.stream())
+        self._end(ev)
         centres = (_lib.C.c_float * (3 * V))()
         for v, view in enumerate(views):
             cc = self._camera(view).cam_center
@@ -381,7 +414,7 @@ class Trainer:
         ev = self._begin("sh_bwd")
         _lib.call("mg_sh_backward_views", ptr(self.param("means")), ptr(self.param("sh_dc")),
                   ptr(self.param("sh_rest")), self.sh_degree, self.n,
-                  _lib.C.cast(centres, _lib.C.c_void_p), ptr(self._dpre), V,
+                  _lib.C.cast(centres, _lib.C.c_void_p), ptr(b.dpre), V,
                   ptr(self.grad("means")), ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")),
                   _lib.stream())
         self._end(ev)
@@ -460,11 +493,20 @@ class Trainer:
         stats = stats or self.last_stats
         n = self.n
         nv = float(self.visibility_count().gt(0).sum()) if self.selective else n
-        total = 0.0
+        V = len(stats)
+        # multi-view preprocess: parameters + SH rows once, 48 B out per view,
+        # visibility read-modify-write
+        total = (44.0 + 192.0 + 8.0) * n + 48.0 * V * n
+        # multi-view projection adjoint: parameters once; per view the gradient
+        # record, valid flag, colour and gated colour gradient; one
+        # read-modify-write of the 11 gradient floats
+        total += 44.0 * n + (48.0 + 4.0 + 12.0 + 12.0) * V * n + 88.0 * n
+        # SH adjoint over the views: means + SH rows in, per view the gated
+        # colour gradient, SH gradient rows out, d_means read-modify-write
+        total += (12.0 + 192.0 + 192.0 + 24.0) * n + 12.0 * V * n
         for v, st in zip(views, stats):
             P = v.width * v.height
             M = st.pairs
-            total += (44 + 192 + 48) * n            # preprocess fwd
             total += 40 * n + 8 * n + 16 * n        # bin count, depth keys, scan
             total += 16 * n * 4                     # depth sort (4 passes x r/w 8 B)
             total += (36 + 8) * n + 8 * M           # pair emission
@@ -476,7 +518,6 @@ class Trainer:
             total += 52 * Wk + 24 * P               # raster fwd (walked id + record)
             total += 40 * P + 36 * P                # fused loss (2 kernels)
             total += 52 * Wk + 36 * P + 48 * n      # raster bwd (+ gradient record)
-            total += (44 + 48 + 192) * n + 236 * 2 * n  # preprocess bwd (+ RMW grads)
         total += 28 * FLOATS_PER_GAUSSIAN * nv + 8 * n   # selective Adam
         return total
 

@@ -3,8 +3,9 @@
 The reference's viewer and camera-path renderer call `render` under
 `torch.no_grad()` view after view (viewer.py:477-485, render_path.py:
 440-456). This renderer keeps the Gaussians resident in the form the kernels
-read and, per view, runs the projection with SH colour, the antialias
-opacity compensation when asked for (metal_backend.py:506-511), the binning
+read; per batch of views it projects and colours every view in one launch,
+and per view it runs the antialias opacity compensation when asked for
+(metal_backend.py:506-511), the binning
 with the saturation cut, the packing and a forward-only rasterisation that
 writes no transmittance, stop indices or checkpoints and keeps no autograd
 state. Views are processed in batches with one host read per batch (the pair
@@ -17,7 +18,7 @@ import torch
 
 from . import _lib
 from ._lib import ptr
-from .engine import _ViewState
+from .engine import _ViewBatch, _ViewState, _views_array
 
 
 class _FrameBuffers:
@@ -57,7 +58,8 @@ class Renderer:
         self.background = None if background is None or all(b == 0 for b in background) \
             else tuple(float(b) for b in background)
         self.batch = batch
-        self._states: list[_ViewState] = []
+        self._batch = _ViewBatch(n, batch, self.device, grads=False)
+        self._states = [_ViewState(self._batch, v, self.device) for v in range(batch)]
         self._bufs: dict = {}
         # per-view opacity after the antialias compensation
         self._opac_view: list[torch.Tensor] = []
@@ -72,11 +74,8 @@ class Renderer:
                                 self.max_radius_frac * max(view.width, view.height), cc)
 
     def _state(self, v: int) -> _ViewState:
-        while len(self._states) <= v:
-            self._states.append(_ViewState(self.n, self.device))
-            if self.antialias:
-                self._opac_view.append(torch.empty(self.n, dtype=torch.float32,
-                                                   device=self.device))
+        while self.antialias and len(self._opac_view) <= v:
+            self._opac_view.append(torch.empty(self.n, dtype=torch.float32, device=self.device))
         return self._states[v]
 
     def _opacity(self, v: int) -> torch.Tensor:
@@ -100,15 +99,17 @@ class Renderer:
         L = _lib.load()
         s = _lib.stream()
         n = self.n
-        cams = [self._camera(v) for v in views]
-        for v, (view, cam) in enumerate(zip(views, cams)):
+        b = self._batch
+        cams = _views_array([self._camera(v) for v in views])
+        # every view's projection + SH colour in one launch
+        _lib.check(L.mg_preprocess_forward_views(
+            ptr(self.means), ptr(self.quats), ptr(self.scales), ptr(self.sh_dc),
+            ptr(self.sh_rest), _lib.SH_SPLIT, ptr(self.opac), _lib.C.cast(cams, _lib.C.c_void_p),
+            len(views), self.sh_degree, n, n, ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy),
+            ptr(b.valid), ptr(b.color), None, s), "preprocess_forward_views")
+        for v, view in enumerate(views):
             st = self._state(v)
             opac = self._opacity(v)
-            _lib.check(L.mg_preprocess_forward(
-                ptr(self.means), ptr(self.quats), ptr(self.scales), ptr(self.sh_dc),
-                ptr(self.sh_rest), _lib.SH_SPLIT, ptr(self.opac), _lib.C.byref(cam),
-                self.sh_degree, n, ptr(st.uv), ptr(st.conic), ptr(st.depth), ptr(st.rxy),
-                ptr(st.valid), ptr(st.color), s), "preprocess_forward")
             if self.antialias:
                 # before binning, as the reference does: the exact tile test
                 # then uses the opacity that is composited
