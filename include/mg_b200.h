@@ -478,7 +478,9 @@ mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
 
 /* Reads and clears the device error word of the current device (bounded
  * spins that gave up, checked-mode index faults). Synchronises `stream`.
- * *code_out receives 0 when nothing was recorded. */
+ * *code_out receives 0 when nothing was recorded, else the first code:
+ * 1 a sort look-back wait gave up, 2 a tile list reached past the sized pair
+ * count. */
 mg_status mg_read_device_error(int32_t* code_out, mg_stream_t stream);
 
 #ifdef __cplusplus

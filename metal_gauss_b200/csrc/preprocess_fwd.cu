@@ -386,6 +386,56 @@ __global__ void bin_write_kernel(const float2* __restrict__ uv,
                           (int32_t)g);
 }
 
+// Reorders a 256-thread block's work items by a cost class (a counting sort
+// in shared memory): returns the block-local index this thread takes, so
+// each warp holds items of similar cost instead of waiting on its largest.
+// Every output is indexed by item, so the order changes nothing but the
+// warps' divergence. `cls` is in [0, kCostClasses); put items past the end
+// in the last class.
+constexpr int kCostClasses = 16;
+__device__ __forceinline__ int block_sorted_slot(int cls) {
+    __shared__ int s_count[kCostClasses];
+    __shared__ int s_slot[256];
+    const int tid = threadIdx.x;
+    if (tid < kCostClasses) s_count[tid] = 0;
+    __syncthreads();
+    const int rank = atomicAdd(&s_count[cls], 1);
+    __syncthreads();
+    if (tid == 0) {  // exclusive prefix over the classes
+        int run = 0;
+#pragma unroll
+        for (int k = 0; k < kCostClasses; ++k) {
+            const int c = s_count[k];
+            s_count[k] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    s_slot[s_count[cls] + rank] = tid;
+    __syncthreads();
+    return s_slot[tid];
+}
+
+// Cost class of a Gaussian's count walk: its tile rectangle's area.
+__device__ __forceinline__ int64_t block_sorted_gaussian(const float2* __restrict__ uv,
+                                                         const float2* __restrict__ rxy,
+                                                         const int32_t* __restrict__ valid,
+                                                         int64_t n, int tile, int tiles_x,
+                                                         int tiles_y) {
+    const int64_t own = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int cls = kCostClasses - 1;
+    if (own < n) {
+        cls = 0;
+        if (valid[own] != 0) {
+            const float2 mu = uv[own], r = rxy[own];
+            const TileRect tr = tile_rect(mu.x, mu.y, r.x, r.y, tile, tiles_x, tiles_y);
+            const int area = (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1);
+            cls = min(kCostClasses - 2, (area + 3) >> 2);
+        }
+    }
+    return (int64_t)blockIdx.x * blockDim.x + block_sorted_slot(cls);
+}
+
 // Stage A of the two-stage binning: tile counts plus the depth sort keys.
 // Gaussians that claim no tile get key 0xffffffff and sort behind every
 // positive depth (valid depths are > near > 0, whose bit patterns are below
@@ -403,7 +453,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
                                        uint4* __restrict__ recs,
                                        const uint32_t* __restrict__ range,
                                        uint32_t* __restrict__ hist) {
-    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t g = block_sorted_gaussian(uv, rxy, valid, n, tile, tiles_x, tiles_y);
     if (g >= n) return;
     uint32_t c = 0u;
     if (valid[g] != 0) {
