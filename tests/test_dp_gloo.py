@@ -28,6 +28,21 @@ def _free_port():
     return port
 
 
+def _run_ranks(fn, extra, world=2, attempts=3):
+    """Spawn `world` ranks of fn(rank, world, port, *extra) to completion.
+    The port is probed free and then released, so another process can take
+    it before rank 0 binds it; a launch that fails is retried on a new port,
+    and the last failure is raised."""
+    for attempt in range(attempts):
+        try:
+            mp.start_processes(fn, args=(world, _free_port(), *extra), nprocs=world, join=True,
+                               start_method="spawn")
+            return
+        except (mp.ProcessRaisedException, mp.ProcessExitedException):
+            if attempt + 1 == attempts:
+                raise
+
+
 def _scene():
     p, _, _ = scenes.config("cfg3", n=N, seed=5)
     views = scenes.sphere_views(6, 4.0, W, H, 40.0, 2, hemisphere=True)
@@ -86,9 +101,7 @@ def test_sharding_covers_the_batch_once():
 
 
 def test_two_gloo_ranks_sum_to_the_single_process_gradient(tmp_path):
-    port = _free_port()
-    mp.start_processes(_worker, args=(2, port, str(tmp_path), 1), nprocs=2, join=True,
-                       start_method="spawn")
+    _run_ranks(_worker, (str(tmp_path), 1))
     r0 = torch.load(tmp_path / "r0.pt")
     r1 = torch.load(tmp_path / "r1.pt")
     assert r0["idx"] != r1["idx"]
@@ -149,9 +162,7 @@ def _shard_worker(rank, world, port, out_dir):
 def test_sharded_update_matches_the_replicated_one(tmp_path):
     """ZeRO-1 plumbing: reduce-scatter of a gradient segment, an update on
     each rank's row shard, all-gather of the parameters."""
-    port = _free_port()
-    mp.start_processes(_shard_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
+    _run_ranks(_shard_worker, (str(tmp_path),))
     p0, p1 = torch.load(tmp_path / "p0.pt"), torch.load(tmp_path / "p1.pt")
     ref = 1.0 - 0.5 * (torch.arange(24, dtype=torch.float32) * 3)     # sum over ranks 1 + 2
     assert torch.equal(p0, p1) and torch.allclose(p0, ref)
