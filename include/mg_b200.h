@@ -163,13 +163,17 @@ mg_status mg_preprocess_backward_accumulate(
  * grad2d records (MG_G2D_STRIDE floats), valid flags and forward colours
  * start at row v * view_stride; dpre_out row v * view_stride + g receives
  * view v's colour gradient gated by colour > 0, the input of
- * mg_sh_backward_views. No reference counterpart. */
+ * mg_sh_backward_views. With filter_3d (N,) given, scales and opacities are
+ * the activations BEFORE Mip-Splatting's 3D filter (mipfilter.py:79-93): the
+ * forward projected mg_apply_3d_filter's outputs, and the gradients are
+ * carried back through the filter (train.py:221-227 with filter_3d constant).
+ * No reference counterpart. */
 mg_status mg_preprocess_backward_views(
     const float* means, const float* quats, const float* scales,
     const float* opacities, const float* grad2d, const int32_t* valid,
     const float* color, const mg_camera* cams, int32_t n_views, int64_t n,
-    int64_t view_stride, float* d_means, float* d_quats, float* d_log_scales,
-    float* d_logit_opac, float* dpre_out, mg_stream_t stream);
+    int64_t view_stride, const float* filter_3d, float* d_means, float* d_quats,
+    float* d_log_scales, float* d_logit_opac, float* dpre_out, mg_stream_t stream);
 
 /* Deferred SH gradient of a batch of views, once per step. With dpre_out
  * given, mg_preprocess_backward_accumulate skips its SH branch and instead
@@ -471,6 +475,39 @@ mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
                           float w_ssim, float scale, float* grad_x,
                           float* loss_dev, void* scratch, size_t scratch_bytes,
                           mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Mip-Splatting 3D filter                                                  */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces compute_3d_filter (metal_gauss/mipfilter.py:30-76): per Gaussian,
+ * the smallest camera depth among the n_views cameras (<= 64) in whose frame,
+ * widened by `margin` on every side, the mean projects in front of
+ * `near_plane`; Gaussians no camera sees take the largest such depth of any
+ * Gaussian (all take 1 when none is seen); then depth / max focal * sqrt(0.2).
+ * Only viewmat, fx, fy, cx, cy, width and height of `cams` are read.
+ * Synchronises `stream` (the filter is recomputed every few hundred steps). */
+size_t mg_compute_3d_filter_scratch_bytes(void);
+mg_status mg_compute_3d_filter(const float* means, int64_t n, const mg_camera* cams,
+                               int32_t n_views, float near_plane, float margin,
+                               float* filter_out, void* scratch, size_t scratch_bytes,
+                               mg_stream_t stream);
+
+/* Replaces apply_3d_filter (mipfilter.py:79-93): out_scales =
+ * sqrt(scales^2 + f^2), out_opacities = opacities * sqrt(clamp(prod(scales^2)
+ * / prod(scales^2 + f^2), 0, 1)); scales (N,3), opacities and filter_3d (N,). */
+mg_status mg_apply_3d_filter(const float* scales, const float* opacities,
+                             const float* filter_3d, int64_t n, float* out_scales,
+                             float* out_opacities, mg_stream_t stream);
+
+/* The adjoint of mg_apply_3d_filter (the autograd of mipfilter.py:79-93 with
+ * filter_3d constant): d_scales (N,3) and d_opacities (N,) OVERWRITTEN from
+ * the gradients of its two outputs. */
+mg_status mg_apply_3d_filter_backward(const float* scales, const float* opacities,
+                                      const float* filter_3d, const float* d_out_scales,
+                                      const float* d_out_opacities, int64_t n,
+                                      float* d_scales, float* d_opacities,
+                                      mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Device error word                                                        */

@@ -59,10 +59,14 @@ SIGNATURES = {
     "mg_preprocess_backward_accumulate": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, CAM, i32, i64,
                                                 vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "mg_sh_backward_views": (i32, [vp, vp, vp, i32, i64, vp, vp, i32, vp, vp, vp, vp]),
+    "mg_compute_3d_filter_scratch_bytes": (sz, []),
+    "mg_compute_3d_filter": (i32, [vp, i64, vp, i32, f32, f32, vp, vp, sz, vp]),
+    "mg_apply_3d_filter": (i32, [vp, vp, vp, i64, vp, vp, vp]),
+    "mg_apply_3d_filter_backward": (i32, [vp, vp, vp, vp, vp, i64, vp, vp, vp]),
     "mg_preprocess_forward_views": (i32, [vp, vp, vp, vp, vp, ShLayout, vp, vp, i32, i32, i64,
                                           i64, vp, vp, vp, vp, vp, vp, vp, vp]),
     "mg_preprocess_backward_views": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i64, i64, vp,
-                                           vp, vp, vp, vp, vp]),
+                                           vp, vp, vp, vp, vp, vp]),
     "mg_bin_count": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]),
     "mg_bin_write": (i32, [vp, vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32, vp, vp,
                            vp]),

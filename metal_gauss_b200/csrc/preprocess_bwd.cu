@@ -10,6 +10,7 @@
 // 192 B, so per-thread access would scatter every load and store across 32
 // rows; the warp moves its 32 rows as one contiguous block instead.
 #include "exact_math.cuh"
+#include "filter3d.cuh"
 #include "kernels.cuh"
 
 namespace mg {
@@ -380,6 +381,9 @@ struct ViewCams {
 // gradient rows once, and each view's ReLU-gated colour gradient goes to
 // dpre[v * view_stride + g] for sh_backward_views_kernel. View v's grad2d
 // records, valid flags and forward colours start at v * view_stride rows.
+// With `filt`, scales and opacities are the activations before Mip-Splatting's
+// 3D filter: the projection adjoint runs at the widened scales and the summed
+// gradients are carried back through the filter (filter_3d constant).
 __global__ void __launch_bounds__(kBwdBlock)
 preprocess_backward_views_kernel(const float* __restrict__ means,
                                  const float* __restrict__ quats,
@@ -388,17 +392,26 @@ preprocess_backward_views_kernel(const float* __restrict__ means,
                                  const float* __restrict__ grad2d,
                                  const int32_t* __restrict__ valid,
                                  const float* __restrict__ color, ViewCams cams, int n_views,
-                                 int64_t n, int64_t view_stride, float* __restrict__ d_means,
+                                 int64_t n, int64_t view_stride,
+                                 const float* __restrict__ filt, float* __restrict__ d_means,
                                  float* __restrict__ d_quats, float* __restrict__ d_log_scales,
                                  float* __restrict__ d_logit, float* __restrict__ dpre) {
     const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
     if (g >= n) return;
     const float mx = means[3 * g], my = means[3 * g + 1], mz = means[3 * g + 2];
     const float4 q4 = reinterpret_cast<const float4*>(quats)[g];
-    const float s[3] = {scales[3 * g], scales[3 * g + 1], scales[3 * g + 2]};
+    const float s_act[3] = {scales[3 * g], scales[3 * g + 1], scales[3 * g + 2]};
     const float op = opac[g];
-    float dmx = 0.f, dmy = 0.f, dmz = 0.f, dl = 0.f;
-    float dls[3] = {0.f, 0.f, 0.f};
+    float s[3] = {s_act[0], s_act[1], s_act[2]};  // the scales the forward projected
+    Filter3d fl;
+    float f = 0.0f;
+    if (filt) {
+        f = filt[g];
+        fl = filter3d(s_act[0], s_act[1], s_act[2], f);
+        s[0] = fl.s[0]; s[1] = fl.s[1]; s[2] = fl.s[2];
+    }
+    float dmx = 0.f, dmy = 0.f, dmz = 0.f, dop = 0.f;
+    float dsa[3] = {0.f, 0.f, 0.f};  // d loss / d (projected) scales, all views
     float4 dqa = make_float4(0.f, 0.f, 0.f, 0.f);
     bool any = false;
     for (int v = 0; v < n_views; ++v) {
@@ -413,14 +426,28 @@ preprocess_backward_views_kernel(const float* __restrict__ means,
         projection_adjoint(cams.c[v], mx, my, mz, q4, s, r[MG_G2D_UV], r[MG_G2D_UV + 1],
                            r[MG_G2D_CONIC], r[MG_G2D_CONIC + 1], r[MG_G2D_CONIC + 2], dmx, dmy,
                            dmz, ds, dq);
-        dls[0] += ds[0] * s[0];
-        dls[1] += ds[1] * s[1];
-        dls[2] += ds[2] * s[2];
-        dl += r[MG_G2D_OPACITY] * (op * (1.0f - op));
+        dsa[0] += ds[0];
+        dsa[1] += ds[1];
+        dsa[2] += ds[2];
+        dop += r[MG_G2D_OPACITY];
         dqa = make_float4(dqa.x + dq.x, dqa.y + dq.y, dqa.z + dq.z, dqa.w + dq.w);
         any = true;
     }
     if (!any) return;
+    // activation chain: d log s = d s * s, d logit = d op * op (1 - op), through
+    // the 3D filter when there is one (s' = sqrt(s^2 + f^2), op' = op coef)
+    float dls[3], dl;
+    if (filt) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            dls[i] = (dsa[i] * s_act[i] / fl.s[i] + filter3d_dcoef(fl, s_act[i], f) * (dop * op)) *
+                     s_act[i];
+        dl = dop * fl.coef * (op * (1.0f - op));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) dls[i] = dsa[i] * s_act[i];
+        dl = dop * (op * (1.0f - op));
+    }
     d_means[3 * g + 0] += dmx;
     d_means[3 * g + 1] += dmy;
     d_means[3 * g + 2] += dmz;
@@ -588,8 +615,9 @@ extern "C" mg_status mg_preprocess_backward_accumulate(
 extern "C" mg_status mg_preprocess_backward_views(
     const float* means, const float* quats, const float* scales, const float* opacities,
     const float* grad2d, const int32_t* valid, const float* color, const mg_camera* cams,
-    int32_t n_views, int64_t n, int64_t view_stride, float* d_means, float* d_quats,
-    float* d_log_scales, float* d_logit_opac, float* dpre_out, mg_stream_t stream) {
+    int32_t n_views, int64_t n, int64_t view_stride, const float* filter_3d, float* d_means,
+    float* d_quats, float* d_log_scales, float* d_logit_opac, float* dpre_out,
+    mg_stream_t stream) {
     MG_REQUIRE(n_views >= 0, "preprocess_backward_views: negative view count");
     if (n == 0 || n_views == 0) return MG_OK;
     MG_REQUIRE(cams != nullptr, "preprocess_backward_views: null cameras");
@@ -608,7 +636,7 @@ extern "C" mg_status mg_preprocess_backward_views(
         const int64_t o = (int64_t)v0 * view_stride;
         preprocess_backward_views_kernel<<<ceil_div(n, kBwdBlock), kBwdBlock, 0, st>>>(
             means, quats, scales, opacities, grad2d + o * MG_G2D_STRIDE, valid + o,
-            color + 3 * o, vc, nv, n, view_stride, d_means, d_quats, d_log_scales,
+            color + 3 * o, vc, nv, n, view_stride, filter_3d, d_means, d_quats, d_log_scales,
             d_logit_opac, dpre_out + 3 * o);
         MG_TRY(check_launch("preprocess_backward_views"));
     }

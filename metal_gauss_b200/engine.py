@@ -176,8 +176,15 @@ class Trainer:
         for name, _ in SEGMENTS:
             self.param(name).copy_(params[name].to(self.device, torch.float32).reshape(
                 (n,) + SHAPES[name]))
+        # the activations the forward projects: exp / sigmoid of the
+        # parameters, widened and dimmed by the 3D filter when one is set
         self.scales = torch.empty(n, 3, **f32)
         self.opac = torch.empty(n, **f32)
+        # Mip-Splatting's 3D filter (N,) or None; with it, the activations
+        # before the filter are kept for the gradient chain
+        self.filter_3d: torch.Tensor | None = None
+        self._scales_act = torch.empty(0, **f32)
+        self._opac_act = torch.empty(0, **f32)
         self.loss = self.G[self.loss_offset:self.loss_offset + 1]
         self.window = torch.empty(11, **f32)
         x = torch.arange(11, dtype=torch.float32) - 5
@@ -239,9 +246,39 @@ class Trainer:
 
     def export_ply(self, path, filter_3d=None) -> None:
         """Write the current model as an INRIA-convention .ply, the file the
-        reference's `train.export_ply` writes (see `metal_gauss_b200.ply`)."""
+        reference's `train.export_ply` writes (see `metal_gauss_b200.ply`);
+        with `filter_3d` (e.g. `trainer.filter_3d`) the filter is baked in."""
         from .ply import export_ply
         export_ply(self.parameters(), path, filter_3d=filter_3d)
+
+    def compute_filter_3d(self, views, near: float = 0.2, margin: float = 0.15) -> torch.Tensor:
+        """Mip-Splatting's 3D filter of the current means for the training
+        cameras `views` (mipfilter.compute_3d_filter, mipfilter.py:30-76),
+        used by every following step until it is recomputed or cleared
+        (`trainer.filter_3d = None`)."""
+        from .mipfilter import compute_3d_filter
+        self.filter_3d = compute_3d_filter(self.param("means"), views, near, margin)
+        return self.filter_3d
+
+    def _activate(self) -> None:
+        """The forward's scales and opacities: exp / sigmoid of the
+        parameters (train.py:221-222), then the 3D filter when one is set
+        (train.py:223-227)."""
+        if self.filter_3d is None:
+            torch.exp(self.param("log_scales"), out=self.scales)
+            torch.sigmoid(self.param("logit_opac"), out=self.opac)
+            return
+        if self._scales_act.shape != self.scales.shape:
+            self._scales_act = torch.empty_like(self.scales)
+            self._opac_act = torch.empty_like(self.opac)
+        torch.exp(self.param("log_scales"), out=self._scales_act)
+        torch.sigmoid(self.param("logit_opac"), out=self._opac_act)
+        f = self.filter_3d.to(self.device, torch.float32).contiguous()
+        if f.numel() != self.n:
+            raise ValueError(f"filter_3d has {f.numel()} values for {self.n} Gaussians")
+        self.filter_3d = f
+        _lib.call("mg_apply_3d_filter", ptr(self._scales_act), ptr(self._opac_act), ptr(f), self.n,
+                  ptr(self.scales), ptr(self.opac), _lib.stream())
 
     def visibility_count(self) -> torch.Tensor:
         return self.G[self.vis_offset:self.vis_offset + self.n]
@@ -400,10 +437,12 @@ class Trainer:
         b = self._batch
         cams = _views_array([self._camera(view) for view in views])
         ev = self._begin("preprocess_bwd")
+        filt = self.filter_3d
         _lib.call("mg_preprocess_backward_views", ptr(self.param("means")),
-                  ptr(self.param("quats")), ptr(self.scales), ptr(self.opac), ptr(b.grad2d),
+                  ptr(self.param("quats")), ptr(self.scales if filt is None else self._scales_act),
+                  ptr(self.opac if filt is None else self._opac_act), ptr(b.grad2d),
                   ptr(b.valid), ptr(b.color), _lib.C.cast(cams, _lib.C.c_void_p), V, self.n,
-                  self.n, ptr(self.grad("means")), ptr(self.grad("quats")),
+                  self.n, ptr(filt), ptr(self.grad("means")), ptr(self.grad("quats")),
                   ptr(self.grad("log_scales")), ptr(self.grad("logit_opac")), ptr(b.dpre),
                   _lib.stream())
         self._end(ev)
@@ -459,8 +498,7 @@ class Trainer:
         world = self._world_size()
         gb = global_batch or len(views) * world
         ev = self._begin("activations")
-        torch.exp(self.param("log_scales"), out=self.scales)
-        torch.sigmoid(self.param("logit_opac"), out=self.opac)
+        self._activate()
         self.G.zero_()
         self.loss.zero_()
         self._end(ev)
@@ -523,7 +561,8 @@ class Trainer:
 
 
 def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: int = 0,
-        lr_means_end: float | None = None, sh_warmup: int = 0, callback=None) -> list[float]:
+        lr_means_end: float | None = None, sh_warmup: int = 0, filter_3d_every: int = 0,
+        callback=None) -> list[float]:
     """The reference's training loop (train.py:311-366) over batches of views.
 
     Views are drawn in epoch permutations (numpy's default_rng(seed), a new
@@ -531,10 +570,13 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
     rate decays geometrically from its initial value to `lr_means_end` over
     `steps`; with `sh_warmup`, the SH degree grows by one band every
     `sh_warmup` steps up to 3. Densification, the appearance model and the
-    opacity/scale regularisers are not part of this loop. `targets` are
-    (H, W, 3) uint8 or float images, moved to the device per step; returns the
-    per-step losses (one host read per step). With several ranks every rank
-    draws the same batches and renders its own share of each."""
+    opacity/scale regularisers are not part of this loop. With
+    `filter_3d_every`, Mip-Splatting's 3D filter is computed from all `views`
+    before the first step and again every that many steps (train.py:343-380).
+    `targets` are (H, W, 3) uint8 or float images, moved to the device per
+    step; returns the per-step losses (one host read per step). With several
+    ranks every rank draws the same batches and renders its own share of
+    each."""
     import numpy as np
     rng = np.random.default_rng(seed)
     order = rng.permutation(len(views))
@@ -553,6 +595,8 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
             oi += 1
         trainer.lrs["means"] = lr0 * decay ** step
         trainer.sh_degree = min(3, step // sh_warmup) if sh_warmup else 3
+        if filter_3d_every and (step == 1 or step % filter_3d_every == 0):
+            trainer.compute_filter_3d(views)
         mine = [idx[i] for i in rank_views]
         ts = []
         for i in mine:

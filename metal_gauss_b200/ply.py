@@ -77,13 +77,35 @@ def records(p: dict) -> np.ndarray:
     return rec
 
 
+def bake_3d_filter(p: dict, filter_3d) -> dict:
+    """`p` with Mip-Splatting's 3D filter baked into its stored scales and
+    opacity (train.py:609-616): the filter is applied to exp(log_scales) and
+    sigmoid(logit_opac) (mipfilter.py:79-93) and the results are written back
+    in log / logit space, opacity clamped to [1e-6, 1 - 1e-6] so a fully
+    suppressed Gaussian stays finite. float32 arithmetic on the host."""
+    f = torch.as_tensor(filter_3d).detach().to("cpu", torch.float32)
+    ls = torch.as_tensor(p["log_scales"]).detach().to("cpu", torch.float32)
+    lo = torch.as_tensor(p["logit_opac"]).detach().to("cpu", torch.float32)
+    n = ls.shape[0]
+    f = f[:n]
+    s2 = torch.exp(ls) ** 2
+    s2f = s2 + (f ** 2).unsqueeze(-1)
+    sc = torch.sqrt(s2f)
+    op = torch.sigmoid(lo) * torch.sqrt((s2.prod(dim=-1) / s2f.prod(dim=-1)).clamp(0.0, 1.0))
+    op = op.clamp(1e-6, 1.0 - 1e-6)
+    out = dict(p)
+    out["log_scales"] = torch.log(sc.clamp_min(1e-12))
+    out["logit_opac"] = torch.log(op / (1.0 - op))
+    return out
+
+
 def export_ply(p: dict, path: str | Path, filter_3d=None) -> None:
     """Write `p` as an INRIA-convention .ply, the layout of the reference's
-    `export_ply(p, path)` (train.py:583-624). Baking Mip-Splatting's 3D
-    filter into the file (`filter_3d`) is not supported here."""
+    `export_ply(p, path, filter_3d)` (train.py:583-624); with `filter_3d` the
+    filter is baked into the stored scales and opacity, so any viewer renders
+    the model as the trainer does."""
     if filter_3d is not None:
-        raise NotImplementedError("export_ply: baking the 3D filter into the file is not "
-                                  "supported by this backend")
+        p = bake_3d_filter(p, filter_3d)
     rec = records(p)
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)

@@ -35,13 +35,14 @@ class _FrameBuffers:
 
 class Renderer:
     """`params` in the trainer's storage form (means, quats, log_scales,
-    logit_opac, sh_dc (N,1,3), sh_rest (N,15,3)); activations are applied
+    logit_opac, sh_dc (N,1,3), sh_rest (N,15,3)); activations, and
+    Mip-Splatting's 3D filter when `filter_3d` (N,) is given, are applied
     once here."""
 
     def __init__(self, params: dict, device="cuda", *, sh_degree: int = 3, tile: int = 16,
                  background=(0.0, 0.0, 0.0), antialias: bool = False, near: float = 0.01,
                  far: float = 100.0, max_radius_frac: float = 1.0, saturation_cut: bool = True,
-                 batch: int = 8):
+                 batch: int = 8, filter_3d=None):
         self.device = torch.device(device)
         f32 = dict(dtype=torch.float32, device=self.device)
         self.n = n = int(params["means"].shape[0])
@@ -49,6 +50,12 @@ class Renderer:
         self.quats = params["quats"].to(**f32).reshape(n, 4).contiguous()
         self.scales = torch.exp(params["log_scales"].to(**f32)).reshape(n, 3).contiguous()
         self.opac = torch.sigmoid(params["logit_opac"].to(**f32)).reshape(n).contiguous()
+        if filter_3d is not None:  # Mip-Splatting's 3D filter, applied once (train.py:223-227)
+            f = torch.as_tensor(filter_3d).to(**f32).reshape(n).contiguous()
+            scales, opac = torch.empty_like(self.scales), torch.empty_like(self.opac)
+            _lib.call("mg_apply_3d_filter", ptr(self.scales), ptr(self.opac), ptr(f), n,
+                      ptr(scales), ptr(opac), _lib.stream())
+            self.scales, self.opac = scales, opac
         self.sh_dc = params["sh_dc"].to(**f32).reshape(n, 1, 3).contiguous()
         self.sh_rest = params["sh_rest"].to(**f32).reshape(n, 15, 3).contiguous()
         self.sh_degree, self.tile = sh_degree, tile

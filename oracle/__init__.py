@@ -216,6 +216,67 @@ def antialias_scale(conic: np.ndarray, blur: float) -> np.ndarray:
     return np.sqrt(np.clip(np.maximum(det_before, 0) / det_after, 0, 1)).astype(np.float32)
 
 
+# ---------------------------------------------------------------- 3D filter
+
+def compute_3d_filter(means, views, near=0.2, margin=0.15) -> np.ndarray:
+    """Mip-Splatting's 3D filter (metal_gauss/mipfilter.py:30-76) in float32:
+    views are (K (3,3), viewmat (4,4), W, H). The smallest camera depth among
+    the cameras whose margin-widened frame holds the projected mean in front
+    of `near`; unseen Gaussians take the largest such depth (1 when nothing
+    is seen); then depth / max focal * sqrt(0.2)."""
+    m = _f32(means)
+    n = m.shape[0]
+    dist = np.full(n, np.inf, np.float32)
+    seen = np.zeros(n, bool)
+    focal = 0.0
+    for K, vm, W, H in views:
+        K, vm = _f32(K), _f32(vm)
+        pc = (m @ vm[:3, :3].T + vm[:3, 3]).astype(np.float32)
+        z = pc[:, 2]
+        fx, fy, cx, cy = (np.float32(K[0, 0]), np.float32(K[1, 1]), np.float32(K[0, 2]),
+                          np.float32(K[1, 2]))
+        zc = np.maximum(z, np.float32(1e-6))
+        u = fx * pc[:, 0] / zc + cx
+        w = fy * pc[:, 1] / zc + cy
+        mW, mH = np.float32(margin * W), np.float32(margin * H)
+        inview = ((z > np.float32(near)) & (u > -mW) & (u < np.float32((1.0 + margin) * W))
+                  & (w > -mH) & (w < np.float32((1.0 + margin) * H)))
+        dist = np.where(inview, np.minimum(dist, z), dist).astype(np.float32)
+        seen |= inview
+        focal = max(focal, float(K[0, 0]), float(K[1, 1]))
+    if seen.any():
+        dist[~seen] = dist[seen].max()
+    else:
+        dist[:] = 1.0
+    if focal <= 0.0:
+        focal = 1.0
+    return ((dist / np.float32(focal)) * np.float32(0.2 ** 0.5)).astype(np.float32)
+
+
+def apply_3d_filter(scales, opac, filter_3d):
+    """(sqrt(s^2 + f^2), op * sqrt(clamp(prod s^2 / prod (s^2 + f^2), 0, 1)))
+    (mipfilter.py:79-93), float32."""
+    s, o, f = _f32(scales), _f32(opac), _f32(filter_3d)
+    s2 = s * s
+    s2f = s2 + (f * f)[:, None]
+    coef = np.sqrt(np.clip((s2[:, 0] * s2[:, 1] * s2[:, 2]) /
+                           (s2f[:, 0] * s2f[:, 1] * s2f[:, 2]), 0, 1))
+    return np.sqrt(s2f).astype(np.float32), (o * coef).astype(np.float32)
+
+
+def apply_3d_filter_backward(scales, opac, filter_3d, d_scales_out, d_opac_out):
+    """Gradients of apply_3d_filter's outputs carried to (scales, opacities),
+    the filter held constant: d s_i = g_si s_i / s'_i + g_o op coef f^2 /
+    (s_i (s_i^2 + f^2)), d op = g_o coef. Computed in float64."""
+    s, o, f = (np.asarray(x, np.float64) for x in (scales, opac, filter_3d))
+    gs, go = np.asarray(d_scales_out, np.float64), np.asarray(d_opac_out, np.float64)
+    s2 = s * s
+    s2f = s2 + (f * f)[:, None]
+    coef = np.sqrt(np.clip(s2.prod(1) / s2f.prod(1), 0, 1))
+    ds = gs * s / np.sqrt(s2f) + (go * o * coef)[:, None] * (f * f)[:, None] / (s * s2f)
+    return ds.astype(np.float32), (go * coef).astype(np.float32)
+
+
 # ------------------------------------------------------------------ binning
 
 def tiles_of(W: int, H: int, tile: int) -> tuple[int, int]:

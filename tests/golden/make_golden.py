@@ -7,7 +7,9 @@ kernels, so everything it can compute on a CPU is used here as ground truth:
 torch_ref.render / torch_ref.project (torch_ref.py:49-337), sh.eval_sh,
 metal_backend.build_tile_lists with the exact ellipse test
 (metal_backend.py:111-214), metal_backend.antialias_scale (:367-393),
-ssim.ssim (ssim.py:49-108) and selective_adam.SelectiveAdam. Inputs are seeded
+ssim.ssim (ssim.py:49-108), selective_adam.SelectiveAdam, and
+mipfilter.compute_3d_filter / apply_3d_filter with its autograd and the .ply
+bake of train.export_ply (train.py:609-616). Inputs are seeded
 and stored in the fixtures, so tests never need the reference or this script.
 The binning fixture takes its inputs from the CPU oracle's preprocess (the
 reference's own binning consumes the Metal preprocess outputs, which cannot run
@@ -254,6 +256,48 @@ def main() -> None:
                                      sh_degree=3)
         energy.append(rgb.sum().item())
     np.savez_compressed(HERE / "boundary.npz", us=us, energy=np.array(energy))
+    # ------------------------------------------------- Mip-Splatting 3D filter
+    from metal_gauss import mipfilter  # noqa: E402
+
+    class _FView:
+        def __init__(self, K, vm, W, H):
+            self.K, self.viewmat = K, vm
+            self.image = torch.zeros(H, W, 3, dtype=torch.uint8)
+
+    g = torch.Generator().manual_seed(17)
+    nf = 400
+    fmeans = torch.randn(nf, 3, generator=g) * 1.5
+    fmeans[:5, 2] = 50.0                       # behind every camera: unseen
+    fviews, fk, fvm, fwh = [], [], [], []
+    for i, (ang, f, W, H) in enumerate([(0.0, 300.0, 160, 120), (0.7, 450.0, 200, 100),
+                                        (-0.5, 250.0, 128, 128)]):
+        vm = torch.eye(4)
+        c, s_ = math.cos(ang), math.sin(ang)
+        vm[:3, :3] = torch.tensor([[c, 0.0, -s_], [0.0, 1.0, 0.0], [s_, 0.0, c]])
+        vm[2, 3] = 5.0 + i
+        K = torch.tensor([[f, 0.0, W / 2], [0.0, f, H / 2], [0.0, 0.0, 1.0]])
+        fviews.append(_FView(K, vm, W, H))
+        fk.append(np32(K)); fvm.append(np32(vm)); fwh.append((W, H))
+    filt = mipfilter.compute_3d_filter(fmeans, fviews)
+    fs = (torch.rand(nf, 3, generator=g) * 0.2 + 1e-3).requires_grad_(True)
+    fo = torch.rand(nf, generator=g).requires_grad_(True)
+    ns, no = mipfilter.apply_3d_filter(fs, fo, filt)
+    gs = torch.randn(nf, 3, generator=g)
+    go = torch.randn(nf, generator=g)
+    (ns * gs).sum().backward(retain_graph=True)
+    (no * go).sum().backward()
+    # the bake of train.export_ply (train.py:609-616) on log / logit parameters
+    fls, flo = torch.log(fs.detach()), torch.logit(fo.detach().clamp(1e-4, 1 - 1e-4))
+    sc, op = mipfilter.apply_3d_filter(torch.exp(fls), torch.sigmoid(flo), filt)
+    baked_ls = torch.log(sc.clamp_min(1e-12))
+    op = op.clamp(1e-6, 1.0 - 1e-6)
+    baked_lo = torch.log(op / (1.0 - op))
+    np.savez_compressed(HERE / "filter3d.npz", means=np32(fmeans), K=np.stack(fk),
+                        viewmat=np.stack(fvm), wh=np.array(fwh), filter=np32(filt),
+                        scales=np32(fs), opac=np32(fo), new_scales=np32(ns), new_opac=np32(no),
+                        g_scales=np32(gs), g_opac=np32(go), d_scales=np32(fs.grad),
+                        d_opac=np32(fo.grad), log_scales=np32(fls), logit_opac=np32(flo),
+                        baked_log_scales=np32(baked_ls), baked_logit_opac=np32(baked_lo))
     for f_ in sorted(HERE.glob("*.npz")):
         print(f_.name, f_.stat().st_size)
 

@@ -152,3 +152,20 @@ def test_boundary_energy_matches_reference():
                                   sh, K, np.eye(4, dtype=np.float32), W, H, sh_degree=3, tile=32)
         out.append(rgb.sum())
     assert np.abs(np.array(out) - f["energy"]).max() < 1e-3
+
+
+def test_3d_filter_matches_reference():
+    """compute_3d_filter / apply_3d_filter and its gradient
+    (mipfilter.py:30-93) against the reference's own values."""
+    f = load("filter3d")
+    views = [(K, vm, int(w), int(h)) for K, vm, (w, h) in zip(f["K"], f["viewmat"], f["wh"])]
+    got = oracle.compute_3d_filter(f["means"], views)
+    assert np.abs(got - f["filter"]).max() <= 1e-6 * float(np.abs(f["filter"]).max())
+    assert np.all(got[:5] == got.max())          # the unseen rows: the most filtered
+    ns, no = oracle.apply_3d_filter(f["scales"], f["opac"], f["filter"])
+    assert np.abs(ns - f["new_scales"]).max() < 1e-6
+    assert np.abs(no - f["new_opac"]).max() < 1e-6
+    ds, do = oracle.apply_3d_filter_backward(f["scales"], f["opac"], f["filter"], f["g_scales"],
+                                             f["g_opac"])
+    assert rel_l2(ds, f["d_scales"]) < 1e-5
+    assert rel_l2(do, f["d_opac"]) < 1e-6

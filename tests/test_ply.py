@@ -84,5 +84,24 @@ def test_reader_rejects_what_it_cannot_read(tmp_path):
                     b"property double x\nend_header\n" + bytes(8))
     with pytest.raises(ValueError, match="not float"):
         ply.read_ply(dbl)
-    with pytest.raises(NotImplementedError):
-        ply.export_ply(_params(2), tmp_path / "f.ply", filter_3d=torch.zeros(2))
+
+
+def test_export_bakes_the_3d_filter_as_the_reference_does(tmp_path):
+    """train.export_ply with filter_3d (train.py:609-616): the filtered scales
+    and opacity written in log / logit space, against the values the
+    reference's own mipfilter and bake produced (tests/golden/filter3d.npz)."""
+    from tests.golden.fixtures import load
+    f = load("filter3d")
+    n = f["filter"].shape[0]
+    p = _params(n)
+    p["log_scales"] = torch.from_numpy(f["log_scales"])
+    p["logit_opac"] = torch.from_numpy(f["logit_opac"])
+    ply.export_ply(p, tmp_path / "baked.ply", filter_3d=torch.from_numpy(f["filter"]))
+    q = ply.read_ply(tmp_path / "baked.ply")
+    assert np.abs(q["log_scales"].numpy() - f["baked_log_scales"]).max() < 1e-5
+    assert np.abs(q["logit_opac"].numpy() - f["baked_logit_opac"]).max() < 1e-4
+    assert torch.equal(q["means"], p["means"].float())
+    # a zero filter changes the scales by at most rounding
+    ply.export_ply(p, tmp_path / "zero.ply", filter_3d=torch.zeros(n))
+    z = ply.read_ply(tmp_path / "zero.ply")
+    assert np.abs(z["log_scales"].numpy() - f["log_scales"]).max() < 1e-6

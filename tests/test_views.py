@@ -116,7 +116,8 @@ def test_multi_view_adjoint_equals_the_per_view_sum(cuda):
     arr = (_lib.Camera * V)(*cams)
     _lib.call("mg_preprocess_backward_views", ptr(d["means"]), ptr(d["quats"]), ptr(d["scales"]),
               ptr(d["opac"]), ptr(grad2d), ptr(fw["valid"]), ptr(fw["color"]),
-              _lib.C.cast(arr, _lib.C.c_void_p), V, n, n, ptr(got["means"]), ptr(got["quats"]),
+              _lib.C.cast(arr, _lib.C.c_void_p), V, n, n, None, ptr(got["means"]),
+              ptr(got["quats"]),
               ptr(got["scales"]), ptr(got["logit"]), ptr(dpre), _lib.stream())
     assert torch.equal(dpre, ref_dpre)
     for k in ref:
