@@ -356,6 +356,13 @@ mg_status mg_rasterize_forward(
 mg_status mg_antialias_opacity(const float* conic, const float* opacity, int64_t n,
                                float blur, float* out, mg_stream_t stream);
 
+/* Adjoint of mg_antialias_opacity (the autograd of metal_backend.py:506-511
+ * through antialias_scale, :367-393): from grad_out (N,) = d loss / d out,
+ * d_conic (N,3) and d_opacity (N,) are OVERWRITTEN. */
+mg_status mg_antialias_opacity_backward(const float* conic, const float* opacity,
+                                        const float* grad_out, int64_t n, float blur,
+                                        float* d_conic, float* d_opacity, mg_stream_t stream);
+
 /* Replaces rasterize_backward (rasterize.mm:147-194; rasterize.metal:
  * 173-340). grad2d (N, MG_G2D_STRIDE) is ACCUMULATED into (zero it first for
  * a fresh gradient). background as in the forward: the blend's adjoint is

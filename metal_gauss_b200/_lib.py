@@ -82,6 +82,7 @@ SIGNATURES = {
                           vp]),
     "mg_pack_splats": (i32, [vp, vp, vp, vp, i64, vp, vp]),
     "mg_antialias_opacity": (i32, [vp, vp, i64, f32, vp, vp]),
+    "mg_antialias_opacity_backward": (i32, [vp, vp, vp, i64, f32, vp, vp, vp]),
     "mg_raster_scratch_bytes": (sz, [i32, i32, i32, i64]),
     "mg_rasterize_forward": (i32, [vp, vp, vp, i64, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,
                                    vp, sz, vp]),

@@ -733,6 +733,38 @@ __global__ void antialias_opacity_kernel(const float* __restrict__ conic,
     out[i] = opacity[i] * sqrtf(fminf(fmaxf(det_before, 0.0f) / det_after, 1.0f));
 }
 
+// Adjoint of antialias_opacity_kernel. With beta the blur, the ratio
+// det_before / det_after equals 1 - beta (cxx + cyy) + beta^2 (cxx cyy - cxy^2)
+// (the blurred covariance is the conic's inverse), so with
+// k = sqrt(clamp(ratio, 0, 1)): d op = g k and, where 0 < ratio < 1,
+// d conic = g op / (2 k) * d ratio / d conic.
+__global__ void antialias_opacity_backward_kernel(const float* __restrict__ conic,
+                                                  const float* __restrict__ opacity,
+                                                  const float* __restrict__ grad_out, int64_t n,
+                                                  float blur, float* __restrict__ d_conic,
+                                                  float* __restrict__ d_opacity) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float cxx = conic[3 * i], cxy = conic[3 * i + 1], cyy = conic[3 * i + 2];
+    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
+    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
+    const float ratio = ((a - blur) * (c - blur) - b * b) / det_after;
+    const float k = sqrtf(fminf(fmaxf(ratio, 0.0f), 1.0f));
+    const float g = grad_out[i];
+    d_opacity[i] = g * k;
+    float dxx = 0.0f, dxy = 0.0f, dyy = 0.0f;
+    if (ratio > 0.0f && ratio < 1.0f) {
+        const float h = g * opacity[i] / (2.0f * k);
+        const float b2 = blur * blur;
+        dxx = h * (b2 * cyy - blur);
+        dyy = h * (b2 * cxx - blur);
+        dxy = h * (-2.0f * b2 * cxy);
+    }
+    d_conic[3 * i] = dxx;
+    d_conic[3 * i + 1] = dxy;
+    d_conic[3 * i + 2] = dyy;
+}
+
 // ---------------------------------------------------------------- host side
 
 int blocks_per_tile(int tile) { return (tile * tile + 31) / 32; }
@@ -989,4 +1021,18 @@ extern "C" mg_status mg_antialias_opacity(const float* conic, const float* opaci
     antialias_opacity_kernel<<<ceil_div(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         conic, opacity, n, blur, out);
     return check_launch("antialias_opacity");
+}
+
+extern "C" mg_status mg_antialias_opacity_backward(const float* conic, const float* opacity,
+                                                   const float* grad_out, int64_t n, float blur,
+                                                   float* d_conic, float* d_opacity,
+                                                   mg_stream_t stream) {
+    MG_REQUIRE(n >= 0, "antialias_opacity_backward: negative count");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(conic && opacity && grad_out && d_conic && d_opacity,
+               "antialias_opacity_backward: null pointer");
+    antialias_opacity_backward_kernel<<<ceil_div(n, 256), 256, 0,
+                                        reinterpret_cast<cudaStream_t>(stream)>>>(
+        conic, opacity, grad_out, n, blur, d_conic, d_opacity);
+    return check_launch("antialias_opacity_backward");
 }

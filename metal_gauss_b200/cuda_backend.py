@@ -20,8 +20,8 @@ import math
 
 import torch
 
-from . import ext
-from ._lib import G2D_ABSUV
+from . import _lib, ext
+from ._lib import G2D_ABSUV, ptr
 
 SUPPORTED_TILES = (8, 12, 16, 32)
 
@@ -119,10 +119,43 @@ class _RasterizeCUDA(torch.autograd.Function):
         return (g[:, 0:2], g[:, 4:7], g[:, 2], g[:, 8:11]) + (None,) * 8
 
 
+class _AntialiasOpacity(torch.autograd.Function):
+    """opacity * antialias_scale(conic, blur) (metal_backend.py:506-511) in
+    one kernel each way: mg_antialias_opacity and its adjoint, which carries
+    the gradient to both the conic and the opacity."""
+
+    @staticmethod
+    def forward(ctx, conic, opacities, blur):
+        c = conic.detach().to(torch.float32).contiguous()
+        o = opacities.detach().to(torch.float32).contiguous()
+        out = torch.empty_like(o)
+        _lib.call("mg_antialias_opacity", ptr(c), ptr(o), c.shape[0], float(blur), ptr(out),
+                  _lib.stream())
+        ctx.save_for_backward(c, o)
+        ctx.blur = float(blur)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        c, o = ctx.saved_tensors
+        d_c, d_o = torch.empty_like(c), torch.empty_like(o)
+        _lib.call("mg_antialias_opacity_backward", ptr(c), ptr(o),
+                  ptr(g.to(torch.float32).contiguous()), c.shape[0], ctx.blur, ptr(d_c),
+                  ptr(d_o), _lib.stream())
+        return d_c, d_o, None
+
+
+def antialias_opacity(conic: torch.Tensor, opacities: torch.Tensor, blur: float) -> torch.Tensor:
+    """The compensated opacities the rasteriser draws with antialiasing on,
+    differentiable in the conic and the opacities."""
+    return _AntialiasOpacity.apply(conic, opacities, blur)
+
+
 def antialias_scale(conic: torch.Tensor, blur: float) -> torch.Tensor:
     """Mip-Splatting opacity compensation sqrt(det_before/det_after),
-    recovered from the conic (metal_backend.py:367-393); torch autograd
-    carries its gradient back to the conic."""
+    recovered from the conic (metal_backend.py:367-393), as a torch
+    expression (the reference's own helper; render() uses the fused
+    antialias_opacity)."""
     cxx, cxy, cyy = conic[:, 0], conic[:, 1], conic[:, 2]
     det_conic = (cxx * cyy - cxy * cxy).clamp_min(1e-12)
     det_after = 1.0 / det_conic
@@ -207,7 +240,7 @@ def render(means, quats, scales, opacities, sh, K, viewmat, W, H,
     valid_b = valid_i.bool()
     if antialias:
         # before binning: the SnugBox bound then uses the compensated opacity
-        opacities = opacities * antialias_scale(conic, 0.3)
+        opacities = antialias_opacity(conic, opacities, 0.3)
 
     gauss_ids, tile_offsets, tiles_x = build_tile_lists_cuda(
         uv.detach(), rxy.detach(), depth.detach(), valid_i, conic.detach(), opacities.detach(),

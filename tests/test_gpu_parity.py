@@ -521,6 +521,26 @@ def test_antialias_matches_oracle_and_darkens(cuda):
     assert float(on.sum()) <= float(off.sum()) + 1e-3
 
 
+def test_fused_antialias_gradient_matches_the_reference_expression(cuda):
+    """antialias_opacity (one kernel each way) against torch autograd through
+    the reference's antialias_scale expression (metal_backend.py:367-393)."""
+    from metal_gauss_b200.cuda_backend import antialias_opacity, antialias_scale
+    f = load("antialias")
+    conic = torch.from_numpy(f["conic"]).cuda()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    opac = torch.rand(conic.shape[0], device="cuda", generator=g) * 0.9 + 0.05
+    up = torch.randn(conic.shape[0], device="cuda", generator=g)
+    c1, o1 = conic.clone().double().requires_grad_(True), opac.clone().double().requires_grad_(True)
+    ref = o1 * antialias_scale(c1, 0.3)
+    (ref * up.double()).sum().backward()
+    c2, o2 = conic.clone().requires_grad_(True), opac.clone().requires_grad_(True)
+    got = antialias_opacity(c2, o2, 0.3)
+    (got * up).sum().backward()
+    assert float((got.detach() - ref.detach().float()).abs().max()) < 1e-6
+    assert rel_l2(N(o2.grad), N(o1.grad)) < 1e-5
+    assert rel_l2(N(c2.grad), N(c1.grad)) < 1e-4
+
+
 def test_boundary_energy_matches_reference(cuda):
     f = load("boundary")
     W = H = 128
