@@ -517,6 +517,62 @@ mg_status mg_apply_3d_filter_backward(const float* scales, const float* opacitie
                                       mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* 3DGS-MCMC densification (metal_gauss/mcmc.py)                            */
+/* ------------------------------------------------------------------------ */
+
+/* Rows of `width` floats per Gaussian starting at `ptr` (a parameter, an Adam
+ * moment, or a per-row step count with width 1). */
+typedef struct {
+    float* ptr;
+    int32_t width;
+} mg_row_segment;
+
+/* Scratch for the MCMC entry points, for `n` rows (the active count for
+ * relocation, the capacity for growth). */
+size_t mg_mcmc_scratch_bytes(int64_t n);
+
+/* Replaces relocate (mcmc.py:52-104) with reset_adam_state (:107-121) on a
+ * Gaussian table: `params` are its parameter segments (<= 32; params[logit_index]
+ * the opacity logits, params[log_scales_index] the (N,3) log-scales; every
+ * other segment is copied verbatim), `opt_rows` the optimizer rows to zero
+ * for every row whose meaning changes. Rows < n_active whose opacity is
+ * below dead_thresh are dead; each takes a live row drawn with probability
+ * proportional to `weights` (NULL: opacity; non-finite or all-zero weights
+ * fall back to opacity), with the multiplicity corrections of the split
+ * (o' = 1 - (1 - o)^(1/n), scales times the binomial ratio; n = the draw
+ * count of the target, clamped to [1, 51]) applied to copies and targets.
+ * `picks` (n_dead rows, NULL: draw them from `seed`) fixes the draws.
+ * *moved receives the number of dead rows. Synchronises `stream`. */
+mg_status mg_mcmc_relocate(const mg_row_segment* params, int32_t n_params,
+                           int32_t logit_index, int32_t log_scales_index,
+                           const mg_row_segment* opt_rows, int32_t n_opt_rows,
+                           int64_t n_active, float dead_thresh, const float* weights,
+                           const int32_t* picks, uint64_t seed, int64_t* moved,
+                           void* scratch, size_t scratch_bytes, mg_stream_t stream);
+
+/* Replaces grow (mcmc.py:124-163): rows [n_active, min(target, capacity)) are
+ * cloned from rows < n_active drawn with probability proportional to
+ * max(weights, 1e-8) (NULL or invalid weights: opacity), with the split's
+ * corrections for n = clamp(draws, 1, 51) + 1 applied to clones and targets
+ * and their optimizer rows zeroed. *new_active receives the new active
+ * count. `picks` as for mg_mcmc_relocate. Synchronises `stream`. */
+mg_status mg_mcmc_grow(const mg_row_segment* params, int32_t n_params, int32_t logit_index,
+                       int32_t log_scales_index, const mg_row_segment* opt_rows,
+                       int32_t n_opt_rows, int64_t n_active, int64_t target, int64_t capacity,
+                       const float* weights, const int32_t* picks, uint64_t seed,
+                       int64_t* new_active, void* scratch, size_t scratch_bytes,
+                       mg_stream_t stream);
+
+/* Replaces add_noise (mcmc.py:166-192): means (N,3) += R(q) (eps * scales)
+ * * sigmoid(-100 (opacity - opacity_gate)) * lr_means * weight for the
+ * first n rows, eps ~ N(0, 1) from `seed` (or the given (N,3) `eps`),
+ * R(q) the rotation of the normalised quaternion (w, x, y, z). */
+mg_status mg_mcmc_add_noise(float* means, const float* quats, const float* log_scales,
+                            const float* logit_opac, int64_t n, float lr_means, float weight,
+                            float opacity_gate, uint64_t seed, const float* eps,
+                            mg_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Device error word                                                        */
 /* ------------------------------------------------------------------------ */
 

@@ -41,6 +41,10 @@ class AdamSegment(C.Structure):
                 ("elem_begin", C.c_int64), ("elem_end", C.c_int64)]
 
 
+class RowSegment(C.Structure):
+    _fields_ = [("ptr", C.c_void_p), ("width", C.c_int32)]
+
+
 SH_FUSED = ShLayout(16, 16, 1, 0)
 SH_SPLIT = ShLayout(1, 15, 0, 0)
 
@@ -59,6 +63,12 @@ SIGNATURES = {
     "mg_preprocess_backward_accumulate": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, CAM, i32, i64,
                                                 vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "mg_sh_backward_views": (i32, [vp, vp, vp, i32, i64, vp, vp, i32, vp, vp, vp, vp]),
+    "mg_mcmc_scratch_bytes": (sz, [i64]),
+    "mg_mcmc_relocate": (i32, [vp, i32, i32, i32, vp, i32, i64, f32, vp, vp, C.c_uint64, vp, vp,
+                               sz, vp]),
+    "mg_mcmc_grow": (i32, [vp, i32, i32, i32, vp, i32, i64, i64, i64, vp, vp, C.c_uint64, vp, vp,
+                           sz, vp]),
+    "mg_mcmc_add_noise": (i32, [vp, vp, vp, vp, i64, f32, f32, f32, C.c_uint64, vp, vp]),
     "mg_compute_3d_filter_scratch_bytes": (sz, []),
     "mg_compute_3d_filter": (i32, [vp, i64, vp, i32, f32, f32, vp, vp, sz, vp]),
     "mg_apply_3d_filter": (i32, [vp, vp, vp, i64, vp, vp, vp]),

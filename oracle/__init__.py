@@ -277,6 +277,92 @@ def apply_3d_filter_backward(scales, opac, filter_3d, d_scales_out, d_opac_out):
     return ds.astype(np.float32), (go * coef).astype(np.float32)
 
 
+# -------------------------------------------------------------- MCMC (mcmc.py)
+
+def _sigmoid32(x):
+    x = _f32(x)
+    with np.errstate(over="ignore"):  # exp(-x) = inf gives the exact limit 0
+        return (np.float32(1) / (np.float32(1) + np.exp(-x))).astype(np.float32)
+
+
+def _mcmc_split(o, n):
+    """(logit of 1 - (1-o)^(1/n), log of the binomial scale ratio), float32
+    (mcmc.py:43-50, :83-86)."""
+    o = _f32(o)
+    nf = np.asarray(n, np.float32)
+    o_new = (np.float32(1) - np.maximum(np.float32(1) - o, np.float32(1e-6)) **
+             (np.float32(1) / nf)).astype(np.float32)
+    logit = np.log(np.clip(o_new, 1e-6, 1 - 1e-6) / np.maximum(1 - o_new, np.float32(1e-6)))
+    denom = np.maximum(np.maximum(nf, 1) * np.maximum(o_new, np.float32(1e-6)), np.float32(1e-6))
+    ratio = np.sqrt(np.clip(o_new / denom, 0.05, 1.0))
+    return logit.astype(np.float32), np.log(ratio).astype(np.float32)
+
+
+def mcmc_relocate(params: dict, picks, dead_thresh=0.005, active=None):
+    """relocate (mcmc.py:52-104) with its draws given: returns (new params,
+    rows whose optimizer state is reset). `picks` are row indices, one per
+    dead row in increasing row order."""
+    p = {k: np.array(v, dtype=np.float32, copy=True) for k, v in params.items()}
+    n_act = p["logit_opac"].shape[0] if active is None else active
+    opac = _sigmoid32(p["logit_opac"][:n_act])
+    dead = np.nonzero(opac < np.float32(dead_thresh))[0]
+    pick = np.asarray(picks, np.int64)
+    if dead.size == 0:
+        return p, np.zeros(0, np.int64)
+    counts = np.clip(np.bincount(pick, minlength=n_act), 1, 51)
+    logit_new, log_ratio = _mcmc_split(opac[pick], counts[pick])
+    for k in p:
+        if k not in ("logit_opac", "log_scales"):
+            p[k][dead] = p[k][pick]
+    p["log_scales"][dead] = p["log_scales"][pick] + log_ratio[:, None]
+    p["logit_opac"][dead] = logit_new
+    uniq = np.unique(pick)
+    lu, ru = _mcmc_split(opac[uniq], counts[uniq])
+    p["logit_opac"][uniq] = lu
+    p["log_scales"][uniq] += ru[:, None]
+    return p, np.concatenate([dead, uniq])
+
+
+def mcmc_grow(params: dict, picks, target: int, active: int):
+    """grow (mcmc.py:124-163) with its draws given: (new params, reset rows)."""
+    p = {k: np.array(v, dtype=np.float32, copy=True) for k, v in params.items()}
+    target = min(target, p["logit_opac"].shape[0])
+    if target <= active:
+        return p, np.zeros(0, np.int64)
+    opac = _sigmoid32(p["logit_opac"][:active])
+    pick = np.asarray(picks, np.int64)
+    dst = np.arange(active, target)
+    counts = np.clip(np.bincount(pick, minlength=active), 1, 51) + 1
+    logit_new, log_ratio = _mcmc_split(opac[pick], counts[pick])
+    for k in p:
+        if k not in ("logit_opac", "log_scales"):
+            p[k][dst] = p[k][pick]
+    p["log_scales"][dst] = p["log_scales"][pick] + log_ratio[:, None]
+    p["logit_opac"][dst] = logit_new
+    uniq = np.unique(pick)
+    lu, ru = _mcmc_split(opac[uniq], counts[uniq])
+    p["logit_opac"][uniq] = lu
+    p["log_scales"][uniq] += ru[:, None]
+    return p, np.concatenate([dst, uniq])
+
+
+def mcmc_add_noise(params: dict, eps, lr_means, weight=4e4, opacity_gate=0.005, active=None):
+    """add_noise (mcmc.py:166-192) with its normal draws `eps` (N,3) given:
+    the new means."""
+    m = np.array(params["means"], dtype=np.float32, copy=True)
+    n = m.shape[0] if active is None else active
+    opac = _sigmoid32(params["logit_opac"][:n])
+    gate = _sigmoid32(np.float32(-100.0) * (opac - np.float32(opacity_gate)))
+    e = _f32(eps)[:n] * np.exp(_f32(params["log_scales"][:n]))
+    q = _f32(params["quats"][:n])
+    q = q / np.maximum(np.linalg.norm(q, axis=1, keepdims=True), np.float32(1e-12))
+    w, u = q[:, 0:1], q[:, 1:4]
+    t = np.float32(2.0) * np.cross(u, e)
+    world = e + w * t + np.cross(u, t)
+    m[:n] += world * gate[:, None] * np.float32(lr_means) * np.float32(weight)
+    return m
+
+
 # ------------------------------------------------------------------ binning
 
 def tiles_of(W: int, H: int, tile: int) -> tuple[int, int]:

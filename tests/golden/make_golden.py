@@ -9,7 +9,8 @@ metal_backend.build_tile_lists with the exact ellipse test
 (metal_backend.py:111-214), metal_backend.antialias_scale (:367-393),
 ssim.ssim (ssim.py:49-108), selective_adam.SelectiveAdam, and
 mipfilter.compute_3d_filter / apply_3d_filter with its autograd and the .ply
-bake of train.export_ply (train.py:609-616). Inputs are seeded
+bake of train.export_ply (train.py:609-616), and mcmc.relocate / grow /
+add_noise with their torch.multinomial / torch.randn_like draws recorded. Inputs are seeded
 and stored in the fixtures, so tests never need the reference or this script.
 The binning fixture takes its inputs from the CPU oracle's preprocess (the
 reference's own binning consumes the Metal preprocess outputs, which cannot run
@@ -298,6 +299,58 @@ def main() -> None:
                         g_scales=np32(gs), g_opac=np32(go), d_scales=np32(fs.grad),
                         d_opac=np32(fo.grad), log_scales=np32(fls), logit_opac=np32(flo),
                         baked_log_scales=np32(baked_ls), baked_logit_opac=np32(baked_lo))
+    # ------------------------------------------------------------ MCMC
+    from metal_gauss import mcmc  # noqa: E402
+
+    def mcmc_params(n, seed):
+        gm = torch.Generator().manual_seed(seed)
+        return {"means": torch.randn(n, 3, generator=gm),
+                "quats": torch.randn(n, 4, generator=gm),
+                "log_scales": torch.randn(n, 3, generator=gm) * 0.5 - 3.0,
+                "logit_opac": torch.randn(n, generator=gm) * 3.0 - 2.0,
+                "sh_dc": torch.randn(n, 1, 3, generator=gm),
+                "sh_rest": torch.randn(n, 15, 3, generator=gm) * 0.1}
+
+    captured = {}
+    real_multinomial, real_randn_like = torch.multinomial, torch.randn_like
+
+    def multinomial(w, k, replacement=False, **kw):
+        out = real_multinomial(w, k, replacement=replacement, **kw)
+        captured["draw"] = out.clone()
+        return out
+
+    def randn_like(t, **kw):
+        out = real_randn_like(t, **kw)
+        captured["eps"] = out.clone()
+        return out
+
+    torch.multinomial, torch.randn_like = multinomial, randn_like
+    try:
+        torch.manual_seed(23)
+        pr = mcmc_params(300, 29)
+        before = {k: v.clone() for k, v in pr.items()}
+        opac_b = torch.sigmoid(before["logit_opac"])
+        alive = (opac_b >= 0.005).nonzero(as_tuple=True)[0]
+        moved = mcmc.relocate(pr)
+        reloc_picks = alive[captured["draw"]]
+        pg = mcmc_params(300, 31)
+        gbefore = {k: v.clone() for k, v in pg.items()}
+        new_active = mcmc.grow(pg, 260, 200)
+        grow_picks = captured["draw"].clone()
+        pn = mcmc_params(300, 37)
+        nbefore = {k: v.clone() for k, v in pn.items()}
+        mcmc.add_noise(pn, 1.6e-4, 4e4)
+        eps = captured["eps"].clone()
+    finally:
+        torch.multinomial, torch.randn_like = real_multinomial, real_randn_like
+    out = {"moved": np.int64(moved), "reloc_picks": reloc_picks.numpy().astype(np.int32),
+           "new_active": np.int64(new_active), "grow_picks": grow_picks.numpy().astype(np.int32),
+           "eps": np32(eps)}
+    for tag, b, a in (("reloc", before, pr), ("grow", gbefore, pg), ("noise", nbefore, pn)):
+        for k in b:
+            out[f"{tag}_before_{k}"] = np32(b[k])
+            out[f"{tag}_after_{k}"] = np32(a[k])
+    np.savez_compressed(HERE / "mcmc.npz", **out)
     for f_ in sorted(HERE.glob("*.npz")):
         print(f_.name, f_.stat().st_size)
 

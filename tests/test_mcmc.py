@@ -1,0 +1,140 @@
+"""3DGS-MCMC on the GPU (metal_gauss_b200.mcmc over mg_mcmc_*): relocate,
+grow and add_noise replayed with the reference's own recorded draws
+(tests/golden/mcmc.npz) reproduce its parameters, and reset exactly the
+optimizer rows reset_adam_state would; the device generator's draws follow
+the weights, the noise has the stated scale and the opacity gate."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from metal_gauss_b200 import mcmc
+from tests.golden.fixtures import load
+
+pytestmark = pytest.mark.gpu
+
+KEYS = ("means", "quats", "log_scales", "logit_opac", "sh_dc", "sh_rest")
+
+
+def _side(f, tag, when):
+    return {k: torch.from_numpy(f[f"{tag}_{when}_{k}"]).cuda().contiguous() for k in KEYS}
+
+
+class _Opt:
+    """Optimizer stand-in with SelectiveAdam's state layout."""
+    def __init__(self, params):
+        self.state = {t: {"exp_avg": torch.ones_like(t), "exp_avg_sq": torch.ones_like(t),
+                          "steps": torch.ones(t.shape[0], device=t.device)}
+                      for t in params.values()}
+
+
+def _check_reset(opt, params, rows):
+    n = params["means"].shape[0]
+    changed = np.zeros(n, bool)
+    changed[rows] = True
+    for t in params.values():
+        st = opt.state[t]
+        for key in ("exp_avg", "exp_avg_sq"):
+            v = st[key].reshape(n, -1).cpu().numpy()
+            assert np.all(v[changed] == 0) and np.all(v[~changed] == 1), key
+        s = st["steps"].cpu().numpy()
+        assert np.all(s[changed] == 0) and np.all(s[~changed] == 1)
+
+
+def test_relocate_replays_the_reference(cuda):
+    f = load("mcmc")
+    p = _side(f, "reloc", "before")
+    opt = _Opt(p)
+    moved = mcmc.relocate(p, opt=opt, picks=torch.from_numpy(f["reloc_picks"]))
+    assert moved == int(f["moved"])
+    for k in KEYS:
+        assert np.abs(p[k].cpu().numpy() - f[f"reloc_after_{k}"]).max() < 2e-5, k
+    _, rows = oracle.mcmc_relocate({k: f[f"reloc_before_{k}"] for k in KEYS}, f["reloc_picks"])
+    _check_reset(opt, p, rows)
+
+
+def test_grow_replays_the_reference(cuda):
+    f = load("mcmc")
+    p = _side(f, "grow", "before")
+    opt = _Opt(p)
+    active = mcmc.grow(p, 260, 200, opt=opt, picks=torch.from_numpy(f["grow_picks"]))
+    assert active == int(f["new_active"]) == 260
+    for k in KEYS:
+        assert np.abs(p[k].cpu().numpy() - f[f"grow_after_{k}"]).max() < 2e-5, k
+    _, rows = oracle.mcmc_grow({k: f[f"grow_before_{k}"] for k in KEYS}, f["grow_picks"], 260,
+                               200)
+    _check_reset(opt, p, rows)
+
+
+def test_add_noise_replays_the_reference(cuda):
+    f = load("mcmc")
+    p = _side(f, "noise", "before")
+    mcmc.add_noise(p, 1.6e-4, 4e4, eps=torch.from_numpy(f["eps"]))
+    assert np.abs(p["means"].cpu().numpy() - f["noise_after_means"]).max() < 1e-6
+    for k in KEYS[1:]:
+        assert torch.equal(p[k].cpu(), torch.from_numpy(f[f"noise_before_{k}"])), k
+
+
+def _table(n_alive, n_dead, seed):
+    g = torch.Generator().manual_seed(seed)
+    n = n_alive + n_dead
+    p = {"means": torch.zeros(n, 3), "quats": torch.randn(n, 4, generator=g),
+         "log_scales": torch.full((n, 3), -3.0), "logit_opac": torch.full((n,), -9.0),
+         "sh_dc": torch.zeros(n, 1, 3), "sh_rest": torch.zeros(n, 15, 3)}
+    p["means"][:, 0] = torch.arange(n, dtype=torch.float32)   # a row's identity
+    p["logit_opac"][:n_alive] = 2.0                            # opacity 0.88: alive
+    return {k: v.cuda().contiguous() for k, v in p.items()}
+
+
+def test_device_draws_follow_the_weights(cuda):
+    """100k dead rows relocated onto 8 live rows weighted 1:2:...:8: every
+    dead row lands on a live one, in proportion to its weight."""
+    n_alive, n_dead = 8, 100_000
+    p = _table(n_alive, n_dead, 1)
+    w = torch.zeros(n_alive + n_dead, device="cuda")
+    w[:n_alive] = torch.arange(1, n_alive + 1, dtype=torch.float32)
+    assert mcmc.relocate(p, weights=w, seed=123) == n_dead
+    src = p["means"][n_alive:, 0].round().long().cpu()
+    hist = torch.bincount(src, minlength=n_alive).double()
+    assert int(hist.sum()) == n_dead and hist[n_alive:].sum() == 0
+    expect = torch.arange(1, n_alive + 1, dtype=torch.float64) / 36.0 * n_dead
+    chi2 = float(((hist[:n_alive] - expect) ** 2 / expect).sum())
+    assert chi2 < 30.0, chi2                                   # 7 dof: p < 1e-4
+    # multiplicity 51 (the clamp): the copies and the targets are split
+    o = torch.sigmoid(p["logit_opac"]).cpu()
+    want = 1.0 - (1.0 - torch.sigmoid(torch.tensor(2.0))) ** (1.0 / 51)
+    assert torch.allclose(o, torch.full_like(o, float(want)), rtol=1e-4)
+    # the same seed draws the same rows
+    q = _table(n_alive, n_dead, 1)
+    mcmc.relocate(q, weights=w, seed=123)
+    assert torch.equal(p["means"], q["means"])
+
+
+def test_grow_clones_into_the_tail(cuda):
+    p = _table(1000, 0, 2)
+    cap = 1000
+    p = {k: torch.cat([v, torch.zeros((600,) + v.shape[1:], device="cuda")]).contiguous()
+         for k, v in p.items()}
+    assert mcmc.grow(p, 1500, 1000, seed=7) == 1500
+    src = p["means"][1000:1500, 0].round().long()
+    assert int(src.min()) >= 0 and int(src.max()) < cap
+    assert torch.all(p["logit_opac"][1500:] == 0)                # beyond the target: untouched
+    assert mcmc.grow(p, 10_000, 1500, seed=8) == 1600            # clamped to the capacity
+
+
+def test_noise_scale_and_gate(cuda):
+    n = 200_000
+    p = {"means": torch.zeros(n, 3), "quats": torch.tensor([[1.0, 0, 0, 0]]).repeat(n, 1),
+         "log_scales": torch.full((n, 3), float(np.log(0.01))), "logit_opac": torch.full((n,), -9.0)}
+    p["logit_opac"][n // 2:] = 3.0                             # opaque: gated off
+    p = {k: v.cuda().contiguous() for k, v in p.items()}
+    mcmc.add_noise(p, 1e-4, 4e4, seed=11)
+    d = p["means"].cpu()
+    low = d[: n // 2]
+    o_low = 1.0 / (1.0 + np.exp(9.0))
+    gate = 1.0 / (1.0 + np.exp(100.0 * (o_low - 0.005)))
+    std = 0.01 * 1e-4 * 4e4 * gate
+    assert abs(float(low.mean())) < 0.02 * std
+    assert abs(float(low.std()) / std - 1.0) < 0.01
+    assert float(d[n // 2:].abs().max()) < 1e-3 * std

@@ -169,3 +169,26 @@ def test_3d_filter_matches_reference():
                                              f["g_opac"])
     assert rel_l2(ds, f["d_scales"]) < 1e-5
     assert rel_l2(do, f["d_opac"]) < 1e-6
+
+
+def _mcmc_side(f, tag, when):
+    keys = ("means", "quats", "log_scales", "logit_opac", "sh_dc", "sh_rest")
+    return {k: f[f"{tag}_{when}_{k}"] for k in keys}
+
+
+def test_mcmc_relocate_grow_and_noise_match_reference():
+    """relocate / grow / add_noise (mcmc.py:52-192) replayed with the
+    reference's own recorded draws reproduce its parameters."""
+    f = load("mcmc")
+    before = _mcmc_side(f, "reloc", "before")
+    got, reset = oracle.mcmc_relocate(before, f["reloc_picks"])
+    assert len(f["reloc_picks"]) == int(f["moved"]) > 0
+    want = _mcmc_side(f, "reloc", "after")
+    for k in want:
+        assert np.abs(got[k] - want[k]).max() < 2e-5, k
+    got, _ = oracle.mcmc_grow(_mcmc_side(f, "grow", "before"), f["grow_picks"], 260, 200)
+    want = _mcmc_side(f, "grow", "after")
+    for k in want:
+        assert np.abs(got[k] - want[k]).max() < 2e-5, k
+    m = oracle.mcmc_add_noise(_mcmc_side(f, "noise", "before"), f["eps"], 1.6e-4, 4e4)
+    assert np.abs(m - f["noise_after_means"]).max() < 1e-6
