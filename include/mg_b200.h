@@ -183,11 +183,13 @@ mg_status mg_preprocess_backward_views(
  * all n_views views together: d_sh (split layout, OVERWRITTEN) = sum over
  * views of B(dir_v) x dpre_v, and d_means += the view-direction term, reading
  * the coefficients once instead of once per view. cam_centers: n_views x 3
- * host floats; dpre: (n_views, N, 3) device; n_views <= 64. */
+ * host floats; dpre: view v's rows start at row v * view_stride (>= N) of a
+ * device array of 3-float rows; n_views <= 64. */
 mg_status mg_sh_backward_views(const float* means, const float* sh_dc,
                                const float* sh_rest, int32_t sh_degree,
                                int64_t n, const float* cam_centers,
                                const float* dpre, int32_t n_views,
+                               int64_t view_stride,
                                float* d_means, float* d_sh_dc,
                                float* d_sh_rest, mg_stream_t stream);
 

@@ -62,7 +62,7 @@ SIGNATURES = {
                                      vp, CAM, i32, i64, vp, vp, vp, vp, vp, vp]),
     "mg_preprocess_backward_accumulate": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, CAM, i32, i64,
                                                 vp, vp, vp, vp, vp, vp, vp, vp, vp]),
-    "mg_sh_backward_views": (i32, [vp, vp, vp, i32, i64, vp, vp, i32, vp, vp, vp, vp]),
+    "mg_sh_backward_views": (i32, [vp, vp, vp, i32, i64, vp, vp, i32, i64, vp, vp, vp, vp]),
     "mg_mcmc_scratch_bytes": (sz, [i64]),
     "mg_mcmc_relocate": (i32, [vp, i32, i32, i32, vp, i32, i64, f32, vp, vp, C.c_uint64, vp, vp,
                                sz, vp]),

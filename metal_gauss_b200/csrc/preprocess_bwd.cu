@@ -472,8 +472,8 @@ __global__ void __launch_bounds__(kBwdBlock)
 sh_backward_views_kernel(const float* __restrict__ means, const float* __restrict__ sh_dc,
                          const float* __restrict__ sh_rest, int sh_degree, int64_t n,
                          ViewCentres centres, const float* __restrict__ dpre, int n_views,
-                         float* __restrict__ d_means, float* __restrict__ d_sh_dc,
-                         float* __restrict__ d_sh_rest) {
+                         int64_t view_stride, float* __restrict__ d_means,
+                         float* __restrict__ d_sh_dc, float* __restrict__ d_sh_rest) {
     __shared__ float s_sh[kBwdBlock / 32][32 * 45];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
@@ -494,7 +494,7 @@ sh_backward_views_kernel(const float* __restrict__ means, const float* __restric
         const float* dc = sh_dc + 3 * g;
         const float* rest = blk + lane * 45;
         for (int v = 0; v < n_views; ++v) {
-            const float* dp = dpre + ((int64_t)v * n + g) * 3;
+            const float* dp = dpre + ((int64_t)v * view_stride + g) * 3;
             const float er = dp[0], eg = dp[1], eb = dp[2];
             if (er == 0.f && eg == 0.f && eb == 0.f) continue;
             const float dvx = mx - centres.c[v][0], dvy = my - centres.c[v][1],
@@ -646,9 +646,10 @@ extern "C" mg_status mg_preprocess_backward_views(
 extern "C" mg_status mg_sh_backward_views(const float* means, const float* sh_dc,
                                           const float* sh_rest, int32_t sh_degree, int64_t n,
                                           const float* cam_centers, const float* dpre,
-                                          int32_t n_views, float* d_means, float* d_sh_dc,
-                                          float* d_sh_rest, mg_stream_t stream) {
+                                          int32_t n_views, int64_t view_stride, float* d_means,
+                                          float* d_sh_dc, float* d_sh_rest, mg_stream_t stream) {
     MG_REQUIRE(n_views >= 0 && n_views <= kMaxViews, "sh_backward_views: at most 64 views");
+    MG_REQUIRE(view_stride >= n, "sh_backward_views: view_stride below n");
     MG_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_backward_views: sh_degree must be 0..3");
     if (n == 0) return MG_OK;
     MG_REQUIRE(means && sh_dc && sh_rest && d_means && d_sh_dc && d_sh_rest &&
@@ -659,6 +660,7 @@ extern "C" mg_status mg_sh_backward_views(const float* means, const float* sh_dc
         for (int k = 0; k < 3; ++k) c.c[v][k] = cam_centers[3 * v + k];
     sh_backward_views_kernel<<<ceil_div(n, kBwdBlock), kBwdBlock, 0,
                                reinterpret_cast<cudaStream_t>(stream)>>>(
-        means, sh_dc, sh_rest, sh_degree, n, c, dpre, n_views, d_means, d_sh_dc, d_sh_rest);
+        means, sh_dc, sh_rest, sh_degree, n, c, dpre, n_views, view_stride, d_means, d_sh_dc,
+        d_sh_rest);
     return check_launch("sh_backward_views");
 }

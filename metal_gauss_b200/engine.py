@@ -131,6 +131,9 @@ class Trainer:
                  saturation_cut: bool = True):
         self.device = torch.device(device)
         self.n = n = int(params["means"].shape[0])
+        # rows < active are rendered and densified (3DGS-MCMC grows it toward
+        # the capacity n); buffers are sized for the capacity
+        self.active = n
         self.world = dp.world_size(group)
         self.rank = dp.rank(group)
         # ZeRO-1: with several ranks each one owns the optimizer state of a
@@ -260,6 +263,76 @@ class Trainer:
         self.filter_3d = compute_3d_filter(self.param("means"), views, near, margin)
         return self.filter_3d
 
+    # ------------------------------------------------------------- MCMC
+
+    def _mcmc_tables(self):
+        """The Gaussian table as row segments: the parameter segments of P,
+        then the Adam rows to reset (M and V in P's layout, the per-row step
+        counts)."""
+        params = [_lib.RowSegment(self.P.data_ptr() + 4 * self.offsets[name], w)
+                  for name, w in SEGMENTS]
+        rows = [_lib.RowSegment(buf.data_ptr() + 4 * self.offsets[name], w)
+                for buf in (self.M, self.V) for name, w in SEGMENTS]
+        rows.append(_lib.RowSegment(self.steps.data_ptr(), 1))
+        names = [name for name, _ in SEGMENTS]
+        return ((_lib.RowSegment * len(params))(*params), len(params),
+                names.index("logit_opac"), names.index("log_scales"),
+                (_lib.RowSegment * len(rows))(*rows), len(rows))
+
+    def _mcmc_seed(self, seed) -> int:
+        # identical on every rank (the table is replicated), new every step
+        if seed is not None:
+            return int(seed)
+        return (0x5EED * 1_000_003 + self.step_count) & (2 ** 63 - 1)
+
+    def _mcmc_weights(self, weights):
+        if weights is None:
+            return None
+        return weights[:self.active].to(self.device, torch.float32).contiguous()
+
+    def relocate(self, dead_thresh: float = 0.005, weights: torch.Tensor | None = None,
+                 seed: int | None = None, picks: torch.Tensor | None = None) -> int:
+        """3DGS-MCMC relocation (mcmc.relocate, mcmc.py:52-121) of the active
+        rows in the trainer's own buffers, Adam rows of every changed row
+        reset. Returns how many dead Gaussians moved."""
+        P, nP, il, isc, R, nR = self._mcmc_tables()
+        w = self._mcmc_weights(weights)
+        pk = None if picks is None else picks.to(self.device, torch.int32).contiguous()
+        scratch = torch.empty(_lib.load().mg_mcmc_scratch_bytes(self.active), dtype=torch.uint8,
+                              device=self.device)
+        moved = _lib.C.c_int64(0)
+        _lib.call("mg_mcmc_relocate", P, nP, il, isc, R, nR, self.active, float(dead_thresh),
+                  ptr(w), ptr(pk), self._mcmc_seed(seed), _lib.C.byref(moved), ptr(scratch),
+                  scratch.numel(), _lib.stream())
+        return int(moved.value)
+
+    def grow(self, target: int, weights: torch.Tensor | None = None, seed: int | None = None,
+             picks: torch.Tensor | None = None) -> int:
+        """3DGS-MCMC growth (mcmc.grow, mcmc.py:124-163): rows [active,
+        target) cloned from weight-drawn active rows; returns the new active
+        count."""
+        P, nP, il, isc, R, nR = self._mcmc_tables()
+        w = self._mcmc_weights(weights)
+        pk = None if picks is None else picks.to(self.device, torch.int32).contiguous()
+        scratch = torch.empty(_lib.load().mg_mcmc_scratch_bytes(self.n), dtype=torch.uint8,
+                              device=self.device)
+        out = _lib.C.c_int64(0)
+        _lib.call("mg_mcmc_grow", P, nP, il, isc, R, nR, self.active, int(target), self.n, ptr(w),
+                  ptr(pk), self._mcmc_seed(seed), _lib.C.byref(out), ptr(scratch),
+                  scratch.numel(), _lib.stream())
+        self.active = int(out.value)
+        return self.active
+
+    def add_noise(self, lr_means: float | None = None, weight: float = 4e4,
+                  opacity_gate: float = 0.005, seed: int | None = None) -> None:
+        """3DGS-MCMC exploration noise (mcmc.add_noise, mcmc.py:166-192) on the
+        active means, scaled by the current means learning rate."""
+        lr = self.lrs["means"] if lr_means is None else lr_means
+        _lib.call("mg_mcmc_add_noise", ptr(self.param("means")), ptr(self.param("quats")),
+                  ptr(self.param("log_scales")), ptr(self.param("logit_opac")), self.active,
+                  float(lr), float(weight), float(opacity_gate),
+                  self._mcmc_seed(seed) ^ 0x9E3779B97F4A7C15, None, _lib.stream())
+
     def _activate(self) -> None:
         """The forward's scales and opacities: exp / sigmoid of the
         parameters (train.py:221-222), then the 3D filter when one is set
@@ -338,7 +411,8 @@ class Trainer:
         _lib.call("mg_preprocess_forward_views", ptr(self.param("means")),
                   ptr(self.param("quats")), ptr(self.scales), ptr(self.param("sh_dc")),
                   ptr(self.param("sh_rest")), _lib.SH_SPLIT, ptr(self.opac),
-                  _lib.C.cast(cams, _lib.C.c_void_p), len(views), self.sh_degree, self.n, self.n,
+                  _lib.C.cast(cams, _lib.C.c_void_p), len(views), self.sh_degree, self.active,
+                  self.n,
                   ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color),
                   ptr(self.visibility_count()), _lib.stream())
         self._end(ev)
@@ -353,7 +427,7 @@ class Trainer:
         prep = st.prep_scratch(-(-view.width // self.tile) * -(-view.height // self.tile))
         _lib.check(L.mg_bin_prepare(
             ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), ptr(st.valid), ptr(st.depth),
-            self.n, view.width, view.height, self.tile, self.saturation_cut,
+            self.active, view.width, view.height, self.tile, self.saturation_cut,
             ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(), s), "bin_prepare")
         self._end(ev)
 
@@ -364,7 +438,7 @@ class Trainer:
         backward into the view's gradient records."""
         L = _lib.load()
         s = _lib.stream()
-        W, H, n = view.width, view.height, self.n
+        W, H, n = view.width, view.height, self.active
         st = self._state(v)
         b = self._buffers(W, H)
         tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
@@ -441,7 +515,7 @@ class Trainer:
         _lib.call("mg_preprocess_backward_views", ptr(self.param("means")),
                   ptr(self.param("quats")), ptr(self.scales if filt is None else self._scales_act),
                   ptr(self.opac if filt is None else self._opac_act), ptr(b.grad2d),
-                  ptr(b.valid), ptr(b.color), _lib.C.cast(cams, _lib.C.c_void_p), V, self.n,
+                  ptr(b.valid), ptr(b.color), _lib.C.cast(cams, _lib.C.c_void_p), V, self.active,
                   self.n, ptr(filt), ptr(self.grad("means")), ptr(self.grad("quats")),
                   ptr(self.grad("log_scales")), ptr(self.grad("logit_opac")), ptr(b.dpre),
                   _lib.stream())
@@ -452,8 +526,8 @@ class Trainer:
             centres[3 * v:3 * v + 3] = [cc[0], cc[1], cc[2]]
         ev = self._begin("sh_bwd")
         _lib.call("mg_sh_backward_views", ptr(self.param("means")), ptr(self.param("sh_dc")),
-                  ptr(self.param("sh_rest")), self.sh_degree, self.n,
-                  _lib.C.cast(centres, _lib.C.c_void_p), ptr(b.dpre), V,
+                  ptr(self.param("sh_rest")), self.sh_degree, self.active,
+                  _lib.C.cast(centres, _lib.C.c_void_p), ptr(b.dpre), V, self.n,
                   ptr(self.grad("means")), ptr(self.grad("sh_dc")), ptr(self.grad("sh_rest")),
                   _lib.stream())
         self._end(ev)
@@ -562,6 +636,8 @@ class Trainer:
 
 def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: int = 0,
         lr_means_end: float | None = None, sh_warmup: int = 0, filter_3d_every: int = 0,
+        noise_weight: float = 0.0, relocate_every: int = 0, relocate_until: int | None = None,
+        grow_to: int | None = None, grow_until: int | None = None,
         callback=None) -> list[float]:
     """The reference's training loop (train.py:311-366) over batches of views.
 
@@ -573,6 +649,11 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
     opacity/scale regularisers are not part of this loop. With
     `filter_3d_every`, Mip-Splatting's 3D filter is computed from all `views`
     before the first step and again every that many steps (train.py:343-380).
+    3DGS-MCMC as train.py:416-462 runs it: with `noise_weight`, the
+    exploration noise after every step at the current means learning rate;
+    with `relocate_every`, relocation every that many steps before
+    `relocate_until`, and with `grow_to`, growth of the active count from its
+    value at the start toward `grow_to` by `grow_until` on the same steps.
     `targets` are (H, W, 3) uint8 or float images, moved to the device per
     step; returns the per-step losses (one host read per step). With several
     ranks every rank draws the same batches and renders its own share of
@@ -584,6 +665,7 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
     lr0 = trainer.lrs["means"]
     decay = 1.0 if lr_means_end is None else (lr_means_end / max(lr0, 1e-12)) ** (1.0 / steps)
     rank_views = dp.shard(list(range(batch)), trainer.rank, trainer.world)
+    start_active = trainer.active
     losses = []
     for step in range(1, steps + 1):
         idx = []
@@ -604,6 +686,14 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
             t = torch.as_tensor(t).to(trainer.device, non_blocking=True)
             ts.append(t.float().div_(255.0) if t.dtype == torch.uint8 else t.float())
         losses.append(float(trainer.train_step([views[i] for i in mine], ts, batch)))
+        if noise_weight:
+            trainer.add_noise(trainer.lrs["means"], noise_weight)
+        densify_now = bool(relocate_every) and step % relocate_every == 0
+        if densify_now and step < (relocate_until if relocate_until is not None else steps + 1):
+            trainer.relocate()
+        if densify_now and grow_to is not None and step <= (grow_until or steps):
+            frac = min(1.0, step / max(grow_until or steps, 1))
+            trainer.grow(int(start_active + (grow_to - start_active) * frac))
         if callback is not None:
             callback(step, losses[-1])
     return losses

@@ -138,3 +138,71 @@ def test_noise_scale_and_gate(cuda):
     assert abs(float(low.mean())) < 0.02 * std
     assert abs(float(low.std()) / std - 1.0) < 0.01
     assert float(d[n // 2:].abs().max()) < 1e-3 * std
+
+
+# ------------------------------------------------------------ training engine
+
+def _engine_scene(seed=51, n=20000, W=160, H=120):
+    from metal_gauss_b200 import scenes
+    p, _, _ = scenes.config("cfg3", n=n, seed=seed)
+    p["logit_opac"][: n // 10] = -8.0                        # a tenth of the rows are dead
+    views = scenes.sphere_views(4, 4.0, W, H, 40.0, seed + 1, hemisphere=True)
+    g = np.random.default_rng(seed)
+    targets = [torch.from_numpy(g.random((H, W, 3)).astype(np.float32)).cuda() for _ in views]
+    return p, views, targets
+
+
+def test_trainer_relocation_equals_the_drop_in_on_its_buffers(cuda):
+    """Trainer.relocate on the flat buffers equals mcmc.relocate on the same
+    parameters as a dict, and resets the trainer's Adam rows it changed."""
+    from metal_gauss_b200.engine import SEGMENTS, Trainer
+    p, views, targets = _engine_scene()
+    tr = Trainer(p, cuda, sh_degree=3)
+    tr.train_step(views[:2], targets[:2], 2)                  # non-zero Adam state
+    d = {name: tr.param(name).clone().contiguous() for name, _ in SEGMENTS}
+    opac = torch.sigmoid(d["logit_opac"])
+    alive = (opac >= 0.005).nonzero(as_tuple=True)[0]
+    n_dead = int((opac < 0.005).sum())
+    picks = alive[torch.randint(0, alive.numel(), (n_dead,), device="cuda")]
+    assert tr.relocate(picks=picks) == n_dead > 0
+    mcmc.relocate(d, picks=picks)
+    for name, _ in SEGMENTS:
+        assert torch.equal(tr.param(name), d[name]), name
+    dead = (opac < 0.005).nonzero(as_tuple=True)[0]
+    changed = torch.cat([dead, torch.unique(picks)])
+    for name, w in SEGMENTS:
+        o = tr.offsets[name]
+        m = tr.M[o:o + w * tr.n].view(tr.n, w)
+        assert float(m[changed].abs().max()) == 0.0, name
+    assert float(tr.steps[changed].abs().max()) == 0.0
+
+
+def test_inactive_rows_are_not_rendered(cuda):
+    """With active = k the trainer renders and differentiates only the first
+    k rows: the same loss and gradients as a trainer holding only those."""
+    from metal_gauss_b200.engine import SEGMENTS, Trainer
+    from tests.golden.fixtures import rel_l2
+    p, views, targets = _engine_scene(53)
+    k = 15000
+    full = Trainer(p, cuda, sh_degree=3)
+    full.active = k
+    part = Trainer({name: v[:k] for name, v in p.items()}, cuda, sh_degree=3)
+    lf = float(full.train_step(views[:2], targets[:2], 2))
+    lp = float(part.train_step(views[:2], targets[:2], 2))
+    assert abs(lf - lp) < 1e-6
+    for name, _ in SEGMENTS:
+        assert rel_l2(full.grad(name)[:k].cpu().numpy(), part.grad(name).cpu().numpy()) < 1e-5
+        assert float(full.grad(name)[k:].abs().max()) == 0.0, name
+
+
+def test_fit_with_mcmc_grows_relocates_and_trains(cuda):
+    from metal_gauss_b200.engine import Trainer, fit
+    p, views, targets = _engine_scene(55)
+    tr = Trainer(p, cuda, sh_degree=3, lrs={"means": 1e-3})
+    tr.active = 12000
+    losses = fit(tr, views, [t.cpu() for t in targets], steps=6, batch=2, noise_weight=4e4,
+                 relocate_every=2, grow_to=20000, grow_until=6)
+    assert tr.active == 20000
+    assert all(np.isfinite(losses)) and losses[-1] < losses[0]
+    opac = torch.sigmoid(tr.param("logit_opac")[: tr.active])
+    assert float((opac < 0.005).float().mean()) < 0.05        # the dead tenth was relocated
