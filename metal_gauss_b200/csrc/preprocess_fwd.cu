@@ -436,10 +436,24 @@ __device__ __forceinline__ int64_t block_sorted_gaussian(const float2* __restric
     return (int64_t)blockIdx.x * blockDim.x + block_sorted_slot(cls);
 }
 
-// Stage A of the two-stage binning: tile counts plus the depth sort keys.
-// Gaussians that claim no tile get key 0xffffffff and sort behind every
-// positive depth (valid depths are > near > 0, whose bit patterns are below
-// 0x7f800000).
+// Depth sort keys. Valid depths are positive, so their bit patterns order
+// like the depths. When the view's depth range (range[0] = ~smallest bits,
+// range[1] = largest, from the saturation cut's range pass) spans fewer than
+// 2^24 - 1 patterns, keys are taken relative to the smallest: the same order,
+// every key below 2^24, so the sort's top 8-bit pass finds one digit and only
+// copies. Gaussians that claim no tile take the largest key and sort last.
+__device__ __forceinline__ bool relative_depth_keys(const uint32_t* range) {
+    return range != nullptr && range[1] != 0u && range[1] - ~range[0] < 0x00ffffffu;
+}
+__device__ __forceinline__ uint32_t depth_key(float d, const uint32_t* range) {
+    return relative_depth_keys(range) ? __float_as_uint(d) - ~range[0] : __float_as_uint(d);
+}
+__device__ __forceinline__ uint32_t no_depth_key(const uint32_t* range) {
+    return relative_depth_keys(range) ? 0x00ffffffu : 0xffffffffu;
+}
+
+// Stage A of the two-stage binning: tile counts plus the depth sort keys
+// (depth_key: Gaussians that claim no tile sort behind every valid depth).
 __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(const float2* __restrict__ uv,
                                        const float2* __restrict__ rxy,
                                        const float* __restrict__ conic,
@@ -472,7 +486,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
         }
     }
     counts[g] = c;
-    dkeys[g] = c > 0u ? __float_as_uint(depth[g]) : 0xffffffffu;
+    dkeys[g] = c > 0u ? depth_key(depth[g], range) : no_depth_key(range);
     dvals[g] = (uint32_t)g;
 }
 
@@ -612,6 +626,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
                                    int tile, int tiles_x, int tiles_y,
                                    const uint4* __restrict__ recs,
                                    const int32_t* __restrict__ cutoff,
+                                   const uint32_t* __restrict__ range,
                                    uint32_t* __restrict__ counts,
                                    uint32_t* __restrict__ dkeys) {
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -642,7 +657,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
                                          0u, 0, nullptr, CutArgs{nullptr, cutoff, gbin});
     }
     counts[g] = kept;
-    if (kept == 0u) dkeys[g] = 0xffffffffu;
+    if (kept == 0u) dkeys[g] = no_depth_key(range);
 }
 
 }  // namespace
@@ -737,7 +752,7 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
     MG_TRY(check_launch("bin_cutoff"));
     bin_recount_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
-        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, counts, dkeys);
+        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, cut_range, counts, dkeys);
     return check_launch("bin_recount");
 }
 

@@ -160,6 +160,21 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t mask = (1u << digit_bits) - 1u;
 
+    // A pass whose digit is the same for every key keeps the order: copy the
+    // tile through (each block decides alike from the digit offsets).
+    {
+        const uint32_t d0 = digit_of(keys_in[0], shift, mask);
+        const uint32_t next = d0 + 1u < (uint32_t)kRadix ? digit_offsets[d0 + 1u] : (uint32_t)n;
+        if (digit_offsets[d0] == 0u && (int64_t)next == n) {
+            for (int64_t i = (int64_t)blockIdx.x * TK + tid;
+                 i < min(n, (int64_t)(blockIdx.x + 1) * TK); i += kSortThreads) {
+                keys_out[i] = keys_in[i];
+                vals_out[i] = vals_in[i];
+            }
+            return;
+        }
+    }
+
     for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads)
         (&sm.warp_hist[0][0])[i] = 0u;
     if (tid == 0) sm.tile_id = atomicAdd(tile_counter, 1u);
