@@ -444,11 +444,14 @@ typedef struct mg_adam_segment {
     int64_t elem_begin;  /* update elements [elem_begin, elem_end) of the  */
     int64_t elem_end;    /* segment; elem_end == 0 means all rows * width  */
 } mg_adam_segment;
+/* row_scratch (selective mode, optional): `rows` floats the entry point uses
+ * to form each visible row's bias correction once instead of once per
+ * thread; NULL forms it in place. */
 mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
                         int64_t rows, const mg_adam_segment* segments,
                         int32_t n_segments, float b1, float b2, float eps,
                         const float* visible_count, float* steps, int64_t step,
-                        mg_stream_t stream);
+                        float* row_scratch, mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* SSIM (11-tap separable Gaussian, zero padding) and the training loss     */

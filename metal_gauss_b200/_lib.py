@@ -105,7 +105,7 @@ SIGNATURES = {
                                      vp]),
     "mg_selective_adam_advance_steps": (i32, [vp, vp, i64, i64, vp]),
     "mg_adam_multi": (i32, [vp, vp, vp, vp, i64, C.POINTER(AdamSegment), i32, f32, f32, f32, vp,
-                            vp, i64, vp]),
+                            vp, i64, vp, vp]),
     "mg_ssim_stack_blur_h": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "mg_ssim_blur15": (i32, [vp, vp, i32, i32, i32, vp, vp]),
     "mg_ssim_tail_forward": (i32, [vp, i32, i32, vp, vp]),

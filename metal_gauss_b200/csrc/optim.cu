@@ -63,6 +63,15 @@ __global__ void advance_steps_kernel(float* __restrict__ steps,
     if (r < n_visible && visible[r] != 0) steps[r] = __fadd_rn(steps[r], 1.0f);
 }
 
+// SelectiveAdam's per-row bias correction sqrt(1 - b2^k) / (1 - b1^k), k the
+// row's step count + 1, in the reference's operation order.
+__device__ __forceinline__ float selective_row_factor(float steps, float b1, float b2) {
+    const float k = __fadd_rn(steps, 1.0f);
+    const float c1 = __fsub_rn(1.0f, powf(b1, k));
+    const float c2 = __fsub_rn(1.0f, powf(b2, k));
+    return __fdiv_rn(__fsqrt_rn(c2), c1);
+}
+
 struct AdamSegments {
     int64_t offset[MG_MAX_ADAM_SEGMENTS];
     int64_t begin[MG_MAX_ADAM_SEGMENTS];
@@ -82,7 +91,9 @@ __global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict
                                   float* __restrict__ m, float* __restrict__ v, int64_t rows,
                                   AdamSegments segs, float b1, float b2, float eps, float w1,
                                   float w2, const float* __restrict__ vis,
-                                  const float* __restrict__ steps, float bc1, float sqrt_bc2) {
+                                  const float* __restrict__ steps,
+                                  const float* __restrict__ row_factor, float bc1,
+                                  float sqrt_bc2) {
     const int s = blockIdx.y;
     const int64_t off = segs.offset[s], first = segs.begin[s];
     const int width = segs.width[s];
@@ -125,12 +136,14 @@ __global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict
                 if (j < nk) {
                     if (r != r_done) {
                         r_done = r;
-                        live = vis[r] > 0.0f;
-                        if (live) {
-                            const float k = __fadd_rn(steps[r], 1.0f);
-                            const float c1 = __fsub_rn(1.0f, powf(b1, k));
-                            const float c2 = __fsub_rn(1.0f, powf(b2, k));
-                            step_size = __fmul_rn(lr, __fdiv_rn(__fsqrt_rn(c2), c1));
+                        if (row_factor) {  // precomputed once per row
+                            const float f = row_factor[r];
+                            live = f > 0.0f;
+                            step_size = __fmul_rn(lr, f);
+                        } else {
+                            live = vis[r] > 0.0f;
+                            if (live)
+                                step_size = __fmul_rn(lr, selective_row_factor(steps[r], b1, b2));
                         }
                     }
                     if (live) {
@@ -175,6 +188,16 @@ __global__ void adam_multi_kernel(float* __restrict__ p, const float* __restrict
             }
         }
     }
+}
+
+// sqrt(1 - b2^k) / (1 - b1^k) of every visible row (0 for the others), k its
+// step count + 1: the bias-correction factor of selective_adam_kernel, so
+// adam_multi_kernel's threads read it instead of each forming it again.
+__global__ void row_factor_kernel(const float* __restrict__ vis, const float* __restrict__ steps,
+                                  int64_t rows, float b1, float b2, float* __restrict__ out) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    out[r] = vis[r] > 0.0f ? selective_row_factor(steps[r], b1, b2) : 0.0f;
 }
 
 __global__ void advance_steps_count_kernel(float* __restrict__ steps,
@@ -235,7 +258,8 @@ extern "C" mg_status mg_selective_adam_advance_steps(float* steps, const uint8_t
 extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v, int64_t rows,
                                    const mg_adam_segment* segments, int32_t n_segments,
                                    float b1, float b2, float eps, const float* visible_count,
-                                   float* steps, int64_t step, mg_stream_t stream) {
+                                   float* steps, int64_t step, float* row_scratch,
+                                   mg_stream_t stream) {
     MG_REQUIRE(n_segments >= 0 && n_segments <= MG_MAX_ADAM_SEGMENTS &&
                    (n_segments == 0 || segments != nullptr),
                "adam_multi: 0..MG_MAX_ADAM_SEGMENTS segments");
@@ -265,9 +289,16 @@ extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int gx = (int)std::min<int64_t>((max_count + 1023) / 1024, 148 * 8);
     if (n_segments > 0) {
+        const float* rowf = nullptr;
+        if (visible_count && row_scratch) {
+            row_factor_kernel<<<ceil_div(rows, 256), 256, 0, st>>>(visible_count, steps, rows, b1,
+                                                                    b2, row_scratch);
+            MG_TRY(check_launch("adam_multi row factors"));
+            rowf = row_scratch;
+        }
         adam_multi_kernel<<<dim3(std::max(gx, 1), n_segments), 256, 0, st>>>(
-            p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, (float)bc1,
-            (float)sq);
+            p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, rowf,
+            (float)bc1, (float)sq);
         MG_TRY(check_launch("adam_multi"));
     }
     if (visible_count) {

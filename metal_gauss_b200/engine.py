@@ -175,6 +175,7 @@ class Trainer:
         self.M = torch.zeros(self.p_total, **f32)
         self.V = torch.zeros(self.p_total, **f32)
         self.steps = torch.zeros(self.n_pad, **f32)
+        self._adam_rows = torch.empty(self.n_pad, **f32)  # per-row bias factors
         self.step_count = 0
         for name, _ in SEGMENTS:
             self.param(name).copy_(params[name].to(self.device, torch.float32).reshape(
@@ -557,11 +558,11 @@ class Trainer:
             arr = (_lib.AdamSegment * len(segs))(*segs)
             _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
                       arr, len(segs), b1, b2, self.eps, ptr(vis), ptr(self.steps),
-                      self.step_count, _lib.stream())
+                      self.step_count, ptr(self._adam_rows), _lib.stream())
         elif vis is not None:  # no elements here: still advance the shared step counts
             _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
                       (_lib.AdamSegment * 1)(_lib.AdamSegment(0, 1, 0.0, 0, 0)), 0, b1, b2,
-                      self.eps, ptr(vis), ptr(self.steps), self.step_count, _lib.stream())
+                      self.eps, ptr(vis), ptr(self.steps), self.step_count, None, _lib.stream())
         self._end(ev)
 
     def train_step(self, views, targets, global_batch: int | None = None) -> torch.Tensor:
