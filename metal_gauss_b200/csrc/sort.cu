@@ -26,6 +26,14 @@ namespace {
 
 constexpr int kRadixBits = 8;
 constexpr int kRadix = 1 << kRadixBits;
+
+// Bits per pass: the key bits split evenly over the fewest 8-bit-or-narrower
+// passes (12-bit tile ids sort as 6 + 6, not 8 + 4: 64 bins per pass keep the
+// scatter's runs longer than 256 would).
+__host__ __device__ __forceinline__ int pass_bits(int bits) {
+    const int passes = (bits + kRadixBits - 1) / kRadixBits;
+    return (bits + passes - 1) / passes;
+}
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kHistPrivatePasses = 4;  // per-warp histogram copies up to this many passes
@@ -106,8 +114,8 @@ radix_histogram_kernel(const K* __restrict__ keys, int64_t n, int bits, int pass
          i += (int64_t)gridDim.x * kSortThreads) {
         const K k = keys[i];
         for (int p = 0; p < passes; ++p) {
-            const int shift = p * kRadixBits;
-            const int db = min(kRadixBits, bits - shift);
+            const int shift = p * pass_bits(bits);
+            const int db = min(pass_bits(bits), bits - shift);
             atomicAdd(&mine[p * kRadix + digit_of(k, shift, (1u << db) - 1u)], 1u);
         }
     }
@@ -223,12 +231,17 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
         sm.warp_hist[w][d] = tile_count;
         tile_count += c;
     }
-    // Publish this tile's aggregate first so successors can proceed.
+    // Publish this tile's aggregate first so successors can proceed. Digits a
+    // narrow pass cannot produce are empty in every tile: no tile publishes
+    // or reads their words.
+    const bool in_pass = d <= (int)mask;
     uint32_t* my_status = status + (int64_t)tile * kRadix + d;
-    if (tile == 0) {
-        atomicExch(my_status, kFlagInc | tile_count);
-    } else {
-        atomicExch(my_status, kFlagAgg | tile_count);
+    if (in_pass) {
+        if (tile == 0) {
+            atomicExch(my_status, kFlagInc | tile_count);
+        } else {
+            atomicExch(my_status, kFlagAgg | tile_count);
+        }
     }
     // Exclusive scan of tile counts over digits -> local layout.
     sm.local_start[d] = tile_count;
@@ -246,7 +259,7 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     // up to the first inclusive prefix; a word not yet published ends the
     // round and is read again.
     uint32_t excl = 0u;
-    if (tile > 0) {
+    if (tile > 0 && in_pass) {
         int64_t t = (int64_t)tile - 1;
         uint32_t spins = 0u;
         for (;;) {
@@ -491,8 +504,8 @@ mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_
     K* kin = keys; uint32_t* vin = vals;
     K* kout = keys_alt; uint32_t* vout = vals_alt;
     for (int p = 0; p < s.passes; ++p) {
-        const int shift = p * kRadixBits;
-        const int db = std::min(kRadixBits, bits - shift);
+        const int shift = p * pass_bits(bits);
+        const int db = std::min(pass_bits(bits), bits - shift);
         onesweep_pass_kernel<K><<<s.tiles, kSortThreads, 0, stream>>>(
             kin, vin, kout, vout, n, shift, db, s.hist + p * kRadix, s.tile_counter + p,
             s.status + (size_t)p * s.tiles * kRadix, err);
