@@ -494,9 +494,12 @@ class Trainer:
         return ViewStats(pairs=m)
 
     def forward_backward_views(self, views, targets, scale: float) -> list[ViewStats]:
-        """Render this rank's views, adding scale * each loss into self.loss
-        and scale * each parameter gradient into self.G. One device->host
-        read per call (all views' pair totals)."""
+        """Render this rank's views: scale * each loss is added into
+        self.loss, scale * the views' gradients of means, quats, log-scales and
+        opacity logits are added into self.G and the views' SH gradients are
+        written into it (the SH adjoint covers all of a call's views at once
+        and overwrites its rows; `train_step` zeroes the rest of G first). One
+        device->host read per call (all views' pair totals)."""
         V = len(views)
         if V > self._totals.numel():
             self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
@@ -574,8 +577,10 @@ class Trainer:
         gb = global_batch or len(views) * world
         ev = self._begin("activations")
         self._activate()
-        self.G.zero_()
-        self.loss.zero_()
+        # the SH rows are overwritten by the SH adjoint; the geometry rows and
+        # the visibility/loss tail accumulate
+        self.G[:self.offsets["sh_dc"]].zero_()
+        self.G[self.vis_offset:].zero_()  # visibility counts and the loss
         self._end(ev)
         self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb)
         if world > 1 and self.shard_optimizer:

@@ -98,3 +98,16 @@ def test_renderer_applies_the_3d_filter(cuda):
                                   v.viewmat.numpy(), W, H, sh_degree=3, sh_rest=pn["sh_rest"],
                                   background=None)
         assert np.abs(rgb.cpu().numpy() - ref).max() < 1e-4
+
+
+def test_filter_when_no_camera_sees_anything(cuda):
+    """Every Gaussian behind the camera: all take depth 1, as the reference
+    does (mipfilter.py:70-73), and the result matches the oracle."""
+    means = torch.zeros(100, 3)
+    means[:, 2] = -10.0                                        # camera looks along +z
+    K = np.array([[500.0, 0, 80], [0, 500.0, 60], [0, 0, 1]], np.float32)
+    vm = np.eye(4, dtype=np.float32)
+    got = mipfilter.compute_3d_filter(means.cuda(), [_View(K, vm, 160, 120)]).cpu().numpy()
+    ref = oracle.compute_3d_filter(means.numpy(), [(K, vm, 160, 120)])
+    assert np.array_equal(got, ref)
+    assert np.allclose(got, (1.0 / 500.0) * np.sqrt(0.2), rtol=1e-6)

@@ -206,3 +206,25 @@ def test_fit_with_mcmc_grows_relocates_and_trains(cuda):
     assert all(np.isfinite(losses)) and losses[-1] < losses[0]
     opac = torch.sigmoid(tr.param("logit_opac")[: tr.active])
     assert float((opac < 0.005).float().mean()) < 0.05        # the dead tenth was relocated
+
+
+def test_relocate_and_grow_edge_cases(cuda):
+    """No dead rows, no live rows, non-finite weights (the reference falls
+    back to opacity), growth to at most the current count: as mcmc.py."""
+    p = _table(50, 0, 4)                                       # nothing dead
+    before = {k: v.clone() for k, v in p.items()}
+    assert mcmc.relocate(p, seed=1) == 0
+    assert all(torch.equal(p[k], before[k]) for k in p)
+    q = _table(0, 40, 5)                                       # nothing alive
+    qb = {k: v.clone() for k, v in q.items()}
+    assert mcmc.relocate(q, seed=1) == 0
+    assert all(torch.equal(q[k], qb[k]) for k in q)
+    r = _table(8, 1000, 6)
+    w = torch.full((1008,), float("nan"), device="cuda")      # -> opacity weights
+    assert mcmc.relocate(r, weights=w, seed=2) == 1000
+    src = r["means"][8:, 0].round().long()
+    assert int(src.max()) < 8                                  # all landed on live rows
+    s = _table(30, 0, 7)
+    sb = {k: v.clone() for k, v in s.items()}
+    assert mcmc.grow(s, 20, 30, seed=3) == 30                  # target below active
+    assert all(torch.equal(s[k], sb[k]) for k in s)
