@@ -302,6 +302,39 @@ mg_status mg_bin_emit(
     const void* prepare_scratch, int32_t* gauss_ids, int32_t* tile_offsets,
     void* scratch, size_t scratch_bytes, mg_stream_t stream);
 
+/* The two binning stages for a batch of 1..64 views of one frame size in one
+ * call each (no reference counterpart: the reference bins each view inside
+ * its own render call, metal_backend.py:239-262). The inputs are view-major
+ * (view v's Gaussian g at row v * view_stride + g, opacity at
+ * v * opacity_view_stride + g, 0 when the views share it); n * n_views must
+ * stay below 2^31.
+ *   mg_bin_prepare_views writes n_views + 2 int64 words to totals_dev: each
+ *     view's pair total, the batch's total, and an overflow flag. A set flag
+ *     means some view's visible depths span more float bit patterns than
+ *     the batch's shared depth keys hold (2^(32 - ceil(log2 n_views)) - 1):
+ *     the call's results are then unusable and the caller bins that batch one
+ *     view at a time with mg_bin_prepare / mg_bin_emit.
+ *   mg_bin_emit_views takes the batch total m_total and writes the pairs of
+ *     view v to gauss_ids[base_v, base_v + m_v) (base_v: the totals of the
+ *     views before v) and its tile offsets, starting at 0 as mg_bin_emit's,
+ *     to tile_offsets[v * (n_tiles + 1) ...]. Each view's lists equal the
+ *     lists mg_bin_prepare / mg_bin_emit give for that view alone. */
+size_t mg_bin_prepare_views_scratch_bytes(int64_t n, int32_t n_views, int32_t n_tiles);
+mg_status mg_bin_prepare_views(
+    const float* uv, const float* rxy, const float* conic, const float* opacity,
+    const int32_t* valid, const float* depth, int64_t n, int32_t n_views,
+    int64_t view_stride, int64_t opacity_view_stride, int32_t width, int32_t height,
+    int32_t tile, int32_t saturation_cut, int64_t* totals_dev, void* scratch,
+    size_t scratch_bytes, mg_stream_t stream);
+size_t mg_bin_emit_views_scratch_bytes(int64_t n, int32_t n_views, int64_t m_total,
+                                       int32_t n_tiles);
+mg_status mg_bin_emit_views(
+    const float* uv, const float* rxy, const float* conic, const float* opacity, int64_t n,
+    int32_t n_views, int64_t view_stride, int64_t opacity_view_stride, int64_t m_total,
+    int32_t width, int32_t height, int32_t tile, int32_t saturation_cut,
+    const void* prepare_scratch, int32_t* gauss_ids, int32_t* tile_offsets, void* scratch,
+    size_t scratch_bytes, mg_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* Rasterisation                                                            */
 /* ------------------------------------------------------------------------ */

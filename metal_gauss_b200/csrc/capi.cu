@@ -35,7 +35,9 @@ struct PrepareScratch {
     uint32_t* dvals_alt;
     uint32_t* offsets;
     uint4* recs;  // per Gaussian: the count walk's pass mask and rectangle
-    uint32_t* cut_range;  // saturation cut: depth range words, then the histogram
+    uint32_t* cut_range;  // depth range words (two per view), then the histogram
+    int32_t* overflow;    // batch depth keys that did not fit (after the range words)
+    size_t range_bytes;   // range words + overflow word
     uint32_t* cut_hist;
     int32_t* cutoff;
     size_t cut_zero_bytes;  // range words + histogram, zeroed per call
@@ -45,9 +47,12 @@ struct PrepareScratch {
     size_t total;
 };
 
-PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles) {
+// Rows for n_views * n Gaussians; n_views = 1 is the single-view layout.
+PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles, int n_views = 1) {
     PrepareScratch s;
     char* p = const_cast<char*>(static_cast<const char*>(base));
+    n *= n_views;
+    n_tiles *= n_views;
     const size_t arr = align256(sizeof(uint32_t) * (size_t)std::max<int64_t>(n, 1));
     s.counts = reinterpret_cast<uint32_t*>(p); p += arr;
     s.dkeys = reinterpret_cast<uint32_t*>(p); p += arr;
@@ -58,8 +63,12 @@ PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles) {
     s.recs = reinterpret_cast<uint4*>(p);
     p += align256(sizeof(uint4) * (size_t)std::max<int64_t>(n, 1));
     s.cut_range = reinterpret_cast<uint32_t*>(p);
-    s.cut_hist = s.cut_range + 64;  // keeps the histogram 256-byte aligned
-    s.cut_zero_bytes = sizeof(uint32_t) * (64 + (size_t)std::max(n_tiles, 1) * kSaturationBins);
+    s.overflow = reinterpret_cast<int32_t*>(s.cut_range + 2 * n_views);
+    const size_t range_words = ((size_t)(2 * n_views + 1) + 63) & ~(size_t)63;
+    s.range_bytes = sizeof(uint32_t) * range_words;
+    s.cut_hist = s.cut_range + range_words;  // keeps the histogram 256-byte aligned
+    s.cut_zero_bytes =
+        s.range_bytes + sizeof(uint32_t) * (size_t)std::max(n_tiles, 1) * kSaturationBins;
     p += align256(s.cut_zero_bytes);
     s.cutoff = reinterpret_cast<int32_t*>(p);
     p += align256(sizeof(int32_t) * (size_t)std::max(n_tiles, 1));
@@ -74,22 +83,33 @@ struct EmitScratch {
     uint32_t* pair_tiles;
     uint32_t* tiles_alt;
     uint32_t* ids_alt;
+    int32_t* batch_offsets;  // batches: tile ranges over all views' tiles
     void* sort;
     size_t sort_bytes;
     size_t total;
 };
 
-EmitScratch carve_emit(void* base, int64_t m, int n_tiles) {
+// m pairs over n_views views of n_tiles tiles each.
+EmitScratch carve_emit(void* base, int64_t m, int n_tiles, int n_views = 1) {
     EmitScratch s;
     char* p = static_cast<char*>(base);
     const size_t arr = align256(sizeof(uint32_t) * (size_t)std::max<int64_t>(m, 1));
     s.pair_tiles = reinterpret_cast<uint32_t*>(p); p += arr;
     s.tiles_alt = reinterpret_cast<uint32_t*>(p); p += arr;
     s.ids_alt = reinterpret_cast<uint32_t*>(p); p += arr;
-    s.sort_bytes = align256(radix_sort_scratch_bytes(m, tile_bits(n_tiles), 4));
+    s.batch_offsets = reinterpret_cast<int32_t*>(p);
+    if (n_views > 1) p += align256(sizeof(int32_t) * ((size_t)n_tiles * n_views + 1));
+    s.sort_bytes = align256(radix_sort_scratch_bytes(m, tile_bits(n_tiles * n_views), 4));
     s.sort = p; p += s.sort_bytes;
     s.total = (size_t)(p - static_cast<char*>(base));
     return s;
+}
+
+// Bits of a view index in a batch of n_views (0 for one view).
+int view_bits(int n_views) {
+    int b = 0;
+    while ((1 << b) < n_views) ++b;
+    return b;
 }
 
 }  // namespace
@@ -289,7 +309,7 @@ extern "C" mg_status mg_bin_prepare(const float* uv, const float* rxy, const flo
                                   tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, s.recs,
                                   saturation_cut ? s.cut_range : nullptr,
                                   saturation_cut ? s.cut_hist : nullptr,
-                                  saturation_cut ? s.cutoff : nullptr, st));
+                                  saturation_cut ? s.cutoff : nullptr, BinViews{}, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, n, 32, s.sort,
                                       s.sort_bytes, &in_alt, st));
@@ -325,7 +345,8 @@ extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float*
     uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
     MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m, width,
                            height, tile, tiles_x, tiles_y, p.recs,
-                           saturation_cut ? p.cutoff : nullptr, e.pair_tiles, ids, st));
+                           saturation_cut ? p.cutoff : nullptr, e.pair_tiles, ids, BinViews{},
+                           st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m,
                                       tile_bits(n_tiles), e.sort, e.sort_bytes, &in_alt, st));
@@ -334,4 +355,143 @@ extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float*
                                   cudaMemcpyDeviceToDevice, st) != cudaSuccess)
         return check_launch("bin_emit copy");
     return launch_tile_ranges(sorted_tiles, nullptr, m, n_tiles, tile_offsets, st);
+}
+
+// ------------------------------------------------------ batches of views
+//
+// The same two stages for every view of a batch (all of one frame size) at
+// once: each stage is one launch over all views, and the batch shares one
+// depth sort and one tile sort, whose keys carry the view above the depth
+// (tile), so each view's order is the one its own sort gives.
+
+namespace {
+
+mg_status check_views(int64_t n, int32_t n_views, int64_t view_stride,
+                      int64_t opacity_view_stride, int32_t width, int32_t height, int32_t tile,
+                      const char* what) {
+    if (tile <= 0 || width <= 0 || height <= 0)
+        return fail(MG_ERR_INVALID_ARGUMENT, std::string(what) + ": bad tiling");
+    if (n_views < 1 || n_views > 64)
+        return fail(MG_ERR_INVALID_ARGUMENT, std::string(what) + ": 1..64 views");
+    if (n < 0 || view_stride < n || opacity_view_stride < 0)
+        return fail(MG_ERR_INVALID_ARGUMENT, std::string(what) + ": bad view strides");
+    if (n * n_views >= ((int64_t)1 << 31))
+        return fail(MG_ERR_CAPACITY, std::string(what) + ": views x Gaussians exceed 2^31");
+    return MG_OK;
+}
+
+}  // namespace
+
+extern "C" size_t mg_bin_prepare_views_scratch_bytes(int64_t n, int32_t n_views,
+                                                     int32_t n_tiles) {
+    if (n < 0 || n_views < 1 || n_tiles <= 0) return 0;
+    return carve_prepare(nullptr, n, n_tiles, n_views).total;
+}
+
+extern "C" mg_status mg_bin_prepare_views(const float* uv, const float* rxy, const float* conic,
+                                          const float* opacity, const int32_t* valid,
+                                          const float* depth, int64_t n, int32_t n_views,
+                                          int64_t view_stride, int64_t opacity_view_stride,
+                                          int32_t width, int32_t height, int32_t tile,
+                                          int32_t saturation_cut, int64_t* totals_dev,
+                                          void* scratch, size_t scratch_bytes,
+                                          mg_stream_t stream) {
+    MG_TRY(check_views(n, n_views, view_stride, opacity_view_stride, width, height, tile,
+                       "bin_prepare_views"));
+    MG_REQUIRE(totals_dev != nullptr, "bin_prepare_views: null totals");
+    const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
+    const PrepareScratch s = carve_prepare(scratch, n, tiles_x * tiles_y, n_views);
+    MG_REQUIRE(scratch != nullptr && scratch_bytes >= s.total,
+               "bin_prepare_views: scratch too small");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(s.cut_range, 0, saturation_cut ? s.cut_zero_bytes : s.range_bytes, st) !=
+        cudaSuccess)
+        return check_launch("bin_prepare_views memset");
+    const int64_t rows = n * n_views;
+    if (n > 0) {
+        MG_REQUIRE(uv && rxy && conic && opacity && valid && depth,
+                   "bin_prepare_views: null pointer");
+        BinViews bv;
+        bv.n_views = n_views;
+        bv.in_stride = view_stride;
+        bv.opac_stride = opacity_view_stride;
+        bv.key_shift = n_views > 1 ? 32 - view_bits(n_views) : 0;
+        bv.overflow = s.overflow;
+        MG_TRY(launch_bin_count_depth(uv, rxy, conic, opacity, valid, depth, n, width, height,
+                                      tile, tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, s.recs,
+                                      s.cut_range, saturation_cut ? s.cut_hist : nullptr,
+                                      saturation_cut ? s.cutoff : nullptr, bv, st));
+        bool in_alt = false;
+        MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, rows, 32,
+                                          s.sort, s.sort_bytes, &in_alt, st));
+        if (in_alt && cudaMemcpyAsync(s.dvals, s.dvals_alt, sizeof(uint32_t) * rows,
+                                      cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return check_launch("bin_prepare_views copy");
+    }
+    MG_TRY(exclusive_scan_gather(s.counts, s.dvals, rows, s.offsets, totals_dev + n_views, s.scan,
+                                 st));
+    if (n == 0)
+        return cudaMemsetAsync(totals_dev, 0, sizeof(int64_t) * (n_views + 2), st) == cudaSuccess
+                   ? MG_OK
+                   : check_launch("bin_prepare_views totals");
+    return launch_view_totals(s.offsets, n, n_views, s.overflow, totals_dev, st);
+}
+
+extern "C" size_t mg_bin_emit_views_scratch_bytes(int64_t n, int32_t n_views, int64_t m_total,
+                                                  int32_t n_tiles) {
+    (void)n;
+    if (n_views < 1 || n_tiles <= 0 || m_total < 0) return 0;
+    return carve_emit(nullptr, m_total, n_tiles, n_views).total;
+}
+
+extern "C" mg_status mg_bin_emit_views(const float* uv, const float* rxy, const float* conic,
+                                       const float* opacity, int64_t n, int32_t n_views,
+                                       int64_t view_stride, int64_t opacity_view_stride,
+                                       int64_t m_total, int32_t width, int32_t height,
+                                       int32_t tile, int32_t saturation_cut,
+                                       const void* prepare_scratch, int32_t* gauss_ids,
+                                       int32_t* tile_offsets, void* scratch,
+                                       size_t scratch_bytes, mg_stream_t stream) {
+    MG_TRY(check_views(n, n_views, view_stride, opacity_view_stride, width, height, tile,
+                       "bin_emit_views"));
+    MG_REQUIRE(m_total >= 0 && m_total < ((int64_t)1 << 31),
+               "bin_emit_views: pair count exceeds 2^31");
+    MG_REQUIRE(prepare_scratch != nullptr && tile_offsets != nullptr,
+               "bin_emit_views: null pointer");
+    const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
+    const int n_tiles = tiles_x * tiles_y;
+    MG_REQUIRE((int64_t)n_tiles * n_views < ((int64_t)1 << 31), "bin_emit_views: too many tiles");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (m_total == 0) {
+        if (cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t) * (size_t)n_views * (n_tiles + 1),
+                            st) != cudaSuccess)
+            return check_launch("bin_emit_views memset");
+        return MG_OK;
+    }
+    MG_REQUIRE(gauss_ids != nullptr && uv && rxy && conic && opacity,
+               "bin_emit_views: null pointer");
+    const EmitScratch e = carve_emit(scratch, m_total, n_tiles, n_views);
+    MG_REQUIRE(scratch != nullptr && scratch_bytes >= e.total, "bin_emit_views: scratch too small");
+    const PrepareScratch p = carve_prepare(prepare_scratch, n, n_tiles, n_views);
+    BinViews bv;
+    bv.n_views = n_views;
+    bv.in_stride = view_stride;
+    bv.opac_stride = opacity_view_stride;
+    uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
+    MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m_total,
+                           width, height, tile, tiles_x, tiles_y, p.recs,
+                           saturation_cut ? p.cutoff : nullptr, e.pair_tiles, ids, bv, st));
+    bool in_alt = false;
+    MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m_total,
+                                      tile_bits(n_tiles * n_views), e.sort, e.sort_bytes,
+                                      &in_alt, st));
+    const uint32_t* sorted_tiles = in_alt ? e.tiles_alt : e.pair_tiles;
+    if (in_alt && cudaMemcpyAsync(ids, e.ids_alt, sizeof(uint32_t) * m_total,
+                                  cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return check_launch("bin_emit_views copy");
+    if (n_views == 1)
+        return launch_tile_ranges(sorted_tiles, nullptr, m_total, n_tiles, tile_offsets, st);
+    MG_TRY(launch_tile_ranges(sorted_tiles, nullptr, m_total, n_tiles * n_views,
+                              e.batch_offsets, st));
+    return launch_view_tile_offsets(e.batch_offsets, n_tiles, n_views, tile_offsets, st);
 }

@@ -31,13 +31,31 @@ mg_status launch_bin_write(const float* uv, const float* rxy, const float* conic
                            int64_t n, int W, int H, int tile, int tiles_x,
                            int tiles_y, uint64_t* keys, int32_t* ids,
                            cudaStream_t stream);
+// A batch of views binned by one launch per stage (blockIdx.y is the view).
+// Inputs are view-major with in_stride rows between views (opacity:
+// opac_stride, 0 when the views share it); the per-Gaussian outputs are
+// compact, view v's rows at v * n, and view v's cut words at cut_range + 2 v,
+// its histogram and cutoffs after those of the views before it. key_shift 0
+// keeps the single-view depth keys; otherwise a key is (v << key_shift) |
+// (depth bits - the view's smallest depth bits), so one sort orders every
+// view, and a view whose depth range needs more than key_shift bits sets
+// *overflow (the caller then bins the views one at a time).
+struct BinViews {
+    int n_views = 1;
+    int64_t in_stride = 0;
+    int64_t opac_stride = 0;
+    int key_shift = 0;
+    int32_t* overflow = nullptr;
+};
+// cut_range non-null: the range pass runs (relative depth keys); cut_hist
+// non-null: the saturation cut runs as well.
 mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float* conic,
                                  const float* opacity, const int32_t* valid,
                                  const float* depth, int64_t n, int W, int H, int tile,
                                  int tiles_x, int tiles_y, uint32_t* counts,
                                  uint32_t* dkeys, uint32_t* dvals, uint4* recs,
                                  uint32_t* cut_range, uint32_t* cut_hist, int32_t* cutoff,
-                                 cudaStream_t stream);
+                                 const BinViews& bv, cudaStream_t stream);
 // Saturation-cut histogram bins per tile (cut_hist holds n_tiles of them;
 // cut_range two zeroed words before the call; see preprocess_fwd.cu).
 constexpr int kSaturationBins = 64;
@@ -46,7 +64,16 @@ mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
                           const uint4* recs, const int32_t* cutoff, uint32_t* pair_tiles,
-                          uint32_t* pair_ids, cudaStream_t stream);
+                          uint32_t* pair_ids, const BinViews& bv, cudaStream_t stream);
+// Batch bookkeeping: per-view pair totals from the scan of the batch's depth
+// order (view v's n sorted slots start at v * n; totals[n_views] holds the
+// grand total already), and totals[n_views + 1] = *overflow.
+mg_status launch_view_totals(const uint32_t* offsets, int64_t n, int n_views,
+                             const int32_t* overflow, int64_t* totals, cudaStream_t stream);
+// Per-view tile offsets starting at 0 from the batch's tile ranges
+// (global: n_views * n_tiles + 1 entries; local: n_views * (n_tiles + 1)).
+mg_status launch_view_tile_offsets(const int32_t* global, int n_tiles, int n_views,
+                                   int32_t* local, cudaStream_t stream);
 
 // sort.cu
 // Sorts in place between (keys, vals) and (keys_alt, vals_alt); returns in

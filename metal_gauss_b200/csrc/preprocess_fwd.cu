@@ -273,13 +273,14 @@ __device__ __forceinline__ uint32_t tile_optical_depth(float mux, float muy, flo
 // depth bin), so the emission can expand the mask instead of testing every
 // tile again. kCut: 1 adds covering Gaussians to the saturation histogram,
 // 2 keeps only tiles whose cutoff bin is not before the Gaussian's bin.
+// Emitted pair tiles are offset by tile_base (a view's first tile in a batch).
 template <bool kEmit64, bool kEmitPair, int kCut = 0>
 __device__ __forceinline__ uint32_t bin_walk(
     float mux, float muy, float rx, float ry, float ca, float cb, float cc,
     float op, uint32_t dbits, int tile, int tiles_x, int tiles_y, int W, int H,
     uint64_t* keys, int32_t* ids, uint32_t* pair_tiles, uint32_t* pair_ids,
     int64_t write_at, uint32_t cap, int32_t gid, uint4* rec = nullptr,
-    CutArgs cut = CutArgs{nullptr, nullptr, 0}) {
+    CutArgs cut = CutArgs{nullptr, nullptr, 0}, uint32_t tile_base = 0u) {
     const TileRect tr = tile_rect(mux, muy, rx, ry, tile, tiles_x, tiles_y);
     const float oa = 255.0f * op;
     if (oa <= 1.0f) return 0u;
@@ -327,7 +328,7 @@ __device__ __forceinline__ uint32_t bin_walk(
                         keys[write_at + cnt] = ((uint64_t)tid << 32) | (uint64_t)dbits;
                         ids[write_at + cnt] = gid;
                     } else {
-                        pair_tiles[write_at + cnt] = tid;
+                        pair_tiles[write_at + cnt] = tile_base + tid;
                         pair_ids[write_at + cnt] = (uint32_t)gid;
                     }
                 }
@@ -451,6 +452,19 @@ __device__ __forceinline__ uint32_t depth_key(float d, const uint32_t* range) {
 __device__ __forceinline__ uint32_t no_depth_key(const uint32_t* range) {
     return relative_depth_keys(range) ? 0x00ffffffu : 0xffffffffu;
 }
+// Batch keys (BinViews::key_shift > 0): the view above the depth relative to
+// the view's smallest, so a stable sort of the batch orders every view as its
+// own sort would; the no-tile key is the view's largest.
+__device__ __forceinline__ uint32_t view_depth_key(float d, const uint32_t* range, int v,
+                                                   int key_shift) {
+    if (key_shift == 0) return depth_key(d, range);
+    return ((uint32_t)v << key_shift) | (__float_as_uint(d) - ~range[0]);
+}
+__device__ __forceinline__ uint32_t view_no_depth_key(const uint32_t* range, int v,
+                                                      int key_shift) {
+    if (key_shift == 0) return no_depth_key(range);
+    return ((uint32_t)v << key_shift) | ((1u << key_shift) - 1u);
+}
 
 // Stage A of the two-stage binning: tile counts plus the depth sort keys
 // (depth_key: Gaussians that claim no tile sort behind every valid depth).
@@ -466,7 +480,19 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
                                        uint32_t* __restrict__ dvals,
                                        uint4* __restrict__ recs,
                                        const uint32_t* __restrict__ range,
-                                       uint32_t* __restrict__ hist) {
+                                       uint32_t* __restrict__ hist, BinViews bv) {
+    const int v = blockIdx.y;
+    {  // view v's slice of the batch
+        const int64_t vin = (int64_t)v * bv.in_stride, vout = (int64_t)v * n;
+        uv += vin; rxy += vin; conic += 3 * vin; valid += vin; depth += vin;
+        opacity += (int64_t)v * bv.opac_stride;
+        counts += vout; dkeys += vout; dvals += vout; recs += vout;
+        if (range) range += 2 * v;
+        if (hist) hist += (int64_t)v * tiles_x * tiles_y * kCutBins;
+        if (bv.key_shift && blockIdx.x == 0 && threadIdx.x == 0 &&
+            range[1] - ~range[0] > (1u << bv.key_shift) - 2u)
+            *bv.overflow = 1;
+    }
     const int64_t g = block_sorted_gaussian(uv, rxy, valid, n, tile, tiles_x, tiles_y);
     if (g >= n) return;
     uint32_t c = 0u;
@@ -486,8 +512,9 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
         }
     }
     counts[g] = c;
-    dkeys[g] = c > 0u ? depth_key(depth[g], range) : no_depth_key(range);
-    dvals[g] = (uint32_t)g;
+    dkeys[g] = c > 0u ? view_depth_key(depth[g], range, v, bv.key_shift)
+                      : view_no_depth_key(range, v, bv.key_shift);
+    dvals[g] = (uint32_t)((int64_t)v * n + g);
 }
 
 // Stage B: emit every (tile, Gaussian) pair with Gaussians in depth order.
@@ -504,15 +531,29 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
                                 int tiles_y, const uint4* __restrict__ recs,
                                 const int32_t* __restrict__ cutoff,
                                 uint32_t* __restrict__ pair_tiles,
-                                uint32_t* __restrict__ pair_ids) {
-    const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= n) return;
-    const uint32_t g = sorted_gid[s];
-    const uint32_t cnt = counts[g];
+                                uint32_t* __restrict__ pair_ids, BinViews bv) {
+    const int64_t sl = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (sl >= n) return;
+    // view v owns the batch's sorted slots [v n, (v + 1) n); its pairs carry
+    // tiles v * n_tiles + t and the Gaussian's index within the view
+    const int v = blockIdx.y;
+    const int64_t vout = (int64_t)v * n, s = vout + sl;
+    const uint32_t gv = sorted_gid[s];
+    const uint32_t g = gv - (uint32_t)vout;
+    if ((int64_t)g >= n) return;
+    const uint32_t cnt = counts[gv];
     if (cnt == 0u) return;
     const int64_t at = offsets[s];
     if (at + cnt > m) return;
-    const uint4 rec = recs[g];
+    const int n_tiles = tiles_x * tiles_y;
+    const uint32_t tile_base = (uint32_t)v * (uint32_t)n_tiles;
+    {
+        const int64_t vin = (int64_t)v * bv.in_stride;
+        uv += vin; rxy += vin; conic += 3 * vin;
+        opacity += (int64_t)v * bv.opac_stride;
+        if (cutoff) cutoff += (int64_t)v * n_tiles;
+    }
+    const uint4 rec = recs[gv];
     const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
     const int gbin = (int)((rec.w >> 16) & 0xffu);
     if (rw != 0u) {
@@ -530,7 +571,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
                 row &= row - 1ull;
                 if (cutoff && cutoff[trow + b] < gbin) continue;
                 if (k < cnt) {
-                    pair_tiles[at + k] = trow + b;
+                    pair_tiles[at + k] = tile_base + trow + b;
                     pair_ids[at + k] = g;
                 }
                 ++k;
@@ -544,12 +585,13 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
                                  conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
                                  opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
                                  nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g, nullptr,
-                                 CutArgs{nullptr, cutoff, gbin});
+                                 CutArgs{nullptr, cutoff, gbin}, tile_base);
     else
         bin_walk<false, true>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
                               conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
                               opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
-                              nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g);
+                              nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g, nullptr,
+                              CutArgs{nullptr, nullptr, 0}, tile_base);
 }
 
 // Saturation cut, step 1: the view's visible depth range as bit patterns
@@ -557,7 +599,10 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
 // zero-initialised words).
 __global__ void __launch_bounds__(256)
 bin_depth_range_kernel(const int32_t* __restrict__ valid, const float* __restrict__ depth,
-                       int64_t n, uint32_t* __restrict__ range) {
+                       int64_t n, uint32_t* __restrict__ range, int64_t in_stride) {
+    valid += blockIdx.y * in_stride;  // view blockIdx.y of a batch
+    depth += blockIdx.y * in_stride;
+    range += 2 * blockIdx.y;
     __shared__ uint32_t s_lo[8], s_hi[8];
     uint32_t lo = 0u, hi = 0u;
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n;
@@ -628,7 +673,16 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
                                    const int32_t* __restrict__ cutoff,
                                    const uint32_t* __restrict__ range,
                                    uint32_t* __restrict__ counts,
-                                   uint32_t* __restrict__ dkeys) {
+                                   uint32_t* __restrict__ dkeys, BinViews bv) {
+    const int v = blockIdx.y;
+    {  // view v's slice of the batch
+        const int64_t vin = (int64_t)v * bv.in_stride, vout = (int64_t)v * n;
+        uv += vin; rxy += vin; conic += 3 * vin; depth += vin;
+        opacity += (int64_t)v * bv.opac_stride;
+        counts += vout; dkeys += vout; recs += vout;
+        cutoff += (int64_t)v * tiles_x * tiles_y;
+        range += 2 * v;
+    }
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n || counts[g] == 0u) return;
     const uint4 rec = recs[g];
@@ -657,7 +711,31 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
                                          0u, 0, nullptr, CutArgs{nullptr, cutoff, gbin});
     }
     counts[g] = kept;
-    if (kept == 0u) dkeys[g] = no_depth_key(range);
+    if (kept == 0u) dkeys[g] = view_no_depth_key(range, v, bv.key_shift);
+}
+
+// Per-view pair totals of a batch: view v's pairs start at the scan value of
+// its first sorted slot v * n.
+__global__ void view_totals_kernel(const uint32_t* __restrict__ offsets, int64_t n,
+                                   int n_views, const int32_t* __restrict__ overflow,
+                                   int64_t* __restrict__ totals) {
+    const int v = threadIdx.x;
+    if (v > n_views) return;
+    if (v == n_views) {
+        totals[n_views + 1] = *overflow != 0 ? 1 : 0;
+        return;
+    }
+    const int64_t next = v + 1 < n_views ? (int64_t)offsets[(int64_t)(v + 1) * n]
+                                         : totals[n_views];
+    totals[v] = next - (int64_t)offsets[(int64_t)v * n];
+}
+
+__global__ void view_tile_offsets_kernel(const int32_t* __restrict__ global, int n_tiles,
+                                         int n_views, int32_t* __restrict__ local) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n_views * (n_tiles + 1)) return;
+    const int64_t v = i / (n_tiles + 1), t = i - v * (n_tiles + 1);
+    local[i] = global[v * n_tiles + t] - global[v * n_tiles];
 }
 
 }  // namespace
@@ -732,27 +810,32 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
                                  int tiles_x, int tiles_y, uint32_t* counts,
                                  uint32_t* dkeys, uint32_t* dvals, uint4* recs,
                                  uint32_t* cut_range, uint32_t* cut_hist, int32_t* cutoff,
-                                 cudaStream_t stream) {
-    if (n == 0) return MG_OK;
+                                 const BinViews& bv, cudaStream_t stream) {
+    if (n == 0 || bv.n_views == 0) return MG_OK;
     const bool cut = cut_hist != nullptr;
-    if (cut) {
-        bin_depth_range_kernel<<<std::min(ceil_div(n, 256), 148 * 4), 256, 0, stream>>>(
-            valid, depth, n, cut_range);
+    const int V = bv.n_views;
+    if (cut_range) {
+        const int per_view = (int)std::max<int64_t>(1, std::min<int64_t>(
+                                 ceil_div(n, 256), ceil_div(148 * 4, V)));
+        bin_depth_range_kernel<<<dim3(per_view, V), 256, 0, stream>>>(valid, depth, n,
+                                                                       cut_range, bv.in_stride);
         MG_TRY(check_launch("bin_depth_range"));
     }
-    bin_count_depth_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+    const dim3 grid((unsigned)ceil_div(n, 256), (unsigned)V);
+    bin_count_depth_kernel<<<grid, 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
         opacity, valid, depth, n, W, H, tile, tiles_x, tiles_y, counts, dkeys, dvals, recs,
-        cut_range, cut_hist);
+        cut_range, cut_hist, bv);
     MG_TRY(check_launch("bin_count_depth"));
     if (!cut) return MG_OK;
-    const int n_tiles = tiles_x * tiles_y;
-    bin_cutoff_kernel<<<ceil_div((int64_t)n_tiles * 32, 256), 256, 0, stream>>>(cut_hist, n_tiles,
-                                                                             cutoff);
+    const int64_t cut_tiles = (int64_t)tiles_x * tiles_y * V;
+    bin_cutoff_kernel<<<ceil_div(cut_tiles * 32, 256), 256, 0, stream>>>(cut_hist,
+                                                                       (int)cut_tiles, cutoff);
     MG_TRY(check_launch("bin_cutoff"));
-    bin_recount_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+    bin_recount_kernel<<<grid, 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
-        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, cut_range, counts, dkeys);
+        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, cut_range, counts, dkeys,
+        bv);
     return check_launch("bin_recount");
 }
 
@@ -761,13 +844,28 @@ mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
                           const uint4* recs, const int32_t* cutoff, uint32_t* pair_tiles,
-                          uint32_t* pair_ids, cudaStream_t stream) {
-    if (n == 0 || m == 0) return MG_OK;
-    bin_emit_kernel<<<ceil_div(n, 256), 256, 0, stream>>>(
+                          uint32_t* pair_ids, const BinViews& bv, cudaStream_t stream) {
+    if (n == 0 || m == 0 || bv.n_views == 0) return MG_OK;
+    bin_emit_kernel<<<dim3((unsigned)ceil_div(n, 256), (unsigned)bv.n_views), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
         opacity, sorted_gid, counts, offsets, n, m, W, H, tile, tiles_x, tiles_y,
-        recs, cutoff, pair_tiles, pair_ids);
+        recs, cutoff, pair_tiles, pair_ids, bv);
     return check_launch("bin_emit");
+}
+
+mg_status launch_view_totals(const uint32_t* offsets, int64_t n, int n_views,
+                             const int32_t* overflow, int64_t* totals, cudaStream_t stream) {
+    view_totals_kernel<<<1, ((n_views + 1 + 31) / 32) * 32, 0, stream>>>(offsets, n, n_views,
+                                                                         overflow, totals);
+    return check_launch("view_totals");
+}
+
+mg_status launch_view_tile_offsets(const int32_t* global, int n_tiles, int n_views,
+                                   int32_t* local, cudaStream_t stream) {
+    const int64_t count = (int64_t)n_views * (n_tiles + 1);
+    view_tile_offsets_kernel<<<ceil_div(count, 256), 256, 0, stream>>>(global, n_tiles, n_views,
+                                                                       local);
+    return check_launch("view_tile_offsets");
 }
 
 }  // namespace mg

@@ -114,6 +114,80 @@ class _ViewState:
         return self.prep
 
 
+class _BatchBinning:
+    """Binning of a batch of views of one frame size with one library call
+    per stage (mg_bin_prepare_views / mg_bin_emit_views): one depth sort and
+    one tile sort for the whole batch instead of one of each per view. View
+    v's lists land in ids[base_v, base_v + m_v) with tile offsets from 0, the
+    lists the per-view calls give."""
+
+    def __init__(self, device):
+        u8 = dict(dtype=torch.uint8, device=device)
+        self.device = device
+        self.prep = torch.empty(0, **u8)
+        self.emit = torch.empty(0, **u8)
+        self.ids = torch.empty(0, dtype=torch.int32, device=device)
+        self.offsets = torch.empty(0, dtype=torch.int32, device=device)
+        self.totals = torch.zeros(66, dtype=torch.int64, device=device)
+        self.bases: list[int] = []
+
+    @staticmethod
+    def fits(views) -> bool:
+        return 1 < len(views) <= 64 and len({(v.width, v.height) for v in views}) == 1
+
+    def prepare(self, batch: "_ViewBatch", V: int, n: int, W: int, H: int, tile: int, cut: int,
+                opac: torch.Tensor, opac_stride: int) -> None:
+        """Tile counts, depth sort and scan of views 0..V-1 of `batch` (n
+        Gaussians each); `totals` reads the result."""
+        L = _lib.load()
+        n_tiles = -(-W // tile) * -(-H // tile)
+        nbytes = L.mg_bin_prepare_views_scratch_bytes(n, V, n_tiles)
+        if self.prep.numel() < nbytes:
+            self.prep = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        _lib.check(L.mg_bin_prepare_views(
+            ptr(batch.uv), ptr(batch.rxy), ptr(batch.conic), ptr(opac), ptr(batch.valid),
+            ptr(batch.depth), n, V, batch.n, opac_stride, W, H, tile, cut, ptr(self.totals),
+            ptr(self.prep), self.prep.numel(), _lib.stream()), "bin_prepare_views")
+
+    def read_totals(self, V: int) -> list[int] | None:
+        """The views' pair totals (one device->host read), or None when the
+        batch has to be binned one view at a time (a view's depth range
+        outgrew the batch keys, or 2^31 pairs)."""
+        t = self.totals[:V + 2].tolist()
+        if t[V + 1] or t[V] >= 2 ** 31:
+            return None
+        self.bases = [0] * V
+        for v in range(1, V):
+            self.bases[v] = self.bases[v - 1] + int(t[v - 1])
+        return [int(x) for x in t[:V]]
+
+    def emit_all(self, batch: "_ViewBatch", V: int, n: int, W: int, H: int, tile: int, cut: int,
+                 opac: torch.Tensor, opac_stride: int, m_total: int) -> None:
+        L = _lib.load()
+        n_tiles = -(-W // tile) * -(-H // tile)
+        if self.ids.numel() < max(m_total, 1):
+            self.ids = torch.empty(int(max(m_total, 1) * 1.25), dtype=torch.int32,
+                                   device=self.device)
+        if self.offsets.numel() < V * (n_tiles + 1):
+            self.offsets = torch.empty(V * (n_tiles + 1), dtype=torch.int32, device=self.device)
+        ebytes = L.mg_bin_emit_views_scratch_bytes(n, V, m_total, n_tiles)
+        if self.emit.numel() < ebytes:
+            self.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
+                                    device=self.device)
+        _lib.check(L.mg_bin_emit_views(
+            ptr(batch.uv), ptr(batch.rxy), ptr(batch.conic), ptr(opac), n, V, batch.n,
+            opac_stride, m_total, W, H, tile, cut, ptr(self.prep), ptr(self.ids),
+            ptr(self.offsets), ptr(self.emit), self.emit.numel(), _lib.stream()),
+            "bin_emit_views")
+        self.n_tiles = n_tiles
+
+    def view(self, v: int, m: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """View v's gauss ids and tile offsets (views into the batch's)."""
+        base = self.bases[v]
+        k = self.n_tiles + 1
+        return self.ids[base:base + max(m, 1)], self.offsets[v * k:(v + 1) * k]
+
+
 def _views_array(cams: list) -> "_lib.C.Array":
     return (_lib.Camera * len(cams))(*cams)
 
@@ -145,6 +219,9 @@ class Trainer:
         # provably saturate every pixel (mg_bin_prepare): same images and
         # gradients, fewer pairs to emit and sort
         self.saturation_cut = int(bool(saturation_cut))
+        # bin a step's views of one frame size together (one depth sort and
+        # one tile sort for all of them); False bins them one at a time
+        self.batch_binning = True
         self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
@@ -198,6 +275,7 @@ class Trainer:
         self._batch: _ViewBatch | None = None
         self._states: list[_ViewState] = []
         self._totals = torch.zeros(64, dtype=torch.int64, device=self.device)
+        self._bb = _BatchBinning(self.device)
         self._cams: dict[int, _lib.Camera] = {}
         self.last_stats: list[ViewStats] = []
         # stage name -> list of (start, end) CUDA events, when timing is on;
@@ -433,10 +511,11 @@ class Trainer:
         self._end(ev)
 
     def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
-                             scale: float) -> ViewStats:
+                             scale: float, batched: bool = False) -> ViewStats:
         """Phase B for view v (its pair total m known on the host): pair
-        emission and tile sort, raster forward, fused loss and raster
-        backward into the view's gradient records."""
+        emission and tile sort (already done for the whole batch when
+        `batched`), raster forward, fused loss and raster backward into the
+        view's gradient records."""
         L = _lib.load()
         s = _lib.stream()
         W, H, n = view.width, view.height, self.active
@@ -444,24 +523,31 @@ class Trainer:
         b = self._buffers(W, H)
         tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
         n_tiles = tiles_x * tiles_y
-        if b.ids.numel() < max(m, 1):
-            b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32, device=self.device)
-        if b.offsets is None or b.offsets.numel() != n_tiles + 1:
-            b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
+        if b.tile_work is None or b.tile_work.numel() != n_tiles:
             b.tile_work = torch.empty(n_tiles, dtype=torch.int32, device=self.device)
         rbytes = L.mg_raster_scratch_bytes(W, H, self.tile, m)
         if b.raster.numel() < rbytes:
             b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
                                    device=self.device)
-        ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
-        if b.emit.numel() < ebytes:
-            b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8, device=self.device)
-        ev = self._begin("bin_emit")
-        _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), n, m, W,
-                                 H, self.tile, self.saturation_cut, ptr(st.prep), ptr(b.ids),
-                                 ptr(b.offsets),
-                                 ptr(b.emit), b.emit.numel(), s), "bin_emit")
-        self._end(ev)
+        if batched:
+            ids, offsets = self._bb.view(v, m)
+        else:
+            if b.ids.numel() < max(m, 1):
+                b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32,
+                                    device=self.device)
+            if b.offsets is None or b.offsets.numel() != n_tiles + 1:
+                b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
+            ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
+            if b.emit.numel() < ebytes:
+                b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
+                                     device=self.device)
+            ev = self._begin("bin_emit")
+            _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), n,
+                                     m, W, H, self.tile, self.saturation_cut, ptr(st.prep),
+                                     ptr(b.ids), ptr(b.offsets), ptr(b.emit), b.emit.numel(), s),
+                       "bin_emit")
+            self._end(ev)
+            ids, offsets = b.ids, b.offsets
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
         ev = self._begin("pack")
@@ -472,7 +558,7 @@ class Trainer:
         work = b.tile_work if self.stage_events is not None else None
         ev = self._begin("raster_fwd")
         _lib.check(L.mg_rasterize_forward(
-            ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, W, H, self.tile, tiles_x, bgp,
+            ptr(b.splats), ptr(ids), ptr(offsets), m, W, H, self.tile, tiles_x, bgp,
             ptr(b.rgb), ptr(b.alpha), ptr(b.T), ptr(b.stop), ptr(work), ptr(b.raster),
             b.raster.numel(), s), "rasterize_forward")
         self._end(ev)
@@ -487,7 +573,7 @@ class Trainer:
         self._end(ev)
         ev = self._begin("raster_bwd")
         _lib.check(L.mg_rasterize_backward(
-            ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, ptr(b.rgb), ptr(b.alpha), ptr(b.T),
+            ptr(b.splats), ptr(ids), ptr(offsets), m, ptr(b.rgb), ptr(b.alpha), ptr(b.T),
             ptr(b.stop), ptr(b.grad_rgb), None, W, H, self.tile, tiles_x, bgp, 0, n,
             ptr(st.grad2d), 1, ptr(b.raster), b.raster.numel(), s), "rasterize_backward")
         self._end(ev)
@@ -505,10 +591,25 @@ class Trainer:
             self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
         self._ensure_views(V)
         self._project_views(views)
-        for v, view in enumerate(views):
-            self._prepare(v, view)
-        totals = self._totals[:V].tolist()
-        stats = [self._render_and_backprop(v, view, t, int(m), scale)
+        totals = None
+        if self.batch_binning and _BatchBinning.fits(views):
+            W, H = views[0].width, views[0].height
+            ev = self._begin("bin_prepare")
+            self._bb.prepare(self._batch, V, self.active, W, H, self.tile,
+                             self.saturation_cut, self.opac, 0)
+            self._end(ev)
+            totals = self._bb.read_totals(V)
+            if totals is not None:
+                ev = self._begin("bin_emit")
+                self._bb.emit_all(self._batch, V, self.active, W, H, self.tile,
+                                  self.saturation_cut, self.opac, 0, sum(totals))
+                self._end(ev)
+        batched = totals is not None
+        if not batched:
+            for v, view in enumerate(views):
+                self._prepare(v, view)
+            totals = self._totals[:V].tolist()
+        stats = [self._render_and_backprop(v, view, t, int(m), scale, batched)
                  for v, (view, t, m) in enumerate(zip(views, targets, totals))]
         # the projection adjoint of all views at once (parameters read and
         # gradient rows updated once), then the SH adjoint likewise

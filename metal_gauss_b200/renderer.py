@@ -9,7 +9,8 @@ and per view it runs the antialias opacity compensation when asked for
 with the saturation cut, the packing and a forward-only rasterisation that
 writes no transmittance, stop indices or checkpoints and keeps no autograd
 state. Views are processed in batches with one host read per batch (the pair
-totals of all its views).
+totals of all its views); a batch of one frame size is binned with one call
+per binning stage for all its views.
 """
 
 from __future__ import annotations
@@ -18,7 +19,7 @@ import torch
 
 from . import _lib
 from ._lib import ptr
-from .engine import _ViewBatch, _ViewState, _views_array
+from .engine import _BatchBinning, _ViewBatch, _ViewState, _views_array
 
 
 class _FrameBuffers:
@@ -68,9 +69,11 @@ class Renderer:
         self._batch = _ViewBatch(n, batch, self.device, grads=False)
         self._states = [_ViewState(self._batch, v, self.device) for v in range(batch)]
         self._bufs: dict = {}
-        # per-view opacity after the antialias compensation
-        self._opac_view: list[torch.Tensor] = []
+        # per-view opacity after the antialias compensation (view-major)
+        self._opac_view = torch.empty(batch if antialias else 0, n, **f32)
         self._totals = torch.zeros(batch, dtype=torch.int64, device=self.device)
+        self._bb = _BatchBinning(self.device)
+        self.batch_binning = True
 
     def _camera(self, view) -> _lib.Camera:
         vm = view.viewmat.to(torch.float32)
@@ -81,8 +84,6 @@ class Renderer:
                                 self.max_radius_frac * max(view.width, view.height), cc)
 
     def _state(self, v: int) -> _ViewState:
-        while self.antialias and len(self._opac_view) <= v:
-            self._opac_view.append(torch.empty(self.n, dtype=torch.float32, device=self.device))
         return self._states[v]
 
     def _opacity(self, v: int) -> torch.Tensor:
@@ -115,20 +116,35 @@ class Renderer:
             len(views), self.sh_degree, n, n, ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy),
             ptr(b.valid), ptr(b.color), None, s), "preprocess_forward_views")
         for v, view in enumerate(views):
-            st = self._state(v)
-            opac = self._opacity(v)
             if self.antialias:
                 # before binning, as the reference does: the exact tile test
                 # then uses the opacity that is composited
-                _lib.check(L.mg_antialias_opacity(ptr(st.conic), ptr(self.opac), n, 0.3,
-                                                  ptr(opac), s), "antialias_opacity")
-            tiles = -(-view.width // self.tile) * -(-view.height // self.tile)
-            prep = st.prep_scratch(tiles)
-            _lib.check(L.mg_bin_prepare(
-                ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), ptr(st.valid),
-                ptr(st.depth), n, view.width, view.height, self.tile, self.saturation_cut,
-                ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(), s), "bin_prepare")
-        totals = self._totals[:len(views)].tolist()
+                _lib.check(L.mg_antialias_opacity(ptr(self._state(v).conic), ptr(self.opac), n,
+                                                  0.3, ptr(self._opacity(v)), s),
+                           "antialias_opacity")
+        V = len(views)
+        opac_all, opac_stride = (self._opac_view, n) if self.antialias else (self.opac, 0)
+        totals = None
+        if self.batch_binning and _BatchBinning.fits(views):
+            W, H = views[0].width, views[0].height
+            self._bb.prepare(self._batch, V, n, W, H, self.tile, self.saturation_cut, opac_all,
+                             opac_stride)
+            totals = self._bb.read_totals(V)
+            if totals is not None:
+                self._bb.emit_all(self._batch, V, n, W, H, self.tile, self.saturation_cut,
+                                  opac_all, opac_stride, sum(totals))
+        batched = totals is not None
+        if not batched:
+            for v, view in enumerate(views):
+                st = self._state(v)
+                tiles = -(-view.width // self.tile) * -(-view.height // self.tile)
+                prep = st.prep_scratch(tiles)
+                _lib.check(L.mg_bin_prepare(
+                    ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self._opacity(v)),
+                    ptr(st.valid), ptr(st.depth), n, view.width, view.height, self.tile,
+                    self.saturation_cut, ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(),
+                    s), "bin_prepare")
+            totals = self._totals[:V].tolist()
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
         out = []
@@ -139,28 +155,33 @@ class Renderer:
             b = self._buffers(W, H)
             tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
             n_tiles = tiles_x * tiles_y
-            if b.ids.numel() < max(m, 1):
-                b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32, device=self.device)
-            if b.offsets is None or b.offsets.numel() != n_tiles + 1:
-                b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
-            ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
-            if b.emit.numel() < ebytes:
-                b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
-                                     device=self.device)
             rbytes = L.mg_raster_scratch_bytes(W, H, self.tile, m)
             if b.raster.numel() < rbytes:
                 b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
                                        device=self.device)
-            _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), n, m,
-                                     W, H, self.tile, self.saturation_cut, ptr(st.prep),
-                                     ptr(b.ids), ptr(b.offsets), ptr(b.emit), b.emit.numel(),
-                                     s), "bin_emit")
+            if batched:
+                ids, offsets = self._bb.view(v, m)
+            else:
+                if b.ids.numel() < max(m, 1):
+                    b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32,
+                                        device=self.device)
+                if b.offsets is None or b.offsets.numel() != n_tiles + 1:
+                    b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
+                ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
+                if b.emit.numel() < ebytes:
+                    b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
+                                         device=self.device)
+                _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), n,
+                                         m, W, H, self.tile, self.saturation_cut, ptr(st.prep),
+                                         ptr(b.ids), ptr(b.offsets), ptr(b.emit),
+                                         b.emit.numel(), s), "bin_emit")
+                ids, offsets = b.ids, b.offsets
             _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(opac), ptr(st.color),
                                         n, ptr(b.splats), s), "pack_splats")
             rgb = torch.empty(H, W, 3, dtype=torch.float32, device=self.device)
             alpha = torch.empty(H, W, dtype=torch.float32, device=self.device)
             _lib.check(L.mg_rasterize_forward(
-                ptr(b.splats), ptr(b.ids), ptr(b.offsets), m, W, H, self.tile, tiles_x, bgp,
+                ptr(b.splats), ptr(ids), ptr(offsets), m, W, H, self.tile, tiles_x, bgp,
                 ptr(rgb), ptr(alpha), None, None, None, ptr(b.raster), b.raster.numel(), s),
                 "rasterize_forward")
             out.append((rgb, alpha))

@@ -42,6 +42,13 @@ def test_scratch_queries_need_no_device():
     assert lib.mg_sort_scratch_bytes(1 << 20, 32, 4) > 0
     assert lib.mg_bin_prepare_scratch_bytes(1000, 2500) > 4 * 1000 + 64 * 4 * 2500
     assert lib.mg_bin_emit_scratch_bytes(1000, 5000, 2500) > 4 * 5000
+    # a batch of one view has the single-view layout; eight views eight times the rows
+    assert lib.mg_bin_prepare_views_scratch_bytes(1000, 1, 2500) == \
+        lib.mg_bin_prepare_scratch_bytes(1000, 2500)
+    assert lib.mg_bin_prepare_views_scratch_bytes(1000, 8, 2500) > 8 * 40 * 1000
+    assert lib.mg_bin_emit_views_scratch_bytes(1000, 8, 5000, 2500) > \
+        lib.mg_bin_emit_scratch_bytes(1000, 5000, 2500)
+    assert lib.mg_bin_prepare_views_scratch_bytes(1000, 0, 2500) == 0
     assert lib.mg_l1_ssim_scratch_bytes(64, 64) >= 9 * 64 * 64 * 4
     # counters + tile order + block walks + items + checkpoints (5 floats per
     # pixel slot per MG_RASTER_SEGMENT entries)
