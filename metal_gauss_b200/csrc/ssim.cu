@@ -363,7 +363,8 @@ __global__ void loss_finish_kernel(const float* __restrict__ partial, int nblock
     }
     if (threadIdx.x == 0) {
         const double ssim = s[0][0] * inv_n, l1 = s[1][0] * inv_n;
-        *loss_dev += (float)(scale * (w_l1 * l1 + w_ssim * (1.0 - ssim)));
+        // atomic: views rendered on concurrent streams add into one word
+        atomicAdd(loss_dev, (float)(scale * (w_l1 * l1 + w_ssim * (1.0 - ssim))));
     }
 }
 

@@ -222,6 +222,11 @@ class Trainer:
         # bin a step's views of one frame size together (one depth sort and
         # one tile sort for all of them); False bins them one at a time
         self.batch_binning = True
+        # phase B's per-view chains (pack, raster forward, loss, raster
+        # backward) run on this many streams, each with its own frame
+        # buffers, so one view's raster tail overlaps the next view's work
+        self.view_streams = 3
+        self._streams: list = []
         self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
@@ -461,12 +466,23 @@ class Trainer:
             self._cams[key] = cam
         return cam
 
-    def _buffers(self, W: int, H: int) -> _ImageBuffers:
-        b = self._bufs.get((W, H))
+    def _buffers(self, W: int, H: int, slot: int = 0) -> _ImageBuffers:
+        b = self._bufs.get((W, H, slot))
         if b is None:
             b = _ImageBuffers(self.n, W, H, self.device)
-            self._bufs[(W, H)] = b
+            self._bufs[(W, H, slot)] = b
         return b
+
+    def _phase_b_streams(self, V: int) -> list:
+        """The streams phase B's view chains take turns on; none (the
+        current stream) with one view, one stream asked for, or while every
+        stage is being timed (overlapping stages would blur the split)."""
+        k = min(int(self.view_streams), V)
+        if k <= 1 or (self.stage_events is not None and self.timed_stages is None):
+            return []
+        while len(self._streams) < k:
+            self._streams.append(torch.cuda.Stream(self.device))
+        return self._streams[:k]
 
     def _ensure_views(self, V: int) -> None:
         """View-major buffers for V views (grown, never shrunk)."""
@@ -511,16 +527,17 @@ class Trainer:
         self._end(ev)
 
     def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
-                             scale: float, batched: bool = False) -> ViewStats:
-        """Phase B for view v (its pair total m known on the host): pair
-        emission and tile sort (already done for the whole batch when
-        `batched`), raster forward, fused loss and raster backward into the
-        view's gradient records."""
+                             scale: float, batched: bool = False, slot: int = 0) -> ViewStats:
+        """Phase B for view v (its pair total m known on the host) on the
+        current stream with frame buffer set `slot`: pair emission and tile
+        sort (already done for the whole batch when `batched`), raster
+        forward, fused loss and raster backward into the view's gradient
+        records."""
         L = _lib.load()
         s = _lib.stream()
         W, H, n = view.width, view.height, self.active
         st = self._state(v)
-        b = self._buffers(W, H)
+        b = self._buffers(W, H, slot)
         tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
         n_tiles = tiles_x * tiles_y
         if b.tile_work is None or b.tile_work.numel() != n_tiles:
@@ -609,8 +626,28 @@ class Trainer:
             for v, view in enumerate(views):
                 self._prepare(v, view)
             totals = self._totals[:V].tolist()
-        stats = [self._render_and_backprop(v, view, t, int(m), scale, batched)
-                 for v, (view, t, m) in enumerate(zip(views, targets, totals))]
+        streams = self._phase_b_streams(V)
+        if not streams:
+            stats = [self._render_and_backprop(v, view, t, int(m), scale, batched)
+                     for v, (view, t, m) in enumerate(zip(views, targets, totals))]
+        else:
+            # view v on stream v mod k after everything queued so far; the
+            # current stream waits for all of them before the adjoints
+            main = torch.cuda.current_stream(self.device)
+            ready = torch.cuda.Event()
+            ready.record(main)
+            for sk in streams:
+                sk.wait_event(ready)
+            stats = []
+            for v, (view, t, m) in enumerate(zip(views, targets, totals)):
+                k = v % len(streams)
+                with torch.cuda.stream(streams[k]):
+                    stats.append(self._render_and_backprop(v, view, t, int(m), scale, batched,
+                                                           k))
+            for sk in streams:
+                done = torch.cuda.Event()
+                done.record(sk)
+                main.wait_event(done)
         # the projection adjoint of all views at once (parameters read and
         # gradient rows updated once), then the SH adjoint likewise
         b = self._batch

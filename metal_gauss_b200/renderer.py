@@ -74,6 +74,10 @@ class Renderer:
         self._totals = torch.zeros(batch, dtype=torch.int64, device=self.device)
         self._bb = _BatchBinning(self.device)
         self.batch_binning = True
+        # views are packed and rasterised on this many streams in turn (one
+        # view's raster tail overlaps the next view's work)
+        self.view_streams = 3
+        self._streams: list = []
 
     def _camera(self, view) -> _lib.Camera:
         vm = view.viewmat.to(torch.float32)
@@ -89,11 +93,11 @@ class Renderer:
     def _opacity(self, v: int) -> torch.Tensor:
         return self._opac_view[v] if self.antialias else self.opac
 
-    def _buffers(self, W: int, H: int) -> _FrameBuffers:
-        b = self._bufs.get((W, H))
+    def _buffers(self, W: int, H: int, slot: int = 0) -> _FrameBuffers:
+        b = self._bufs.get((W, H, slot))
         if b is None:
             b = _FrameBuffers(self.n, self.device)
-            self._bufs[(W, H)] = b
+            self._bufs[(W, H, slot)] = b
         return b
 
     def render(self, views) -> list[tuple[torch.Tensor, torch.Tensor]]:
@@ -147,42 +151,67 @@ class Renderer:
             totals = self._totals[:V].tolist()
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
+        k = min(int(self.view_streams), V)
+        while len(self._streams) < k:
+            self._streams.append(torch.cuda.Stream(self.device))
+        main = torch.cuda.current_stream(self.device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        streams = self._streams[:k] if k > 1 else [main]
+        if k > 1:
+            for sk in streams:
+                sk.wait_event(ready)
         out = []
         for v, (view, m) in enumerate(zip(views, totals)):
-            st = self._states[v]
-            opac = self._opacity(v)
-            W, H, m = view.width, view.height, int(m)
-            b = self._buffers(W, H)
-            tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
-            n_tiles = tiles_x * tiles_y
-            rbytes = L.mg_raster_scratch_bytes(W, H, self.tile, m)
-            if b.raster.numel() < rbytes:
-                b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
-                                       device=self.device)
-            if batched:
-                ids, offsets = self._bb.view(v, m)
-            else:
-                if b.ids.numel() < max(m, 1):
-                    b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32,
-                                        device=self.device)
-                if b.offsets is None or b.offsets.numel() != n_tiles + 1:
-                    b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
-                ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
-                if b.emit.numel() < ebytes:
-                    b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
-                                         device=self.device)
-                _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), n,
-                                         m, W, H, self.tile, self.saturation_cut, ptr(st.prep),
-                                         ptr(b.ids), ptr(b.offsets), ptr(b.emit),
-                                         b.emit.numel(), s), "bin_emit")
-                ids, offsets = b.ids, b.offsets
-            _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(opac), ptr(st.color),
-                                        n, ptr(b.splats), s), "pack_splats")
-            rgb = torch.empty(H, W, 3, dtype=torch.float32, device=self.device)
-            alpha = torch.empty(H, W, dtype=torch.float32, device=self.device)
-            _lib.check(L.mg_rasterize_forward(
-                ptr(b.splats), ptr(ids), ptr(offsets), m, W, H, self.tile, tiles_x, bgp,
-                ptr(rgb), ptr(alpha), None, None, None, ptr(b.raster), b.raster.numel(), s),
-                "rasterize_forward")
+            # the outputs belong to the caller's stream, which waits below
+            rgb = torch.empty(view.height, view.width, 3, dtype=torch.float32, device=self.device)
+            alpha = torch.empty(view.height, view.width, dtype=torch.float32, device=self.device)
+            with torch.cuda.stream(streams[v % k]):
+                self._render_view(v, view, int(m), batched, v % k, rgb, alpha, bgp)
             out.append((rgb, alpha))
+        if k > 1:
+            for sk in streams:
+                done = torch.cuda.Event()
+                done.record(sk)
+                main.wait_event(done)
         return out
+
+    def _render_view(self, v: int, view, m: int, batched: bool, slot: int, rgb, alpha, bgp):
+        """Pair lists (unless the batch has them), packing and the forward-only
+        rasterisation of view v on the current stream."""
+        L = _lib.load()
+        s = _lib.stream()
+        n = self.n
+        st = self._states[v]
+        opac = self._opacity(v)
+        W, H = view.width, view.height
+        b = self._buffers(W, H, slot)
+        tiles_x, tiles_y = -(-W // self.tile), -(-H // self.tile)
+        n_tiles = tiles_x * tiles_y
+        rbytes = L.mg_raster_scratch_bytes(W, H, self.tile, m)
+        if b.raster.numel() < rbytes:
+            b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
+                                   device=self.device)
+        if batched:
+            ids, offsets = self._bb.view(v, m)
+        else:
+            if b.ids.numel() < max(m, 1):
+                b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32,
+                                    device=self.device)
+            if b.offsets is None or b.offsets.numel() != n_tiles + 1:
+                b.offsets = torch.empty(n_tiles + 1, dtype=torch.int32, device=self.device)
+            ebytes = L.mg_bin_emit_scratch_bytes(n, m, n_tiles)
+            if b.emit.numel() < ebytes:
+                b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
+                                     device=self.device)
+            _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(opac), n,
+                                     m, W, H, self.tile, self.saturation_cut, ptr(st.prep),
+                                     ptr(b.ids), ptr(b.offsets), ptr(b.emit),
+                                     b.emit.numel(), s), "bin_emit")
+            ids, offsets = b.ids, b.offsets
+        _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(opac), ptr(st.color),
+                                    n, ptr(b.splats), s), "pack_splats")
+        _lib.check(L.mg_rasterize_forward(
+            ptr(b.splats), ptr(ids), ptr(offsets), m, W, H, self.tile, tiles_x, bgp,
+            ptr(rgb), ptr(alpha), None, None, None, ptr(b.raster), b.raster.numel(), s),
+            "rasterize_forward")
