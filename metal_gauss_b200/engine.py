@@ -135,19 +135,23 @@ class _BatchBinning:
     def fits(views) -> bool:
         return 1 < len(views) <= 64 and len({(v.width, v.height) for v in views}) == 1
 
-    def prepare(self, batch: "_ViewBatch", V: int, n: int, W: int, H: int, tile: int, cut: int,
-                opac: torch.Tensor, opac_stride: int) -> None:
-        """Tile counts, depth sort and scan of views 0..V-1 of `batch` (n
-        Gaussians each); `totals` reads the result."""
+    def prepare(self, batch: "_ViewBatch", first: int, V: int, n: int, W: int, H: int, tile: int,
+                cut: int, opac: torch.Tensor, opac_stride: int) -> None:
+        """Tile counts, depth sort and scan of views first..first+V-1 of
+        `batch` (n Gaussians each; opacity rows from view `first` on when
+        opac_stride is not 0); `read_totals` reads the result."""
         L = _lib.load()
         n_tiles = -(-W // tile) * -(-H // tile)
         nbytes = L.mg_bin_prepare_views_scratch_bytes(n, V, n_tiles)
         if self.prep.numel() < nbytes:
             self.prep = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.first = first
+        op = opac[first] if opac_stride else opac
         _lib.check(L.mg_bin_prepare_views(
-            ptr(batch.uv), ptr(batch.rxy), ptr(batch.conic), ptr(opac), ptr(batch.valid),
-            ptr(batch.depth), n, V, batch.n, opac_stride, W, H, tile, cut, ptr(self.totals),
-            ptr(self.prep), self.prep.numel(), _lib.stream()), "bin_prepare_views")
+            ptr(batch.uv[first]), ptr(batch.rxy[first]), ptr(batch.conic[first]), ptr(op),
+            ptr(batch.valid[first]), ptr(batch.depth[first]), n, V, batch.n, opac_stride, W, H,
+            tile, cut, ptr(self.totals), ptr(self.prep), self.prep.numel(), _lib.stream()),
+            "bin_prepare_views")
 
     def read_totals(self, V: int) -> list[int] | None:
         """The views' pair totals (one device->host read), or None when the
@@ -174,15 +178,18 @@ class _BatchBinning:
         if self.emit.numel() < ebytes:
             self.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
                                     device=self.device)
+        f = self.first
+        op = opac[f] if opac_stride else opac
         _lib.check(L.mg_bin_emit_views(
-            ptr(batch.uv), ptr(batch.rxy), ptr(batch.conic), ptr(opac), n, V, batch.n,
+            ptr(batch.uv[f]), ptr(batch.rxy[f]), ptr(batch.conic[f]), ptr(op), n, V, batch.n,
             opac_stride, m_total, W, H, tile, cut, ptr(self.prep), ptr(self.ids),
             ptr(self.offsets), ptr(self.emit), self.emit.numel(), _lib.stream()),
             "bin_emit_views")
         self.n_tiles = n_tiles
 
     def view(self, v: int, m: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """View v's gauss ids and tile offsets (views into the batch's)."""
+        """Gauss ids and tile offsets of the batch's view v (counted from
+        `first`; views into the batch's arrays)."""
         base = self.bases[v]
         k = self.n_tiles + 1
         return self.ids[base:base + max(m, 1)], self.offsets[v * k:(v + 1) * k]
@@ -225,8 +232,11 @@ class Trainer:
         # phase B's per-view chains (pack, raster forward, loss, raster
         # backward) run on this many streams, each with its own frame
         # buffers, so one view's raster tail overlaps the next view's work
-        self.view_streams = 3
+        self.view_streams = 4
         self._streams: list = []
+        # views binned per batch binning call (0: all of a step's views); a
+        # chunk's rendering on the streams overlaps the binning of the next
+        self.bin_chunk = 0
         self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
@@ -280,7 +290,8 @@ class Trainer:
         self._batch: _ViewBatch | None = None
         self._states: list[_ViewState] = []
         self._totals = torch.zeros(64, dtype=torch.int64, device=self.device)
-        self._bb = _BatchBinning(self.device)
+        # one batch binning per chunk of a step's views
+        self._bbs: list[_BatchBinning] = []
         self._cams: dict[int, _lib.Camera] = {}
         self.last_stats: list[ViewStats] = []
         # stage name -> list of (start, end) CUDA events, when timing is on;
@@ -512,6 +523,32 @@ class Trainer:
                   ptr(self.visibility_count()), _lib.stream())
         self._end(ev)
 
+    def _bin_chunk(self, c: int, first: int, chunk) -> tuple[list[int], "_BatchBinning | None"]:
+        """Phase A, second half, for views first.. of a chunk: their pair
+        totals (one host read) and, when binned together, the batch binning
+        that holds their lists; otherwise each view's stage A ran into its
+        own state and its pairs are emitted in phase B."""
+        V = len(chunk)
+        if self.batch_binning and _BatchBinning.fits(chunk):
+            while len(self._bbs) <= c:
+                self._bbs.append(_BatchBinning(self.device))
+            bb = self._bbs[c]
+            W, H = chunk[0].width, chunk[0].height
+            ev = self._begin("bin_prepare")
+            bb.prepare(self._batch, first, V, self.active, W, H, self.tile, self.saturation_cut,
+                       self.opac, 0)
+            self._end(ev)
+            totals = bb.read_totals(V)
+            if totals is not None:
+                ev = self._begin("bin_emit")
+                bb.emit_all(self._batch, V, self.active, W, H, self.tile, self.saturation_cut,
+                            self.opac, 0, sum(totals))
+                self._end(ev)
+                return totals, bb
+        for i, view in enumerate(chunk):
+            self._prepare(first + i, view)
+        return [int(x) for x in self._totals[first:first + V].tolist()], None
+
     def _prepare(self, v: int, view) -> None:
         """Phase A, second half, for view v: tile counts, depth sort and the
         scan that yields the view's pair total."""
@@ -527,12 +564,13 @@ class Trainer:
         self._end(ev)
 
     def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
-                             scale: float, batched: bool = False, slot: int = 0) -> ViewStats:
+                             scale: float, lists: tuple | None = None,
+                             slot: int = 0) -> ViewStats:
         """Phase B for view v (its pair total m known on the host) on the
         current stream with frame buffer set `slot`: pair emission and tile
-        sort (already done for the whole batch when `batched`), raster
-        forward, fused loss and raster backward into the view's gradient
-        records."""
+        sort (unless `lists`, the view's ids and tile offsets from a batch
+        binning, are given), raster forward, fused loss and raster backward
+        into the view's gradient records."""
         L = _lib.load()
         s = _lib.stream()
         W, H, n = view.width, view.height, self.active
@@ -546,8 +584,8 @@ class Trainer:
         if b.raster.numel() < rbytes:
             b.raster = torch.empty(int(rbytes * 1.25) + 256, dtype=torch.uint8,
                                    device=self.device)
-        if batched:
-            ids, offsets = self._bb.view(v, m)
+        if lists is not None:
+            ids, offsets = lists
         else:
             if b.ids.numel() < max(m, 1):
                 b.ids = torch.empty(int(max(m, 1) * 1.25), dtype=torch.int32,
@@ -602,52 +640,39 @@ class Trainer:
         opacity logits are added into self.G and the views' SH gradients are
         written into it (the SH adjoint covers all of a call's views at once
         and overwrites its rows; `train_step` zeroes the rest of G first). One
-        device->host read per call (all views' pair totals)."""
+        device->host read per binning chunk (its views' pair totals)."""
         V = len(views)
         if V > self._totals.numel():
             self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
         self._ensure_views(V)
         self._project_views(views)
-        totals = None
-        if self.batch_binning and _BatchBinning.fits(views):
-            W, H = views[0].width, views[0].height
-            ev = self._begin("bin_prepare")
-            self._bb.prepare(self._batch, V, self.active, W, H, self.tile,
-                             self.saturation_cut, self.opac, 0)
-            self._end(ev)
-            totals = self._bb.read_totals(V)
-            if totals is not None:
-                ev = self._begin("bin_emit")
-                self._bb.emit_all(self._batch, V, self.active, W, H, self.tile,
-                                  self.saturation_cut, self.opac, 0, sum(totals))
-                self._end(ev)
-        batched = totals is not None
-        if not batched:
-            for v, view in enumerate(views):
-                self._prepare(v, view)
-            totals = self._totals[:V].tolist()
         streams = self._phase_b_streams(V)
-        if not streams:
-            stats = [self._render_and_backprop(v, view, t, int(m), scale, batched)
-                     for v, (view, t, m) in enumerate(zip(views, targets, totals))]
-        else:
-            # view v on stream v mod k after everything queued so far; the
-            # current stream waits for all of them before the adjoints
-            main = torch.cuda.current_stream(self.device)
-            ready = torch.cuda.Event()
-            ready.record(main)
-            for sk in streams:
-                sk.wait_event(ready)
-            stats = []
-            for v, (view, t, m) in enumerate(zip(views, targets, totals)):
-                k = v % len(streams)
-                with torch.cuda.stream(streams[k]):
-                    stats.append(self._render_and_backprop(v, view, t, int(m), scale, batched,
-                                                           k))
-            for sk in streams:
-                done = torch.cuda.Event()
-                done.record(sk)
-                main.wait_event(done)
+        main = torch.cuda.current_stream(self.device)
+        C = V if self.bin_chunk <= 0 else min(V, int(self.bin_chunk))
+        stats: list = [None] * V
+        for c, first in enumerate(range(0, V, C)):
+            chunk = views[first:first + C]
+            totals, bb = self._bin_chunk(c, first, chunk)
+            if streams:
+                # the chunk's views on the streams in turn, after its binning
+                ready = torch.cuda.Event()
+                ready.record(main)
+                for sk in streams:
+                    sk.wait_event(ready)
+            for i, view in enumerate(chunk):
+                v, m = first + i, int(totals[i])
+                lists = None if bb is None else bb.view(i, m)
+                if streams:
+                    k = v % len(streams)
+                    with torch.cuda.stream(streams[k]):
+                        stats[v] = self._render_and_backprop(v, view, targets[v], m, scale,
+                                                             lists, k)
+                else:
+                    stats[v] = self._render_and_backprop(v, view, targets[v], m, scale, lists)
+        for sk in streams:  # the adjoints below wait for every view
+            done = torch.cuda.Event()
+            done.record(sk)
+            main.wait_event(done)
         # the projection adjoint of all views at once (parameters read and
         # gradient rows updated once), then the SH adjoint likewise
         b = self._batch

@@ -76,7 +76,7 @@ class Renderer:
         self.batch_binning = True
         # views are packed and rasterised on this many streams in turn (one
         # view's raster tail overlaps the next view's work)
-        self.view_streams = 3
+        self.view_streams = 4
         self._streams: list = []
 
     def _camera(self, view) -> _lib.Camera:
@@ -131,8 +131,8 @@ class Renderer:
         totals = None
         if self.batch_binning and _BatchBinning.fits(views):
             W, H = views[0].width, views[0].height
-            self._bb.prepare(self._batch, V, n, W, H, self.tile, self.saturation_cut, opac_all,
-                             opac_stride)
+            self._bb.prepare(self._batch, 0, V, n, W, H, self.tile, self.saturation_cut,
+                             opac_all, opac_stride)
             totals = self._bb.read_totals(V)
             if totals is not None:
                 self._bb.emit_all(self._batch, V, n, W, H, self.tile, self.saturation_cut,

@@ -154,22 +154,26 @@ def test_batch_entry_points_refuse_bad_arguments(cuda):
                                   0, ptr(tot), ptr(buf), 16, None) != 0
 
 
-def _trainer_run(batch_binning, p, views, targets):
+def _trainer_run(p, views, targets, batch_binning, view_streams, bin_chunk):
     tr = Trainer({k: v.clone() for k, v in p.items()}, "cuda", sh_degree=3)
-    tr.batch_binning = batch_binning
+    tr.batch_binning, tr.view_streams, tr.bin_chunk = batch_binning, view_streams, bin_chunk
     tr._activate()
     stats = tr.forward_backward_views(views, targets, 1.0 / len(views))
     torch.cuda.synchronize()
     return tr, stats
 
 
-def test_trainer_batch_binning_changes_nothing(cuda):
+@pytest.mark.parametrize("bb,streams,chunk", [(True, 3, 0), (True, 2, 2), (True, 1, 3),
+                                              (False, 3, 0)])
+def test_trainer_binning_and_streams_change_nothing(cuda, bb, streams, chunk):
+    """Batch binning (whole step or chunks), and the view chains on several
+    streams, against one view at a time on one stream."""
     p, _, _ = scenes.config("cfg3", n=N_G, seed=8)
     views = scenes.sphere_views(5, 4.0, W, H, 40.0, 9, hemisphere=True)
     g = torch.Generator().manual_seed(1)
     targets = [torch.rand(H, W, 3, generator=g).cuda() for _ in views]
-    a, sa = _trainer_run(True, p, views, targets)
-    b, sb = _trainer_run(False, p, views, targets)
+    a, sa = _trainer_run(p, views, targets, bb, streams, chunk)
+    b, sb = _trainer_run(p, views, targets, False, 1, 0)
     assert [s.pairs for s in sa] == [s.pairs for s in sb]
     assert float(a.loss.sum()) == pytest.approx(float(b.loss.sum()), rel=1e-6)
     for name in ("means", "quats", "log_scales", "logit_opac", "sh_dc", "sh_rest"):
@@ -180,9 +184,9 @@ def test_renderer_batch_binning_changes_nothing(cuda):
     p, _, _ = scenes.config("cfg3", n=N_G, seed=10)
     views = scenes.sphere_views(6, 4.0, W, H, 40.0, 11, hemisphere=True)
     outs = []
-    for bb in (True, False):
+    for bb, streams in ((True, 3), (False, 1)):
         r = Renderer(p, "cuda", batch=4, antialias=True)
-        r.batch_binning = bb
+        r.batch_binning, r.view_streams = bb, streams
         outs.append(r.render(views))
     for (ra, aa), (rb, ab) in zip(*outs):
         assert torch.equal(ra, rb) and torch.equal(aa, ab)
