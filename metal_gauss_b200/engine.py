@@ -237,6 +237,7 @@ class Trainer:
         # views binned per batch binning call (0: all of a step's views); a
         # chunk's rendering on the streams overlaps the binning of the next
         self.bin_chunk = 0
+        self._bin_stream = None
         self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
@@ -649,14 +650,23 @@ class Trainer:
         streams = self._phase_b_streams(V)
         main = torch.cuda.current_stream(self.device)
         C = V if self.bin_chunk <= 0 else min(V, int(self.bin_chunk))
+        # chunked binning runs on a high-priority stream: it is the critical
+        # path while the earlier chunks' views render on the others
+        bin_stream = main
+        if streams and C < V:
+            if self._bin_stream is None:
+                self._bin_stream = torch.cuda.Stream(self.device, priority=-1)
+            bin_stream = self._bin_stream
+            bin_stream.wait_stream(main)
         stats: list = [None] * V
         for c, first in enumerate(range(0, V, C)):
             chunk = views[first:first + C]
-            totals, bb = self._bin_chunk(c, first, chunk)
+            with torch.cuda.stream(bin_stream):
+                totals, bb = self._bin_chunk(c, first, chunk)
             if streams:
                 # the chunk's views on the streams in turn, after its binning
                 ready = torch.cuda.Event()
-                ready.record(main)
+                ready.record(bin_stream)
                 for sk in streams:
                     sk.wait_event(ready)
             for i, view in enumerate(chunk):
@@ -669,6 +679,8 @@ class Trainer:
                                                              lists, k)
                 else:
                     stats[v] = self._render_and_backprop(v, view, targets[v], m, scale, lists)
+        if bin_stream is not main:
+            main.wait_stream(bin_stream)
         for sk in streams:  # the adjoints below wait for every view
             done = torch.cuda.Event()
             done.record(sk)
