@@ -393,22 +393,35 @@ __global__ void bin_write_kernel(const float2* __restrict__ uv,
 // Every output is indexed by item, so the order changes nothing but the
 // warps' divergence. `cls` is in [0, kCostClasses); put items past the end
 // in the last class.
-constexpr int kCostClasses = 16;
+constexpr int kCostClasses = 160;  // 5 per lane of the scanning warp
 __device__ __forceinline__ int block_sorted_slot(int cls) {
+    static_assert(kCostClasses % 32 == 0, "whole classes per lane");
+    constexpr int kPerLane = kCostClasses / 32;
     __shared__ int s_count[kCostClasses];
     __shared__ int s_slot[256];
     const int tid = threadIdx.x;
-    if (tid < kCostClasses) s_count[tid] = 0;
+    for (int k = tid; k < kCostClasses; k += blockDim.x) s_count[k] = 0;
     __syncthreads();
     const int rank = atomicAdd(&s_count[cls], 1);
     __syncthreads();
-    if (tid == 0) {  // exclusive prefix over the classes
-        int run = 0;
+    if (tid < 32) {  // exclusive prefix over the classes: kPerLane per lane
+        int c[kPerLane], sum = 0;
 #pragma unroll
-        for (int k = 0; k < kCostClasses; ++k) {
-            const int c = s_count[k];
-            s_count[k] = run;
-            run += c;
+        for (int k = 0; k < kPerLane; ++k) {
+            c[k] = s_count[tid * kPerLane + k];
+            sum += c[k];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (tid >= o) incl += t;
+        }
+        int run = incl - sum;
+#pragma unroll
+        for (int k = 0; k < kPerLane; ++k) {
+            s_count[tid * kPerLane + k] = run;
+            run += c[k];
         }
     }
     __syncthreads();
@@ -417,7 +430,9 @@ __device__ __forceinline__ int block_sorted_slot(int cls) {
     return s_slot[tid];
 }
 
-// Cost class of a Gaussian's count walk: its tile rectangle's area.
+// Cost class of a Gaussian's count walk: the shape of its tile rectangle
+// (rows, then columns), so a warp's lanes mostly run the same row and column
+// loop trip counts; no tile (invalid) first, items past the end last.
 __device__ __forceinline__ int64_t block_sorted_gaussian(const float2* __restrict__ uv,
                                                          const float2* __restrict__ rxy,
                                                          const int32_t* __restrict__ valid,
@@ -430,8 +445,8 @@ __device__ __forceinline__ int64_t block_sorted_gaussian(const float2* __restric
         if (valid[own] != 0) {
             const float2 mu = uv[own], r = rxy[own];
             const TileRect tr = tile_rect(mu.x, mu.y, r.x, r.y, tile, tiles_x, tiles_y);
-            const int area = (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1);
-            cls = min(kCostClasses - 2, (area + 3) >> 2);
+            const int rh = min(tr.y1 - tr.y0 + 1, 9), rw = min(tr.x1 - tr.x0 + 1, 16);
+            cls = 1 + (rh - 1) * 16 + (rw - 1);  // 1 .. 144
         }
     }
     return (int64_t)blockIdx.x * blockDim.x + block_sorted_slot(cls);
