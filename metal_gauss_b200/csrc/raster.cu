@@ -32,7 +32,11 @@
 //
 // Backward, back to front: work items are (warp block, segment) pairs, a
 // segment being MG_RASTER_SEGMENT consecutive entries of the block's walk,
-// which the forward appends as it finishes each block. A segment starts from
+// which the forward appends as it finishes each block. A backward warp block
+// is two vertically adjacent forward blocks when the tile side is a multiple
+// of 8 (each lane holds two pixels, so the record loads, the cull and the
+// gradient reduction are shared by both); the last of the pair to finish in
+// the forward appends the pair's segments. A segment starts from
 // the checkpoint at its upper end (T
 // there; the colour behind it is the final colour minus the checkpointed one),
 // so a long list is split over many warps instead of forming the kernel's
@@ -116,10 +120,17 @@ __device__ __forceinline__ bool rect_live(const float4 q0, const float C, const 
 }
 
 // Bounding rectangle of the warp's in-image pixel centres, in every lane.
-__device__ __forceinline__ void warp_rect(bool inimg, float fx, float fy, float& x0, float& x1,
+template <int PX>
+__device__ __forceinline__ void warp_rect(const bool (&inimg)[PX], const float (&fx)[PX],
+                                          const float (&fy)[PX], float& x0, float& x1,
                                           float& y0, float& y1) {
-    x0 = inimg ? fx : 3.0e38f; x1 = inimg ? fx : -3.0e38f;
-    y0 = inimg ? fy : 3.0e38f; y1 = inimg ? fy : -3.0e38f;
+    x0 = 3.0e38f; x1 = -3.0e38f; y0 = 3.0e38f; y1 = -3.0e38f;
+#pragma unroll
+    for (int p = 0; p < PX; ++p) {
+        if (!inimg[p]) continue;
+        x0 = fminf(x0, fx[p]); x1 = fmaxf(x1, fx[p]);
+        y0 = fminf(y0, fy[p]); y1 = fmaxf(y1, fy[p]);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         x0 = fminf(x0, __shfl_xor_sync(0xffffffffu, x0, o));
@@ -127,6 +138,13 @@ __device__ __forceinline__ void warp_rect(bool inimg, float fx, float fy, float&
         y0 = fminf(y0, __shfl_xor_sync(0xffffffffu, y0, o));
         y1 = fmaxf(y1, __shfl_xor_sync(0xffffffffu, y1, o));
     }
+}
+
+__device__ __forceinline__ void warp_rect(bool inimg, float fx, float fy, float& x0, float& x1,
+                                          float& y0, float& y1) {
+    const bool in[1] = {inimg};
+    const float x[1] = {fx}, y[1] = {fy};
+    warp_rect<1>(in, x, y, x0, x1, y0, y1);
 }
 
 // ---------------------------------------------------------------- staging
@@ -179,8 +197,8 @@ struct WarpStage {
     }
 };
 
-// Pixels of a tile in warp blocks: 8x4 when the side is a multiple of 8,
-// otherwise row-major with the last block padded.
+// Pixels of a tile in the forward's warp blocks: 8x4 when the side is a
+// multiple of 8, otherwise row-major with the last block padded.
 template <int TILE>
 struct Blocks {
     static constexpr int kPix = TILE * TILE;
@@ -196,6 +214,38 @@ struct Blocks {
             lx = t < kPix ? t % TILE : TILE;  // padding lanes sit outside the tile
             ly = t < kPix ? t / TILE : TILE;
         }
+    }
+};
+
+// Forward blocks per backward warp block (1 or 2) when the tile side is a
+// multiple of 8.
+#ifndef MG_RASTER_PX
+#define MG_RASTER_PX 2
+#endif
+
+// The backward's warp blocks: kPx vertically adjacent forward blocks (8 x 4
+// kPx pixels when the side is a multiple of 8), lane l holding the pixel of
+// lane l in each. A list entry's record, its cull vote and the warp reduction
+// of its gradient are then shared by kPx pixels per lane. (The forward keeps
+// 32-pixel blocks: its heaviest block's walk is a serial chain per warp, and
+// two pixels per lane would double it.)
+template <int TILE>
+struct BwdBlocks {
+    using F = Blocks<TILE>;
+    static constexpr int kPx = TILE % 8 == 0 ? MG_RASTER_PX : 1;
+    static constexpr int kCount = F::kCount / kPx;
+    static_assert(F::kCount % kPx == 0, "whole forward blocks per backward block");
+    // forward block holding pixel p of backward block b
+    __device__ __forceinline__ static int fwd_block(int b, int p) {
+        if (kPx == 1) return b;
+        const int bx = TILE / 8;
+        return ((b / bx) * kPx + p) * bx + b % bx;
+    }
+    // backward block holding forward block wb
+    __device__ __forceinline__ static int of_fwd(int wb) {
+        if (kPx == 1) return wb;
+        const int bx = TILE / 8;
+        return ((wb / bx) / kPx) * bx + wb % bx;
     }
 };
 
@@ -223,9 +273,10 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                       float* __restrict__ out_T, int32_t* __restrict__ out_stop,
                       const int32_t* __restrict__ order, int32_t* __restrict__ counter,
                       int32_t* __restrict__ block_work, int32_t* __restrict__ tile_work,
-                      float* __restrict__ ckpt, int2* __restrict__ items, int m_cap,
-                      int32_t* __restrict__ err) {
+                      float* __restrict__ ckpt, int2* __restrict__ items,
+                      int32_t* __restrict__ pair_done, int m_cap, int32_t* __restrict__ err) {
     using G = Blocks<TILE>;
+    using B = BwdBlocks<TILE>;
     constexpr int kStages = kFwdStages;
     __shared__ WarpStage<kStages> s_stage[kRasterWarps];
     const int lane = threadIdx.x & 31;
@@ -335,20 +386,40 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
             __syncwarp();
         }
         const int walk = __reduce_max_sync(0xffffffffu, stop) - start;
-        // the backward's work items for this block: one per MG_RASTER_SEGMENT
-        // entries of its walk (appended in completion order; every item is at
-        // most one segment, so their order forms no tail)
-        const int nseg = (walk + kSeg - 1) / kSeg;
-        int ibase = 0;
+        // the backward's work items for this block's backward block: one per
+        // MG_RASTER_SEGMENT entries of its walk (the longest of its forward
+        // blocks), appended by the last of those to finish (in completion
+        // order; every item is at most one segment, so their order forms no
+        // tail)
+        const int bb = B::of_fwd(wb);
+        int nseg = 0, ibase = 0;
         if (lane == 0) {
             block_work[tile_id * G::kCount + wb] = walk;
             if (tile_work && walk > 0) atomicMax(&tile_work[tile_id], walk);
-            if (items && nseg > 0) ibase = atomicAdd(&counter[2], nseg);
+            if (items) {
+                int w = walk;
+                bool last = true;
+                if (B::kPx > 1) {
+                    __threadfence();  // this walk is visible before the count
+                    last = atomicAdd(&pair_done[tile_id * B::kCount + bb], 1) == B::kPx - 1;
+                    if (last) {
+                        __threadfence();
+#pragma unroll
+                        for (int p = 0; p < B::kPx; ++p)
+                            w = max(w, *reinterpret_cast<volatile int32_t*>(
+                                           &block_work[tile_id * G::kCount + B::fwd_block(bb, p)]));
+                    }
+                }
+                if (last) {
+                    nseg = (w + kSeg - 1) / kSeg;
+                    if (nseg > 0) ibase = atomicAdd(&counter[2], nseg);
+                }
+            }
         }
+        nseg = __shfl_sync(0xffffffffu, nseg, 0);
         ibase = __shfl_sync(0xffffffffu, ibase, 0);
-        if (items)
-            for (int sgi = lane; sgi < nseg; sgi += 32)
-                items[ibase + sgi] = make_int2(tile_id * G::kCount + wb, sgi);
+        for (int sgi = lane; sgi < nseg; sgi += 32)
+            items[ibase + sgi] = make_int2(tile_id * B::kCount + bb, sgi);
         if (inimg) {
             const int64_t o = (int64_t)py * W + px;
             if (has_bg) {
@@ -417,7 +488,10 @@ __device__ __forceinline__ void record_gather_lanes(int lane, int& s0, int& s1, 
 
 // kSegmented: items are (block, segment) pairs and segments start from the
 // forward's checkpoints; otherwise one item per block walks the whole list
-// from the pixels' stop indices (no forward state needed).
+// from the pixels' stop indices (no forward state needed). With kPx pixels
+// per lane, a lane adds its pixels' contributions to an entry before the
+// warp reduction (or its own atomics), so the reduction and the record loads
+// are shared by kPx pixels.
 template <int TILE, bool kSegmented>
 __global__ void __launch_bounds__(kRasterWarps * 32)
 raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restrict__ ids,
@@ -431,6 +505,8 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                        int32_t* __restrict__ counters, const float* __restrict__ ckpt,
                        int m_cap, int32_t* __restrict__ err) {
     using G = Blocks<TILE>;
+    using B = BwdBlocks<TILE>;
+    constexpr int PX = B::kPx;
     constexpr int kStages = kBwdStages;
     __shared__ WarpStage<kStages> s_stage[kRasterWarps];
     const int lane = threadIdx.x & 31;
@@ -442,11 +518,7 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
     for (int item = pull_item(counters + 1, lane); item < n_items;
          item = pull_item(counters + 1, lane)) {
         const int2 it = items[item];
-        const int tile_id = it.x / G::kCount, wb = it.x % G::kCount, seg = it.y;
-        int lx, ly;
-        G::pixel(wb, lane, lx, ly);
-        const int px = (tile_id % tiles_x) * TILE + lx, py = (tile_id / tiles_x) * TILE + ly;
-        const bool inimg = lx < TILE && ly < TILE && px < W && py < H;
+        const int tile_id = it.x / B::kCount, wb = it.x % B::kCount, seg = it.y;
         const int start = offsets[tile_id], end = offsets[tile_id + 1];
         if (end > m_cap) {
             if (lane == 0) record_device_error(err, DEV_ERR_INDEX);
@@ -454,39 +526,53 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
         }
         const int seg_lo = start + seg * kSeg;
         const int seg_top = kSegmented ? min(seg_lo + kSeg, end) : end;
-        const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-        const int64_t o = inimg ? (int64_t)py * W + px : 0;
+        const int tx0 = (tile_id % tiles_x) * TILE, ty0 = (tile_id / tiles_x) * TILE;
 
         // S = <d L / d (rgb, alpha), colour and alpha blended behind the
         // current entry>: one running dot product instead of four suffix sums
-        float T = 1.0f, S = 0.0f;
-        float gr = 0.f, gg = 0.f, gb = 0.f, ga = 0.f;
-        int my_stop = start;
-        if (inimg) {
-            my_stop = stop_idx[o];
-            gr = grad_rgb[3 * o]; gg = grad_rgb[3 * o + 1]; gb = grad_rgb[3 * o + 2];
-            ga = grad_alpha ? grad_alpha[o] : 0.0f;
+        bool inimg[PX];
+        float fx[PX], fy[PX], T[PX], S[PX], gr[PX], gg[PX], gb[PX], ga[PX];
+        int my_stop[PX];
+        int hi = seg_lo;
+#pragma unroll
+        for (int p = 0; p < PX; ++p) {
+            const int fb = B::fwd_block(wb, p);
+            int lx, ly;
+            G::pixel(fb, lane, lx, ly);
+            const int px = tx0 + lx, py = ty0 + ly;
+            inimg[p] = lx < TILE && ly < TILE && px < W && py < H;
+            fx[p] = (float)px + 0.5f;
+            fy[p] = (float)py + 0.5f;
+            T[p] = 1.0f; S[p] = 0.0f;
+            gr[p] = gg[p] = gb[p] = ga[p] = 0.0f;
+            my_stop[p] = start;
+            if (!inimg[p]) continue;
+            const int64_t o = (int64_t)py * W + px;
+            my_stop[p] = stop_idx[o];
+            gr[p] = grad_rgb[3 * o]; gg[p] = grad_rgb[3 * o + 1]; gb[p] = grad_rgb[3 * o + 2];
+            ga[p] = grad_alpha ? grad_alpha[o] : 0.0f;
             const float a_fin = (has_bg || kSegmented) ? out_alpha[o] : 0.0f;
             const float kbg = fmaxf(1.0f - a_fin, 0.0f);
             // rgb_out = rgb + max(1 - alpha, 0) * bg  =>  d alpha -= <d rgb, bg>
-            if (has_bg && 1.0f - a_fin >= 0.0f) ga -= gr * bg_r + gg * bg_g + gb * bg_b;
-            if (kSegmented && my_stop > seg_lo + kSeg) {
+            if (has_bg && 1.0f - a_fin >= 0.0f)
+                ga[p] -= gr[p] * bg_r + gg[p] * bg_g + gb[p] * bg_b;
+            if (kSegmented && my_stop[p] > seg_lo + kSeg) {
                 const float* c = ckpt + ckpt_slot(start, tile_id, seg + 1) * 5 * G::kPixPad +
-                                 wb * 32 + lane;
+                                 fb * 32 + lane;
                 float cr = out_rgb[3 * o], cg = out_rgb[3 * o + 1], cbl = out_rgb[3 * o + 2];
                 if (has_bg) { cr -= kbg * bg_r; cg -= kbg * bg_g; cbl -= kbg * bg_b; }
-                T = c[0];
-                S = gr * (cr - c[G::kPixPad]) + gg * (cg - c[2 * G::kPixPad]) +
-                    gb * (cbl - c[3 * G::kPixPad]) + ga * (a_fin - c[4 * G::kPixPad]);
+                T[p] = c[0];
+                S[p] = gr[p] * (cr - c[G::kPixPad]) + gg[p] * (cg - c[2 * G::kPixPad]) +
+                       gb[p] * (cbl - c[3 * G::kPixPad]) + ga[p] * (a_fin - c[4 * G::kPixPad]);
             } else {
-                T = final_T[o];
+                T[p] = final_T[o];
             }
+            hi = max(hi, min(my_stop[p], seg_top));
         }
-        const int hi = inimg ? min(my_stop, seg_top) : seg_lo;
         const int warp_hi = __reduce_max_sync(0xffffffffu, hi);
         if (warp_hi <= seg_lo) continue;
         float rx0, rx1, ry0, ry1;
-        warp_rect(inimg, fx, fy, rx0, rx1, ry0, ry1);
+        warp_rect<PX>(inimg, fx, fy, rx0, rx1, ry0, ry1);
 
         // chunks are aligned to the list start (seg_lo is a chunk boundary)
         // and walked from the top one down: chunk c starts at top - 32 c
@@ -521,46 +607,65 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                 live &= ~(1u << k);
                 const float4 a = st.q[buf][0][k], b4 = st.q[buf][1][k];
                 const float cbk = st.q[buf][2][k].x;
-                const float dx = fx - a.x, dy = fy - a.y;
-                const float power = pair_power(dx, dy, a.z, a.w, b4.x);
-                const float gauss = __expf(fminf(power, 0.0f));
-                const float alpha_raw = b4.y * gauss;
-                const float alpha = fminf(0.999f, alpha_raw);
-                const bool active = inimg && (base + k < my_stop) && (power <= 0.0f) &&
-                                    (alpha >= 1.0f / 255.0f);
-                const uint32_t act = __ballot_sync(0xffffffffu, active);
-                if (act == 0u) continue;
-                // every lane evaluates; inactive lanes are masked to zero
-                const float om = fmaxf(1.0f - alpha, 1e-8f);
-                // segments bound the recovery chain to kSeg divisions
-                const float inv = kSegmented ? __fdividef(1.0f, om) : __frcp_rn(om);
-                const float Tn = T * inv;
-                const float q = gr * b4.z + gg * b4.w + gb * cbk + ga;
-                const float dL_dalpha = Tn * q - inv * S;
-                const float w = active ? alpha * Tn : 0.0f;
-                T = active ? Tn : T;
-                S += w * q;
-                // the 0.999 clamp cuts the gradient to opacity and position
-                const float dLg = (active && alpha_raw <= 0.999f) ? dL_dalpha * gauss : 0.0f;
-                const float dp = dLg * b4.y;
+                float dx[PX], dy[PX], gauss[PX], alpha_raw[PX], alpha[PX];
+                bool active[PX];
+                bool any = false;
+                int n_act = 0;
+#pragma unroll
+                for (int p = 0; p < PX; ++p) {
+                    dx[p] = fx[p] - a.x;
+                    dy[p] = fy[p] - a.y;
+                    const float power = pair_power(dx[p], dy[p], a.z, a.w, b4.x);
+                    gauss[p] = __expf(fminf(power, 0.0f));
+                    alpha_raw[p] = b4.y * gauss[p];
+                    alpha[p] = fminf(0.999f, alpha_raw[p]);
+                    active[p] = inimg[p] && (base + k < my_stop[p]) && (power <= 0.0f) &&
+                                (alpha[p] >= 1.0f / 255.0f);
+                    any = any || active[p];
+                    n_act += __popc(__ballot_sync(0xffffffffu, active[p]));
+                }
+                if (n_act == 0) continue;
+                // every lane evaluates; inactive pixels are masked to zero
                 float v[10];
-                // d power / d u = ca dx + cb dy = -(2A dx + B dy)
-                v[0] = -dp * (2.0f * a.z * dx + a.w * dy);
-                v[1] = -dp * (a.w * dx + 2.0f * b4.x * dy);
-                v[2] = dLg;
-                v[3] = want_absgrad ? sqrtf(v[0] * v[0] + v[1] * v[1]) : 0.0f;
-                v[4] = dp * (-0.5f * dx * dx);
-                v[5] = dp * (-1.0f * dx * dy);
-                v[6] = dp * (-0.5f * dy * dy);
-                v[7] = w * gr; v[8] = w * gg; v[9] = w * gb;
+#pragma unroll
+                for (int i = 0; i < 10; ++i) v[i] = 0.0f;
+                bool has_dp = false;
+#pragma unroll
+                for (int p = 0; p < PX; ++p) {
+                    const float om = fmaxf(1.0f - alpha[p], 1e-8f);
+                    // segments bound the recovery chain to kSeg divisions
+                    const float inv = kSegmented ? __fdividef(1.0f, om) : __frcp_rn(om);
+                    const float Tn = T[p] * inv;
+                    const float q = gr[p] * b4.z + gg[p] * b4.w + gb[p] * cbk + ga[p];
+                    const float dL_dalpha = Tn * q - inv * S[p];
+                    const float w = active[p] ? alpha[p] * Tn : 0.0f;
+                    T[p] = active[p] ? Tn : T[p];
+                    S[p] += w * q;
+                    // the 0.999 clamp cuts the gradient to opacity and position
+                    const float dLg =
+                        (active[p] && alpha_raw[p] <= 0.999f) ? dL_dalpha * gauss[p] : 0.0f;
+                    const float dp = dLg * b4.y;
+                    has_dp = has_dp || dp != 0.0f;
+                    // d power / d u = ca dx + cb dy = -(2A dx + B dy)
+                    const float g0v = -dp * (2.0f * a.z * dx[p] + a.w * dy[p]);
+                    const float g1v = -dp * (a.w * dx[p] + 2.0f * b4.x * dy[p]);
+                    v[0] += g0v;
+                    v[1] += g1v;
+                    v[2] += dLg;
+                    if (want_absgrad) v[3] += sqrtf(g0v * g0v + g1v * g1v);
+                    v[4] += dp * (-0.5f * dx[p] * dx[p]);
+                    v[5] += dp * (-1.0f * dx[p] * dy[p]);
+                    v[6] += dp * (-0.5f * dy[p] * dy[p]);
+                    v[7] += w * gr[p]; v[8] += w * gg[p]; v[9] += w * gb[p];
+                }
                 float4* dst =
                     reinterpret_cast<float4*>(grad2d + (int64_t)st.id[buf][k] * MG_G2D_STRIDE);
-                if (__popc(act) <= kBwdDirectMax) {
-                    // few contributing pixels: each adds its own record (the
+                if (n_act <= kBwdDirectMax) {
+                    // few contributing pixels: each lane adds its own sum (the
                     // warp reduction costs more than a few sets of atomics)
-                    if (active) {
+                    if (any) {
                         atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
-                        if (dp != 0.f) atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
+                        if (has_dp) atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
                         atomicAdd(dst + 2, make_float4(v[7], v[8], v[9], 0.f));
                     }
                     continue;
@@ -631,12 +736,13 @@ __device__ __forceinline__ int length_class(int w) {
 }
 
 // Longest-first tile order by list-length class (order inside a class is
-// unspecified). Optionally zeroes a work counter and a per-tile array for the
-// kernel that follows.
+// unspecified). Optionally zeroes a work counter, a per-tile array and the
+// per-backward-block completion counters for the kernel that follows.
 __global__ void __launch_bounds__(1024)
 tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict__ work,
                   int n_tiles, int32_t* __restrict__ order, int32_t* __restrict__ zero_word,
-                  int32_t* __restrict__ zero_tiles) {
+                  int32_t* __restrict__ zero_tiles, int32_t* __restrict__ zero_pairs,
+                  int n_pairs) {
     __shared__ int s_total[kOrderClasses];
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid < kOrderClasses) s_total[tid] = 0;
@@ -651,6 +757,8 @@ tile_order_kernel(const int32_t* __restrict__ offsets, const int32_t* __restrict
         for (int c = 0; c < kOrderClasses; ++c) cnt[c] += cls == c;
         if (zero_tiles) zero_tiles[t] = 0;
     }
+    if (zero_pairs)
+        for (int b = tid; b < n_pairs; b += 1024) zero_pairs[b] = 0;
     class_positions<kOrderClasses>(cnt, pos, lane, s_total);
     for (int t = tid; t < n_tiles; t += 1024) {
         const int cls = length_class(work ? work[t] : offsets[t + 1] - offsets[t]);
@@ -767,13 +875,18 @@ __global__ void antialias_opacity_backward_kernel(const float* __restrict__ coni
 
 // ---------------------------------------------------------------- host side
 
+// Forward and backward warp blocks per tile (Blocks / BwdBlocks on the host).
 int blocks_per_tile(int tile) { return (tile * tile + 31) / 32; }
+int bwd_blocks_per_tile(int tile) {
+    return tile % 8 == 0 ? blocks_per_tile(tile) / MG_RASTER_PX : blocks_per_tile(tile);
+}
 
 // Scratch shared by one view's forward and backward.
 struct RasterScratch {
     int32_t* counters;    // [0] forward pull, [1] backward pull, [2] backward item count
     int32_t* order;       // n_tiles, longest list first
     int32_t* block_work;  // n_blocks walk lengths (forward)
+    int32_t* pair_done;   // per backward block: its forward blocks finished
     int2* items;          // backward work items
     float* ckpt;          // checkpoint slots x 5 x pixel slots
     size_t bytes;
@@ -782,17 +895,18 @@ struct RasterScratch {
 RasterScratch carve_raster(void* base, int W, int H, int tile, int64_t m) {
     const int64_t tiles_x = (W + tile - 1) / tile, tiles_y = (H + tile - 1) / tile;
     const int64_t n_tiles = tiles_x * tiles_y;
-    const int bpt = blocks_per_tile(tile);
-    const int64_t n_blocks = n_tiles * bpt;
+    const int bpt = blocks_per_tile(tile), bbpt = bwd_blocks_per_tile(tile);
+    const int64_t n_blocks = n_tiles * bpt, n_bwd = n_tiles * bbpt;
     const int64_t m1 = std::max<int64_t>(m, 1);
-    // sum over blocks of ceil(walk / kSeg) <= n_blocks + bpt * m / kSeg
-    const int64_t n_items = n_blocks + (int64_t)bpt * ((m1 + kSeg - 1) / kSeg);
+    // sum over backward blocks of ceil(walk / kSeg) <= n_bwd + bbpt * m / kSeg
+    const int64_t n_items = n_bwd + (int64_t)bbpt * ((m1 + kSeg - 1) / kSeg);
     const int64_t slots = m1 / kSeg + n_tiles;
     RasterScratch s;
     char* p = static_cast<char*>(base);
     s.counters = reinterpret_cast<int32_t*>(p); p += 256;
     s.order = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * n_tiles);
     s.block_work = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * n_blocks);
+    s.pair_done = reinterpret_cast<int32_t*>(p); p += align256(sizeof(int32_t) * n_bwd);
     s.items = reinterpret_cast<int2*>(p); p += align256(sizeof(int2) * n_items);
     s.ckpt = reinterpret_cast<float*>(p);
     p += align256(sizeof(float) * (size_t)slots * 5 * (size_t)bpt * 32);
@@ -827,7 +941,8 @@ mg_status launch_fwd(const float4* splats, const int32_t* ids, const int32_t* of
                      const RasterScratch& sc, int m_cap, cudaStream_t stream) {
     const int n_tiles = tiles_x * tiles_y;
     tile_order_kernel<<<1, 1024, 0, stream>>>(offsets, nullptr, n_tiles, sc.order, sc.counters,
-                                              tile_work);
+                                              tile_work, T ? sc.pair_done : nullptr,
+                                              n_tiles * BwdBlocks<TILE>::kCount);
     MG_TRY(check_launch("rasterize_forward order"));
     const void* k = reinterpret_cast<const void*>(&raster_forward_kernel<TILE>);
     const int grid = persistent_grid(k, kRasterWarps * 32);
@@ -835,8 +950,8 @@ mg_status launch_fwd(const float4* splats, const int32_t* ids, const int32_t* of
     raster_forward_kernel<TILE><<<grid, kRasterWarps * 32, 0, stream>>>(
         splats, ids, offsets, W, H, tiles_x, n_tiles, bg != nullptr, bg ? bg[0] : 0.f,
         bg ? bg[1] : 0.f, bg ? bg[2] : 0.f, rgb, alpha, T, stop, sc.order, sc.counters,
-        sc.block_work, tile_work, T ? sc.ckpt : nullptr, T ? sc.items : nullptr, m_cap,
-        device_error_word());
+        sc.block_work, tile_work, T ? sc.ckpt : nullptr, T ? sc.items : nullptr, sc.pair_done,
+        m_cap, device_error_word());
     return check_launch("rasterize_forward");
 }
 
@@ -855,7 +970,7 @@ mg_status launch_bwd_mode(const float4* splats, const int32_t* ids, const int32_
             return check_launch("rasterize_backward counter");
     } else {
         backward_items_kernel<<<1, 1024, 0, stream>>>(offsets, nullptr, n_tiles,
-                                                      Blocks<TILE>::kCount, 0, sc.items,
+                                                      BwdBlocks<TILE>::kCount, 0, sc.items,
                                                       sc.counters);
         MG_TRY(check_launch("rasterize_backward items"));
     }
@@ -996,7 +1111,7 @@ extern "C" mg_status mg_tile_order(const int32_t* tile_offsets, const int32_t* w
     MG_REQUIRE(n_tiles > 0 && order != nullptr, "tile_order: bad arguments");
     MG_REQUIRE(work != nullptr || tile_offsets != nullptr, "tile_order: no work measure");
     tile_order_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        tile_offsets, work, n_tiles, order, nullptr, nullptr);
+        tile_offsets, work, n_tiles, order, nullptr, nullptr, nullptr, 0);
     return check_launch("tile_order");
 }
 
