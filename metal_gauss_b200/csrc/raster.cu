@@ -42,8 +42,8 @@
 // so a long list is split over many warps instead of forming the kernel's
 // tail. The colour and alpha behind an entry enter its gradient only through
 // their dot product with the pixel's output gradient, so a pixel carries one
-// running sum for them. A live entry to which at most 16 of the warp's
-// pixels contribute is added as per-pixel 16-byte vector atomics; otherwise
+// running sum for them. A live entry to which at most 24 of the warp's
+// pixels contribute is added as per-lane 16-byte vector atomics; otherwise
 // the warp reduces its 32 pixels' contributions with a 10-slot butterfly
 // reduce-scatter (12 shuffles) and three lanes add the 48-byte gradient record
 // with three vector atomics (the crossover measured on B200).
@@ -173,10 +173,12 @@ __device__ __forceinline__ void cp_async_wait() {
 #endif
 constexpr int kFwdStages = MG_FWD_STAGES;
 #ifndef MG_BWD_DIRECT_MAX
-#define MG_BWD_DIRECT_MAX 16
+#define MG_BWD_DIRECT_MAX 24
 #endif
-// Up to this many contributing pixels, a live entry's gradient goes out as
-// per-pixel vector atomics instead of through the warp reduction.
+// Up to this many contributing pixels (of a backward block's 64 when the
+// tile side is a multiple of 8), a live entry's gradient goes out as per-lane
+// vector atomics instead of through the warp reduction (8 / 16 / 24 / 32
+// measured on the bench: 24 and 32 best).
 constexpr int kBwdDirectMax = MG_BWD_DIRECT_MAX;
 constexpr int kBwdStages = MG_BWD_STAGES;
 
