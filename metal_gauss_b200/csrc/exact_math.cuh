@@ -73,26 +73,16 @@ struct Projected {
     float a, b, c;     // dilated 2D covariance (used by the backward)
 };
 
-__device__ __forceinline__ Projected project_one(
-    const CamParams& P, float mx, float my, float mz,
-    float qw0, float qx0, float qy0, float qz0,
-    float sx, float sy, float sz, float op)
-{
-    Projected o;
-    const float pcx = ((P.R0.x * mx + P.R0.y * my) + P.R0.z * mz) + P.R0.w;
-    const float pcy = ((P.R1.x * mx + P.R1.y * my) + P.R1.z * mz) + P.R1.w;
-    const float pcz = ((P.R2.x * mx + P.R2.y * my) + P.R2.z * mz) + P.R2.w;
-    const float z = pcz;
-    const float zc = fmaxf(z, P.near_plane);
+// The view-independent part of a projection: the 3D covariance from the
+// quaternion and scales, and the opacity's radius factor sqrt(2 ln(255 op)).
+struct GaussianCov {
+    float S00, S01, S02, S11, S12, S22;
+    float rs;
+};
 
-    const float u = ((P.fx * pcx) / zc) + P.cx;
-    const float v = ((P.fy * pcy) / zc) + P.cy;
-
-    const float lim_x = 1.3f * ((0.5f * (float)P.W) / P.fx);
-    const float lim_y = 1.3f * ((0.5f * (float)P.H) / P.fy);
-    const float tx = clampf(pcx / zc, -lim_x, lim_x) * zc;
-    const float ty = clampf(pcy / zc, -lim_y, lim_y) * zc;
-
+__device__ __forceinline__ GaussianCov gaussian_cov(float qw0, float qx0, float qy0, float qz0,
+                                                    float sx, float sy, float sz, float op) {
+    GaussianCov G;
     const float qn = sqrtf(((qw0 * qw0 + qx0 * qx0) + qy0 * qy0) + qz0 * qz0);
     const float qd = fmaxf(qn, 1e-12f);
     const float w = qw0 / qd, x = qx0 / qd, y = qy0 / qd, zq = qz0 / qd;
@@ -110,12 +100,37 @@ __device__ __forceinline__ Projected project_one(
     const float M00 = R00 * sx, M01 = R01 * sy, M02 = R02 * sz;
     const float M10 = R10 * sx, M11 = R11 * sy, M12 = R12 * sz;
     const float M20 = R20 * sx, M21 = R21 * sy, M22 = R22 * sz;
-    const float S00 = (M00 * M00 + M01 * M01) + M02 * M02;
-    const float S01 = (M00 * M10 + M01 * M11) + M02 * M12;
-    const float S02 = (M00 * M20 + M01 * M21) + M02 * M22;
-    const float S11 = (M10 * M10 + M11 * M11) + M12 * M12;
-    const float S12 = (M10 * M20 + M11 * M21) + M12 * M22;
-    const float S22 = (M20 * M20 + M21 * M21) + M22 * M22;
+    G.S00 = (M00 * M00 + M01 * M01) + M02 * M02;
+    G.S01 = (M00 * M10 + M01 * M11) + M02 * M12;
+    G.S02 = (M00 * M20 + M01 * M21) + M02 * M22;
+    G.S11 = (M10 * M10 + M11 * M11) + M12 * M12;
+    G.S12 = (M10 * M20 + M11 * M21) + M12 * M22;
+    G.S22 = (M20 * M20 + M21 * M21) + M22 * M22;
+
+    const float twoL = 2.0f * log_f32_via_f64(fmaxf(255.0f * op, 1.0f));
+    G.rs = sqrtf(twoL);
+    return G;
+}
+
+// The view-dependent part: everything preprocess_forward produces for one
+// Gaussian and camera except colour, from its mean and GaussianCov.
+__device__ __forceinline__ Projected project_with(const CamParams& P, float mx, float my,
+                                                  float mz, const GaussianCov& G) {
+    Projected o;
+    const float S00 = G.S00, S01 = G.S01, S02 = G.S02, S11 = G.S11, S12 = G.S12, S22 = G.S22;
+    const float pcx = ((P.R0.x * mx + P.R0.y * my) + P.R0.z * mz) + P.R0.w;
+    const float pcy = ((P.R1.x * mx + P.R1.y * my) + P.R1.z * mz) + P.R1.w;
+    const float pcz = ((P.R2.x * mx + P.R2.y * my) + P.R2.z * mz) + P.R2.w;
+    const float z = pcz;
+    const float zc = fmaxf(z, P.near_plane);
+
+    const float u = ((P.fx * pcx) / zc) + P.cx;
+    const float v = ((P.fy * pcy) / zc) + P.cy;
+
+    const float lim_x = 1.3f * ((0.5f * (float)P.W) / P.fx);
+    const float lim_y = 1.3f * ((0.5f * (float)P.H) / P.fy);
+    const float tx = clampf(pcx / zc, -lim_x, lim_x) * zc;
+    const float ty = clampf(pcy / zc, -lim_y, lim_y) * zc;
 
     const float izc = 1.0f / zc, izc2 = izc * izc;
     const float J0x = P.fx * izc, J0z = ((-P.fx) * tx) * izc2;
@@ -146,8 +161,7 @@ __device__ __forceinline__ Projected project_one(
     const float lam = fmaxf(mid + disc, 1e-12f);
     const float radius = 3.0f * sqrtf(lam);
 
-    const float twoL = 2.0f * log_f32_via_f64(fmaxf(255.0f * op, 1.0f));
-    const float rs = sqrtf(twoL);
+    const float rs = G.rs;
     const float rx = fminf(rs * sqrtf(fmaxf(a, 0.0f)), radius);
     const float ry = fminf(rs * sqrtf(fmaxf(c, 0.0f)), radius);
 
@@ -160,6 +174,14 @@ __device__ __forceinline__ Projected project_one(
     o.z = z; o.rx = rx; o.ry = ry;
     o.a = a; o.b = b; o.c = c;
     return o;
+}
+
+__device__ __forceinline__ Projected project_one(
+    const CamParams& P, float mx, float my, float mz,
+    float qw0, float qx0, float qy0, float qz0,
+    float sx, float sy, float sz, float op)
+{
+    return project_with(P, mx, my, mz, gaussian_cov(qw0, qx0, qy0, qz0, sx, sy, sz, op));
 }
 
 // Minimum of a x^2 + 2 b x y + c y^2 (x, y relative to mu) over the closed

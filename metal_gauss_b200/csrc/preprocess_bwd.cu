@@ -53,16 +53,48 @@ struct ShBlock {
     }
 };
 
-// Projection adjoint of one valid Gaussian for one camera (preprocess.metal:
-// 265-411): the incoming uv and conic gradients are carried through the conic
-// inverse, the EWA covariance J W Sigma W^T J^T (with the Jacobian's clamp
-// routing to zc), Sigma = R S S^T R^T and the quaternion normalisation.
-// Adds the mean gradient into dmx/dmy/dmz; returns d scales and d quat.
-__device__ __forceinline__ void projection_adjoint(const CamParams& P, float mx, float my,
-                                                   float mz, const float4 q4, const float (&s)[3],
-                                                   float dux, float duy, float dcx, float dcy,
-                                                   float dcz, float& dmx, float& dmy,
-                                                   float& dmz, float (&ds)[3], float4& dq) {
+// Projection adjoint (preprocess.metal:265-411), in two parts: the incoming
+// uv and conic gradients of one camera are carried through the conic inverse
+// and the EWA covariance J W Sigma W^T J^T (with the Jacobian's clamp routing
+// to zc) to the mean and to d Sigma; d Sigma goes through Sigma = R S S^T R^T
+// and the quaternion normalisation to d scales and d quat. The second part is
+// linear in d Sigma, so a Gaussian seen by several cameras sums their
+// (symmetrised) d Sigma and runs it once; the view-independent rotation and
+// covariance are formed once as well.
+struct CovFrame {
+    float w, x, y, zq, qd;  // normalised quaternion and the norm it was divided by
+    float R[3][3], M[3][3], S[3][3];
+};
+
+__device__ __forceinline__ CovFrame cov_frame(const float4 q4, const float (&s)[3]) {
+    CovFrame F;
+    const float qn = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
+    F.qd = fmaxf(qn, 1e-12f);
+    const float w = q4.x / F.qd, x = q4.y / F.qd, y = q4.z / F.qd, zq = q4.w / F.qd;
+    F.w = w; F.x = x; F.y = y; F.zq = zq;
+    F.R[0][0] = 1.f - 2.f * (y * y + zq * zq); F.R[0][1] = 2.f * (x * y - w * zq); F.R[0][2] = 2.f * (x * zq + w * y);
+    F.R[1][0] = 2.f * (x * y + w * zq); F.R[1][1] = 1.f - 2.f * (x * x + zq * zq); F.R[1][2] = 2.f * (y * zq - w * x);
+    F.R[2][0] = 2.f * (x * zq - w * y); F.R[2][1] = 2.f * (y * zq + w * x); F.R[2][2] = 1.f - 2.f * (x * x + y * y);
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) F.M[i][j] = F.R[i][j] * s[j];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+            F.S[i][j] = F.M[i][0] * F.M[j][0] + F.M[i][1] * F.M[j][1] + F.M[i][2] * F.M[j][2];
+    return F;
+}
+
+// One camera: adds the mean gradient into dmx/dmy/dmz and the symmetrised
+// covariance gradient (entries 00 01 02 11 12 22) into dSym.
+__device__ __forceinline__ void projection_adjoint_view(const CamParams& P, float mx, float my,
+                                                        float mz, const float (&S)[3][3],
+                                                        float dux, float duy, float dcx,
+                                                        float dcy, float dcz, float& dmx,
+                                                        float& dmy, float& dmz,
+                                                        float (&dSym)[6]) {
     const float fx = P.fx, fy = P.fy;
     const float pcx = P.R0.x * mx + P.R0.y * my + P.R0.z * mz + P.R0.w;
     const float pcy = P.R1.x * mx + P.R1.y * my + P.R1.z * mz + P.R1.w;
@@ -76,23 +108,6 @@ __device__ __forceinline__ void projection_adjoint(const CamParams& P, float mx,
     const bool cly = (tyn < -lim_y) || (tyn > lim_y);
     const float tx = clampf(txn, -lim_x, lim_x) * zc;
     const float ty = clampf(tyn, -lim_y, lim_y) * zc;
-    const float qn = sqrtf(q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w);
-    const float qd = fmaxf(qn, 1e-12f);
-    const float w = q4.x / qd, x = q4.y / qd, y = q4.z / qd, zq = q4.w / qd;
-    float R[3][3];
-    R[0][0] = 1.f - 2.f * (y * y + zq * zq); R[0][1] = 2.f * (x * y - w * zq); R[0][2] = 2.f * (x * zq + w * y);
-    R[1][0] = 2.f * (x * y + w * zq); R[1][1] = 1.f - 2.f * (x * x + zq * zq); R[1][2] = 2.f * (y * zq - w * x);
-    R[2][0] = 2.f * (x * zq - w * y); R[2][1] = 2.f * (y * zq + w * x); R[2][2] = 1.f - 2.f * (x * x + y * y);
-
-    float M[3][3], S[3][3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) M[i][j] = R[i][j] * s[j];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) S[i][j] = M[i][0] * M[j][0] + M[i][1] * M[j][1] + M[i][2] * M[j][2];
 
     const float Rw[3][3] = {{P.R0.x, P.R0.y, P.R0.z}, {P.R1.x, P.R1.y, P.R1.z},
                             {P.R2.x, P.R2.y, P.R2.z}};
@@ -121,13 +136,14 @@ __device__ __forceinline__ void projection_adjoint(const CamParams& P, float mx,
     float dc = dcx * id + ddet * a;
     if (det <= 1e-12f) { da = db = dc = 0.f; }
 
-    // dSigma (unsymmetrised) = da T0 T0^T + db T0 T1^T + dc T1 T1^T
-    float dS[3][3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j)
-            dS[i][j] = da * T0[i] * T0[j] + db * T0[i] * T1[j] + dc * T1[i] * T1[j];
+    // d Sigma = da T0 T0^T + db T0 T1^T + dc T1 T1^T, symmetrised
+    const float hb = 0.5f * db;
+    dSym[0] += da * T0[0] * T0[0] + db * T0[0] * T1[0] + dc * T1[0] * T1[0];
+    dSym[1] += da * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T0[1] * T1[0]) + dc * T1[0] * T1[1];
+    dSym[2] += da * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T0[2] * T1[0]) + dc * T1[0] * T1[2];
+    dSym[3] += da * T0[1] * T0[1] + db * T0[1] * T1[1] + dc * T1[1] * T1[1];
+    dSym[4] += da * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T0[2] * T1[1]) + dc * T1[1] * T1[2];
+    dSym[5] += da * T0[2] * T0[2] + db * T0[2] * T1[2] + dc * T1[2] * T1[2];
     float dT0[3], dT1[3];
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
@@ -153,34 +169,51 @@ __device__ __forceinline__ void projection_adjoint(const CamParams& P, float mx,
     dmx += Rw[0][0] * dpx + Rw[1][0] * dpy + Rw[2][0] * dpz;
     dmy += Rw[0][1] * dpx + Rw[1][1] * dpy + Rw[2][1] * dpz;
     dmz += Rw[0][2] * dpx + Rw[1][2] * dpy + Rw[2][2] * dpz;
+}
 
+// From the (summed, symmetrised) covariance gradient to d scales and d quat.
+__device__ __forceinline__ void covariance_adjoint(const CovFrame& F, const float (&s)[3],
+                                                   const float (&dSym)[6], float (&ds)[3],
+                                                   float4& dq) {
+    const float D[3][3] = {{dSym[0], dSym[1], dSym[2]},
+                           {dSym[1], dSym[3], dSym[4]},
+                           {dSym[2], dSym[4], dSym[5]}};
     // dM = 2 sym(dSigma) M
     float dM[3][3];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
-        for (int j = 0; j < 3; ++j) {
-            float acc = 0.f;
+        for (int j = 0; j < 3; ++j)
+            dM[i][j] = 2.0f * (D[i][0] * F.M[0][j] + D[i][1] * F.M[1][j] + D[i][2] * F.M[2][j]);
 #pragma unroll
-            for (int k = 0; k < 3; ++k) acc += 0.5f * (dS[i][k] + dS[k][i]) * M[k][j];
-            dM[i][j] = 2.0f * acc;
-        }
-    const float ds0 = dM[0][0] * R[0][0] + dM[1][0] * R[1][0] + dM[2][0] * R[2][0];
-    const float ds1 = dM[0][1] * R[0][1] + dM[1][1] * R[1][1] + dM[2][1] * R[2][1];
-    const float ds2 = dM[0][2] * R[0][2] + dM[1][2] * R[1][2] + dM[2][2] * R[2][2];
-    ds[0] = ds0; ds[1] = ds1; ds[2] = ds2;
+    for (int j = 0; j < 3; ++j)
+        ds[j] = dM[0][j] * F.R[0][j] + dM[1][j] * F.R[1][j] + dM[2][j] * F.R[2][j];
     float G[3][3];  // dL/dR
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
         for (int j = 0; j < 3; ++j) G[i][j] = dM[i][j] * s[j];
+    const float w = F.w, x = F.x, y = F.y, zq = F.zq;
     const float dw = 2.f * (x * (G[2][1] - G[1][2]) + y * (G[0][2] - G[2][0]) + zq * (G[1][0] - G[0][1]));
     const float dqx = 2.f * (w * (G[2][1] - G[1][2]) + y * (G[1][0] + G[0][1]) + zq * (G[2][0] + G[0][2]) - 2.f * x * (G[1][1] + G[2][2]));
     const float dqy = 2.f * (w * (G[0][2] - G[2][0]) + x * (G[1][0] + G[0][1]) + zq * (G[2][1] + G[1][2]) - 2.f * y * (G[0][0] + G[2][2]));
     const float dqz = 2.f * (w * (G[1][0] - G[0][1]) + x * (G[2][0] + G[0][2]) + y * (G[2][1] + G[1][2]) - 2.f * zq * (G[0][0] + G[1][1]));
     const float qdot = w * dw + x * dqx + y * dqy + zq * dqz;
-    dq = make_float4((dw - w * qdot) / qd, (dqx - x * qdot) / qd, (dqy - y * qdot) / qd,
-                     (dqz - zq * qdot) / qd);
+    dq = make_float4((dw - w * qdot) / F.qd, (dqx - x * qdot) / F.qd, (dqy - y * qdot) / F.qd,
+                     (dqz - zq * qdot) / F.qd);
+}
+
+// Both parts for one camera. Adds the mean gradient into dmx/dmy/dmz;
+// returns d scales and d quat.
+__device__ __forceinline__ void projection_adjoint(const CamParams& P, float mx, float my,
+                                                   float mz, const float4 q4, const float (&s)[3],
+                                                   float dux, float duy, float dcx, float dcy,
+                                                   float dcz, float& dmx, float& dmy,
+                                                   float& dmz, float (&ds)[3], float4& dq) {
+    const CovFrame F = cov_frame(q4, s);
+    float dSym[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    projection_adjoint_view(P, mx, my, mz, F.S, dux, duy, dcx, dcy, dcz, dmx, dmy, dmz, dSym);
+    covariance_adjoint(F, s, dSym, ds, dq);
 }
 
 // kAccum = false: the reference bridge's semantics (every output overwritten).
@@ -411,8 +444,10 @@ preprocess_backward_views_kernel(const float* __restrict__ means,
         s[0] = fl.s[0]; s[1] = fl.s[1]; s[2] = fl.s[2];
     }
     float dmx = 0.f, dmy = 0.f, dmz = 0.f, dop = 0.f;
-    float dsa[3] = {0.f, 0.f, 0.f};  // d loss / d (projected) scales, all views
-    float4 dqa = make_float4(0.f, 0.f, 0.f, 0.f);
+    // the views' symmetrised covariance gradients, carried to the scales and
+    // the quaternion once after the loop (that part is linear in them)
+    float dSym[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const CovFrame F = cov_frame(q4, s);
     bool any = false;
     for (int v = 0; v < n_views; ++v) {
         const int64_t o = (int64_t)v * view_stride + g;
@@ -421,19 +456,16 @@ preprocess_backward_views_kernel(const float* __restrict__ means,
         dpre[3 * o + 1] = color[3 * o + 1] > 0.f ? r[MG_G2D_COLOR + 1] : 0.f;
         dpre[3 * o + 2] = color[3 * o + 2] > 0.f ? r[MG_G2D_COLOR + 2] : 0.f;
         if (valid[o] == 0) continue;
-        float ds[3];
-        float4 dq;
-        projection_adjoint(cams.c[v], mx, my, mz, q4, s, r[MG_G2D_UV], r[MG_G2D_UV + 1],
-                           r[MG_G2D_CONIC], r[MG_G2D_CONIC + 1], r[MG_G2D_CONIC + 2], dmx, dmy,
-                           dmz, ds, dq);
-        dsa[0] += ds[0];
-        dsa[1] += ds[1];
-        dsa[2] += ds[2];
+        projection_adjoint_view(cams.c[v], mx, my, mz, F.S, r[MG_G2D_UV], r[MG_G2D_UV + 1],
+                                r[MG_G2D_CONIC], r[MG_G2D_CONIC + 1], r[MG_G2D_CONIC + 2], dmx,
+                                dmy, dmz, dSym);
         dop += r[MG_G2D_OPACITY];
-        dqa = make_float4(dqa.x + dq.x, dqa.y + dq.y, dqa.z + dq.z, dqa.w + dq.w);
         any = true;
     }
     if (!any) return;
+    float dsa[3];  // d loss / d (projected) scales, all views
+    float4 dqa;
+    covariance_adjoint(F, s, dSym, dsa, dqa);
     // activation chain: d log s = d s * s, d logit = d op * op (1 - op), through
     // the 3D filter when there is one (s' = sqrt(s^2 + f^2), op' = op coef)
     float dls[3], dl;

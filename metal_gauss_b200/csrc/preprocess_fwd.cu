@@ -158,13 +158,13 @@ preprocess_forward_views_kernel(const float* __restrict__ means,
     const bool colour = sh_degree >= 0 && sh_dc != nullptr;
     const int nb = (sh_degree + 1) * (sh_degree + 1);
 
-    float mx = 0.f, my = 0.f, mz = 0.f, sx = 0.f, sy = 0.f, sz = 0.f, op = 0.f;
-    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+    float mx = 0.f, my = 0.f, mz = 0.f;
+    GaussianCov gc{};  // view-independent: computed once for every view
     if (in) {
         mx = means[3 * g + 0]; my = means[3 * g + 1]; mz = means[3 * g + 2];
-        q = __ldg(reinterpret_cast<const float4*>(quats) + g);
-        sx = scales[3 * g + 0]; sy = scales[3 * g + 1]; sz = scales[3 * g + 2];
-        op = opacities[g];
+        const float4 q = __ldg(reinterpret_cast<const float4*>(quats) + g);
+        gc = gaussian_cov(q.x, q.y, q.z, q.w, scales[3 * g + 0], scales[3 * g + 1],
+                          scales[3 * g + 2], opacities[g]);
     }
     bool staged = false;  // warp-uniform: the SH rows are staged at first use
     int visible = 0;
@@ -174,7 +174,7 @@ preprocess_forward_views_kernel(const float* __restrict__ means,
         Projected pr;
         pr.ok = false;
         if (in) {
-            pr = project_one(P, mx, my, mz, q.x, q.y, q.z, q.w, sx, sy, sz, op);
+            pr = project_with(P, mx, my, mz, gc);
             out_uv[o] = make_float2(pr.u, pr.v);
             out_conic[3 * o + 0] = pr.ca;
             out_conic[3 * o + 1] = pr.cb;
