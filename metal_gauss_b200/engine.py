@@ -132,8 +132,11 @@ class _BatchBinning:
         self.bases: list[int] = []
 
     @staticmethod
-    def fits(views) -> bool:
-        return 1 < len(views) <= 64 and len({(v.width, v.height) for v in views}) == 1
+    def fits(views, n: int) -> bool:
+        """Whether views of n Gaussians each can be binned as one batch: 2..64
+        views of one frame size, fewer than 2^31 (Gaussian, view) rows."""
+        return (1 < len(views) <= 64 and len(views) * n < 2 ** 31 and
+                len({(v.width, v.height) for v in views}) == 1)
 
     def prepare(self, batch: "_ViewBatch", first: int, V: int, n: int, W: int, H: int, tile: int,
                 cut: int, opac: torch.Tensor, opac_stride: int) -> None:
@@ -530,7 +533,7 @@ class Trainer:
         that holds their lists; otherwise each view's stage A ran into its
         own state and its pairs are emitted in phase B."""
         V = len(chunk)
-        if self.batch_binning and _BatchBinning.fits(chunk):
+        if self.batch_binning and _BatchBinning.fits(chunk, self.active):
             while len(self._bbs) <= c:
                 self._bbs.append(_BatchBinning(self.device))
             bb = self._bbs[c]

@@ -129,7 +129,7 @@ class Renderer:
         V = len(views)
         opac_all, opac_stride = (self._opac_view, n) if self.antialias else (self.opac, 0)
         totals = None
-        if self.batch_binning and _BatchBinning.fits(views):
+        if self.batch_binning and _BatchBinning.fits(views, n):
             W, H = views[0].width, views[0].height
             self._bb.prepare(self._batch, 0, V, n, W, H, self.tile, self.saturation_cut,
                              opac_all, opac_stride)

@@ -190,3 +190,21 @@ def test_renderer_batch_binning_changes_nothing(cuda):
         outs.append(r.render(views))
     for (ra, aa), (rb, ab) in zip(*outs):
         assert torch.equal(ra, rb) and torch.equal(aa, ab)
+
+
+def test_trainer_mixed_frame_sizes_bin_view_by_view(cuda):
+    """Views of two sizes in one step: no batch binning (one frame size per
+    batch), per-size frame buffers on the streams; the same results as one
+    view at a time on one stream."""
+    p, _, _ = scenes.config("cfg3", n=N_G, seed=12)
+    views = (scenes.sphere_views(3, 4.0, W, H, 40.0, 13, hemisphere=True) +
+             scenes.sphere_views(2, 4.0, 96, 64, 40.0, 14, hemisphere=True))
+    g = torch.Generator().manual_seed(2)
+    targets = [torch.rand(v.height, v.width, 3, generator=g).cuda() for v in views]
+    a, sa = _trainer_run(p, views, targets, True, 4, 0)
+    b, sb = _trainer_run(p, views, targets, False, 1, 0)
+    assert [s.pairs for s in sa] == [s.pairs for s in sb]
+    assert not a._bbs  # never batch-binned
+    assert float(a.loss.sum()) == pytest.approx(float(b.loss.sum()), rel=1e-6)
+    for name in ("means", "quats", "log_scales", "logit_opac", "sh_dc", "sh_rest"):
+        assert rel_l2(a.grad(name).cpu().numpy(), b.grad(name).cpu().numpy()) < 1e-5, name
