@@ -59,7 +59,10 @@ namespace {
 constexpr int kSeg = MG_RASTER_SEGMENT;
 static_assert(kSeg % 32 == 0 && (kSeg & (kSeg - 1)) == 0,
               "segments are a power of two number of whole chunks");
-constexpr int kRasterWarps = 4;  // warps per CTA of the persistent kernels
+#ifndef MG_RASTER_WARPS
+#define MG_RASTER_WARPS 4
+#endif
+constexpr int kRasterWarps = MG_RASTER_WARPS;  // warps per CTA of the persistent kernels
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
