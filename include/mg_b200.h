@@ -486,6 +486,17 @@ mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
                         const float* visible_count, float* steps, int64_t step,
                         float* row_scratch, mg_stream_t stream);
 
+/* The MCMC regularisers of the reference's training loss (train.py:393-398):
+ *   loss += c_opac * mean(sigmoid(logit_opac[:n])) + c_scale * mean(exp(log_scales[:n, 0..2]))
+ * where the caller folds the weights (--opac-reg / --scale-reg, 0.01 each) and
+ * the ramp aux = max(0, 1 - step / (0.9 steps)) into c_*. ADDS
+ * c_opac / n * s (1 - s) to d_logit[i] and c_scale / (3 n) * exp(log_scales)
+ * to d_log_scales[i, j], and the loss value to *loss_dev. scratch: 16 bytes. */
+mg_status mg_regularizer_grad(const float* logit_opac, const float* log_scales, int64_t n,
+                              float c_opac, float c_scale, float* d_logit,
+                              float* d_log_scales, float* loss_dev, void* scratch,
+                              size_t scratch_bytes, mg_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* SSIM (11-tap separable Gaussian, zero padding) and the training loss     */
 /* ------------------------------------------------------------------------ */

@@ -307,3 +307,79 @@ extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
     }
     return MG_OK;
 }
+
+// ------------------------------------------------ training-loss regularisers
+//
+// The MCMC regularisers of the reference's training loss (train.py:393-398):
+//   loss += c_opac * mean(sigmoid(logit_opac[:n])) + c_scale * mean(exp(log_scales[:n]))
+// (the caller folds the ramp aux = max(0, 1 - step / (0.9 steps)) and the
+// weights into c_*). One pass over the rows adds the gradients into the
+// parameter gradient rows and the value into the loss word.
+namespace mg {
+namespace {
+
+__global__ void __launch_bounds__(256)
+regularizer_kernel(const float* __restrict__ logit, const float* __restrict__ log_scales,
+                   int64_t n, float k_opac, float k_scale, float* __restrict__ d_logit,
+                   float* __restrict__ d_log_scales, double* __restrict__ sums) {
+    double so = 0.0, ss = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float s = 1.0f / (1.0f + expf(-logit[i]));
+        so += s;
+        if (k_opac != 0.0f) d_logit[i] += k_opac * (s * (1.0f - s));
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const float e = expf(log_scales[3 * i + j]);
+            ss += e;
+            if (k_scale != 0.0f) d_log_scales[3 * i + j] += k_scale * e;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        so += __shfl_xor_sync(0xffffffffu, so, o);
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    __shared__ double s_o[8], s_s[8];
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { s_o[warp] = so; s_s[warp] = ss; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) { so += s_o[w]; ss += s_s[w]; }
+        atomicAdd(&sums[0], so);
+        atomicAdd(&sums[1], ss);
+    }
+}
+
+__global__ void regularizer_finish_kernel(const double* __restrict__ sums, int64_t n,
+                                          float c_opac, float c_scale, float* __restrict__ loss) {
+    *loss += (float)((double)c_opac * sums[0] / (double)n +
+                     (double)c_scale * sums[1] / (3.0 * (double)n));
+}
+
+}  // namespace
+}  // namespace mg
+
+extern "C" mg_status mg_regularizer_grad(const float* logit_opac, const float* log_scales,
+                                         int64_t n, float c_opac, float c_scale, float* d_logit,
+                                         float* d_log_scales, float* loss_dev, void* scratch,
+                                         size_t scratch_bytes, mg_stream_t stream) {
+    using namespace mg;
+    MG_REQUIRE(n >= 0, "regularizer_grad: negative count");
+    if (n == 0) return MG_OK;
+    MG_REQUIRE(logit_opac && log_scales && d_logit && d_log_scales && loss_dev,
+               "regularizer_grad: null pointer");
+    MG_REQUIRE(scratch && scratch_bytes >= 2 * sizeof(double),
+               "regularizer_grad: scratch too small");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    double* sums = static_cast<double*>(scratch);
+    if (cudaMemsetAsync(sums, 0, 2 * sizeof(double), st) != cudaSuccess)
+        return check_launch("regularizer_grad memset");
+    const float k_opac = (float)((double)c_opac / (double)n);
+    const float k_scale = (float)((double)c_scale / (3.0 * (double)n));
+    regularizer_kernel<<<(int)std::min<int64_t>(ceil_div(n, 256), 148 * 8), 256, 0, st>>>(
+        logit_opac, log_scales, n, k_opac, k_scale, d_logit, d_log_scales, sums);
+    MG_TRY(check_launch("regularizer_grad"));
+    regularizer_finish_kernel<<<1, 1, 0, st>>>(sums, n, c_opac, c_scale, loss_dev);
+    return check_launch("regularizer_grad finish");
+}

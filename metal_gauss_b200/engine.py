@@ -212,7 +212,7 @@ class Trainer:
                  w_ssim: float = 0.2, selective: bool = True, near: float = 0.01,
                  far: float = 100.0, max_radius_frac: float = 1.0, group=None,
                  betas=(0.9, 0.999), eps: float = 1e-15, shard_optimizer: bool | None = None,
-                 saturation_cut: bool = True):
+                 saturation_cut: bool = True, opac_reg: float = 0.0, scale_reg: float = 0.0):
         self.device = torch.device(device)
         self.n = n = int(params["means"].shape[0])
         # rows < active are rendered and densified (3DGS-MCMC grows it toward
@@ -232,6 +232,11 @@ class Trainer:
         # bin a step's views of one frame size together (one depth sort and
         # one tile sort for all of them); False bins them one at a time
         self.batch_binning = True
+        # the MCMC regularisers of the training loss (train.py:393-398):
+        # reg_weight * (opac_reg * mean(opacity) + scale_reg * mean(scale)) over
+        # the active rows; fit() ramps reg_weight down as the reference does
+        self.opac_reg, self.scale_reg = float(opac_reg), float(scale_reg)
+        self.reg_weight = 1.0
         # phase B's per-view chains (pack, raster forward, loss, raster
         # backward) run on this many streams, each with its own frame
         # buffers, so one view's raster tail overlaps the next view's work
@@ -241,6 +246,7 @@ class Trainer:
         # chunk's rendering on the streams overlaps the binning of the next
         self.bin_chunk = 0
         self._bin_stream = None
+        self._reg_scratch = None
         self.n_pad = -(-n // self.world) * self.world if self.shard_optimizer else n
         self.sh_degree, self.tile = sh_degree, tile
         self.background = None if background is None or all(b == 0 for b in background) \
@@ -761,6 +767,8 @@ class Trainer:
         self.G[self.vis_offset:].zero_()  # visibility counts and the loss
         self._end(ev)
         self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb)
+        if self.opac_reg or self.scale_reg:
+            self._regularize(world)
         if world > 1 and self.shard_optimizer:
             ev = self._begin("reduce_scatter")
             dp.all_reduce_(self.G[self.vis_offset:], self.group)     # visibility + loss
@@ -777,6 +785,18 @@ class Trainer:
             self._end(ev)
         self.optimizer_step()
         return self.loss
+
+    def _regularize(self, world: int) -> None:
+        """The MCMC regularisers (train.py:393-398) over the active rows: their
+        gradient added into G and their value into the loss, a 1/world share
+        on each rank (the ranks' gradients and losses are summed)."""
+        if self._reg_scratch is None:
+            self._reg_scratch = torch.empty(16, dtype=torch.uint8, device=self.device)
+        w = self.reg_weight / world
+        _lib.call("mg_regularizer_grad", ptr(self.param("logit_opac")),
+                  ptr(self.param("log_scales")), self.active, w * self.opac_reg,
+                  w * self.scale_reg, ptr(self.grad("logit_opac")), ptr(self.grad("log_scales")),
+                  ptr(self.loss), ptr(self._reg_scratch), 16, _lib.stream())
 
     def _world_size(self) -> int:
         return dp.world_size(self.group)
@@ -822,15 +842,17 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
         lr_means_end: float | None = None, sh_warmup: int = 0, filter_3d_every: int = 0,
         noise_weight: float = 0.0, relocate_every: int = 0, relocate_until: int | None = None,
         grow_to: int | None = None, grow_until: int | None = None,
-        callback=None) -> list[float]:
+        opac_reg: float = 0.01, scale_reg: float = 0.01, callback=None) -> list[float]:
     """The reference's training loop (train.py:311-366) over batches of views.
 
     Views are drawn in epoch permutations (numpy's default_rng(seed), a new
     permutation whenever one is used up), `batch` per step; the means learning
     rate decays geometrically from its initial value to `lr_means_end` over
     `steps`; with `sh_warmup`, the SH degree grows by one band every
-    `sh_warmup` steps up to 3. Densification, the appearance model and the
-    opacity/scale regularisers are not part of this loop. With
+    `sh_warmup` steps up to 3. The appearance model is not part of this loop.
+    The loss carries the reference's MCMC regularisers, `opac_reg` * mean opacity +
+    `scale_reg` * mean scale over the active rows, ramped down by max(0, 1 -
+    step / (0.9 steps)) (train.py:393-398; 0 turns them off). With
     `filter_3d_every`, Mip-Splatting's 3D filter is computed from all `views`
     before the first step and again every that many steps (train.py:343-380).
     3DGS-MCMC as train.py:416-462 runs it: with `noise_weight`, the
@@ -850,6 +872,7 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
     decay = 1.0 if lr_means_end is None else (lr_means_end / max(lr0, 1e-12)) ** (1.0 / steps)
     rank_views = dp.shard(list(range(batch)), trainer.rank, trainer.world)
     start_active = trainer.active
+    trainer.opac_reg, trainer.scale_reg = float(opac_reg), float(scale_reg)
     losses = []
     for step in range(1, steps + 1):
         idx = []
@@ -860,6 +883,7 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
             idx.append(int(order[oi]))
             oi += 1
         trainer.lrs["means"] = lr0 * decay ** step
+        trainer.reg_weight = max(0.0, 1.0 - step / (0.9 * steps))
         trainer.sh_degree = min(3, step // sh_warmup) if sh_warmup else 3
         if filter_3d_every and (step == 1 or step % filter_3d_every == 0):
             trainer.compute_filter_3d(views)
