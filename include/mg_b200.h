@@ -398,6 +398,21 @@ mg_status mg_antialias_opacity_backward(const float* conic, const float* opacity
                                         const float* grad_out, int64_t n, float blur,
                                         float* d_conic, float* d_opacity, mg_stream_t stream);
 
+/* The training engine's forms for a batch of views (no reference
+ * counterpart; the reference applies the compensation per render call):
+ * view v's conics, outputs and gradient records at rows v * view_stride,
+ * the opacities shared. mg_antialias_opacity_views writes the compensated
+ * opacities; mg_antialias_grad2d_views applies the adjoint IN PLACE to
+ * gradient records (MG_G2D_*): d opacity against the compensated opacity
+ * becomes d opacity against `opacity`, and the compensation's conic term is
+ * added to d conic. */
+mg_status mg_antialias_opacity_views(const float* conic, const float* opacity, int64_t n,
+                                     int32_t n_views, int64_t view_stride, float blur,
+                                     float* out, mg_stream_t stream);
+mg_status mg_antialias_grad2d_views(const float* conic, const float* opacity, int64_t n,
+                                    int32_t n_views, int64_t view_stride, float blur,
+                                    float* grad2d, mg_stream_t stream);
+
 /* Replaces rasterize_backward (rasterize.mm:147-194; rasterize.metal:
  * 173-340). grad2d (N, MG_G2D_STRIDE) is ACCUMULATED into (zero it first for
  * a fresh gradient). background as in the forward: the blend's adjoint is

@@ -88,6 +88,8 @@ SIGNATURES = {
     "mg_bin_prepare_scratch_bytes": (sz, [i64, i32]),
     "mg_bin_prepare": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, vp, vp, sz, vp]),
     "mg_regularizer_grad": (i32, [vp, vp, i64, f32, f32, vp, vp, vp, vp, sz, vp]),
+    "mg_antialias_opacity_views": (i32, [vp, vp, i64, i32, i64, f32, vp, vp]),
+    "mg_antialias_grad2d_views": (i32, [vp, vp, i64, i32, i64, f32, vp, vp]),
     "mg_bin_prepare_views_scratch_bytes": (sz, [i64, i32, i32]),
     "mg_bin_prepare_views": (i32, [vp, vp, vp, vp, vp, vp, i64, i32, i64, i64, i32, i32, i32,
                                    i32, vp, vp, sz, vp]),

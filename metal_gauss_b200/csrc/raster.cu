@@ -834,16 +834,31 @@ __global__ void pack_intersections_kernel(const float2* __restrict__ uv,
 // Mip-Splatting opacity compensation (metal_backend.py:367-393): the 2D
 // covariance before the 0.3 px blur, recovered from the blurred conic, gives
 // op * sqrt(clamp(det_before / det_after, 0, 1)).
+__device__ __forceinline__ float antialias_factor(float cxx, float cxy, float cyy, float blur) {
+    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
+    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
+    const float det_before = (a - blur) * (c - blur) - b * b;
+    return sqrtf(fminf(fmaxf(det_before, 0.0f) / det_after, 1.0f));
+}
+
 __global__ void antialias_opacity_kernel(const float* __restrict__ conic,
                                          const float* __restrict__ opacity, int64_t n,
                                          float blur, float* __restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const float cxx = conic[3 * i], cxy = conic[3 * i + 1], cyy = conic[3 * i + 2];
-    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
-    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
-    const float det_before = (a - blur) * (c - blur) - b * b;
-    out[i] = opacity[i] * sqrtf(fminf(fmaxf(det_before, 0.0f) / det_after, 1.0f));
+    out[i] = opacity[i] * antialias_factor(conic[3 * i], conic[3 * i + 1], conic[3 * i + 2], blur);
+}
+
+// The same for a batch of views (blockIdx.y): view v's conics and outputs at
+// rows v * view_stride, the opacities shared.
+__global__ void antialias_opacity_views_kernel(const float* __restrict__ conic,
+                                               const float* __restrict__ opacity, int64_t n,
+                                               int64_t view_stride, float blur,
+                                               float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t o = (int64_t)blockIdx.y * view_stride + i;
+    out[o] = opacity[i] * antialias_factor(conic[3 * o], conic[3 * o + 1], conic[3 * o + 2], blur);
 }
 
 // Adjoint of antialias_opacity_kernel. With beta the blur, the ratio
@@ -851,6 +866,27 @@ __global__ void antialias_opacity_kernel(const float* __restrict__ conic,
 // (the blurred covariance is the conic's inverse), so with
 // k = sqrt(clamp(ratio, 0, 1)): d op = g k and, where 0 < ratio < 1,
 // d conic = g op / (2 k) * d ratio / d conic.
+// d out -> (d conic, d opacity) of one Gaussian (conic c, opacity op).
+struct AntialiasAdjoint {
+    float d_op, dxx, dxy, dyy;
+};
+__device__ __forceinline__ AntialiasAdjoint antialias_adjoint(float cxx, float cxy, float cyy,
+                                                              float op, float g, float blur) {
+    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
+    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
+    const float ratio = ((a - blur) * (c - blur) - b * b) / det_after;
+    const float k = sqrtf(fminf(fmaxf(ratio, 0.0f), 1.0f));
+    AntialiasAdjoint r{g * k, 0.0f, 0.0f, 0.0f};
+    if (ratio > 0.0f && ratio < 1.0f) {
+        const float h = g * op / (2.0f * k);
+        const float b2 = blur * blur;
+        r.dxx = h * (b2 * cyy - blur);
+        r.dyy = h * (b2 * cxx - blur);
+        r.dxy = h * (-2.0f * b2 * cxy);
+    }
+    return r;
+}
+
 __global__ void antialias_opacity_backward_kernel(const float* __restrict__ conic,
                                                   const float* __restrict__ opacity,
                                                   const float* __restrict__ grad_out, int64_t n,
@@ -858,24 +894,35 @@ __global__ void antialias_opacity_backward_kernel(const float* __restrict__ coni
                                                   float* __restrict__ d_opacity) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const float cxx = conic[3 * i], cxy = conic[3 * i + 1], cyy = conic[3 * i + 2];
-    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
-    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
-    const float ratio = ((a - blur) * (c - blur) - b * b) / det_after;
-    const float k = sqrtf(fminf(fmaxf(ratio, 0.0f), 1.0f));
-    const float g = grad_out[i];
-    d_opacity[i] = g * k;
-    float dxx = 0.0f, dxy = 0.0f, dyy = 0.0f;
-    if (ratio > 0.0f && ratio < 1.0f) {
-        const float h = g * opacity[i] / (2.0f * k);
-        const float b2 = blur * blur;
-        dxx = h * (b2 * cyy - blur);
-        dyy = h * (b2 * cxx - blur);
-        dxy = h * (-2.0f * b2 * cxy);
-    }
-    d_conic[3 * i] = dxx;
-    d_conic[3 * i + 1] = dxy;
-    d_conic[3 * i + 2] = dyy;
+    const AntialiasAdjoint r = antialias_adjoint(conic[3 * i], conic[3 * i + 1],
+                                                 conic[3 * i + 2], opacity[i], grad_out[i], blur);
+    d_opacity[i] = r.d_op;
+    d_conic[3 * i] = r.dxx;
+    d_conic[3 * i + 1] = r.dxy;
+    d_conic[3 * i + 2] = r.dyy;
+}
+
+// The adjoint in place on a batch of views' gradient records (MG_G2D_*,
+// view v's conics and records at rows v * view_stride): the record's d
+// opacity, taken against the compensated opacity, becomes the one against
+// the opacity before compensation, and the compensation's conic term is
+// added to its d conic.
+__global__ void antialias_grad2d_views_kernel(const float* __restrict__ conic,
+                                              const float* __restrict__ opacity, int64_t n,
+                                              int64_t view_stride, float blur,
+                                              float* __restrict__ grad2d) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t o = (int64_t)blockIdx.y * view_stride + i;
+    float* rec = grad2d + o * MG_G2D_STRIDE;
+    const float g = rec[MG_G2D_OPACITY];
+    if (g == 0.0f) return;  // no pixel took it: nothing to carry
+    const AntialiasAdjoint r = antialias_adjoint(conic[3 * o], conic[3 * o + 1],
+                                                 conic[3 * o + 2], opacity[i], g, blur);
+    rec[MG_G2D_OPACITY] = r.d_op;
+    rec[MG_G2D_CONIC] += r.dxx;
+    rec[MG_G2D_CONIC + 1] += r.dxy;
+    rec[MG_G2D_CONIC + 2] += r.dyy;
 }
 
 // ---------------------------------------------------------------- host side
@@ -1141,6 +1188,32 @@ extern "C" mg_status mg_antialias_opacity(const float* conic, const float* opaci
     antialias_opacity_kernel<<<ceil_div(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         conic, opacity, n, blur, out);
     return check_launch("antialias_opacity");
+}
+
+extern "C" mg_status mg_antialias_opacity_views(const float* conic, const float* opacity,
+                                                int64_t n, int32_t n_views, int64_t view_stride,
+                                                float blur, float* out, mg_stream_t stream) {
+    MG_REQUIRE(n >= 0 && n_views >= 0 && n_views <= 65535, "antialias_opacity_views: bad counts");
+    MG_REQUIRE(view_stride >= n, "antialias_opacity_views: view_stride below n");
+    if (n == 0 || n_views == 0) return MG_OK;
+    MG_REQUIRE(conic && opacity && out, "antialias_opacity_views: null pointer");
+    antialias_opacity_views_kernel<<<dim3((unsigned)ceil_div(n, 256), (unsigned)n_views), 256, 0,
+                                     reinterpret_cast<cudaStream_t>(stream)>>>(
+        conic, opacity, n, view_stride, blur, out);
+    return check_launch("antialias_opacity_views");
+}
+
+extern "C" mg_status mg_antialias_grad2d_views(const float* conic, const float* opacity,
+                                               int64_t n, int32_t n_views, int64_t view_stride,
+                                               float blur, float* grad2d, mg_stream_t stream) {
+    MG_REQUIRE(n >= 0 && n_views >= 0 && n_views <= 65535, "antialias_grad2d_views: bad counts");
+    MG_REQUIRE(view_stride >= n, "antialias_grad2d_views: view_stride below n");
+    if (n == 0 || n_views == 0) return MG_OK;
+    MG_REQUIRE(conic && opacity && grad2d, "antialias_grad2d_views: null pointer");
+    antialias_grad2d_views_kernel<<<dim3((unsigned)ceil_div(n, 256), (unsigned)n_views), 256, 0,
+                                    reinterpret_cast<cudaStream_t>(stream)>>>(
+        conic, opacity, n, view_stride, blur, grad2d);
+    return check_launch("antialias_grad2d_views");
 }
 
 extern "C" mg_status mg_antialias_opacity_backward(const float* conic, const float* opacity,

@@ -80,9 +80,12 @@ class _ViewBatch:
     belongs to Gaussian g in view v, so one multi-view launch fills or reads
     every view of a batch."""
 
-    def __init__(self, n: int, cap: int, device, grads: bool = True):
+    def __init__(self, n: int, cap: int, device, grads: bool = True,
+                 per_view_opacity: bool = False):
         f32 = dict(dtype=torch.float32, device=device)
         self.n, self.cap = n, cap
+        # antialiased training: each view's compensated opacities
+        self.opac = torch.empty(cap, n, **f32) if per_view_opacity else None
         self.uv = torch.empty(cap, n, 2, **f32)
         self.conic = torch.empty(cap, n, 3, **f32)
         self.depth = torch.empty(cap, n, **f32)
@@ -103,6 +106,7 @@ class _ViewState:
         self.bind(batch, v)
 
     def bind(self, batch: _ViewBatch, v: int) -> None:
+        self.opac = None if batch.opac is None else batch.opac[v]
         self.uv, self.conic, self.depth = batch.uv[v], batch.conic[v], batch.depth[v]
         self.rxy, self.valid, self.color = batch.rxy[v], batch.valid[v], batch.color[v]
         self.grad2d = None if batch.grad2d is None else batch.grad2d[v]
@@ -212,7 +216,8 @@ class Trainer:
                  w_ssim: float = 0.2, selective: bool = True, near: float = 0.01,
                  far: float = 100.0, max_radius_frac: float = 1.0, group=None,
                  betas=(0.9, 0.999), eps: float = 1e-15, shard_optimizer: bool | None = None,
-                 saturation_cut: bool = True, opac_reg: float = 0.0, scale_reg: float = 0.0):
+                 saturation_cut: bool = True, opac_reg: float = 0.0, scale_reg: float = 0.0,
+                 antialias: bool = False):
         self.device = torch.device(device)
         self.n = n = int(params["means"].shape[0])
         # rows < active are rendered and densified (3DGS-MCMC grows it toward
@@ -237,6 +242,11 @@ class Trainer:
         # the active rows; fit() ramps reg_weight down as the reference does
         self.opac_reg, self.scale_reg = float(opac_reg), float(scale_reg)
         self.reg_weight = 1.0
+        # Mip-Splatting's 2D antialias compensation (train.py --antialias,
+        # metal_backend.py:506-511): each view draws with its compensated
+        # opacities, and their adjoint is applied to the views' gradient
+        # records before the projection adjoint
+        self.antialias = bool(antialias)
         # phase B's per-view chains (pack, raster forward, loss, raster
         # backward) run on this many streams, each with its own frame
         # buffers, so one view's raster tail overlaps the next view's work
@@ -507,8 +517,9 @@ class Trainer:
 
     def _ensure_views(self, V: int) -> None:
         """View-major buffers for V views (grown, never shrunk)."""
-        if self._batch is None or self._batch.cap < V:
-            self._batch = _ViewBatch(self.n, V, self.device)
+        if (self._batch is None or self._batch.cap < V or
+                (self._batch.opac is None) == self.antialias):
+            self._batch = _ViewBatch(self.n, V, self.device, per_view_opacity=self.antialias)
             for v, st in enumerate(self._states):
                 st.bind(self._batch, v)
         while len(self._states) < V:
@@ -531,7 +542,19 @@ class Trainer:
                   self.n,
                   ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color),
                   ptr(self.visibility_count()), _lib.stream())
+        if self.antialias:
+            _lib.call("mg_antialias_opacity_views", ptr(b.conic), ptr(self.opac), self.active,
+                      len(views), self.n, 0.3, ptr(b.opac), _lib.stream())
         self._end(ev)
+
+    def _view_opacities(self) -> tuple[torch.Tensor, int]:
+        """The opacities the views draw with and their view stride (0: shared)."""
+        if self.antialias:
+            return self._batch.opac, self._batch.n
+        return self.opac, 0
+
+    def _opacity(self, st: "_ViewState") -> torch.Tensor:
+        return st.opac if self.antialias else self.opac
 
     def _bin_chunk(self, c: int, first: int, chunk) -> tuple[list[int], "_BatchBinning | None"]:
         """Phase A, second half, for views first.. of a chunk: their pair
@@ -545,14 +568,15 @@ class Trainer:
             bb = self._bbs[c]
             W, H = chunk[0].width, chunk[0].height
             ev = self._begin("bin_prepare")
+            op, op_stride = self._view_opacities()
             bb.prepare(self._batch, first, V, self.active, W, H, self.tile, self.saturation_cut,
-                       self.opac, 0)
+                       op, op_stride)
             self._end(ev)
             totals = bb.read_totals(V)
             if totals is not None:
                 ev = self._begin("bin_emit")
                 bb.emit_all(self._batch, V, self.active, W, H, self.tile, self.saturation_cut,
-                            self.opac, 0, sum(totals))
+                            op, op_stride, sum(totals))
                 self._end(ev)
                 return totals, bb
         for i, view in enumerate(chunk):
@@ -568,7 +592,8 @@ class Trainer:
         ev = self._begin("bin_prepare")
         prep = st.prep_scratch(-(-view.width // self.tile) * -(-view.height // self.tile))
         _lib.check(L.mg_bin_prepare(
-            ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), ptr(st.valid), ptr(st.depth),
+            ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self._opacity(st)), ptr(st.valid),
+            ptr(st.depth),
             self.active, view.width, view.height, self.tile, self.saturation_cut,
             ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(), s), "bin_prepare")
         self._end(ev)
@@ -607,16 +632,18 @@ class Trainer:
                 b.emit = torch.empty(int(ebytes * 1.25) + 256, dtype=torch.uint8,
                                      device=self.device)
             ev = self._begin("bin_emit")
-            _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic), ptr(self.opac), n,
-                                     m, W, H, self.tile, self.saturation_cut, ptr(st.prep),
-                                     ptr(b.ids), ptr(b.offsets), ptr(b.emit), b.emit.numel(), s),
+            _lib.check(L.mg_bin_emit(ptr(st.uv), ptr(st.rxy), ptr(st.conic),
+                                     ptr(self._opacity(st)), n, m, W, H, self.tile,
+                                     self.saturation_cut, ptr(st.prep), ptr(b.ids),
+                                     ptr(b.offsets), ptr(b.emit), b.emit.numel(), s),
                        "bin_emit")
             self._end(ev)
             ids, offsets = b.ids, b.offsets
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
         ev = self._begin("pack")
-        _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(self.opac), ptr(st.color), n,
+        _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(self._opacity(st)),
+                                    ptr(st.color), n,
                                     ptr(b.splats), s), "pack_splats")
         self._end(ev)
         # tile walk lengths only when the instrumented pass asks for them
@@ -699,6 +726,9 @@ class Trainer:
         b = self._batch
         cams = _views_array([self._camera(view) for view in views])
         ev = self._begin("preprocess_bwd")
+        if self.antialias:  # the compensation's adjoint on every view's records
+            _lib.call("mg_antialias_grad2d_views", ptr(b.conic), ptr(self.opac), self.active, V,
+                      self.n, 0.3, ptr(b.grad2d), _lib.stream())
         filt = self.filter_3d
         _lib.call("mg_preprocess_backward_views", ptr(self.param("means")),
                   ptr(self.param("quats")), ptr(self.scales if filt is None else self._scales_act),

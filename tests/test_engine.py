@@ -145,3 +145,36 @@ def test_fit_runs_the_reference_loop_over_batches(cuda):
     assert losses[-1] < losses[0]
     assert [d for _, d, _ in seen] == [0, 1, 1, 2, 2, 3]
     assert abs(seen[-1][2] - 1e-4) < 1e-9
+
+
+def test_engine_antialias_matches_the_drop_in_path(cuda):
+    """Training with the antialias compensation (train.py --antialias): the
+    engine's batched step against the drop-in render
+    (cuda_backend.render(antialias=True), whose compensation and adjoint are
+    checked against the reference's antialias_scale expression) with torch
+    autograd through the same activations and loss."""
+    from metal_gauss_b200 import cuda_backend
+    from metal_gauss_b200.ssim import l1_ssim_loss
+    p, views, targets = _setup(9)
+    views, targets = views[:2], [torch.from_numpy(t).cuda() for t in targets[:2]]
+    tr = Trainer(p, cuda, sh_degree=3, antialias=True)
+    tr._activate()
+    tr.forward_backward_views(views, targets, 0.5)
+    torch.cuda.synchronize()
+    leaf = {k: v.detach().clone().float().cuda().requires_grad_(True) for k, v in p.items()}
+    total = 0.0
+    for v, t in zip(views, targets):
+        rgb, _, _ = cuda_backend.render(leaf["means"], leaf["quats"], torch.exp(leaf["log_scales"]),
+                                        torch.sigmoid(leaf["logit_opac"]), leaf["sh_dc"], v.K,
+                                        v.viewmat, W, H, sh_degree=3, sh_rest=leaf["sh_rest"],
+                                        antialias=True)
+        total = total + 0.5 * l1_ssim_loss(rgb, t)
+    total.backward()
+    assert abs(float(tr.loss) - float(total.detach())) < 1e-5
+    for name, _ in SEGMENTS:
+        assert rel_l2(tr.grad(name).cpu().numpy(), leaf[name].grad.cpu().numpy()) < 1e-3, name
+    # the compensation changes the result
+    plain = Trainer(p, cuda, sh_degree=3)
+    plain._activate()
+    plain.forward_backward_views(views, targets, 0.5)
+    assert abs(float(plain.loss) - float(tr.loss)) > 1e-6
