@@ -3,14 +3,13 @@
 The reference's viewer and camera-path renderer call `render` under
 `torch.no_grad()` view after view (viewer.py:477-485, render_path.py:
 440-456). This renderer keeps the Gaussians resident in the form the kernels
-read; per batch of views it projects and colours every view in one launch,
-and per view it runs the antialias opacity compensation when asked for
-(metal_backend.py:506-511), the binning
-with the saturation cut, the packing and a forward-only rasterisation that
-writes no transmittance, stop indices or checkpoints and keeps no autograd
-state. Views are processed in batches with one host read per batch (the pair
-totals of all its views); a batch of one frame size is binned with one call
-per binning stage for all its views.
+read. Per batch of views it projects and colours every view in one launch,
+runs the antialias opacity compensation of every view in one more when asked
+for (metal_backend.py:506-511), and bins the views with the saturation cut
+(one call per binning stage for all views of one frame size, one host read
+per batch for the pair totals); then per view, on four streams in turn, it
+packs the splats and runs a forward-only rasterisation that writes no
+transmittance, stop indices or checkpoints and keeps no autograd state.
 """
 
 from __future__ import annotations
@@ -119,14 +118,14 @@ class Renderer:
             ptr(self.sh_rest), _lib.SH_SPLIT, ptr(self.opac), _lib.C.cast(cams, _lib.C.c_void_p),
             len(views), self.sh_degree, n, n, ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy),
             ptr(b.valid), ptr(b.color), None, s), "preprocess_forward_views")
-        for v, view in enumerate(views):
-            if self.antialias:
-                # before binning, as the reference does: the exact tile test
-                # then uses the opacity that is composited
-                _lib.check(L.mg_antialias_opacity(ptr(self._state(v).conic), ptr(self.opac), n,
-                                                  0.3, ptr(self._opacity(v)), s),
-                           "antialias_opacity")
         V = len(views)
+        if self.antialias:
+            # every view's compensated opacities in one launch, before binning
+            # as the reference does: the exact tile test then uses the opacity
+            # that is composited
+            _lib.check(L.mg_antialias_opacity_views(ptr(b.conic), ptr(self.opac), n, V, n, 0.3,
+                                                    ptr(self._opac_view), s),
+                       "antialias_opacity_views")
         opac_all, opac_stride = (self._opac_view, n) if self.antialias else (self.opac, 0)
         totals = None
         if self.batch_binning and _BatchBinning.fits(views, n):
