@@ -12,11 +12,19 @@ ranks when torch.distributed is initialised:
     sh_dc (N,1,3) | sh_rest (N,15,3);
   * the gradient buffer has the same segments plus the number of views in
     which each Gaussian was visible and the loss;
-  * per view: preprocess -> binning (device sort) -> raster forward -> fused
-    loss -> raster backward (packed gradient record) -> preprocess backward
-    that ADDS into the flat gradient with the exp/sigmoid chain applied;
+  * a step runs in three phases: (A) the projection and SH colour of every
+    view in one launch, then the binning of all views of one frame size
+    with one call per stage (one depth sort and one tile sort for the
+    batch) and one host read of the pair totals; (B) per view, on one of
+    `view_streams` CUDA streams in turn, packing, raster forward, fused loss
+    and raster backward into the view's packed gradient records, so one
+    view's raster tail overlaps the next views' work; (C) the projection and
+    SH adjoints of all views in one launch each, ADDING into the flat
+    gradient with the exp/sigmoid chain applied, then Adam;
   * the loss of a batch is the mean over its views, so each view's
-    gradient is scaled by 1 / (global batch).
+    gradient is scaled by 1 / (global batch); the MCMC regularisers
+    (train.py:393-398) and the antialias compensation (train.py
+    --antialias) are options.
 
 With several ranks the optimizer is sharded (ZeRO-1): the visibility counts
 and the loss are all-reduced, the parameter gradient is reduce-scattered so
