@@ -62,8 +62,9 @@ class ViewStats:
 
 
 class _ImageBuffers:
-    """Per-resolution scratch shared by the views of that size (phase B runs
-    the views one after another on the stream)."""
+    """Frame scratch of one phase-B stream for one frame size: the views that
+    stream renders use it one after another (their order on the stream
+    serialises the reuse)."""
 
     def __init__(self, n: int, W: int, H: int, device):
         f32 = dict(dtype=torch.float32, device=device)
