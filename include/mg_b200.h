@@ -306,8 +306,9 @@ mg_status mg_bin_emit(
  * call each (no reference counterpart: the reference bins each view inside
  * its own render call, metal_backend.py:239-262). The inputs are view-major
  * (view v's Gaussian g at row v * view_stride + g, opacity at
- * v * opacity_view_stride + g, 0 when the views share it); n * n_views must
- * stay below 2^31.
+ * v * opacity_view_stride + g, 0 when the views share it); n * n_views and
+ * the batch's pair total must stay below 2^30 - 1 (the radix sort's key
+ * count; the per-view calls take more pairs per view).
  *   mg_bin_prepare_views writes n_views + 2 int64 words to totals_dev: each
  *     view's pair total, the batch's total, and an overflow flag. A set flag
  *     means some view's visible depths span more float bit patterns than

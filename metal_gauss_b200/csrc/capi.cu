@@ -375,8 +375,8 @@ mg_status check_views(int64_t n, int32_t n_views, int64_t view_stride,
         return fail(MG_ERR_INVALID_ARGUMENT, std::string(what) + ": 1..64 views");
     if (n < 0 || view_stride < n || opacity_view_stride < 0)
         return fail(MG_ERR_INVALID_ARGUMENT, std::string(what) + ": bad view strides");
-    if (n * n_views >= ((int64_t)1 << 31))
-        return fail(MG_ERR_CAPACITY, std::string(what) + ": views x Gaussians exceed 2^31");
+    if (n * n_views >= ((int64_t)1 << 30) - 1)  // the radix sort's key count limit
+        return fail(MG_ERR_CAPACITY, std::string(what) + ": views x Gaussians reach 2^30 - 1");
     return MG_OK;
 }
 
@@ -454,8 +454,8 @@ extern "C" mg_status mg_bin_emit_views(const float* uv, const float* rxy, const 
                                        size_t scratch_bytes, mg_stream_t stream) {
     MG_TRY(check_views(n, n_views, view_stride, opacity_view_stride, width, height, tile,
                        "bin_emit_views"));
-    MG_REQUIRE(m_total >= 0 && m_total < ((int64_t)1 << 31),
-               "bin_emit_views: pair count exceeds 2^31");
+    if (m_total < 0 || m_total >= ((int64_t)1 << 30) - 1)  // the tile sort's key count limit
+        return fail(MG_ERR_CAPACITY, "bin_emit_views: pair count reaches 2^30 - 1");
     MG_REQUIRE(prepare_scratch != nullptr && tile_offsets != nullptr,
                "bin_emit_views: null pointer");
     const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;

@@ -147,8 +147,9 @@ class _BatchBinning:
     @staticmethod
     def fits(views, n: int) -> bool:
         """Whether views of n Gaussians each can be binned as one batch: 2..64
-        views of one frame size, fewer than 2^31 (Gaussian, view) rows."""
-        return (1 < len(views) <= 64 and len(views) * n < 2 ** 31 and
+        views of one frame size, fewer than 2^30 - 1 (Gaussian, view) rows
+        (the radix sort's key count)."""
+        return (1 < len(views) <= 64 and len(views) * n < 2 ** 30 - 1 and
                 len({(v.width, v.height) for v in views}) == 1)
 
     def prepare(self, batch: "_ViewBatch", first: int, V: int, n: int, W: int, H: int, tile: int,
@@ -172,9 +173,9 @@ class _BatchBinning:
     def read_totals(self, V: int) -> list[int] | None:
         """The views' pair totals (one device->host read), or None when the
         batch has to be binned one view at a time (a view's depth range
-        outgrew the batch keys, or 2^31 pairs)."""
+        outgrew the batch keys, or 2^30 - 1 pairs, the tile sort's limit)."""
         t = self.totals[:V + 2].tolist()
-        if t[V + 1] or t[V] >= 2 ** 31:
+        if t[V + 1] or t[V] >= 2 ** 30 - 1:
             return None
         self.bases = [0] * V
         for v in range(1, V):
