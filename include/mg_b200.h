@@ -287,7 +287,8 @@ mg_status mg_tile_ranges(const uint32_t* tile_ids, const uint64_t* keys64,
  * optical depth over 64 log-spaced depth bins, with a margin). The lists are
  * then a front-to-back prefix of the full ones: rasterisation results are
  * unchanged, but the lists no longer equal the reference's. 0 gives the
- * reference's lists. */
+ * reference's lists. n and the pair total must stay below 2^30 - 1 (the
+ * radix sort's key count). */
 size_t mg_bin_prepare_scratch_bytes(int64_t n, int32_t n_tiles);
 mg_status mg_bin_prepare(
     const float* uv, const float* rxy, const float* conic,

@@ -297,7 +297,7 @@ extern "C" mg_status mg_bin_prepare(const float* uv, const float* rxy, const flo
                                     void* scratch, size_t scratch_bytes, mg_stream_t stream) {
     MG_REQUIRE(tile > 0 && width > 0 && height > 0, "bin_prepare: bad tiling");
     MG_REQUIRE(total_dev != nullptr, "bin_prepare: null total");
-    MG_REQUIRE(n < (int64_t)1 << 30, "bin_prepare: more than 2^30 Gaussians");
+    MG_REQUIRE(n < ((int64_t)1 << 30) - 1, "bin_prepare: 2^30 - 1 Gaussians or more (sort limit)");
     const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
     const PrepareScratch s = carve_prepare(scratch, n, tiles_x * tiles_y);
     MG_REQUIRE(scratch != nullptr && scratch_bytes >= s.total, "bin_prepare: scratch too small");
@@ -332,7 +332,8 @@ extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float*
                                  int32_t* tile_offsets, void* scratch, size_t scratch_bytes,
                                  mg_stream_t stream) {
     MG_REQUIRE(tile > 0 && width > 0 && height > 0, "bin_emit: bad tiling");
-    MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 31), "bin_emit: pair count exceeds 2^31");
+    MG_REQUIRE(m >= 0 && m < ((int64_t)1 << 30) - 1,
+               "bin_emit: 2^30 - 1 pairs or more (sort limit)");
     MG_REQUIRE(prepare_scratch != nullptr && tile_offsets != nullptr, "bin_emit: null pointer");
     const int tiles_x = (width + tile - 1) / tile, tiles_y = (height + tile - 1) / tile;
     const int n_tiles = tiles_x * tiles_y;
