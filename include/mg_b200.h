@@ -554,12 +554,14 @@ mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
 /* ------------------------------------------------------------------------ */
 
 /* Replaces compute_3d_filter (metal_gauss/mipfilter.py:30-76): per Gaussian,
- * the smallest camera depth among the n_views cameras (<= 64) in whose frame,
+ * the smallest camera depth among the n_views cameras (any number; 64 per
+ * kernel launch, the running minimum carried between launches) in whose frame,
  * widened by `margin` on every side, the mean projects in front of
  * `near_plane`; Gaussians no camera sees take the largest such depth of any
  * Gaussian (all take 1 when none is seen); then depth / max focal * sqrt(0.2).
  * Only viewmat, fx, fy, cx, cy, width and height of `cams` are read.
- * Synchronises `stream` (the filter is recomputed every few hundred steps). */
+ * Synchronises `stream` once per 64 cameras (the filter is recomputed every
+ * few hundred steps). */
 size_t mg_compute_3d_filter_scratch_bytes(void);
 mg_status mg_compute_3d_filter(const float* means, int64_t n, const mg_camera* cams,
                                int32_t n_views, float near_plane, float margin,

@@ -24,12 +24,14 @@ struct FilterCams {
 
 // Pass 1 (mipfilter.py:49-68): the smallest camera depth among the views in
 // whose (margin-widened) frame the mean projects in front of `near`, +inf
-// when none; the largest such depth over all Gaussians goes to *max_bits
+// when none. Cameras come in chunks of at most kMaxFilterViews: a chunk
+// after the first continues from the running minimum in dist, and the last
+// one puts the largest finite minimum over all Gaussians into *max_bits
 // (positive floats order like their bit patterns).
 __global__ void filter_depth_kernel(const float* __restrict__ means, int64_t n,
                                     const FilterCams* __restrict__ cams, int n_views,
-                                    float near, float margin, float* __restrict__ dist,
-                                    uint32_t* __restrict__ max_bits) {
+                                    float near, float margin, int first, int last,
+                                    float* __restrict__ dist, uint32_t* __restrict__ max_bits) {
     __shared__ FilterCams s;
     for (int i = threadIdx.x; i < (int)(sizeof(FilterCams) / 4); i += blockDim.x)
         reinterpret_cast<float*>(&s)[i] = reinterpret_cast<const float*>(cams)[i];
@@ -37,6 +39,7 @@ __global__ void filter_depth_kernel(const float* __restrict__ means, int64_t n,
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     float d = __int_as_float(0x7f800000);
     if (g < n) {
+        if (!first) d = dist[g];
         const float x = means[3 * g], y = means[3 * g + 1], z = means[3 * g + 2];
         for (int v = 0; v < n_views; ++v) {
             const float* R = s.R[v];
@@ -53,6 +56,7 @@ __global__ void filter_depth_kernel(const float* __restrict__ means, int64_t n,
         }
         dist[g] = d;
     }
+    if (!last) return;  // (block-uniform)
     // block maximum of the finite depths, then one atomic
     uint32_t m = (g < n && d < __int_as_float(0x7f800000)) ? __float_as_uint(d) : 0u;
     m = __reduce_max_sync(0xffffffffu, m);
@@ -124,40 +128,49 @@ extern "C" mg_status mg_compute_3d_filter(const float* means, int64_t n, const m
                                           int32_t n_views, float near_plane, float margin,
                                           float* filter_out, void* scratch, size_t scratch_bytes,
                                           mg_stream_t stream) {
-    MG_REQUIRE(n >= 0 && n_views >= 0 && n_views <= kMaxFilterViews,
-               "compute_3d_filter: 0..64 views");
+    MG_REQUIRE(n >= 0 && n_views >= 0, "compute_3d_filter: negative count");
     if (n == 0) return MG_OK;
     MG_REQUIRE(means && filter_out && (n_views == 0 || cams), "compute_3d_filter: null pointer");
     MG_REQUIRE(scratch && scratch_bytes >= mg_compute_3d_filter_scratch_bytes(),
                "compute_3d_filter: scratch too small");
-    FilterCams h{};
     float focal = 0.0f;
-    for (int v = 0; v < n_views; ++v) {
-        const mg_camera& c = cams[v];
-        for (int r = 0; r < 3; ++r)
-            for (int k = 0; k < 4; ++k) h.R[v][4 * r + k] = c.viewmat[4 * r + k];
-        h.fx[v] = c.fx; h.fy[v] = c.fy; h.cx[v] = c.cx; h.cy[v] = c.cy;
-        h.W[v] = (float)c.width; h.H[v] = (float)c.height;
-        focal = std::max(focal, std::max(c.fx, c.fy));
-    }
+    for (int v = 0; v < n_views; ++v)
+        focal = std::max(focal, std::max(cams[v].fx, cams[v].fy));
     if (!(focal > 0.0f)) focal = 1.0f;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     char* p = static_cast<char*>(scratch);
     uint32_t* max_bits = reinterpret_cast<uint32_t*>(p);
     FilterCams* d_cams = reinterpret_cast<FilterCams*>(p + 256);
-    if (cudaMemcpyAsync(d_cams, &h, sizeof(FilterCams), cudaMemcpyHostToDevice, st) !=
-            cudaSuccess ||
-        cudaMemsetAsync(max_bits, 0, sizeof(uint32_t), st) != cudaSuccess)
-        return check_launch("compute_3d_filter copies");
-    filter_depth_kernel<<<ceil_div(n, 256), 256, 0, st>>>(means, n, d_cams, n_views, near_plane,
-                                                         margin, filter_out, max_bits);
-    MG_TRY(check_launch("compute_3d_filter depth"));
+    if (cudaMemsetAsync(max_bits, 0, sizeof(uint32_t), st) != cudaSuccess)
+        return check_launch("compute_3d_filter memset");
+    // cameras in chunks of kMaxFilterViews (one launch each, the running
+    // minimum carried in filter_out); no cameras: one launch that sees none
+    const int chunks = std::max(1, (n_views + kMaxFilterViews - 1) / kMaxFilterViews);
+    for (int c = 0; c < chunks; ++c) {
+        const int v0 = c * kMaxFilterViews;
+        const int nv = std::min(kMaxFilterViews, n_views - v0);
+        FilterCams h{};
+        for (int k = 0; k < nv; ++k) {
+            const mg_camera& cm = cams[v0 + k];
+            for (int r = 0; r < 3; ++r)
+                for (int q = 0; q < 4; ++q) h.R[k][4 * r + q] = cm.viewmat[4 * r + q];
+            h.fx[k] = cm.fx; h.fy[k] = cm.fy; h.cx[k] = cm.cx; h.cy[k] = cm.cy;
+            h.W[k] = (float)cm.width; h.H[k] = (float)cm.height;
+        }
+        // the kernel reads the camera block from device memory: the host copy
+        // must outlive the copy, and the next chunk reuses the device block
+        if (cudaMemcpyAsync(d_cams, &h, sizeof(FilterCams), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess)
+            return check_launch("compute_3d_filter copies");
+        filter_depth_kernel<<<ceil_div(n, 256), 256, 0, st>>>(
+            means, n, d_cams, std::max(nv, 0), near_plane, margin, c == 0 ? 1 : 0,
+            c == chunks - 1 ? 1 : 0, filter_out, max_bits);
+        MG_TRY(check_launch("compute_3d_filter depth"));
+        if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("compute_3d_filter");
+    }
     filter_finish_kernel<<<ceil_div(n, 256), 256, 0, st>>>(filter_out, n, max_bits, focal,
                                                           std::sqrt(0.2f));
-    MG_TRY(check_launch("compute_3d_filter finish"));
-    // the camera block is read by the kernels above: keep the host copy
-    // alive until they have it
-    return cudaStreamSynchronize(st) == cudaSuccess ? MG_OK : check_launch("compute_3d_filter");
+    return check_launch("compute_3d_filter finish");
 }
 
 extern "C" size_t mg_compute_3d_filter_scratch_bytes(void) {

@@ -46,8 +46,6 @@ def compute_3d_filter(means: torch.Tensor, views, near: float = 0.2,
     if means.device.type != "cuda":
         raise RuntimeError("compute_3d_filter: the CUDA backend needs CUDA tensors")
     views = list(views)
-    if len(views) > 64:
-        raise ValueError("compute_3d_filter: at most 64 cameras per call")
     m = means.detach().to(torch.float32).contiguous()
     n = m.shape[0]
     out = torch.empty(n, dtype=torch.float32, device=m.device)

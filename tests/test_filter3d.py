@@ -111,3 +111,20 @@ def test_filter_when_no_camera_sees_anything(cuda):
     ref = oracle.compute_3d_filter(means.numpy(), [(K, vm, 160, 120)])
     assert np.array_equal(got, ref)
     assert np.allclose(got, (1.0 / 500.0) * np.sqrt(0.2), rtol=1e-6)
+
+
+def test_filter_over_more_cameras_than_one_launch_takes(cuda):
+    """150 cameras (three launches of at most 64): the running minimum is
+    carried from chunk to chunk and the unseen fill uses the largest final
+    minimum, as one pass over all cameras does (the oracle)."""
+    N, W, H = 5000, 96, 72
+    p, _, _ = scenes.config("cfg3", n=N, seed=43)
+    views = scenes.sphere_views(150, 4.0, W, H, 40.0, 44, hemisphere=True)
+    means = p["means"].float()
+    got = mipfilter.compute_3d_filter(means.cuda(), views).cpu().numpy()
+    ref = oracle.compute_3d_filter(means.numpy(), [(v.K.numpy(), v.viewmat.numpy(), W, H)
+                                                   for v in views])
+    assert np.abs(got - ref).max() <= 1e-6 * float(ref.max())
+    # the later chunks matter: the first 64 cameras alone give another filter
+    first = mipfilter.compute_3d_filter(means.cuda(), views[:64]).cpu().numpy()
+    assert not np.array_equal(first, got)
