@@ -49,6 +49,8 @@ SEGMENTS = (("means", 3), ("quats", 4), ("log_scales", 3), ("logit_opac", 1), ("
 FLOATS_PER_GAUSSIAN = sum(w for _, w in SEGMENTS)           # 59
 SHAPES = {"means": (3,), "quats": (4,), "log_scales": (3,), "logit_opac": (), "sh_dc": (1, 3),
           "sh_rest": (15, 3)}
+# views one rank renders per step (the multi-view SH adjoint's camera table)
+MAX_VIEWS_PER_STEP = 64
 # make_optimizer's learning rates (train.py:167-191) with its defaults
 DEFAULT_LRS = {"means": 2e-4, "log_scales": 5e-3, "quats": 1e-3, "logit_opac": 1e-2,
                "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
@@ -689,6 +691,9 @@ class Trainer:
         and overwrites its rows; `train_step` zeroes the rest of G first). One
         device->host read per binning chunk (its views' pair totals)."""
         V = len(views)
+        if V > MAX_VIEWS_PER_STEP:
+            raise ValueError(f"a step takes at most {MAX_VIEWS_PER_STEP} views per rank, got "
+                             f"{V} (split the batch over more ranks or steps)")
         if V > self._totals.numel():
             self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
         self._ensure_views(V)

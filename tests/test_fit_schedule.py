@@ -119,3 +119,9 @@ def test_filter_noise_relocation_and_growth_schedule():
     grow = [(e[1], e[2]) for e in tr.events if e[0] == "grow"]
     # growth on relocation steps up to grow_until, toward grow_to linearly
     assert grow == [(2, 125), (4, 150), (6, 175), (8, 200)]
+
+
+def test_a_step_refuses_more_views_than_the_adjoint_table_holds():
+    from metal_gauss_b200.engine import MAX_VIEWS_PER_STEP, Trainer
+    with pytest.raises(ValueError, match="views per rank"):
+        Trainer.forward_backward_views(object(), [None] * (MAX_VIEWS_PER_STEP + 1), [], 1.0)
