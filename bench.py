@@ -238,6 +238,23 @@ def profiled_traffic(kernel: str, args):
     return None, f"no capture of {kernel}"
 
 
+def profiled_issue(kernel: str, args):
+    """Share of issue slots busy (per active cycle) of `kernel` in the same
+    committed capture, the bound that applies to an issue-limited kernel, or
+    (None, reason) as profiled_traffic."""
+    if (args.n_gaussians, args.width, args.height) != (1_000_000, 800, 800):
+        return None, "no capture for this workload size"
+    try:
+        text = TRAFFIC_PROFILE.read_text()
+    except OSError:
+        return None, "capture summary missing"
+    for name, val in re.findall(r"<!-- issue_active_pct (\S+) ([0-9.]+) -->", text):
+        if name == kernel:
+            return round(float(val) / 100.0, 4), \
+                f"{TRAFFIC_PROFILE.relative_to(ROOT)} (ncu --set full, one view)"
+    return None, f"no capture of {kernel}"
+
+
 # ---------------------------------------------------------------- our arm
 
 def run_ours(args, rank, world, local):
@@ -312,13 +329,17 @@ def run_ours(args, rank, world, local):
     peaks = measured_peaks()
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
     traffic, traffic_src = profiled_traffic(dom, args)
+    issue, issue_src = profiled_issue(dom, args)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "peak_source": peaks["source"], "traffic": traffic,
                 "traffic_source": traffic_src,
                 "bytes_per_launch": dom_bytes, "avg_launch_ms": round(dom_ms, 4),
-                "launches_timed": len(dom_times)}
+                "launches_timed": len(dom_times),
+                # the kernel is instruction-issue-bound, not HBM-bound: its
+                # issue-slot occupancy from the same capture
+                "issue_slots_busy": {"frac": issue, "source": issue_src}}
 
     # whole-step algorithmic bytes against the same peak
     for st in trainer.last_stats:
