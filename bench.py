@@ -6,16 +6,19 @@ Workload (BASELINE.json's metric is quoted on it, configs[2]): 1M Gaussians
 near the surfaces of 20 random ellipsoids, SH degree 3, 800x800, cameras on a
 radius-4 hemisphere; one step = a batch of 8 views (sharded over the N GPUs)
 rendered, lossed (0.8 L1 + 0.2 (1 - SSIM) against seeded U[0,1] targets) and
-back-propagated, the gradient all-reduced over NCCL, then selective Adam on the
-union-visible Gaussians. Inputs are seeded synthetic data of those shapes; the
-reference's datasets are not available here.
+back-propagated, then selective Adam on the union-visible Gaussians; with N > 1
+the optimizer is sharded (ZeRO-1: the gradient is reduce-scattered over NCCL,
+each rank updates its chunk, the parameters are all-gathered). Inputs are
+seeded synthetic data of those shapes; the reference's datasets are not
+available here.
 
 `value` is whole-job steps/s with every input resident in HBM (K steps timed
 with CUDA events, max over ranks). `e2e` is the same metric through the public
 API (engine.Trainer.train_step) with the targets copied host->device from
 pinned memory every step and the loss read back every step. `--impl
 reference` times the reference's algorithm on the host cores (the CPU oracle,
-all threads) on the same workload, one view of each step as the sample.
+all threads) on the same workload: every view of each timed step, then one
+selective Adam update on the views' union visibility.
 """
 
 from __future__ import annotations
@@ -41,8 +44,15 @@ sys.path.insert(0, str(ROOT))
 METRIC = ("train steps/s (fwd+bwd+Adam) at 800×800, 1M Gaussians, 1/2/4/8 B200; "
           "% HBM roofline")
 WORKLOAD = ("cfg3: 1M Gaussians near the surfaces of 20 random ellipsoids, SH3, 800x800, "
-            "100 hemisphere cameras, batch of 8 views per step sharded over the GPUs, NCCL "
-            "all-reduce of the flat gradient, selective Adam on union-visible Gaussians")
+            "100 hemisphere cameras, batch of 8 views per step sharded over the GPUs, "
+            "selective Adam on union-visible Gaussians; on several GPUs ZeRO-1 (NCCL "
+            "reduce-scatter of the gradient, Adam on each rank's chunk, all-gather of the "
+            "parameters)")
+# why the reference's own CPU renderer (metal_gauss.torch_ref) is not timed
+# beside the oracle: it cannot be installed in this environment
+TORCH_REF_UNAVAILABLE = ("the reference package does not install here: its build backend "
+                         "(hatchling) is not in the offline wheelhouse, so metal_gauss.torch_ref "
+                         "is not importable on the GPU box")
 
 
 def parse():
@@ -58,7 +68,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--dense-adam", action="store_true")
-    ap.add_argument("--cpu-budget-s", type=float, default=120.0)
+    ap.add_argument("--cpu-budget-s", type=float, default=240.0,
+                    help="--impl reference: stop timing further steps once this many seconds "
+                         "of CPU work have been spent (the line reports the steps run)")
     ap.add_argument("--render", action="store_true",
                     help="forward-only render throughput on cfg4 (3M heavy-tailed Gaussians, "
                          "1920x1080, antialias, 256 orbit views) instead of the training step")
@@ -204,10 +216,15 @@ def stage_bytes(stage: str, n: int, walked: float, P: int, n_tiles: int,
         # rgb, alpha, T, stop out (24)
         return 52.0 * walked + 12.0 * n_tiles + 24.0 * P
     if stage == "pack":
-        return (36.0 + 48.0) * n
+        # uv, conic, opacity, colour in; the 48-byte record out; the view's
+        # 48-byte gradient record zeroed
+        return (36.0 + 48.0 + 48.0) * n
     if stage == "preprocess_fwd":
-        # parameters + SH rows once, 48 B of outputs per view, visibility RMW
-        return (44.0 + 192.0 + 8.0) * n + 48.0 * views * n
+        # parameters (log-scales and logits for the step prologue) + SH rows
+        # once; activations written (16), the 11 accumulated gradient floats
+        # zeroed (44), the visibility count written (4); 48 B of outputs per
+        # view
+        return (44.0 + 192.0 + 16.0 + 44.0 + 4.0) * n + 48.0 * views * n
     if stage == "preprocess_bwd":
         # parameters once; per view gradient record, valid, colour, gated
         # colour gradient; one read-modify-write of 11 gradient floats
@@ -285,6 +302,12 @@ def run_ours(args, rank, world, local):
         step(args.warmup + i)
     torch.cuda.synchronize()
     stage_ms = {k: v for k, v in trainer.stage_times_ms().items()}
+    # per-step collective times (each includes waiting for the slowest rank),
+    # max over ranks
+    coll = {}
+    for k in ("reduce_scatter", "all_gather", "allreduce"):
+        if k in stage_ms:
+            coll[k + "_ms"] = round(max_over_ranks(float(np.sum(stage_ms[k])) / n_instr, world), 4)
     singles = {k: v for k, v in stage_ms.items()
                if k in ("raster_bwd", "raster_fwd", "preprocess_fwd", "preprocess_bwd", "loss",
                         "adam")}
@@ -313,7 +336,13 @@ def run_ours(args, rank, world, local):
     trainer.stage_events = None
     trainer.timed_stages = None
     trainer.walked = []
-    n_vis_view = float(trainer.visibility_count().gt(0).sum()) / max(1, len(trainer.last_stats))
+    # visible Gaussians per view: the mean over the last step's views of the
+    # projection's valid flags (each view's own visible set)
+    V_rank = max(1, len(trainer.last_stats))
+    n_vis_view = float(trainer._batch.valid[:V_rank].ne(0).sum()) / V_rank
+    # the device error word after the timed steps: 0 unless a bounded wait
+    # gave up or an index was out of range, which voids the run
+    dev_err = _lib.device_error()
     ms = t0.elapsed_time(t1) / args.steps
     ms = max_over_ranks(ms, world)
     pairs = [s.pairs for s in trainer.last_stats]
@@ -403,9 +432,14 @@ def run_ours(args, rank, world, local):
             "pairs_per_view": int(m_avg), "walked_entries_per_view": int(walked),
             "loss": round(loss_val, 6),
             "e2e": e2e, "cpu_baseline": cpu, "gpu_launches": int(launches),
-            "clocks": clk,
+            "clocks": clk, "device_error": int(dev_err),
         }
+        if coll:
+            out["collectives_ms"] = coll
         emit(out)
+    if dev_err:
+        raise SystemExit(f"device error {dev_err} during the timed steps: "
+                         f"{_lib.DEVICE_ERRORS.get(dev_err, 'unknown')}")
 
 
 def run_render(args, rank, world, local):
@@ -469,7 +503,7 @@ def run_render(args, rank, world, local):
 
 # ----------------------------------------------------------- CPU (oracle)
 
-def cpu_view_step(op, params_np, view, target, batch, selective_state=None):
+def cpu_view_step(op, params_np, view, target, batch):
     """One view of the training step on the host with the CPU oracle: render,
     loss, backward, activation chain. Returns (loss, grads dict, visible)."""
     means, quats = params_np["means"], params_np["quats"]
@@ -495,24 +529,40 @@ def cpu_adam(op, params_np, grads, visible, state, lrs):
                                st[2], visible, lr)
 
 
+def cpu_step(op, params_np, views, targets_u8, idx, batch, state, lrs):
+    """One whole training step on the host: every view of the batch `idx`
+    rendered, lossed and back-propagated (gradients summed), then one
+    selective Adam update on the views' union visibility. Returns
+    (seconds in the views, seconds in Adam)."""
+    acc, vis = None, None
+    t = time.perf_counter()
+    for j in idx:
+        tgt = targets_u8[j].numpy().astype(np.float32) / np.float32(255.0)
+        _, grads, v = cpu_view_step(op, params_np, views[j], tgt, batch)
+        if acc is None:
+            acc, vis = grads, v.copy()
+        else:
+            for k in acc:
+                acc[k] += grads[k]
+            vis |= v
+    t_views = time.perf_counter() - t
+    t = time.perf_counter()
+    cpu_adam(op, params_np, acc, vis.astype(np.uint8), state, lrs)
+    return t_views, time.perf_counter() - t
+
+
 def cpu_baseline(args, p, views, targets_u8, max_views: int = 1) -> dict:
     """The oracle (the reference's algorithm restated in C, OpenMP over all host
-    cores) on a bounded sample: `max_views` view(s) of the step plus the
-    selective Adam update over all 1M Gaussians; scaled to steps/s of the
-    whole 8-view step."""
+    cores) on a bounded sample, to keep the default GPU run short:
+    `max_views` view(s) of the step plus the selective Adam update over all 1M
+    Gaussians, scaled to steps/s of the whole 8-view step (the reference arm,
+    --impl reference, runs whole steps)."""
     import oracle as op
     from metal_gauss_b200.engine import DEFAULT_LRS
     params_np = {k: np.ascontiguousarray(v.numpy(), np.float32) for k, v in p.items()}
-    t_views = []
-    for j in range(max_views):
-        tgt = (targets_u8[j].numpy().astype(np.float32) / 255.0)
-        t = time.perf_counter()
-        _, grads, vis = cpu_view_step(op, params_np, views[j], tgt, args.batch)
-        t_views.append(time.perf_counter() - t)
-    t = time.perf_counter()
-    cpu_adam(op, params_np, grads, vis.astype(np.uint8), {}, DEFAULT_LRS)
-    t_adam = time.perf_counter() - t
-    t_view = float(np.mean(t_views))
+    t_views, t_adam = cpu_step(op, params_np, views, targets_u8, list(range(max_views)),
+                               args.batch, {}, DEFAULT_LRS)
+    t_view = t_views / max_views
     step_s = args.batch * t_view + t_adam
     return {"value": round(1.0 / step_s, 5), "unit": "steps/s", "cores": os.cpu_count(),
             "kind": "port",
@@ -520,7 +570,7 @@ def cpu_baseline(args, p, views, targets_u8, max_views: int = 1) -> dict:
                       f"{t_view:.2f} s each) + selective Adam over all "
                       f"{args.n_gaussians} Gaussians ({t_adam:.2f} s); steps/s = "
                       f"1 / ({args.batch} x view + Adam)",
-            "cpu_model": _cpu_model()}
+            "cpu_model": _cpu_model(), "torch_ref": {"unavailable": TORCH_REF_UNAVAILABLE}}
 
 
 def _cpu_model() -> str:
@@ -535,7 +585,12 @@ def _cpu_model() -> str:
 
 def run_reference(args, rank, world):
     """--impl reference: the reference's algorithm (CPU oracle, all host
-    threads) on the same workload and metric. Rank 0 only."""
+    threads) on the same workload and metric, rank 0 only. Each timed step is
+    the whole step: all `batch` views rendered, lossed and back-propagated,
+    then selective Adam on their union visibility. Warm-up steps run one view
+    each (they only warm the host's caches and thread pool). Timing stops once
+    --cpu-budget-s seconds have gone into timed steps; `steps` reports how
+    many ran."""
     if rank != 0:
         return
     import oracle as op
@@ -544,25 +599,21 @@ def run_reference(args, rank, world):
     p, views, spec, targets_u8 = workload(args)
     params_np = {k: np.ascontiguousarray(v.numpy(), np.float32) for k, v in p.items()}
     state: dict = {}
+    for i in range(args.warmup):
+        cpu_step(op, params_np, views, targets_u8, batch_indices(i, args.batch, len(views))[:1],
+                 args.batch, state, DEFAULT_LRS)
     times = []
-    budget_t0 = time.perf_counter()
-    total = args.warmup + args.steps
-    done = 0
-    for i in range(total):
-        j = batch_indices(i, args.batch, len(views))[0]
-        tgt = targets_u8[j].numpy().astype(np.float32) / 255.0
-        t = time.perf_counter()
-        _, grads, vis = cpu_view_step(op, params_np, views[j], tgt, args.batch)
-        t_view = time.perf_counter() - t
-        t = time.perf_counter()
-        cpu_adam(op, params_np, grads, vis.astype(np.uint8), state, DEFAULT_LRS)
-        t_adam = time.perf_counter() - t
-        if i >= args.warmup or total == 1:
-            times.append(args.batch * t_view + t_adam)
-            done += 1
-        if time.perf_counter() - budget_t0 > args.cpu_budget_s and done >= 1:
+    t_region = time.perf_counter()
+    for i in range(args.steps):
+        idx = batch_indices(args.warmup + i, args.batch, len(views))
+        t_views, t_adam = cpu_step(op, params_np, views, targets_u8, idx, args.batch, state,
+                                   DEFAULT_LRS)
+        times.append(t_views + t_adam)
+        if time.perf_counter() - t_region > args.cpu_budget_s:
             break
-    step_s = float(np.mean(times))
+    region_s = time.perf_counter() - t_region
+    done = len(times)
+    step_s = region_s / done
     value = 1.0 / step_s
     emit({
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "steps/s",
@@ -570,13 +621,17 @@ def run_reference(args, rank, world):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "n_gaussians": args.n_gaussians, "width": args.width,
-                   "height": args.height, "global_batch": args.batch},
+                   "height": args.height, "global_batch": args.batch, "views_per_gpu": args.batch,
+                   "parallelism": "single", "optimizer": "selective Adam"},
+        "timed_region_s": round(region_s, 2),
         "cpu_baseline": {"value": round(value, 5), "unit": "steps/s", "cores": os.cpu_count(),
                          "kind": "port",
-                         "sample": f"per step: 1 of its {args.batch} views (fwd+loss+bwd) timed "
-                                   "and scaled by the batch, plus the selective Adam update over "
-                                   "all Gaussians; CPU oracle (C, OpenMP, all host threads)",
-                         "cpu_model": _cpu_model()},
+                         "sample": f"{done} whole steps of {args.batch} views each (fwd+loss+bwd "
+                                   "of every view, then selective Adam on their union "
+                                   "visibility); warm-up steps one view each; CPU oracle (C, "
+                                   "OpenMP, all host threads)",
+                         "cpu_model": _cpu_model(),
+                         "torch_ref": {"unavailable": TORCH_REF_UNAVAILABLE}},
         "e2e": {"value": round(value, 5), "unit": "steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     })

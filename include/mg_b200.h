@@ -102,21 +102,49 @@ mg_status mg_preprocess_forward(
     float* uv, float* conic, float* depth, float* rxy, int32_t* valid,
     float* color, mg_stream_t stream);
 
+/* The start of a training step, folded into mg_preprocess_forward_views so
+ * it costs no launch of its own (the reference forms the activations with
+ * torch elementwise ops, train.py:214-229, and clears gradients through
+ * autograd). For every row g < n the projection kernel then
+ *   - forms act_scales[g] = exp(log_scales[g]) (N,3) and act_opac[g] =
+ *     1 / (1 + exp(-logit_opac[g])) (N,) and writes them;
+ *   - with filter_3d (N,) given, applies Mip-Splatting's 3D filter to them as
+ *     mg_apply_3d_filter does and writes out_scales / out_opac; the filtered
+ *     values are projected, otherwise the activations are;
+ *   - sets rows g of each non-NULL zero[k] (row width zero_width[k] floats)
+ *     to 0: the gradient rows the step accumulates into;
+ *   - WRITES the visibility count (instead of adding to it);
+ * and *zero_word (the loss accumulator) is set to 0 once. */
+typedef struct mg_step_prologue {
+    const float* log_scales;
+    const float* logit_opac;
+    const float* filter_3d;
+    float* act_scales;
+    float* act_opac;
+    float* out_scales;
+    float* out_opac;
+    float* zero[4];
+    int32_t zero_width[4];
+    float* zero_word;
+} mg_step_prologue;
+
 /* Training-engine form of mg_preprocess_forward for the views of one batch
  * (same math per view, preprocess.metal:114-221): each Gaussian's
  * parameters and SH rows are read once and projected and coloured for all
  * n_views cameras `cams`. View v's outputs start at row v * view_stride
  * (view_stride >= n) of uv, conic, depth, rxy, valid and color, laid out as
  * in mg_preprocess_forward. With `visibility` given, the number of views in
- * which a Gaussian is valid is ADDED to visibility[g] (float). No reference
- * counterpart: the reference projects one camera per call. */
+ * which a Gaussian is valid is ADDED to visibility[g] (float). With
+ * `prologue` given (may be NULL), `scales` and `opacities` are ignored and
+ * the step prologue above runs first. No reference counterpart: the
+ * reference projects one camera per call. */
 mg_status mg_preprocess_forward_views(
     const float* means, const float* quats, const float* scales,
     const float* sh_dc, const float* sh_rest, mg_sh_layout shl,
     const float* opacities, const mg_camera* cams, int32_t n_views,
     int32_t sh_degree, int64_t n, int64_t view_stride, float* uv, float* conic,
     float* depth, float* rxy, int32_t* valid, float* color, float* visibility,
-    mg_stream_t stream);
+    const mg_step_prologue* prologue, mg_stream_t stream);
 
 /* Replaces preprocess_backward (rasterize.mm:286-327, kernel
  * preprocess.metal:223-411). The incoming gradients are read through row
@@ -246,7 +274,8 @@ mg_status mg_sort_pairs_u64(uint64_t* keys, uint32_t* vals,
  *     MG_ERR_CAPACITY and a message, nothing is launched.
  *   - The first call on a device looks up the array's device address for that
  *     device (cudaGetSymbolAddress with that device current); make that first
- *     call before any stream capture.
+ *     call before any stream capture. The address is cached per device and
+ *     context: after a device reset the next call looks it up again.
  *   - Every call on a device shares the one array, so calls whose work
  *     overlaps on the GPU (different streams, or different host threads)
  *     race and corrupt each other's results: serialise them. The array keeps
@@ -355,9 +384,13 @@ mg_status mg_bin_emit_views(
 /* Packs n splats into `splats` (n * MG_SPLAT_BYTES, 16-byte aligned). The
  * reference's rasterize_forward / rasterize_backward (rasterize.mm:79-194)
  * take uv (N,2), conic (N,3), opacity (N,), color (N,3); a caller of this ABI
- * packs them once per view and hands the record array to both passes. */
+ * packs them once per view and hands the record array to both passes.
+ * grad2d_zero (may be NULL; 16-byte aligned, N x MG_G2D_STRIDE floats) is set
+ * to zero in the same pass: the gradient records mg_rasterize_backward of
+ * this view accumulates into. */
 mg_status mg_pack_splats(const float* uv, const float* conic, const float* opacity,
-                         const float* color, int64_t n, void* splats, mg_stream_t stream);
+                         const float* color, int64_t n, void* splats, float* grad2d_zero,
+                         mg_stream_t stream);
 
 /* Bytes of rasteriser scratch for one view of width x height with `m`
  * (tile, splat) pairs: work counters, the tile order, per-warp-block walk
@@ -648,8 +681,26 @@ mg_status mg_mcmc_add_noise(float* means, const float* quats, const float* log_s
  * spins that gave up, checked-mode index faults). Synchronises `stream`.
  * *code_out receives 0 when nothing was recorded, else the first code:
  * 1 a sort look-back wait gave up, 2 a tile list reached past the sized pair
- * count. */
+ * count. The reference refuses instead of continuing silently
+ * (metal_gauss/api.py:18-26); callers raise on a non-zero code. */
 mg_status mg_read_device_error(int32_t* code_out, mg_stream_t stream);
+
+/* Copies the device error word of the current device, without clearing it,
+ * to the device int64 *code_dev on `stream` (one tiny kernel, no host
+ * synchronisation), so a caller can fetch it with a device->host read it
+ * already makes. No reference counterpart. */
+mg_status mg_peek_device_error(int64_t* code_dev, mg_stream_t stream);
+
+/* Self-test of the sort's bounded wait (no reference counterpart): launches
+ * one onesweep pass as the second tile of a two-tile sort whose first tile
+ * never publishes its look-back word, with the wait limited to spin_limit
+ * rounds (1..2^22; the sort itself uses 2^22). The pass gives up, records code
+ * 1 in the device error word and returns; nothing hangs or traps. Read the
+ * word with mg_read_device_error afterwards. scratch (256-byte aligned) holds
+ * the self-test's own keys and look-back words. */
+size_t mg_sort_lookback_selftest_scratch_bytes(void);
+mg_status mg_sort_lookback_selftest(uint32_t spin_limit, void* scratch, size_t scratch_bytes,
+                                    mg_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -45,6 +45,17 @@ class RowSegment(C.Structure):
     _fields_ = [("ptr", C.c_void_p), ("width", C.c_int32)]
 
 
+class StepPrologue(C.Structure):
+    """mg_step_prologue: the start of a training step folded into the
+    multi-view projection (activations, optional 3D filter, gradient rows and
+    the loss set to zero, visibility written)."""
+    _fields_ = [("log_scales", C.c_void_p), ("logit_opac", C.c_void_p),
+                ("filter_3d", C.c_void_p), ("act_scales", C.c_void_p),
+                ("act_opac", C.c_void_p), ("out_scales", C.c_void_p),
+                ("out_opac", C.c_void_p), ("zero", C.c_void_p * 4),
+                ("zero_width", C.c_int32 * 4), ("zero_word", C.c_void_p)]
+
+
 SH_FUSED = ShLayout(16, 16, 1, 0)
 SH_SPLIT = ShLayout(1, 15, 0, 0)
 
@@ -74,7 +85,8 @@ SIGNATURES = {
     "mg_apply_3d_filter": (i32, [vp, vp, vp, i64, vp, vp, vp]),
     "mg_apply_3d_filter_backward": (i32, [vp, vp, vp, vp, vp, i64, vp, vp, vp]),
     "mg_preprocess_forward_views": (i32, [vp, vp, vp, vp, vp, ShLayout, vp, vp, i32, i32, i64,
-                                          i64, vp, vp, vp, vp, vp, vp, vp, vp]),
+                                          i64, vp, vp, vp, vp, vp, vp, vp,
+                                          C.POINTER(StepPrologue), vp]),
     "mg_preprocess_backward_views": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i64, i64, vp,
                                            vp, vp, vp, vp, vp, vp]),
     "mg_bin_count": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]),
@@ -99,7 +111,7 @@ SIGNATURES = {
     "mg_bin_emit_scratch_bytes": (sz, [i64, i64, i32]),
     "mg_bin_emit": (i32, [vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, vp, vp, vp, vp, sz,
                           vp]),
-    "mg_pack_splats": (i32, [vp, vp, vp, vp, i64, vp, vp]),
+    "mg_pack_splats": (i32, [vp, vp, vp, vp, i64, vp, vp, vp]),
     "mg_antialias_opacity": (i32, [vp, vp, i64, f32, vp, vp]),
     "mg_antialias_opacity_backward": (i32, [vp, vp, vp, i64, f32, vp, vp, vp]),
     "mg_raster_scratch_bytes": (sz, [i32, i32, i32, i64]),
@@ -123,6 +135,9 @@ SIGNATURES = {
     "mg_l1_ssim_scratch_bytes": (sz, [i32, i32]),
     "mg_l1_ssim_loss": (i32, [vp, vp, vp, i32, i32, f32, f32, f32, vp, vp, vp, sz, vp]),
     "mg_read_device_error": (i32, [C.POINTER(i32), vp]),
+    "mg_peek_device_error": (i32, [vp, vp]),
+    "mg_sort_lookback_selftest_scratch_bytes": (sz, []),
+    "mg_sort_lookback_selftest": (i32, [C.c_uint32, vp, sz, vp]),
 }
 
 _lib = None
@@ -195,11 +210,37 @@ def make_camera(viewmat: torch.Tensor, fx: float, fy: float, cx: float, cy: floa
     return cam
 
 
+DEVICE_ERRORS = {1: "a radix-sort look-back wait gave up (a predecessor tile never published)",
+                 2: "a tile list reached past the sized pair count"}
+
+
+class DeviceError(RuntimeError):
+    """A kernel recorded a code in the device error word: its results are
+    not trustworthy, so the caller refuses to continue (the reference's
+    stance, metal_gauss/api.py:18-26)."""
+
+
 def device_error(clear: bool = True) -> int:
     """Read (and clear) the device error word; 0 when nothing was recorded."""
     code = C.c_int32(0)
     call("mg_read_device_error", C.byref(code), stream())
     return code.value
+
+
+def raise_device_error(code: int, where: str) -> None:
+    """Clear the device error word and raise DeviceError for `code` (non-zero)
+    observed by `where`."""
+    device_error()
+    raise DeviceError(f"{where}: device error {code}: "
+                      f"{DEVICE_ERRORS.get(int(code), 'unknown code')}; results discarded")
+
+
+def check_device_error(where: str) -> None:
+    """Synchronising check of the device error word (raises DeviceError)."""
+    code = device_error()
+    if code:
+        raise DeviceError(f"{where}: device error {code}: "
+                          f"{DEVICE_ERRORS.get(int(code), 'unknown code')}; results discarded")
 
 
 def library_path() -> Path:

@@ -14,9 +14,39 @@ std::atomic<uint64_t> g_launches{0};
 
 __device__ int32_t g_device_error_word;
 
-constexpr int kMaxDevices = 64;
-int32_t* g_error_ptr[kMaxDevices] = {nullptr};
-std::mutex g_error_mu;
+DeviceSymbolCache g_error_cache;
+std::mutex g_symbol_mu;
+
+// The driver's cuCtxGetCurrent / cuCtxGetId, resolved through the runtime (the
+// library links no driver stub). Null when the driver lacks them.
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
+
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = [] {
+        void* f = nullptr;
+        return cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault) == cudaSuccess
+                   ? reinterpret_cast<CtxGetCurrentFn>(f)
+                   : nullptr;
+    }();
+    static CtxGetIdFn get_id = [] {
+        void* f = nullptr;
+        return cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault) == cudaSuccess
+                   ? reinterpret_cast<CtxGetIdFn>(f)
+                   : nullptr;
+    }();
+    if (get_current == nullptr || get_id == nullptr) return 0ull;
+    void* ctx = nullptr;
+    if (get_current(&ctx) != 0 || ctx == nullptr) return 0ull;
+    unsigned long long id = 0ull;
+    return get_id(ctx, &id) == 0 ? id : 0ull;
+}
+
+// Copies the current device's error word (without clearing it) to a device
+// int64, on the stream.
+__global__ void peek_error_kernel(const int32_t* word, int64_t* out) {
+    *out = (int64_t)*(const volatile int32_t*)word;
+}
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -124,16 +154,32 @@ mg_status check_launch(const char* what) {
     return MG_ERR_CUDA;
 }
 
-int32_t* device_error_word() {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-    std::lock_guard<std::mutex> lock(g_error_mu);
-    if (g_error_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_device_error_word) != cudaSuccess) return nullptr;
-        g_error_ptr[dev] = static_cast<int32_t*>(p);
+void* device_symbol_address(const void* symbol, DeviceSymbolCache* cache, std::string* why) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= DeviceSymbolCache::kMaxDevices) {
+        if (why) *why = "no current CUDA device";
+        return nullptr;
     }
-    return g_error_ptr[dev];
+    std::lock_guard<std::mutex> lock(g_symbol_mu);
+    const unsigned long long id = current_context_id();
+    if (cache->addr[dev] != nullptr && id != 0ull && cache->ctx_id[dev] == id)
+        return cache->addr[dev];
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, symbol);
+    if (e != cudaSuccess || p == nullptr) {
+        if (why) *why = std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e);
+        return nullptr;
+    }
+    // the lookup made the device's context current if it was not yet; an id
+    // of 0 (driver without context ids) caches nothing and looks up every time
+    cache->ctx_id[dev] = current_context_id();
+    cache->addr[dev] = cache->ctx_id[dev] != 0ull ? p : nullptr;
+    return p;
+}
+
+int32_t* device_error_word() {
+    return static_cast<int32_t*>(
+        device_symbol_address(&g_device_error_word, &g_error_cache, nullptr));
 }
 
 }  // namespace mg
@@ -158,6 +204,14 @@ extern "C" mg_status mg_read_device_error(int32_t* code_out, mg_stream_t stream)
         return check_launch("read_device_error");
     *code_out = host;
     return MG_OK;
+}
+
+extern "C" mg_status mg_peek_device_error(int64_t* code_dev, mg_stream_t stream) {
+    MG_REQUIRE(code_dev != nullptr, "peek_device_error: null output");
+    int32_t* w = device_error_word();
+    if (w == nullptr) return fail(MG_ERR_CUDA, "peek_device_error: no device error word");
+    peek_error_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(w, code_dev);
+    return check_launch("peek_device_error");
 }
 
 extern "C" mg_status mg_preprocess_forward(const float* means, const float* quats,
@@ -192,7 +246,7 @@ extern "C" mg_status mg_preprocess_forward_views(
     const float* sh_rest, mg_sh_layout shl, const float* opacities, const mg_camera* cams,
     int32_t n_views, int32_t sh_degree, int64_t n, int64_t view_stride, float* uv, float* conic,
     float* depth, float* rxy, int32_t* valid, float* color, float* visibility,
-    mg_stream_t stream) {
+    const mg_step_prologue* prologue, mg_stream_t stream) {
     MG_REQUIRE(n_views >= 0, "preprocess_forward_views: negative view count");
     MG_REQUIRE(sh_degree <= 3, "preprocess_forward_views: sh_degree must be <= 3");
     if (n == 0 || n_views == 0) return MG_OK;
@@ -201,7 +255,20 @@ extern "C" mg_status mg_preprocess_forward_views(
     for (int v = 0; v < n_views; ++v)
         MG_REQUIRE(cams[v].width > 0 && cams[v].height > 0,
                    "preprocess_forward_views: empty image");
-    MG_REQUIRE(means && quats && scales && opacities && uv && conic && depth && rxy && valid,
+    if (prologue != nullptr) {
+        const mg_step_prologue& p = *prologue;
+        MG_REQUIRE(p.log_scales && p.logit_opac && p.act_scales && p.act_opac,
+                   "preprocess_forward_views: prologue needs log_scales, logit_opac and the "
+                   "activation outputs");
+        MG_REQUIRE(p.filter_3d == nullptr || (p.out_scales && p.out_opac),
+                   "preprocess_forward_views: prologue with filter_3d needs out_scales/out_opac");
+        for (int k = 0; k < 4; ++k)
+            MG_REQUIRE(p.zero[k] == nullptr || p.zero_width[k] > 0,
+                       "preprocess_forward_views: prologue zero row width must be positive");
+    } else {
+        MG_REQUIRE(scales && opacities, "preprocess_forward_views: null scales or opacities");
+    }
+    MG_REQUIRE(means && quats && uv && conic && depth && rxy && valid,
                "preprocess_forward_views: null pointer");
     MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u,
                "preprocess_forward_views: quats must be 16-byte aligned");
@@ -214,7 +281,7 @@ extern "C" mg_status mg_preprocess_forward_views(
     }
     return launch_preprocess_forward_views(means, quats, scales, sh_dc, sh_rest, shl, opacities,
                                            cams, n_views, sh_degree, n, view_stride, uv, conic,
-                                           depth, rxy, valid, color, visibility,
+                                           depth, rxy, valid, color, visibility, prologue,
                                            reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -40,6 +40,19 @@ inline mg_status fail(mg_status s, const std::string& msg) {
 // checked-mode index faults record a code here instead of trapping.
 int32_t* device_error_word();
 
+// Device address of a file-scope __device__ variable on the current device.
+// In host code the variable's name is only a stand-in for it, so the address
+// is looked up with cudaGetSymbolAddress with the device current, and cached
+// per device together with the unique id of the context it belongs to: after
+// a device reset the runtime creates a new context (and loads the module
+// again), the id changes and the address is looked up afresh.
+struct DeviceSymbolCache {
+    static constexpr int kMaxDevices = 64;
+    unsigned long long ctx_id[kMaxDevices] = {};
+    void* addr[kMaxDevices] = {};
+};
+void* device_symbol_address(const void* symbol, DeviceSymbolCache* cache, std::string* why);
+
 enum DeviceErrorCode : int32_t {
     DEV_ERR_NONE = 0,
     DEV_ERR_SORT_LOOKBACK_TIMEOUT = 1,

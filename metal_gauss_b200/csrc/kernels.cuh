@@ -20,7 +20,9 @@ mg_status launch_preprocess_forward_views(const float* means, const float* quats
                                           int n_views, int sh_degree, int64_t n,
                                           int64_t view_stride, float* uv, float* conic,
                                           float* depth, float* rxy, int32_t* valid,
-                                          float* color, float* vis, cudaStream_t stream);
+                                          float* color, float* vis,
+                                          const mg_step_prologue* prologue,
+                                          cudaStream_t stream);
 mg_status launch_bin_count(const float* uv, const float* rxy, const float* conic,
                            const float* opacity, const int32_t* valid, int64_t n,
                            int W, int H, int tile, int tiles_x, int tiles_y,

@@ -10,6 +10,7 @@
 #include <algorithm>
 
 #include "exact_math.cuh"
+#include "filter3d.cuh"
 #include "kernels.cuh"
 
 namespace mg {
@@ -149,7 +150,8 @@ preprocess_forward_views_kernel(const float* __restrict__ means,
                                 float2* __restrict__ out_uv, float* __restrict__ out_conic,
                                 float* __restrict__ out_depth, float2* __restrict__ out_rxy,
                                 int32_t* __restrict__ out_valid,
-                                float* __restrict__ out_color, float* __restrict__ vis) {
+                                float* __restrict__ out_color, float* __restrict__ vis,
+                                const mg_step_prologue pro, bool with_prologue) {
     __shared__ float s_rest[kPreBlock / 32][32 * 15 * 3];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t g = (int64_t)blockIdx.x * kPreBlock + threadIdx.x;
@@ -163,8 +165,42 @@ preprocess_forward_views_kernel(const float* __restrict__ means,
     if (in) {
         mx = means[3 * g + 0]; my = means[3 * g + 1]; mz = means[3 * g + 2];
         const float4 q = __ldg(reinterpret_cast<const float4*>(quats) + g);
-        gc = gaussian_cov(q.x, q.y, q.z, q.w, scales[3 * g + 0], scales[3 * g + 1],
-                          scales[3 * g + 2], opacities[g]);
+        float sx, sy, sz, op;
+        if (with_prologue) {
+            // the step's activations (train.py:221-222, torch's exp and
+            // 1 / (1 + exp(-x))), then the 3D filter when one is set
+            // (train.py:223-227, mipfilter.py:79-93)
+            sx = expf(pro.log_scales[3 * g + 0]);
+            sy = expf(pro.log_scales[3 * g + 1]);
+            sz = expf(pro.log_scales[3 * g + 2]);
+            op = 1.0f / (1.0f + expf(-pro.logit_opac[g]));
+            pro.act_scales[3 * g + 0] = sx;
+            pro.act_scales[3 * g + 1] = sy;
+            pro.act_scales[3 * g + 2] = sz;
+            pro.act_opac[g] = op;
+            if (pro.filter_3d != nullptr) {
+                const Filter3d f = filter3d(sx, sy, sz, pro.filter_3d[g]);
+                sx = f.s[0]; sy = f.s[1]; sz = f.s[2];
+                op = op * f.coef;
+                pro.out_scales[3 * g + 0] = sx;
+                pro.out_scales[3 * g + 1] = sy;
+                pro.out_scales[3 * g + 2] = sz;
+                pro.out_opac[g] = op;
+            }
+            // the gradient rows this step accumulates into start at zero
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float* z = pro.zero[k];
+                if (z == nullptr) continue;
+                const int w = pro.zero_width[k];
+                for (int j = 0; j < w; ++j) z[g * w + j] = 0.0f;
+            }
+            if (g == 0 && pro.zero_word != nullptr) *pro.zero_word = 0.0f;
+        } else {
+            sx = scales[3 * g + 0]; sy = scales[3 * g + 1]; sz = scales[3 * g + 2];
+            op = opacities[g];
+        }
+        gc = gaussian_cov(q.x, q.y, q.z, q.w, sx, sy, sz, op);
     }
     bool staged = false;  // warp-uniform: the SH rows are staged at first use
     int visible = 0;
@@ -202,7 +238,10 @@ preprocess_forward_views_kernel(const float* __restrict__ means,
         out_color[3 * o + 1] = col.y;
         out_color[3 * o + 2] = col.z;
     }
-    if (vis != nullptr && in && visible > 0) vis[g] += (float)visible;
+    if (vis != nullptr && in) {
+        if (with_prologue) vis[g] = (float)visible;  // the step's first count
+        else if (visible > 0) vis[g] += (float)visible;
+    }
 }
 
 // Walk the Gaussian's clamped tile rectangle row-major and count (or emit)
@@ -778,18 +817,31 @@ mg_status launch_preprocess_forward_views(const float* means, const float* quats
                                           int n_views, int sh_degree, int64_t n,
                                           int64_t view_stride, float* uv, float* conic,
                                           float* depth, float* rxy, int32_t* valid,
-                                          float* color, float* vis, cudaStream_t stream) {
+                                          float* color, float* vis,
+                                          const mg_step_prologue* prologue,
+                                          cudaStream_t stream) {
     if (n == 0) return MG_OK;
+    const mg_step_prologue none{};
     for (int v0 = 0; v0 < n_views; v0 += kMaxViewsPerLaunch) {
         const int nv = std::min(kMaxViewsPerLaunch, n_views - v0);
         ViewCams vc;
         for (int k = 0; k < nv; ++k) vc.c[k] = make_cam_params(cams[v0 + k]);
         const int64_t o = (int64_t)v0 * view_stride;
+        // the prologue runs with the first launch; later launches (more than
+        // 16 views) project the activations it wrote and add to the count
+        const bool pro = prologue != nullptr && v0 == 0;
+        const float* sc = scales;
+        const float* op = opacities;
+        if (prologue != nullptr && v0 > 0) {
+            const bool filt = prologue->filter_3d != nullptr;
+            sc = filt ? prologue->out_scales : prologue->act_scales;
+            op = filt ? prologue->out_opac : prologue->act_opac;
+        }
         preprocess_forward_views_kernel<<<ceil_div(n, kPreBlock), kPreBlock, 0, stream>>>(
-            means, quats, scales, sh_dc, sh_rest, shl, opacities, vc, nv, sh_degree, n,
-            view_stride, reinterpret_cast<float2*>(uv) + o, conic + 3 * o, depth + o,
-            reinterpret_cast<float2*>(rxy) + o, valid + o, color ? color + 3 * o : nullptr,
-            vis);
+            means, quats, sc, sh_dc, sh_rest, shl, op, vc, nv, sh_degree, n, view_stride,
+            reinterpret_cast<float2*>(uv) + o, conic + 3 * o, depth + o,
+            reinterpret_cast<float2*>(rxy) + o, valid + o, color ? color + 3 * o : nullptr, vis,
+            pro ? *prologue : none, pro);
         MG_TRY(check_launch("preprocess_forward_views"));
     }
     return MG_OK;

@@ -72,9 +72,15 @@ __global__ void pack_splats_kernel(const float2* __restrict__ uv,
                                    const float* __restrict__ conic,
                                    const float* __restrict__ opacity,
                                    const float* __restrict__ color, int64_t n,
-                                   float4* __restrict__ out) {
+                                   float4* __restrict__ out, float4* __restrict__ g2d_zero) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
+    if (g2d_zero != nullptr) {  // the view's gradient records, before its backward
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        g2d_zero[3 * i] = z;
+        g2d_zero[3 * i + 1] = z;
+        g2d_zero[3 * i + 2] = z;
+    }
     const float2 m = uv[i];
     const float ca = conic[3 * i], cb = conic[3 * i + 1], cc = conic[3 * i + 2];
     const float op = opacity[i];
@@ -1074,15 +1080,16 @@ extern "C" size_t mg_raster_scratch_bytes(int32_t width, int32_t height, int32_t
 
 extern "C" mg_status mg_pack_splats(const float* uv, const float* conic, const float* opacity,
                                     const float* color, int64_t n, void* splats,
-                                    mg_stream_t stream) {
+                                    float* grad2d_zero, mg_stream_t stream) {
     MG_REQUIRE(n >= 0, "pack_splats: negative count");
     if (n == 0) return MG_OK;
     MG_REQUIRE(uv && conic && opacity && color && splats, "pack_splats: null pointer");
-    MG_REQUIRE((reinterpret_cast<uintptr_t>(splats) & 15u) == 0u,
-               "pack_splats: splats must be 16-byte aligned");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(splats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(grad2d_zero) & 15u) == 0u,
+               "pack_splats: splats and grad2d_zero must be 16-byte aligned");
     pack_splats_kernel<<<ceil_div(n, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         reinterpret_cast<const float2*>(uv), conic, opacity, color, n,
-        static_cast<float4*>(splats));
+        static_cast<float4*>(splats), reinterpret_cast<float4*>(grad2d_zero));
     return check_launch("pack_splats");
 }
 

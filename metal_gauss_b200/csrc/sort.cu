@@ -15,7 +15,6 @@
 // in warp order, tiles in tile order, so equal digits keep their input order
 // and the sort is stable across passes.
 #include <algorithm>
-#include <mutex>
 #include <string>
 
 #include "kernels.cuh"
@@ -51,6 +50,8 @@ __host__ __device__ constexpr int tile_keys() { return kSortThreads * SortTraits
 constexpr uint32_t kFlagAgg = 1u << 30;
 constexpr uint32_t kFlagInc = 2u << 30;
 constexpr uint32_t kCountMask = (1u << 30) - 1u;
+// Look-back rounds a tile waits on an unpublished predecessor before it gives
+// up (a few milliseconds; a healthy predecessor publishes within microseconds).
 constexpr uint32_t kLookbackSpinLimit = 1u << 22;
 #ifndef MG_SORT_LOOKBACK
 #define MG_SORT_LOOKBACK 4
@@ -161,7 +162,7 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
                      int64_t n, int shift, int digit_bits,
                      const uint32_t* __restrict__ digit_offsets,
                      uint32_t* __restrict__ tile_counter, uint32_t* status,
-                     int32_t* err_word) {
+                     int32_t* err_word, uint32_t spin_limit) {
     constexpr int ITEMS = SortTraits<K>::kItems;
     constexpr int TK = tile_keys<K>();
     __shared__ OnesweepSmem<K> sm;
@@ -279,7 +280,7 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
                 if (flag == kFlagInc) { found = true; break; }
             }
             if (found) break;
-            if (k == 0 && ++spins > kLookbackSpinLimit) {
+            if (k == 0 && ++spins > spin_limit) {
                 record_device_error(err_word, DEV_ERR_SORT_LOOKBACK_TIMEOUT);
                 break;
             }
@@ -508,7 +509,7 @@ mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_
         const int db = std::min(pass_bits(bits), bits - shift);
         onesweep_pass_kernel<K><<<s.tiles, kSortThreads, 0, stream>>>(
             kin, vin, kout, vout, n, shift, db, s.hist + p * kRadix, s.tile_counter + p,
-            s.status + (size_t)p * s.tiles * kRadix, err);
+            s.status + (size_t)p * s.tiles * kRadix, err, kLookbackSpinLimit);
         MG_TRY(check_launch("onesweep_pass"));
         std::swap(kin, kout);
         std::swap(vin, vout);
@@ -590,26 +591,16 @@ static_assert(kNoallocBytes == MG_SORT_NOALLOC_SCRATCH_BYTES,
 
 static __device__ __align__(256) unsigned char g_noalloc_sort_scratch[kNoallocBytes];
 
-constexpr int kNoallocMaxDevices = 64;
-unsigned char* g_noalloc_base[kNoallocMaxDevices] = {nullptr};
-std::mutex g_noalloc_mu;
+DeviceSymbolCache g_noalloc_cache;
 
-// Device address of the static array on the current device, looked up once
-// per device with that device current.
+// Device address of the static array on the current device: looked up with
+// that device current, cached per device and context (a device reset, which
+// replaces the context, triggers a fresh lookup).
 mg_status noalloc_base(unsigned char** out) {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices)
-        return fail(MG_ERR_CUDA, "sort_pairs_u32_noalloc: no current CUDA device");
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_base[dev] == nullptr) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_sort_scratch);
-        if (e != cudaSuccess || p == nullptr)
-            return fail(MG_ERR_CUDA, std::string("sort_pairs_u32_noalloc: cudaGetSymbolAddress "
-                                                 "failed: ") + cudaGetErrorString(e));
-        g_noalloc_base[dev] = static_cast<unsigned char*>(p);
-    }
-    *out = g_noalloc_base[dev];
+    std::string why;
+    void* p = device_symbol_address(&g_noalloc_sort_scratch, &g_noalloc_cache, &why);
+    if (p == nullptr) return fail(MG_ERR_CUDA, "sort_pairs_u32_noalloc: " + why);
+    *out = static_cast<unsigned char*>(p);
     return MG_OK;
 }
 
@@ -649,4 +640,79 @@ extern "C" mg_status mg_sort_pairs_u32_noalloc(uint32_t* keys, uint32_t* vals, i
             return check_launch("sort_pairs_u32_noalloc copy");
     }
     return MG_OK;
+}
+
+// ------------------------------------------------ bounded-wait self-test
+//
+// mg_sort_lookback_selftest: one onesweep pass launched as the second tile of
+// a two-tile sort whose first tile never runs, so the look-back waits on a
+// status word that nothing publishes. With a short spin limit the wait runs
+// out, the kernel records DEV_ERR_SORT_LOOKBACK_TIMEOUT in the device error
+// word and returns; every store stays inside the self-test's own buffers.
+namespace mg {
+namespace {
+
+constexpr int64_t kSelftestKeys = 2 * (int64_t)tile_keys<uint32_t>();
+
+struct SelftestScratch {
+    uint32_t *keys_in, *vals_in, *keys_out, *vals_out, *hist, *tile_counter, *status;
+    size_t bytes;
+};
+
+SelftestScratch carve_selftest(void* base) {
+    SelftestScratch s;
+    char* p = static_cast<char*>(base);
+    const size_t arr = align256(sizeof(uint32_t) * kSelftestKeys);
+    s.keys_in = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.vals_in = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.keys_out = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.vals_out = reinterpret_cast<uint32_t*>(p); p += arr;
+    s.hist = reinterpret_cast<uint32_t*>(p); p += align256(sizeof(uint32_t) * kRadix);
+    s.tile_counter = reinterpret_cast<uint32_t*>(p); p += 256;
+    s.status = reinterpret_cast<uint32_t*>(p); p += align256(sizeof(uint32_t) * 2 * kRadix);
+    s.bytes = (size_t)(p - static_cast<char*>(base));
+    return s;
+}
+
+// Keys with digits 0..127 (never a single digit, so the pass does not take
+// its copy-through shortcut), zero digit offsets and look-back words, and the
+// tile counter at 1 so the one launched CTA claims tile 1.
+__global__ void lookback_selftest_init_kernel(SelftestScratch s) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < kSelftestKeys) {
+        s.keys_in[i] = (uint32_t)(i & 0x7f);
+        s.vals_in[i] = (uint32_t)i;
+        s.keys_out[i] = 0u;
+        s.vals_out[i] = 0u;
+    }
+    if (i < kRadix) s.hist[i] = 0u;
+    if (i < 2 * kRadix) s.status[i] = 0u;
+    if (i == 0) *s.tile_counter = 1u;
+}
+
+}  // namespace
+}  // namespace mg
+
+extern "C" size_t mg_sort_lookback_selftest_scratch_bytes(void) {
+    return mg::carve_selftest(nullptr).bytes;
+}
+
+extern "C" mg_status mg_sort_lookback_selftest(uint32_t spin_limit, void* scratch,
+                                               size_t scratch_bytes, mg_stream_t stream) {
+    using namespace mg;
+    MG_REQUIRE(spin_limit >= 1u && spin_limit <= kLookbackSpinLimit,
+               "sort_lookback_selftest: spin_limit must be in 1..2^22");
+    MG_REQUIRE(scratch != nullptr && (reinterpret_cast<uintptr_t>(scratch) & 255u) == 0u,
+               "sort_lookback_selftest: scratch must be 256-byte aligned");
+    const SelftestScratch s = carve_selftest(scratch);
+    MG_REQUIRE(scratch_bytes >= s.bytes, "sort_lookback_selftest: scratch too small");
+    int32_t* err = device_error_word();
+    if (err == nullptr) return fail(MG_ERR_CUDA, "sort_lookback_selftest: no device error word");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    lookback_selftest_init_kernel<<<ceil_div(kSelftestKeys, 256), 256, 0, st>>>(s);
+    MG_TRY(check_launch("lookback_selftest_init"));
+    onesweep_pass_kernel<uint32_t><<<1, kSortThreads, 0, st>>>(
+        s.keys_in, s.vals_in, s.keys_out, s.vals_out, kSelftestKeys, 0, kRadixBits, s.hist,
+        s.tile_counter, s.status, err, spin_limit);
+    return check_launch("lookback_selftest_pass");
 }

@@ -1,13 +1,18 @@
 """Data-parallel plumbing for the batched trainer: which views a rank renders
-and the one gradient exchange per step.
+and the collectives of a step.
 
 The reference has no distributed code (one view per step on one device,
 train.py:352-402). Here a step's batch of views is split into equal
-contiguous shards, one per rank; every rank holds the full Gaussian set; after
-its views are back-propagated the flat gradient buffer -- which also carries
-each Gaussian's per-rank visibility count -- is summed across ranks in one
-all-reduce (NCCL over NVLink on the GPUs, gloo in the CPU tests), together
-with the loss.
+contiguous shards, one per rank, and every rank holds the full Gaussian set.
+After its views are back-propagated, the optimizer is sharded (ZeRO-1, the
+default with several ranks): the visibility counts and the loss (the tail of
+the flat gradient buffer) are all-reduced, the parameter gradient is
+reduce-scattered so each rank holds the sum of its own contiguous chunk, each
+rank runs Adam on that chunk only, and the updated parameters are
+all-gathered in place. `exchange` (one all-reduce of the whole gradient, every
+rank then running the full Adam) is the replicated alternative. NCCL over
+NVLink on the GPUs; gloo in the CPU tests, which has no reduce-scatter, sums
+with an all-reduce instead.
 """
 
 from __future__ import annotations

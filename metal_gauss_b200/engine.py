@@ -143,7 +143,9 @@ class _BatchBinning:
         self.emit = torch.empty(0, **u8)
         self.ids = torch.empty(0, dtype=torch.int32, device=device)
         self.offsets = torch.empty(0, dtype=torch.int32, device=device)
-        self.totals = torch.zeros(66, dtype=torch.int64, device=device)
+        # per-view pair totals, the batch total, the overflow flag and the
+        # device error word (copied in just before the one host read)
+        self.totals = torch.zeros(67, dtype=torch.int64, device=device)
         self.bases: list[int] = []
 
     @staticmethod
@@ -175,8 +177,14 @@ class _BatchBinning:
     def read_totals(self, V: int) -> list[int] | None:
         """The views' pair totals (one device->host read), or None when the
         batch has to be binned one view at a time (a view's depth range
-        outgrew the batch keys, or 2^30 - 1 pairs, the tile sort's limit)."""
-        t = self.totals[:V + 2].tolist()
+        outgrew the batch keys, or 2^30 - 1 pairs, the tile sort's limit).
+        The device error word rides on the same read: a kernel that gave up
+        a bounded wait or met a bad index since the last check raises
+        DeviceError here, before its results are used."""
+        _lib.call("mg_peek_device_error", ptr(self.totals[V + 2:V + 3]), _lib.stream())
+        t = self.totals[:V + 3].tolist()
+        if t[V + 2]:
+            _lib.raise_device_error(t[V + 2], "binning")
         if t[V + 1] or t[V] >= 2 ** 30 - 1:
             return None
         self.bases = [0] * V
@@ -321,7 +329,9 @@ class Trainer:
         self._bufs: dict[tuple[int, int], _ImageBuffers] = {}
         self._batch: _ViewBatch | None = None
         self._states: list[_ViewState] = []
-        self._totals = torch.zeros(64, dtype=torch.int64, device=self.device)
+        # per-view pair totals of the one-view-at-a-time binning; the last
+        # slot receives the device error word before the host reads them
+        self._totals = torch.zeros(MAX_VIEWS_PER_STEP + 1, dtype=torch.int64, device=self.device)
         # one batch binning per chunk of a step's views
         self._bbs: list[_BatchBinning] = []
         self._cams: dict[int, _lib.Camera] = {}
@@ -460,25 +470,56 @@ class Trainer:
                   float(lr), float(weight), float(opacity_gate),
                   self._mcmc_seed(seed) ^ 0x9E3779B97F4A7C15, None, _lib.stream())
 
-    def _activate(self) -> None:
-        """The forward's scales and opacities: exp / sigmoid of the
-        parameters (train.py:221-222), then the 3D filter when one is set
-        (train.py:223-227)."""
+    def _filter_tensor(self) -> torch.Tensor | None:
+        """The 3D filter as a contiguous (N,) device tensor (None when unset),
+        with the pre-filter activation buffers the gradient chain needs."""
         if self.filter_3d is None:
-            torch.exp(self.param("log_scales"), out=self.scales)
-            torch.sigmoid(self.param("logit_opac"), out=self.opac)
-            return
-        if self._scales_act.shape != self.scales.shape:
-            self._scales_act = torch.empty_like(self.scales)
-            self._opac_act = torch.empty_like(self.opac)
-        torch.exp(self.param("log_scales"), out=self._scales_act)
-        torch.sigmoid(self.param("logit_opac"), out=self._opac_act)
+            return None
         f = self.filter_3d.to(self.device, torch.float32).contiguous()
         if f.numel() != self.n:
             raise ValueError(f"filter_3d has {f.numel()} values for {self.n} Gaussians")
         self.filter_3d = f
+        if self._scales_act.shape != self.scales.shape:
+            self._scales_act = torch.empty_like(self.scales)
+            self._opac_act = torch.empty_like(self.opac)
+        return f
+
+    def _activate(self) -> None:
+        """The forward's scales and opacities: exp / sigmoid of the
+        parameters (train.py:221-222), then the 3D filter when one is set
+        (train.py:223-227). `train_step` does the same inside the projection
+        kernel (`_prologue`); this form serves callers that drive
+        `forward_backward_views` themselves."""
+        f = self._filter_tensor()
+        if f is None:
+            torch.exp(self.param("log_scales"), out=self.scales)
+            torch.sigmoid(self.param("logit_opac"), out=self.opac)
+            return
+        torch.exp(self.param("log_scales"), out=self._scales_act)
+        torch.sigmoid(self.param("logit_opac"), out=self._opac_act)
         _lib.call("mg_apply_3d_filter", ptr(self._scales_act), ptr(self._opac_act), ptr(f), self.n,
                   ptr(self.scales), ptr(self.opac), _lib.stream())
+
+    def _prologue(self) -> "_lib.StepPrologue":
+        """The start of a step for the projection kernel (mg_step_prologue):
+        the activations (through the 3D filter when one is set), the
+        geometry gradient rows and the loss set to zero, the visibility
+        count written rather than added."""
+        f = self._filter_tensor()
+        pro = _lib.StepPrologue()
+        pro.log_scales = ptr(self.param("log_scales"))
+        pro.logit_opac = ptr(self.param("logit_opac"))
+        if f is None:
+            pro.act_scales, pro.act_opac = ptr(self.scales), ptr(self.opac)
+        else:
+            pro.filter_3d = ptr(f)
+            pro.act_scales, pro.act_opac = ptr(self._scales_act), ptr(self._opac_act)
+            pro.out_scales, pro.out_opac = ptr(self.scales), ptr(self.opac)
+        for k, name in enumerate(("means", "quats", "log_scales", "logit_opac")):
+            pro.zero[k] = ptr(self.grad(name))
+            pro.zero_width[k] = dict(SEGMENTS)[name]
+        pro.zero_word = ptr(self.loss)
+        return pro
 
     def visibility_count(self) -> torch.Tensor:
         return self.G[self.vis_offset:self.vis_offset + self.n]
@@ -540,12 +581,14 @@ class Trainer:
     def _state(self, v: int) -> _ViewState:
         return self._states[v]
 
-    def _project_views(self, views) -> None:
+    def _project_views(self, views, begin_step: bool = False) -> None:
         """Phase A, first half: projection + SH colour of every view in one
         launch (parameters and SH rows read once), adding each Gaussian's
-        count of valid views to the visibility count."""
+        count of valid views to the visibility count. With `begin_step` the
+        same launch runs the step's prologue (`_prologue`)."""
         b = self._batch
         cams = _views_array([self._camera(view) for view in views])
+        pro = _lib.C.byref(self._prologue()) if begin_step else None
         ev = self._begin("preprocess_fwd")
         _lib.call("mg_preprocess_forward_views", ptr(self.param("means")),
                   ptr(self.param("quats")), ptr(self.scales), ptr(self.param("sh_dc")),
@@ -553,7 +596,7 @@ class Trainer:
                   _lib.C.cast(cams, _lib.C.c_void_p), len(views), self.sh_degree, self.active,
                   self.n,
                   ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color),
-                  ptr(self.visibility_count()), _lib.stream())
+                  ptr(self.visibility_count()), pro, _lib.stream())
         if self.antialias:
             _lib.call("mg_antialias_opacity_views", ptr(b.conic), ptr(self.opac), self.active,
                       len(views), self.n, 0.3, ptr(b.opac), _lib.stream())
@@ -593,7 +636,11 @@ class Trainer:
                 return totals, bb
         for i, view in enumerate(chunk):
             self._prepare(first + i, view)
-        return [int(x) for x in self._totals[first:first + V].tolist()], None
+        _lib.call("mg_peek_device_error", ptr(self._totals[-1:]), _lib.stream())
+        t = self._totals.tolist()
+        if t[-1]:
+            _lib.raise_device_error(t[-1], "binning")
+        return [int(x) for x in t[first:first + V]], None
 
     def _prepare(self, v: int, view) -> None:
         """Phase A, second half, for view v: tile counts, depth sort and the
@@ -655,8 +702,8 @@ class Trainer:
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
         ev = self._begin("pack")
         _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(self._opacity(st)),
-                                    ptr(st.color), n,
-                                    ptr(b.splats), s), "pack_splats")
+                                    ptr(st.color), n, ptr(b.splats), ptr(st.grad2d), s),
+                   "pack_splats")
         self._end(ev)
         # tile walk lengths only when the instrumented pass asks for them
         work = b.tile_work if self.stage_events is not None else None
@@ -673,7 +720,6 @@ class Trainer:
             ptr(b.rgb), ptr(target), ptr(self.window), H, W, self.w_l1, self.w_ssim, scale,
             ptr(b.grad_rgb), ptr(self.loss), ptr(b.loss_scratch), b.loss_scratch.numel(), s),
             "l1_ssim_loss")
-        st.grad2d.zero_()
         self._end(ev)
         ev = self._begin("raster_bwd")
         _lib.check(L.mg_rasterize_backward(
@@ -683,13 +729,18 @@ class Trainer:
         self._end(ev)
         return ViewStats(pairs=m)
 
-    def forward_backward_views(self, views, targets, scale: float) -> list[ViewStats]:
+    def forward_backward_views(self, views, targets, scale: float,
+                               begin_step: bool = False) -> list[ViewStats]:
         """Render this rank's views: scale * each loss is added into
         self.loss, scale * the views' gradients of means, quats, log-scales and
         opacity logits are added into self.G and the views' SH gradients are
         written into it (the SH adjoint covers all of a call's views at once
-        and overwrites its rows; `train_step` zeroes the rest of G first). One
-        device->host read per binning chunk (its views' pair totals)."""
+        and overwrites its rows). With `begin_step` the projection kernel
+        first forms the activations and sets the geometry gradient rows, the
+        visibility count and the loss to zero (what `train_step` uses);
+        otherwise the caller has run `_activate` and the call adds to G. One
+        device->host read per binning chunk (its views' pair totals, with the
+        device error word)."""
         V = len(views)
         if V > MAX_VIEWS_PER_STEP:
             raise ValueError(f"a step takes at most {MAX_VIEWS_PER_STEP} views per rank, got "
@@ -697,7 +748,7 @@ class Trainer:
         if V > self._totals.numel():
             self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
         self._ensure_views(V)
-        self._project_views(views)
+        self._project_views(views, begin_step)
         streams = self._phase_b_streams(V)
         main = torch.cuda.current_stream(self.device)
         C = V if self.bin_chunk <= 0 else min(V, int(self.bin_chunk))
@@ -804,14 +855,10 @@ class Trainer:
         batch-mean loss as a device tensor (1,), all-reduced across ranks."""
         world = self._world_size()
         gb = global_batch or len(views) * world
-        ev = self._begin("activations")
-        self._activate()
-        # the SH rows are overwritten by the SH adjoint; the geometry rows and
-        # the visibility/loss tail accumulate
-        self.G[:self.offsets["sh_dc"]].zero_()
-        self.G[self.vis_offset:].zero_()  # visibility counts and the loss
-        self._end(ev)
-        self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb)
+        # the activations and the zeroing of the accumulated gradient rows,
+        # visibility counts and loss run inside the projection kernel; the SH
+        # rows are overwritten by the SH adjoint
+        self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb, begin_step=True)
         if self.opac_reg or self.scale_reg:
             self._regularize(world)
         if world > 1 and self.shard_optimizer:
@@ -846,18 +893,28 @@ class Trainer:
     def _world_size(self) -> int:
         return dp.world_size(self.group)
 
+    def check_device_error(self) -> None:
+        """Synchronising check of the device error word; raises
+        _lib.DeviceError when a kernel recorded a failure. Every step already
+        checks the word for free at its pair-total read (the failures of the
+        previous step's later kernels and of this step's binning); this one
+        covers the last step too."""
+        _lib.check_device_error("training step")
+
     # ------------------------------------------------------------ counters
 
     def bytes_per_step(self, views, stats: list[ViewStats] | None = None) -> float:
-        """Algorithmic HBM bytes of one step on this rank (the compulsory
-        traffic of the dataflow; see the per-stage table in DESIGN.md)."""
+        """Algorithmic HBM bytes of one step on this rank: the compulsory
+        traffic of the dataflow, every input read once and every output
+        written once, stage by stage as commented below."""
         stats = stats or self.last_stats
         n = self.n
         nv = float(self.visibility_count().gt(0).sum()) if self.selective else n
         V = len(stats)
-        # multi-view preprocess: parameters + SH rows once, 48 B out per view,
-        # visibility read-modify-write
-        total = (44.0 + 192.0 + 8.0) * n + 48.0 * V * n
+        # multi-view preprocess with the step prologue: parameters + SH rows
+        # once, activations written (16 B), 11 gradient floats zeroed (44 B),
+        # the visibility count written (4 B), 48 B out per view
+        total = (44.0 + 192.0 + 16.0 + 44.0 + 4.0) * n + 48.0 * V * n
         # multi-view projection adjoint: parameters once; per view the gradient
         # record, valid flag, colour and gated colour gradient; one
         # read-modify-write of the 11 gradient floats
@@ -875,7 +932,7 @@ class Trainer:
                                                        * (v.height // self.tile + 1))) / 8)
             total += 4 * M                          # ranges
             Wk = st.walked if st.walked else M
-            total += (36 + 48) * n                  # pack splat records
+            total += (36 + 48 + 48) * n             # pack splat records, zero grad records
             total += 52 * Wk + 24 * P               # raster fwd (walked id + record)
             total += 40 * P + 36 * P                # fused loss (2 kernels)
             total += 52 * Wk + 36 * P + 48 * n      # raster bwd (+ gradient record)
@@ -949,5 +1006,6 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
             trainer.grow(int(start_active + (grow_to - start_active) * frac))
         if callback is not None:
             callback(step, losses[-1])
+    trainer.check_device_error()
     return losses
 

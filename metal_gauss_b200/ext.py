@@ -245,7 +245,7 @@ def pack_splats(uv, conic, opacity, color) -> torch.Tensor:
     n = uv.shape[0]
     splats = _empty((n, _lib.SPLAT_FLOATS), uv)
     _lib.call("mg_pack_splats", ptr(uv), ptr(conic), ptr(opacity), ptr(color), n, ptr(splats),
-              _lib.stream())
+              None, _lib.stream())
     return splats
 
 

@@ -70,7 +70,8 @@ class Renderer:
         self._bufs: dict = {}
         # per-view opacity after the antialias compensation (view-major)
         self._opac_view = torch.empty(batch if antialias else 0, n, **f32)
-        self._totals = torch.zeros(batch, dtype=torch.int64, device=self.device)
+        # pair totals of the one-view-at-a-time binning, then the error word
+        self._totals = torch.zeros(batch + 1, dtype=torch.int64, device=self.device)
         self._bb = _BatchBinning(self.device)
         self.batch_binning = True
         # views are packed and rasterised on this many streams in turn (one
@@ -99,11 +100,17 @@ class Renderer:
             self._bufs[(W, H, slot)] = b
         return b
 
-    def render(self, views) -> list[tuple[torch.Tensor, torch.Tensor]]:
-        """[(rgb (H,W,3), alpha (H,W))] device tensors, one pair per view."""
+    def render(self, views, check: bool = True) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        """[(rgb (H,W,3), alpha (H,W))] device tensors, one pair per view.
+        Each batch's pair-total read also checks the device error word; with
+        `check` (default) one more synchronising read after the last batch
+        covers its kernels, so a failed bounded wait or bad index raises
+        _lib.DeviceError instead of returning wrong frames."""
         out = []
         for i in range(0, len(views), self.batch):
             out += self._render_batch(views[i:i + self.batch])
+        if check:
+            _lib.check_device_error("render")
         return out
 
     def _render_batch(self, views):
@@ -117,7 +124,7 @@ class Renderer:
             ptr(self.means), ptr(self.quats), ptr(self.scales), ptr(self.sh_dc),
             ptr(self.sh_rest), _lib.SH_SPLIT, ptr(self.opac), _lib.C.cast(cams, _lib.C.c_void_p),
             len(views), self.sh_degree, n, n, ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy),
-            ptr(b.valid), ptr(b.color), None, s), "preprocess_forward_views")
+            ptr(b.valid), ptr(b.color), None, None, s), "preprocess_forward_views")
         V = len(views)
         if self.antialias:
             # every view's compensated opacities in one launch, before binning
@@ -147,7 +154,11 @@ class Renderer:
                     ptr(st.valid), ptr(st.depth), n, view.width, view.height, self.tile,
                     self.saturation_cut, ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(),
                     s), "bin_prepare")
-            totals = self._totals[:V].tolist()
+            _lib.call("mg_peek_device_error", ptr(self._totals[-1:]), s)
+            t = self._totals.tolist()
+            if t[-1]:
+                _lib.raise_device_error(t[-1], "render binning")
+            totals = t[:V]
         bg = None if self.background is None else (_lib.C.c_float * 3)(*self.background)
         bgp = None if bg is None else _lib.C.cast(bg, _lib.C.c_void_p)
         k = min(int(self.view_streams), V)
@@ -209,7 +220,7 @@ class Renderer:
                                      b.emit.numel(), s), "bin_emit")
             ids, offsets = b.ids, b.offsets
         _lib.check(L.mg_pack_splats(ptr(st.uv), ptr(st.conic), ptr(opac), ptr(st.color),
-                                    n, ptr(b.splats), s), "pack_splats")
+                                    n, ptr(b.splats), None, s), "pack_splats")
         _lib.check(L.mg_rasterize_forward(
             ptr(b.splats), ptr(ids), ptr(offsets), m, W, H, self.tile, tiles_x, bgp,
             ptr(rgb), ptr(alpha), None, None, None, ptr(b.raster), b.raster.numel(), s),

@@ -50,6 +50,9 @@ class _Recorder:
         self.active = target
         return target
 
+    def check_device_error(self):
+        self.events.append(("device_error_check", len(self.steps)))
+
 
 def _targets(n):
     return [np.full((3, 4, 3), 255, np.uint8) for _ in range(n)]
@@ -119,6 +122,9 @@ def test_filter_noise_relocation_and_growth_schedule():
     grow = [(e[1], e[2]) for e in tr.events if e[0] == "grow"]
     # growth on relocation steps up to grow_until, toward grow_to linearly
     assert grow == [(2, 125), (4, 150), (6, 175), (8, 200)]
+    # the run ends with a synchronising check of the device error word, so a
+    # failure in the last step's kernels is not returned as a result
+    assert tr.events[-1] == ("device_error_check", 10)
 
 
 def test_a_step_refuses_more_views_than_the_adjoint_table_holds():

@@ -58,7 +58,7 @@ def _forward_views(d, views, vis=None):
               ptr(d["sh_dc"]), ptr(d["sh_rest"]), _lib.SH_SPLIT, ptr(d["opac"]),
               _lib.C.cast(cams, _lib.C.c_void_p), V, 3, n, n, ptr(out["uv"]), ptr(out["conic"]),
               ptr(out["depth"]), ptr(out["rxy"]), ptr(out["valid"]), ptr(out["color"]), ptr(vis),
-              _lib.stream())
+              None, _lib.stream())
     return out
 
 

@@ -54,6 +54,24 @@ def test_noalloc_sort_matches_the_scratch_entry_point_twice(cuda):
     assert ext.device_error() == 0
 
 
+@pytest.mark.parametrize("n,bits", [(MAX_N, 32), (200_003, 8)])
+def test_noalloc_sort_at_its_maximum_and_with_one_pass(cuda, n, bits):
+    """Exactly MAX_N pairs (the static look-back region used to its last
+    word), and an 8-bit key (one pass: the result comes back from the static
+    buffers)."""
+    keys, vals = _case(n, bits, 5 + bits, 1 << 31)
+    k = torch.from_numpy(keys.view(np.int32)).cuda()
+    v = torch.from_numpy(vals.view(np.int32)).cuda()
+    _noalloc(k, v, bits)
+    ref_k, ref_v = ext.sort_pairs(torch.from_numpy(keys.view(np.int32)).cuda(),
+                                  torch.from_numpy(vals.view(np.int32)).cuda(), bits)
+    torch.cuda.synchronize()
+    assert torch.equal(k, ref_k) and torch.equal(v, ref_v)
+    order = np.argsort(keys, kind="stable")
+    assert np.array_equal(v.cpu().numpy().view(np.uint32), vals[order])
+    assert ext.device_error() == 0
+
+
 def test_noalloc_sort_rejects_sizes_beyond_its_maximum(cuda):
     lib = _lib.load()
     k = torch.zeros(1, dtype=torch.int32, device="cuda")
