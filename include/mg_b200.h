@@ -146,6 +146,20 @@ mg_status mg_preprocess_forward_views(
     float* depth, float* rxy, int32_t* valid, float* color, float* visibility,
     const mg_step_prologue* prologue, mg_stream_t stream);
 
+/* The SH colour half of mg_preprocess_forward_views (preprocess.metal:
+ * 203-221), for a projection that ran with sh_dc = NULL and sh_degree = -1:
+ * color row v * view_stride + g = the SH colour of Gaussian g seen from
+ * camera centre v (+0.5, clamped at 0), or 0 where valid (from that
+ * projection) is 0. cam_centers: n_views x 3 host floats, n_views <= 64.
+ * The arithmetic is the fused projection's, so the colours are identical.
+ * The training engine uses it on several GPUs, so that the next step's
+ * projection and binning can run while the SH rows are still being
+ * gathered. No reference counterpart. */
+mg_status mg_sh_colour_views(const float* means, const float* sh_dc, const float* sh_rest,
+                             mg_sh_layout shl, const float* cam_centers, int32_t n_views,
+                             int32_t sh_degree, int64_t n, int64_t view_stride,
+                             const int32_t* valid, float* color, mg_stream_t stream);
+
 /* Replaces preprocess_backward (rasterize.mm:286-327, kernel
  * preprocess.metal:223-411). The incoming gradients are read through row
  * strides (in floats) so they may point into a packed MG_G2D record
@@ -529,12 +543,20 @@ typedef struct mg_adam_segment {
 } mg_adam_segment;
 /* row_scratch (selective mode, optional): `rows` floats the entry point uses
  * to form each visible row's bias correction once instead of once per
- * thread; NULL forms it in place. */
+ * thread; NULL forms it in place. flags: 0, or a step's update split over
+ * several calls (e.g. one per parameter group, on different streams):
+ *   MG_ADAM_KEEP_STEPS: do not advance `steps` (another call of the same step
+ *     does);
+ *   MG_ADAM_ROW_FACTORS_READY: row_scratch already holds this step's factors
+ *     (formed by an earlier call of the same step); neither form them again
+ *     nor read visible_count's values. */
+#define MG_ADAM_ROW_FACTORS_READY 1
+#define MG_ADAM_KEEP_STEPS 2
 mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
                         int64_t rows, const mg_adam_segment* segments,
                         int32_t n_segments, float b1, float b2, float eps,
                         const float* visible_count, float* steps, int64_t step,
-                        float* row_scratch, mg_stream_t stream);
+                        float* row_scratch, int32_t flags, mg_stream_t stream);
 
 /* The MCMC regularisers of the reference's training loss (train.py:393-398):
  *   loss += c_opac * mean(sigmoid(logit_opac[:n])) + c_scale * mean(exp(log_scales[:n, 0..2]))
@@ -581,6 +603,18 @@ mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
                           float w_ssim, float scale, float* grad_x,
                           float* loss_dev, void* scratch, size_t scratch_bytes,
                           mg_stream_t stream);
+
+/* mg_l1_ssim_loss with an 8-bit target image y (H,W,3) uint8, read as
+ * y / 255 in float32 with IEEE division -- the reference's trainer holds its
+ * images as bytes and divides them by 255 (`v.image.to(device).float() /
+ * 255.0`, train.py:385) -- so a trainer can keep its targets as the bytes it
+ * loaded and copy a quarter of the bytes per step. (torch's CUDA division by
+ * a scalar multiplies by the rounded reciprocal instead, which can differ in
+ * the last bit.) */
+mg_status mg_l1_ssim_loss_u8(const float* x, const uint8_t* y, const float* w,
+                             int32_t height, int32_t width, float w_l1, float w_ssim,
+                             float scale, float* grad_x, float* loss_dev, void* scratch,
+                             size_t scratch_bytes, mg_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Mip-Splatting 3D filter                                                  */

@@ -21,6 +21,7 @@ LIB_PATH = build_native.LIB
 G2D_STRIDE = 12
 G2D_UV, G2D_OPACITY, G2D_ABSUV, G2D_CONIC, G2D_COLOR = 0, 2, 3, 4, 8
 SPLAT_FLOATS = 12        # MG_SPLAT_FLOATS: one packed splat record
+ADAM_ROW_FACTORS_READY, ADAM_KEEP_STEPS = 1, 2   # mg_adam_multi flags
 RASTER_SEGMENT = 256     # MG_RASTER_SEGMENT
 
 
@@ -87,6 +88,7 @@ SIGNATURES = {
     "mg_preprocess_forward_views": (i32, [vp, vp, vp, vp, vp, ShLayout, vp, vp, i32, i32, i64,
                                           i64, vp, vp, vp, vp, vp, vp, vp,
                                           C.POINTER(StepPrologue), vp]),
+    "mg_sh_colour_views": (i32, [vp, vp, vp, ShLayout, vp, i32, i32, i64, i64, vp, vp, vp]),
     "mg_preprocess_backward_views": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i64, i64, vp,
                                            vp, vp, vp, vp, vp, vp]),
     "mg_bin_count": (i32, [vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]),
@@ -126,7 +128,7 @@ SIGNATURES = {
                                      vp]),
     "mg_selective_adam_advance_steps": (i32, [vp, vp, i64, i64, vp]),
     "mg_adam_multi": (i32, [vp, vp, vp, vp, i64, C.POINTER(AdamSegment), i32, f32, f32, f32, vp,
-                            vp, i64, vp, vp]),
+                            vp, i64, vp, i32, vp]),
     "mg_ssim_stack_blur_h": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "mg_ssim_blur15": (i32, [vp, vp, i32, i32, i32, vp, vp]),
     "mg_ssim_tail_forward": (i32, [vp, i32, i32, vp, vp]),
@@ -134,6 +136,7 @@ SIGNATURES = {
     "mg_ssim_chain_backward": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "mg_l1_ssim_scratch_bytes": (sz, [i32, i32]),
     "mg_l1_ssim_loss": (i32, [vp, vp, vp, i32, i32, f32, f32, f32, vp, vp, vp, sz, vp]),
+    "mg_l1_ssim_loss_u8": (i32, [vp, vp, vp, i32, i32, f32, f32, f32, vp, vp, vp, sz, vp]),
     "mg_read_device_error": (i32, [C.POINTER(i32), vp]),
     "mg_peek_device_error": (i32, [vp, vp]),
     "mg_sort_lookback_selftest_scratch_bytes": (sz, []),

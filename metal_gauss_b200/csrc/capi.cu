@@ -285,6 +285,26 @@ extern "C" mg_status mg_preprocess_forward_views(
                                            reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" mg_status mg_sh_colour_views(const float* means, const float* sh_dc,
+                                        const float* sh_rest, mg_sh_layout shl,
+                                        const float* cam_centers, int32_t n_views,
+                                        int32_t sh_degree, int64_t n, int64_t view_stride,
+                                        const int32_t* valid, float* color,
+                                        mg_stream_t stream) {
+    MG_REQUIRE(n_views >= 0 && n_views <= 64, "sh_colour_views: 0..64 views");
+    MG_REQUIRE(sh_degree >= 0 && sh_degree <= 3, "sh_colour_views: sh_degree must be 0..3");
+    if (n == 0 || n_views == 0) return MG_OK;
+    MG_REQUIRE(view_stride >= n, "sh_colour_views: view_stride below n");
+    MG_REQUIRE(means && sh_dc && sh_rest && cam_centers && valid && color,
+               "sh_colour_views: null pointer");
+    const bool fused = shl.stride_dc == 16 && shl.stride_rest == 16 && shl.offset_rest == 1;
+    const bool split = shl.stride_dc == 1 && shl.stride_rest == 15 && shl.offset_rest == 0;
+    MG_REQUIRE(fused || split, "SH must be either one (N,16,3) tensor or (N,1,3)+(N,15,3)");
+    return launch_sh_colour_views(means, sh_dc, sh_rest, shl, cam_centers, n_views, sh_degree, n,
+                                  view_stride, valid, color,
+                                  reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" mg_status mg_bin_count(const float* uv, const float* rxy, const float* conic,
                                   const float* opacity, const int32_t* valid, int64_t n,
                                   int32_t width, int32_t height, int32_t tile, int32_t tiles_x,

@@ -23,6 +23,12 @@ mg_status launch_preprocess_forward_views(const float* means, const float* quats
                                           float* color, float* vis,
                                           const mg_step_prologue* prologue,
                                           cudaStream_t stream);
+// The colour of every view for a projection run without it (n_views <= 64;
+// cam_centers: n_views x 3 host floats).
+mg_status launch_sh_colour_views(const float* means, const float* sh_dc, const float* sh_rest,
+                                mg_sh_layout shl, const float* cam_centers, int n_views,
+                                int sh_degree, int64_t n, int64_t view_stride,
+                                const int32_t* valid, float* color, cudaStream_t stream);
 mg_status launch_bin_count(const float* uv, const float* rxy, const float* conic,
                            const float* opacity, const int32_t* valid, int64_t n,
                            int W, int H, int tile, int tiles_x, int tiles_y,

@@ -259,13 +259,17 @@ extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
                                    const mg_adam_segment* segments, int32_t n_segments,
                                    float b1, float b2, float eps, const float* visible_count,
                                    float* steps, int64_t step, float* row_scratch,
-                                   mg_stream_t stream) {
+                                   int32_t flags, mg_stream_t stream) {
     MG_REQUIRE(n_segments >= 0 && n_segments <= MG_MAX_ADAM_SEGMENTS &&
                    (n_segments == 0 || segments != nullptr),
                "adam_multi: 0..MG_MAX_ADAM_SEGMENTS segments");
     MG_REQUIRE(p && g && m && v, "adam_multi: null pointer");
     MG_REQUIRE(visible_count == nullptr || steps != nullptr, "adam_multi: selective mode needs steps");
     MG_REQUIRE(visible_count != nullptr || step >= 1, "adam_multi: dense mode needs step >= 1");
+    MG_REQUIRE((flags & ~(MG_ADAM_ROW_FACTORS_READY | MG_ADAM_KEEP_STEPS)) == 0,
+               "adam_multi: unknown flags");
+    MG_REQUIRE(!(flags & MG_ADAM_ROW_FACTORS_READY) || row_scratch != nullptr,
+               "adam_multi: MG_ADAM_ROW_FACTORS_READY needs row_scratch");
     if (rows == 0) return MG_OK;
     AdamSegments segs;
     int64_t max_count = 1;
@@ -288,20 +292,24 @@ extern "C" mg_status mg_adam_multi(float* p, const float* g, float* m, float* v,
     const float w1 = (float)(1.0 - (double)b1), w2 = (float)(1.0 - (double)b2);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int gx = (int)std::min<int64_t>((max_count + 1023) / 1024, 148 * 8);
-    if (n_segments > 0) {
-        const float* rowf = nullptr;
-        if (visible_count && row_scratch) {
+    // the row factors are formed even with no segment here: a later call of
+    // the same step (MG_ADAM_ROW_FACTORS_READY) may use them
+    const float* rowf = nullptr;
+    if (visible_count && row_scratch) {
+        if (!(flags & MG_ADAM_ROW_FACTORS_READY)) {
             row_factor_kernel<<<ceil_div(rows, 256), 256, 0, st>>>(visible_count, steps, rows, b1,
                                                                     b2, row_scratch);
             MG_TRY(check_launch("adam_multi row factors"));
-            rowf = row_scratch;
         }
+        rowf = row_scratch;
+    }
+    if (n_segments > 0) {
         adam_multi_kernel<<<dim3(std::max(gx, 1), n_segments), 256, 0, st>>>(
             p, g, m, v, rows, segs, b1, b2, eps, w1, w2, visible_count, steps, rowf,
             (float)bc1, (float)sq);
         MG_TRY(check_launch("adam_multi"));
     }
-    if (visible_count) {
+    if (visible_count && !(flags & MG_ADAM_KEEP_STEPS)) {
         advance_steps_count_kernel<<<ceil_div(rows, 256), 256, 0, st>>>(steps, visible_count, rows);
         return check_launch("adam_multi steps");
     }

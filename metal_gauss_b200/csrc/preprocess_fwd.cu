@@ -244,6 +244,52 @@ preprocess_forward_views_kernel(const float* __restrict__ means,
     }
 }
 
+// The colour half of preprocess_forward_views_kernel, for a projection that
+// ran without it (SH pointers null): view v's colour of Gaussian g from its
+// SH rows and the direction from camera centre v, or 0 where valid is 0.
+// The rows are staged per warp and the arithmetic is sh_colour's, so the
+// colours are bit-identical to the fused projection's.
+constexpr int kMaxColourViews = 64;
+struct ColourCentres {
+    float c[kMaxColourViews][3];
+};
+
+__global__ void __launch_bounds__(kPreBlock)
+sh_colour_views_kernel(const float* __restrict__ means, const float* __restrict__ sh_dc,
+                       const float* __restrict__ sh_rest, mg_sh_layout shl, ColourCentres cc,
+                       int n_views, int sh_degree, int64_t n, int64_t view_stride,
+                       const int32_t* __restrict__ valid, float* __restrict__ out_color) {
+    __shared__ float s_rest[kPreBlock / 32][32 * 15 * 3];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t g = (int64_t)blockIdx.x * kPreBlock + threadIdx.x;
+    const int64_t g0 = g - lane;
+    const bool in = g < n;
+    const int nb = (sh_degree + 1) * (sh_degree + 1);
+    float mx = 0.f, my = 0.f, mz = 0.f;
+    if (in) { mx = means[3 * g + 0]; my = means[3 * g + 1]; mz = means[3 * g + 2]; }
+    bool staged = false;
+    for (int v = 0; v < n_views; ++v) {
+        const int64_t o = (int64_t)v * view_stride + g;
+        const bool ok = in && valid[o] != 0;
+        const unsigned any_ok = __ballot_sync(0xffffffffu, ok);
+        if (!staged && any_ok != 0u && nb > 1) {
+            stage_rows(sh_rest, g0, n, shl.stride_rest, shl.offset_rest, nb - 1, s_rest[wib],
+                       lane);
+            __syncwarp();
+            staged = true;
+        }
+        if (!in) continue;
+        float3 col = make_float3(0.f, 0.f, 0.f);
+        if (ok)
+            col = sh_colour(sh_degree, nb, mx - cc.c[v][0], my - cc.c[v][1], mz - cc.c[v][2],
+                            sh_dc + g * (int64_t)shl.stride_dc * 3,
+                            s_rest[wib] + lane * (nb - 1) * 3);
+        out_color[3 * o + 0] = col.x;
+        out_color[3 * o + 1] = col.y;
+        out_color[3 * o + 2] = col.z;
+    }
+}
+
 // Walk the Gaussian's clamped tile rectangle row-major and count (or emit)
 // the tiles that pass the exact ellipse test (binning.metal:46-90).
 // Saturation cut (engine binning). A tile's pairs behind the depth at which
@@ -845,6 +891,19 @@ mg_status launch_preprocess_forward_views(const float* means, const float* quats
         MG_TRY(check_launch("preprocess_forward_views"));
     }
     return MG_OK;
+}
+
+mg_status launch_sh_colour_views(const float* means, const float* sh_dc, const float* sh_rest,
+                                mg_sh_layout shl, const float* cam_centers, int n_views,
+                                int sh_degree, int64_t n, int64_t view_stride,
+                                const int32_t* valid, float* color, cudaStream_t stream) {
+    if (n == 0 || n_views == 0) return MG_OK;
+    ColourCentres cc;
+    for (int v = 0; v < n_views; ++v)
+        for (int k = 0; k < 3; ++k) cc.c[v][k] = cam_centers[3 * v + k];
+    sh_colour_views_kernel<<<ceil_div(n, kPreBlock), kPreBlock, 0, stream>>>(
+        means, sh_dc, sh_rest, shl, cc, n_views, sh_degree, n, view_stride, valid, color);
+    return check_launch("sh_colour_views");
 }
 
 mg_status launch_bin_count(const float* uv, const float* rxy, const float* conic,

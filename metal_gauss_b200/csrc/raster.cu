@@ -42,11 +42,14 @@
 // so a long list is split over many warps instead of forming the kernel's
 // tail. The colour and alpha behind an entry enter its gradient only through
 // their dot product with the pixel's output gradient, so a pixel carries one
-// running sum for them. A live entry to which at most 24 of the warp's
-// pixels contribute is added as per-lane 16-byte vector atomics; otherwise
-// the warp reduces its 32 pixels' contributions with a 10-slot butterfly
-// reduce-scatter (12 shuffles) and three lanes add the 48-byte gradient record
-// with three vector atomics (the crossover measured on B200).
+// running sum for them. Per live entry a lane sums, over its pixels, the raw
+// moments of g = dL/dalpha * gauss (g dx, g dy, g, g dx^2, g dx dy, g dy^2)
+// and the colour weights; the conic and opacity factors every pixel shares
+// are applied once per entry, after the sum over lanes. An entry to which at
+// most 24 of the warp's lanes contribute is added as per-lane 16-byte vector
+// atomics; otherwise the warp reduces its lanes' sums with a 10-slot
+// butterfly reduce-scatter (12 shuffles) and three lanes add the 48-byte
+// gradient record with three vector atomics (the crossover measured on B200).
 #include <mutex>
 #include <unordered_map>
 
@@ -181,14 +184,14 @@ __device__ __forceinline__ void cp_async_wait() {
 #define MG_BWD_STAGES 3
 #endif
 constexpr int kFwdStages = MG_FWD_STAGES;
-#ifndef MG_BWD_DIRECT_MAX
-#define MG_BWD_DIRECT_MAX 24
+#ifndef MG_BWD_DIRECT_LANES
+#define MG_BWD_DIRECT_LANES 24
 #endif
-// Up to this many contributing pixels (of a backward block's 64 when the
-// tile side is a multiple of 8), a live entry's gradient goes out as per-lane
-// vector atomics instead of through the warp reduction (8 / 16 / 24 / 32
-// measured on the bench: 24 and 32 best).
-constexpr int kBwdDirectMax = MG_BWD_DIRECT_MAX;
+// Up to this many lanes (of 32) with a contributing pixel, a live entry's
+// gradient goes out as per-lane vector atomics instead of through the warp
+// reduction (8 / 12 / 16 / 20 / 24 / 32 measured on the bench: 24 best; 32,
+// atomics only, is 30% slower).
+constexpr int kBwdDirectLanes = MG_BWD_DIRECT_LANES;
 constexpr int kBwdStages = MG_BWD_STAGES;
 
 // A warp's ring of chunk buffers: q[buffer][word][entry], so a lane's three
@@ -240,10 +243,18 @@ struct Blocks {
 // of its gradient are then shared by kPx pixels per lane. (The forward keeps
 // 32-pixel blocks: its heaviest block's walk is a serial chain per warp, and
 // two pixels per lane would double it.)
+// Pixels per lane of the backward for a tile side: MG_RASTER_PX when the
+// side is a multiple of 8 (at most the tile's forward blocks), else 1.
+__host__ __device__ constexpr int bwd_px_for(int tile) {
+    return tile % 8 != 0 ? 1
+                         : ((tile * tile + 31) / 32 >= MG_RASTER_PX ? MG_RASTER_PX
+                                                                   : (tile * tile + 31) / 32);
+}
+
 template <int TILE>
 struct BwdBlocks {
     using F = Blocks<TILE>;
-    static constexpr int kPx = TILE % 8 == 0 ? MG_RASTER_PX : 1;
+    static constexpr int kPx = bwd_px_for(TILE);
     static constexpr int kCount = F::kCount / kPx;
     static_assert(F::kCount % kPx == 0, "whole forward blocks per backward block");
     // forward block holding pixel p of backward block b
@@ -618,29 +629,37 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                 live &= ~(1u << k);
                 const float4 a = st.q[buf][0][k], b4 = st.q[buf][1][k];
                 const float cbk = st.q[buf][2][k].x;
-                float dx[PX], dy[PX], gauss[PX], alpha_raw[PX], alpha[PX];
-                bool active[PX];
+                // a = {u, v, A, B}, b4 = {C, op, r, g}, cbk = b
+                float dx[PX], dy[PX], gauss[PX], alpha[PX];
+                bool active[PX], unclamped[PX];
                 bool any = false;
-                int n_act = 0;
 #pragma unroll
                 for (int p = 0; p < PX; ++p) {
                     dx[p] = fx[p] - a.x;
                     dy[p] = fy[p] - a.y;
                     const float power = pair_power(dx[p], dy[p], a.z, a.w, b4.x);
                     gauss[p] = __expf(fminf(power, 0.0f));
-                    alpha_raw[p] = b4.y * gauss[p];
-                    alpha[p] = fminf(0.999f, alpha_raw[p]);
+                    const float alpha_raw = b4.y * gauss[p];
+                    alpha[p] = fminf(0.999f, alpha_raw);
+                    // the 0.999 clamp cuts the gradient to opacity and position
+                    unclamped[p] = alpha_raw <= 0.999f;
                     active[p] = inimg[p] && (base + k < my_stop[p]) && (power <= 0.0f) &&
                                 (alpha[p] >= 1.0f / 255.0f);
                     any = any || active[p];
-                    n_act += __popc(__ballot_sync(0xffffffffu, active[p]));
                 }
-                if (n_act == 0) continue;
-                // every lane evaluates; inactive pixels are masked to zero
+                const uint32_t lanes = __ballot_sync(0xffffffffu, any);
+                if (lanes == 0u) continue;
+                // Per lane, the raw moments of g = dL/dalpha * gauss over its
+                // pixels (g dx, g dy, g, g dx^2, g dx dy, g dy^2) and the colour
+                // weights; the conic and opacity factors common to every pixel
+                // are applied once per entry after the reduction:
+                //   d u = -op (2A Sx + B Sy),  d v = -op (B Sx + 2C Sy),
+                //   d op = Sg,  d conic = -op (Sxx / 2, Sxy, Syy / 2),
+                // since d power / d u = -(2A dx + B dy) and A = -ca/2, B = -cb,
+                // C = -cc/2.
                 float v[10];
 #pragma unroll
                 for (int i = 0; i < 10; ++i) v[i] = 0.0f;
-                bool has_dp = false;
 #pragma unroll
                 for (int p = 0; p < PX; ++p) {
                     const float om = fmaxf(1.0f - alpha[p], 1e-8f);
@@ -652,40 +671,56 @@ raster_backward_kernel(const float4* __restrict__ splats, const int32_t* __restr
                     const float w = active[p] ? alpha[p] * Tn : 0.0f;
                     T[p] = active[p] ? Tn : T[p];
                     S[p] += w * q;
-                    // the 0.999 clamp cuts the gradient to opacity and position
-                    const float dLg =
-                        (active[p] && alpha_raw[p] <= 0.999f) ? dL_dalpha * gauss[p] : 0.0f;
-                    const float dp = dLg * b4.y;
-                    has_dp = has_dp || dp != 0.0f;
-                    // d power / d u = ca dx + cb dy = -(2A dx + B dy)
-                    const float g0v = -dp * (2.0f * a.z * dx[p] + a.w * dy[p]);
-                    const float g1v = -dp * (a.w * dx[p] + 2.0f * b4.x * dy[p]);
-                    v[0] += g0v;
-                    v[1] += g1v;
-                    v[2] += dLg;
-                    if (want_absgrad) v[3] += sqrtf(g0v * g0v + g1v * g1v);
-                    v[4] += dp * (-0.5f * dx[p] * dx[p]);
-                    v[5] += dp * (-1.0f * dx[p] * dy[p]);
-                    v[6] += dp * (-0.5f * dy[p] * dy[p]);
-                    v[7] += w * gr[p]; v[8] += w * gg[p]; v[9] += w * gb[p];
+                    const float g = (active[p] && unclamped[p]) ? dL_dalpha * gauss[p] : 0.0f;
+                    const float gx = g * dx[p], gy = g * dy[p];
+                    v[0] += gx;
+                    v[1] += gy;
+                    v[2] += g;
+                    if (want_absgrad) {  // per-pixel |d uv|, before the factors
+                        const float ux = -(2.0f * a.z * dx[p] + a.w * dy[p]);
+                        const float uy = -(a.w * dx[p] + 2.0f * b4.x * dy[p]);
+                        v[3] += b4.y * fabsf(g) * sqrtf(ux * ux + uy * uy);
+                    }
+                    v[4] = fmaf(gx, dx[p], v[4]);
+                    v[5] = fmaf(gx, dy[p], v[5]);
+                    v[6] = fmaf(gy, dy[p], v[6]);
+                    v[7] = fmaf(w, gr[p], v[7]);
+                    v[8] = fmaf(w, gg[p], v[8]);
+                    v[9] = fmaf(w, gb[p], v[9]);
                 }
                 float4* dst =
                     reinterpret_cast<float4*>(grad2d + (int64_t)st.id[buf][k] * MG_G2D_STRIDE);
-                if (n_act <= kBwdDirectMax) {
-                    // few contributing pixels: each lane adds its own sum (the
-                    // warp reduction costs more than a few sets of atomics)
+                const float op = b4.y;
+                if (__popc(lanes) <= kBwdDirectLanes) {
+                    // few contributing lanes: each adds its own sums (the warp
+                    // reduction costs more than a few sets of atomics)
                     if (any) {
-                        atomicAdd(dst, make_float4(v[0], v[1], v[2], v[3]));
-                        if (has_dp) atomicAdd(dst + 1, make_float4(v[4], v[5], v[6], 0.f));
+                        atomicAdd(dst, make_float4(-op * (2.0f * a.z * v[0] + a.w * v[1]),
+                                                   -op * (a.w * v[0] + 2.0f * b4.x * v[1]),
+                                                   v[2], v[3]));
+                        if (v[4] != 0.f || v[5] != 0.f || v[6] != 0.f)
+                            atomicAdd(dst + 1, make_float4(-0.5f * op * v[4], -op * v[5],
+                                                           -0.5f * op * v[6], 0.f));
                         atomicAdd(dst + 2, make_float4(v[7], v[8], v[9], 0.f));
                     }
                     continue;
                 }
                 const float r = reduce_scatter10(v, lane);
-                const float r0 = __shfl_sync(0xffffffffu, r, g0);
-                const float r1 = __shfl_sync(0xffffffffu, r, g1);
-                const float r2 = __shfl_sync(0xffffffffu, r, g2);
+                float r0 = __shfl_sync(0xffffffffu, r, g0);
+                float r1 = __shfl_sync(0xffffffffu, r, g1);
+                float r2 = __shfl_sync(0xffffffffu, r, g2);
                 const float r3 = __shfl_sync(0xffffffffu, r, g3);
+                // lane 0 holds (Sx, Sy, Sg, |uv|), lane 1 (Sxx, Sxy, Syy, 0),
+                // lane 2 the colour sums
+                if (lane == 0) {
+                    const float sx = r0, sy = r1;
+                    r0 = -op * (2.0f * a.z * sx + a.w * sy);
+                    r1 = -op * (a.w * sx + 2.0f * b4.x * sy);
+                } else if (lane == 1) {
+                    r0 = -0.5f * op * r0;
+                    r1 = -op * r1;
+                    r2 = -0.5f * op * r2;
+                }
                 if (lane < 3 && (r0 != 0.f || r1 != 0.f || r2 != 0.f || r3 != 0.f))
                     atomicAdd(dst + lane, make_float4(r0, r1, r2, r3));
             }
@@ -840,11 +875,18 @@ __global__ void pack_intersections_kernel(const float2* __restrict__ uv,
 // Mip-Splatting opacity compensation (metal_backend.py:367-393): the 2D
 // covariance before the 0.3 px blur, recovered from the blurred conic, gives
 // op * sqrt(clamp(det_before / det_after, 0, 1)).
+// Every operation explicitly rounded, in the order of the reference's
+// float32 expression (metal_backend.py:367-393), so the compensated opacity
+// -- which decides the 1/255 binning and blending thresholds -- is
+// bit-identical to the CPU restatement's.
 __device__ __forceinline__ float antialias_factor(float cxx, float cxy, float cyy, float blur) {
-    const float det_after = 1.0f / fmaxf(cxx * cyy - cxy * cxy, 1e-12f);
-    const float a = cyy * det_after, b = -cxy * det_after, c = cxx * det_after;
-    const float det_before = (a - blur) * (c - blur) - b * b;
-    return sqrtf(fminf(fmaxf(det_before, 0.0f) / det_after, 1.0f));
+    const float det_conic = fmaxf(__fsub_rn(__fmul_rn(cxx, cyy), __fmul_rn(cxy, cxy)), 1e-12f);
+    const float det_after = __fdiv_rn(1.0f, det_conic);
+    const float a = __fmul_rn(cyy, det_after), b = __fmul_rn(-cxy, det_after);
+    const float c = __fmul_rn(cxx, det_after);
+    const float det_before = __fsub_rn(__fmul_rn(__fsub_rn(a, blur), __fsub_rn(c, blur)),
+                                       __fmul_rn(b, b));
+    return __fsqrt_rn(fminf(fmaxf(__fdiv_rn(fmaxf(det_before, 0.0f), det_after), 0.0f), 1.0f));
 }
 
 __global__ void antialias_opacity_kernel(const float* __restrict__ conic,
@@ -935,9 +977,7 @@ __global__ void antialias_grad2d_views_kernel(const float* __restrict__ conic,
 
 // Forward and backward warp blocks per tile (Blocks / BwdBlocks on the host).
 int blocks_per_tile(int tile) { return (tile * tile + 31) / 32; }
-int bwd_blocks_per_tile(int tile) {
-    return tile % 8 == 0 ? blocks_per_tile(tile) / MG_RASTER_PX : blocks_per_tile(tile);
-}
+int bwd_blocks_per_tile(int tile) { return blocks_per_tile(tile) / bwd_px_for(tile); }
 
 // Scratch shared by one view's forward and backward.
 struct RasterScratch {

@@ -139,15 +139,37 @@ __device__ __forceinline__ void load16(const float* row, int g, float (&v)[16]) 
     }
 }
 
+// Target values. Float images are read as they are; 8-bit images as x / 255
+// in float32 with IEEE division (what numpy's float32 x / 255 and the CPU
+// restatement give), looked up in a 256-entry table each block fills once.
+struct TargetTable {
+    float v[256];
+    __device__ __forceinline__ void fill() {
+        const int t = threadIdx.y * blockDim.x + threadIdx.x;
+        for (int i = t; i < 256; i += blockDim.x * blockDim.y)
+            v[i] = __fdiv_rn((float)i, 255.0f);
+    }
+};
+__device__ __forceinline__ float pixel_value(const float* __restrict__ src, int64_t i,
+                                             const TargetTable*) {
+    return src[i];
+}
+__device__ __forceinline__ float pixel_value(const uint8_t* __restrict__ src, int64_t i,
+                                             const TargetTable* tab) {
+    return tab->v[src[i]];
+}
+
 // Stages channel c of `src` (H, W, 3) around the tile at (ox, oy), zero outside.
-__device__ __forceinline__ void stage_channel(const float* __restrict__ src, int c, int W, int H,
-                                              int ox, int oy, float (*dst)[kSP]) {
+template <typename T>
+__device__ __forceinline__ void stage_channel(const T* __restrict__ src, int c, int W, int H,
+                                              int ox, int oy, float (*dst)[kSP],
+                                              const TargetTable* tab = nullptr) {
     for (int ly = threadIdx.y; ly < kSH; ly += 8) {
         const int gy = oy + ly - kR;
         for (int lx = threadIdx.x; lx < kSP; lx += 32) {
             const int gx = ox + lx - kR;
             const bool ok = lx < kSW && gx >= 0 && gx < W && gy >= 0 && gy < H;
-            dst[ly][lx] = ok ? src[((int64_t)gy * W + gx) * 3 + c] : 0.f;
+            dst[ly][lx] = ok ? pixel_value(src, ((int64_t)gy * W + gx) * 3 + c, tab) : 0.f;
         }
     }
 }
@@ -157,14 +179,16 @@ __device__ __forceinline__ void stage_channel(const float* __restrict__ src, int
 #define MG_LOSS_MIN_BLOCKS 6
 #endif
 // Six blocks per SM keep an 800 x 800 image (850 tiles) in one wave.
+template <typename TY>
 __global__ void __launch_bounds__(256, MG_LOSS_MIN_BLOCKS)
-loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
+loss_moments_kernel(const float* __restrict__ x, const TY* __restrict__ y,
                     const float* __restrict__ win, int W, int H, float g_ssim,
                     float* __restrict__ adj, float* __restrict__ partial) {
     __shared__ __align__(16) float s_x[kSH][kSP];
     __shared__ __align__(16) float s_y[kSH][kSP];
     __shared__ __align__(16) float s_h[5][kSH][kLW];
     __shared__ float s_red[2][8];
+    __shared__ TargetTable s_tab;
     const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * 32 + tx;
     const int ox = blockIdx.x * kLW, oy = blockIdx.y * kLH;
     const int64_t npix = (int64_t)W * H;
@@ -172,10 +196,14 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
 #pragma unroll
     for (int k = 0; k < 11; ++k) wk[k] = win[k];
     float sum_s = 0.f, sum_l1 = 0.f;
+    if (sizeof(TY) == 1) {
+        s_tab.fill();
+        __syncthreads();
+    }
     {
         const int c = blockIdx.z;  // one colour channel per block
         stage_channel(x, c, W, H, ox, oy, s_x);
-        stage_channel(y, c, W, H, ox, oy, s_y);
+        stage_channel(y, c, W, H, ox, oy, s_y, &s_tab);
         __syncthreads();
         for (int it = tid; it < kHItems; it += 256) {
             const int row = it >> 3, g = it & 7;
@@ -262,18 +290,21 @@ loss_moments_kernel(const float* __restrict__ x, const float* __restrict__ y,
 }
 
 // Kernel 2: blur the adjoint maps back and apply the chain rule + L1 term.
+template <typename TY>
 __global__ void __launch_bounds__(256, 6)
-loss_grad_kernel(const float* __restrict__ x, const float* __restrict__ y,
+loss_grad_kernel(const float* __restrict__ x, const TY* __restrict__ y,
                  const float* __restrict__ adj, const float* __restrict__ win, int W, int H,
                  float g_l1, float* __restrict__ grad_x) {
     __shared__ __align__(16) float s_a[3][kSH][kSP];
     __shared__ __align__(16) float s_h[3][kSH][kLW];
+    __shared__ TargetTable s_tab;
     const int tx = threadIdx.x, ty = threadIdx.y, tid = ty * 32 + tx;
     const int ox = blockIdx.x * kLW, oy = blockIdx.y * kLH;
     const int64_t npix = (int64_t)W * H;
     float wk[11];
 #pragma unroll
     for (int k = 0; k < 11; ++k) wk[k] = win[k];
+    if (sizeof(TY) == 1) s_tab.fill();  // ordered by the barrier after the staging
     {
         const int c = blockIdx.z;  // one colour channel per block
         for (int ly = ty; ly < kSH; ly += 8) {
@@ -333,7 +364,7 @@ loss_grad_kernel(const float* __restrict__ x, const float* __restrict__ y,
             const int py = oy + ty * kLRows + p;
             if (px >= W || py >= H) continue;
             const int64_t o = ((int64_t)py * W + px) * 3 + c;
-            const float xv = x[o], yv = y[o];
+            const float xv = x[o], yv = pixel_value(y, o, &s_tab);
             const float diff = xv - yv;
             const float sgn = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
             grad_x[o] = b[0][p] + 2.0f * xv * b[1][p] + yv * b[2][p] + g_l1 * sgn;
@@ -436,10 +467,11 @@ extern "C" size_t mg_l1_ssim_scratch_bytes(int32_t height, int32_t width) {
     return ((adj + 255) & ~(size_t)255) + ((part + 255) & ~(size_t)255);
 }
 
-extern "C" mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
-                                     int32_t height, int32_t width, float w_l1, float w_ssim,
-                                     float scale, float* grad_x, float* loss_dev, void* scratch,
-                                     size_t scratch_bytes, mg_stream_t stream) {
+template <typename TY>
+static mg_status l1_ssim_loss_impl(const float* x, const TY* y, const float* w, int32_t height,
+                                   int32_t width, float w_l1, float w_ssim, float scale,
+                                   float* grad_x, float* loss_dev, void* scratch,
+                                   size_t scratch_bytes, mg_stream_t stream) {
     MG_REQUIRE(height > 0 && width > 0, "l1_ssim_loss: empty image");
     MG_REQUIRE(x && y && w && grad_x && loss_dev, "l1_ssim_loss: null pointer");
     MG_REQUIRE(scratch && scratch_bytes >= mg_l1_ssim_scratch_bytes(height, width),
@@ -452,13 +484,30 @@ extern "C" mg_status mg_l1_ssim_loss(const float* x, const float* y, const float
                                               ((sizeof(float) * 9 * npix + 255) & ~(size_t)255));
     const float inv_n = 1.0f / (float)(3 * npix);
     // d loss / d S_p = -scale * w_ssim / n ; d loss / d x = scale * w_l1 * sign / n
-    loss_moments_kernel<<<g, dim3(32, 8), 0, s>>>(x, y, w, width, height,
-                                                     -scale * w_ssim * inv_n, adj, partial);
+    loss_moments_kernel<TY><<<g, dim3(32, 8), 0, s>>>(x, y, w, width, height,
+                                                         -scale * w_ssim * inv_n, adj, partial);
     MG_TRY(check_launch("l1_ssim_loss moments"));
-    loss_grad_kernel<<<g, dim3(32, 8), 0, s>>>(x, y, adj, w, width, height,
-                                                  scale * w_l1 * inv_n, grad_x);
+    loss_grad_kernel<TY><<<g, dim3(32, 8), 0, s>>>(x, y, adj, w, width, height,
+                                                      scale * w_l1 * inv_n, grad_x);
     MG_TRY(check_launch("l1_ssim_loss grad"));
     loss_finish_kernel<<<1, 256, 0, s>>>(partial, (int)(g.x * g.y * g.z), w_l1, w_ssim, scale,
                                          inv_n, loss_dev);
     return check_launch("l1_ssim_loss finish");
+}
+
+extern "C" mg_status mg_l1_ssim_loss(const float* x, const float* y, const float* w,
+                                     int32_t height, int32_t width, float w_l1, float w_ssim,
+                                     float scale, float* grad_x, float* loss_dev, void* scratch,
+                                     size_t scratch_bytes, mg_stream_t stream) {
+    return l1_ssim_loss_impl<float>(x, y, w, height, width, w_l1, w_ssim, scale, grad_x,
+                                    loss_dev, scratch, scratch_bytes, stream);
+}
+
+extern "C" mg_status mg_l1_ssim_loss_u8(const float* x, const uint8_t* y, const float* w,
+                                        int32_t height, int32_t width, float w_l1, float w_ssim,
+                                        float scale, float* grad_x, float* loss_dev,
+                                        void* scratch, size_t scratch_bytes,
+                                        mg_stream_t stream) {
+    return l1_ssim_loss_impl<uint8_t>(x, y, w, height, width, w_l1, w_ssim, scale, grad_x,
+                                      loss_dev, scratch, scratch_bytes, stream);
 }

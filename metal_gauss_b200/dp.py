@@ -100,3 +100,61 @@ def all_reduce_(t: torch.Tensor, group=None) -> None:
     import torch.distributed as dist
     if world_size(group) > 1:
         dist.all_reduce(t, group=group)
+
+
+class ZeroExchange:
+    """The ZeRO-1 exchange of a flat fp32 gradient / parameter pair whose
+    segments form `ranges` = [(lo, hi), ...] exchange groups (the trainer's:
+    the geometry segments, then the SH segments), each (hi - lo) a multiple of
+    the world size. Each group is reduce-scattered, updated and all-gathered
+    on a process group of its own, so a small group's collectives never queue
+    behind a large group's on one communicator's stream, and every call is
+    asynchronous: it returns a work handle whose `wait()` makes the current
+    CUDA stream (nothing on the host) wait for it. Rank r owns chunk r of
+    every group. Every rank must build it, and call its methods, in the same
+    order."""
+
+    def __init__(self, ranges, group=None):
+        import torch.distributed as dist
+        self.world, self.rank = world_size(group), rank(group)
+        for lo, hi in ranges:
+            if (hi - lo) % self.world:
+                raise ValueError(f"exchange group [{lo}, {hi}) does not split over "
+                                 f"{self.world} ranks")
+        self.ranges = list(ranges)
+        self.backend = dist.get_backend(group)
+        ranks = list(range(self.world)) if group is None else dist.get_process_group_ranks(group)
+        # one communicator per exchange group (new_group is collective)
+        self.groups = [dist.new_group(ranks, backend=self.backend) for _ in self.ranges]
+
+    def owned(self, k: int) -> tuple[int, int]:
+        """Flat [lo, hi) of exchange group k that this rank updates."""
+        lo, hi = self.ranges[k]
+        chunk = (hi - lo) // self.world
+        return lo + self.rank * chunk, lo + (self.rank + 1) * chunk
+
+    def reduce_scatter(self, flat: torch.Tensor, k: int):
+        """Sum group k of `flat` over ranks, leaving this rank's chunk summed
+        in place (the rest of the group is left undefined). gloo, which has no
+        reduce-scatter, sums the whole group with an all-reduce."""
+        import torch.distributed as dist
+        lo, hi = self.ranges[k]
+        seg = flat[lo:hi]
+        if self.backend == "nccl":
+            a, b = self.owned(k)
+            return dist.reduce_scatter_tensor(flat[a:b], seg, group=self.groups[k],
+                                              async_op=True)
+        return dist.all_reduce(seg, group=self.groups[k], async_op=True)
+
+    def all_gather(self, flat: torch.Tensor, k: int):
+        """Every rank's chunk of group k of `flat`, gathered in place."""
+        import torch.distributed as dist
+        lo, hi = self.ranges[k]
+        a, b = self.owned(k)
+        src = flat[a:b] if self.backend == "nccl" else flat[a:b].clone()
+        return dist.all_gather_into_tensor(flat[lo:hi], src, group=self.groups[k],
+                                           async_op=True)
+
+    def all_reduce(self, t: torch.Tensor, k: int = 0):
+        import torch.distributed as dist
+        return dist.all_reduce(t, group=self.groups[k], async_op=True)

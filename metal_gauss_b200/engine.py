@@ -289,15 +289,19 @@ class Trainer:
         self.lrs = dict(DEFAULT_LRS, **(lrs or {}))
         f32 = dict(dtype=torch.float32, device=self.device)
         # segment starts rounded up to 64 floats (256 B): quaternions are read
-        # as float4 and every segment stays aligned for vector access
+        # as float4 and every segment stays aligned for vector access. The
+        # geometry segments and the SH segments form two exchange groups, each
+        # padded so it splits into equal 64-float-aligned chunks, one per rank
+        # (the unit of the reduce-scatter / all-gather)
+        unit = 64 * self.world
         self.offsets = {}
         off = 0
         for name, w in SEGMENTS:
+            if name == "sh_dc":
+                off = -(-off // unit) * unit
+                self.geo_end = off
             self.offsets[name] = off
             off += (w * self.n_pad + 63) // 64 * 64
-        # parameter region padded so it splits into equal 64-float-aligned
-        # chunks, one per rank (the unit of the reduce-scatter / all-gather)
-        unit = 64 * self.world
         self.p_total = -(-off // unit) * unit
         self.vis_offset = self.p_total
         # gradient buffer: parameter region | visibility counts | loss
@@ -343,6 +347,21 @@ class Trainer:
         # per-view list entries walked by the rasteriser (device scalars),
         # recorded while timing is on
         self.walked: list[torch.Tensor] = []
+        # ZeRO-1 over several ranks: the geometry and SH groups are exchanged
+        # asynchronously on communicators of their own; a step leaves its two
+        # parameter all-gathers in flight, and the next step waits for the
+        # geometry before its projection and for the SH rows only before the
+        # colour of its views (computed after its binning)
+        self._xchg = (dp.ZeroExchange([(0, self.geo_end), (self.geo_end, self.p_total)], group)
+                      if self.world > 1 and self.shard_optimizer else None)
+        self.split_colour = self._xchg is not None
+        self._pending: dict[str, object] = {"geo": None, "sh": None}
+        self._side = None
+        # host targets are copied on this stream while the step projects and
+        # bins; the loss kernels wait for the copies' event
+        self._copy_stream = None
+        self._target_bufs: list[torch.Tensor] = []
+        self._targets_ready = None
 
     # ---------------------------------------------------------------- timing
 
@@ -382,6 +401,7 @@ class Trainer:
         """The current parameters in the trainer's storage form (views into
         the flat device buffer): means, quats, log_scales, logit_opac,
         sh_dc (N,1,3), sh_rest (N,15,3)."""
+        self.synchronize_params()
         return {name: self.param(name) for name, _ in SEGMENTS}
 
     def export_ply(self, path, filter_3d=None) -> None:
@@ -397,6 +417,7 @@ class Trainer:
         used by every following step until it is recomputed or cleared
         (`trainer.filter_3d = None`)."""
         from .mipfilter import compute_3d_filter
+        self.synchronize_params()
         self.filter_3d = compute_3d_filter(self.param("means"), views, near, margin)
         return self.filter_3d
 
@@ -406,6 +427,7 @@ class Trainer:
         """The Gaussian table as row segments: the parameter segments of P,
         then the Adam rows to reset (M and V in P's layout, the per-row step
         counts)."""
+        self.synchronize_params()
         params = [_lib.RowSegment(self.P.data_ptr() + 4 * self.offsets[name], w)
                   for name, w in SEGMENTS]
         rows = [_lib.RowSegment(buf.data_ptr() + 4 * self.offsets[name], w)
@@ -465,6 +487,7 @@ class Trainer:
         """3DGS-MCMC exploration noise (mcmc.add_noise, mcmc.py:166-192) on the
         active means, scaled by the current means learning rate."""
         lr = self.lrs["means"] if lr_means is None else lr_means
+        self.synchronize_params()
         _lib.call("mg_mcmc_add_noise", ptr(self.param("means")), ptr(self.param("quats")),
                   ptr(self.param("log_scales")), ptr(self.param("logit_opac")), self.active,
                   float(lr), float(weight), float(opacity_gate),
@@ -490,6 +513,7 @@ class Trainer:
         (train.py:223-227). `train_step` does the same inside the projection
         kernel (`_prologue`); this form serves callers that drive
         `forward_backward_views` themselves."""
+        self.synchronize_params()
         f = self._filter_tensor()
         if f is None:
             torch.exp(self.param("log_scales"), out=self.scales)
@@ -533,6 +557,7 @@ class Trainer:
         return buf[o:o + w * self.n_pad]
 
     def state_dict(self) -> dict:
+        self.synchronize_params()
         return {name: self.param(name).detach().clone() for name, _ in SEGMENTS}
 
     # --------------------------------------------------------------- views
@@ -589,17 +614,38 @@ class Trainer:
         b = self._batch
         cams = _views_array([self._camera(view) for view in views])
         pro = _lib.C.byref(self._prologue()) if begin_step else None
+        # with the colour split the SH rows are not read here (`_colour_views`
+        # colours the views after the binning)
+        colour = not self.split_colour
         ev = self._begin("preprocess_fwd")
         _lib.call("mg_preprocess_forward_views", ptr(self.param("means")),
-                  ptr(self.param("quats")), ptr(self.scales), ptr(self.param("sh_dc")),
-                  ptr(self.param("sh_rest")), _lib.SH_SPLIT, ptr(self.opac),
-                  _lib.C.cast(cams, _lib.C.c_void_p), len(views), self.sh_degree, self.active,
-                  self.n,
+                  ptr(self.param("quats")), ptr(self.scales),
+                  ptr(self.param("sh_dc")) if colour else None,
+                  ptr(self.param("sh_rest")) if colour else None, _lib.SH_SPLIT, ptr(self.opac),
+                  _lib.C.cast(cams, _lib.C.c_void_p), len(views),
+                  self.sh_degree if colour else -1, self.active, self.n,
                   ptr(b.uv), ptr(b.conic), ptr(b.depth), ptr(b.rxy), ptr(b.valid), ptr(b.color),
                   ptr(self.visibility_count()), pro, _lib.stream())
         if self.antialias:
             _lib.call("mg_antialias_opacity_views", ptr(b.conic), ptr(self.opac), self.active,
                       len(views), self.n, 0.3, ptr(b.opac), _lib.stream())
+        self._end(ev)
+
+    def _colour_views(self, views) -> None:
+        """The SH colour of every view of the batch (mg_sh_colour_views), for a
+        projection that skipped it; waits first for the previous step's SH
+        all-gather."""
+        self._wait("sh", "wait_sh_gather")
+        centres = (_lib.C.c_float * (3 * len(views)))()
+        for v, view in enumerate(views):
+            cc = self._camera(view).cam_center
+            centres[3 * v:3 * v + 3] = [cc[0], cc[1], cc[2]]
+        b = self._batch
+        ev = self._begin("colour")
+        _lib.call("mg_sh_colour_views", ptr(self.param("means")), ptr(self.param("sh_dc")),
+                  ptr(self.param("sh_rest")), _lib.SH_SPLIT,
+                  _lib.C.cast(centres, _lib.C.c_void_p), len(views), self.sh_degree, self.active,
+                  self.n, ptr(b.valid), ptr(b.color), _lib.stream())
         self._end(ev)
 
     def _view_opacities(self) -> tuple[torch.Tensor, int]:
@@ -656,6 +702,44 @@ class Trainer:
             self.active, view.width, view.height, self.tile, self.saturation_cut,
             ptr(self._totals[v:v + 1]), ptr(prep), prep.numel(), s), "bin_prepare")
         self._end(ev)
+
+    def _stage_targets(self, targets) -> list[torch.Tensor]:
+        """Device tensors of the step's targets (H, W, 3): float32 in [0, 1]
+        or uint8 bytes, which the loss reads as x / 255 (the reference divides
+        its byte images by 255, train.py:385). Device targets are used as they
+        are; host targets are copied into resident buffers on a side stream,
+        so the copy overlaps the step's projection and binning (it is
+        asynchronous from pinned memory), and the loss kernels wait for it."""
+        out = []
+        host = [t for t in targets if t.device.type != "cuda"]
+        self._targets_ready = None
+        if host:
+            if self._copy_stream is None:
+                self._copy_stream = torch.cuda.Stream(self.device)
+            # the previous step's loss kernels (joined into this stream) are
+            # done with the buffers before they are overwritten
+            self._copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+        k = 0
+        for t in targets:
+            if t.dtype not in (torch.uint8, torch.float32) or t.dim() != 3 or t.shape[2] != 3:
+                raise ValueError("targets must be (H, W, 3) uint8 or float32 images")
+            if t.device.type == "cuda":
+                out.append(t.contiguous())
+                continue
+            while len(self._target_bufs) <= k:
+                self._target_bufs.append(torch.empty(0, dtype=torch.uint8, device=self.device))
+            buf = self._target_bufs[k]
+            if buf.shape != t.shape or buf.dtype != t.dtype:
+                buf = torch.empty(t.shape, dtype=t.dtype, device=self.device)
+                self._target_bufs[k] = buf
+            with torch.cuda.stream(self._copy_stream):
+                buf.copy_(t, non_blocking=True)
+            out.append(buf)
+            k += 1
+        if host:
+            self._targets_ready = torch.cuda.Event()
+            self._targets_ready.record(self._copy_stream)
+        return out
 
     def _render_and_backprop(self, v: int, view, target: torch.Tensor, m: int,
                              scale: float, lists: tuple | None = None,
@@ -716,7 +800,12 @@ class Trainer:
         if work is not None:
             self.walked.append(work.sum())
         ev = self._begin("loss")
-        _lib.check(L.mg_l1_ssim_loss(
+        if self._targets_ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(self._targets_ready)
+        if tuple(target.shape) != (H, W, 3):
+            raise ValueError(f"target of view {v} is {tuple(target.shape)}, not ({H}, {W}, 3)")
+        loss_fn = L.mg_l1_ssim_loss_u8 if target.dtype == torch.uint8 else L.mg_l1_ssim_loss
+        _lib.check(loss_fn(
             ptr(b.rgb), ptr(target), ptr(self.window), H, W, self.w_l1, self.w_ssim, scale,
             ptr(b.grad_rgb), ptr(self.loss), ptr(b.loss_scratch), b.loss_scratch.numel(), s),
             "l1_ssim_loss")
@@ -745,8 +834,11 @@ class Trainer:
         if V > MAX_VIEWS_PER_STEP:
             raise ValueError(f"a step takes at most {MAX_VIEWS_PER_STEP} views per rank, got "
                              f"{V} (split the batch over more ranks or steps)")
-        if V > self._totals.numel():
-            self._totals = torch.zeros(V, dtype=torch.int64, device=self.device)
+        if begin_step:
+            # the projection reads (and its prologue writes) only geometry rows
+            self._wait("geo", "wait_geo_gather")
+        else:
+            self.synchronize_params()
         self._ensure_views(V)
         self._project_views(views, begin_step)
         streams = self._phase_b_streams(V)
@@ -765,6 +857,8 @@ class Trainer:
             chunk = views[first:first + C]
             with torch.cuda.stream(bin_stream):
                 totals, bb = self._bin_chunk(c, first, chunk)
+                if c == 0 and self.split_colour:
+                    self._colour_views(views)
             if streams:
                 # the chunk's views on the streams in turn, after its binning
                 ready = torch.cuda.Event()
@@ -817,59 +911,65 @@ class Trainer:
         self._end(ev)
         return stats
 
-    def optimizer_step(self) -> None:
-        """Adam over this rank's share: every element, or under ZeRO-1 the
-        rank's contiguous chunk of the flat parameter region (segments clipped
-        to it; a chunk may start or end inside a row)."""
-        self.step_count += 1
-        if self.shard_optimizer:
-            chunk = self.p_total // self.world
-            c_lo, c_hi = self.rank * chunk, (self.rank + 1) * chunk
-        else:
-            c_lo, c_hi = 0, self.p_total
+    def owned_ranges(self) -> list[tuple[int, int]]:
+        """Flat [lo, hi) ranges of the parameter region whose optimizer update
+        this rank runs: the whole region, or under ZeRO-1 its chunk of the
+        geometry group and its chunk of the SH group."""
+        if self._xchg is None:
+            return [(0, self.p_total)]
+        return [self._xchg.owned(0), self._xchg.owned(1)]
+
+    def _adam(self, ranges, flags: int = 0) -> None:
+        """Adam over the flat ranges (segments clipped to them; a range may
+        start or end inside a row), at the current step count."""
         segs = []
         for name, w in SEGMENTS:
             o = self.offsets[name]
-            b = max(c_lo, o) - o
-            e = min(c_hi, o + w * self.n) - o
-            if e > b:
-                segs.append(_lib.AdamSegment(o, w, self.lrs[name], b, e))
+            for c_lo, c_hi in ranges:
+                b = max(c_lo, o) - o
+                e = min(c_hi, o + w * self.n) - o
+                if e > b:
+                    segs.append(_lib.AdamSegment(o, w, self.lrs[name], b, e))
         b1, b2 = self.betas
         vis = self.visibility_count() if self.selective else None
-        ev = self._begin("adam")
         if segs:
             arr = (_lib.AdamSegment * len(segs))(*segs)
             _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
                       arr, len(segs), b1, b2, self.eps, ptr(vis), ptr(self.steps),
-                      self.step_count, ptr(self._adam_rows), _lib.stream())
-        elif vis is not None:  # no elements here: still advance the shared step counts
+                      self.step_count, ptr(self._adam_rows), flags, _lib.stream())
+        elif vis is not None:  # no elements here: still form / advance the step counts
             _lib.call("mg_adam_multi", ptr(self.P), ptr(self.G), ptr(self.M), ptr(self.V), self.n,
                       (_lib.AdamSegment * 1)(_lib.AdamSegment(0, 1, 0.0, 0, 0)), 0, b1, b2,
-                      self.eps, ptr(vis), ptr(self.steps), self.step_count, None, _lib.stream())
+                      self.eps, ptr(vis), ptr(self.steps), self.step_count, ptr(self._adam_rows),
+                      flags, _lib.stream())
+
+    def optimizer_step(self) -> None:
+        """Adam over this rank's share (`owned_ranges`) in one launch."""
+        self.synchronize_params()
+        self.step_count += 1
+        ev = self._begin("adam")
+        self._adam(self.owned_ranges())
         self._end(ev)
 
     def train_step(self, views, targets, global_batch: int | None = None) -> torch.Tensor:
-        """One optimisation step over this rank's `views` (with device
-        targets (H,W,3) in [0,1]). `global_batch` is the batch size summed
-        over ranks (defaults to len(views) times the world size). Returns the
-        batch-mean loss as a device tensor (1,), all-reduced across ranks."""
+        """One optimisation step over this rank's `views`. `targets` are the
+        views' images (H, W, 3): float32 in [0, 1] or uint8 bytes, on the
+        device or on the host (host images are copied while the step projects
+        and bins; pass pinned memory for an asynchronous copy). `global_batch`
+        is the batch size summed over ranks (defaults to len(views) times the
+        world size). Returns the batch-mean loss as a device tensor (1,),
+        all-reduced across ranks."""
         world = self._world_size()
         gb = global_batch or len(views) * world
+        targets = self._stage_targets(targets)
         # the activations and the zeroing of the accumulated gradient rows,
         # visibility counts and loss run inside the projection kernel; the SH
         # rows are overwritten by the SH adjoint
         self.last_stats = self.forward_backward_views(views, targets, 1.0 / gb, begin_step=True)
         if self.opac_reg or self.scale_reg:
             self._regularize(world)
-        if world > 1 and self.shard_optimizer:
-            ev = self._begin("reduce_scatter")
-            dp.all_reduce_(self.G[self.vis_offset:], self.group)     # visibility + loss
-            dp.reduce_scatter_segment(self.G[:self.p_total], self.group)
-            self._end(ev)
-            self.optimizer_step()
-            ev = self._begin("all_gather")
-            dp.all_gather_segment(self.P, self.group)
-            self._end(ev)
+        if self._xchg is not None:
+            self._exchange_and_update()
             return self.loss
         if world > 1:
             ev = self._begin("allreduce")
@@ -877,6 +977,39 @@ class Trainer:
             self._end(ev)
         self.optimizer_step()
         return self.loss
+
+    def _exchange_and_update(self) -> None:
+        """ZeRO-1 with the exchange overlapped. The visibility counts and the
+        loss are all-reduced and both gradient groups reduce-scattered at once;
+        the current stream waits only for the counts and the geometry chunk,
+        updates it (forming the selective rows' bias factors and advancing the
+        step counts) and starts its all-gather; a side stream waits for the SH
+        chunk, updates it with the same factors (reading neither the counts,
+        which the next step's projection rewrites, nor the step counts) and
+        starts its all-gather. Neither gather is waited for here: the next
+        step waits for the geometry before its projection and for the SH rows
+        before its colour, which comes after its binning."""
+        x = self._xchg
+        main = torch.cuda.current_stream(self.device)
+        ev = self._begin("exchange_wait")
+        w_tail = x.all_reduce(self.G[self.vis_offset:], 0)   # visibility counts + loss
+        w_geo = x.reduce_scatter(self.G, 0)
+        w_sh = x.reduce_scatter(self.G, 1)
+        w_tail.wait()
+        w_geo.wait()
+        self._end(ev)
+        self.step_count += 1
+        ev = self._begin("adam")
+        self._adam([x.owned(0)])
+        self._end(ev)
+        self._pending["geo"] = x.all_gather(self.P, 0)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(main)   # the all-reduced counts and the row factors
+        with torch.cuda.stream(self._side):
+            w_sh.wait()
+            self._adam([x.owned(1)], _lib.ADAM_ROW_FACTORS_READY | _lib.ADAM_KEEP_STEPS)
+            self._pending["sh"] = x.all_gather(self.P, 1)
 
     def _regularize(self, world: int) -> None:
         """The MCMC regularisers (train.py:393-398) over the active rows: their
@@ -892,6 +1025,24 @@ class Trainer:
 
     def _world_size(self) -> int:
         return dp.world_size(self.group)
+
+    def _wait(self, kind: str, stage: str | None = None) -> None:
+        """Make the current stream wait for the previous step's parameter
+        all-gather of group `kind` ("geo" or "sh"), if one is in flight."""
+        w = self._pending.get(kind)
+        if w is None:
+            return
+        ev = self._begin(stage) if stage else None
+        w.wait()
+        self._end(ev)
+        self._pending[kind] = None
+
+    def synchronize_params(self) -> None:
+        """Order the current stream after every parameter exchange still in
+        flight, so P (and the optimizer state) may be read or changed. Every
+        method that touches them outside a step calls it."""
+        self._wait("geo")
+        self._wait("sh")
 
     def check_device_error(self) -> None:
         """Synchronising check of the device error word; raises
@@ -934,7 +1085,7 @@ class Trainer:
             Wk = st.walked if st.walked else M
             total += (36 + 48 + 48) * n             # pack splat records, zero grad records
             total += 52 * Wk + 24 * P               # raster fwd (walked id + record)
-            total += 40 * P + 36 * P                # fused loss (2 kernels)
+            total += 27 * P                         # loss: image + uint8 target in, gradient out
             total += 52 * Wk + 36 * P + 48 * n      # raster bwd (+ gradient record)
         total += 28 * FLOATS_PER_GAUSSIAN * nv + 8 * n   # selective Adam
         return total
@@ -990,11 +1141,12 @@ def fit(trainer: Trainer, views, targets, steps: int, batch: int = 8, *, seed: i
         if filter_3d_every and (step == 1 or step % filter_3d_every == 0):
             trainer.compute_filter_3d(views)
         mine = [idx[i] for i in rank_views]
+        # host images as they are (uint8 bytes or float32 in [0, 1]): the
+        # trainer copies them while it bins and its loss reads bytes directly
         ts = []
         for i in mine:
-            t = targets[i]
-            t = torch.as_tensor(t).to(trainer.device, non_blocking=True)
-            ts.append(t.float().div_(255.0) if t.dtype == torch.uint8 else t.float())
+            t = torch.as_tensor(targets[i])
+            ts.append(t if t.dtype == torch.uint8 else t.float())
         losses.append(float(trainer.train_step([views[i] for i in mine], ts, batch)))
         if noise_weight:
             trainer.add_noise(trainer.lrs["means"], noise_weight)

@@ -87,7 +87,7 @@ def cfg3_two_views():
 def _engine_step(p, views, targets_u8, spec, cut: bool):
     dev = torch.device("cuda:0")
     tr = Trainer(p, dev, sh_degree=3, background=spec["background"], saturation_cut=cut)
-    tg = [t.to(dev).float().div_(255.0) for t in targets_u8]
+    tg = [t.to(dev) for t in targets_u8]   # bytes on the device, as bench.py keeps them
     loss = float(tr.train_step(views, tg, 2))
     torch.cuda.synchronize()
     return tr, loss

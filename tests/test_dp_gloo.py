@@ -166,3 +166,38 @@ def test_sharded_update_matches_the_replicated_one(tmp_path):
     p0, p1 = torch.load(tmp_path / "p0.pt"), torch.load(tmp_path / "p1.pt")
     ref = 1.0 - 0.5 * (torch.arange(24, dtype=torch.float32) * 3)     # sum over ranks 1 + 2
     assert torch.equal(p0, p1) and torch.allclose(p0, ref)
+
+
+def _zero_exchange_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    # a flat buffer of two exchange groups of different sizes (the trainer's
+    # geometry and SH groups), each a multiple of the world size
+    ranges = [(0, 8), (8, 32)]
+    x = dp.ZeroExchange(ranges)
+    g = torch.arange(32, dtype=torch.float32) * (rank + 1)     # this rank's gradient
+    p = torch.ones(32)                                        # replicated parameters
+    works = [x.reduce_scatter(g, k) for k in range(2)]        # both groups in flight
+    owned = [x.owned(k) for k in range(2)]
+    for k in (1, 0):                                          # completed in any order
+        works[k].wait()
+        a, b = owned[k]
+        p[a:b] -= 0.5 * g[a:b]                                # update the rank's chunk only
+    gathers = [x.all_gather(p, k) for k in range(2)]
+    for w in gathers:
+        w.wait()
+    torch.save({"p": p, "owned": owned}, os.path.join(out_dir, f"z{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_grouped_zero_exchange_matches_the_replicated_update(tmp_path):
+    """ZeRO-1 over two exchange groups (dp.ZeroExchange, as the trainer's
+    geometry and SH segments): each rank owns chunk r of every group, the
+    asynchronous reduce-scatters, chunk updates and all-gathers leave every
+    rank with the replicated update."""
+    _run_ranks(_zero_exchange_worker, (str(tmp_path),))
+    z0, z1 = torch.load(tmp_path / "z0.pt"), torch.load(tmp_path / "z1.pt")
+    assert z0["owned"] == [(0, 4), (8, 20)] and z1["owned"] == [(4, 8), (20, 32)]
+    ref = 1.0 - 0.5 * (torch.arange(32, dtype=torch.float32) * 3)     # sum over ranks 1 + 2
+    assert torch.equal(z0["p"], z1["p"]) and torch.allclose(z0["p"], ref)

@@ -30,7 +30,9 @@ class _Recorder:
         self.steps, self.events = [], []
 
     def train_step(self, views, targets, global_batch):
-        assert all(t.dtype == torch.float32 and float(t.max()) <= 1.0 for t in targets)
+        # host images go to the trainer as they are (bytes stay bytes)
+        assert all(t.device.type == "cpu" and (t.dtype == torch.uint8 or float(t.max()) <= 1.0)
+                   for t in targets)
         self.steps.append(dict(views=[v.i for v in views], lr=self.lrs["means"],
                                sh=self.sh_degree, reg=(self.opac_reg, self.scale_reg,
                                                        self.reg_weight), batch=global_batch))

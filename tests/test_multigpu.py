@@ -1,5 +1,7 @@
-"""Data-parallel training on 2 GPUs (NCCL): sharded (ZeRO-1) and replicated
-optimizer steps both equal the single-GPU step on the same batch, and the
+"""Data-parallel training on 2 GPUs (NCCL): sharded (ZeRO-1, with the
+overlapped per-group exchange) and replicated optimizer steps both equal the
+single-GPU steps on the same batches over two consecutive steps (the second
+starts while the first's parameter all-gathers are in flight), and the
 ranks' parameters stay identical. Needs >= 2 GPUs; skipped otherwise."""
 
 import datetime
@@ -45,19 +47,24 @@ def _run(rank, world, port, out, shard):
     tr = Trainer(p, f"cuda:{rank}", shard_optimizer=shard)
     tg = [t.cuda(rank) for t in targets]
     idx = dp.shard(dp.batch_indices(0, BATCH, len(views)), rank, world)
+    idx2 = dp.shard(dp.batch_indices(1, BATCH, len(views)), rank, world)
     loss = float(tr.train_step([views[j] for j in idx], [tg[j] for j in idx], BATCH))
-    # the gradient elements this rank holds summed: its chunk of the flat
-    # parameter region under ZeRO-1, everything otherwise
-    chunk = tr.p_total // world if (shard and world > 1) else tr.p_total
-    c_lo, c_hi = (rank * chunk, (rank + 1) * chunk) if (shard and world > 1) else (0, chunk)
+    # a second step: the first step's parameter all-gathers are still in
+    # flight when it starts (the overlapped exchange), and it must see them
+    loss2 = float(tr.train_step([views[j] for j in idx2], [tg[j] for j in idx2], BATCH))
+    tr.synchronize_params()
+    # the gradient elements this rank holds summed: its chunks of the flat
+    # parameter region under ZeRO-1 (one per exchange group), everything
+    # otherwise
     grads = {}
-    for k, w in SEGMENTS:
-        o = tr.offsets[k]
-        b, e = max(c_lo, o) - o, min(c_hi, o + w * tr.n) - o
-        if e > b:
-            grads[k] = (b, tr.G[o + b:o + e].cpu())
+    for c_lo, c_hi in tr.owned_ranges():
+        for k, w in SEGMENTS:
+            o = tr.offsets[k]
+            b, e = max(c_lo, o) - o, min(c_hi, o + w * tr.n) - o
+            if e > b:
+                grads.setdefault(k, []).append((b, tr.G[o + b:o + e].cpu()))
     torch.save({"params": {k: v.cpu() for k, v in tr.state_dict().items()}, "loss": loss,
-                "grads": grads},
+                "loss2": loss2, "grads": grads},
                os.path.join(out, f"{'s' if shard else 'r'}{world}_{rank}.pt"))
     if world > 1:
         dist.destroy_process_group()
@@ -75,9 +82,15 @@ def test_two_ranks_match_one(tmp_path, shard):
     ranks = [torch.load(tmp_path / f"{tag}2_{r}.pt") for r in range(2)]
     for k in one["params"]:
         assert torch.equal(ranks[0]["params"][k], ranks[1]["params"][k]), k   # replicas agree
+    for k in one["params"]:   # two steps on two ranks equal two steps on one
+        rel = float((ranks[0]["params"][k] - one["params"][k]).norm() /
+                    one["params"][k].norm().clamp_min(1e-30))
+        assert rel < 1e-6, (k, rel)
     for r in ranks:
         assert abs(r["loss"] - one["loss"]) < 1e-5
-        for k, (b, g) in r["grads"].items():
-            ref = one["grads"][k][1][b:b + g.numel()]
-            rel = float((g - ref).norm() / ref.norm().clamp_min(1e-30))
-            assert rel < 1e-5, (k, rel)
+        assert abs(r["loss2"] - one["loss2"]) < 1e-5
+        for k, chunks in r["grads"].items():
+            for b, g in chunks:
+                ref = one["grads"][k][0][1][b:b + g.numel()]
+                rel = float((g - ref).norm() / ref.norm().clamp_min(1e-30))
+                assert rel < 1e-5, (k, rel)

@@ -123,3 +123,52 @@ def test_multi_view_adjoint_equals_the_per_view_sum(cuda):
     for k in ref:
         assert float(ref[k].abs().max()) > 0, k
         assert rel_l2(got[k].cpu().numpy(), ref[k].cpu().numpy()) < 1e-6, k
+
+
+def test_colour_after_the_projection_equals_the_fused_colour(cuda):
+    """mg_sh_colour_views (the colour of a projection run without SH, as the
+    trainer does on several GPUs so the SH rows can still be in flight) is bit
+    for bit the fused projection's colour, for every view, with 0 where a
+    Gaussian is not valid."""
+    _, d, views = _scene(37, 5)
+    fused = _forward_views(d, views)
+    V, n = len(views), N_G
+    cams = (_lib.Camera * V)(*[_cam(v) for v in views])
+    geo = {k: torch.empty_like(v) for k, v in fused.items()}
+    _lib.call("mg_preprocess_forward_views", ptr(d["means"]), ptr(d["quats"]), ptr(d["scales"]),
+              None, None, _lib.SH_SPLIT, ptr(d["opac"]), _lib.C.cast(cams, _lib.C.c_void_p), V,
+              -1, n, n, ptr(geo["uv"]), ptr(geo["conic"]), ptr(geo["depth"]), ptr(geo["rxy"]),
+              ptr(geo["valid"]), None, None, None, _lib.stream())
+    for name in ("uv", "conic", "depth", "rxy", "valid"):
+        assert torch.equal(geo[name], fused[name]), name
+    centres = (_lib.C.c_float * (3 * V))()
+    for v in range(V):
+        centres[3 * v:3 * v + 3] = list(cams[v].cam_center)[:3]
+    colour = torch.full((V, n, 3), -1.0, device="cuda")
+    _lib.call("mg_sh_colour_views", ptr(d["means"]), ptr(d["sh_dc"]), ptr(d["sh_rest"]),
+              _lib.SH_SPLIT, _lib.C.cast(centres, _lib.C.c_void_p), V, 3, n, n,
+              ptr(geo["valid"]), ptr(colour), _lib.stream())
+    assert torch.equal(colour, fused["color"])
+    assert bool((colour[geo["valid"] == 0] == 0).all())
+
+
+def test_trainer_step_with_the_colour_split_equals_the_fused_step(cuda):
+    """The trainer's colour split (projection without SH, colour after the
+    binning; the default on several GPUs) gives the same loss and gradients as
+    the fused projection on one GPU."""
+    from metal_gauss_b200.engine import SEGMENTS, Trainer
+    p, _, _ = scenes.config("cfg3", n=N_G, seed=39)
+    views = scenes.sphere_views(3, 4.0, W, H, 40.0, 40, hemisphere=True)
+    g = np.random.default_rng(39)
+    targets = [torch.from_numpy(g.random((H, W, 3)).astype(np.float32)).cuda() for _ in views]
+    fused = Trainer(p, cuda, sh_degree=3)
+    split = Trainer(p, cuda, sh_degree=3)
+    split.split_colour = True
+    lf = float(fused.train_step(views, targets, 3))
+    ls = float(split.train_step(views, targets, 3))
+    # the images are identical; the views' losses are added in stream order
+    assert abs(lf - ls) <= 1e-6 * abs(lf)
+    assert torch.equal(fused._batch.color[:3], split._batch.color[:3])
+    for name, _ in SEGMENTS:   # up to the order of the rasteriser's float atomics
+        assert rel_l2(split.grad(name).cpu().numpy(), fused.grad(name).cpu().numpy()) < 1e-5, name
+        assert rel_l2(split.param(name).cpu().numpy(), fused.param(name).cpu().numpy()) < 1e-6, name
