@@ -275,9 +275,11 @@ def profiled_traffic(kernel: str, args):
         text = TRAFFIC_PROFILE.read_text()
     except OSError:
         return None, "capture summary missing"
+    commit = re.search(r"<!-- capture_commit (\S+) -->", text)
+    at = f", captured at commit {commit.group(1)}" if commit else ""
     for name, val in re.findall(r"<!-- traffic_bytes_per_launch (\S+) (\d+) -->", text):
         if name == kernel:
-            return int(val), f"{TRAFFIC_PROFILE.relative_to(ROOT)} (ncu --set full, one view)"
+            return int(val), f"{TRAFFIC_PROFILE.relative_to(ROOT)} (ncu --set full, one view{at})"
     return None, f"no capture of {kernel}"
 
 
@@ -325,10 +327,14 @@ def run_ours(args, rank, world, local):
     # overhead would perturb the timed region, so it runs separately)
     n_instr = max(2, min(5, args.steps))
     trainer.stage_events = {}
+    trainer.walked = []
     for i in range(n_instr):
         step(args.warmup + i)
     torch.cuda.synchronize()
     stage_ms = {k: v for k, v in trainer.stage_times_ms().items()}
+    # list entries the rasteriser walks per view, averaged over the
+    # instrumented pass's views (the timed steps launch no reduction for it)
+    walked = float(torch.stack(trainer.walked).double().mean()) if trainer.walked else 0.0
     # ZeRO-1 on several GPUs: per step, max over ranks, the time the step's
     # stream waited for the counts, loss and geometry reduce-scatter, and at
     # the next step for the geometry and SH all-gathers -- the part of the
@@ -345,7 +351,6 @@ def run_ours(args, rank, world, local):
     # timed region: events only around the dominant kernel
     trainer.stage_events = {}
     trainer.timed_stages = {dom}
-    trainer.walked = []
     barrier(world)
     L = _lib.load()
     launches0 = L.mg_launch_count()
@@ -362,7 +367,6 @@ def run_ours(args, rank, world, local):
         torch.cuda.synchronize()
         barrier(world)
     launches = L.mg_launch_count() - launches0
-    walked = float(torch.stack(trainer.walked).double().mean()) if trainer.walked else 0.0
     dom_times = trainer.stage_times_ms().get(dom, [])
     trainer.stage_events = None
     trainer.timed_stages = None

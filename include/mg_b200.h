@@ -626,9 +626,9 @@ mg_status mg_l1_ssim_loss_u8(const float* x, const uint8_t* y, const float* w,
  * widened by `margin` on every side, the mean projects in front of
  * `near_plane`; Gaussians no camera sees take the largest such depth of any
  * Gaussian (all take 1 when none is seen); then depth / max focal * sqrt(0.2).
- * Only viewmat, fx, fy, cx, cy, width and height of `cams` are read.
- * Synchronises `stream` once per 64 cameras (the filter is recomputed every
- * few hundred steps). */
+ * Only viewmat, fx, fy, cx, cy, width and height of `cams` are read; they
+ * travel in the launches' parameters, so nothing is copied to the device and
+ * nothing synchronises. */
 size_t mg_compute_3d_filter_scratch_bytes(void);
 mg_status mg_compute_3d_filter(const float* means, int64_t n, const mg_camera* cams,
                                int32_t n_views, float near_plane, float margin,

@@ -24,17 +24,19 @@ struct FilterCams {
 
 // Pass 1 (mipfilter.py:49-68): the smallest camera depth among the views in
 // whose (margin-widened) frame the mean projects in front of `near`, +inf
-// when none. Cameras come in chunks of at most kMaxFilterViews: a chunk
+// when none. Cameras come in chunks of at most kMaxFilterViews, each passed
+// by value in the launch's parameters (4.6 KB; sm_100 takes up to 32 KB), so
+// the launches need no device copy of them and no synchronisation: a chunk
 // after the first continues from the running minimum in dist, and the last
 // one puts the largest finite minimum over all Gaussians into *max_bits
 // (positive floats order like their bit patterns).
 __global__ void filter_depth_kernel(const float* __restrict__ means, int64_t n,
-                                    const FilterCams* __restrict__ cams, int n_views,
+                                    const __grid_constant__ FilterCams cams, int n_views,
                                     float near, float margin, int first, int last,
                                     float* __restrict__ dist, uint32_t* __restrict__ max_bits) {
     __shared__ FilterCams s;
     for (int i = threadIdx.x; i < (int)(sizeof(FilterCams) / 4); i += blockDim.x)
-        reinterpret_cast<float*>(&s)[i] = reinterpret_cast<const float*>(cams)[i];
+        reinterpret_cast<float*>(&s)[i] = reinterpret_cast<const float*>(&cams)[i];
     __syncthreads();
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     float d = __int_as_float(0x7f800000);
@@ -138,9 +140,7 @@ extern "C" mg_status mg_compute_3d_filter(const float* means, int64_t n, const m
         focal = std::max(focal, std::max(cams[v].fx, cams[v].fy));
     if (!(focal > 0.0f)) focal = 1.0f;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    char* p = static_cast<char*>(scratch);
-    uint32_t* max_bits = reinterpret_cast<uint32_t*>(p);
-    FilterCams* d_cams = reinterpret_cast<FilterCams*>(p + 256);
+    uint32_t* max_bits = static_cast<uint32_t*>(scratch);
     if (cudaMemsetAsync(max_bits, 0, sizeof(uint32_t), st) != cudaSuccess)
         return check_launch("compute_3d_filter memset");
     // cameras in chunks of kMaxFilterViews (one launch each, the running
@@ -157,25 +157,17 @@ extern "C" mg_status mg_compute_3d_filter(const float* means, int64_t n, const m
             h.fx[k] = cm.fx; h.fy[k] = cm.fy; h.cx[k] = cm.cx; h.cy[k] = cm.cy;
             h.W[k] = (float)cm.width; h.H[k] = (float)cm.height;
         }
-        // the kernel reads the camera block from device memory: the host copy
-        // must outlive the copy, and the next chunk reuses the device block
-        if (cudaMemcpyAsync(d_cams, &h, sizeof(FilterCams), cudaMemcpyHostToDevice, st) !=
-            cudaSuccess)
-            return check_launch("compute_3d_filter copies");
         filter_depth_kernel<<<ceil_div(n, 256), 256, 0, st>>>(
-            means, n, d_cams, std::max(nv, 0), near_plane, margin, c == 0 ? 1 : 0,
+            means, n, h, std::max(nv, 0), near_plane, margin, c == 0 ? 1 : 0,
             c == chunks - 1 ? 1 : 0, filter_out, max_bits);
         MG_TRY(check_launch("compute_3d_filter depth"));
-        if (cudaStreamSynchronize(st) != cudaSuccess) return check_launch("compute_3d_filter");
     }
     filter_finish_kernel<<<ceil_div(n, 256), 256, 0, st>>>(filter_out, n, max_bits, focal,
                                                           std::sqrt(0.2f));
     return check_launch("compute_3d_filter finish");
 }
 
-extern "C" size_t mg_compute_3d_filter_scratch_bytes(void) {
-    return 256 + ((sizeof(FilterCams) + 255) & ~(size_t)255);
-}
+extern "C" size_t mg_compute_3d_filter_scratch_bytes(void) { return 256; }
 
 extern "C" mg_status mg_apply_3d_filter(const float* scales, const float* opacities,
                                         const float* filter_3d, int64_t n, float* out_scales,

@@ -789,8 +789,10 @@ class Trainer:
                                     ptr(st.color), n, ptr(b.splats), ptr(st.grad2d), s),
                    "pack_splats")
         self._end(ev)
-        # tile walk lengths only when the instrumented pass asks for them
-        work = b.tile_work if self.stage_events is not None else None
+        # tile walk lengths only in a fully instrumented pass (every stage
+        # timed): their sum is a torch reduction, kept out of timed steps
+        work = (b.tile_work if self.stage_events is not None and self.timed_stages is None
+                else None)
         ev = self._begin("raster_fwd")
         _lib.check(L.mg_rasterize_forward(
             ptr(b.splats), ptr(ids), ptr(offsets), m, W, H, self.tile, tiles_x, bgp,
