@@ -65,6 +65,46 @@ __device__ __forceinline__ void record_device_error(int32_t* word, int32_t code)
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// One warp copies `count` floats from global `src` to shared `dst`: 16-byte
+// asynchronous copies (cp.async, every copy in flight before one wait) when
+// both addresses are 16-byte aligned and count is a multiple of 4, otherwise
+// plain loads. A loop of dependent 4-byte load/store pairs leaves the warp
+// waiting on one load at a time; here the latency is paid once. Arguments
+// are warp-uniform; ends with __syncwarp().
+__device__ __forceinline__ void warp_copy_to_shared(const float* __restrict__ src, int count,
+                                                    float* dst, int lane) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) &
+                      15u) == 0u &&
+                     (count & 3) == 0;
+    if (vec) {
+        const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst);
+        for (int i = lane; i < count / 4; i += 32)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s + 16u * i),
+                         "l"(src + 4 * i)
+                         : "memory");
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    } else {
+        for (int i = lane; i < count; i += 32) dst[i] = __ldg(src + i);
+    }
+    __syncwarp();
+}
+
+// The reverse: one warp writes `count` floats from shared `src` to global
+// `dst`, as 16-byte stores when aligned.
+__device__ __forceinline__ void warp_copy_from_shared(const float* src, int count,
+                                                      float* __restrict__ dst, int lane) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) &
+                      15u) == 0u &&
+                     (count & 3) == 0;
+    if (vec) {
+        for (int i = lane; i < count / 4; i += 32)
+            reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+    } else {
+        for (int i = lane; i < count; i += 32) dst[i] = src[i];
+    }
+}
+
 // ---------------------------------------------------------------- camera
 
 // Camera as the kernels see it: rows of the world->camera transform with the

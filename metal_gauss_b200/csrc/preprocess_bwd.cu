@@ -516,7 +516,7 @@ sh_backward_views_kernel(const float* __restrict__ means, const float* __restric
                          ViewCentres centres, const float* __restrict__ dpre, int n_views,
                          int64_t view_stride, float* __restrict__ d_means,
                          float* __restrict__ d_sh_dc, float* __restrict__ d_sh_rest) {
-    __shared__ float s_sh[kBwdBlock / 32][32 * 45];
+    __shared__ __align__(16) float s_sh[kBwdBlock / 32][32 * 45];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t g = (int64_t)blockIdx.x * kBwdBlock + threadIdx.x;
     const int64_t g0 = g - lane;
@@ -524,8 +524,7 @@ sh_backward_views_kernel(const float* __restrict__ means, const float* __restric
     const int64_t warp_n = min((int64_t)32, n - g0);
     float* blk = s_sh[wib];
     const int total = (int)max((int64_t)0, warp_n) * 45;
-    for (int i = lane; i < total; i += 32) blk[i] = __ldg(sh_rest + g0 * 45 + i);
-    __syncwarp();
+    warp_copy_to_shared(sh_rest + g0 * 45, total, blk, lane);
     const int nb = (sh_degree + 1) * (sh_degree + 1);
     float acc[16][3];
 #pragma unroll
@@ -576,7 +575,7 @@ sh_backward_views_kernel(const float* __restrict__ means, const float* __restric
         }
     }
     __syncwarp();
-    for (int i = lane; i < total; i += 32) d_sh_rest[g0 * 45 + i] = blk[i];
+    warp_copy_from_shared(blk, total, d_sh_rest + g0 * 45, lane);
 }
 
 }  // namespace
