@@ -209,6 +209,7 @@ mg_status mg_preprocess_backward_accumulate(
  * the activations BEFORE Mip-Splatting's 3D filter (mipfilter.py:79-93): the
  * forward projected mg_apply_3d_filter's outputs, and the gradients are
  * carried back through the filter (train.py:221-227 with filter_3d constant).
+ * grad2d must be 16-byte aligned (records are read as three 16-byte words).
  * No reference counterpart. */
 mg_status mg_preprocess_backward_views(
     const float* means, const float* quats, const float* scales,

@@ -456,17 +456,24 @@ preprocess_backward_views_kernel(const float* __restrict__ means,
     float dSym[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const CovFrame F = cov_frame(q4, s);
     bool any = false;
+    static_assert(MG_G2D_STRIDE == 12 && MG_G2D_UV == 0 && MG_G2D_OPACITY == 2 &&
+                      MG_G2D_CONIC == 4 && MG_G2D_COLOR == 8,
+                  "the record is read as three float4: uv op abs | conic pad | colour pad");
     for (int v = 0; v < n_views; ++v) {
         const int64_t o = (int64_t)v * view_stride + g;
-        const float* r = grad2d + o * MG_G2D_STRIDE;
-        dpre[3 * o + 0] = color[3 * o + 0] > 0.f ? r[MG_G2D_COLOR + 0] : 0.f;
-        dpre[3 * o + 1] = color[3 * o + 1] > 0.f ? r[MG_G2D_COLOR + 1] : 0.f;
-        dpre[3 * o + 2] = color[3 * o + 2] > 0.f ? r[MG_G2D_COLOR + 2] : 0.f;
-        if (valid[o] == 0) continue;
-        projection_adjoint_view(cams.c[v], mx, my, mz, F.S, r[MG_G2D_UV], r[MG_G2D_UV + 1],
-                                r[MG_G2D_CONIC], r[MG_G2D_CONIC + 1], r[MG_G2D_CONIC + 2], dmx,
+        // the record's three 16-byte words, the forward colour and the valid
+        // flag are loaded together before any of them is used
+        const float4* rec = reinterpret_cast<const float4*>(grad2d) + 3 * o;
+        const float4 r0 = rec[0], r1 = rec[1], r2 = rec[2];
+        const float c0 = color[3 * o + 0], c1 = color[3 * o + 1], c2 = color[3 * o + 2];
+        const int32_t ok = valid[o];
+        dpre[3 * o + 0] = c0 > 0.f ? r2.x : 0.f;
+        dpre[3 * o + 1] = c1 > 0.f ? r2.y : 0.f;
+        dpre[3 * o + 2] = c2 > 0.f ? r2.z : 0.f;
+        if (ok == 0) continue;
+        projection_adjoint_view(cams.c[v], mx, my, mz, F.S, r0.x, r0.y, r1.x, r1.y, r1.z, dmx,
                                 dmy, dmz, dSym);
-        dop += r[MG_G2D_OPACITY];
+        dop += r0.z;
         any = true;
     }
     if (!any) return;
@@ -667,8 +674,9 @@ extern "C" mg_status mg_preprocess_backward_views(
                    d_quats && d_log_scales && d_logit_opac && dpre_out,
                "preprocess_backward_views: null pointer");
     MG_REQUIRE((reinterpret_cast<uintptr_t>(quats) & 15u) == 0u &&
-                   (reinterpret_cast<uintptr_t>(d_quats) & 15u) == 0u,
-               "preprocess_backward_views: quats must be 16-byte aligned");
+                   (reinterpret_cast<uintptr_t>(d_quats) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(grad2d) & 15u) == 0u,
+               "preprocess_backward_views: quats and grad2d must be 16-byte aligned");
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     for (int v0 = 0; v0 < n_views; v0 += kMaxViewsPerLaunch) {
         const int nv = n_views - v0 < kMaxViewsPerLaunch ? n_views - v0 : kMaxViewsPerLaunch;

@@ -159,6 +159,24 @@ __device__ __forceinline__ float pixel_value(const uint8_t* __restrict__ src, in
     return tab->v[src[i]];
 }
 
+// stage_channel for a float image as 4-byte asynchronous copies (zero-filled
+// outside the image); the caller commits and waits.
+__device__ __forceinline__ void stage_channel_async(const float* __restrict__ src, int c, int W,
+                                                    int H, int ox, int oy, float (*dst)[kSP]) {
+    for (int ly = threadIdx.y; ly < kSH; ly += 8) {
+        const int gy = oy + ly - kR;
+        for (int lx = threadIdx.x; lx < kSP; lx += 32) {
+            const int gx = ox + lx - kR;
+            const bool ok = lx < kSW && gx >= 0 && gx < W && gy >= 0 && gy < H;
+            const int64_t i = ok ? ((int64_t)gy * W + gx) * 3 + c : 0;
+            const uint32_t d = (uint32_t)__cvta_generic_to_shared(&dst[ly][lx]);
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src + i),
+                         "r"(ok ? 4 : 0)
+                         : "memory");
+        }
+    }
+}
+
 // Stages channel c of `src` (H, W, 3) around the tile at (ox, oy), zero outside.
 template <typename T>
 __device__ __forceinline__ void stage_channel(const T* __restrict__ src, int c, int W, int H,
@@ -202,8 +220,10 @@ loss_moments_kernel(const float* __restrict__ x, const TY* __restrict__ y,
     }
     {
         const int c = blockIdx.z;  // one colour channel per block
-        stage_channel(x, c, W, H, ox, oy, s_x);
+        stage_channel_async(x, c, W, H, ox, oy, s_x);  // in flight while y is staged
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
         stage_channel(y, c, W, H, ox, oy, s_y, &s_tab);
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncthreads();
         for (int it = tid; it < kHItems; it += 256) {
             const int row = it >> 3, g = it & 7;
@@ -307,17 +327,26 @@ loss_grad_kernel(const float* __restrict__ x, const TY* __restrict__ y,
     if (sizeof(TY) == 1) s_tab.fill();  // ordered by the barrier after the staging
     {
         const int c = blockIdx.z;  // one colour channel per block
+        // the three adjoint maps with their halo, as 4-byte asynchronous
+        // copies (all in flight before one wait; zero-filled outside the
+        // image)
         for (int ly = ty; ly < kSH; ly += 8) {
             const int gy = oy + ly - kR;
             for (int lx = tx; lx < kSP; lx += 32) {
                 const int gx = ox + lx - kR;
                 const bool ok = lx < kSW && gx >= 0 && gx < W && gy >= 0 && gy < H;
-                const int64_t o = (int64_t)gy * W + gx;
+                const int64_t o = ok ? (int64_t)gy * W + gx : 0;
 #pragma unroll
-                for (int q = 0; q < 3; ++q)
-                    s_a[q][ly][lx] = ok ? adj[(3 * c + q) * npix + o] : 0.f;
+                for (int q = 0; q < 3; ++q) {
+                    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&s_a[q][ly][lx]);
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst),
+                                 "l"(adj + (3 * c + q) * npix + o), "r"(ok ? 4 : 0)
+                                 : "memory");
+                }
             }
         }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncthreads();
         for (int it = tid; it < kHItems; it += 256) {
             const int row = it >> 3, g = it & 7;
