@@ -155,8 +155,13 @@ struct OnesweepSmem {
     uint32_t tile_id;
 };
 
+// Resident 256-thread CTAs per SM the pass's registers are held to (0: none;
+// 4 -- 64 registers, no spills -- measured the same on the bench).
+#ifndef MG_SORT_MIN_CTAS
+#define MG_SORT_MIN_CTAS 0
+#endif
 template <typename K>
-__global__ void __launch_bounds__(kSortThreads)
+__global__ void __launch_bounds__(kSortThreads, MG_SORT_MIN_CTAS)
 onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                      K* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                      int64_t n, int shift, int digit_bits,
