@@ -497,7 +497,7 @@ def run_render(args, rank, world, local):
     r = Renderer(p, dev, sh_degree=spec["sh_degree"], antialias=spec["antialias"],
                  background=spec["background"], batch=spec["batch"])
     for _ in range(max(args.warmup, 3)):
-        r.render(mine[:spec["batch"]])
+        r.render(mine[:spec["batch"]], check=False)
     torch.cuda.synchronize()
     steps = max(1, min(args.steps, 3))
     L = _lib.load()
@@ -507,19 +507,23 @@ def run_render(args, rank, world, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            out = r.render(mine)
+            # the device error word is checked once after the timed passes
+            # (a check per pass synchronises the host between them)
+            out = r.render(mine, check=False)
             del out
         e1.record()
         torch.cuda.synchronize()
         launches = (L.mg_launch_count() - launches0) // steps
+    _lib.check_device_error("render")
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     W, H = views[0].width, views[0].height
     host = [torch.empty(H, W, 4, dtype=torch.float32).pin_memory() for _ in range(2)]
     barrier(world)
     e0.record()
-    for k, (rgb, alpha) in enumerate(r.render(mine)):
+    for k, (rgb, alpha) in enumerate(r.render(mine, check=False)):
         host[k % 2][..., :3].copy_(rgb, non_blocking=True)
         host[k % 2][..., 3].copy_(alpha, non_blocking=True)
+    _lib.check_device_error("render")    # before the frames count as delivered
     e1.record()
     torch.cuda.synchronize()
     e_ms = max_over_ranks(e0.elapsed_time(e1), world)
