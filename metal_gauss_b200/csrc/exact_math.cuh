@@ -244,6 +244,33 @@ struct RectQuadratic {
         e.ta = (a * e.ex) * e.ex;
         return e;
     }
+    // The candidate of min_q_over_rect on a vertical side at column edge e
+    // between rows t and bt. A walk along a row computes it once per column
+    // edge: the right side's candidate of one tile is the left side's of the
+    // next (same operations on the same operands).
+    __device__ __forceinline__ float side_q(const ColEdge& e, const RowEdge& t,
+                                            const RowEdge& bt) const {
+        const float ey = clampf(muy - e.s, t.y, bt.y) - muy;
+        return (e.ta + ((b2 * e.ex) * ey)) + ((c * ey) * ey);
+    }
+    // min_q with the two vertical sides' candidates given (ql = side_q(l, t,
+    // bt), qr = side_q(r, t, bt)): the same minimum of the same four values.
+    __device__ __forceinline__ float min_q_sides(const ColEdge& l, const ColEdge& r,
+                                                 const RowEdge& t, const RowEdge& bt, float ql,
+                                                 float qr) const {
+        if (mux >= l.x && mux <= r.x && muy >= t.y && muy <= bt.y) return 0.0f;
+        float best = __int_as_float(0x7f800000);
+        {
+            const float ex = clampf(mux - t.s, l.x, r.x) - mux;
+            best = fminf(best, (((a * ex) * ex) + ((b2 * ex) * t.ey)) + t.tc);
+        }
+        {
+            const float ex = clampf(mux - bt.s, l.x, r.x) - mux;
+            best = fminf(best, (((a * ex) * ex) + ((b2 * ex) * bt.ey)) + bt.tc);
+        }
+        best = fminf(best, ql);
+        return fminf(best, qr);
+    }
     // min_q_over_rect(mux, muy, ca, cb, ccz, l.x, r.x, t.y, bt.y)
     __device__ __forceinline__ float min_q(const ColEdge& l, const ColEdge& r, const RowEdge& t,
                                            const RowEdge& bt) const {

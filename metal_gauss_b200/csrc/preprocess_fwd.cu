@@ -398,12 +398,15 @@ __device__ __forceinline__ uint32_t bin_walk(
         const RowEdge bottom = rq.row_edge(fminf((float)((ty + 1) * tile), (float)H));
         const float y0 = top.y, y1 = bottom.y;
         ColEdge right = rq.col_edge((float)(tr.x0 * tile));
+        float q_right = rq.side_q(right, top, bottom);
         for (int tx = tr.x0; tx <= tr.x1; ++tx) {
             const ColEdge left = right;
+            const float q_left = q_right;
             right = rq.col_edge(fminf((float)((tx + 1) * tile), (float)W));
+            q_right = rq.side_q(right, top, bottom);
             const float x0 = left.x, x1 = right.x;
             const int b = bit++;
-            if (rq.min_q(left, right, top, bottom) >= thr) continue;
+            if (rq.min_q_sides(left, right, top, bottom, q_left, q_right) >= thr) continue;
             if (masked) mask |= 1ull << b;
             if (kCut == 1 && can_cover) {
                 const uint32_t q =
@@ -433,6 +436,89 @@ __device__ __forceinline__ uint32_t bin_walk(
                           (masked ? ((uint32_t)rw | ((uint32_t)rh << 8)) : 0u) |
                               ((uint32_t)cut.bin << 16));
     return cnt;
+}
+
+// Rectangles of more than kCoopTiles tiles (the largest whose pass mask a
+// record holds) are walked by a whole warp, one Gaussian at a time: one lane
+// walking hundreds of tiles would hold its warp, and at the end of a launch
+// its SM, while the other lanes idle. Every lane calls warp_walk with the
+// same Gaussian. The lanes form a grid of cw columns x ch rows (cw = the
+// rectangle's width up to 32, ch = 32 / cw) stepped over the rectangle;
+// each tile gets bin_walk's test on edges computed from the same
+// coordinates, so the decisions, the histogram adds and the pair set are
+// bin_walk's (a tile's top edge is the row above's bottom edge there, and a
+// left edge the previous column's right edge). Pairs are written in the order
+// the warp finds them, not row-major: a Gaussian's pairs lie in distinct
+// tiles, so the stable tile sort puts them in the same places either way.
+// Returns the count (kept pairs for kCut 2) in every lane.
+constexpr int kCoopTiles = 64;
+
+template <bool kEmitPair, int kCut>
+__device__ __forceinline__ uint32_t warp_walk(int lane, float mux, float muy, float rx, float ry,
+                                              float ca, float cb, float cc, float op, int tile,
+                                              int tiles_x, int tiles_y, int W, int H,
+                                              uint32_t* pair_tiles, uint32_t* pair_ids,
+                                              int64_t write_at, uint32_t cap, uint32_t gid,
+                                              CutArgs cut, uint32_t tile_base) {
+    const TileRect tr = tile_rect(mux, muy, rx, ry, tile, tiles_x, tiles_y);
+    const float oa = 255.0f * op;
+    if (oa <= 1.0f) return 0u;
+    const float thr = 2.0f * log_f32_via_f64(oa);
+    const int rw = tr.x1 - tr.x0 + 1, rh = tr.y1 - tr.y0 + 1;
+    bool can_cover = false;  // as in bin_walk
+    if (kCut == 1) {
+        const float half_tr = 0.5f * (ca + cc);
+        const float lmax = half_tr + sqrtf(fmaxf(half_tr * half_tr - (ca * cc - cb * cb), 0.0f));
+        const float side = (float)(tile - 1);
+        can_cover = lmax * side * side <= 4.0f * thr * 1.001f;
+    }
+    const RectQuadratic rq(mux, muy, ca, cb, cc);
+    const int cw = min(rw, 32), ch = 32 / cw;
+    const int cx = lane % cw, cy = lane / cw;
+    uint32_t cnt = 0u;
+    for (int bx = 0; bx < rw; bx += cw) {
+        const int tx = tr.x0 + bx + cx;
+        const bool col = cy < ch && bx + cx < rw;
+        ColEdge left{}, right{};
+        if (col) {
+            left = rq.col_edge((float)(tx * tile));
+            right = rq.col_edge(fminf((float)((tx + 1) * tile), (float)W));
+        }
+        for (int by = 0; by < rh; by += ch) {
+            const int ty = tr.y0 + by + cy;
+            bool pass = false;
+            if (col && by + cy < rh) {
+                const RowEdge top = rq.row_edge((float)(ty * tile));
+                const RowEdge bottom = rq.row_edge(fminf((float)((ty + 1) * tile), (float)H));
+                pass = !(rq.min_q(left, right, top, bottom) >= thr);
+                if (kCut == 1 && pass && can_cover) {
+                    const uint32_t q = tile_optical_depth(mux, muy, ca, cb, cc, op, thr, left.x,
+                                                          right.x, top.y, bottom.y);
+                    if (q) atomicAdd(&cut.hist[(ty * tiles_x + tx) * kCutBins + cut.bin], q);
+                }
+                if (kCut == 2 && pass && cut.cutoff[ty * tiles_x + tx] < cut.bin) pass = false;
+            }
+            if (kEmitPair) {
+                const uint32_t bal = __ballot_sync(0xffffffffu, pass);
+                if (pass) {
+                    const uint32_t k = cnt + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+                    if (k < cap) {
+                        pair_tiles[write_at + k] = tile_base + (uint32_t)(ty * tiles_x + tx);
+                        pair_ids[write_at + k] = gid;
+                    }
+                }
+                cnt += (uint32_t)__popc(bal);
+            } else {
+                cnt += pass ? 1u : 0u;
+            }
+        }
+    }
+    if (!kEmitPair) cnt = __reduce_add_sync(0xffffffffu, cnt);
+    return cnt;
+}
+
+__device__ __forceinline__ bool coop_rect(const TileRect& tr) {
+    return (tr.x1 - tr.x0 + 1) * (tr.y1 - tr.y0 + 1) > kCoopTiles;
 }
 
 __global__ void bin_count_kernel(const float2* __restrict__ uv,
@@ -522,7 +608,8 @@ __device__ __forceinline__ int block_sorted_slot(int cls) {
 
 // Cost class of a Gaussian's count walk: the shape of its tile rectangle
 // (rows, then columns), so a warp's lanes mostly run the same row and column
-// loop trip counts; no tile (invalid) first, items past the end last.
+// loop trip counts; no tile (invalid) first, rectangles the whole warp walks
+// (warp_walk) together, items past the end last.
 __device__ __forceinline__ int64_t block_sorted_gaussian(const float2* __restrict__ uv,
                                                          const float2* __restrict__ rxy,
                                                          const int32_t* __restrict__ valid,
@@ -536,7 +623,7 @@ __device__ __forceinline__ int64_t block_sorted_gaussian(const float2* __restric
             const float2 mu = uv[own], r = rxy[own];
             const TileRect tr = tile_rect(mu.x, mu.y, r.x, r.y, tile, tiles_x, tiles_y);
             const int rh = min(tr.y1 - tr.y0 + 1, 9), rw = min(tr.x1 - tr.x0 + 1, 16);
-            cls = 1 + (rh - 1) * 16 + (rw - 1);  // 1 .. 144
+            cls = coop_rect(tr) ? 145 : 1 + (rh - 1) * 16 + (rw - 1);  // 1 .. 145
         }
     }
     return (int64_t)blockIdx.x * blockDim.x + block_sorted_slot(cls);
@@ -599,23 +686,49 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
             *bv.overflow = 1;
     }
     const int64_t g = block_sorted_gaussian(uv, rxy, valid, n, tile, tiles_x, tiles_y);
-    if (g >= n) return;
+    const int lane = threadIdx.x & 31;
     uint32_t c = 0u;
-    if (valid[g] != 0) {
+    bool big = false;
+    int gbin = 0;
+    if (g < n && valid[g] != 0) {
         const float2 mu = uv[g], r = rxy[g];
-        if (hist) {
-            const CutArgs cut{hist, nullptr, cut_bin(depth[g], ~range[0], range[1])};
-            c = bin_walk<false, false, 1>(mu.x, mu.y, r.x, r.y, conic[3 * g],
-                                          conic[3 * g + 1], conic[3 * g + 2], opacity[g],
-                                          0u, tile, tiles_x, tiles_y, W, H, nullptr, nullptr,
-                                          nullptr, nullptr, 0, 0u, 0, recs + g, cut);
-        } else {
-            c = bin_walk<false, false>(mu.x, mu.y, r.x, r.y, conic[3 * g], conic[3 * g + 1],
-                                       conic[3 * g + 2], opacity[g], 0u, tile, tiles_x,
-                                       tiles_y, W, H, nullptr, nullptr, nullptr, nullptr,
-                                       0, 0u, 0, recs + g);
+        big = coop_rect(tile_rect(mu.x, mu.y, r.x, r.y, tile, tiles_x, tiles_y));
+        if (hist) gbin = cut_bin(depth[g], ~range[0], range[1]);
+        if (!big) {
+            if (hist)
+                c = bin_walk<false, false, 1>(mu.x, mu.y, r.x, r.y, conic[3 * g],
+                                              conic[3 * g + 1], conic[3 * g + 2], opacity[g],
+                                              0u, tile, tiles_x, tiles_y, W, H, nullptr,
+                                              nullptr, nullptr, nullptr, 0, 0u, 0, recs + g,
+                                              CutArgs{hist, nullptr, gbin});
+            else
+                c = bin_walk<false, false>(mu.x, mu.y, r.x, r.y, conic[3 * g],
+                                           conic[3 * g + 1], conic[3 * g + 2], opacity[g], 0u,
+                                           tile, tiles_x, tiles_y, W, H, nullptr, nullptr,
+                                           nullptr, nullptr, 0, 0u, 0, recs + g);
         }
     }
+    // the warp's large rectangles, one at a time (their records say: walk
+    // again)
+    for (uint32_t pend = __ballot_sync(0xffffffffu, big); pend; pend &= pend - 1u) {
+        const int src = __ffs(pend) - 1;
+        const int64_t gs = __shfl_sync(0xffffffffu, g, src);
+        const int bin = __shfl_sync(0xffffffffu, gbin, src);
+        const float2 mu = uv[gs], r = rxy[gs];
+        const float ca = conic[3 * gs], cb = conic[3 * gs + 1], cc = conic[3 * gs + 2];
+        const uint32_t k =
+            hist ? warp_walk<false, 1>(lane, mu.x, mu.y, r.x, r.y, ca, cb, cc, opacity[gs], tile,
+                                       tiles_x, tiles_y, W, H, nullptr, nullptr, 0, 0u, 0u,
+                                       CutArgs{hist, nullptr, bin}, 0u)
+                 : warp_walk<false, 0>(lane, mu.x, mu.y, r.x, r.y, ca, cb, cc, opacity[gs], tile,
+                                       tiles_x, tiles_y, W, H, nullptr, nullptr, 0, 0u, 0u,
+                                       CutArgs{nullptr, nullptr, 0}, 0u);
+        if (lane == src) {
+            c = k;
+            recs[g] = make_uint4(0u, 0u, 0u, (uint32_t)bin << 16);
+        }
+    }
+    if (g >= n) return;
     counts[g] = c;
     dkeys[g] = c > 0u ? view_depth_key(depth[g], range, v, bv.key_shift)
                       : view_no_depth_key(range, v, bv.key_shift);
@@ -638,19 +751,11 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
                                 uint32_t* __restrict__ pair_tiles,
                                 uint32_t* __restrict__ pair_ids, BinViews bv) {
     const int64_t sl = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (sl >= n) return;
+    const int lane = threadIdx.x & 31;
+    const int n_tiles = tiles_x * tiles_y;
     // view v owns the batch's sorted slots [v n, (v + 1) n); its pairs carry
     // tiles v * n_tiles + t and the Gaussian's index within the view
     const int v = blockIdx.y;
-    const int64_t vout = (int64_t)v * n, s = vout + sl;
-    const uint32_t gv = sorted_gid[s];
-    const uint32_t g = gv - (uint32_t)vout;
-    if ((int64_t)g >= n) return;
-    const uint32_t cnt = counts[gv];
-    if (cnt == 0u) return;
-    const int64_t at = offsets[s];
-    if (at + cnt > m) return;
-    const int n_tiles = tiles_x * tiles_y;
     const uint32_t tile_base = (uint32_t)v * (uint32_t)n_tiles;
     {
         const int64_t vin = (int64_t)v * bv.in_stride;
@@ -658,45 +763,66 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
         opacity += (int64_t)v * bv.opac_stride;
         if (cutoff) cutoff += (int64_t)v * n_tiles;
     }
-    const uint4 rec = recs[gv];
-    const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
-    const int gbin = (int)((rec.w >> 16) & 0xffu);
-    if (rw != 0u) {
-        // the count walk's decisions: row-major bits over the rectangle
-        uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
-        const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
-        const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
-        uint32_t k = 0u;
-        for (uint32_t r = 0; r < rh && mask; ++r) {
-            uint64_t row = mask & row_bits;
-            mask >>= rw;
-            const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
-            while (row) {
-                const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
-                row &= row - 1ull;
-                if (cutoff && cutoff[trow + b] < gbin) continue;
-                if (k < cnt) {
-                    pair_tiles[at + k] = tile_base + trow + b;
-                    pair_ids[at + k] = g;
+    int gbin = 0;
+    uint32_t g = 0u, cnt = 0u;
+    int64_t at = 0;
+    bool again = false;
+    if (sl < n) {
+        const int64_t s = (int64_t)v * n + sl;
+        const uint32_t gv = sorted_gid[s];
+        g = gv - (uint32_t)v * (uint32_t)n;
+        if ((int64_t)g < n) cnt = counts[gv];
+        if (cnt != 0u) {
+            at = offsets[s];
+            if (at + cnt > m) cnt = 0u;
+        }
+        if (cnt != 0u) {
+            const uint4 rec = recs[gv];
+            const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
+            gbin = (int)((rec.w >> 16) & 0xffu);
+            again = rw == 0u;  // a large rectangle: the warp walks it again
+            if (!again) {
+                // the count walk's decisions: row-major bits over the rectangle
+                uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
+                const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
+                const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
+                uint32_t k = 0u;
+                for (uint32_t r = 0; r < rh && mask; ++r) {
+                    uint64_t row = mask & row_bits;
+                    mask >>= rw;
+                    const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
+                    while (row) {
+                        const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
+                        row &= row - 1ull;
+                        if (cutoff && cutoff[trow + b] < gbin) continue;
+                        if (k < cnt) {
+                            pair_tiles[at + k] = tile_base + trow + b;
+                            pair_ids[at + k] = g;
+                        }
+                        ++k;
+                    }
                 }
-                ++k;
             }
         }
-        return;
     }
-    const float2 mu = uv[g], r = rxy[g];
-    if (cutoff)
-        bin_walk<false, true, 2>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
-                                 conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
-                                 opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
-                                 nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g, nullptr,
-                                 CutArgs{nullptr, cutoff, gbin}, tile_base);
-    else
-        bin_walk<false, true>(mu.x, mu.y, r.x, r.y, conic[3 * (int64_t)g],
-                              conic[3 * (int64_t)g + 1], conic[3 * (int64_t)g + 2],
-                              opacity[g], 0u, tile, tiles_x, tiles_y, W, H, nullptr,
-                              nullptr, pair_tiles, pair_ids, at, cnt, (int32_t)g, nullptr,
-                              CutArgs{nullptr, nullptr, 0}, tile_base);
+    for (uint32_t pend = __ballot_sync(0xffffffffu, again); pend; pend &= pend - 1u) {
+        const int src = __ffs(pend) - 1;
+        const uint32_t gs = __shfl_sync(0xffffffffu, g, src);
+        const int bin = __shfl_sync(0xffffffffu, gbin, src);
+        const int64_t ats = __shfl_sync(0xffffffffu, at, src);
+        const uint32_t cap = __shfl_sync(0xffffffffu, cnt, src);
+        const float2 mu = uv[gs], r = rxy[gs];
+        const float ca = conic[3 * (int64_t)gs], cb = conic[3 * (int64_t)gs + 1],
+                    cc = conic[3 * (int64_t)gs + 2];
+        if (cutoff)
+            warp_walk<true, 2>(lane, mu.x, mu.y, r.x, r.y, ca, cb, cc, opacity[gs], tile,
+                               tiles_x, tiles_y, W, H, pair_tiles, pair_ids, ats, cap, gs,
+                               CutArgs{nullptr, cutoff, bin}, tile_base);
+        else
+            warp_walk<true, 0>(lane, mu.x, mu.y, r.x, r.y, ca, cb, cc, opacity[gs], tile,
+                               tiles_x, tiles_y, W, H, pair_tiles, pair_ids, ats, cap, gs,
+                               CutArgs{nullptr, nullptr, 0}, tile_base);
+    }
 }
 
 // Saturation cut, step 1: the view's visible depth range as bit patterns
@@ -789,32 +915,45 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
         range += 2 * v;
     }
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= n || counts[g] == 0u) return;
-    const uint4 rec = recs[g];
-    const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
-    const int gbin = (int)((rec.w >> 16) & 0xffu);
+    const int lane = threadIdx.x & 31;
+    const bool has = g < n && counts[g] != 0u;
     uint32_t kept = 0u;
-    if (rw != 0u) {
-        uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
-        const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
-        const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
-        for (uint32_t r = 0; r < rh && mask; ++r) {
-            uint64_t row = mask & row_bits;
-            mask >>= rw;
-            const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
-            while (row) {
-                const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
-                row &= row - 1ull;
-                kept += cutoff[trow + b] >= gbin;
+    bool again = false;
+    int gbin = 0;
+    if (has) {
+        const uint4 rec = recs[g];
+        const uint32_t rw = rec.w & 0xffu, rh = (rec.w >> 8) & 0xffu;
+        gbin = (int)((rec.w >> 16) & 0xffu);
+        if (rw != 0u) {
+            uint64_t mask = (uint64_t)rec.x | ((uint64_t)rec.y << 32);
+            const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
+            const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
+            for (uint32_t r = 0; r < rh && mask; ++r) {
+                uint64_t row = mask & row_bits;
+                mask >>= rw;
+                const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
+                while (row) {
+                    const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
+                    row &= row - 1ull;
+                    kept += cutoff[trow + b] >= gbin;
+                }
             }
+        } else {
+            again = true;  // a large rectangle: the warp walks it again
         }
-    } else {
-        const float2 mu = uv[g], r = rxy[g];
-        kept = bin_walk<false, false, 2>(mu.x, mu.y, r.x, r.y, conic[3 * g], conic[3 * g + 1],
-                                         conic[3 * g + 2], opacity[g], 0u, tile, tiles_x,
-                                         tiles_y, W, H, nullptr, nullptr, nullptr, nullptr, 0,
-                                         0u, 0, nullptr, CutArgs{nullptr, cutoff, gbin});
     }
+    for (uint32_t pend = __ballot_sync(0xffffffffu, again); pend; pend &= pend - 1u) {
+        const int src = __ffs(pend) - 1;
+        const int64_t gs = __shfl_sync(0xffffffffu, g, src);
+        const int bin = __shfl_sync(0xffffffffu, gbin, src);
+        const float2 mu = uv[gs], r = rxy[gs];
+        const uint32_t k = warp_walk<false, 2>(
+            lane, mu.x, mu.y, r.x, r.y, conic[3 * gs], conic[3 * gs + 1], conic[3 * gs + 2],
+            opacity[gs], tile, tiles_x, tiles_y, W, H, nullptr, nullptr, 0, 0u, 0u,
+            CutArgs{nullptr, cutoff, bin}, 0u);
+        if (lane == src) kept = k;
+    }
+    if (!has) return;
     counts[g] = kept;
     if (kept == 0u) dkeys[g] = view_no_depth_key(range, v, bv.key_shift);
 }
