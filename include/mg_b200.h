@@ -355,11 +355,9 @@ mg_status mg_bin_emit(
  * the batch's pair total must stay below 2^30 - 1 (the radix sort's key
  * count; the per-view calls take more pairs per view).
  *   mg_bin_prepare_views writes n_views + 2 int64 words to totals_dev: each
- *     view's pair total, the batch's total, and an overflow flag. A set flag
- *     means some view's visible depths span more float bit patterns than
- *     the batch's shared depth keys hold (2^(32 - ceil(log2 n_views)) - 1):
- *     the call's results are then unusable and the caller bins that batch one
- *     view at a time with mg_bin_prepare / mg_bin_emit.
+ *     view's pair total, the batch's total, and a reserved word (0). One
+ *     depth sort orders the whole batch, each view's rows on their own
+ *     (keys relative to the view's nearest visible depth: any range fits).
  *   mg_bin_emit_views takes the batch total m_total and writes the pairs of
  *     view v to gauss_ids[base_v, base_v + m_v) (base_v: the totals of the
  *     views before v) and its tile offsets, starting at 0 as mg_bin_emit's,

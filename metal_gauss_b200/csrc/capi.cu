@@ -66,8 +66,7 @@ struct PrepareScratch {
     uint32_t* offsets;
     uint4* recs;  // per Gaussian: the count walk's pass mask and rectangle
     uint32_t* cut_range;  // depth range words (two per view), then the histogram
-    int32_t* overflow;    // batch depth keys that did not fit (after the range words)
-    size_t range_bytes;   // range words + overflow word
+    size_t range_bytes;   // the range words
     uint32_t* cut_hist;
     int32_t* cutoff;
     size_t cut_zero_bytes;  // range words + histogram, zeroed per call
@@ -93,8 +92,7 @@ PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles, int n_vie
     s.recs = reinterpret_cast<uint4*>(p);
     p += align256(sizeof(uint4) * (size_t)std::max<int64_t>(n, 1));
     s.cut_range = reinterpret_cast<uint32_t*>(p);
-    s.overflow = reinterpret_cast<int32_t*>(s.cut_range + 2 * n_views);
-    const size_t range_words = ((size_t)(2 * n_views + 1) + 63) & ~(size_t)63;
+    const size_t range_words = ((size_t)(2 * n_views) + 63) & ~(size_t)63;
     s.range_bytes = sizeof(uint32_t) * range_words;
     s.cut_hist = s.cut_range + range_words;  // keeps the histogram 256-byte aligned
     s.cut_zero_bytes =
@@ -102,7 +100,7 @@ PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles, int n_vie
     p += align256(s.cut_zero_bytes);
     s.cutoff = reinterpret_cast<int32_t*>(p);
     p += align256(sizeof(int32_t) * (size_t)std::max(n_tiles, 1));
-    s.sort_bytes = align256(radix_sort_scratch_bytes(n, 32, 4));
+    s.sort_bytes = align256(radix_sort_scratch_bytes(n, 32, 4, n_views));
     s.sort = p; p += s.sort_bytes;
     s.scan = p; p += align256(scan_scratch_bytes(n));
     s.total = (size_t)(p - static_cast<const char*>(base));
@@ -135,12 +133,6 @@ EmitScratch carve_emit(void* base, int64_t m, int n_tiles, int n_views = 1) {
     return s;
 }
 
-// Bits of a view index in a batch of n_views (0 for one view).
-int view_bits(int n_views) {
-    int b = 0;
-    while ((1 << b) < n_views) ++b;
-    return b;
-}
 
 }  // namespace
 
@@ -399,7 +391,7 @@ extern "C" mg_status mg_bin_prepare(const float* uv, const float* rxy, const flo
                                   saturation_cut ? s.cutoff : nullptr, BinViews{}, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, n, 32, s.sort,
-                                      s.sort_bytes, &in_alt, st));
+                                      s.sort_bytes, &in_alt, st, 1, false));
     if (in_alt &&
         cudaMemcpyAsync(s.dvals, s.dvals_alt, sizeof(uint32_t) * n, cudaMemcpyDeviceToDevice,
                         st) != cudaSuccess)
@@ -503,15 +495,14 @@ extern "C" mg_status mg_bin_prepare_views(const float* uv, const float* rxy, con
         bv.n_views = n_views;
         bv.in_stride = view_stride;
         bv.opac_stride = opacity_view_stride;
-        bv.key_shift = n_views > 1 ? 32 - view_bits(n_views) : 0;
-        bv.overflow = s.overflow;
+        bv.batch_keys = 1;
         MG_TRY(launch_bin_count_depth(uv, rxy, conic, opacity, valid, depth, n, width, height,
                                       tile, tiles_x, tiles_y, s.counts, s.dkeys, s.dvals, s.recs,
                                       s.cut_range, saturation_cut ? s.cut_hist : nullptr,
                                       saturation_cut ? s.cutoff : nullptr, bv, st));
         bool in_alt = false;
         MG_TRY(radix_sort_pairs<uint32_t>(s.dkeys, s.dvals, s.dkeys_alt, s.dvals_alt, rows, 32,
-                                          s.sort, s.sort_bytes, &in_alt, st));
+                                          s.sort, s.sort_bytes, &in_alt, st, n_views, false));
         if (in_alt && cudaMemcpyAsync(s.dvals, s.dvals_alt, sizeof(uint32_t) * rows,
                                       cudaMemcpyDeviceToDevice, st) != cudaSuccess)
             return check_launch("bin_prepare_views copy");
@@ -522,7 +513,7 @@ extern "C" mg_status mg_bin_prepare_views(const float* uv, const float* rxy, con
         return cudaMemsetAsync(totals_dev, 0, sizeof(int64_t) * (n_views + 2), st) == cudaSuccess
                    ? MG_OK
                    : check_launch("bin_prepare_views totals");
-    return launch_view_totals(s.offsets, n, n_views, s.overflow, totals_dev, st);
+    return launch_view_totals(s.offsets, n, n_views, totals_dev, st);
 }
 
 extern "C" size_t mg_bin_emit_views_scratch_bytes(int64_t n, int32_t n_views, int64_t m_total,

@@ -43,17 +43,16 @@ mg_status launch_bin_write(const float* uv, const float* rxy, const float* conic
 // Inputs are view-major with in_stride rows between views (opacity:
 // opac_stride, 0 when the views share it); the per-Gaussian outputs are
 // compact, view v's rows at v * n, and view v's cut words at cut_range + 2 v,
-// its histogram and cutoffs after those of the views before it. key_shift 0
-// keeps the single-view depth keys; otherwise a key is (v << key_shift) |
-// (depth bits - the view's smallest depth bits), so one sort orders every
-// view, and a view whose depth range needs more than key_shift bits sets
-// *overflow (the caller then bins the views one at a time).
+// its histogram and cutoffs after those of the views before it. With
+// batch_keys set, a depth key is the depth's bit pattern minus that of the
+// view's smallest visible depth (rows without a pair: 2^24 - 1), and the
+// caller sorts each view's n rows as a segment of its own; otherwise the
+// single-view keys.
 struct BinViews {
     int n_views = 1;
     int64_t in_stride = 0;
     int64_t opac_stride = 0;
-    int key_shift = 0;
-    int32_t* overflow = nullptr;
+    int batch_keys = 0;
 };
 // cut_range non-null: the range pass runs (relative depth keys); cut_hist
 // non-null: the saturation cut runs as well.
@@ -75,9 +74,9 @@ mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           uint32_t* pair_ids, const BinViews& bv, cudaStream_t stream);
 // Batch bookkeeping: per-view pair totals from the scan of the batch's depth
 // order (view v's n sorted slots start at v * n; totals[n_views] holds the
-// grand total already), and totals[n_views + 1] = *overflow.
+// grand total already), and totals[n_views + 1] = 0 (a reserved word).
 mg_status launch_view_totals(const uint32_t* offsets, int64_t n, int n_views,
-                             const int32_t* overflow, int64_t* totals, cudaStream_t stream);
+                             int64_t* totals, cudaStream_t stream);
 // Per-view tile offsets starting at 0 from the batch's tile ranges
 // (global: n_views * n_tiles + 1 entries; local: n_views * (n_tiles + 1)).
 mg_status launch_view_tile_offsets(const int32_t* global, int n_tiles, int n_views,
@@ -86,11 +85,15 @@ mg_status launch_view_tile_offsets(const int32_t* global, int n_tiles, int n_vie
 // sort.cu
 // Sorts in place between (keys, vals) and (keys_alt, vals_alt); returns in
 // *result_in_alt whether the sorted data ended in the alt buffers.
+// With segments > 1 (1..256, dividing n), each run of n / segments keys is
+// sorted on its own and stays in place. keys_out false: the sorted values
+// only (the last pass writes no keys; the result buffer's keys are stale).
 template <typename K>
 mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt,
                            int64_t n, int bits, void* scratch, size_t scratch_bytes,
-                           bool* result_in_alt, cudaStream_t stream);
-size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes);
+                           bool* result_in_alt, cudaStream_t stream, int segments = 1,
+                           bool keys_out = true);
+size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes, int segments = 1);
 // Exclusive scan of counts[order[i]] (order may be null: identity) into
 // out[i] (u32); writes the 64-bit total to *total_dev.
 size_t scan_scratch_bytes(int64_t n);

@@ -644,18 +644,17 @@ __device__ __forceinline__ uint32_t depth_key(float d, const uint32_t* range) {
 __device__ __forceinline__ uint32_t no_depth_key(const uint32_t* range) {
     return relative_depth_keys(range) ? 0x00ffffffu : 0xffffffffu;
 }
-// Batch keys (BinViews::key_shift > 0): the view above the depth relative to
-// the view's smallest, so a stable sort of the batch orders every view as its
-// own sort would; the no-tile key is the view's largest.
-__device__ __forceinline__ uint32_t view_depth_key(float d, const uint32_t* range, int v,
-                                                   int key_shift) {
-    if (key_shift == 0) return depth_key(d, range);
-    return ((uint32_t)v << key_shift) | (__float_as_uint(d) - ~range[0]);
+// Batch keys (BinViews::batch_keys): the depth relative to the view's
+// smallest, each view sorted as a segment of its own; rows without a pair
+// take 2^24 - 1, so when a view's range spans fewer than 2^24 patterns the
+// top 8-bit pass finds one digit in that view and only copies.
+constexpr uint32_t kBatchNoDepthKey = 0x00ffffffu;
+__device__ __forceinline__ uint32_t view_depth_key(float d, const uint32_t* range,
+                                                   int batch_keys) {
+    return batch_keys ? __float_as_uint(d) - ~range[0] : depth_key(d, range);
 }
-__device__ __forceinline__ uint32_t view_no_depth_key(const uint32_t* range, int v,
-                                                      int key_shift) {
-    if (key_shift == 0) return no_depth_key(range);
-    return ((uint32_t)v << key_shift) | ((1u << key_shift) - 1u);
+__device__ __forceinline__ uint32_t view_no_depth_key(const uint32_t* range, int batch_keys) {
+    return batch_keys ? kBatchNoDepthKey : no_depth_key(range);
 }
 
 // Stage A of the two-stage binning: tile counts plus the depth sort keys
@@ -681,9 +680,6 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
         counts += vout; dkeys += vout; dvals += vout; recs += vout;
         if (range) range += 2 * v;
         if (hist) hist += (int64_t)v * tiles_x * tiles_y * kCutBins;
-        if (bv.key_shift && blockIdx.x == 0 && threadIdx.x == 0 &&
-            range[1] - ~range[0] > (1u << bv.key_shift) - 2u)
-            *bv.overflow = 1;
     }
     const int64_t g = block_sorted_gaussian(uv, rxy, valid, n, tile, tiles_x, tiles_y);
     const int lane = threadIdx.x & 31;
@@ -730,8 +726,8 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
     }
     if (g >= n) return;
     counts[g] = c;
-    dkeys[g] = c > 0u ? view_depth_key(depth[g], range, v, bv.key_shift)
-                      : view_no_depth_key(range, v, bv.key_shift);
+    dkeys[g] = c > 0u ? view_depth_key(depth[g], range, bv.batch_keys)
+                      : view_no_depth_key(range, bv.batch_keys);
     dvals[g] = (uint32_t)((int64_t)v * n + g);
 }
 
@@ -955,18 +951,18 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
     }
     if (!has) return;
     counts[g] = kept;
-    if (kept == 0u) dkeys[g] = view_no_depth_key(range, v, bv.key_shift);
+    if (kept == 0u) dkeys[g] = view_no_depth_key(range, bv.batch_keys);
 }
 
 // Per-view pair totals of a batch: view v's pairs start at the scan value of
 // its first sorted slot v * n.
 __global__ void view_totals_kernel(const uint32_t* __restrict__ offsets, int64_t n,
-                                   int n_views, const int32_t* __restrict__ overflow,
+                                   int n_views,
                                    int64_t* __restrict__ totals) {
     const int v = threadIdx.x;
     if (v > n_views) return;
     if (v == n_views) {
-        totals[n_views + 1] = *overflow != 0 ? 1 : 0;
+        totals[n_views + 1] = 0;
         return;
     }
     const int64_t next = v + 1 < n_views ? (int64_t)offsets[(int64_t)(v + 1) * n]
@@ -1124,9 +1120,9 @@ mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
 }
 
 mg_status launch_view_totals(const uint32_t* offsets, int64_t n, int n_views,
-                             const int32_t* overflow, int64_t* totals, cudaStream_t stream) {
+                             int64_t* totals, cudaStream_t stream) {
     view_totals_kernel<<<1, ((n_views + 1 + 31) / 32) * 32, 0, stream>>>(offsets, n, n_views,
-                                                                         overflow, totals);
+                                                                         totals);
     return check_launch("view_totals");
 }
 

@@ -14,6 +14,12 @@
 // __match_any_sync peer groups and warp-private counters; warps are combined
 // in warp order, tiles in tile order, so equal digits keep their input order
 // and the sort is stable across passes.
+//
+// Segments: the input may be `segments` equal runs, each sorted on its own
+// and kept in place (a batch of views sorting each view's rows). Tiles never
+// straddle a segment, digits are counted per segment, and a tile looks back
+// only over its own segment's tiles. A pass in which all of a segment's keys
+// share one digit copies that segment's tiles through.
 #include <algorithm>
 #include <string>
 
@@ -59,36 +65,47 @@ constexpr uint32_t kLookbackSpinLimit = 1u << 22;
 constexpr int kLookback = MG_SORT_LOOKBACK;  // predecessor words read per round trip
 
 struct SortScratch {
-    uint32_t* hist;           // passes x 256: histogram, then exclusive offsets
+    uint32_t* hist;           // passes x 256 (x segments): histogram, then exclusive offsets
     uint32_t* tile_counter;   // passes
     uint32_t* status;         // passes x tiles x 256 look-back words
-    int tiles;
+    uint32_t* one_digit;      // segmented: passes x segments flags (all keys share a digit)
+    int tiles;                // segments x tiles_per_seg
+    int tiles_per_seg;
     int passes;
+    size_t bytes;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-SortScratch carve(void* base, int64_t n, int bits, int key_bytes) {
+// n keys in `segments` equal runs (segments divides n). With one segment the
+// layout is hist | counters | status, as the allocation-free entry point's
+// fixed array assumes.
+SortScratch carve(void* base, int64_t n, int bits, int key_bytes, int segments = 1) {
     SortScratch s;
     s.passes = (bits + kRadixBits - 1) / kRadixBits;
     const int tk = key_bytes == 4 ? tile_keys<uint32_t>() : tile_keys<uint64_t>();
-    s.tiles = (int)std::max<int64_t>(1, (n + tk - 1) / tk);
+    segments = std::max(segments, 1);
+    const int64_t seg_n = n / segments;
+    s.tiles_per_seg = (int)std::max<int64_t>(1, (seg_n + tk - 1) / tk);
+    s.tiles = s.tiles_per_seg * segments;
     char* p = static_cast<char*>(base);
     s.hist = reinterpret_cast<uint32_t*>(p);
-    p += align256(sizeof(uint32_t) * kRadix * s.passes);
+    p += align256(sizeof(uint32_t) * kRadix * s.passes * segments);
     s.tile_counter = reinterpret_cast<uint32_t*>(p);
     p += align256(sizeof(uint32_t) * s.passes);
     s.status = reinterpret_cast<uint32_t*>(p);
+    p += align256(sizeof(uint32_t) * (size_t)s.tiles * kRadix * s.passes);
+    s.one_digit = nullptr;
+    if (segments > 1) {
+        s.one_digit = reinterpret_cast<uint32_t*>(p);
+        p += align256(sizeof(uint32_t) * (size_t)s.passes * segments);
+    }
+    s.bytes = (size_t)(p - static_cast<char*>(base));
     return s;
 }
 
-size_t sort_scratch_size(int64_t n, int bits, int key_bytes) {
-    const int passes = (bits + kRadixBits - 1) / kRadixBits;
-    const int tk = key_bytes == 4 ? tile_keys<uint32_t>() : tile_keys<uint64_t>();
-    const int64_t tiles = std::max<int64_t>(1, (n + tk - 1) / tk);
-    return align256(sizeof(uint32_t) * kRadix * passes) +
-           align256(sizeof(uint32_t) * passes) +
-           align256(sizeof(uint32_t) * (size_t)tiles * kRadix * passes);
+size_t sort_scratch_size(int64_t n, int bits, int key_bytes, int segments = 1) {
+    return carve(nullptr, n, bits, key_bytes, segments).bytes;
 }
 
 template <typename K>
@@ -96,11 +113,15 @@ __device__ __forceinline__ uint32_t digit_of(K key, int shift, uint32_t mask) {
     return (uint32_t)(key >> shift) & mask;
 }
 
-// Digit histograms of all passes in one read of the keys.
+// Digit histograms of all passes in one read of the keys (blockIdx.y is the
+// segment, of seg_n keys; hist is passes x segments x 256).
 template <typename K>
 __global__ void __launch_bounds__(kSortThreads)
-radix_histogram_kernel(const K* __restrict__ keys, int64_t n, int bits, int passes,
+radix_histogram_kernel(const K* __restrict__ keys, int64_t seg_n, int bits, int passes,
                        uint32_t* __restrict__ hist) {
+    const int seg = blockIdx.y, segments = gridDim.y;
+    keys += (int64_t)seg * seg_n;
+    const int64_t n = seg_n;
     // One counter set per warp (keys with few distinct digits, such as the
     // high bits of tile ids, would otherwise serialise every warp of the
     // block on the same shared-memory words), when they fit.
@@ -124,16 +145,24 @@ radix_histogram_kernel(const K* __restrict__ keys, int64_t n, int bits, int pass
     for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) {
         uint32_t c = 0u;
         for (int w = 0; w < sets; ++w) c += s_hist[w * passes * kRadix + i];
-        if (c) atomicAdd(&hist[i], c);
+        const int p = i / kRadix, d = i % kRadix;
+        if (c) atomicAdd(&hist[((int64_t)p * segments + seg) * kRadix + d], c);
     }
 }
 
-// Exclusive scan of each pass's 256 digit counts (one CTA per pass).
-__global__ void __launch_bounds__(kRadix) radix_offsets_kernel(uint32_t* hist) {
+// Exclusive scan of each (pass, segment)'s 256 digit counts (one CTA each);
+// with one_digit given, also whether one digit holds all seg_n keys.
+__global__ void __launch_bounds__(kRadix) radix_offsets_kernel(uint32_t* hist,
+                                                               uint32_t* one_digit,
+                                                               int64_t seg_n) {
     __shared__ uint32_t s[kRadix];
     uint32_t* h = hist + blockIdx.x * kRadix;
     const int t = threadIdx.x;
     const uint32_t v = h[t];
+    if (one_digit) {
+        const int all = __syncthreads_or((int64_t)v == seg_n);
+        if (t == 0) one_digit[blockIdx.x] = all ? 1u : 0u;
+    }
     s[t] = v;
     __syncthreads();
     for (int off = 1; off < kRadix; off <<= 1) {
@@ -145,6 +174,8 @@ __global__ void __launch_bounds__(kRadix) radix_offsets_kernel(uint32_t* hist) {
     h[t] = s[t] - v;
 }
 
+constexpr int kMaxSortSegments = 256;
+
 template <typename K>
 struct OnesweepSmem {
     K keys[tile_keys<K>()];
@@ -152,6 +183,7 @@ struct OnesweepSmem {
     uint32_t warp_hist[kSortWarps][kRadix];
     uint32_t local_start[kRadix];
     uint32_t bin_offset[kRadix];
+    uint32_t one_digit[kMaxSortSegments];  // segmented passes: the per-segment flags
     uint32_t tile_id;
 };
 
@@ -160,14 +192,19 @@ struct OnesweepSmem {
 #ifndef MG_SORT_MIN_CTAS
 #define MG_SORT_MIN_CTAS 0
 #endif
-template <typename K>
+template <typename K, bool kSegmented = false>
 __global__ void __launch_bounds__(kSortThreads, MG_SORT_MIN_CTAS)
 onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
                      K* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                      int64_t n, int shift, int digit_bits,
                      const uint32_t* __restrict__ digit_offsets,
                      uint32_t* __restrict__ tile_counter, uint32_t* status,
-                     int32_t* err_word, uint32_t spin_limit) {
+                     int32_t* err_word, uint32_t spin_limit, int tiles_per_seg = 0,
+                     const uint32_t* __restrict__ one_digit = nullptr,
+                     bool write_keys = true) {
+    // kSegmented: n keys per segment, tiles_per_seg tiles each, one_digit the
+    // pass's per-segment flags; otherwise one segment of n keys. write_keys
+    // false: only the values go out (a last pass whose keys nobody reads).
     constexpr int ITEMS = SortTraits<K>::kItems;
     constexpr int TK = tile_keys<K>();
     __shared__ OnesweepSmem<K> sm;
@@ -175,14 +212,15 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     const uint32_t mask = (1u << digit_bits) - 1u;
 
     // A pass whose digit is the same for every key keeps the order: copy the
-    // tile through (each block decides alike from the digit offsets).
-    {
+    // tile through (each block decides alike from the digit offsets). With
+    // segments the test is per segment, after the claim.
+    if (!kSegmented) {
         const uint32_t d0 = digit_of(keys_in[0], shift, mask);
         const uint32_t next = d0 + 1u < (uint32_t)kRadix ? digit_offsets[d0 + 1u] : (uint32_t)n;
         if (digit_offsets[d0] == 0u && (int64_t)next == n) {
             for (int64_t i = (int64_t)blockIdx.x * TK + tid;
                  i < min(n, (int64_t)(blockIdx.x + 1) * TK); i += kSortThreads) {
-                keys_out[i] = keys_in[i];
+                if (write_keys) keys_out[i] = keys_in[i];
                 vals_out[i] = vals_in[i];
             }
             return;
@@ -191,10 +229,30 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
 
     for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads)
         (&sm.warp_hist[0][0])[i] = 0u;
+    // the segments' one-digit flags, read while the tile is claimed
+    if (kSegmented && tid < (int)(gridDim.x / (unsigned)tiles_per_seg))
+        sm.one_digit[tid] = one_digit[tid];
     if (tid == 0) sm.tile_id = atomicAdd(tile_counter, 1u);
     __syncthreads();
     const uint32_t tile = sm.tile_id;
-    const int64_t base = (int64_t)tile * TK;
+    int tl = (int)tile;  // the tile's index within its segment
+    int64_t seg_base = 0, end = n;
+    if (kSegmented) {
+        const int seg = (int)(tile / (uint32_t)tiles_per_seg);
+        tl -= seg * tiles_per_seg;
+        seg_base = (int64_t)seg * n;
+        end = seg_base + n;
+        digit_offsets += (int64_t)seg * kRadix;
+        if (sm.one_digit[seg]) {  // block-uniform: copy the tile through
+            for (int64_t i = seg_base + (int64_t)tl * TK + tid;
+                 i < min(end, seg_base + (int64_t)(tl + 1) * TK); i += kSortThreads) {
+                if (write_keys) keys_out[i] = keys_in[i];
+                vals_out[i] = vals_in[i];
+            }
+            return;
+        }
+    }
+    const int64_t base = seg_base + (int64_t)tl * TK;
 
     // Warp w owns input slots [w*32*ITEMS, (w+1)*32*ITEMS) of the tile; item i
     // of lane l is slot i*32 + l inside it, so (i, l) order is input order.
@@ -204,7 +262,7 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
         const int64_t idx = base + (int64_t)warp * 32 * ITEMS + i * 32 + lane;
-        if (idx < n) {
+        if (idx < end) {
             key[i] = keys_in[idx];
             val[i] = vals_in[idx];
         } else {
@@ -243,7 +301,7 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     const bool in_pass = d <= (int)mask;
     uint32_t* my_status = status + (int64_t)tile * kRadix + d;
     if (in_pass) {
-        if (tile == 0) {
+        if (tl == 0) {
             atomicExch(my_status, kFlagInc | tile_count);
         } else {
             atomicExch(my_status, kFlagAgg | tile_count);
@@ -265,14 +323,15 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     // up to the first inclusive prefix; a word not yet published ends the
     // round and is read again.
     uint32_t excl = 0u;
-    if (tile > 0 && in_pass) {
+    if (tl > 0 && in_pass) {
         int64_t t = (int64_t)tile - 1;
+        const int64_t first = (int64_t)tile - tl;  // the segment's first tile: inclusive
         uint32_t spins = 0u;
         for (;;) {
             uint32_t sv[kLookback];
 #pragma unroll
-            for (int k = 0; k < kLookback; ++k)  // tile 0 is inclusive: never read past it
-                sv[k] = t - k >= 0
+            for (int k = 0; k < kLookback; ++k)  // never read past the first tile
+                sv[k] = t - k >= first
                             ? (uint32_t)*(volatile uint32_t*)(status + (t - k) * kRadix + d)
                             : (uint32_t)kFlagInc;
             int k = 0;
@@ -306,15 +365,16 @@ onesweep_pass_kernel(const K* __restrict__ keys_in, const uint32_t* __restrict__
     }
     __syncthreads();
     // ...and write out; consecutive positions of a digit run are consecutive
-    // in the output. Padding keys land at output positions >= n.
+    // in the output. Padding keys land at or past the segment's end.
 #pragma unroll
     for (int i = 0; i < ITEMS; ++i) {
         const int p = i * kSortThreads + tid;
         const K k = sm.keys[p];
         const uint32_t dd = digit_of(k, shift, mask);
-        const int64_t out = (int64_t)sm.bin_offset[dd] + (p - (int)sm.local_start[dd]);
-        if (out < n) {
-            keys_out[out] = k;
+        const int64_t out =
+            seg_base + (int64_t)sm.bin_offset[dd] + (p - (int)sm.local_start[dd]);
+        if (out < end) {
+            if (write_keys) keys_out[out] = k;
             vals_out[out] = sm.vals[p];
         }
     }
@@ -476,34 +536,39 @@ __global__ void tile_ranges4_kernel(const uint32_t* __restrict__ tiles, int64_t 
 
 }  // namespace
 
-size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes) {
-    return sort_scratch_size(n, bits, key_bytes);
+size_t radix_sort_scratch_bytes(int64_t n, int bits, int key_bytes, int segments) {
+    return sort_scratch_size(n, bits, key_bytes, segments);
 }
 
 template <typename K>
 mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_alt,
                            int64_t n, int bits, void* scratch, size_t scratch_bytes,
-                           bool* result_in_alt, cudaStream_t stream) {
+                           bool* result_in_alt, cudaStream_t stream, int segments,
+                           bool keys_out) {
     *result_in_alt = false;
     if (n <= 1 || bits <= 0) return MG_OK;
     if (bits > (int)(8 * sizeof(K)))
         return fail(MG_ERR_INVALID_ARGUMENT, "sort: bits exceeds the key width");
     if (n >= (int64_t)kCountMask)
         return fail(MG_ERR_CAPACITY, "sort: more than 2^30 elements");
-    const size_t need = sort_scratch_size(n, bits, (int)sizeof(K));
+    if (segments < 1 || segments > kMaxSortSegments || n % segments != 0)
+        return fail(MG_ERR_INVALID_ARGUMENT, "sort: 1..256 segments that divide the key count");
+    const size_t need = sort_scratch_size(n, bits, (int)sizeof(K), segments);
     if (scratch == nullptr || scratch_bytes < need)
         return fail(MG_ERR_INVALID_ARGUMENT, "sort: scratch buffer too small");
-    SortScratch s = carve(scratch, n, bits, (int)sizeof(K));
+    SortScratch s = carve(scratch, n, bits, (int)sizeof(K), segments);
     if (cudaMemsetAsync(scratch, 0, need, stream) != cudaSuccess)
         return check_launch("sort scratch memset");
+    const int64_t seg_n = n / segments;
 
-    const int hist_blocks = std::min<int64_t>((n + 4095) / 4096, 148 * 4);
+    const int hist_blocks = (int)std::max<int64_t>(
+        1, std::min<int64_t>((seg_n + 4095) / 4096, (148 * 4 + segments - 1) / segments));
     const size_t hist_smem = sizeof(uint32_t) * kRadix * s.passes *
                              (s.passes <= kHistPrivatePasses ? kSortWarps : 1);
-    radix_histogram_kernel<K><<<std::max(1, hist_blocks), kSortThreads, hist_smem, stream>>>(
-        keys, n, bits, s.passes, s.hist);
+    radix_histogram_kernel<K><<<dim3(hist_blocks, segments), kSortThreads, hist_smem, stream>>>(
+        keys, seg_n, bits, s.passes, s.hist);
     MG_TRY(check_launch("radix_histogram"));
-    radix_offsets_kernel<<<s.passes, kRadix, 0, stream>>>(s.hist);
+    radix_offsets_kernel<<<s.passes * segments, kRadix, 0, stream>>>(s.hist, s.one_digit, seg_n);
     MG_TRY(check_launch("radix_offsets"));
 
     int32_t* err = device_error_word();
@@ -512,9 +577,17 @@ mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_
     for (int p = 0; p < s.passes; ++p) {
         const int shift = p * pass_bits(bits);
         const int db = std::min(pass_bits(bits), bits - shift);
-        onesweep_pass_kernel<K><<<s.tiles, kSortThreads, 0, stream>>>(
-            kin, vin, kout, vout, n, shift, db, s.hist + p * kRadix, s.tile_counter + p,
-            s.status + (size_t)p * s.tiles * kRadix, err, kLookbackSpinLimit);
+        const bool wk = keys_out || p + 1 < s.passes;
+        if (segments > 1)
+            onesweep_pass_kernel<K, true><<<s.tiles, kSortThreads, 0, stream>>>(
+                kin, vin, kout, vout, seg_n, shift, db, s.hist + (size_t)p * segments * kRadix,
+                s.tile_counter + p, s.status + (size_t)p * s.tiles * kRadix, err,
+                kLookbackSpinLimit, s.tiles_per_seg, s.one_digit + (size_t)p * segments, wk);
+        else
+            onesweep_pass_kernel<K><<<s.tiles, kSortThreads, 0, stream>>>(
+                kin, vin, kout, vout, n, shift, db, s.hist + p * kRadix, s.tile_counter + p,
+                s.status + (size_t)p * s.tiles * kRadix, err, kLookbackSpinLimit, 0, nullptr,
+                wk);
         MG_TRY(check_launch("onesweep_pass"));
         std::swap(kin, kout);
         std::swap(vin, vout);
@@ -525,10 +598,10 @@ mg_status radix_sort_pairs(K* keys, uint32_t* vals, K* keys_alt, uint32_t* vals_
 
 template mg_status radix_sort_pairs<uint32_t>(uint32_t*, uint32_t*, uint32_t*, uint32_t*,
                                               int64_t, int, void*, size_t, bool*,
-                                              cudaStream_t);
+                                              cudaStream_t, int, bool);
 template mg_status radix_sort_pairs<uint64_t>(uint64_t*, uint32_t*, uint64_t*, uint32_t*,
                                               int64_t, int, void*, size_t, bool*,
-                                              cudaStream_t);
+                                              cudaStream_t, int, bool);
 
 size_t scan_scratch_bytes(int64_t n) {
     const int64_t blocks = std::max<int64_t>(1, (n + kScanTile - 1) / kScanTile);

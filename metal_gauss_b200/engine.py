@@ -143,7 +143,7 @@ class _BatchBinning:
         self.emit = torch.empty(0, **u8)
         self.ids = torch.empty(0, dtype=torch.int32, device=device)
         self.offsets = torch.empty(0, dtype=torch.int32, device=device)
-        # per-view pair totals, the batch total, the overflow flag and the
+        # per-view pair totals, the batch total, a reserved word (0) and the
         # device error word (copied in just before the one host read)
         self.totals = torch.zeros(67, dtype=torch.int64, device=device)
         self.bases: list[int] = []
@@ -176,8 +176,8 @@ class _BatchBinning:
 
     def read_totals(self, V: int) -> list[int] | None:
         """The views' pair totals (one device->host read), or None when the
-        batch has to be binned one view at a time (a view's depth range
-        outgrew the batch keys, or 2^30 - 1 pairs, the tile sort's limit).
+        batch has to be binned one view at a time (2^30 - 1 pairs or more,
+        the tile sort's limit).
         The device error word rides on the same read: a kernel that gave up
         a bounded wait or met a bad index since the last check raises
         DeviceError here, before its results are used."""
@@ -185,7 +185,7 @@ class _BatchBinning:
         t = self.totals[:V + 3].tolist()
         if t[V + 2]:
             _lib.raise_device_error(t[V + 2], "binning")
-        if t[V + 1] or t[V] >= 2 ** 30 - 1:
+        if t[V] >= 2 ** 30 - 1:
             return None
         self.bases = [0] * V
         for v in range(1, V):

@@ -2,8 +2,8 @@
 gauss ids and tile offsets equal the lists of the per-view calls
 (mg_bin_prepare / mg_bin_emit, themselves pinned to the reference's lists),
 with and without the saturation cut, with shared and per-view opacities and a
-view stride above the Gaussian count; the overflow flag for depth ranges the
-batch keys cannot hold; and the trainer and renderer give the same results
+view stride above the Gaussian count; views of wide and narrow depth range in
+one batch; and the trainer and renderer give the same results
 either way."""
 
 import numpy as np
@@ -54,7 +54,7 @@ def _batch(out, V, n, stride, opac, opac_stride, cut):
               ptr(opac), ptr(out["valid"]), ptr(out["depth"]), n, V, stride, opac_stride, W, H,
               TILE, cut, ptr(tot), ptr(prep), prep.numel(), s)
     t = tot.cpu().numpy()
-    assert t[V + 1] == 0, "overflow flag set"
+    assert t[V + 1] == 0
     assert t[V] == t[:V].sum()
     m = int(t[V])
     ids = torch.empty(max(m, 1), dtype=torch.int32, device="cuda")
@@ -116,9 +116,13 @@ def test_views_without_pairs_in_a_batch(cuda):
         assert np.array_equal(lists[v][0], ids) and np.array_equal(lists[v][1], off)
 
 
-def test_overflow_flag_for_a_depth_range_beyond_the_batch_keys(cuda):
-    """40 views leave 26 bits of relative depth: depths from 0.01 to 90 span
-    about 1.1e8 float patterns, past 2^26 - 1, so the call says so."""
+def test_wide_depth_ranges_in_a_batch(cuda):
+    """The batch's depth sort takes each view's rows as a segment of their
+    own, keyed relative to the view's nearest visible depth. A view whose
+    depths run from 0.01 to 90 (about 1.1e8 float patterns, past 2^24, so its
+    top pass ranks while the other views' copy) among 39 views of narrow range
+    gives the lists of its own binning, and so do its neighbours; the word
+    after the batch total stays 0."""
     V, n = 40, 512
     g = torch.Generator().manual_seed(0)
     f32 = dict(dtype=torch.float32, device="cuda")
@@ -127,19 +131,16 @@ def test_overflow_flag_for_a_depth_range_beyond_the_batch_keys(cuda):
     conic = torch.tensor([0.05, 0.0, 0.05]).expand(V, n, 3).contiguous().to(**f32)
     valid = torch.ones(V, n, dtype=torch.int32, device="cuda")
     opac = torch.full((n,), 0.8, **f32)
-    L = _lib.load()
-    for lo, hi, flag in ((0.5, 8.0, 0), (0.01, 90.0, 1)):
+    for lo, hi in ((0.5, 8.0), (0.01, 90.0)):
         depth = torch.linspace(2.0, 3.0, n).expand(V, n).contiguous().to(**f32)
-        depth[17] = torch.linspace(lo, hi, n, **f32)
-        tot = torch.zeros(V + 2, dtype=torch.int64, device="cuda")
-        prep = torch.empty(L.mg_bin_prepare_views_scratch_bytes(n, V, N_TILES),
-                           dtype=torch.uint8, device="cuda")
-        _lib.call("mg_bin_prepare_views", ptr(uv), ptr(rxy), ptr(conic), ptr(opac), ptr(valid),
-                  ptr(depth), n, V, n, 0, W, H, TILE, 0, ptr(tot), ptr(prep), prep.numel(),
-                  _lib.stream())
-        t = tot.cpu().numpy()
-        assert t[V + 1] == flag
-        assert t[V] == t[:V].sum() > 0
+        depth[17] = torch.linspace(lo, hi, n, **f32).flip(0)
+        out = dict(uv=uv, rxy=rxy, conic=conic, valid=valid, depth=depth)
+        for cut in (0, 1):
+            lists = _batch(out, V, n, n, opac, 0, cut)
+            for v in (0, 16, 17, 18, 39):
+                ids, off = _per_view(out, v, n, opac, cut)
+                assert np.array_equal(lists[v][0], ids), (lo, cut, v)
+                assert np.array_equal(lists[v][1], off), (lo, cut, v)
 
 
 def test_batch_entry_points_refuse_bad_arguments(cuda):
