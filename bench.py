@@ -120,6 +120,17 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def gather_ranks(x: float, world: int) -> list[float]:
+    """x from every rank, in rank order (all ranks call it)."""
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -341,9 +352,15 @@ def run_ours(args, rank, world, local):
     # exchange the overlap does not hide
     coll = {}
     if world > 1:
-        for k in ("exchange_wait", "wait_geo_gather", "wait_sh_gather", "allreduce"):
+        waits = ("exchange_wait", "wait_geo_gather", "wait_sh_gather", "allreduce")
+        for k in waits:
             v = float(np.sum(stage_ms[k])) / n_instr if k in stage_ms else 0.0
             coll[k + "_ms"] = round(max_over_ranks(v, world), 4)
+        # each rank's own stage time per step (its views' kernels, no waits):
+        # the spread is the part of exchange_wait that is waiting for the
+        # slowest rank rather than for the transfer
+        busy = sum(float(np.sum(v)) for k, v in stage_ms.items() if k not in waits) / n_instr
+        coll["rank_busy_ms"] = [round(b, 3) for b in gather_ranks(busy, world)]
     singles = {k: v for k, v in stage_ms.items()
                if k in ("raster_bwd", "raster_fwd", "preprocess_fwd", "preprocess_bwd", "loss",
                         "adam")}
