@@ -107,6 +107,12 @@ PrepareScratch carve_prepare(const void* base, int64_t n, int n_tiles, int n_vie
     return s;
 }
 
+// The keep table the prepare stage left over its cut histogram, when it
+// built one (the emission ignores it without a cutoff).
+const uint64_t* cut_keep(const PrepareScratch& p, int tiles_x) {
+    return cut_keep_fits(tiles_x) ? reinterpret_cast<const uint64_t*>(p.cut_hist) : nullptr;
+}
+
 struct EmitScratch {
     uint32_t* pair_tiles;
     uint32_t* tiles_alt;
@@ -425,7 +431,8 @@ extern "C" mg_status mg_bin_emit(const float* uv, const float* rxy, const float*
     uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
     MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m, width,
                            height, tile, tiles_x, tiles_y, p.recs,
-                           saturation_cut ? p.cutoff : nullptr, e.pair_tiles, ids, BinViews{},
+                           saturation_cut ? p.cutoff : nullptr, cut_keep(p, tiles_x),
+                           e.pair_tiles, ids, BinViews{},
                            st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m,
@@ -559,7 +566,8 @@ extern "C" mg_status mg_bin_emit_views(const float* uv, const float* rxy, const 
     uint32_t* ids = reinterpret_cast<uint32_t*>(gauss_ids);
     MG_TRY(launch_bin_emit(uv, rxy, conic, opacity, p.dvals, p.counts, p.offsets, n, m_total,
                            width, height, tile, tiles_x, tiles_y, p.recs,
-                           saturation_cut ? p.cutoff : nullptr, e.pair_tiles, ids, bv, st));
+                           saturation_cut ? p.cutoff : nullptr, cut_keep(p, tiles_x),
+                           e.pair_tiles, ids, bv, st));
     bool in_alt = false;
     MG_TRY(radix_sort_pairs<uint32_t>(e.pair_tiles, ids, e.tiles_alt, e.ids_alt, m_total,
                                       tile_bits(n_tiles * n_views), e.sort, e.sort_bytes,

@@ -66,12 +66,20 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
 // Saturation-cut histogram bins per tile (cut_hist holds n_tiles of them;
 // cut_range two zeroed words before the call; see preprocess_fwd.cu).
 constexpr int kSaturationBins = 64;
+// The saturation cut's keep table: per view, tile row and depth bin, the
+// bits of the row's tiles whose cutoff bin is not before that bin, in
+// cut_keep_stride(tiles_x) 64-bit words (the last one zero). It is written
+// over the cut histogram (consumed by then), which holds it when a row has
+// at least 4 tiles; launch_bin_count_depth builds it there in that case.
+__host__ __device__ inline int cut_keep_stride(int tiles_x) { return (tiles_x + 63) / 64 + 1; }
+inline bool cut_keep_fits(int tiles_x) { return tiles_x >= 4; }
 mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const float* opacity, const uint32_t* sorted_gid,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
-                          const uint4* recs, const int32_t* cutoff, uint32_t* pair_tiles,
-                          uint32_t* pair_ids, const BinViews& bv, cudaStream_t stream);
+                          const uint4* recs, const int32_t* cutoff, const uint64_t* keep,
+                          uint32_t* pair_tiles, uint32_t* pair_ids, const BinViews& bv,
+                          cudaStream_t stream);
 // Batch bookkeeping: per-view pair totals from the scan of the batch's depth
 // order (view v's n sorted slots start at v * n; totals[n_views] holds the
 // grand total already), and totals[n_views + 1] = 0 (a reserved word).

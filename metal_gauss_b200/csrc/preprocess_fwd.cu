@@ -731,6 +731,15 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
     dvals[g] = (uint32_t)((int64_t)v * n + g);
 }
 
+// The keep bits of tiles x0 .. x0 + 63 of one (row, bin) entry of the keep
+// table (bit i: tile x0 + i).
+__device__ __forceinline__ uint64_t keep_bits(const uint64_t* __restrict__ words, uint32_t x0) {
+    const uint32_t w = x0 >> 6, s = x0 & 63u;
+    uint64_t bits = words[w] >> s;
+    if (s) bits |= words[w + 1] << (64u - s);
+    return bits;
+}
+
 // Stage B: emit every (tile, Gaussian) pair with Gaussians in depth order.
 // offsets are the exclusive scan of the counts in that order; each thread
 // writes at most its own count so a disagreement can never overrun.
@@ -744,6 +753,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
                                 int64_t m, int W, int H, int tile, int tiles_x,
                                 int tiles_y, const uint4* __restrict__ recs,
                                 const int32_t* __restrict__ cutoff,
+                                const uint64_t* __restrict__ keep,
                                 uint32_t* __restrict__ pair_tiles,
                                 uint32_t* __restrict__ pair_ids, BinViews bv) {
     const int64_t sl = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -758,6 +768,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
         uv += vin; rxy += vin; conic += 3 * vin;
         opacity += (int64_t)v * bv.opac_stride;
         if (cutoff) cutoff += (int64_t)v * n_tiles;
+        if (keep) keep += (int64_t)v * tiles_y * kCutBins * cut_keep_stride(tiles_x);
     }
     int gbin = 0;
     uint32_t g = 0u, cnt = 0u;
@@ -783,14 +794,17 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_emit_kernel(const fl
                 const uint32_t x0 = rec.z & 0xffffu, y0 = rec.z >> 16;
                 const uint64_t row_bits = rw == 64u ? ~0ull : (1ull << rw) - 1ull;
                 uint32_t k = 0u;
+                const int ks = cut_keep_stride(tiles_x);
                 for (uint32_t r = 0; r < rh && mask; ++r) {
                     uint64_t row = mask & row_bits;
                     mask >>= rw;
+                    if (keep)  // only the tiles the cut keeps
+                        row &= keep_bits(keep + ((int64_t)(y0 + r) * kCutBins + gbin) * ks, x0);
                     const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
                     while (row) {
                         const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
                         row &= row - 1ull;
-                        if (cutoff && cutoff[trow + b] < gbin) continue;
+                        if (!keep && cutoff && cutoff[trow + b] < gbin) continue;
                         if (k < cnt) {
                             pair_tiles[at + k] = tile_base + trow + b;
                             pair_ids[at + k] = g;
@@ -888,6 +902,26 @@ __global__ void bin_cutoff_kernel(const uint32_t* __restrict__ hist, int n_tiles
     }
 }
 
+// Saturation cut, step 2b: the keep table (see cut_keep_stride), one thread
+// per (view, tile row, bin, word).
+__global__ void bin_keep_kernel(const int32_t* __restrict__ cutoff, int tiles_x, int tiles_y,
+                                int n_views, uint64_t* __restrict__ keep) {
+    const int stride = cut_keep_stride(tiles_x);
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n_views * tiles_y * kCutBins * stride) return;
+    const int w = (int)(i % stride);
+    const int64_t rb = i / stride;
+    const int b = (int)(rb % kCutBins);
+    const int64_t row = rb / kCutBins;  // view * tiles_y + tile row
+    const int32_t* c = cutoff + row * tiles_x;
+    uint64_t bits = 0ull;
+    for (int k = 0; k < 64; ++k) {
+        const int tx = w * 64 + k;
+        if (tx < tiles_x && c[tx] >= b) bits |= 1ull << k;
+    }
+    keep[i] = bits;
+}
+
 // Saturation cut, step 3: per Gaussian, the pairs that survive the cut (its
 // count and depth key are rewritten; the emission keeps the same pairs).
 __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const float2* __restrict__ uv,
@@ -898,6 +932,7 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
                                    int tile, int tiles_x, int tiles_y,
                                    const uint4* __restrict__ recs,
                                    const int32_t* __restrict__ cutoff,
+                                   const uint64_t* __restrict__ keep,
                                    const uint32_t* __restrict__ range,
                                    uint32_t* __restrict__ counts,
                                    uint32_t* __restrict__ dkeys, BinViews bv) {
@@ -908,8 +943,10 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
         opacity += (int64_t)v * bv.opac_stride;
         counts += vout; dkeys += vout; recs += vout;
         cutoff += (int64_t)v * tiles_x * tiles_y;
+        if (keep) keep += (int64_t)v * tiles_y * kCutBins * cut_keep_stride(tiles_x);
         range += 2 * v;
     }
+    const int ks = cut_keep_stride(tiles_x);
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
     const bool has = g < n && counts[g] != 0u;
@@ -927,6 +964,10 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_recount_kernel(const
             for (uint32_t r = 0; r < rh && mask; ++r) {
                 uint64_t row = mask & row_bits;
                 mask >>= rw;
+                if (keep) {  // the row's kept tiles from the keep table
+                    kept += __popcll(row & keep_bits(keep + ((int64_t)(y0 + r) * kCutBins + gbin) * ks, x0));
+                    continue;
+                }
                 const uint32_t trow = (y0 + r) * (uint32_t)tiles_x + x0;
                 while (row) {
                     const uint32_t b = (uint32_t)__ffsll((long long)row) - 1u;
@@ -1098,10 +1139,18 @@ mg_status launch_bin_count_depth(const float* uv, const float* rxy, const float*
     bin_cutoff_kernel<<<ceil_div(cut_tiles * 32, 256), 256, 0, stream>>>(cut_hist,
                                                                        (int)cut_tiles, cutoff);
     MG_TRY(check_launch("bin_cutoff"));
+    uint64_t* keep = nullptr;
+    if (cut_keep_fits(tiles_x)) {  // over the histogram, which the cutoff pass has consumed
+        keep = reinterpret_cast<uint64_t*>(cut_hist);
+        const int64_t words = (int64_t)V * tiles_y * kCutBins * cut_keep_stride(tiles_x);
+        bin_keep_kernel<<<ceil_div(words, 256), 256, 0, stream>>>(cutoff, tiles_x, tiles_y, V,
+                                                                  keep);
+        MG_TRY(check_launch("bin_keep"));
+    }
     bin_recount_kernel<<<grid, 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
-        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, cut_range, counts, dkeys,
-        bv);
+        opacity, depth, n, W, H, tile, tiles_x, tiles_y, recs, cutoff, keep, cut_range, counts,
+        dkeys, bv);
     return check_launch("bin_recount");
 }
 
@@ -1109,13 +1158,14 @@ mg_status launch_bin_emit(const float* uv, const float* rxy, const float* conic,
                           const float* opacity, const uint32_t* sorted_gid,
                           const uint32_t* counts, const uint32_t* offsets, int64_t n,
                           int64_t m, int W, int H, int tile, int tiles_x, int tiles_y,
-                          const uint4* recs, const int32_t* cutoff, uint32_t* pair_tiles,
-                          uint32_t* pair_ids, const BinViews& bv, cudaStream_t stream) {
+                          const uint4* recs, const int32_t* cutoff, const uint64_t* keep,
+                          uint32_t* pair_tiles, uint32_t* pair_ids, const BinViews& bv,
+                          cudaStream_t stream) {
     if (n == 0 || m == 0 || bv.n_views == 0) return MG_OK;
     bin_emit_kernel<<<dim3((unsigned)ceil_div(n, 256), (unsigned)bv.n_views), 256, 0, stream>>>(
         reinterpret_cast<const float2*>(uv), reinterpret_cast<const float2*>(rxy), conic,
         opacity, sorted_gid, counts, offsets, n, m, W, H, tile, tiles_x, tiles_y,
-        recs, cutoff, pair_tiles, pair_ids, bv);
+        recs, cutoff, cutoff ? keep : nullptr, pair_tiles, pair_ids, bv);
     return check_launch("bin_emit");
 }
 
