@@ -306,11 +306,22 @@ __device__ __forceinline__ TileRect tile_rect(float mux, float muy, float rx,
                                               float ry, int tile, int tiles_x,
                                               int tiles_y) {
     const float tf = (float)tile;
+    float ex0, ex1, ey0, ey1;
+    if ((tile & (tile - 1)) == 0) {
+        // a power-of-two side: x * (1 / tile) is x / tile exactly (scaling by
+        // a power of two rounds once, as the division does)
+        const float inv = 1.0f / tf;
+        ex0 = (mux - rx) * inv; ex1 = (mux + rx) * inv;
+        ey0 = (muy - ry) * inv; ey1 = (muy + ry) * inv;
+    } else {
+        ex0 = (mux - rx) / tf; ex1 = (mux + rx) / tf;
+        ey0 = (muy - ry) / tf; ey1 = (muy + ry) / tf;
+    }
     TileRect r;
-    r.x0 = min(max((int)floorf((mux - rx) / tf), 0), tiles_x - 1);
-    r.x1 = min(max((int)floorf((mux + rx) / tf), 0), tiles_x - 1);
-    r.y0 = min(max((int)floorf((muy - ry) / tf), 0), tiles_y - 1);
-    r.y1 = min(max((int)floorf((muy + ry) / tf), 0), tiles_y - 1);
+    r.x0 = min(max((int)floorf(ex0), 0), tiles_x - 1);
+    r.x1 = min(max((int)floorf(ex1), 0), tiles_x - 1);
+    r.y0 = min(max((int)floorf(ey0), 0), tiles_y - 1);
+    r.y1 = min(max((int)floorf(ey1), 0), tiles_y - 1);
     return r;
 }
 

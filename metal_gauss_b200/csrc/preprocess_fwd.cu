@@ -327,7 +327,8 @@ struct CutArgs {
 __device__ __forceinline__ int cut_bin(float depth, uint32_t dmin_bits, uint32_t dmax_bits) {
     const float lo = __logf(__uint_as_float(dmin_bits));
     const float hi = __logf(__uint_as_float(dmax_bits));
-    const float inv = (float)kCutBins / fmaxf(hi - lo, 1e-6f);
+    // fast division: any deterministic, monotone binning serves the cut
+    const float inv = __fdividef((float)kCutBins, fmaxf(hi - lo, 1e-6f));
     const int b = (int)((__logf(depth) - lo) * inv);
     return min(max(b, 0), kCutBins - 1);
 }
@@ -370,8 +371,10 @@ __device__ __forceinline__ uint32_t bin_walk(
     float op, uint32_t dbits, int tile, int tiles_x, int tiles_y, int W, int H,
     uint64_t* keys, int32_t* ids, uint32_t* pair_tiles, uint32_t* pair_ids,
     int64_t write_at, uint32_t cap, int32_t gid, uint4* rec = nullptr,
-    CutArgs cut = CutArgs{nullptr, nullptr, 0}, uint32_t tile_base = 0u) {
-    const TileRect tr = tile_rect(mux, muy, rx, ry, tile, tiles_x, tiles_y);
+    CutArgs cut = CutArgs{nullptr, nullptr, 0}, uint32_t tile_base = 0u,
+    const TileRect* known_rect = nullptr) {
+    const TileRect tr =
+        known_rect ? *known_rect : tile_rect(mux, muy, rx, ry, tile, tiles_x, tiles_y);
     const float oa = 255.0f * op;
     if (oa <= 1.0f) return 0u;
     const float thr = 2.0f * log_f32_via_f64(oa);
@@ -688,7 +691,8 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
     int gbin = 0;
     if (g < n && valid[g] != 0) {
         const float2 mu = uv[g], r = rxy[g];
-        big = coop_rect(tile_rect(mu.x, mu.y, r.x, r.y, tile, tiles_x, tiles_y));
+        const TileRect tr = tile_rect(mu.x, mu.y, r.x, r.y, tile, tiles_x, tiles_y);
+        big = coop_rect(tr);
         if (hist) gbin = cut_bin(depth[g], ~range[0], range[1]);
         if (!big) {
             if (hist)
@@ -696,12 +700,13 @@ __global__ void __launch_bounds__(256, MG_BIN_MIN_CTAS) bin_count_depth_kernel(c
                                               conic[3 * g + 1], conic[3 * g + 2], opacity[g],
                                               0u, tile, tiles_x, tiles_y, W, H, nullptr,
                                               nullptr, nullptr, nullptr, 0, 0u, 0, recs + g,
-                                              CutArgs{hist, nullptr, gbin});
+                                              CutArgs{hist, nullptr, gbin}, 0u, &tr);
             else
                 c = bin_walk<false, false>(mu.x, mu.y, r.x, r.y, conic[3 * g],
                                            conic[3 * g + 1], conic[3 * g + 2], opacity[g], 0u,
                                            tile, tiles_x, tiles_y, W, H, nullptr, nullptr,
-                                           nullptr, nullptr, 0, 0u, 0, recs + g);
+                                           nullptr, nullptr, 0, 0u, 0, recs + g,
+                                           CutArgs{nullptr, nullptr, 0}, 0u, &tr);
         }
     }
     // the warp's large rectangles, one at a time (their records say: walk
