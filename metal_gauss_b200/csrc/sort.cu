@@ -132,15 +132,32 @@ radix_histogram_kernel(const K* __restrict__ keys, int64_t seg_n, int bits, int 
     for (int i = threadIdx.x; i < words; i += kSortThreads) s_hist[i] = 0u;
     __syncthreads();
     uint32_t* mine = s_hist + (per_warp ? (threadIdx.x >> 5) * passes * kRadix : 0);
-    for (int64_t i = (int64_t)blockIdx.x * kSortThreads + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * kSortThreads) {
-        const K k = keys[i];
+    const int pb = pass_bits(bits);
+    auto count = [&](K k) {
         for (int p = 0; p < passes; ++p) {
-            const int shift = p * pass_bits(bits);
-            const int db = min(pass_bits(bits), bits - shift);
-            atomicAdd(&mine[p * kRadix + digit_of(k, shift, (1u << db) - 1u)], 1u);
+            const int shift = p * pb;
+            atomicAdd(&mine[p * kRadix + digit_of(k, shift, (1u << min(pb, bits - shift)) - 1u)],
+                      1u);
         }
+    };
+    // 16-byte loads over the aligned body (several keys in flight per
+    // thread), single keys before and after it
+    constexpr int VW = 16 / (int)sizeof(K);
+    const int64_t lead =
+        (VW - (int64_t)((reinterpret_cast<uintptr_t>(keys) / sizeof(K)) % VW)) % VW;
+    const int64_t head = lead < n ? lead : n;
+    const int64_t body = (n - head) / VW;
+    const int64_t tid = (int64_t)blockIdx.x * kSortThreads + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * kSortThreads;
+    if (tid < head) count(keys[tid]);
+    const uint4* vec = reinterpret_cast<const uint4*>(keys + head);
+    for (int64_t i = tid; i < body; i += nthreads) {
+        const uint4 q = vec[i];
+        const K* kk = reinterpret_cast<const K*>(&q);
+#pragma unroll
+        for (int j = 0; j < VW; ++j) count(kk[j]);
     }
+    for (int64_t i = head + body * VW + tid; i < n; i += nthreads) count(keys[i]);
     __syncthreads();
     for (int i = threadIdx.x; i < passes * kRadix; i += kSortThreads) {
         uint32_t c = 0u;
