@@ -851,14 +851,33 @@ bin_depth_range_kernel(const int32_t* __restrict__ valid, const float* __restric
     range += 2 * blockIdx.y;
     __shared__ uint32_t s_lo[8], s_hi[8];
     uint32_t lo = 0u, hi = 0u;
-    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n;
-         g += (int64_t)gridDim.x * blockDim.x) {
-        if (valid[g] != 0) {
-            const uint32_t bits = __float_as_uint(depth[g]);  // positive depths
+    auto take = [&](int32_t ok, float d) {
+        if (ok != 0) {
+            const uint32_t bits = __float_as_uint(d);  // positive depths
             lo = max(lo, ~bits);
             hi = max(hi, bits);
         }
+    };
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    // 16-byte loads of both arrays when they share an alignment (four rows in
+    // flight per load pair), single rows before and after the aligned body
+    const uintptr_t av = reinterpret_cast<uintptr_t>(valid), ad = reinterpret_cast<uintptr_t>(depth);
+    int64_t head = n, body = 0;
+    if ((av & 15u) == (ad & 15u) && (av & 3u) == 0u) {
+        const int64_t lead = (int64_t)(((16u - (av & 15u)) & 15u) >> 2);
+        head = lead < n ? lead : n;
+        body = (n - head) >> 2;
     }
+    for (int64_t g = tid; g < head; g += nthreads) take(valid[g], depth[g]);
+    const int4* v4 = reinterpret_cast<const int4*>(valid + head);
+    const float4* d4 = reinterpret_cast<const float4*>(depth + head);
+    for (int64_t i = tid; i < body; i += nthreads) {
+        const int4 ok = v4[i];
+        const float4 d = d4[i];
+        take(ok.x, d.x); take(ok.y, d.y); take(ok.z, d.z); take(ok.w, d.w);
+    }
+    for (int64_t g = head + 4 * body + tid; g < n; g += nthreads) take(valid[g], depth[g]);
     lo = __reduce_max_sync(0xffffffffu, lo);
     hi = __reduce_max_sync(0xffffffffu, hi);
     const int warp = threadIdx.x >> 5;
