@@ -114,9 +114,12 @@ def test_saturation_cut_changes_nothing_but_the_pair_count(cuda):
     assert lf == lc
     for a, b in zip(full.last_stats, cut.last_stats):
         assert b.pairs < 0.67 * a.pairs, (a.pairs, b.pairs)
+    # Adam's first step moves a row by about lr * sign(gradient): rows whose
+    # gradient is near zero can move either way when the atomics add in
+    # another order, so the parameters are held to 1e-5, like the gradients
     for name, _ in SEGMENTS:
         assert rel_l2(cut.grad(name).cpu().numpy(), full.grad(name).cpu().numpy()) < 1e-5, name
-        assert rel_l2(cut.param(name).cpu().numpy(), full.param(name).cpu().numpy()) < 1e-6, name
+        assert rel_l2(cut.param(name).cpu().numpy(), full.param(name).cpu().numpy()) < 1e-5, name
     assert torch.equal(cut.visibility_count(), full.visibility_count())
 
 
