@@ -357,6 +357,7 @@ class Trainer:
         self.split_colour = self._xchg is not None
         self._pending: dict[str, object] = {"geo": None, "sh": None}
         self._side = None
+        self._colour_stream = None
         # start the SH reduce-scatter only once the geometry's all-gather is
         # done, so the geometry path (which the next step waits for first)
         # has the links to itself
@@ -849,6 +850,20 @@ class Trainer:
         self._project_views(views, begin_step)
         streams = self._phase_b_streams(V)
         main = torch.cuda.current_stream(self.device)
+        # with the colour split, the views' colour waits for the previous
+        # step's SH all-gather on a stream of its own, beside the binning
+        # (the rendering waits for it); while every stage is timed it runs
+        # after the first chunk's binning instead
+        colour_done = None
+        if self.split_colour and not (self.stage_events is not None and
+                                      self.timed_stages is None):
+            if self._colour_stream is None:
+                self._colour_stream = torch.cuda.Stream(self.device)
+            self._colour_stream.wait_stream(main)   # the projection's valid flags
+            with torch.cuda.stream(self._colour_stream):
+                self._colour_views(views)
+            colour_done = torch.cuda.Event()
+            colour_done.record(self._colour_stream)
         C = V if self.bin_chunk <= 0 else min(V, int(self.bin_chunk))
         # chunked binning runs on a high-priority stream: it is the critical
         # path while the earlier chunks' views render on the others
@@ -863,8 +878,11 @@ class Trainer:
             chunk = views[first:first + C]
             with torch.cuda.stream(bin_stream):
                 totals, bb = self._bin_chunk(c, first, chunk)
-                if c == 0 and self.split_colour:
+                if c == 0 and self.split_colour and colour_done is None:
                     self._colour_views(views)
+            if c == 0 and colour_done is not None:
+                for sk in streams or [main]:
+                    sk.wait_event(colour_done)
             if streams:
                 # the chunk's views on the streams in turn, after its binning
                 ready = torch.cuda.Event()

@@ -171,4 +171,6 @@ def test_trainer_step_with_the_colour_split_equals_the_fused_step(cuda):
     assert torch.equal(fused._batch.color[:3], split._batch.color[:3])
     for name, _ in SEGMENTS:   # up to the order of the rasteriser's float atomics
         assert rel_l2(split.grad(name).cpu().numpy(), fused.grad(name).cpu().numpy()) < 1e-5, name
-        assert rel_l2(split.param(name).cpu().numpy(), fused.param(name).cpu().numpy()) < 1e-6, name
+        # (Adam's first step follows the gradient's sign, so near-zero rows
+        # may move either way: held to 1e-5 like the gradients)
+        assert rel_l2(split.param(name).cpu().numpy(), fused.param(name).cpu().numpy()) < 1e-5, name
