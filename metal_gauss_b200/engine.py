@@ -362,6 +362,9 @@ class Trainer:
         # done, so the geometry path (which the next step waits for first)
         # has the links to itself
         self.late_sh_exchange = False
+        # all-reduce the visibility counts and the loss on the SH group's
+        # communicator, beside the geometry reduce-scatter instead of before it
+        self.tail_on_sh_group = False
         # host targets are copied on this stream while the step projects and
         # bins; the loss kernels wait for the copies' event
         self._copy_stream = None
@@ -1016,7 +1019,8 @@ class Trainer:
         x = self._xchg
         main = torch.cuda.current_stream(self.device)
         ev = self._begin("exchange_wait")
-        w_tail = x.all_reduce(self.G[self.vis_offset:], 0)   # visibility counts + loss
+        # visibility counts + loss
+        w_tail = x.all_reduce(self.G[self.vis_offset:], 1 if self.tail_on_sh_group else 0)
         w_geo = x.reduce_scatter(self.G, 0)
         w_sh = None if self.late_sh_exchange else x.reduce_scatter(self.G, 1)
         w_tail.wait()
