@@ -74,12 +74,6 @@ def parse():
     ap.add_argument("--render", action="store_true",
                     help="forward-only render throughput on cfg4 (3M heavy-tailed Gaussians, "
                          "1920x1080, antialias, 256 orbit views) instead of the training step")
-    ap.add_argument("--late-sh-exchange", action="store_true",
-                    help="several GPUs: start the SH gradient reduce-scatter after the "
-                         "geometry's all-gather")
-    ap.add_argument("--tail-on-sh-group", action="store_true",
-                    help="several GPUs: all-reduce the visibility counts and loss on the SH "
-                         "communicator, beside the geometry reduce-scatter")
     ap.add_argument("--cfg5-shard", action="store_true",
                     help="cfg5 as one GPU's shard: 6M Gaussians in a 20x20x5 box with a dense "
                          "ground layer, 1600x1200, 8 of the batch's 64 orbit views per step (the "
@@ -327,8 +321,6 @@ def run_ours(args, rank, world, local):
     p, views, spec, targets_u8 = workload(args)
     trainer = Trainer(p, dev, sh_degree=3, background=spec["background"],
                       selective=not args.dense_adam)
-    trainer.late_sh_exchange = args.late_sh_exchange
-    trainer.tail_on_sh_group = args.tail_on_sh_group
     # the images stay bytes on the device; the loss reads them as x / 255
     targets = [t.to(dev) for t in targets_u8]
     B = args.batch

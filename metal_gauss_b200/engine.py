@@ -358,13 +358,6 @@ class Trainer:
         self._pending: dict[str, object] = {"geo": None, "sh": None}
         self._side = None
         self._colour_stream = None
-        # start the SH reduce-scatter only once the geometry's all-gather is
-        # done, so the geometry path (which the next step waits for first)
-        # has the links to itself
-        self.late_sh_exchange = False
-        # all-reduce the visibility counts and the loss on the SH group's
-        # communicator, beside the geometry reduce-scatter instead of before it
-        self.tail_on_sh_group = False
         # host targets are copied on this stream while the step projects and
         # bins; the loss kernels wait for the copies' event
         self._copy_stream = None
@@ -1019,10 +1012,9 @@ class Trainer:
         x = self._xchg
         main = torch.cuda.current_stream(self.device)
         ev = self._begin("exchange_wait")
-        # visibility counts + loss
-        w_tail = x.all_reduce(self.G[self.vis_offset:], 1 if self.tail_on_sh_group else 0)
+        w_tail = x.all_reduce(self.G[self.vis_offset:], 0)   # visibility counts + loss
         w_geo = x.reduce_scatter(self.G, 0)
-        w_sh = None if self.late_sh_exchange else x.reduce_scatter(self.G, 1)
+        w_sh = x.reduce_scatter(self.G, 1)
         w_tail.wait()
         w_geo.wait()
         self._end(ev)
@@ -1035,9 +1027,6 @@ class Trainer:
             self._side = torch.cuda.Stream(self.device)
         self._side.wait_stream(main)   # the all-reduced counts and the row factors
         with torch.cuda.stream(self._side):
-            if w_sh is None:
-                self._pending["geo"].wait()
-                w_sh = x.reduce_scatter(self.G, 1)
             w_sh.wait()
             self._adam([x.owned(1)], _lib.ADAM_ROW_FACTORS_READY | _lib.ADAM_KEEP_STEPS)
             self._pending["sh"] = x.all_gather(self.P, 1)
