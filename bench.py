@@ -24,6 +24,7 @@ selective Adam update on the views' union visibility.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -139,10 +140,13 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the
-    timed region runs."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms around the
+    timed region. The sampler is running (its first sample written) before
+    the region starts; the summary keeps the samples whose timestamps fall
+    inside the region, or the one nearest to it when the region is shorter
+    than the sampling period."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -150,6 +154,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t_start = self.t_end = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -157,14 +162,20 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0   # until the first sample is written
+            while time.time() < deadline and Path(self.path).stat().st_size == 0:
+                time.sleep(0.02)
         except (OSError, FileNotFoundError):
             self.proc = None
+        self.t_start = time.time()
         return self
 
     def __exit__(self, *exc):
+        self.t_end = time.time()
         if self.proc is not None:
+            time.sleep(0.06)   # one more sample after the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -177,27 +188,37 @@ class ClockSampler:
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                rows.append(dict(sm=float(parts[1]), sm_max=float(parts[2]),
-                                 power=float(parts[3]), hw=parts[5], hw_th=parts[6],
-                                 sw_th=parts[7], sw_pc=parts[8]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append(dict(ts=ts, sm=float(parts[2]), sm_max=float(parts[3]),
+                                 power=float(parts[4]), hw=parts[6], hw_th=parts[7],
+                                 sw_th=parts[8], sw_pc=parts[9]))
             except ValueError:
                 continue
         os.unlink(self.path)
         if not rows:
             return None
+        inside = [r for r in rows if self.t_start <= r["ts"] <= self.t_end]
+        nearest = not inside
+        if nearest:
+            mid = 0.5 * (self.t_start + self.t_end)
+            inside = [min(rows, key=lambda r: abs(r["ts"] - mid))]
         reasons = set()
-        for r in rows:
+        for r in inside:
             for key, name in (("hw", "hw_slowdown"), ("hw_th", "hw_thermal_slowdown"),
                               ("sw_th", "sw_thermal_slowdown"), ("sw_pc", "sw_power_cap")):
                 if r[key].lower().startswith("active"):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
-                "sm_max_mhz": max(r["sm_max"] for r in rows),
-                "power_w_max": max(r["power"] for r in rows),
-                "samples": len(rows), "reasons": sorted(reasons)}
+        out = {"sm_mhz": statistics.median(r["sm"] for r in inside),
+               "sm_max_mhz": max(r["sm_max"] for r in inside),
+               "power_w_max": max(r["power"] for r in inside),
+               "samples": len(inside), "reasons": sorted(reasons),
+               "window_s": round(self.t_end - self.t_start, 3)}
+        if nearest:
+            out["nearest_sample"] = True   # the region was shorter than the 50 ms period
+        return out
 
 
 # ---------------------------------------------------------------- workload
