@@ -217,6 +217,38 @@ def test_binning_mixes_recorded_and_rewalked_rectangles(cuda, tile):
     ids, off, _ = ext.bin_and_sort(o[0], o[3], o[1], T(opac), o[4], o[2], W, H, tile)
     assert np.array_equal(N(ids), r_ids)
     assert np.array_equal(N(off), r_off)
+    # with the saturation cut (the large rectangles' histogram adds, recount
+    # and emission run as whole-warp walks): each tile keeps a front prefix of
+    # its full list
+    c_ids, c_off = _cut_lists(o, T(opac), W, H, tile)
+    assert c_off[-1] <= r_off[-1]
+    for t in range(len(r_off) - 1):
+        kept = c_ids[c_off[t]:c_off[t + 1]]
+        assert np.array_equal(kept, r_ids[r_off[t]:r_off[t] + kept.size]), t
+
+
+def _cut_lists(o, opac, W, H, tile):
+    """mg_bin_prepare / mg_bin_emit with the saturation cut on."""
+    from metal_gauss_b200 import _lib
+    from metal_gauss_b200._lib import ptr
+    L = _lib.load()
+    s = _lib.stream()
+    uv, conic, depth, rxy, valid = o[0], o[1], o[2], o[3], o[4]
+    n = uv.shape[0]
+    n_tiles = -(-W // tile) * -(-H // tile)
+    tot = torch.zeros(1, dtype=torch.int64, device="cuda")
+    prep = torch.empty(L.mg_bin_prepare_scratch_bytes(n, n_tiles), dtype=torch.uint8,
+                       device="cuda")
+    _lib.call("mg_bin_prepare", ptr(uv), ptr(rxy), ptr(conic), ptr(opac), ptr(valid), ptr(depth),
+              n, W, H, tile, 1, ptr(tot), ptr(prep), prep.numel(), s)
+    m = int(tot.item())
+    ids = torch.empty(max(m, 1), dtype=torch.int32, device="cuda")
+    off = torch.empty(n_tiles + 1, dtype=torch.int32, device="cuda")
+    emit = torch.empty(L.mg_bin_emit_scratch_bytes(n, m, n_tiles), dtype=torch.uint8,
+                       device="cuda")
+    _lib.call("mg_bin_emit", ptr(uv), ptr(rxy), ptr(conic), ptr(opac), n, m, W, H, tile, 1,
+              ptr(prep), ptr(ids), ptr(off), ptr(emit), emit.numel(), s)
+    return ids[:m].cpu().numpy(), off.cpu().numpy()
 
 
 def test_binning_of_an_empty_and_an_invisible_scene(cuda):
