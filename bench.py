@@ -382,6 +382,13 @@ def run_ours(args, rank, world, local):
         # slowest rank rather than for the transfer
         busy = sum(float(np.sum(v)) for k, v in stage_ms.items() if k not in waits) / n_instr
         coll["rank_busy_ms"] = [round(b, 3) for b in gather_ranks(busy, world)]
+        # the wait that exposes the most of the exchange, by name
+        names = {"exchange_wait_ms": "count/loss all-reduce + geometry reduce-scatter",
+                 "wait_geo_gather_ms": "geometry all-gather",
+                 "wait_sh_gather_ms": "SH reduce-scatter + all-gather",
+                 "allreduce_ms": "gradient all-reduce (replicated optimizer)"}
+        top = max(names, key=lambda k: coll.get(k, 0.0))
+        coll["limiting"] = names[top]
     singles = {k: v for k, v in stage_ms.items()
                if k in ("raster_bwd", "raster_fwd", "preprocess_fwd", "preprocess_bwd", "loss",
                         "adam")}
