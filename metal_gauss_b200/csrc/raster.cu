@@ -367,6 +367,7 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                                 rect_live(st.q[buf][0][lane], st.q[buf][1][lane].x,
                                           st.q[buf][2][lane], rx0, rx1, ry0, ry1);
                 uint32_t live = __ballot_sync(0xffffffffu, lv);
+                int round = 0;
                 while (live) {
                     const int k1 = __ffs(live) - 1;
                     live &= live - 1;
@@ -397,7 +398,11 @@ raster_forward_kernel(const float4* __restrict__ splats, const int32_t* __restri
                         stop = base + k2 + 1;
                         done = T < 1e-4f;
                     }
-                    if (__all_sync(0xffffffffu, done)) break;
+                    // every other round: a round after every pixel stopped
+                    // blends nothing, and the vote costs an instruction per
+                    // round (launch lists: 348-363 us per view against
+                    // 361-363 voting every round, within box-to-box noise)
+                    if ((++round & 1) == 0 && __all_sync(0xffffffffu, done)) break;
                 }
                 const bool all_done = __all_sync(0xffffffffu, done);  // releases buffer buf
                 if (all_done || ci + 1 >= n_chunks) break;
